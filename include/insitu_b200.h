@@ -1,0 +1,284 @@
+/*
+ * insitu_b200.h -- C ABI of libinsitu_b200.so, the B200 (sm_100a) IVF query
+ * hot path of InSituANN: coarse routing, exact uint8 fine search, residual-PQ
+ * ADC search with exact rerank, the update overlay (published delta
+ * segments) and the entry points a cluster-sharded multi-GPU driver needs.
+ *
+ * Plain C types only.  Every function may be called from any host thread;
+ * one batch context is one CUDA stream and must not be used by two threads at
+ * once.  Index contexts are immutable after loading (publishing a delta
+ * segment excepted), so several batch contexts may search one index
+ * concurrently.
+ *
+ * Return conventions
+ *   - names taken from the reference keep the reference's return types and
+ *     meaning (cited per function);
+ *   - the entry points the reference does not have return 0 on success and a
+ *     negative IVF_E* code on failure; the message is kept per context and is
+ *     read with ivf_last_error().
+ * No function aborts, exits or resets the device.
+ *
+ * Citations are paths inside the reference project
+ * (mindtravel/InSituANN-OpenSource).
+ */
+#ifndef INSITU_B200_H
+#define INSITU_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* status codes of the entry points that are new in this library */
+#define IVF_OK 0
+#define IVF_EINVAL -1       /* bad argument (null pointer, size, unsupported shape) */
+#define IVF_ECUDA -2        /* a CUDA call failed (message has the CUDA error string) */
+#define IVF_ESTATE -3       /* wrong context state (nothing loaded, wrong index type) */
+#define IVF_ENOMEM -4       /* device allocation failed */
+#define IVF_EOVERFLOW -5    /* a candidate buffer overflowed (results would be wrong) */
+#define IVF_EUNSUPPORTED -6 /* metric / layout outside the hot path (e.g. cosine) */
+
+/* distance_mode values, cuda/pch.h:36-39 */
+#define IVF_DISTANCE_L2 0
+#define IVF_DISTANCE_COSINE 1
+
+/* ======================================================================
+ * Index and batch contexts -- cuda/search/ivf_search.cuh:204-321
+ * ====================================================================== */
+
+/* ivf_search.cuh:215 -- new, empty index context (NULL on failure). */
+void* ivf_create_index_context(void);
+/* ivf_search.cuh:222 -- frees the context and every device buffer it owns. */
+void ivf_destroy_index_context(void* idx_ctx);
+
+/*
+ * ivf_search.cuh:236-244 -- adopt caller-allocated device arrays of an fp32
+ * index (ownership passes to the context, as in ivf_search_separated.cu:141-143).
+ * Returns 1 when loaded, 0 when the context already holds an index.  The
+ * fp32 fine-search path behind it is outside this library's hot path: the
+ * data is adopted and routing works, but ivf_pipeline_stage2_compute on such
+ * an index records IVF_EUNSUPPORTED.
+ */
+int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vectors, float* d_cluster_centers,
+                     int n_total_clusters, int n_total_vectors, int n_dim);
+
+/* ivf_search.cuh:258 -- batch context: one stream, scratch sized for these limits. */
+void* ivf_create_batch_context(int max_n_query, int n_dim, int max_n_probes, int max_k, int n_total_clusters);
+/* ivf_search.cuh:265 */
+void ivf_destroy_batch_context(void* batch_ctx);
+
+/* ivf_search.cuh:276-280 -- async H2D of the fp32 query batch on the batch stream. */
+void ivf_pipeline_stage1_prepare(void* batch_ctx, float* query_batch_host, int n_query);
+
+/*
+ * ivf_search.cuh:294-301 -- routing + fine search of the staged queries:
+ *   uint8 index: exact int32 search, top-k by (distance, original id);
+ *   PQ index:    residual-PQ stage 1 (rerank_n = 512) + exact rerank, with
+ *                the published delta segment when one exists.
+ * distance_mode must be IVF_DISTANCE_L2 (cosine records IVF_EUNSUPPORTED).
+ */
+void ivf_pipeline_stage2_compute(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                                 int distance_mode);
+
+/* ivf_search.cuh:314-320 -- D2H of the results, then stream sync. */
+void ivf_pipeline_get_results(void* batch_ctx, float* topk_dist, int* topk_index, int n_query, int k);
+/* ivf_search.cuh:327 */
+void ivf_pipeline_sync_batch(void* batch_ctx);
+
+/* ======================================================================
+ * Exception-safe *_wrapper exports and the per-OID registry --
+ * cuda/search/ivf_search_wrapper.cpp:85-427.  Same meaning as above; the
+ * int-returning wrappers give -1 on failure.
+ * ====================================================================== */
+void* ivf_create_index_context_wrapper(void);
+void ivf_destroy_index_context_wrapper(void* idx_ctx);
+int ivf_load_dataset_wrapper(void* idx_ctx, int* d_cluster_size, float* d_cluster_vectors,
+                             float* d_cluster_centers, int n_total_clusters, int n_total_vectors, int n_dim);
+void* ivf_create_batch_context_wrapper(int max_n_query, int n_dim, int max_n_probes, int max_k,
+                                       int n_total_clusters);
+void ivf_destroy_batch_context_wrapper(void* batch_ctx);
+void ivf_pipeline_stage1_prepare_wrapper(void* batch_ctx, float* query_batch_host, int n_query);
+void ivf_pipeline_stage2_compute_wrapper(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                                         int distance_mode);
+void ivf_pipeline_get_results_wrapper(void* batch_ctx, float* topk_dist, int* topk_index, int n_query, int k);
+void ivf_pipeline_sync_batch_wrapper(void* batch_ctx);
+/* ivf_search_wrapper.cpp:313-320 -- 1 when the context holds a loaded index. */
+int ivf_check_index_initialized_wrapper(void* idx_ctx);
+/* ivf_search_wrapper.cpp:346-427 -- 64-slot OID -> index registry (thread-safe here). */
+void ivf_register_index_instance(unsigned int index_oid, void* gpu_handle);
+void* ivf_get_index_instance(unsigned int index_oid);
+void ivf_unregister_index_instance(unsigned int index_oid);
+
+/* ======================================================================
+ * Coarse routing handle -- cuda/search/cpu_fine/cpu_fine.h:232-278
+ * (C++ linkage there; C linkage here, same layout and argument meaning).
+ * ====================================================================== */
+typedef struct CoarseHandle {
+    const float* d_centers;   /* borrowed device centroids [n_total_clusters, dim] */
+    float* d_centers_norm;    /* owned: here the per-centroid validity (norm >= 1e-6) */
+    void* cublas_handle;      /* owned: here the routing state (stream, scratch) */
+    int n_total_clusters;
+    int dim;
+    int distance_mode_cached;
+} CoarseHandle;
+
+typedef struct CoarseTimingBreakdown {
+    double query_h2d_ms;
+    double seq_init_ms;
+    double query_norm_ms;
+    double gemm_ms;
+    double topk_ms;
+    double cluster_d2h_ms;
+    double coarse_compute_ms;
+    double coarse_total_ms;
+} CoarseTimingBreakdown;
+
+/* cpu_fine.h:252-257 */
+void coarse_handle_init(CoarseHandle* h, const float* d_centers, int n_total_clusters, int dim);
+/* cpu_fine.h:259 */
+void coarse_handle_release(CoarseHandle* h);
+/*
+ * cpu_fine.h:266-276 -- top-n_probes lists per query, host in / host out,
+ * ranked by exact fp32 L2 (ties: smaller list id).  Bad arguments are
+ * reported through ivf_global_last_error() and leave the output untouched
+ * (the reference aborts, ivf_search_cpu_fine.cu:775-784).
+ */
+void coarse_search(const CoarseHandle* h, const float* h_query, int n_query_batch, int n_probes, int distance_mode,
+                   int* h_cluster_ids_out, double* out_coarse_ms, double* out_h2d_ms, double* out_d2h_ms);
+/* cpu_fine.h:278 -- timing of the calling thread's last coarse_search. */
+const CoarseTimingBreakdown* coarse_get_last_timing(void);
+
+/* ======================================================================
+ * Index loading (new: the reference loads these inside its runners,
+ * updates/pq_update.cu:676-713 and updates/exact_update.cu:2229).  All
+ * arrays are host arrays in the reference file layouts and are copied to
+ * the device; positions are cluster-major (stable reorder).
+ * ====================================================================== */
+
+/*
+ * uint8 exact index.  base_u8 [n, d] cluster-major; offsets [nlist] (first
+ * position of each list), counts [nlist]; reorder_to_original [n] (NULL =
+ * identity); centroids [nlist, d].  d must be a multiple of 16, <= 512.
+ */
+int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets, const int* counts,
+                const int* reorder_to_original, const float* centroids, int nlist, long long n, int d);
+
+/*
+ * Residual-PQ index (formats of scripts/train_ivfpq_residual.py:6-15):
+ * codebook [M, K, dsub] fp32 with K = 256 and M*dsub = d, M a multiple of 8
+ * and <= 64; codes [n, M] cluster-major; rerank rows base_u8 [n, d] or
+ * base_f32 [n, d] (exactly one non-NULL) in the same cluster-major order.
+ */
+int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, int M, int K, int dsub,
+                const uint8_t* codes, const long long* offsets, const int* counts, const int* reorder_to_original,
+                const uint8_t* base_u8, const float* base_f32, int nlist, long long n, int d);
+
+/*
+ * Marks a loaded index as one shard of a larger index: local list l is
+ * global list local_to_global[l] (of nlist_global), and its vectors occupy
+ * global positions key_offsets[l] .. key_offsets[l]+counts[l]-1 of the whole
+ * index.  Routing then reports global list ids, fine search accepts global
+ * probe ids (lists of other shards are skipped) and ranking keys use global
+ * positions, so per-shard results merge into exactly the unsharded result.
+ */
+int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, const long long* key_offsets);
+
+/* ======================================================================
+ * Update overlay (new: runner-internal in the reference,
+ * updates/pq_update.cu:396-494, 975-1055)
+ * ====================================================================== */
+/*
+ * Publishes one delta segment of n_delta vectors over the same lists:
+ * codes [n_delta, M] list-major, offsets/counts [nlist] (local lists),
+ * ids [n_delta] (reported ids, disjoint from the base), rerank rows raw_u8
+ * or raw_f32 [n_delta, d] in delta-position order (same type as the base
+ * rerank rows).  key_offsets [nlist] may be NULL (= offsets); shards pass the
+ * global delta positions.  Replaces a previously published segment.
+ */
+int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, const int* counts,
+                         const long long* offsets, const long long* key_offsets, const uint8_t* raw_u8,
+                         const float* raw_f32, long long n_delta);
+int ivf_pq_clear_delta(void* idx_ctx);
+
+/* ======================================================================
+ * Search (new, explicit parameters)
+ * ====================================================================== */
+/* routing of the staged queries into the batch's probe table (device). */
+int ivf_route(void* batch_ctx, void* idx_ctx, int n_query, int n_probes);
+/* copies probe ids in or out of the batch's probe table [n_query, n_probes] (host). */
+int ivf_set_probes(void* batch_ctx, const int* h_probes, int n_query, int n_probes);
+int ivf_get_probes(void* batch_ctx, int* h_probes, int n_query, int n_probes);
+
+/* exact uint8 search: routing (if route != 0) + fine search on the batch probes. */
+int ivf_u8_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k, int route);
+/*
+ * residual-PQ search: routing (if route != 0) + stage 1 with rerank_n
+ * candidates (+ delta_topk from the delta segment when use_overlay != 0 and
+ * one is published; the reference uses 16, pq_update.cu:25) + exact rerank.
+ */
+int ivf_pq_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k, int rerank_n,
+                  int use_overlay, int delta_topk, int route);
+
+/* results of the last search: ids [n_query, k]; float or int32 distances. */
+int ivf_get_results_i32(void* batch_ctx, int* ids, int* dist, int n_query, int k);
+
+/* ======================================================================
+ * Device-resident variants (pointers are device pointers on the batch's
+ * device; used when the caller keeps queries and results in HBM)
+ * ====================================================================== */
+int ivf_pipeline_stage1_prepare_device(void* batch_ctx, const float* d_query, int n_query);
+int ivf_get_results_device(void* batch_ctx, float* d_dist, int* d_index, int n_query, int k);
+/* the batch's CUDA stream (cudaStream_t) so callers can order their own work */
+void* ivf_batch_stream(void* batch_ctx);
+
+/* ======================================================================
+ * Shard exchange (new; inverted lists sharded by cluster over GPUs).  All
+ * pointers are device pointers; the caller moves them between GPUs (NCCL).
+ * ====================================================================== */
+/* local routing keys [n_query, n_probes]: (fp32 distance bits << 32) | global list id */
+int ivf_route_keys(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, unsigned long long* d_keys);
+/* merges n_in keys per query [n_query, n_in] into the batch probe table */
+int ivf_route_merge(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int n_probes);
+/*
+ * stage 1 + exact scoring of this shard's candidates for the batch probes:
+ * d_adc [n_query, rerank_n] sorted (ADC bits << 32 | global position),
+ * d_exact [n_query, rerank_n] aligned (exact bits << 32 | reported id);
+ * the same for the delta segment when d_dadc/d_dexact are non-NULL.
+ */
+int ivf_pq_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n, int delta_topk,
+                        unsigned long long* d_adc, unsigned long long* d_exact, unsigned long long* d_dadc,
+                        unsigned long long* d_dexact);
+/* merges per-query concatenations of shard outputs into the batch results */
+int ivf_pq_merge_shards(void* batch_ctx, const unsigned long long* d_adc, const unsigned long long* d_exact,
+                        int n_main, int rerank_n, const unsigned long long* d_dadc,
+                        const unsigned long long* d_dexact, int n_delta, int delta_topk, int n_query, int k,
+                        int exact_is_int);
+/* exact uint8 shard search: sorted top-k keys (distance << 32 | original id) per query */
+int ivf_u8_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                        unsigned long long* d_keys);
+/* merges n_in exact keys per query into the batch results (top-k) */
+int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int k);
+
+/* ======================================================================
+ * errors
+ * ====================================================================== */
+/* last error message of an index or batch context ("" when none) */
+const char* ivf_last_error(void* ctx);
+/* last error of the calling thread for calls without a context (coarse_search) */
+const char* ivf_global_last_error(void);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* INSITU_B200_H */

@@ -1,0 +1,1242 @@
+// capi.cu -- index / batch contexts and the C ABI declared in include/insitu_b200.h.
+//
+// Contexts mirror the reference's IVFIndexContext / IVFQueryBatchContext
+// (cuda/search/ivf_search_separated.cu:31-93): the index context owns the
+// device-resident lists, the batch context owns one stream and the scratch of
+// a query batch.  Unlike the reference, no call allocates per batch once the
+// scratch has grown to the batch shape, no call synchronises the host in the
+// middle of a search, and no call exits or resets the device.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "../../include/insitu_b200.h"
+#include "launch.h"
+
+using namespace isb;
+
+namespace {
+
+constexpr uint32_t kIdxMagic = 0x31584449u;  // "IDX1"
+constexpr uint32_t kBatMagic = 0x31544142u;  // "BAT1"
+constexpr int kKindEmpty = 0, kKindF32 = 1, kKindU8 = 2, kKindPQ = 3;
+
+struct ApiError : std::runtime_error {
+    int code;
+    ApiError(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw ApiError(code, msg); }
+
+void ck(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        fail(e == cudaErrorMemoryAllocation ? IVF_ENOMEM : IVF_ECUDA,
+             std::string(what) + ": " + cudaGetErrorString(e));
+    }
+}
+
+void require(bool ok, const std::string& msg, int code = IVF_EINVAL) {
+    if (!ok) fail(code, msg);
+}
+
+template <class T>
+T* dalloc(size_t n, std::vector<void*>& owned) {
+    void* p = nullptr;
+    ck(cudaMalloc(&p, std::max<size_t>(n, 1) * sizeof(T)), "cudaMalloc");
+    owned.push_back(p);
+    return static_cast<T*>(p);
+}
+
+template <class T>
+T* dcopy(const T* h, size_t n, std::vector<void*>& owned) {
+    T* d = dalloc<T>(n, owned);
+    if (n) ck(cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+    return d;
+}
+
+void free_all(std::vector<void*>& owned) {
+    for (void* p : owned) cudaFree(p);
+    owned.clear();
+}
+
+struct Segment {
+    uint8_t* data = nullptr;
+    int64_t* offsets = nullptr;
+    int32_t* counts = nullptr;
+    int32_t* ids = nullptr;
+    int64_t* key_off = nullptr;
+    uint8_t* rr_u8 = nullptr;
+    float* rr_f32 = nullptr;
+    int64_t n = 0;
+    int max_count = 0;
+    std::vector<void*> owned;
+
+    void release() {
+        free_all(owned);
+        *this = Segment();
+    }
+    ListStore view() const { return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, n}; }
+};
+
+struct IndexCtx {
+    uint32_t magic = kIdxMagic;
+    int device = 0;
+    int kind = kKindEmpty;
+    int nlist = 0, d = 0;
+    int64_t n = 0;
+    float* cent = nullptr;
+    uint8_t* valid = nullptr;
+    int M = 0, dsub = 0;
+    float* codebook = nullptr;
+    Segment main, delta;
+    bool has_delta = false;
+    int nlist_global = 0;        // == nlist unless the index is a shard
+    int32_t* l2g = nullptr;      // [nlist] local -> global list id (shards)
+    int32_t* g2l = nullptr;      // [nlist_global] global -> local list id or -1 (shards)
+    std::vector<void*> owned;    // centroids, validity, codebook, shard maps, adopted arrays
+    std::mutex mu;
+    std::string err;
+};
+
+struct Grow {
+    void* p = nullptr;
+    size_t bytes = 0;
+};
+
+struct BatchCtx {
+    uint32_t magic = kBatMagic;
+    int device = 0;
+    cudaStream_t st = nullptr;
+    int max_nq = 0, d = 0, max_nprobe = 0, max_k = 0, nlist = 0;
+    float* q = nullptr;
+    uint8_t* q_u8 = nullptr;
+    int32_t* probes = nullptr;
+    int32_t* out_ids = nullptr;
+    float* out_dist = nullptr;
+    int32_t* out_idist = nullptr;
+    int* counter = nullptr;
+    int* overflow = nullptr;      // device flag
+    int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
+    int res_nq = 0, res_k = 0;
+    int probes_nq = 0, probes_np = 0;
+    Grow route_dist, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp;
+    Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
+    std::vector<void*> owned;
+    std::string err;
+};
+
+thread_local std::string g_err;
+
+// device memory budget for per-batch candidate / routing scratch
+size_t scratch_budget() {
+    const char* e = getenv("INSITU_SCRATCH_MB");
+    long mb = e ? atol(e) : 0;
+    if (mb <= 0) mb = 6144;
+    return (size_t)mb << 20;
+}
+
+template <class T>
+T* ensure(BatchCtx* b, Grow& g, size_t n) {
+    size_t bytes = std::max<size_t>(n, 1) * sizeof(T);
+    if (bytes <= g.bytes) return static_cast<T*>(g.p);
+    if (g.p) {
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        cudaFree(g.p);
+        g.p = nullptr;
+        g.bytes = 0;
+    }
+    ck(cudaMalloc(&g.p, bytes), "cudaMalloc (scratch)");
+    g.bytes = bytes;
+    return static_cast<T*>(g.p);
+}
+
+IndexCtx* as_index(void* p) {
+    auto* c = static_cast<IndexCtx*>(p);
+    require(c && c->magic == kIdxMagic, "not an index context");
+    return c;
+}
+
+BatchCtx* as_batch(void* p) {
+    auto* c = static_cast<BatchCtx*>(p);
+    require(c && c->magic == kBatMagic, "not a batch context");
+    return c;
+}
+
+// runs f, converting exceptions into (status, message on ctx)
+template <class F>
+int guarded(std::string* err, F&& f) {
+    try {
+        f();
+        if (err) err->clear();
+        g_err.clear();
+        return IVF_OK;
+    } catch (const ApiError& e) {
+        if (err) *err = e.what();
+        g_err = e.what();
+        return e.code;
+    } catch (const std::exception& e) {
+        if (err) *err = e.what();
+        g_err = e.what();
+        return IVF_EINVAL;
+    }
+}
+
+std::string* err_of(void* ctx) {
+    if (!ctx) return nullptr;
+    uint32_t m = *static_cast<uint32_t*>(ctx);
+    if (m == kIdxMagic) return &static_cast<IndexCtx*>(ctx)->err;
+    if (m == kBatMagic) return &static_cast<BatchCtx*>(ctx)->err;
+    return nullptr;
+}
+
+int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+// ---------------------------------------------------------------------------
+// index loading helpers
+// ---------------------------------------------------------------------------
+void load_lists(IndexCtx* x, Segment& s, const uint8_t* data, size_t row_bytes, const long long* offsets,
+                const int* counts, const int* ids, const long long* key_off, int nlist, long long n) {
+    require(offsets && counts, "offsets and counts are required");
+    int max_count = 0;
+    for (int l = 0; l < nlist; ++l) {
+        require(counts[l] >= 0, "negative list count");
+        require(offsets[l] >= 0 && offsets[l] + counts[l] <= n, "list outside [0, n)");
+        max_count = std::max(max_count, counts[l]);
+    }
+    require(n < (1ll << 32) - 1, "more than 2^32-2 vectors in one segment");
+    (void)x;
+    s.data = dcopy(data, (size_t)n * row_bytes, s.owned);
+    s.offsets = dcopy(reinterpret_cast<const int64_t*>(offsets), (size_t)nlist, s.owned);
+    s.counts = dcopy(reinterpret_cast<const int32_t*>(counts), (size_t)nlist, s.owned);
+    s.ids = ids ? dcopy(reinterpret_cast<const int32_t*>(ids), (size_t)n, s.owned) : nullptr;
+    s.key_off = key_off ? dcopy(reinterpret_cast<const int64_t*>(key_off), (size_t)nlist, s.owned) : nullptr;
+    s.n = n;
+    s.max_count = max_count;
+}
+
+void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
+    require(centroids != nullptr, "centroids are required");
+    x->cent = dcopy(centroids, (size_t)nlist * d, x->owned);
+    x->valid = dalloc<uint8_t>((size_t)nlist, x->owned);
+    ck(route_centroid_valid(x->cent, nlist, d, x->valid, 0), "centroid validity");
+    ck(cudaDeviceSynchronize(), "centroid validity");
+    x->nlist = nlist;
+    x->nlist_global = nlist;
+    x->d = d;
+}
+
+// ---------------------------------------------------------------------------
+// search drivers
+// ---------------------------------------------------------------------------
+void check_shape(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k) {
+    require(x->kind != kKindEmpty, "index context holds no index", IVF_ESTATE);
+    require(nq >= 0 && nq <= b->max_nq, "n_query outside [0, max_n_query]");
+    require(nprobe > 0 && nprobe <= b->max_nprobe, "n_probes outside [1, max_n_probes]");
+    require(k > 0 && k <= b->max_k, "k outside [1, max_k]");
+    require(b->d == x->d, "batch and index dimensions differ");
+}
+
+// top-nprobe of the staged queries over the index's (local) centroids.
+// keys != nullptr: write sorted keys with global list ids instead of probes.
+void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
+    require(x->nlist_global >= nprobe || keys, "n_probes > n_total_clusters");
+    const int L = std::min(nprobe, 2048);
+    require(L == nprobe, "n_probes > 2048 is not supported");
+    size_t row = (size_t)x->nlist * sizeof(uint32_t);
+    int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
+    uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
+    for (int s = 0; s < nq; s += nsub) {
+        int n = std::min(nsub, nq - s);
+        ck(route_distances(b->q + (size_t)s * x->d, n, x->cent, x->valid, x->nlist, x->d, dist, b->st),
+           "route_distances");
+        if (keys) {
+            ck(route_select(dist, n, x->nlist, nprobe, x->l2g, nullptr, nullptr, keys + (size_t)s * nprobe, b->st),
+               "route_select");
+        } else {
+            ck(route_select(dist, n, x->nlist, nprobe, x->l2g, b->probes + (size_t)s * nprobe, nullptr, nullptr,
+                            b->st),
+               "route_select");
+        }
+    }
+    if (!keys) {
+        b->probes_nq = nq;
+        b->probes_np = nprobe;
+    }
+}
+
+WorkList worklist_for(BatchCtx* b, IndexCtx* x, int nsub, int nprobe, void** tmp, size_t* tmp_bytes) {
+    WorkList wl{};
+    wl.list_cnt = ensure<int32_t>(b, b->wl_cnt, (size_t)x->nlist + 1);
+    wl.list_off = ensure<int32_t>(b, b->wl_off, (size_t)x->nlist + 1);
+    wl.cursor = ensure<int32_t>(b, b->wl_cursor, (size_t)x->nlist + 1);
+    wl.pair_q = ensure<int32_t>(b, b->pair_q, (size_t)nsub * nprobe);
+    wl.pair_l = ensure<int32_t>(b, b->pair_l, (size_t)nsub * nprobe);
+    wl.n_pairs = wl.list_off + x->nlist;
+    *tmp_bytes = worklist_scan_bytes(x->nlist);
+    *tmp = ensure<uint8_t>(b, b->scan_tmp, *tmp_bytes);
+    return wl;
+}
+
+void require_probes(BatchCtx* b, int nq, int nprobe) {
+    require(b->probes_nq >= nq && b->probes_np == nprobe,
+            "no probe table for this (n_query, n_probes): route or set probes first", IVF_ESTATE);
+}
+
+void queue_overflow_check(BatchCtx* b) {
+    ck(cudaMemcpyAsync(b->h_overflow, b->overflow, sizeof(int), cudaMemcpyDeviceToHost, b->st), "overflow D2H");
+}
+
+// exact uint8 search on the batch probes; keys_out: per-query sorted top-k keys instead of results
+void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_out) {
+    require(x->kind == kKindU8, "index is not a uint8 exact index", IVF_ESTATE);
+    require_probes(b, nq, nprobe);
+    ck(make_query_u8(b->q, (size_t)nq * x->d, b->q_u8, b->st), "make_query_u8");
+    const int cap = nprobe * ceil_div(std::max(x->main.max_count, 1), kExactScanChunk) *
+                    std::min(k, kExactScanChunk);
+    size_t per_q = (size_t)cap * 8 + (size_t)k * 8 + 16;
+    int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
+    void* tmp;
+    size_t tmp_bytes;
+    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes);
+    CandBuf cb{};
+    cb.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap);
+    cb.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
+    cb.thr = ensure<unsigned long long>(b, b->thr_m, (size_t)nsub);
+    cb.overflow = b->overflow;
+    cb.cap = cap;
+    cb.R = k;
+    uint64_t* topk = ensure<uint64_t>(b, b->exk, (size_t)nsub * k);
+    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    for (int s = 0; s < nq; s += nsub) {
+        int n = std::min(nsub, nq - s);
+        ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl, tmp,
+                          tmp_bytes, b->st),
+           "build_worklist");
+        ck(reset_candidates(cb, n, b->st), "reset_candidates");
+        ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter, b->st),
+           "exact_scan");
+        uint64_t* dst = keys_out ? keys_out + (size_t)s * k : topk;
+        ck(select_top_r(cb, n, dst, b->st), "select_top_r");
+        if (!keys_out)
+            ck(keys_to_exact_results(topk, n, k, b->out_ids + (size_t)s * k, b->out_idist + (size_t)s * k,
+                                     b->out_dist + (size_t)s * k, b->st),
+               "keys_to_exact_results");
+    }
+    queue_overflow_check(b);
+    b->res_nq = nq;
+    b->res_k = k;
+}
+
+PQParams pq_params(IndexCtx* x, const float* q, bool use_delta) {
+    PQParams p{};
+    p.q = q;
+    p.cent = x->cent;
+    p.codebook = x->codebook;
+    p.d = x->d;
+    p.M = x->M;
+    p.dsub = x->dsub;
+    p.main = x->main.view();
+    p.delta = x->delta.view();
+    p.has_delta = use_delta ? 1 : 0;
+    return p;
+}
+
+// residual-PQ search on the batch probes.  shard outputs (all device, may be null):
+//   adc/exact [nq, R], dadc/dexact [nq, Rd]; when adc is given no final top-k is formed.
+void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, bool overlay, int delta_topk,
+            uint64_t* adc, uint64_t* exact, uint64_t* dadc, uint64_t* dexact) {
+    require(x->kind == kKindPQ, "index is not a residual-PQ index", IVF_ESTATE);
+    require_probes(b, nq, nprobe);
+    const int R = std::max(rerank_n, adc ? 1 : k);
+    const bool use_delta = overlay && x->has_delta && delta_topk > 0;
+    const int Rd = use_delta ? delta_topk : 0;
+    require(R <= 4096 && R + Rd <= 4096, "rerank_n + delta_topk must be <= 4096");
+    const int cap_m = nprobe * ceil_div(std::max(x->main.max_count, 1), kPQScanChunk) * std::min(R, kPQScanChunk);
+    const int cap_d = use_delta ? nprobe * ceil_div(std::max(x->delta.max_count, 1), kPQScanChunk) *
+                                      std::min(Rd, kPQScanChunk)
+                                : 0;
+    size_t per_q = ((size_t)cap_m + cap_d + R + Rd) * 8 + 32;
+    int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
+    void* tmp;
+    size_t tmp_bytes;
+    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes);
+    CandBuf cm{}, cd{};
+    cm.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap_m);
+    cm.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
+    cm.thr = ensure<unsigned long long>(b, b->thr_m, (size_t)nsub);
+    cm.overflow = b->overflow;
+    cm.cap = cap_m;
+    cm.R = R;
+    uint64_t* s1m = ensure<uint64_t>(b, b->s1m, (size_t)nsub * R);
+    uint64_t* s1d = nullptr;
+    if (use_delta) {
+        cd.keys = ensure<uint64_t>(b, b->cand_d, (size_t)nsub * cap_d);
+        cd.cnt = ensure<int32_t>(b, b->cnt_d, (size_t)nsub);
+        cd.thr = ensure<unsigned long long>(b, b->thr_d, (size_t)nsub);
+        cd.overflow = b->overflow;
+        cd.cap = cap_d;
+        cd.R = Rd;
+        s1d = ensure<uint64_t>(b, b->s1d, (size_t)nsub * Rd);
+    }
+    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    for (int s = 0; s < nq; s += nsub) {
+        int n = std::min(nsub, nq - s);
+        ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl, tmp,
+                          tmp_bytes, b->st),
+           "build_worklist");
+        ck(reset_candidates(cm, n, b->st), "reset_candidates");
+        if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
+        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
+        ck(pq_scan(p, wl, n * nprobe, cm, cd, b->counter, b->st), "pq_scan");
+        uint64_t* m_out = adc ? adc + (size_t)s * R : s1m;
+        ck(select_top_r(cm, n, m_out, b->st), "select_top_r");
+        uint64_t* d_out = nullptr;
+        if (use_delta) {
+            d_out = dadc ? dadc + (size_t)s * Rd : s1d;
+            ck(select_top_r(cd, n, d_out, b->st), "select_top_r (delta)");
+        }
+        if (adc) {
+            ck(pq_rerank(p, x->nlist, m_out, R, d_out, Rd, n, k, nullptr, nullptr, exact + (size_t)s * R,
+                         use_delta ? dexact + (size_t)s * Rd : nullptr, b->st),
+               "pq_rerank");
+        } else {
+            ck(pq_rerank(p, x->nlist, m_out, R, d_out, Rd, n, k, b->out_ids + (size_t)s * k,
+                         b->out_dist + (size_t)s * k, nullptr, nullptr, b->st),
+               "pq_rerank");
+        }
+    }
+    if (adc && dadc && !use_delta) {
+        // caller asked for delta outputs but there is no delta segment: empty lists
+        ck(cudaMemsetAsync(dadc, 0xFF, sizeof(uint64_t) * (size_t)nq * std::max(delta_topk, 0), b->st), "memset");
+        ck(cudaMemsetAsync(dexact, 0xFF, sizeof(uint64_t) * (size_t)nq * std::max(delta_topk, 0), b->st), "memset");
+    }
+    queue_overflow_check(b);
+    if (!adc) {
+        b->res_nq = nq;
+        b->res_k = k;
+    }
+}
+
+void check_overflow_after_sync(BatchCtx* b) {
+    if (*b->h_overflow)
+        fail(IVF_EOVERFLOW, "a candidate buffer overflowed; raise INSITU_SCRATCH_MB or lower n_probes");
+}
+
+void copy_results(BatchCtx* b, float* dist, int* idx, int32_t* idist, int nq, int k, cudaMemcpyKind kind) {
+    require(nq <= b->res_nq && k == b->res_k, "results of this shape are not available", IVF_ESTATE);
+    size_t n = (size_t)nq * k;
+    if (dist) ck(cudaMemcpyAsync(dist, b->out_dist, n * sizeof(float), kind, b->st), "results copy");
+    if (idx) ck(cudaMemcpyAsync(idx, b->out_ids, n * sizeof(int32_t), kind, b->st), "results copy");
+    if (idist) ck(cudaMemcpyAsync(idist, b->out_idist, n * sizeof(int32_t), kind, b->st), "results copy");
+}
+
+// ---------------------------------------------------------------------------
+// registry (ivf_search_wrapper.cpp:329-427; a mutex makes it thread-safe)
+// ---------------------------------------------------------------------------
+constexpr int kMaxIndices = 64;
+struct RegEntry {
+    unsigned oid;
+    void* handle;
+    bool active;
+};
+RegEntry g_reg[kMaxIndices];
+std::mutex g_reg_mu;
+
+// ---------------------------------------------------------------------------
+// coarse handle state (stored behind CoarseHandle::cublas_handle)
+// ---------------------------------------------------------------------------
+struct RouteState {
+    int device = 0;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+    BatchCtx* b = nullptr;     // scratch reuse through a private batch context
+    IndexCtx* x = nullptr;     // view of the borrowed centroids
+};
+thread_local CoarseTimingBreakdown g_coarse_timing;
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+void* ivf_create_index_context(void) {
+    try {
+        auto* x = new IndexCtx();
+        cudaGetDevice(&x->device);
+        return x;
+    } catch (...) {
+        g_err = "out of host memory";
+        return nullptr;
+    }
+}
+
+void ivf_destroy_index_context(void* idx_ctx) {
+    if (!idx_ctx) return;
+    auto* x = static_cast<IndexCtx*>(idx_ctx);
+    if (x->magic != kIdxMagic) return;
+    cudaSetDevice(x->device);
+    cudaDeviceSynchronize();
+    x->main.release();
+    x->delta.release();
+    free_all(x->owned);
+    x->magic = 0;
+    delete x;
+}
+
+int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vectors, float* d_cluster_centers,
+                     int n_total_clusters, int n_total_vectors, int n_dim) {
+    int ret = 0;
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return 0;
+    }
+    int st = guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        if (x->kind != kKindEmpty) {
+            ret = 0;
+            return;
+        }
+        require(d_cluster_size && d_cluster_vectors && d_cluster_centers, "null device array");
+        require(n_total_clusters > 0 && n_total_vectors >= 0 && n_dim > 0, "bad sizes");
+        cudaSetDevice(x->device);
+        // ownership passes to the context (ivf_search_separated.cu:141-143)
+        x->owned.push_back(d_cluster_size);
+        x->owned.push_back(d_cluster_vectors);
+        x->cent = d_cluster_centers;
+        x->owned.push_back(d_cluster_centers);
+        x->valid = dalloc<uint8_t>((size_t)n_total_clusters, x->owned);
+        ck(route_centroid_valid(x->cent, n_total_clusters, n_dim, x->valid, 0), "centroid validity");
+        ck(cudaDeviceSynchronize(), "centroid validity");
+        x->nlist = x->nlist_global = n_total_clusters;
+        x->d = n_dim;
+        x->n = n_total_vectors;
+        x->kind = kKindF32;
+        ret = 1;
+    });
+    return st == IVF_OK ? ret : 0;
+}
+
+void* ivf_create_batch_context(int max_n_query, int n_dim, int max_n_probes, int max_k, int n_total_clusters) {
+    BatchCtx* b = nullptr;
+    int st = guarded(nullptr, [&] {
+        require(max_n_query > 0 && n_dim > 0 && max_n_probes > 0 && max_k > 0 && n_total_clusters > 0,
+                "bad batch limits");
+        require(n_dim <= 512, "n_dim > 512 is not supported");
+        b = new BatchCtx();
+        try {
+            cudaGetDevice(&b->device);
+            b->max_nq = max_n_query;
+            b->d = n_dim;
+            b->max_nprobe = max_n_probes;
+            b->max_k = max_k;
+            b->nlist = n_total_clusters;
+            ck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "cudaStreamCreate");
+            b->q = dalloc<float>((size_t)max_n_query * n_dim, b->owned);
+            b->q_u8 = dalloc<uint8_t>((size_t)max_n_query * n_dim, b->owned);
+            b->probes = dalloc<int32_t>((size_t)max_n_query * max_n_probes, b->owned);
+            b->out_ids = dalloc<int32_t>((size_t)max_n_query * max_k, b->owned);
+            b->out_dist = dalloc<float>((size_t)max_n_query * max_k, b->owned);
+            b->out_idist = dalloc<int32_t>((size_t)max_n_query * max_k, b->owned);
+            b->counter = dalloc<int>(4, b->owned);
+            b->overflow = dalloc<int>(4, b->owned);
+            ck(cudaMallocHost(&b->h_overflow, sizeof(int) * 4), "cudaMallocHost");
+            *b->h_overflow = 0;
+        } catch (...) {
+            if (b->st) cudaStreamDestroy(b->st);
+            free_all(b->owned);
+            if (b->h_overflow) cudaFreeHost(b->h_overflow);
+            delete b;
+            b = nullptr;
+            throw;
+        }
+    });
+    return st == IVF_OK ? b : nullptr;
+}
+
+void ivf_destroy_batch_context(void* batch_ctx) {
+    if (!batch_ctx) return;
+    auto* b = static_cast<BatchCtx*>(batch_ctx);
+    if (b->magic != kBatMagic) return;
+    cudaSetDevice(b->device);
+    cudaStreamSynchronize(b->st);
+    Grow* gs[] = {&b->route_dist, &b->wl_cnt, &b->wl_off, &b->wl_cursor, &b->pair_q, &b->pair_l, &b->scan_tmp,
+                  &b->cand_m, &b->cand_d, &b->cnt_m, &b->cnt_d, &b->thr_m, &b->thr_d, &b->s1m, &b->s1d, &b->exk};
+    for (Grow* g : gs)
+        if (g->p) cudaFree(g->p);
+    free_all(b->owned);
+    if (b->h_overflow) cudaFreeHost(b->h_overflow);
+    cudaStreamDestroy(b->st);
+    b->magic = 0;
+    delete b;
+}
+
+void ivf_pipeline_stage1_prepare(void* batch_ctx, float* query_batch_host, int n_query) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return;
+    }
+    guarded(&b->err, [&] {
+        require(query_batch_host != nullptr || n_query == 0, "null query pointer");
+        require(n_query >= 0 && n_query <= b->max_nq, "batch size exceeds capacity");
+        cudaSetDevice(b->device);
+        ck(cudaMemcpyAsync(b->q, query_batch_host, sizeof(float) * (size_t)n_query * b->d, cudaMemcpyHostToDevice,
+                           b->st),
+           "query H2D");
+        b->probes_nq = 0;
+    });
+}
+
+int ivf_pipeline_stage1_prepare_device(void* batch_ctx, const float* d_query, int n_query) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_query != nullptr || n_query == 0, "null query pointer");
+        require(n_query >= 0 && n_query <= b->max_nq, "batch size exceeds capacity");
+        cudaSetDevice(b->device);
+        ck(cudaMemcpyAsync(b->q, d_query, sizeof(float) * (size_t)n_query * b->d, cudaMemcpyDeviceToDevice, b->st),
+           "query D2D");
+        b->probes_nq = 0;
+    });
+}
+
+void ivf_pipeline_stage2_compute(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                                 int distance_mode) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return;
+    }
+    guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        require(distance_mode == IVF_DISTANCE_L2, "only distance_mode 0 (L2) is supported", IVF_EUNSUPPORTED);
+        check_shape(b, x, n_query, n_probes, k);
+        cudaSetDevice(b->device);
+        if (x->kind == kKindF32) fail(IVF_EUNSUPPORTED, "fp32 fine search is outside this library");
+        do_route(b, x, n_query, n_probes, nullptr);
+        if (x->kind == kKindU8) run_u8(b, x, n_query, n_probes, k, nullptr);
+        else run_pq(b, x, n_query, n_probes, k, 512, true, 16, nullptr, nullptr, nullptr, nullptr);
+    });
+}
+
+void ivf_pipeline_get_results(void* batch_ctx, float* topk_dist, int* topk_index, int n_query, int k) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return;
+    }
+    guarded(&b->err, [&] {
+        cudaSetDevice(b->device);
+        copy_results(b, topk_dist, topk_index, nullptr, n_query, k, cudaMemcpyDeviceToHost);
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        check_overflow_after_sync(b);
+    });
+}
+
+int ivf_get_results_i32(void* batch_ctx, int* ids, int* dist, int n_query, int k) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        cudaSetDevice(b->device);
+        copy_results(b, nullptr, ids, dist, n_query, k, cudaMemcpyDeviceToHost);
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        check_overflow_after_sync(b);
+    });
+}
+
+int ivf_get_results_device(void* batch_ctx, float* d_dist, int* d_index, int n_query, int k) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        cudaSetDevice(b->device);
+        copy_results(b, d_dist, d_index, nullptr, n_query, k, cudaMemcpyDeviceToDevice);
+    });
+}
+
+void ivf_pipeline_sync_batch(void* batch_ctx) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return;
+    }
+    guarded(&b->err, [&] {
+        cudaSetDevice(b->device);
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+    });
+}
+
+void* ivf_batch_stream(void* batch_ctx) {
+    auto* b = static_cast<BatchCtx*>(batch_ctx);
+    if (!b || b->magic != kBatMagic) return nullptr;
+    return (void*)b->st;
+}
+
+// ---------------------------------------------------------------------------
+// loading
+// ---------------------------------------------------------------------------
+int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets, const int* counts,
+                const int* reorder_to_original, const float* centroids, int nlist, long long n, int d) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->kind == kKindEmpty, "index context already holds an index", IVF_ESTATE);
+        require(nlist > 0 && n >= 0 && d > 0 && d % 16 == 0 && d <= 512, "need nlist > 0, d % 16 == 0, d <= 512");
+        require(base_u8 != nullptr || n == 0, "null base");
+        cudaSetDevice(x->device);
+        try {
+            load_lists(x, x->main, base_u8, (size_t)d, offsets, counts, reorder_to_original, nullptr, nlist, n);
+            load_centroids(x, centroids, nlist, d);
+        } catch (...) {
+            x->main.release();
+            free_all(x->owned);
+            throw;
+        }
+        x->n = n;
+        x->kind = kKindU8;
+    });
+}
+
+int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, int M, int K, int dsub,
+                const uint8_t* codes, const long long* offsets, const int* counts, const int* reorder_to_original,
+                const uint8_t* base_u8, const float* base_f32, int nlist, long long n, int d) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->kind == kKindEmpty, "index context already holds an index", IVF_ESTATE);
+        require(nlist > 0 && n >= 0 && d > 0 && d <= 512, "bad sizes");
+        require(K == 256, "only K = 256 (8-bit codes) is supported");
+        require(pq_supported_m(M), "M must be a multiple of 8 and <= 64");
+        require(dsub > 0 && M * dsub == d, "M * dsub must equal d");
+        require(codebook && (codes || n == 0), "null codebook or codes");
+        require((base_u8 != nullptr) != (base_f32 != nullptr), "exactly one of base_u8 / base_f32 is required");
+        require(base_f32 ? d % 4 == 0 : d % 16 == 0, "rerank rows need d % 16 == 0 (u8) or d % 4 == 0 (fp32)");
+        cudaSetDevice(x->device);
+        try {
+            load_lists(x, x->main, codes, (size_t)M, offsets, counts, reorder_to_original, nullptr, nlist, n);
+            if (base_u8) x->main.rr_u8 = dcopy(base_u8, (size_t)n * d, x->main.owned);
+            else x->main.rr_f32 = dcopy(base_f32, (size_t)n * d, x->main.owned);
+            load_centroids(x, centroids, nlist, d);
+            x->codebook = dcopy(codebook, (size_t)M * K * dsub, x->owned);
+        } catch (...) {
+            x->main.release();
+            free_all(x->owned);
+            throw;
+        }
+        x->M = M;
+        x->dsub = dsub;
+        x->n = n;
+        x->kind = kKindPQ;
+    });
+}
+
+int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, const long long* key_offsets) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->kind == kKindU8 || x->kind == kKindPQ, "load the shard's lists first", IVF_ESTATE);
+        require(x->l2g == nullptr, "shard mapping already set", IVF_ESTATE);
+        require(nlist_global >= x->nlist && local_to_global, "bad shard mapping");
+        std::vector<int32_t> g2l((size_t)nlist_global, -1);
+        for (int l = 0; l < x->nlist; ++l) {
+            int g = local_to_global[l];
+            require(g >= 0 && g < nlist_global, "global list id out of range");
+            require(l == 0 || g > local_to_global[l - 1], "local lists must be in increasing global order");
+            g2l[(size_t)g] = l;
+        }
+        cudaSetDevice(x->device);
+        x->l2g = dcopy(reinterpret_cast<const int32_t*>(local_to_global), (size_t)x->nlist, x->owned);
+        x->g2l = dcopy(g2l.data(), g2l.size(), x->owned);
+        if (key_offsets)
+            x->main.key_off = dcopy(reinterpret_cast<const int64_t*>(key_offsets), (size_t)x->nlist, x->main.owned);
+        x->nlist_global = nlist_global;
+    });
+}
+
+int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, const int* counts,
+                         const long long* offsets, const long long* key_offsets, const uint8_t* raw_u8,
+                         const float* raw_f32, long long n_delta) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->kind == kKindPQ, "publish needs a residual-PQ index", IVF_ESTATE);
+        require(n_delta >= 0, "negative n_delta");
+        require(ids != nullptr, "delta ids are required");
+        const bool f32 = x->main.rr_f32 != nullptr;
+        require(f32 ? raw_f32 != nullptr : raw_u8 != nullptr, "delta rerank rows must match the base type");
+        cudaSetDevice(x->device);
+        ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // no search may still read the old segment
+        x->delta.release();
+        x->has_delta = false;
+        Segment s;
+        try {
+            load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
+            if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
+            else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
+        } catch (...) {
+            s.release();
+            throw;
+        }
+        x->delta = std::move(s);
+        x->has_delta = n_delta > 0;
+    });
+}
+
+int ivf_pq_clear_delta(void* idx_ctx) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        cudaSetDevice(x->device);
+        ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
+        x->delta.release();
+        x->has_delta = false;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// search
+// ---------------------------------------------------------------------------
+int ivf_route(void* batch_ctx, void* idx_ctx, int n_query, int n_probes) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, 1);
+        cudaSetDevice(b->device);
+        do_route(b, x, n_query, n_probes, nullptr);
+    });
+}
+
+int ivf_set_probes(void* batch_ctx, const int* h_probes, int n_query, int n_probes) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(h_probes != nullptr, "null probes");
+        require(n_query >= 0 && n_query <= b->max_nq && n_probes > 0 && n_probes <= b->max_nprobe,
+                "probe table shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        ck(cudaMemcpyAsync(b->probes, h_probes, sizeof(int32_t) * (size_t)n_query * n_probes,
+                           cudaMemcpyHostToDevice, b->st),
+           "probes H2D");
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        b->probes_nq = n_query;
+        b->probes_np = n_probes;
+    });
+}
+
+int ivf_get_probes(void* batch_ctx, int* h_probes, int n_query, int n_probes) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(h_probes != nullptr, "null probes");
+        require_probes(b, n_query, n_probes);
+        cudaSetDevice(b->device);
+        ck(cudaMemcpyAsync(h_probes, b->probes, sizeof(int32_t) * (size_t)n_query * n_probes,
+                           cudaMemcpyDeviceToHost, b->st),
+           "probes D2H");
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+    });
+}
+
+int ivf_u8_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k, int route) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, k);
+        cudaSetDevice(b->device);
+        if (route) do_route(b, x, n_query, n_probes, nullptr);
+        run_u8(b, x, n_query, n_probes, k, nullptr);
+    });
+}
+
+int ivf_pq_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k, int rerank_n, int use_overlay,
+                  int delta_topk, int route) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, k);
+        require(rerank_n > 0, "rerank_n must be > 0");
+        require(delta_topk >= 0, "delta_topk must be >= 0");
+        cudaSetDevice(b->device);
+        if (route) do_route(b, x, n_query, n_probes, nullptr);
+        run_pq(b, x, n_query, n_probes, k, rerank_n, use_overlay != 0, delta_topk, nullptr, nullptr, nullptr,
+               nullptr);
+    });
+}
+
+int ivf_route_keys(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, unsigned long long* d_keys) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, 1);
+        require(d_keys != nullptr, "null key output");
+        cudaSetDevice(b->device);
+        do_route(b, x, n_query, n_probes, reinterpret_cast<uint64_t*>(d_keys));
+    });
+}
+
+int ivf_route_merge(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int n_probes) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_keys != nullptr && n_in > 0, "bad key input");
+        require(n_query >= 0 && n_query <= b->max_nq && n_probes > 0 && n_probes <= b->max_nprobe,
+                "shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        ck(merge_keys(reinterpret_cast<const uint64_t*>(d_keys), n_query, n_in, n_probes, 0, b->probes, nullptr,
+                      nullptr, b->st),
+           "merge_keys");
+        b->probes_nq = n_query;
+        b->probes_np = n_probes;
+    });
+}
+
+int ivf_pq_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n, int delta_topk,
+                        unsigned long long* d_adc, unsigned long long* d_exact, unsigned long long* d_dadc,
+                        unsigned long long* d_dexact) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, 1);
+        require(d_adc && d_exact && rerank_n > 0, "adc and exact outputs are required");
+        require(!d_dadc == !d_dexact, "give both or neither delta outputs");
+        cudaSetDevice(b->device);
+        run_pq(b, x, n_query, n_probes, 1, rerank_n, d_dadc != nullptr, d_dadc ? delta_topk : 0,
+               reinterpret_cast<uint64_t*>(d_adc), reinterpret_cast<uint64_t*>(d_exact),
+               reinterpret_cast<uint64_t*>(d_dadc), reinterpret_cast<uint64_t*>(d_dexact));
+    });
+}
+
+int ivf_pq_merge_shards(void* batch_ctx, const unsigned long long* d_adc, const unsigned long long* d_exact,
+                        int n_main, int rerank_n, const unsigned long long* d_dadc,
+                        const unsigned long long* d_dexact, int n_delta, int delta_topk, int n_query, int k,
+                        int exact_is_int) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_adc && d_exact && n_main > 0 && rerank_n > 0, "bad main inputs");
+        require(n_query >= 0 && n_query <= b->max_nq && k > 0 && k <= b->max_k, "shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        ck(pq_merge_shards(reinterpret_cast<const uint64_t*>(d_adc), reinterpret_cast<const uint64_t*>(d_exact),
+                           n_main, rerank_n, reinterpret_cast<const uint64_t*>(d_dadc),
+                           reinterpret_cast<const uint64_t*>(d_dexact), d_dadc ? n_delta : 0,
+                           d_dadc ? delta_topk : 0, n_query, k, exact_is_int, b->out_ids, b->out_dist, b->st),
+           "pq_merge_shards");
+        b->res_nq = n_query;
+        b->res_k = k;
+    });
+}
+
+int ivf_u8_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                        unsigned long long* d_keys) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, k);
+        require(d_keys != nullptr, "null key output");
+        cudaSetDevice(b->device);
+        run_u8(b, x, n_query, n_probes, k, reinterpret_cast<uint64_t*>(d_keys));
+    });
+}
+
+int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int k) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_keys != nullptr && n_in > 0, "bad key input");
+        require(n_query >= 0 && n_query <= b->max_nq && k > 0 && k <= b->max_k, "shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        ck(merge_keys(reinterpret_cast<const uint64_t*>(d_keys), n_query, n_in, k, 1, b->out_ids, b->out_dist,
+                      b->out_idist, b->st),
+           "merge_keys");
+        b->res_nq = n_query;
+        b->res_k = k;
+    });
+}
+
+const char* ivf_last_error(void* ctx) {
+    std::string* e = err_of(ctx);
+    return e ? e->c_str() : "not a context";
+}
+
+const char* ivf_global_last_error(void) { return g_err.c_str(); }
+
+// ---------------------------------------------------------------------------
+// *_wrapper exports (ivf_search_wrapper.cpp:85-321) and the registry
+// ---------------------------------------------------------------------------
+void* ivf_create_index_context_wrapper(void) { return ivf_create_index_context(); }
+void ivf_destroy_index_context_wrapper(void* idx_ctx) { ivf_destroy_index_context(idx_ctx); }
+int ivf_load_dataset_wrapper(void* idx_ctx, int* d_cluster_size, float* d_cluster_vectors, float* d_cluster_centers,
+                             int n_total_clusters, int n_total_vectors, int n_dim) {
+    auto* x = static_cast<IndexCtx*>(idx_ctx);
+    if (!x || x->magic != kIdxMagic) return -1;
+    int r = ivf_load_dataset(idx_ctx, d_cluster_size, d_cluster_vectors, d_cluster_centers, n_total_clusters,
+                             n_total_vectors, n_dim);
+    return (r == 0 && !x->err.empty()) ? -1 : r;
+}
+void* ivf_create_batch_context_wrapper(int max_n_query, int n_dim, int max_n_probes, int max_k, int n_total_clusters) {
+    return ivf_create_batch_context(max_n_query, n_dim, max_n_probes, max_k, n_total_clusters);
+}
+void ivf_destroy_batch_context_wrapper(void* batch_ctx) { ivf_destroy_batch_context(batch_ctx); }
+void ivf_pipeline_stage1_prepare_wrapper(void* batch_ctx, float* q, int n_query) {
+    ivf_pipeline_stage1_prepare(batch_ctx, q, n_query);
+}
+void ivf_pipeline_stage2_compute_wrapper(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
+                                         int distance_mode) {
+    ivf_pipeline_stage2_compute(batch_ctx, idx_ctx, n_query, n_probes, k, distance_mode);
+}
+void ivf_pipeline_get_results_wrapper(void* batch_ctx, float* topk_dist, int* topk_index, int n_query, int k) {
+    ivf_pipeline_get_results(batch_ctx, topk_dist, topk_index, n_query, k);
+}
+void ivf_pipeline_sync_batch_wrapper(void* batch_ctx) { ivf_pipeline_sync_batch(batch_ctx); }
+int ivf_check_index_initialized_wrapper(void* idx_ctx) {
+    auto* x = static_cast<IndexCtx*>(idx_ctx);
+    if (!x || x->magic != kIdxMagic) return 0;
+    return x->kind != kKindEmpty ? 1 : 0;
+}
+
+void ivf_register_index_instance(unsigned int index_oid, void* gpu_handle) {
+    if (!gpu_handle) return;
+    void* old = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_reg_mu);
+        for (auto& e : g_reg)
+            if (e.active && e.oid == index_oid) {
+                old = e.handle == gpu_handle ? nullptr : e.handle;
+                e.handle = gpu_handle;
+                goto done;
+            }
+        for (auto& e : g_reg)
+            if (!e.active) {
+                e = RegEntry{index_oid, gpu_handle, true};
+                goto done;
+            }
+        g_err = "index registry full (64 entries)";
+    done:;
+    }
+    if (old) ivf_destroy_index_context(old);
+}
+
+void* ivf_get_index_instance(unsigned int index_oid) {
+    std::lock_guard<std::mutex> lk(g_reg_mu);
+    for (auto& e : g_reg)
+        if (e.active && e.oid == index_oid) return e.handle;
+    return nullptr;
+}
+
+void ivf_unregister_index_instance(unsigned int index_oid) {
+    void* old = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_reg_mu);
+        for (auto& e : g_reg)
+            if (e.active && e.oid == index_oid) {
+                old = e.handle;
+                e = RegEntry{0, nullptr, false};
+                break;
+            }
+    }
+    if (old) ivf_destroy_index_context(old);
+}
+
+// ---------------------------------------------------------------------------
+// coarse handle (cpu_fine.h:232-278)
+// ---------------------------------------------------------------------------
+void coarse_handle_init(CoarseHandle* h, const float* d_centers, int n_total_clusters, int dim) {
+    if (!h) return;
+    std::memset(h, 0, sizeof(*h));
+    guarded(nullptr, [&] {
+        require(d_centers && n_total_clusters > 0 && dim > 0 && dim <= 512, "bad coarse handle arguments");
+        auto* rs = new RouteState();
+        try {
+            cudaGetDevice(&rs->device);
+            rs->x = new IndexCtx();
+            rs->x->device = rs->device;
+            rs->x->cent = const_cast<float*>(d_centers);  // borrowed, never freed
+            rs->x->valid = dalloc<uint8_t>((size_t)n_total_clusters, rs->x->owned);
+            ck(route_centroid_valid(d_centers, n_total_clusters, dim, rs->x->valid, 0), "centroid validity");
+            ck(cudaDeviceSynchronize(), "centroid validity");
+            rs->x->nlist = rs->x->nlist_global = n_total_clusters;
+            rs->x->d = dim;
+            rs->x->kind = kKindF32;
+            for (auto& e : rs->ev) ck(cudaEventCreate(&e), "cudaEventCreate");
+        } catch (...) {
+            if (rs->x) {
+                free_all(rs->x->owned);
+                delete rs->x;
+            }
+            delete rs;
+            throw;
+        }
+        h->d_centers = d_centers;
+        h->d_centers_norm = reinterpret_cast<float*>(rs->x->valid);
+        h->cublas_handle = rs;
+        h->n_total_clusters = n_total_clusters;
+        h->dim = dim;
+        h->distance_mode_cached = IVF_DISTANCE_L2;
+    });
+}
+
+void coarse_handle_release(CoarseHandle* h) {
+    if (!h || !h->cublas_handle) return;
+    auto* rs = static_cast<RouteState*>(h->cublas_handle);
+    cudaSetDevice(rs->device);
+    if (rs->b) ivf_destroy_batch_context(rs->b);
+    for (auto& e : rs->ev)
+        if (e) cudaEventDestroy(e);
+    free_all(rs->x->owned);
+    rs->x->magic = 0;
+    delete rs->x;
+    delete rs;
+    std::memset(h, 0, sizeof(*h));
+}
+
+void coarse_search(const CoarseHandle* h, const float* h_query, int n_query_batch, int n_probes, int distance_mode,
+                   int* h_cluster_ids_out, double* out_coarse_ms, double* out_h2d_ms, double* out_d2h_ms) {
+    g_coarse_timing = CoarseTimingBreakdown{};
+    guarded(nullptr, [&] {
+        require(h && h->cublas_handle, "invalid coarse handle");
+        require(distance_mode == IVF_DISTANCE_L2, "only distance_mode 0 (L2) is supported", IVF_EUNSUPPORTED);
+        require(n_query_batch > 0 && n_probes > 0 && n_probes <= h->n_total_clusters,
+                "bad args: need n_query > 0 and 0 < n_probes <= n_total_clusters");
+        require(h_query && h_cluster_ids_out, "null host pointer");
+        auto* rs = static_cast<RouteState*>(h->cublas_handle);
+        cudaSetDevice(rs->device);
+        if (!rs->b || rs->b->max_nq < n_query_batch || rs->b->max_nprobe < n_probes) {
+            if (rs->b) ivf_destroy_batch_context(rs->b);
+            rs->b = static_cast<BatchCtx*>(ivf_create_batch_context(
+                std::max(n_query_batch, rs->b ? rs->b->max_nq : 0), h->dim,
+                std::max(n_probes, rs->b ? rs->b->max_nprobe : 0), 1, h->n_total_clusters));
+            require(rs->b != nullptr, "batch scratch allocation failed: " + g_err, IVF_ENOMEM);
+        }
+        BatchCtx* b = rs->b;
+        ck(cudaEventRecord(rs->ev[0], b->st), "event");
+        ck(cudaMemcpyAsync(b->q, h_query, sizeof(float) * (size_t)n_query_batch * h->dim, cudaMemcpyHostToDevice,
+                           b->st),
+           "query H2D");
+        ck(cudaEventRecord(rs->ev[1], b->st), "event");
+        do_route(b, rs->x, n_query_batch, n_probes, nullptr);
+        ck(cudaEventRecord(rs->ev[2], b->st), "event");
+        ck(cudaMemcpyAsync(h_cluster_ids_out, b->probes, sizeof(int32_t) * (size_t)n_query_batch * n_probes,
+                           cudaMemcpyDeviceToHost, b->st),
+           "ids D2H");
+        ck(cudaEventRecord(rs->ev[3], b->st), "event");
+        ck(cudaEventSynchronize(rs->ev[3]), "cudaEventSynchronize");
+        float t01 = 0, t12 = 0, t23 = 0, t03 = 0;
+        cudaEventElapsedTime(&t01, rs->ev[0], rs->ev[1]);
+        cudaEventElapsedTime(&t12, rs->ev[1], rs->ev[2]);
+        cudaEventElapsedTime(&t23, rs->ev[2], rs->ev[3]);
+        cudaEventElapsedTime(&t03, rs->ev[0], rs->ev[3]);
+        g_coarse_timing.query_h2d_ms = t01;
+        g_coarse_timing.topk_ms = t12;
+        g_coarse_timing.coarse_compute_ms = t12;
+        g_coarse_timing.cluster_d2h_ms = t23;
+        g_coarse_timing.coarse_total_ms = t03;
+        if (out_coarse_ms) *out_coarse_ms = t12;
+        if (out_h2d_ms) *out_h2d_ms = t01;
+        if (out_d2h_ms) *out_d2h_ms = t23;
+    });
+}
+
+const CoarseTimingBreakdown* coarse_get_last_timing(void) { return &g_coarse_timing; }
+
+}  // extern "C"

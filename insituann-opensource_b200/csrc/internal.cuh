@@ -1,0 +1,190 @@
+// internal.cuh -- device-side building blocks shared by the hot-path kernels.
+//
+// Every ranking in this library is a total order on 64-bit keys
+//     key = (distance bits << 32) | id
+// where the distance is a non-negative float (IEEE bits are then monotone) or a
+// non-negative int32, and the id is a list id, a cluster-major position or an
+// original vector id.  Ties between equal distances therefore go to the
+// smaller id, independent of thread schedule, which is what makes the GPU
+// results bit-identical to the CPU restatement.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace isb {
+
+constexpr int kCodes = 256;          // centroids per PQ sub-quantizer (8-bit codes)
+constexpr uint64_t kKeyNone = ~0ull; // empty slot / "no bound yet"
+
+__device__ __forceinline__ uint64_t make_key(uint32_t hi, uint32_t lo) {
+    return ((uint64_t)hi << 32) | (uint64_t)lo;
+}
+__device__ __forceinline__ uint32_t key_hi(uint64_t k) { return (uint32_t)(k >> 32); }
+__device__ __forceinline__ uint32_t key_lo(uint64_t k) { return (uint32_t)k; }
+
+// ---------------------------------------------------------------------------
+// warp / block reductions and scans
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ int warp_incl_scan(int v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        int t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+    }
+    return v;
+}
+
+__device__ __forceinline__ int warp_sum(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Exclusive block scan of one int per thread.  scratch: >= 33 ints.
+// Returns the exclusive prefix; *total receives the block total.
+template <int T>
+__device__ __forceinline__ int block_excl_scan(int v, int* scratch, int* total) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int W = T / 32;
+    int incl = warp_incl_scan(v);
+    if (lane == 31) scratch[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = lane < W ? scratch[lane] : 0;
+        int wi = warp_incl_scan(w);
+        if (lane < W) scratch[lane] = wi - w;
+        if (lane == W - 1) scratch[32] = wi;
+    }
+    __syncthreads();
+    int r = scratch[warp] + incl - v;
+    *total = scratch[32];
+    __syncthreads();
+    return r;
+}
+
+template <int T>
+__device__ __forceinline__ int block_sum(int v, int* scratch) {
+    int tot;
+    (void)block_excl_scan<T>(v, scratch, &tot);
+    return tot;
+}
+
+// ---------------------------------------------------------------------------
+// Radix selection of the need-th smallest 64-bit key (1-based) among the keys
+// k(i), i < n, with k(i) <= upper.  The caller guarantees at least `need`
+// participants.  Returns kappa such that exactly `need` participants satisfy
+// key <= min(kappa, upper) when keys are distinct; when several participants
+// share the final key, returns that key (the caller takes copies as needed).
+// 8 bits per pass from the most significant byte, early exit as soon as the
+// bucket that holds the need-th key is needed in full.
+// hist: 256 ints of shared memory; bc: 4 ints of shared memory.
+// ---------------------------------------------------------------------------
+template <int T, class KeyFn>
+__device__ uint64_t block_kth_key(KeyFn keyf, int n, int need, uint64_t upper, int* hist, int* bc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint64_t prefix = 0, mask = 0;
+    for (int shift = 56; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += T) hist[b] = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += T) {
+            uint64_t k = keyf(i);
+            if (k <= upper && (k & mask) == prefix) atomicAdd(&hist[(int)((k >> shift) & 255u)], 1);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int loc[8];
+            int s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                loc[j] = hist[lane * 8 + j];
+                s += loc[j];
+            }
+            int incl = warp_incl_scan(s);
+            int excl = incl - s;
+            unsigned ball = __ballot_sync(0xffffffffu, incl >= need);
+            int src = __ffs(ball) - 1;
+            if (lane == src) {
+                int acc = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (acc + loc[j] >= need) {
+                        bc[0] = lane * 8 + j;
+                        bc[1] = acc;
+                        bc[2] = loc[j];
+                        break;
+                    }
+                    acc += loc[j];
+                }
+            }
+        }
+        __syncthreads();
+        const int b = bc[0], below = bc[1], cnt = bc[2];
+        __syncthreads();
+        need -= below;
+        prefix |= (uint64_t)b << shift;
+        mask |= (uint64_t)0xFFu << shift;
+        if (cnt == need) return prefix | ~mask;
+    }
+    return prefix;
+}
+
+// ---------------------------------------------------------------------------
+// In-place ascending bitonic sort of n (power of two) keys in shared memory.
+// ---------------------------------------------------------------------------
+template <int T>
+__device__ void block_bitonic_sort(uint64_t* s, int n) {
+    for (int size = 2; size <= n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < n / 2; i += T) {
+                int lo = 2 * i - (i & (stride - 1));
+                int hi = lo + stride;
+                bool asc = ((lo & size) == 0);
+                uint64_t a = s[lo], b = s[hi];
+                if ((a > b) == asc) {
+                    s[lo] = b;
+                    s[hi] = a;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// ---------------------------------------------------------------------------
+// device views of the index
+// ---------------------------------------------------------------------------
+struct ListStore {             // one cluster-major segment (main index or a delta)
+    const uint8_t* data;       // PQ codes [n, M] or uint8 vectors [n, d]
+    const int64_t* offsets;    // [nlist] first position of each list
+    const int32_t* counts;     // [nlist] vectors per list
+    const int32_t* ids;        // [n] id reported for each position (nullptr: the position)
+    const int64_t* key_off;    // [nlist] position of each list's first vector inside ranking
+                               // keys (nullptr: offsets); a shard of a larger index ranks by
+                               // the positions of the whole index so shards merge exactly
+    const uint8_t* rr_u8;      // [n, d] rerank rows (u8), PQ only
+    const float* rr_f32;       // [n, d] rerank rows (fp32), PQ only
+    int64_t n;
+};
+
+struct WorkList {              // probe inversion for one batch: list-major (query, list) pairs
+    int32_t* list_cnt;         // [nlist]   pairs per list
+    int32_t* list_off;         // [nlist+1] exclusive prefix of list_cnt
+    int32_t* cursor;           // [nlist]   fill cursors
+    int32_t* pair_q;           // [max_pairs] query of each pair
+    int32_t* pair_l;           // [max_pairs] (local) list of each pair
+    int32_t* n_pairs;          // -> list_off[nlist]
+};
+
+struct CandBuf {               // per-query candidate buffers of one segment
+    uint64_t* keys;            // [nq, cap]
+    int32_t* cnt;              // [nq]
+    unsigned long long* thr;   // [nq] running upper bound of the rank-R key
+    int32_t* overflow;         // set when a query's buffer would overflow
+    int cap;
+    int R;                     // rank budget (rerank_n or delta top-k)
+};
+
+}  // namespace isb

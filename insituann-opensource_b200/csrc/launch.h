@@ -1,0 +1,80 @@
+// launch.h -- host-side launchers of the hot-path kernels (internal to the library).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "internal.cuh"
+
+namespace isb {
+
+constexpr int kPQScanChunk = 2048;    // vectors per filtered chunk in the PQ scan
+constexpr int kExactScanChunk = 1024; // vectors per filtered chunk in the exact scan
+
+// ---- probe inversion (worklist.cu) ----------------------------------------
+// Scratch for the device-wide scan; query with bytes=0 first.
+size_t worklist_scan_bytes(int nlist);
+// Builds list-major (query, list) pairs from probes [nq, nprobe] (global list
+// ids; list_map maps them to local lists or -1, nullptr = identity).
+cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
+                           const int32_t* list_map, int nlist_local, WorkList wl,
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st);
+
+// ---- coarse routing (route.cu) --------------------------------------------
+// valid[c] = 1 when the centroid's L2 norm is >= 1e-6, else 0.
+cudaError_t route_centroid_valid(const float* cent, int nlist, int d, uint8_t* valid, cudaStream_t st);
+// Exact fp32 squared L2 of every (query, centroid) pair as sortable bits
+// (0xFFFFFFFF for centroids that are not valid): out [nq, nlist].
+cudaError_t route_distances(const float* q, int nq, const float* cent, const uint8_t* valid,
+                            int nlist, int d, uint32_t* out, cudaStream_t st);
+// Top-L (dist, id) per row of dist_bits [nq, n] -> ids [nq, L] (+ dist [nq, L] and/or
+// sorted keys [nq, L], each optional).  Column c has id id_map[c] (nullptr: c).
+cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const int32_t* id_map,
+                         int32_t* out_ids, float* out_dist, uint64_t* out_keys, cudaStream_t st);
+// Top-L of n keys per query [nq, n] -> ids [nq, L]; distances as float bits
+// (int_dist = 0) or as int32 (int_dist = 1, written to out_idist and out_dist).
+cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist, int32_t* out_ids,
+                       float* out_dist, int32_t* out_idist, cudaStream_t st);
+// out[i] = clamp(round(q[i]), 0, 255) (updates/exact_update.cu:410-418)
+cudaError_t make_query_u8(const float* q, size_t n, uint8_t* out, cudaStream_t st);
+
+// ---- candidate selection (select.cu) ---------------------------------------
+cudaError_t reset_candidates(CandBuf cb, int nq, cudaStream_t st);
+// Sorted top-R keys per query from a candidate buffer -> out [nq, R] (padding ~0).
+cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st);
+// Sorted exact keys -> (ids, int32 distances): for the exact path.
+cudaError_t keys_to_exact_results(const uint64_t* keys, int nq, int k, int32_t* ids, int32_t* dist,
+                                  float* fdist, cudaStream_t st);
+
+// ---- exact uint8 fine search (exact.cu) -------------------------------------
+cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkList wl, int max_pairs,
+                       CandBuf cb, int* work_counter, cudaStream_t st);
+
+// ---- residual PQ (pq.cu) -----------------------------------------------------
+struct PQParams {
+    const float* q;          // [nq, d] fp32 queries
+    const float* cent;       // [nlist, d]
+    const float* codebook;   // [M, 256, dsub]
+    int d, M, dsub;
+    ListStore main;
+    ListStore delta;
+    int has_delta;
+};
+bool pq_supported_m(int M);
+cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* work_counter,
+                    cudaStream_t st);
+// Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).
+// When out_exact_main is given, the per-candidate exact keys are written instead
+// of (ids, dist) being selected: [nq, R] and [nq, Rd] aligned with the inputs.
+cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int R, const uint64_t* s1_delta,
+                      int Rd, int nq, int k, int32_t* out_ids, float* out_dist, uint64_t* out_exact_main,
+                      uint64_t* out_exact_delta, cudaStream_t st);
+// Final merge of sharded stage-1 results: per query, G shards each give R
+// (ADC key, exact key) pairs for the main segment and Rd for the delta.
+cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main, int n_main, int R,
+                            const uint64_t* adc_delta, const uint64_t* exact_delta, int n_delta, int Rd,
+                            int nq, int k, int exact_is_int, int32_t* out_ids, float* out_dist,
+                            cudaStream_t st);
+
+}  // namespace isb

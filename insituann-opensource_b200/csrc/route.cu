@@ -1,0 +1,199 @@
+// route.cu -- coarse routing: top-nprobe inverted lists per query by L2.
+//
+// Reference behaviour (cuda/search/cpu_fine/ivf_search_cpu_fine.cu:764-1361 and
+// cuda/search/coarse/fusion_l2_topk_warpsort.cu:61-157): L2 from
+// ||q||^2 + ||c||^2 - 2 q.c with cuBLAS SGEMM, centroids whose norm is below
+// 1e-6 skipped, warp top-k.  Its tie order and rounding depend on cuBLAS.
+// This library defines routing as the exact fp32 direct-difference distance
+// sum_j (q_j - c_j)^2 accumulated in j order without contraction, ranked by
+// (distance, list id), so every probe list is reproducible bit for bit on
+// the CPU.
+#include "launch.h"
+
+namespace isb {
+
+namespace {
+
+__global__ void centroid_valid_kernel(const float* __restrict__ cent, int nlist, int d, uint8_t* valid) {
+    int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= nlist) return;
+    const float* row = cent + (size_t)c * d;
+    float s = 0.f;
+    for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(row[j], row[j]));
+    valid[c] = (sqrtf(s) >= 1e-6f) ? 1 : 0;
+}
+
+// 64 queries x 64 centroids per CTA, 256 threads, 4x4 pairs per thread,
+// 32 dimensions staged per step.  Zero padding beyond d adds exact zeros.
+constexpr int kRB = 64, kRK = 32;
+
+__global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict__ q, int nq,
+                                                         const float* __restrict__ cent,
+                                                         const uint8_t* __restrict__ valid, int nlist,
+                                                         int d, uint32_t* __restrict__ out) {
+    __shared__ float sq[kRK][kRB + 4];
+    __shared__ float sc[kRK][kRB + 4];
+    const int tid = threadIdx.x;
+    const int tx = tid & 15, ty = tid >> 4;
+    const int q0 = blockIdx.y * kRB, c0 = blockIdx.x * kRB;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+
+    for (int k0 = 0; k0 < d; k0 += kRK) {
+        for (int e = tid; e < kRB * kRK; e += 256) {
+            int r = e / kRK, kk = e % kRK;
+            int qi = q0 + r, ci = c0 + r, j = k0 + kk;
+            sq[kk][r] = (qi < nq && j < d) ? q[(size_t)qi * d + j] : 0.f;
+            sc[kk][r] = (ci < nlist && j < d) ? cent[(size_t)ci * d + j] : 0.f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < kRK; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = sq[kk][ty * 4 + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = sc[kk][tx * 4 + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float x = __fsub_rn(a[i], b[j]);
+                    acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(x, x));
+                }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        int qi = q0 + ty * 4 + i;
+        if (qi >= nq) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            int ci = c0 + tx * 4 + j;
+            if (ci >= nlist) continue;
+            out[(size_t)qi * nlist + ci] = valid[ci] ? __float_as_uint(acc[i][j]) : 0xFFFFFFFFu;
+        }
+    }
+}
+
+constexpr int kSelT = 512;
+constexpr int kSelMaxL = 2048;
+
+// One CTA per row: keys (dist bits, column) of the row, top-L sorted.
+template <class KeyFn>
+__device__ void select_row_topl(KeyFn keyf, int n, int L, uint64_t* s, int* hist, int* bc, int* s_cnt) {
+    const int tid = threadIdx.x;
+    int Lp = 1;
+    while (Lp < L) Lp <<= 1;
+    int take = n < L ? n : L;
+    if (n <= L) {
+        for (int i = tid; i < Lp; i += kSelT) s[i] = i < n ? keyf(i) : kKeyNone;
+    } else {
+        uint64_t kap = block_kth_key<kSelT>(keyf, n, L, kKeyNone, hist, bc);
+        if (tid == 0) *s_cnt = 0;
+        __syncthreads();
+        for (int i = tid; i < n; i += kSelT) {
+            uint64_t k = keyf(i);
+            if (k < kap) s[atomicAdd(s_cnt, 1)] = k;
+        }
+        __syncthreads();
+        int cl = *s_cnt;
+        for (int i = cl + tid; i < Lp; i += kSelT) s[i] = i < take ? kap : kKeyNone;
+    }
+    block_bitonic_sort<kSelT>(s, Lp);
+}
+
+__global__ void __launch_bounds__(kSelT) route_select_kernel(const uint32_t* __restrict__ dist_bits, int n, int L,
+                                                             const int32_t* __restrict__ id_map, int32_t* out_ids,
+                                                             float* out_dist, uint64_t* out_keys) {
+    __shared__ uint64_t s[kSelMaxL];
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ int s_cnt;
+    const int row = blockIdx.x;
+    const uint32_t* r = dist_bits + (size_t)row * n;
+    auto keyf = [&](int i) -> uint64_t { return make_key(r[i], id_map ? (uint32_t)id_map[i] : (uint32_t)i); };
+    select_row_topl(keyf, n, L, s, hist, bc, &s_cnt);
+    for (int i = threadIdx.x; i < L; i += kSelT) {
+        uint64_t k = s[i];
+        bool ok = k != kKeyNone && key_hi(k) != 0xFFFFFFFFu;
+        if (out_ids) out_ids[(size_t)row * L + i] = ok ? (int32_t)key_lo(k) : -1;
+        if (out_dist) out_dist[(size_t)row * L + i] = ok ? __uint_as_float(key_hi(k)) : __int_as_float(0x7f800000);
+        if (out_keys) out_keys[(size_t)row * L + i] = k;
+    }
+}
+
+__global__ void __launch_bounds__(kSelT) merge_keys_kernel(const uint64_t* __restrict__ keys, int n, int L,
+                                                           int int_dist, int32_t* out_ids, float* out_dist,
+                                                           int32_t* out_idist) {
+    __shared__ uint64_t s[kSelMaxL];
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ int s_cnt;
+    const int row = blockIdx.x;
+    const uint64_t* r = keys + (size_t)row * n;
+    auto keyf = [&](int i) -> uint64_t { return r[i]; };
+    select_row_topl(keyf, n, L, s, hist, bc, &s_cnt);
+    for (int i = threadIdx.x; i < L; i += kSelT) {
+        uint64_t k = s[i];
+        bool ok = k != kKeyNone && key_hi(k) != 0xFFFFFFFFu;
+        out_ids[(size_t)row * L + i] = ok ? (int32_t)key_lo(k) : -1;
+        if (out_dist) {
+            float f = int_dist ? (float)key_hi(k) : __uint_as_float(key_hi(k));
+            out_dist[(size_t)row * L + i] = ok ? f : __int_as_float(0x7f800000);
+        }
+        if (out_idist) out_idist[(size_t)row * L + i] = ok ? (int32_t)key_hi(k) : 0x7fffffff;
+    }
+}
+
+__global__ void make_u8_kernel(const float* __restrict__ q, size_t n, uint8_t* __restrict__ out) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float x = fminf(fmaxf(q[i], 0.f), 255.f);
+        out[i] = (uint8_t)lroundf(x);
+    }
+}
+
+}  // namespace
+
+cudaError_t route_centroid_valid(const float* cent, int nlist, int d, uint8_t* valid, cudaStream_t st) {
+    centroid_valid_kernel<<<(nlist + 255) / 256, 256, 0, st>>>(cent, nlist, d, valid);
+    return cudaGetLastError();
+}
+
+cudaError_t route_distances(const float* q, int nq, const float* cent, const uint8_t* valid, int nlist, int d,
+                            uint32_t* out, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    dim3 grid((nlist + kRB - 1) / kRB, (nq + kRB - 1) / kRB);
+    route_dist_kernel<<<grid, 256, 0, st>>>(q, nq, cent, valid, nlist, d, out);
+    return cudaGetLastError();
+}
+
+cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const int32_t* id_map, int32_t* out_ids,
+                         float* out_dist, uint64_t* out_keys, cudaStream_t st) {
+    if (L > kSelMaxL || L <= 0) return cudaErrorInvalidValue;
+    if (nq <= 0) return cudaSuccess;
+    route_select_kernel<<<nq, kSelT, 0, st>>>(dist_bits, n, L, id_map, out_ids, out_dist, out_keys);
+    return cudaGetLastError();
+}
+
+cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist, int32_t* out_ids, float* out_dist,
+                       int32_t* out_idist, cudaStream_t st) {
+    if (L > kSelMaxL || L <= 0) return cudaErrorInvalidValue;
+    if (nq <= 0) return cudaSuccess;
+    merge_keys_kernel<<<nq, kSelT, 0, st>>>(keys, n, L, int_dist, out_ids, out_dist, out_idist);
+    return cudaGetLastError();
+}
+
+cudaError_t make_query_u8(const float* q, size_t n, uint8_t* out, cudaStream_t st) {
+    if (n == 0) return cudaSuccess;
+    size_t blocks = (n + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    make_u8_kernel<<<(int)blocks, 256, 0, st>>>(q, n, out);
+    return cudaGetLastError();
+}
+
+}  // namespace isb

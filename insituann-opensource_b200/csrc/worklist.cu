@@ -1,0 +1,84 @@
+// worklist.cu -- query -> list inversion built entirely on the device.
+//
+// The reference builds (query, list, chunk) descriptors with three CUB scans
+// and a host read-back after each (updates/pq_update.cu:181-244, 907-936) and,
+// on the CPU path, a per-batch hash map of touched clusters
+// (cpu_fine_kernels_v3_u8.cpp:373-403).  Here one count pass, one device
+// scan and one fill pass produce list-major (query, list) pairs with no host
+// round trip; the scan kernels then pull pairs from a global counter.
+#include <cub/device/device_scan.cuh>
+
+#include "launch.h"
+
+namespace isb {
+
+namespace {
+
+__device__ __forceinline__ int local_list(const int32_t* probes, size_t i, int nlist_global,
+                                          const int32_t* list_map) {
+    int g = probes[i];
+    if (g < 0 || g >= nlist_global) return -1;
+    return list_map ? list_map[g] : g;
+}
+
+__global__ void count_pairs_kernel(const int32_t* probes, size_t total, int nlist_global,
+                                   const int32_t* list_map, int32_t* list_cnt) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        int l = local_list(probes, i, nlist_global, list_map);
+        if (l >= 0) atomicAdd(&list_cnt[l], 1);
+    }
+}
+
+__global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprobe, int nlist_global,
+                                  const int32_t* list_map, const int32_t* list_off, int32_t* cursor,
+                                  int32_t* pair_q, int32_t* pair_l) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
+         i += (size_t)gridDim.x * blockDim.x) {
+        int l = local_list(probes, i, nlist_global, list_map);
+        if (l < 0) continue;
+        int slot = atomicAdd(&cursor[l], 1);
+        int p = list_off[l] + slot;
+        pair_q[p] = (int32_t)(i / (size_t)nprobe);
+        pair_l[p] = l;
+    }
+}
+
+int grid_for(size_t total, int threads) {
+    size_t b = (total + threads - 1) / threads;
+    if (b < 1) b = 1;
+    if (b > 148 * 16) b = 148 * 16;
+    return (int)b;
+}
+
+}  // namespace
+
+size_t worklist_scan_bytes(int nlist) {
+    size_t bytes = 0;
+    cub::DeviceScan::ExclusiveSum(nullptr, bytes, (int32_t*)nullptr, (int32_t*)nullptr, nlist + 1);
+    return bytes;
+}
+
+cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
+                           const int32_t* list_map, int nlist_local, WorkList wl,
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st) {
+    cudaError_t e;
+    if ((e = cudaMemsetAsync(wl.list_cnt, 0, sizeof(int32_t) * (nlist_local + 1), st))) return e;
+    if ((e = cudaMemsetAsync(wl.cursor, 0, sizeof(int32_t) * nlist_local, st))) return e;
+    size_t total = (size_t)nq * nprobe;
+    if (total > 0) {
+        count_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nlist_global, list_map,
+                                                                 wl.list_cnt);
+        if ((e = cudaGetLastError())) return e;
+    }
+    if ((e = cub::DeviceScan::ExclusiveSum(scan_tmp, scan_bytes, wl.list_cnt, wl.list_off, nlist_local + 1, st)))
+        return e;
+    if (total > 0) {
+        fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, nlist_global, list_map,
+                                                                wl.list_off, wl.cursor, wl.pair_q, wl.pair_l);
+        if ((e = cudaGetLastError())) return e;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace isb

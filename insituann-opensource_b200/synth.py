@@ -1,0 +1,293 @@
+"""Seeded synthetic datasets and offline index building for the benchmark configs.
+
+The reference measures on SIFT1B / DEEP / SPACEV, which are not available
+here; seeded Gaussian mixtures with the shapes, sizes and value ranges of the
+benchmark configs stand in for them.  Index building (k-means, stable
+cluster-major reorder, residual-PQ training and encoding) is the offline
+part of the reference (cuda/clustering/, scripts/train_ivfpq_residual.py); it
+is written here with torch so it runs on the GPU box in seconds, and it is
+not part of the measured query path.
+
+Counter-based seeding: every chunk of rows draws from its own generator
+seeded by (seed, chunk index), so any shard can generate its rows alone.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import numpy as np
+import torch
+
+GOLDEN = 0x9E3779B97F4A7C15
+MASK64 = (1 << 64) - 1
+
+
+# ----------------------------------------------------------------------------
+# hashing helpers (the reference's delta generators, updates/pq_update.cu:42, 431-446)
+# ----------------------------------------------------------------------------
+def splitmix64(x: np.ndarray) -> np.ndarray:
+    """splitmix64 finaliser on uint64 arrays (wrapping arithmetic)."""
+    x = np.asarray(x, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        x = x + np.uint64(GOLDEN)
+        x = (x ^ (x >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        x = (x ^ (x >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        x = x ^ (x >> np.uint64(31))
+    return x
+
+
+def delta_list_of(local_ids: np.ndarray, nlist: int) -> np.ndarray:
+    """list = local * 11400714819323198485 mod 2^64 mod nlist (pq_update.cu:431-433)."""
+    x = np.asarray(local_ids, dtype=np.uint64)
+    with np.errstate(over="ignore"):
+        h = x * np.uint64(11400714819323198485)
+    return (h % np.uint64(nlist)).astype(np.int64)
+
+
+def delta_codes_of(local_ids: np.ndarray, M: int) -> np.ndarray:
+    """code[m] = splitmix64(local ^ (0x9e37...*(m+1))) & 255 (pq_update.cu:444-446)."""
+    x = np.asarray(local_ids, dtype=np.uint64)[:, None]
+    with np.errstate(over="ignore"):
+        salt = np.uint64(GOLDEN) * (np.arange(M, dtype=np.uint64) + np.uint64(1))
+    return (splitmix64(x ^ salt[None, :]) & np.uint64(255)).astype(np.uint8)
+
+
+def _gen(seed: int, stream: int, device) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(int(splitmix64(np.uint64((seed * 1_000_003 + stream) & MASK64))) & ((1 << 63) - 1))
+    return g
+
+
+# ----------------------------------------------------------------------------
+# data
+# ----------------------------------------------------------------------------
+def _component_ids(n, ncomp, seed, stream, device, zipf: Optional[float]):
+    g = _gen(seed, stream, device)
+    if zipf is None:
+        return torch.randint(0, ncomp, (n,), generator=g, device=device)
+    w = 1.0 / torch.arange(1, ncomp + 1, device=device, dtype=torch.float64) ** zipf
+    return torch.multinomial(w.float(), n, replacement=True, generator=g)
+
+
+def mixture_u8(n, d, ncomp, sigma, seed, device="cpu", start=0, zipf=None, lo=32.0, hi=224.0, chunk=1 << 20,
+               stream_base=0):
+    """uint8 rows from a Gaussian mixture: centers U[lo, hi], per-dim sigma, rounded and clipped."""
+    gc = _gen(seed, 1 << 40, device)
+    centers = lo + (hi - lo) * torch.rand((ncomp, d), generator=gc, device=device)
+    out = torch.empty((n, d), dtype=torch.uint8, device=device)
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        s = stream_base + (start + c0) // chunk
+        comp = _component_ids(c1 - c0, ncomp, seed, 2 * s, device, zipf)
+        g = _gen(seed, 2 * s + 1, device)
+        x = centers[comp] + sigma * torch.randn((c1 - c0, d), generator=g, device=device)
+        out[c0:c1] = torch.clamp(torch.round(x), 0, 255).to(torch.uint8)
+    return out
+
+
+def mixture_f32_unit(n, d, ncomp, sigma, seed, device="cpu", start=0, chunk=1 << 20, stream_base=0):
+    """fp32 rows from a Gaussian mixture (centers on the unit sphere, per-dim sigma), unit-normalised."""
+    gc = _gen(seed, 1 << 40, device)
+    centers = torch.randn((ncomp, d), generator=gc, device=device)
+    centers = centers / centers.norm(dim=1, keepdim=True)
+    out = torch.empty((n, d), dtype=torch.float32, device=device)
+    for c0 in range(0, n, chunk):
+        c1 = min(n, c0 + chunk)
+        s = stream_base + (start + c0) // chunk
+        comp = _component_ids(c1 - c0, ncomp, seed, 2 * s, device, None)
+        g = _gen(seed, 2 * s + 1, device)
+        x = centers[comp] + sigma * torch.randn((c1 - c0, d), generator=g, device=device)
+        out[c0:c1] = x / x.norm(dim=1, keepdim=True).clamp_min(1e-12)
+    return out
+
+
+# ----------------------------------------------------------------------------
+# k-means / assignment
+# ----------------------------------------------------------------------------
+def _rows_per_batch(nc, budget_bytes=1 << 31):
+    return max(1024, budget_bytes // max(1, nc * 4 * 3))
+
+
+def assign(x: torch.Tensor, cent: torch.Tensor, batch: Optional[int] = None) -> torch.Tensor:
+    """Nearest centroid (L2) of every row; int64 [n]."""
+    cent = cent.float()
+    cn = (cent * cent).sum(1)
+    bs = batch or _rows_per_batch(cent.shape[0])
+    out = torch.empty(x.shape[0], dtype=torch.int64, device=x.device)
+    for i in range(0, x.shape[0], bs):
+        xb = x[i:i + bs].float()
+        dd = cn[None, :] - 2.0 * (xb @ cent.T)
+        out[i:i + bs] = dd.argmin(1)
+    return out
+
+
+def kmeans(x: torch.Tensor, k: int, iters: int, seed: int, sample: Optional[int] = None) -> torch.Tensor:
+    """Lloyd k-means with a seeded sample init; empty clusters keep their centroid."""
+    dev = x.device
+    g = _gen(seed, 7, dev)
+    if sample is not None and sample < x.shape[0]:
+        idx = torch.randperm(x.shape[0], generator=g, device=dev)[:sample]
+        xs = x[idx].float()
+    else:
+        xs = x.float()
+    init = torch.randperm(xs.shape[0], generator=g, device=dev)[:k]
+    cent = xs[init].clone()
+    for _ in range(iters):
+        a = assign(xs, cent)
+        sums = torch.zeros_like(cent).index_add_(0, a, xs)
+        cnt = torch.bincount(a, minlength=k).float()
+        nz = cnt > 0
+        cent[nz] = sums[nz] / cnt[nz, None]
+    return cent.contiguous()
+
+
+def reorder(assign_ids: np.ndarray, nlist: int):
+    """Stable cluster-major reorder (dataset.cuh:559-592): counts, offsets, reorder_to_original."""
+    a = np.asarray(assign_ids, dtype=np.int64)
+    counts = np.bincount(a, minlength=nlist).astype(np.int32)
+    offsets = np.zeros(nlist, dtype=np.int64)
+    offsets[1:] = np.cumsum(counts, dtype=np.int64)[:-1]
+    r2o = np.argsort(a, kind="stable").astype(np.int32)
+    return counts, offsets, r2o
+
+
+# ----------------------------------------------------------------------------
+# residual PQ
+# ----------------------------------------------------------------------------
+def _pq_dist(r: torch.Tensor, cb: torch.Tensor) -> torch.Tensor:
+    """r [T, M, dsub], cb [M, 256, dsub] -> squared L2 [M, T, 256]."""
+    rm = r.permute(1, 0, 2)  # [M, T, dsub]
+    return (rm * rm).sum(-1, keepdim=True) - 2.0 * torch.bmm(rm, cb.transpose(1, 2)) + (cb * cb).sum(-1)[:, None, :]
+
+
+def train_pq(resid: torch.Tensor, M: int, iters: int, seed: int, K: int = 256) -> torch.Tensor:
+    """Per-sub-space k-means (K centroids) on residuals -> codebook [M, K, dsub]."""
+    T, d = resid.shape
+    dsub = d // M
+    r = resid.float().reshape(T, M, dsub)
+    g = _gen(seed, 11, resid.device)
+    init = torch.randperm(T, generator=g, device=resid.device)[:K]
+    cb = r[init].permute(1, 0, 2).contiguous()  # [M, K, dsub]
+    bs = max(1024, (1 << 30) // (M * K * 4))
+    for _ in range(iters):
+        sums = torch.zeros_like(cb)
+        cnt = torch.zeros((M, K), device=resid.device)
+        for i in range(0, T, bs):
+            rb = r[i:i + bs]
+            a = _pq_dist(rb, cb).argmin(-1)  # [M, t]
+            for m in range(M):
+                sums[m].index_add_(0, a[m], rb[:, m, :])
+                cnt[m] += torch.bincount(a[m], minlength=K).float()
+        nz = cnt > 0
+        cb[nz] = sums[nz] / cnt[nz][:, None]
+    return cb.contiguous()
+
+
+def encode_pq(resid: torch.Tensor, cb: torch.Tensor) -> torch.Tensor:
+    M, K, dsub = cb.shape
+    n = resid.shape[0]
+    out = torch.empty((n, M), dtype=torch.uint8, device=resid.device)
+    bs = max(1024, (1 << 30) // (M * K * 4))
+    for i in range(0, n, bs):
+        rb = resid[i:i + bs].float().reshape(-1, M, dsub)
+        out[i:i + bs] = _pq_dist(rb, cb).argmin(-1).T.to(torch.uint8)
+    return out
+
+
+def build_pq_index(base: torch.Tensor, nlist: int, M: int, seed: int, kmeans_iters: int = 20, pq_iters: int = 12,
+                   train_n: int = 500_000, kmeans_sample: Optional[int] = None):
+    """Residual-PQ index in the reference file layouts (numpy arrays, cluster-major).
+
+    Returns dict(centroids, codebook, codes, offsets, counts, r2o, base_rr) where
+    base_rr is the rerank matrix in cluster-major order (uint8 or fp32 like base).
+    """
+    dev = base.device
+    n, d = base.shape
+    cent = kmeans(base, nlist, kmeans_iters, seed, sample=kmeans_sample or min(n, 64 * nlist))
+    a = assign(base, cent)
+    g = _gen(seed, 13, dev)
+    tr = torch.randperm(n, generator=g, device=dev)[:min(train_n, n)]
+    resid_tr = base[tr].float() - cent[a[tr]]
+    cb = train_pq(resid_tr, M, pq_iters, seed)
+    del resid_tr
+    counts, offsets, r2o = reorder(a.cpu().numpy(), nlist)
+    r2o_t = torch.from_numpy(r2o).to(dev).long()
+    codes = torch.empty((n, M), dtype=torch.uint8, device=dev)
+    bs = 1 << 20
+    for i in range(0, n, bs):
+        ids = r2o_t[i:i + bs]
+        resid = base[ids].float() - cent[a[ids]]
+        codes[i:i + bs] = encode_pq(resid, cb)
+    base_rr = base[r2o_t]
+    return dict(centroids=cent.cpu().numpy(), codebook=cb.cpu().numpy(), codes=codes.cpu().numpy(),
+                offsets=offsets, counts=counts, r2o=r2o, base_rr=base_rr.cpu().numpy(),
+                assign=a.cpu().numpy().astype(np.int32))
+
+
+def build_u8_index(base_u8: torch.Tensor, nlist: int, seed: int, iters: int = 20, kmeans_sample=None):
+    """Exact uint8 index: centroids, stable cluster-major base, offsets/counts/r2o (numpy)."""
+    dev = base_u8.device
+    n = base_u8.shape[0]
+    cent = kmeans(base_u8, nlist, iters, seed, sample=kmeans_sample)
+    a = assign(base_u8, cent)
+    counts, offsets, r2o = reorder(a.cpu().numpy(), nlist)
+    base_cm = base_u8[torch.from_numpy(r2o).to(dev).long()]
+    return dict(centroids=cent.cpu().numpy(), base_cm=base_cm.cpu().numpy(), offsets=offsets, counts=counts,
+                r2o=r2o, assign=a.cpu().numpy().astype(np.int32))
+
+
+def delta_segment(n_delta: int, nlist: int, M: int, base_id: int, d: int, seed: int, f32: bool = False):
+    """Published delta segment built like build_delta_pq_mutable_publish (pq_update.cu:448-489).
+
+    Lists and code bytes come from the reference's hash generators; the raw
+    rerank rows are seeded uniform bytes (the reference draws them with
+    mt19937_64, pq_update.cu:435-442).  Returned arrays are in delta-position
+    order (list-major, local id ascending within a list).
+    """
+    local = np.arange(n_delta, dtype=np.int64)
+    lists = delta_list_of(local, nlist)
+    order = np.argsort(lists, kind="stable")
+    counts = np.bincount(lists, minlength=nlist).astype(np.int32)
+    offsets = np.zeros(nlist, dtype=np.int64)
+    offsets[1:] = np.cumsum(counts, dtype=np.int64)[:-1]
+    codes = np.empty((n_delta, M), dtype=np.uint8)
+    step = 1 << 20
+    for i in range(0, n_delta, step):
+        codes[i:i + step] = delta_codes_of(local[order[i:i + step]], M)
+    ids = (base_id + local[order]).astype(np.int32)
+    g = np.random.default_rng(seed)
+    raw_by_local = g.integers(0, 256, size=(n_delta, d), dtype=np.uint8)
+    raw = raw_by_local[order]
+    out = dict(codes=codes, offsets=offsets, counts=counts, ids=ids, local=local[order])
+    if f32:
+        out["raw_f32"] = raw.astype(np.float32)
+    else:
+        out["raw_u8"] = raw
+    return out
+
+
+def brute_force_gt(base: torch.Tensor, q: torch.Tensor, k: int, batch_rows: int = 1 << 20) -> np.ndarray:
+    """Exact top-k original ids by L2 (ties by smaller id), for recall."""
+    qf = q.float()
+    qn = (qf * qf).sum(1)
+    best_d = torch.full((q.shape[0], k), float("inf"), device=q.device)
+    best_i = torch.full((q.shape[0], k), -1, dtype=torch.int64, device=q.device)
+    for i in range(0, base.shape[0], batch_rows):
+        xb = base[i:i + batch_rows].float()
+        dd = qn[:, None] + (xb * xb).sum(1)[None, :] - 2.0 * (qf @ xb.T)
+        vd, vi = torch.topk(dd, min(k, xb.shape[0]), dim=1, largest=False)
+        cd = torch.cat([best_d, vd], 1)
+        ci = torch.cat([best_i, vi + i], 1)
+        o = torch.argsort(cd, dim=1, stable=True)[:, :k]
+        best_d = torch.gather(cd, 1, o)
+        best_i = torch.gather(ci, 1, o)
+    return best_i.int().cpu().numpy()
+
+
+def recall_at_k(ids: np.ndarray, gt: np.ndarray, k: int) -> float:
+    """updates/io.h:151-168: hits of the first k ids among the first k GT ids."""
+    ids = np.asarray(ids)[:, :k]
+    gt = np.asarray(gt)[:, :k]
+    hit = sum(len(np.intersect1d(a[a >= 0], b)) for a, b in zip(ids, gt))
+    return hit / float(ids.shape[0] * k)

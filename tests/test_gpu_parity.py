@@ -1,0 +1,300 @@
+"""GPU parity: every search through the C ABI equals the CPU oracle bit for bit.
+
+Bar: identical ids and distances (int32 for exact uint8; fp32 bits for PQ,
+whose sums are written without contraction on both sides, so the 1e-4
+relative tolerance of the spec is never needed here).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import insitu_b200 as ib
+import oracle
+import synth
+
+pytestmark = pytest.mark.gpu
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLDEN, name)))
+
+
+def gpu_exact(e, q_u8, probes, k, route=False, nprobe=None):
+    nq = q_u8.shape[0]
+    nprobe = nprobe or probes.shape[1]
+    index = ib.Index().load_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], e["centroids"])
+    b = ib.Batch(max(nq, 1), q_u8.shape[1], nprobe, k, len(e["counts"]))
+    b.stage1_prepare(q_u8.astype(np.float32))
+    if not route:
+        b.set_probes(probes)
+    b.u8_search(index, nq, nprobe, k, route=route)
+    out = b.get_results_i32(nq, k)
+    b.close()
+    index.close()
+    return out
+
+
+def gpu_pq(p, q, probes, k, R, delta=None, delta_topk=16, f32=False):
+    nq, nprobe = probes.shape
+    index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                               base_u8=None if f32 else p["base_u8"], base_f32=p["base_f32"] if f32 else None)
+    if delta is not None:
+        index.publish_delta(delta["codes"], delta["ids"], delta["counts"], delta["offsets"],
+                            raw_u8=delta.get("raw_u8"), raw_f32=delta.get("raw_f32"))
+    b = ib.Batch(nq, q.shape[1], nprobe, k, len(p["counts"]))
+    b.stage1_prepare(q)
+    b.set_probes(probes)
+    b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=delta is not None, delta_topk=delta_topk, route=False)
+    out = b.get_results(nq, k)
+    b.close()
+    index.close()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# golden fixtures
+# ---------------------------------------------------------------------------
+def test_exact_golden(cuda_ok):
+    g = load("exact_small.npz")
+    k = int(g["k"])
+    gi, gd = gpu_exact(g, g["q_u8"], g["probes"], k)
+    oi, od = oracle.exact_u8(g["base_cm"], g["offsets"], g["counts"], g["r2o"], g["q_u8"], g["probes"], k)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+@pytest.mark.parametrize("case", [c for c in json.load(open(os.path.join(GOLDEN, "kat.json")))
+                                  if c["kind"] == "exact"], ids=lambda c: f"k{c['k']}")
+def test_exact_kat(cuda_ok, case):
+    a = {k: np.array(v) for k, v in case.items() if isinstance(v, list)}
+    e = dict(base_cm=a["base_cm"].astype(np.uint8), offsets=a["offsets"], counts=a["counts"], r2o=a["r2o"],
+             centroids=a["centroids"].astype(np.float32))
+    gi, gd = gpu_exact(e, a["q_u8"].astype(np.uint8), a["probes"], case["k"])
+    assert np.array_equal(gi, a["ids"]) and np.array_equal(gd, a["dist"])
+
+
+@pytest.mark.parametrize("name", ["pq_u8_small", "pq_f32_small"])
+def test_pq_golden(cuda_ok, name):
+    g = load(name + ".npz")
+    k, R = int(g["k"]), int(g["R"])
+    f32 = "base_f32" in g
+    gi, gd = gpu_pq(g, g["q"], g["probes"], k, R, f32=f32)
+    oi, od = oracle.pq_search(g["centroids"], g["codebook"], g["codes"], g["offsets"], g["counts"], g["r2o"], g["q"],
+                              g["probes"], k, rerank_n=R, base_u8=g.get("base_u8"), base_f32=g.get("base_f32"))
+    assert np.array_equal(gi, oi)
+    assert np.array_equal(gd, od)
+
+
+@pytest.mark.parametrize("case", [c for c in json.load(open(os.path.join(GOLDEN, "kat.json")))
+                                  if c["kind"] == "pq"], ids=lambda c: f"R{c['R']}k{c['k']}")
+def test_pq_kat(cuda_ok, case):
+    a = {k: np.array(v) for k, v in case.items() if isinstance(v, list) and k != "dist"}
+    p = dict(centroids=a["centroids"].astype(np.float32), codebook=a["codebook"].astype(np.float32),
+             codes=a["codes"].astype(np.uint8), offsets=a["offsets"], counts=a["counts"], r2o=a["r2o"],
+             base_u8=a["base_u8"].astype(np.uint8))
+    gi, gd = gpu_pq(p, a["q"].astype(np.float32), a["probes"], case["k"], case["R"])
+    exp = np.array([[np.inf if x == "inf" else x for x in row] for row in case["dist"]], np.float32)
+    assert np.array_equal(gi, a["ids"]) and np.array_equal(gd, exp)
+
+
+# ---------------------------------------------------------------------------
+# seeded medium cases, routing, overlay, edge cases
+# ---------------------------------------------------------------------------
+@pytest.fixture(scope="module")
+def pq_medium():
+    n, d, nlist, M = 60000, 128, 64, 32
+    base = synth.mixture_u8(n, d, 96, 10.0, seed=31)
+    p = synth.build_pq_index(base, nlist, M, seed=31, kmeans_iters=8, pq_iters=6, train_n=20000)
+    p["base_u8"] = p["base_rr"]
+    q = synth.mixture_u8(300, d, 96, 10.0, seed=31, stream_base=1 << 20).float().numpy()
+    return p, q
+
+
+def test_route_matches_oracle(cuda_ok, pq_medium):
+    p, q = pq_medium
+    nprobe = 12
+    index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                               base_u8=p["base_u8"])
+    b = ib.Batch(q.shape[0], q.shape[1], nprobe, 10, len(p["counts"]))
+    b.stage1_prepare(q)
+    b.route(index, q.shape[0], nprobe)
+    got = b.get_probes(q.shape[0], nprobe)
+    exp, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    assert np.array_equal(got, exp)
+
+
+@pytest.mark.parametrize("R,k", [(512, 10), (100, 7), (33, 33)])
+def test_pq_medium_routed(cuda_ok, pq_medium, R, k):
+    p, q = pq_medium
+    nprobe = 12
+    probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    gi, gd = gpu_pq(p, q, probes, k, R)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              probes, k, rerank_n=R, base_u8=p["base_u8"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+def test_pq_overlay(cuda_ok, pq_medium):
+    p, q = pq_medium
+    nprobe, k, R = 12, 10, 256
+    n = p["codes"].shape[0]
+    delta = synth.delta_segment(20000, len(p["counts"]), p["codebook"].shape[0], base_id=n, d=q.shape[1], seed=3)
+    probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    for dtk in (16, 5):
+        gi, gd = gpu_pq(p, q, probes, k, R, delta=delta, delta_topk=dtk)
+        oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                                  probes, k, rerank_n=R, base_u8=p["base_u8"], delta=delta, delta_topk=dtk)
+        assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+def test_pq_edge_probes(cuda_ok, pq_medium):
+    """invalid ids, a repeated list, an empty list and k larger than the candidates."""
+    p, q = pq_medium
+    p = dict(p)
+    counts = p["counts"].copy()
+    counts[5] = 0                       # an empty list
+    p["counts"] = counts
+    probes, _ = oracle.route_l2(q[:40], p["centroids"], 6)
+    probes[0, :] = 5
+    probes[1, 1] = probes[1, 0]
+    probes[2, 2] = -1
+    probes[3, 3] = 10 ** 6
+    gi, gd = gpu_pq(p, q[:40], probes, 16, 20)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                              q[:40], probes, 16, rerank_n=20, base_u8=p["base_u8"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    assert (gi[0] == -1).all()
+
+
+def test_long_lists_span_many_chunks(cuda_ok):
+    """lists of ~10k vectors (several scan chunks), duplicated codes (ADC ties)."""
+    n, d, nlist, M = 40000, 64, 4, 16
+    base = synth.mixture_u8(n, d, 8, 12.0, seed=41)
+    p = synth.build_pq_index(base, nlist, M, seed=41, kmeans_iters=5, pq_iters=4, train_n=8000)
+    p["codes"][100:3000] = p["codes"][99]      # many identical codes inside one list
+    p["base_u8"] = p["base_rr"]
+    q = synth.mixture_u8(50, d, 8, 12.0, seed=41, stream_base=1 << 20).float().numpy()
+    probes, _ = oracle.route_l2(q, p["centroids"], 3)
+    gi, gd = gpu_pq(p, q, probes, 10, 512)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              probes, 10, rerank_n=512, base_u8=p["base_u8"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    e = synth.build_u8_index(base, nlist, seed=41, iters=5)
+    e["base_cm"][200:2500] = e["base_cm"][199]   # identical vectors: distance ties broken by id
+    qu = oracle.make_query_u8(q)
+    gi, gd = gpu_exact(e, qu, probes, 10)
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], qu, probes, 10)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+def test_exact_routed_pipeline(cuda_ok):
+    """reference pipeline entry points: stage1_prepare -> stage2_compute -> get_results."""
+    n, d, nlist = 30000, 128, 64
+    base = synth.mixture_u8(n, d, 64, 12.0, seed=51)
+    e = synth.build_u8_index(base, nlist, seed=51, iters=6)
+    q = synth.mixture_u8(257, d, 64, 12.0, seed=51, stream_base=1 << 20).float().numpy()
+    index = ib.Index().load_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], e["centroids"])
+    b = ib.Batch(300, d, 16, 10, nlist)
+    b.stage1_prepare(q)
+    b.stage2_compute(index, q.shape[0], 16, 10)
+    gi, gd = b.get_results(q.shape[0], 10)
+    probes, _ = oracle.route_l2(q, e["centroids"], 16)
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], oracle.make_query_u8(q), probes, 10)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od.astype(np.float32))
+
+
+def test_coarse_router_handle(cuda_ok, pq_medium):
+    p, q = pq_medium
+    cent = torch.from_numpy(p["centroids"]).cuda()
+    r = ib.CoarseRouter(cent.data_ptr(), cent.shape[0], cent.shape[1])
+    got = r.search(q, 9)
+    exp, _ = oracle.route_l2(q, p["centroids"], 9)
+    assert np.array_equal(got, exp)
+    assert r.last_timing().coarse_total_ms > 0
+    with pytest.raises(ib.InsituError):
+        r.search(q, cent.shape[0] + 1)   # the reference aborts here; this library reports
+    r.close()
+
+
+def test_sharded_merge_equals_unsharded(cuda_ok, pq_medium):
+    """lists split over 2 shards (two index contexts on one GPU): local routing keys,
+    key merge, per-shard stage 1 + exact scoring, device merge == unsharded result."""
+    p, q = pq_medium
+    nlist = len(p["counts"])
+    nq, nprobe, k, R, dtk = q.shape[0], 12, 10, 256, 16
+    n = p["codes"].shape[0]
+    delta = synth.delta_segment(9000, nlist, p["codebook"].shape[0], base_id=n, d=q.shape[1], seed=9)
+    owner = np.arange(nlist) % 2
+    shards = []
+    for s in range(2):
+        lists = np.where(owner == s)[0]
+        rows = np.concatenate([np.arange(p["offsets"][l], p["offsets"][l] + p["counts"][l]) for l in lists])
+        cnt = p["counts"][lists]
+        off = np.zeros(len(lists), np.int64)
+        off[1:] = np.cumsum(cnt)[:-1]
+        idx = ib.Index().load_pq(p["centroids"][lists], p["codebook"], p["codes"][rows], off, cnt, p["r2o"][rows],
+                                 base_u8=p["base_u8"][rows])
+        idx.set_shard(nlist, lists.astype(np.int32), p["offsets"][lists])
+        drows = np.concatenate([np.arange(delta["offsets"][l], delta["offsets"][l] + delta["counts"][l])
+                                for l in lists])
+        dcnt = delta["counts"][lists]
+        doff = np.zeros(len(lists), np.int64)
+        doff[1:] = np.cumsum(dcnt)[:-1]
+        idx.publish_delta(delta["codes"][drows], delta["ids"][drows], dcnt, doff, raw_u8=delta["raw_u8"][drows],
+                          key_offsets=delta["offsets"][lists])
+        shards.append(idx)
+    dev = torch.device("cuda")
+    keys = torch.empty((2, nq, nprobe), dtype=torch.int64, device=dev)
+    adc = torch.empty((2, nq, R), dtype=torch.int64, device=dev)
+    exa = torch.empty((2, nq, R), dtype=torch.int64, device=dev)
+    dadc = torch.empty((2, nq, dtk), dtype=torch.int64, device=dev)
+    dexa = torch.empty((2, nq, dtk), dtype=torch.int64, device=dev)
+    batches = [ib.Batch(nq, q.shape[1], nprobe, k, nlist) for _ in range(2)]
+    for s in range(2):
+        batches[s].stage1_prepare(q)
+        batches[s].route_keys(shards[s], nq, nprobe, keys[s].data_ptr())
+    torch.cuda.synchronize()
+    for b in batches:
+        b.sync()
+    allk = keys.permute(1, 0, 2).contiguous()          # [nq, 2 * nprobe]
+    for s in range(2):
+        batches[s].route_merge(allk.data_ptr(), 2 * nprobe, nq, nprobe)
+        batches[s].pq_search_shard(shards[s], nq, nprobe, R, dtk, adc[s].data_ptr(), exa[s].data_ptr(),
+                                   dadc[s].data_ptr(), dexa[s].data_ptr())
+    for b in batches:
+        b.sync()
+    exp_probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    assert np.array_equal(batches[0].get_probes(nq, nprobe), exp_probes)
+    cat = lambda t: t.permute(1, 0, 2).contiguous()    # noqa: E731
+    A, E, DA, DE = cat(adc), cat(exa), cat(dadc), cat(dexa)
+    batches[0].pq_merge_shards(A.data_ptr(), E.data_ptr(), 2 * R, R, DA.data_ptr(), DE.data_ptr(), 2 * dtk, dtk,
+                               nq, k, True)
+    gi, gd = batches[0].get_results(nq, k)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              exp_probes, k, rerank_n=R, base_u8=p["base_u8"], delta=delta, delta_topk=dtk)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    for o in batches + shards:
+        o.close()
+
+
+def test_errors_are_reported_not_fatal(cuda_ok, pq_medium):
+    p, q = pq_medium
+    index = ib.Index()
+    b = ib.Batch(8, q.shape[1], 4, 4, len(p["counts"]))
+    b.stage1_prepare(q[:8])
+    with pytest.raises(ib.InsituError):
+        b.pq_search(index, 8, 4, 4)            # nothing loaded
+    index.load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                  base_u8=p["base_u8"])
+    with pytest.raises(ib.InsituError):
+        b.pq_search(index, 9, 4, 4)            # beyond max_n_query
+    with pytest.raises(ib.InsituError):
+        b.stage2_compute(index, 8, 4, 4, distance_mode=1)   # cosine is out of scope
+    b.pq_search(index, 8, 4, 4)                # the context is still usable
+    ids, _ = b.get_results(8, 4)
+    assert (ids >= 0).all()
+    b.close()
+    index.close()

@@ -1,0 +1,151 @@
+"""The CPU oracle pinned against the reference's own kernels and hand-built cases (no GPU)."""
+import hashlib
+import json
+import os
+
+import numpy as np
+import pytest
+
+import oracle
+import synth
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+
+
+def load(name):
+    return dict(np.load(os.path.join(GOLDEN, name)))
+
+
+def test_manifest_hashes():
+    man = json.load(open(os.path.join(GOLDEN, "MANIFEST.json")))
+    for name, h in man.items():
+        assert hashlib.sha256(open(os.path.join(GOLDEN, name), "rb").read()).hexdigest() == h, name
+
+
+def _tie_normalised(ids, dist):
+    """rows sorted by (dist, id): the reference orders equal distances by heap order."""
+    o = np.lexsort((ids, dist), axis=1) if ids.ndim == 1 else None
+    out_i, out_d = [], []
+    for i_row, d_row in zip(ids, dist):
+        o = np.lexsort((i_row, d_row))
+        out_i.append(i_row[o])
+        out_d.append(d_row[o])
+    return np.array(out_i), np.array(out_d)
+
+
+def _compare_to_reference(o_ids, o_dist, r_ids, r_dist, rtol=0.0):
+    """Equal up to the order of exactly tied candidates; at a tie that straddles
+    rank k the member sets may differ, so only the distances are compared there."""
+    oi, od = _tie_normalised(o_ids, o_dist)
+    ri, rd = _tie_normalised(r_ids, r_dist)
+    if rtol == 0:
+        assert np.array_equal(od, rd)
+    else:
+        np.testing.assert_allclose(od, rd, rtol=rtol)
+    for q in range(oi.shape[0]):
+        kth = od[q, -1]
+        sure = od[q] < kth if rtol == 0 else od[q] < kth * (1 - rtol)
+        assert np.array_equal(oi[q][sure], ri[q][sure]), q
+
+
+def test_exact_matches_reference_kernel():
+    g = load("exact_small.npz")
+    k = int(g["k"])
+    ids, dist = oracle.exact_u8(g["base_cm"], g["offsets"], g["counts"], g["r2o"], g["q_u8"], g["probes"], k)
+    r_ids = g["r2o"][g["ref_local_idx"]]
+    _compare_to_reference(ids, dist.astype(np.float32), r_ids, g["ref_dist"])
+
+
+def test_pq_u8_matches_reference_kernel():
+    g = load("pq_u8_small.npz")
+    k, R = int(g["k"]), int(g["R"])
+    ids, dist = oracle.pq_search(g["centroids"], g["codebook"], g["codes"], g["offsets"], g["counts"], g["r2o"],
+                                 g["q"], g["probes"], k, rerank_n=R, base_u8=g["base_u8"])
+    _compare_to_reference(ids, dist, g["r2o"][g["ref_local_idx"]], g["ref_dist"])
+
+
+def test_pq_f32_matches_reference_kernel_within_tolerance():
+    """fp32 rerank: the reference sums 16 lanes with FMA, the oracle sums in order
+    without contraction; the spec tolerance is 1e-4 relative."""
+    g = load("pq_f32_small.npz")
+    k, R = int(g["k"]), int(g["R"])
+    ids, dist = oracle.pq_search(g["centroids"], g["codebook"], g["codes"], g["offsets"], g["counts"], g["r2o"],
+                                 g["q"], g["probes"], k, rerank_n=R, base_f32=g["base_f32"])
+    _compare_to_reference(ids, dist, g["r2o"][g["ref_local_idx"]], g["ref_dist"], rtol=1e-4)
+
+
+def _kat():
+    return json.load(open(os.path.join(GOLDEN, "kat.json")))
+
+
+@pytest.mark.parametrize("case", [c for c in _kat() if c["kind"] == "exact"], ids=lambda c: f"k{c['k']}")
+def test_kat_exact(case):
+    a = {k: np.array(v) for k, v in case.items() if isinstance(v, list)}
+    ids, dist = oracle.exact_u8(a["base_cm"].astype(np.uint8), a["offsets"], a["counts"], a["r2o"],
+                                a["q_u8"].astype(np.uint8), a["probes"], case["k"])
+    assert np.array_equal(ids, a["ids"]) and np.array_equal(dist, a["dist"])
+
+
+@pytest.mark.parametrize("case", [c for c in _kat() if c["kind"] == "pq"], ids=lambda c: f"R{c['R']}k{c['k']}")
+def test_kat_pq(case):
+    a = {k: np.array(v) for k, v in case.items() if isinstance(v, list) and k != "dist"}
+    ids, dist = oracle.pq_search(a["centroids"], a["codebook"], a["codes"].astype(np.uint8), a["offsets"],
+                                 a["counts"], a["r2o"], a["q"], a["probes"], case["k"], rerank_n=case["R"],
+                                 base_u8=a["base_u8"].astype(np.uint8))
+    exp = np.array([[np.inf if x == "inf" else x for x in row] for row in case["dist"]], np.float32)
+    assert np.array_equal(ids, a["ids"]) and np.array_equal(dist, exp)
+
+
+def test_kat_route():
+    case = [c for c in _kat() if c["kind"] == "route"][0]
+    ids, _ = oracle.route_l2(np.array(case["q"], np.float32), np.array(case["centroids"], np.float32),
+                             case["nprobe"])
+    assert ids.tolist() == case["ids"]
+
+
+def test_lut_and_adc_formula():
+    rng = np.random.default_rng(0)
+    M, dsub = 4, 3
+    q = rng.standard_normal(M * dsub).astype(np.float32)
+    c = rng.standard_normal(M * dsub).astype(np.float32)
+    cb = rng.standard_normal((M, 256, dsub)).astype(np.float32)
+    lut = oracle.pq_lut(q, c, cb)
+    r = (q - c).astype(np.float32)
+    for m in range(M):
+        for k in (0, 17, 255):
+            s = np.float32(0)
+            for j in range(dsub):
+                x = np.float32(r[m * dsub + j] - cb[m, k, j])
+                s = np.float32(s + np.float32(x * x))
+            assert lut[m, k] == s
+
+
+def test_make_query_u8_rounding():
+    q = np.array([-3.0, 0.49, 0.5, 1.5, 2.5, 254.6, 300.0], np.float32)
+    assert oracle.make_query_u8(q).tolist() == [0, 0, 1, 2, 3, 255, 255]
+
+
+def test_delta_generators_match_reference_formulas():
+    # list = local * 11400714819323198485 mod 2^64 mod nlist; code = splitmix64(local ^ golden*(m+1)) & 255
+    def sm(x):
+        x = (x + 0x9E3779B97F4A7C15) & ((1 << 64) - 1)
+        x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & ((1 << 64) - 1)
+        x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & ((1 << 64) - 1)
+        return x ^ (x >> 31)
+
+    local = np.array([0, 1, 2, 12345, 999999], np.int64)
+    lists = synth.delta_list_of(local, 65536)
+    codes = synth.delta_codes_of(local, 4)
+    for i, l in enumerate(local.tolist()):
+        assert lists[i] == ((l * 11400714819323198485) % (1 << 64)) % 65536
+        for m in range(4):
+            assert codes[i, m] == sm(l ^ ((0x9E3779B97F4A7C15 * (m + 1)) % (1 << 64))) & 255
+
+
+def test_reorder_is_stable():
+    a = np.array([2, 0, 2, 1, 0, 2], np.int32)
+    counts, offsets, r2o = synth.reorder(a, 3)
+    assert counts.tolist() == [2, 1, 3] and offsets.tolist() == [0, 2, 3]
+    assert r2o.tolist() == [1, 4, 3, 0, 2, 5]
+    c2, o2, r2 = oracle.reorder(a, 3)
+    assert np.array_equal(c2, counts) and np.array_equal(o2, offsets) and np.array_equal(r2, r2o)
