@@ -1,0 +1,518 @@
+#!/usr/bin/env python3
+"""Benchmark of the IVF residual-PQ query hot path (BASELINE.json configs[1] by default).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
+
+Workload c1: 10M x 96 fp32 unit-normalised vectors from a seeded 4096-component
+Gaussian mixture (sigma 0.05), nlist 4096, residual PQ M=48 x 8 bit trained on
+a 500k sample, 10k queries from the same mixture, k=10, rerank_n=512 with fp32
+rerank.  A step is one pass of the hot path over the 10k-query batch: routing,
+probe inversion, ADC scan, top-R selection, exact rerank, top-k.
+
+N>1: inverted lists are sharded over the ranks (LPT by bytes); every rank
+routes over its own centroids, the local routing keys are all-gathered and
+merged, each rank scans its own lists and scores its candidates exactly, the
+per-shard candidate lists go to the owners of the queries with one all-to-all,
+the owners merge on the device and the top-k are all-gathered to rank 0.
+Total work is fixed, so "scaling" is "strong".
+
+--impl reference times the reference's own CPU kernel
+(cuda/search/cpu_fine/cpu_fine_kernels_pq_resid.cpp, compiled unmodified into
+oracle/_ref) on the host cores, on samples of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(ROOT, "insituann-opensource_b200"), os.path.join(ROOT, "oracle"), ROOT):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "QPS @ recall@10≥0.9 vs nprobe; scanned GB/s vs 8 TB/s HBM; at 1/2/4/8 B200"
+
+CONFIGS = {
+    # BASELINE.json configs[1]
+    "c1": dict(kind="f32", n=10_000_000, d=96, ncomp=4096, sigma=0.05, nlist=4096, M=48, train_n=500_000,
+               nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(8, 16, 32, 64, 128), seed=20260601,
+               desc="c1: residual-PQ IVF, 10M x 96 fp32 unit-norm (4096-comp mixture, sigma 0.05), nlist 4096, "
+                    "M=48 x 8b, 10k queries, k=10, rerank_n=512 (fp32 rerank)"),
+    # reduced copy for quick checks of the harness itself (not a bench line)
+    "c1-small": dict(kind="f32", n=400_000, d=96, ncomp=512, sigma=0.05, nlist=512, M=48, train_n=100_000,
+                     nq=2000, k=10, rerank_n=512, nprobe=16, sweep=(8, 16, 32), seed=7,
+                     desc="reduced c1 for harness checks"),
+}
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        j = json.load(open(path))
+        return float(j["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock and throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.idx = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                      stderr=subprocess.DEVNULL)
+        except OSError:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p:
+            self.p.terminate()
+            try:
+                self.p.wait(5)
+            except subprocess.TimeoutExpired:
+                self.p.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in open(self.f.name):
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for _, _, r in rows for i, v in enumerate(r) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ----------------------------------------------------------------------------
+# workload
+# ----------------------------------------------------------------------------
+def build_workload(cfg, device):
+    """Seeded data, index and exact ground truth (all outside any timed region)."""
+    import torch
+
+    import synth
+
+    t0 = time.time()
+    base = synth.mixture_f32_unit(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
+    q = synth.mixture_f32_unit(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
+                               stream_base=1 << 30)
+    log(f"[bench] data {time.time() - t0:.1f}s")
+    idx = synth.build_pq_index(base, cfg["nlist"], cfg["M"], cfg["seed"], kmeans_iters=20, pq_iters=12,
+                               train_n=cfg["train_n"], kmeans_sample=64 * cfg["nlist"])
+    log(f"[bench] index {time.time() - t0:.1f}s")
+    gt = synth.brute_force_gt(base, q, cfg["k"], batch_rows=1 << 16)
+    log(f"[bench] ground truth {time.time() - t0:.1f}s")
+    del base
+    torch.cuda.empty_cache()
+    return idx, q.cpu().numpy(), gt
+
+
+def algorithmic_bytes(probes, counts, M):
+    """codes bytes scanned: sum over (query, probed list) of count * M."""
+    p = probes[(probes >= 0)]
+    return int(counts[p].astype(np.int64).sum()) * M
+
+
+def lpt_shards(counts, row_bytes, n_shards):
+    """Longest-processing-time assignment of lists to shards by bytes."""
+    order = np.argsort(-(counts.astype(np.int64) * row_bytes), kind="stable")
+    load = np.zeros(n_shards, np.int64)
+    owner = np.empty(len(counts), np.int32)
+    for l in order:
+        s = int(np.argmin(load))
+        owner[l] = s
+        load[s] += int(counts[l]) * row_bytes
+    return owner
+
+
+# ----------------------------------------------------------------------------
+# reference arm / CPU baseline
+# ----------------------------------------------------------------------------
+def time_reference(idx, q, probes, cfg, target_s, max_queries):
+    """Times oracle/_ref (the reference's cpu_fine_kernel_pq_resid) on a query sample."""
+    import oracle
+
+    L = oracle.ref_lib()
+    if L is None:
+        return None
+    threads = os.cpu_count() or 1
+    kw = dict(rerank_n=cfg["rerank_n"], base_f32=idx["base_rr"], threads=threads)
+    args = (idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"])
+    n0 = min(64, q.shape[0])
+    t = time.perf_counter()
+    oracle.ref_pq_resid(*args, q[:n0], probes[:n0], cfg["k"], **kw)
+    per_q = (time.perf_counter() - t) / n0
+    S = int(max(n0, min(max_queries, q.shape[0], target_s / max(per_q, 1e-9))))
+    t = time.perf_counter()
+    ids, _, s1, s2 = oracle.ref_pq_resid(*args, q[:S], probes[:S], cfg["k"], **kw)
+    dt = time.perf_counter() - t
+    return dict(qps=S / dt, seconds=dt, sample=S, threads=threads, lib=os.path.basename(L.library_path),
+                local_ids=ids)
+
+
+def run_reference_arm(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    import oracle
+
+    if oracle.ref_lib() is None:
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (needs the reference tree)"}))
+        return
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    idx, q, gt = build_workload(cfg, dev)
+    nprobe = args.nprobe or cfg["nprobe"]
+    probes, _ = oracle.route_l2(q, idx["centroids"], nprobe)
+    times, samples = [], []
+    for step in range(args.warmup + args.steps):
+        r = time_reference(idx, q, probes, cfg, target_s=4.0, max_queries=cfg["nq"])
+        if step >= args.warmup:
+            times.append(r["seconds"])
+            samples.append(r["sample"])
+    qps = sum(samples) / sum(times)
+    ids = idx["r2o"][r["local_ids"]]
+    import synth
+
+    rec = synth.recall_at_k(ids, gt[:ids.shape[0]], cfg["k"])
+    out = {
+        "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "nprobe": nprobe, "k": cfg["k"], "rerank_n": cfg["rerank_n"],
+                   "recall@10": rec, "routing": "not timed (probe lists from the exact fp32 router)"},
+        "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": r["threads"], "kind": "reference",
+                         "sample": f"{samples[-1]} queries per step of the {cfg['nq']}-query batch, "
+                                   f"cpu_fine_kernel_pq_resid stage 1 + fp32 rerank ({r['lib']})"},
+        "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+# ----------------------------------------------------------------------------
+# our arm
+# ----------------------------------------------------------------------------
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--nprobe", type=int, default=0)
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = CONFIGS[args.config]
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference_arm(args, cfg)
+
+    import torch
+    import torch.distributed as dist
+
+    import insitu_b200 as ib
+    import oracle
+    import synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    N = world
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if N > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    nq, d, k, R, M = cfg["nq"], cfg["d"], cfg["k"], cfg["rerank_n"], cfg["M"]
+    nlist = cfg["nlist"]
+    nprobe = args.nprobe or cfg["nprobe"]
+
+    # ---- workload (rank 0 builds, broadcast to the others) ----
+    if rank == 0:
+        idx, q_np, gt = build_workload(cfg, dev)
+    else:
+        idx, q_np, gt = None, None, None
+    if N > 1:
+        shapes = [None]
+        if rank == 0:
+            shapes = [{k_: (v.shape, str(v.dtype)) for k_, v in idx.items()} | {"q": (q_np.shape, "float32")}]
+        dist.broadcast_object_list(shapes, src=0)
+        shapes = shapes[0]
+        tensors = {}
+        for name, (shape, dt) in shapes.items():
+            src = (idx[name] if name != "q" else q_np) if rank == 0 else None
+            t = torch.from_numpy(np.ascontiguousarray(src)).to(dev) if rank == 0 else \
+                torch.empty(shape, dtype=getattr(torch, dt), device=dev)
+            dist.broadcast(t, src=0)
+            tensors[name] = t
+        torch.cuda.synchronize()
+        if rank != 0:
+            idx = {n_: t.cpu().numpy() for n_, t in tensors.items() if n_ != "q"}
+            q_np = tensors["q"].cpu().numpy()
+        del tensors
+
+    counts, offsets = idx["counts"], idx["offsets"]
+    q_dev = torch.from_numpy(q_np).to(dev)
+
+    # ---- load this rank's lists ----
+    index = ib.Index()
+    if N == 1:
+        index.load_pq(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
+                      base_f32=idx["base_rr"])
+        my_lists = np.arange(nlist)
+    else:
+        owner = lpt_shards(counts, M + 4 * d, N)
+        my_lists = np.where(owner == rank)[0].astype(np.int32)
+        rows = np.concatenate([np.arange(offsets[l], offsets[l] + counts[l]) for l in my_lists])
+        cnt = counts[my_lists]
+        off = np.zeros(len(my_lists), np.int64)
+        off[1:] = np.cumsum(cnt, dtype=np.int64)[:-1]
+        index.load_pq(idx["centroids"][my_lists], idx["codebook"], idx["codes"][rows], off, cnt, idx["r2o"][rows],
+                      base_f32=idx["base_rr"][rows])
+        index.set_shard(nlist, my_lists, offsets[my_lists])
+    batch = ib.Batch(nq, d, max(nprobe, max(cfg["sweep"])), k, nlist)
+    ext = torch.cuda.ExternalStream(batch.stream, device=dev)
+
+    # ---- one step of the hot path ----
+    if N > 1:
+        assert nq % N == 0, "nq must divide by the GPU count"
+        qo = nq // N
+        keys_l = torch.empty((nq, nprobe), dtype=torch.int64, device=dev)
+        keys_all = torch.empty((N, nq, nprobe), dtype=torch.int64, device=dev)
+        adc = torch.empty((nq, R), dtype=torch.int64, device=dev)
+        exa = torch.empty((nq, R), dtype=torch.int64, device=dev)
+        adc_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
+        exa_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
+        out_ids = torch.empty((qo, k), dtype=torch.int32, device=dev)
+        out_dist = torch.empty((qo, k), dtype=torch.float32, device=dev)
+        all_ids = torch.empty((N, qo, k), dtype=torch.int32, device=dev)
+        all_dist = torch.empty((N, qo, k), dtype=torch.float32, device=dev)
+
+    def step(np_=nprobe):
+        batch.stage1_prepare_device(q_dev.data_ptr(), nq)
+        if N == 1:
+            batch.pq_search(index, nq, np_, k, rerank_n=R, overlay=False, route=True)
+            return
+        with torch.cuda.stream(ext):
+            batch.route_keys(index, nq, np_, keys_l.data_ptr())
+            dist.all_gather_into_tensor(keys_all, keys_l)
+            kt = keys_all.permute(1, 0, 2).contiguous()
+            batch.route_merge(kt.data_ptr(), N * np_, nq, np_)
+            batch.pq_search_shard(index, nq, np_, R, 0, adc.data_ptr(), exa.data_ptr())
+            dist.all_to_all_single(adc_r, adc.view(N, qo, R))
+            dist.all_to_all_single(exa_r, exa.view(N, qo, R))
+            A = adc_r.permute(1, 0, 2).contiguous()
+            E = exa_r.permute(1, 0, 2).contiguous()
+            batch.pq_merge_shards(A.data_ptr(), E.data_ptr(), N * R, R, None, None, 0, 0, qo, k, False)
+            batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
+            dist.all_gather_into_tensor(all_ids, out_ids)
+            dist.all_gather_into_tensor(all_dist, out_dist)
+
+    def results():
+        if N == 1:
+            return batch.get_results(nq, k)
+        torch.cuda.synchronize()
+        return all_ids.reshape(nq, k).cpu().numpy(), all_dist.reshape(nq, k).cpu().numpy()
+
+    def barrier():
+        torch.cuda.synchronize()
+        batch.sync()
+        if N > 1:
+            dist.barrier()
+
+    # ---- recall sweep over nprobe (untimed) ----
+    sweep = []
+    if not args.no_sweep:
+        for np_ in cfg["sweep"]:
+            if N > 1 and np_ != nprobe:
+                continue  # the sharded step keeps buffers for the headline nprobe only
+            step(np_)
+            ids, _ = results()
+            rec = synth.recall_at_k(ids, gt, k) if rank == 0 else None
+            barrier()
+            t0 = time.perf_counter()
+            reps = 3
+            for _ in range(reps):
+                step(np_)
+            barrier()
+            dt = (time.perf_counter() - t0) / reps
+            sweep.append({"nprobe": np_, "recall@10": rec, "qps": nq / dt})
+            if rank == 0:
+                log(f"[bench] nprobe {np_}: recall@10 {rec} qps {nq / dt:.0f}")
+
+    # ---- parity spot check against the CPU oracle (first 64 queries, untimed) ----
+    step()
+    ids_g, dist_g = results()
+    barrier()
+    parity = None
+    if rank == 0:
+        probes_g = None
+        if N == 1:
+            probes_g = batch.get_probes(nq, nprobe)
+        sub = 64
+        probes_o, _ = oracle.route_l2(q_np[:sub], idx["centroids"], nprobe)
+        oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
+                                  q_np[:sub], probes_o, k, rerank_n=R, base_f32=idx["base_rr"])
+        parity = bool(np.array_equal(oi, ids_g[:sub]) and np.array_equal(od, dist_g[:sub]))
+        if probes_g is not None:
+            parity = parity and bool(np.array_equal(probes_g[:sub], probes_o))
+        recall = synth.recall_at_k(ids_g, gt, k)
+        log(f"[bench] parity(64 queries vs oracle)={parity} recall@10={recall:.4f}")
+
+    # ---- timed region ----
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    probes_all = batch.get_probes(nq, nprobe) if N == 1 else None
+    batch.profile(True)
+    launches0 = ib.kernel_launches()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        barrier()
+        ev0.record(ext)
+        for _ in range(args.steps):
+            step()
+        ev1.record(ext)
+        barrier()
+    launches = ib.kernel_launches() - launches0
+    stage = batch.stage_ms()
+    batch.profile(False)
+    ms_total = ev0.elapsed_time(ev1)
+    if N > 1:
+        t = torch.tensor([ms_total], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_total = float(t.item())
+    ms_step = ms_total / args.steps
+    value = nq / (ms_step / 1000.0)
+    clocks = clk.summary()
+
+    # ---- e2e through the public C ABI with host buffers ----
+    e2e = None
+    hq = torch.from_numpy(q_np).pin_memory()
+    h_ids = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    h_dist = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        batch.stage1_prepare_ptr(hq.data_ptr(), nq)
+        if N == 1:
+            batch.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=False, route=True)
+            batch.get_results_into(h_dist.data_ptr(), h_ids.data_ptr(), nq, k)
+        else:
+            with torch.cuda.stream(ext):
+                q_dev.copy_(hq, non_blocking=True)
+            step()
+            if rank == 0:
+                with torch.cuda.stream(ext):
+                    h_ids.copy_(all_ids.reshape(nq, k), non_blocking=True)
+                    h_dist.copy_(all_dist.reshape(nq, k), non_blocking=True)
+            ext.synchronize()
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(ext)
+    barrier()
+    e_ms = e0.elapsed_time(e1)
+    if N > 1:
+        t = torch.tensor([e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    e2e = {"value": nq / (e_ms / args.steps / 1000.0), "unit": "queries/s",
+           "h2d_bytes_per_step": int(nq * d * 4 * N), "d2h_bytes_per_step": int(nq * k * 8)}
+
+    # ---- roofline of the ADC scan kernel (this rank) ----
+    if probes_all is None:
+        probes_all = batch.get_probes(nq, nprobe)
+    mine = np.zeros(nlist, bool)
+    mine[my_lists] = True
+    p = probes_all.copy()
+    p[(p >= 0) & ~mine[np.clip(p, 0, nlist - 1)]] = -1
+    bytes_per_launch = algorithmic_bytes(p, counts, M)
+    bytes_total = algorithmic_bytes(probes_all, counts, M)
+    scan_ms = stage["scan"] / args.steps
+    peak, peak_kind = peaks()
+    achieved = bytes_per_launch / (scan_ms / 1000.0) / 1e9
+    traffic = None
+    prof_path = os.path.join(ROOT, "profiles", "pq_scan_c1_traffic.json")
+    if os.path.exists(prof_path) and args.config == "c1" and N == 1:
+        traffic = json.load(open(prof_path)).get("dram_bytes_per_launch")
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": "pq_scan_kernel<48>", "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_ms_per_launch": scan_ms}
+
+    cpu = None
+    if rank == 0 and N == 1 and not args.no_cpu_baseline:
+        probes_o, _ = oracle.route_l2(q_np[:4096], idx["centroids"], nprobe)
+        r = time_reference(idx, q_np[:4096], probes_o, cfg, target_s=12.0, max_queries=4096)
+        if r is not None:
+            cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
+                   "sample": f"{r['sample']} of the {nq} queries, reference cpu_fine_kernel_pq_resid "
+                             f"(stage 1 + fp32 rerank, {r['lib']}), probe lists given, {r['seconds']:.1f}s"}
+
+    if rank == 0:
+        out = {
+            "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": N, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": cfg["desc"], "n_base": cfg["n"], "d": d, "nlist": nlist, "M": M,
+                       "nq": nq, "nprobe": nprobe, "k": k, "rerank_n": R,
+                       "recall@10": synth.recall_at_k(ids_g, gt, k), "parity_vs_oracle_64q": parity,
+                       "inputs_exceed_l2": True, "l2_note": "480 MB of codes and 3.84 GB of rerank rows per step",
+                       "parallelism": "single GPU" if N == 1 else f"lists sharded x{N} (LPT by bytes), NCCL"},
+            "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+            "clocks": clocks, "stages_ms_per_step": {s: v / args.steps for s, v in stage.items()},
+            "gbs_scanned_logical": bytes_total / (ms_step / 1000.0) / 1e9,
+            "sweep": sweep,
+        }
+        print(json.dumps(out))
+    batch.close()
+    index.close()
+    if N > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

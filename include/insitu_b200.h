@@ -266,6 +266,25 @@ int ivf_u8_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
 int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int k);
 
 /* ======================================================================
+ * observability
+ * ====================================================================== */
+/* number of kernels this library has launched in this process (all devices) */
+unsigned long long ivf_kernel_launches(void);
+
+/* stages timed by ivf_batch_profile; ivf_batch_stage_ms returns IVF_STAGE_COUNT */
+#define IVF_STAGE_ROUTE 0     /* coarse routing: distances + top-nprobe */
+#define IVF_STAGE_WORKLIST 1  /* probe inversion + candidate reset */
+#define IVF_STAGE_SCAN 2      /* fine scan (ADC or exact) with the block filter */
+#define IVF_STAGE_SELECT 3    /* per-query top-R / top-k selection */
+#define IVF_STAGE_RERANK 4    /* exact rerank of the PQ candidates */
+#define IVF_STAGE_COUNT 5
+/* enable (1) / disable (0) CUDA-event timing of the stages of later searches */
+int ivf_batch_profile(void* batch_ctx, int enable);
+/* syncs the batch stream, writes the summed ms of each stage since the last
+ * call into out_ms[0..n), resets the sums; returns IVF_STAGE_COUNT or < 0 */
+int ivf_batch_stage_ms(void* batch_ctx, double* out_ms, int n);
+
+/* ======================================================================
  * errors
  * ====================================================================== */
 /* last error message of an index or batch context ("" when none) */

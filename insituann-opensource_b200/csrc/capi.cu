@@ -11,6 +11,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <stdexcept>
 #include <string>
@@ -130,9 +131,36 @@ struct BatchCtx {
     Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
     std::vector<void*> owned;
     std::string err;
+    // optional per-stage CUDA-event timing (ivf_batch_profile / ivf_batch_stage_ms)
+    bool prof = false;
+    std::vector<cudaEvent_t> stage_ev[IVF_STAGE_COUNT];
+    size_t stage_used[IVF_STAGE_COUNT] = {};
+};
+
+// Brackets the launches of one stage with events on the batch stream when
+// profiling is on; elapsed times are summed by ivf_batch_stage_ms().
+struct StageScope {
+    BatchCtx* b;
+    int s;
+    StageScope(BatchCtx* b_, int s_) : b(b_), s(s_) { mark(); }
+    ~StageScope() { mark(); }
+    void mark() {
+        if (!b->prof) return;
+        auto& v = b->stage_ev[s];
+        if (b->stage_used[s] >= v.size()) {
+            cudaEvent_t e = nullptr;
+            if (cudaEventCreate(&e) != cudaSuccess) {
+                cudaGetLastError();
+                return;
+            }
+            v.push_back(e);
+        }
+        cudaEventRecord(v[b->stage_used[s]++], b->st);
+    }
 };
 
 thread_local std::string g_err;
+std::atomic<unsigned long long> g_launches{0};
 
 // device memory budget for per-batch candidate / routing scratch
 size_t scratch_budget() {
@@ -252,6 +280,7 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     size_t row = (size_t)x->nlist * sizeof(uint32_t);
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
     uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
+    StageScope stage(b, IVF_STAGE_ROUTE);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
         ck(route_distances(b->q + (size_t)s * x->d, n, x->cent, x->valid, x->nlist, x->d, dist, b->st),
@@ -316,18 +345,28 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
     ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
-        ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl, tmp,
-                          tmp_bytes, b->st),
-           "build_worklist");
-        ck(reset_candidates(cb, n, b->st), "reset_candidates");
-        ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter, b->st),
-           "exact_scan");
+        {
+            StageScope stage(b, IVF_STAGE_WORKLIST);
+            ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
+                              tmp, tmp_bytes, b->st),
+               "build_worklist");
+            ck(reset_candidates(cb, n, b->st), "reset_candidates");
+        }
+        {
+            StageScope stage(b, IVF_STAGE_SCAN);
+            ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter,
+                          b->st),
+               "exact_scan");
+        }
         uint64_t* dst = keys_out ? keys_out + (size_t)s * k : topk;
-        ck(select_top_r(cb, n, dst, b->st), "select_top_r");
-        if (!keys_out)
-            ck(keys_to_exact_results(topk, n, k, b->out_ids + (size_t)s * k, b->out_idist + (size_t)s * k,
-                                     b->out_dist + (size_t)s * k, b->st),
-               "keys_to_exact_results");
+        {
+            StageScope stage(b, IVF_STAGE_SELECT);
+            ck(select_top_r(cb, n, dst, b->st), "select_top_r");
+            if (!keys_out)
+                ck(keys_to_exact_results(topk, n, k, b->out_ids + (size_t)s * k, b->out_idist + (size_t)s * k,
+                                         b->out_dist + (size_t)s * k, b->st),
+                   "keys_to_exact_results");
+        }
     }
     queue_overflow_check(b);
     b->res_nq = nq;
@@ -388,20 +427,30 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
-        ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl, tmp,
-                          tmp_bytes, b->st),
-           "build_worklist");
-        ck(reset_candidates(cm, n, b->st), "reset_candidates");
-        if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
-        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
-        ck(pq_scan(p, wl, n * nprobe, cm, cd, b->counter, b->st), "pq_scan");
-        uint64_t* m_out = adc ? adc + (size_t)s * R : s1m;
-        ck(select_top_r(cm, n, m_out, b->st), "select_top_r");
-        uint64_t* d_out = nullptr;
-        if (use_delta) {
-            d_out = dadc ? dadc + (size_t)s * Rd : s1d;
-            ck(select_top_r(cd, n, d_out, b->st), "select_top_r (delta)");
+        {
+            StageScope stage(b, IVF_STAGE_WORKLIST);
+            ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
+                              tmp, tmp_bytes, b->st),
+               "build_worklist");
+            ck(reset_candidates(cm, n, b->st), "reset_candidates");
+            if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
         }
+        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
+        {
+            StageScope stage(b, IVF_STAGE_SCAN);
+            ck(pq_scan(p, wl, n * nprobe, cm, cd, b->counter, b->st), "pq_scan");
+        }
+        uint64_t* m_out = adc ? adc + (size_t)s * R : s1m;
+        uint64_t* d_out = nullptr;
+        {
+            StageScope stage(b, IVF_STAGE_SELECT);
+            ck(select_top_r(cm, n, m_out, b->st), "select_top_r");
+            if (use_delta) {
+                d_out = dadc ? dadc + (size_t)s * Rd : s1d;
+                ck(select_top_r(cd, n, d_out, b->st), "select_top_r (delta)");
+            }
+        }
+        StageScope stage(b, IVF_STAGE_RERANK);
         if (adc) {
             ck(pq_rerank(p, x->nlist, m_out, R, d_out, Rd, n, k, nullptr, nullptr, exact + (size_t)s * R,
                          use_delta ? dexact + (size_t)s * Rd : nullptr, b->st),
@@ -462,6 +511,10 @@ struct RouteState {
 thread_local CoarseTimingBreakdown g_coarse_timing;
 
 }  // namespace
+
+namespace isb {
+void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+}  // namespace isb
 
 // ===========================================================================
 // C ABI
@@ -576,6 +629,8 @@ void ivf_destroy_batch_context(void* batch_ctx) {
         if (g->p) cudaFree(g->p);
     free_all(b->owned);
     if (b->h_overflow) cudaFreeHost(b->h_overflow);
+    for (auto& v : b->stage_ev)
+        for (cudaEvent_t e : v) cudaEventDestroy(e);
     cudaStreamDestroy(b->st);
     b->magic = 0;
     delete b;
@@ -1052,6 +1107,48 @@ int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n
         b->res_nq = n_query;
         b->res_k = k;
     });
+}
+
+unsigned long long ivf_kernel_launches(void) { return g_launches.load(); }
+
+int ivf_batch_profile(void* batch_ctx, int enable) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        cudaSetDevice(b->device);
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        b->prof = enable != 0;
+        for (auto& u : b->stage_used) u = 0;
+    });
+}
+
+int ivf_batch_stage_ms(void* batch_ctx, double* out_ms, int n) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    int st = guarded(&b->err, [&] {
+        require(out_ms != nullptr && n >= 0, "null output");
+        cudaSetDevice(b->device);
+        ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        for (int s = 0; s < IVF_STAGE_COUNT; ++s) {
+            double acc = 0;
+            for (size_t i = 0; i + 1 < b->stage_used[s]; i += 2) {
+                float ms = 0;
+                ck(cudaEventElapsedTime(&ms, b->stage_ev[s][i], b->stage_ev[s][i + 1]), "cudaEventElapsedTime");
+                acc += ms;
+            }
+            if (s < n) out_ms[s] = acc;
+            b->stage_used[s] = 0;
+        }
+    });
+    return st == IVF_OK ? IVF_STAGE_COUNT : st;
 }
 
 const char* ivf_last_error(void* ctx) {

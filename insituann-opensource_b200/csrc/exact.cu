@@ -94,10 +94,11 @@ cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkLis
     int grid = sms * 4;
     if (grid > max_pairs) grid = max_pairs;
     switch (d / 16) {
-        case 4: exact_scan_kernel<4><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
-        case 6: exact_scan_kernel<6><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
-        case 8: exact_scan_kernel<8><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
-        case 16: exact_scan_kernel<16><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
+        case 4: note_launch(); exact_scan_kernel<4><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
+        case 6: note_launch(); exact_scan_kernel<6><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
+        case 8: note_launch(); exact_scan_kernel<8><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
+        case 16: note_launch(); exact_scan_kernel<16><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
+        note_launch();
         default: exact_scan_kernel<0><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
     }
     return cudaGetLastError();

@@ -9,6 +9,9 @@
 
 namespace isb {
 
+// Counts this library's own kernel launches (reported by ivf_kernel_launches()).
+void note_launch(int n = 1);
+
 constexpr int kPQScanChunk = 2048;    // vectors per filtered chunk in the PQ scan
 constexpr int kExactScanChunk = 1024; // vectors per filtered chunk in the exact scan
 

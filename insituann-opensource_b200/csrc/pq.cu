@@ -138,6 +138,7 @@ cudaError_t launch_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf c
     long long grid = (long long)sms * per_sm;
     if (grid > items) grid = items;
     if (grid < 1) grid = 1;
+    note_launch();
     pq_scan_kernel<M><<<(int)grid, kPT, smem, st>>>(p, wl, cm, cd, counter);
     return cudaGetLastError();
 }
@@ -348,6 +349,7 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
     size_t smem = sizeof(uint64_t) * np;
     cudaError_t e = cudaFuncSetAttribute(pq_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
     if (e) return e;
+    note_launch();
     pq_rerank_kernel<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist,
                                              out_exact_main, out_exact_delta);
     return cudaGetLastError();
@@ -361,6 +363,7 @@ cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main
     size_t smem = (sizeof(uint64_t) + sizeof(int)) * kMMax;
     cudaError_t e = cudaFuncSetAttribute(merge_shards_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
+    note_launch();
     merge_shards_kernel<<<nq, kMT, smem, st>>>(adc_main, exact_main, n_main, R, adc_delta, exact_delta, n_delta, Rd,
                                                k, exact_is_int, out_ids, out_dist);
     return cudaGetLastError();

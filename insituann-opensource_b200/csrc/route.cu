@@ -160,6 +160,7 @@ __global__ void make_u8_kernel(const float* __restrict__ q, size_t n, uint8_t* _
 }  // namespace
 
 cudaError_t route_centroid_valid(const float* cent, int nlist, int d, uint8_t* valid, cudaStream_t st) {
+    note_launch();
     centroid_valid_kernel<<<(nlist + 255) / 256, 256, 0, st>>>(cent, nlist, d, valid);
     return cudaGetLastError();
 }
@@ -168,6 +169,7 @@ cudaError_t route_distances(const float* q, int nq, const float* cent, const uin
                             uint32_t* out, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     dim3 grid((nlist + kRB - 1) / kRB, (nq + kRB - 1) / kRB);
+    note_launch();
     route_dist_kernel<<<grid, 256, 0, st>>>(q, nq, cent, valid, nlist, d, out);
     return cudaGetLastError();
 }
@@ -176,6 +178,7 @@ cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const 
                          float* out_dist, uint64_t* out_keys, cudaStream_t st) {
     if (L > kSelMaxL || L <= 0) return cudaErrorInvalidValue;
     if (nq <= 0) return cudaSuccess;
+    note_launch();
     route_select_kernel<<<nq, kSelT, 0, st>>>(dist_bits, n, L, id_map, out_ids, out_dist, out_keys);
     return cudaGetLastError();
 }
@@ -184,6 +187,7 @@ cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist,
                        int32_t* out_idist, cudaStream_t st) {
     if (L > kSelMaxL || L <= 0) return cudaErrorInvalidValue;
     if (nq <= 0) return cudaSuccess;
+    note_launch();
     merge_keys_kernel<<<nq, kSelT, 0, st>>>(keys, n, L, int_dist, out_ids, out_dist, out_idist);
     return cudaGetLastError();
 }
@@ -192,6 +196,7 @@ cudaError_t make_query_u8(const float* q, size_t n, uint8_t* out, cudaStream_t s
     if (n == 0) return cudaSuccess;
     size_t blocks = (n + 255) / 256;
     if (blocks > 4096) blocks = 4096;
+    note_launch();
     make_u8_kernel<<<(int)blocks, 256, 0, st>>>(q, n, out);
     return cudaGetLastError();
 }

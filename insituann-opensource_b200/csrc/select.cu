@@ -72,6 +72,7 @@ __global__ void keys_to_exact_kernel(const uint64_t* __restrict__ keys, int tota
 
 cudaError_t reset_candidates(CandBuf cb, int nq, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
+    note_launch();
     reset_kernel<<<(nq + 255) / 256, 256, 0, st>>>(cb.cnt, cb.thr, nq);
     return cudaGetLastError();
 }
@@ -86,6 +87,7 @@ cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st) {
     cudaError_t e = cudaFuncSetAttribute(select_top_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          64 * 1024);
     if (e) return e;
+    note_launch();
     select_top_r_kernel<<<nq, kT, smem, st>>>(cb.keys, cb.cnt, cb.cap, cb.R, out);
     return cudaGetLastError();
 }
@@ -94,6 +96,7 @@ cudaError_t keys_to_exact_results(const uint64_t* keys, int nq, int k, int32_t* 
                                   cudaStream_t st) {
     int total = nq * k;
     if (total <= 0) return cudaSuccess;
+    note_launch();
     keys_to_exact_kernel<<<(total + 255) / 256, 256, 0, st>>>(keys, total, ids, dist, fdist);
     return cudaGetLastError();
 }

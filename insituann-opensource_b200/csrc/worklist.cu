@@ -67,6 +67,7 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
     if ((e = cudaMemsetAsync(wl.cursor, 0, sizeof(int32_t) * nlist_local, st))) return e;
     size_t total = (size_t)nq * nprobe;
     if (total > 0) {
+        note_launch();
         count_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nlist_global, list_map,
                                                                  wl.list_cnt);
         if ((e = cudaGetLastError())) return e;
@@ -74,6 +75,7 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
     if ((e = cub::DeviceScan::ExclusiveSum(scan_tmp, scan_bytes, wl.list_cnt, wl.list_off, nlist_local + 1, st)))
         return e;
     if (total > 0) {
+        note_launch();
         fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, nlist_global, list_map,
                                                                 wl.list_off, wl.cursor, wl.pair_q, wl.pair_l);
         if ((e = cudaGetLastError())) return e;

@@ -40,6 +40,7 @@ EXPORTS = [
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
     "ivf_route_keys", "ivf_route_merge", "ivf_pq_search_shard", "ivf_pq_merge_shards",
     "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_last_error", "ivf_global_last_error",
+    "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
     "cuda_pipeline_init", "cuda_pipeline_flush", "cuda_pipeline_flush_vectors_only", "cuda_pipeline_free",
@@ -91,7 +92,12 @@ _SIGS = {
     "ivf_last_error": ([vp], C.c_char_p),
     "ivf_global_last_error": ([], C.c_char_p),
     "cuda_is_available": ([], C.c_bool),
+    "ivf_kernel_launches": ([], C.c_ulonglong),
+    "ivf_batch_profile": ([vp, i32], i32),
+    "ivf_batch_stage_ms": ([vp, vp, i32], i32),
 }
+
+STAGES = ("route", "worklist", "scan", "select", "rerank")
 
 _lib = None
 
@@ -104,6 +110,11 @@ class InsituError(RuntimeError):
 
 def library_path() -> str:
     return LIB_PATH
+
+
+def kernel_launches() -> int:
+    """kernels launched by libinsitu_b200 in this process so far"""
+    return int(load_library().ivf_kernel_launches())
 
 
 def load_library(require_device: bool = False):
@@ -274,6 +285,17 @@ class Batch:
         msg = self.last_error()
         if msg:
             raise InsituError(-1, msg)
+
+    # ---- observability ----
+    def profile(self, enable=True):
+        self._check(self.L.ivf_batch_profile(self.h, 1 if enable else 0))
+
+    def stage_ms(self) -> dict:
+        out = np.zeros(len(STAGES), np.float64)
+        rc = self.L.ivf_batch_stage_ms(self.h, _p(out), len(STAGES))
+        if rc < 0:
+            self._check(rc)
+        return dict(zip(STAGES, out.tolist()))
 
     # ---- explicit entry points ----
     def route(self, index: Index, nq, nprobe):
