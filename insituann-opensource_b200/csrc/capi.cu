@@ -75,6 +75,8 @@ struct Segment {
     int64_t* key_off = nullptr;
     uint8_t* rr_u8 = nullptr;
     float* rr_f32 = nullptr;
+    uint8_t* ring = nullptr;       // PQ codes in the ring-tile layout (M = 16, 32, 48)
+    int64_t* ring_off = nullptr;   // [nlist] byte offset of each list's tiles
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -83,7 +85,9 @@ struct Segment {
         free_all(owned);
         *this = Segment();
     }
-    ListStore view() const { return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, n}; }
+    ListStore view() const {
+        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, ring, ring_off, n};
+    }
 };
 
 struct IndexCtx {
@@ -96,6 +100,7 @@ struct IndexCtx {
     uint8_t* valid = nullptr;
     int M = 0, dsub = 0;
     float* codebook = nullptr;
+    float* codebook_t = nullptr;   // [256, M, dsub]
     Segment main, delta;
     bool has_delta = false;
     int nlist_global = 0;        // == nlist unless the index is a shard
@@ -249,6 +254,29 @@ void load_lists(IndexCtx* x, Segment& s, const uint8_t* data, size_t row_bytes, 
     s.max_count = max_count;
 }
 
+// Re-lays the segment's PQ codes out as ring tiles (pq.cu) when the kernel
+// supports M; the row-major codes are then no longer kept on the device.
+void build_ring(Segment& s, const long long* offsets, const int* counts, int nlist, int M) {
+    if (!pq_ring_m(M)) return;
+    std::vector<int64_t> roff((size_t)nlist);
+    int64_t acc = 0;
+    for (int l = 0; l < nlist; ++l) {
+        roff[(size_t)l] = acc;
+        acc += pq_ring_list_bytes(counts[l], M);
+    }
+    (void)offsets;
+    s.ring_off = dcopy(roff.data(), roff.size(), s.owned);
+    s.ring = dalloc<uint8_t>((size_t)acc + 64, s.owned);
+    ck(pq_build_ring(s.data, s.offsets, s.counts, s.ring_off, nlist, M, s.ring, 0), "pq_build_ring");
+    ck(cudaDeviceSynchronize(), "pq_build_ring");
+    auto it = std::find(s.owned.begin(), s.owned.end(), (void*)s.data);
+    if (it != s.owned.end()) {
+        cudaFree(*it);
+        s.owned.erase(it);
+    }
+    s.data = nullptr;
+}
+
 void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
     require(centroids != nullptr, "centroids are required");
     x->cent = dcopy(centroids, (size_t)nlist * d, x->owned);
@@ -378,6 +406,7 @@ PQParams pq_params(IndexCtx* x, const float* q, bool use_delta) {
     p.q = q;
     p.cent = x->cent;
     p.codebook = x->codebook;
+    p.codebook_t = x->codebook_t;
     p.d = x->d;
     p.M = x->M;
     p.dsub = x->dsub;
@@ -809,6 +838,13 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
             else x->main.rr_f32 = dcopy(base_f32, (size_t)n * d, x->main.owned);
             load_centroids(x, centroids, nlist, d);
             x->codebook = dcopy(codebook, (size_t)M * K * dsub, x->owned);
+            std::vector<float> cbt((size_t)M * K * dsub);
+            for (int m = 0; m < M; ++m)
+                for (int c = 0; c < K; ++c)
+                    for (int e = 0; e < dsub; ++e)
+                        cbt[((size_t)c * M + m) * dsub + e] = codebook[((size_t)m * K + c) * dsub + e];
+            x->codebook_t = dcopy(cbt.data(), cbt.size(), x->owned);
+            build_ring(x->main, offsets, counts, nlist, M);
         } catch (...) {
             x->main.release();
             free_all(x->owned);
@@ -874,6 +910,7 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
             load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
             if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
             else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
+            build_ring(s, offsets, counts, x->nlist, x->M);
         } catch (...) {
             s.release();
             throw;

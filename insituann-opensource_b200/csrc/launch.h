@@ -59,12 +59,20 @@ struct PQParams {
     const float* q;          // [nq, d] fp32 queries
     const float* cent;       // [nlist, d]
     const float* codebook;   // [M, 256, dsub]
+    const float* codebook_t; // [256, M, dsub] (the same codebook, code-major, for coalesced LUT builds)
     int d, M, dsub;
     ListStore main;
     ListStore delta;
     int has_delta;
 };
 bool pq_supported_m(int M);
+// M values scanned by the conflict-free ring kernel (others use the row kernel)
+bool pq_ring_m(int M);
+// bytes of the ring-tile layout of one list of `count` vectors
+int64_t pq_ring_list_bytes(int count, int M);
+// builds the ring-tile layout of every list from row-major codes [n, M]
+cudaError_t pq_build_ring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
+                          const int64_t* ring_off, int nlist, int M, uint8_t* out, cudaStream_t st);
 cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* work_counter,
                     cudaStream_t st);
 // Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).

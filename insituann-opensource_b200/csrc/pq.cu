@@ -123,6 +123,198 @@ __global__ void __launch_bounds__(kPT) pq_scan_kernel(PQParams p, WorkList wl, C
     }
 }
 
+
+// ---------------------------------------------------------------------------
+// Ring ADC scan (M = 16, 32, 48): conflict-free LUT gathers, same sum order.
+//
+// A warp runs two 16-lane systolic rings.  Lane j of a ring owns the MPL = M/16
+// consecutive sub-quantizers m = MPL*j .. MPL*j+MPL-1: at step x it takes the
+// partial sum of vector x-j from lane j-1 (shuffle), adds its MPL LUT entries
+// in m order and passes the sum on; lane 15 finishes vector x-15.  Every
+// vector's distance is therefore sum_m LUT[m][code[m]] accumulated in m
+// order, exactly as in the row kernel and the CPU restatement.
+//
+// The LUT is stored as rows of S floats per code value c (S a multiple of 32),
+// holding two copies of the M entries at column positions posA(m) and
+// posB(m).  Ring A reads copy A, ring B copy B; the positions are chosen so
+// that in every step the 32 lanes of a warp touch 32 different banks, for any
+// code values:
+//   M=16: A at m, B at 16+m                   (banks j | 16+j)
+//   M=32: A at m, B at 32+((m+1)&31)          (banks of opposite parity)
+//   M=48: A at m, B at 48+m                   (banks 3j+s | 3j+s+16, disjoint as 3 is odd)
+//
+// Codes are re-laid out once per index (pq_build_ring) into tiles of 16 steps:
+// tile T of a list holds, for lane j, step i and sub-quantizer s, the byte
+// code[16T+i-j][MPL*j+s] (0 outside the list).  A lane reads its 16*MPL bytes
+// of a tile with MPL coalesced 16-byte loads and indexes them statically.
+// ---------------------------------------------------------------------------
+template <int M>
+struct Ring {
+    static constexpr int MPL = M / 16;
+    static constexpr int S = M == 16 ? 32 : (M == 32 ? 64 : 96);
+    static constexpr int kTileBytes = 256 * MPL;
+    static constexpr int kChunk = M == 48 ? 3072 : (M == 32 ? 2048 : 4096);
+    __host__ __device__ static constexpr int posA(int m) { return m; }
+    __host__ __device__ static constexpr int posB(int m) {
+        return M == 16 ? 16 + m : (M == 32 ? 32 + ((m + 1) & 31) : 48 + m);
+    }
+};
+
+__host__ __device__ inline int64_t ring_tiles(int count) { return (int64_t)(count + 15) / 16 + 2; }
+
+constexpr int kRingT = 256;  // 8 warps = 16 rings per CTA
+
+template <int M>
+__global__ void __launch_bounds__(kRingT, 2) pq_ring_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
+                                                            int* counter) {
+    using RC = Ring<M>;
+    constexpr int MPL = RC::MPL, S = RC::S, CH = RC::kChunk;
+    extern __shared__ __align__(16) float smf[];
+    float* lut = smf;                // [256][S]
+    float* dist = lut + 256 * S;     // [CH]; holds the query residual while the LUT is built
+    __shared__ EmitSmem esm;
+    __shared__ int s_item;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ring = lane >> 4, j = lane & 15;
+    const int d = p.d, dsub = p.dsub;
+    const float keep = j == 0 ? 0.f : 1.f;
+    int col[MPL];
+#pragma unroll
+    for (int s = 0; s < MPL; ++s) col[s] = ring ? RC::posB(MPL * j + s) : RC::posA(MPL * j + s);
+    const int P = *wl.n_pairs;
+    const int total = p.has_delta ? 2 * P : P;
+    for (;;) {
+        const int it = next_item(counter, total, &s_item);
+        if (it < 0) break;
+        const bool seg_delta = it >= P;
+        const int pi = seg_delta ? it - P : it;
+        const int q = wl.pair_q[pi], l = wl.pair_l[pi];
+        const ListStore& SG = seg_delta ? p.delta : p.main;
+        const CandBuf& cb = seg_delta ? cd : cm;
+        const int count = SG.counts[l];
+        if (count <= 0) continue;
+        const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
+        const uint8_t* tiles = SG.ring + SG.ring_off[l];
+        const int64_t ntiles = ring_tiles(count);
+        {
+            const float* qv = p.q + (size_t)q * d;
+            const float* cv = p.cent + (size_t)l * d;
+            float* resid = dist;
+            for (int e = tid; e < d; e += kRingT) resid[e] = __fsub_rn(qv[e], cv[e]);
+            __syncthreads();
+            for (int mm = lane; mm < M; mm += 32) {
+                const float* rv = resid + mm * dsub;
+                for (int c = warp; c < kCodes; c += kRingT / 32) {
+                    const float* cbv = p.codebook_t + ((size_t)c * M + mm) * dsub;
+                    float acc = 0.f;
+                    for (int e = 0; e < dsub; ++e) {
+                        const float x = __fsub_rn(rv[e], __ldg(cbv + e));
+                        acc = __fadd_rn(acc, __fmul_rn(x, x));
+                    }
+                    lut[c * S + RC::posA(mm)] = acc;
+                    lut[c * S + RC::posB(mm)] = acc;
+                }
+            }
+            __syncthreads();
+        }
+        for (int cs = 0; cs < count; cs += CH) {
+            const int len = min(CH, count - cs);
+            const int Lr = (((len + 15) / 16) + 15) & ~15;  // vectors per ring, multiple of 16
+            const int a = cs + (warp * 2 + ring) * Lr;     // this ring's list-relative range [a, b)
+            const int b = min(a + Lr, cs + len);
+            if (cs + warp * 2 * Lr < cs + len) {           // ring A of this warp has work
+                float sv = 0.f, carry = 0.f;
+                const int T0 = a / 16;
+                const int ntr = Lr / 16 + 1;
+                for (int tt = 0; tt < ntr; ++tt) {
+                    const int64_t T = min((int64_t)(T0 + tt), ntiles - 1);
+                    const uint4* tp = reinterpret_cast<const uint4*>(tiles + T * RC::kTileBytes + j * 16 * MPL);
+                    uint32_t w[4 * MPL];
+#pragma unroll
+                    for (int u = 0; u < MPL; ++u) {
+                        const uint4 x = __ldg(tp + u);
+                        w[4 * u + 0] = x.x;
+                        w[4 * u + 1] = x.y;
+                        w[4 * u + 2] = x.z;
+                        w[4 * u + 3] = x.w;
+                    }
+                    float o[16];
+                    o[0] = carry;
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float sin = __shfl_up_sync(0xffffffffu, sv, 1, 16);
+#pragma unroll
+                        for (int s = 0; s < MPL; ++s) {
+                            const int byte = i * MPL + s;
+                            const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
+                            const float v = lut[c * S + col[s]];
+                            sv = (s == 0) ? fmaf(sin, keep, v) : __fadd_rn(sv, v);
+                        }
+                        if (i < 15) o[i + 1] = sv;
+                        else carry = sv;
+                    }
+                    if (j == 15) {
+                        const int gb = 16 * (T0 + tt) - 16;   // list-relative vectors gb .. gb+15
+                        if (gb >= a && gb + 16 <= b) {
+                            float4* dp = reinterpret_cast<float4*>(dist + (gb - cs));
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) dp[e] = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
+                        } else {
+#pragma unroll
+                            for (int e = 0; e < 16; ++e)
+                                if (gb + e >= a && gb + e < b) dist[gb + e - cs] = o[e];
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            const uint32_t kbase = (uint32_t)(koff + cs);
+            auto keyf = [&](int i) -> uint64_t { return make_key(__float_as_uint(dist[i]), kbase + (uint32_t)i); };
+            block_filter_emit<kRingT>(keyf, len, cb, q, esm);
+        }
+    }
+}
+
+template <int M>
+cudaError_t launch_ring(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* counter,
+                        cudaStream_t st) {
+    using RC = Ring<M>;
+    const size_t smem = sizeof(float) * ((size_t)256 * RC::S + RC::kChunk);
+    if ((size_t)p.d > RC::kChunk) return cudaErrorInvalidValue;  // the residual is staged in the distance array
+    cudaError_t e = cudaFuncSetAttribute(pq_ring_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_ring_kernel<M>, kRingT, smem);
+    if (per_sm < 1) per_sm = 1;
+    long long items = (long long)max_pairs * (p.has_delta ? 2 : 1);
+    long long grid = (long long)sms * per_sm;
+    if (grid > items) grid = items;
+    if (grid < 1) grid = 1;
+    note_launch();
+    pq_ring_kernel<M><<<(int)grid, kRingT, smem, st>>>(p, wl, cm, cd, counter);
+    return cudaGetLastError();
+}
+
+template <int MPL>
+__global__ void ring_layout_kernel(const uint8_t* __restrict__ codes, const int64_t* __restrict__ offsets,
+                                   const int32_t* __restrict__ counts, const int64_t* __restrict__ ring_off,
+                                   int nlist, int M, uint8_t* __restrict__ out) {
+    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
+        const int cnt = counts[l];
+        const int64_t off = offsets[l];
+        const int64_t total = ring_tiles(cnt) * 256 * MPL;
+        uint8_t* dst = out + ring_off[l];
+        for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
+            const int64_t T = e / (256 * MPL);
+            const int r = (int)(e % (256 * MPL));
+            const int jj = r / (16 * MPL), r2 = r % (16 * MPL), i = r2 / MPL, s = r2 % MPL;
+            const int64_t v = 16 * T + i - jj;
+            dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
+        }
+    }
+}
+
 template <int M>
 cudaError_t launch_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* counter,
                         cudaStream_t st) {
@@ -318,12 +510,38 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
 
 bool pq_supported_m(int M) { return M > 0 && M <= 64 && M % 8 == 0; }
 
+bool pq_ring_m(int M) { return M == 16 || M == 32 || M == 48; }
+
+int64_t pq_ring_list_bytes(int count, int M) { return ring_tiles(count) * 256 * (M / 16); }
+
+cudaError_t pq_build_ring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
+                          const int64_t* ring_off, int nlist, int M, uint8_t* out, cudaStream_t st) {
+    if (!pq_ring_m(M)) return cudaErrorInvalidValue;
+    if (nlist <= 0) return cudaSuccess;
+    const int grid = nlist < 4096 ? nlist : 4096;
+    note_launch();
+    switch (M / 16) {
+        case 1: ring_layout_kernel<1><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
+        case 2: ring_layout_kernel<2><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
+        default: ring_layout_kernel<3><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* counter,
                     cudaStream_t st) {
     if (p.d > kPMaxD || !pq_supported_m(p.M)) return cudaErrorInvalidValue;
     if (max_pairs <= 0) return cudaSuccess;
     cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int), st);
     if (e) return e;
+    const bool ring = pq_ring_m(p.M) && p.main.ring && (!p.has_delta || p.delta.ring) && p.codebook_t;
+    if (ring) {
+        switch (p.M) {
+            case 16: return launch_ring<16>(p, wl, max_pairs, cm, cd, counter, st);
+            case 32: return launch_ring<32>(p, wl, max_pairs, cm, cd, counter, st);
+            default: return launch_ring<48>(p, wl, max_pairs, cm, cd, counter, st);
+        }
+    }
     switch (p.M) {
         case 8: return launch_scan<8>(p, wl, max_pairs, cm, cd, counter, st);
         case 16: return launch_scan<16>(p, wl, max_pairs, cm, cd, counter, st);

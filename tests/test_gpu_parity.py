@@ -150,6 +150,21 @@ def test_pq_overlay(cuda_ok, pq_medium):
         assert np.array_equal(gi, oi) and np.array_equal(gd, od)
 
 
+@pytest.mark.parametrize("M", [48, 16, 24])
+def test_pq_f32_shapes(cuda_ok, M):
+    """fp32 rerank at the c1 shape (d=96, M=48) and other sub-quantizer counts."""
+    n, d, nlist = 50000, 96, 32
+    base = synth.mixture_f32_unit(n, d, 64, 0.05, seed=61)
+    p = synth.build_pq_index(base, nlist, M, seed=61, kmeans_iters=6, pq_iters=5, train_n=20000)
+    p["base_f32"] = p["base_rr"]
+    q = synth.mixture_f32_unit(200, d, 64, 0.05, seed=61, stream_base=1 << 20).numpy()
+    probes, _ = oracle.route_l2(q, p["centroids"], 5)
+    gi, gd = gpu_pq(p, q, probes, 10, 512, f32=True)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              probes, 10, rerank_n=512, base_f32=p["base_f32"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
 def test_pq_edge_probes(cuda_ok, pq_medium):
     """invalid ids, a repeated list, an empty list and k larger than the candidates."""
     p, q = pq_medium
