@@ -47,6 +47,10 @@ CONFIGS = {
                nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(8, 16, 32, 64, 128), seed=20260601,
                desc="c1: residual-PQ IVF, 10M x 96 fp32 unit-norm (4096-comp mixture, sigma 0.05), nlist 4096, "
                     "M=48 x 8b, 10k queries, k=10, rerank_n=512 (fp32 rerank)"),
+    # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
+    "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
+                   nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,
+                   desc="c1-shaped lists at 1M vectors (profiling case)"),
     # reduced copy for quick checks of the harness itself (not a bench line)
     "c1-small": dict(kind="f32", n=400_000, d=96, ncomp=512, sigma=0.05, nlist=512, M=48, train_n=100_000,
                      nq=2000, k=10, rerank_n=512, nprobe=16, sweep=(8, 16, 32), seed=7,

@@ -75,8 +75,6 @@ struct Segment {
     int64_t* key_off = nullptr;
     uint8_t* rr_u8 = nullptr;
     float* rr_f32 = nullptr;
-    uint8_t* ring = nullptr;       // PQ codes in the ring-tile layout (M = 16, 32, 48)
-    int64_t* ring_off = nullptr;   // [nlist] byte offset of each list's tiles
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -86,7 +84,7 @@ struct Segment {
         *this = Segment();
     }
     ListStore view() const {
-        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, ring, ring_off, n};
+        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, n};
     }
 };
 
@@ -132,7 +130,7 @@ struct BatchCtx {
     int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
     int res_nq = 0, res_k = 0;
     int probes_nq = 0, probes_np = 0;
-    Grow route_dist, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp;
+    Grow route_dist, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
     Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
     std::vector<void*> owned;
     std::string err;
@@ -254,29 +252,6 @@ void load_lists(IndexCtx* x, Segment& s, const uint8_t* data, size_t row_bytes, 
     s.max_count = max_count;
 }
 
-// Re-lays the segment's PQ codes out as ring tiles (pq.cu) when the kernel
-// supports M; the row-major codes are then no longer kept on the device.
-void build_ring(Segment& s, const long long* offsets, const int* counts, int nlist, int M) {
-    if (!pq_ring_m(M)) return;
-    std::vector<int64_t> roff((size_t)nlist);
-    int64_t acc = 0;
-    for (int l = 0; l < nlist; ++l) {
-        roff[(size_t)l] = acc;
-        acc += pq_ring_list_bytes(counts[l], M);
-    }
-    (void)offsets;
-    s.ring_off = dcopy(roff.data(), roff.size(), s.owned);
-    s.ring = dalloc<uint8_t>((size_t)acc + 64, s.owned);
-    ck(pq_build_ring(s.data, s.offsets, s.counts, s.ring_off, nlist, M, s.ring, 0), "pq_build_ring");
-    ck(cudaDeviceSynchronize(), "pq_build_ring");
-    auto it = std::find(s.owned.begin(), s.owned.end(), (void*)s.data);
-    if (it != s.owned.end()) {
-        cudaFree(*it);
-        s.owned.erase(it);
-    }
-    s.data = nullptr;
-}
-
 void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
     require(centroids != nullptr, "centroids are required");
     x->cent = dcopy(centroids, (size_t)nlist * d, x->owned);
@@ -328,8 +303,15 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     }
 }
 
-WorkList worklist_for(BatchCtx* b, IndexCtx* x, int nsub, int nprobe, void** tmp, size_t* tmp_bytes) {
+WorkList worklist_for(BatchCtx* b, IndexCtx* x, int nsub, int nprobe, void** tmp, size_t* tmp_bytes,
+                      bool groups = false) {
     WorkList wl{};
+    if (groups) {
+        wl.grp_cnt = ensure<int32_t>(b, b->grp_cnt, (size_t)x->nlist + 1);
+        wl.grp_off = ensure<int32_t>(b, b->grp_off, (size_t)x->nlist + 1);
+        wl.groups = ensure<int32_t>(b, b->groups, (size_t)nsub * nprobe);
+        wl.n_groups = wl.grp_off + x->nlist;
+    }
     wl.list_cnt = ensure<int32_t>(b, b->wl_cnt, (size_t)x->nlist + 1);
     wl.list_off = ensure<int32_t>(b, b->wl_off, (size_t)x->nlist + 1);
     wl.cursor = ensure<int32_t>(b, b->wl_cursor, (size_t)x->nlist + 1);
@@ -426,15 +408,15 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     const bool use_delta = overlay && x->has_delta && delta_topk > 0;
     const int Rd = use_delta ? delta_topk : 0;
     require(R <= 4096 && R + Rd <= 4096, "rerank_n + delta_topk must be <= 4096");
-    const int cap_m = nprobe * ceil_div(std::max(x->main.max_count, 1), kPQScanChunk) * std::min(R, kPQScanChunk);
-    const int cap_d = use_delta ? nprobe * ceil_div(std::max(x->delta.max_count, 1), kPQScanChunk) *
-                                      std::min(Rd, kPQScanChunk)
+    const int chunk = pq_scan_chunk(x->M, x->d);
+    const int cap_m = nprobe * ceil_div(std::max(x->main.max_count, 1), chunk) * std::min(R, chunk);
+    const int cap_d = use_delta ? nprobe * ceil_div(std::max(x->delta.max_count, 1), chunk) * std::min(Rd, chunk)
                                 : 0;
     size_t per_q = ((size_t)cap_m + cap_d + R + Rd) * 8 + 32;
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
     void* tmp;
     size_t tmp_bytes;
-    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes);
+    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes, pq_group_usable(x->M, x->d));
     CandBuf cm{}, cd{};
     cm.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap_m);
     cm.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
@@ -653,6 +635,7 @@ void ivf_destroy_batch_context(void* batch_ctx) {
     cudaSetDevice(b->device);
     cudaStreamSynchronize(b->st);
     Grow* gs[] = {&b->route_dist, &b->wl_cnt, &b->wl_off, &b->wl_cursor, &b->pair_q, &b->pair_l, &b->scan_tmp,
+                  &b->grp_cnt, &b->grp_off, &b->groups,
                   &b->cand_m, &b->cand_d, &b->cnt_m, &b->cnt_d, &b->thr_m, &b->thr_d, &b->s1m, &b->s1d, &b->exk};
     for (Grow* g : gs)
         if (g->p) cudaFree(g->p);
@@ -844,7 +827,6 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
                     for (int e = 0; e < dsub; ++e)
                         cbt[((size_t)c * M + m) * dsub + e] = codebook[((size_t)m * K + c) * dsub + e];
             x->codebook_t = dcopy(cbt.data(), cbt.size(), x->owned);
-            build_ring(x->main, offsets, counts, nlist, M);
         } catch (...) {
             x->main.release();
             free_all(x->owned);
@@ -910,7 +892,6 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
             load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
             if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
             else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
-            build_ring(s, offsets, counts, x->nlist, x->M);
         } catch (...) {
             s.release();
             throw;

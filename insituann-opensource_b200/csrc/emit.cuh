@@ -17,7 +17,7 @@ namespace isb {
 
 struct EmitSmem {
     int hist[256];
-    int scratch[40];
+    int scratch[4 * 33];
     int bc[4];
     int base;
 };
@@ -55,6 +55,63 @@ __device__ void block_filter_emit(KeyFn keyf, int n, const CandBuf& cb, int q, E
         }
     }
     __syncthreads();
+}
+
+// Sum over the block of four ints per thread.  scratch: >= 4 * 33 ints.
+template <int T>
+__device__ __forceinline__ int4 block_sum4(int4 v, int* scratch) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int W = T / 32;
+    v.x = warp_sum(v.x);
+    v.y = warp_sum(v.y);
+    v.z = warp_sum(v.z);
+    v.w = warp_sum(v.w);
+    if (lane == 0) {
+        scratch[warp] = v.x;
+        scratch[32 + warp] = v.y;
+        scratch[64 + warp] = v.z;
+        scratch[96 + warp] = v.w;
+    }
+    __syncthreads();
+    int4 r = make_int4(0, 0, 0, 0);
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+        r.x += scratch[w];
+        r.y += scratch[32 + w];
+        r.z += scratch[64 + w];
+        r.w += scratch[96 + w];
+    }
+    __syncthreads();
+    return r;
+}
+
+// Appends, warp by warp, every key k(i) <= cut of the items i = threadIdx.x +
+// j*T (j < ITEMS, i < n) to the query's candidate buffer: one atomic per warp
+// and item round, no block-wide synchronisation.
+template <int T, int ITEMS, class KeyFn>
+__device__ __forceinline__ void warp_append(KeyFn keyf, int n, uint64_t cut, const CandBuf& cb, int q) {
+    const int lane = threadIdx.x & 31;
+    uint64_t* out = cb.keys + (size_t)q * cb.cap;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const int i = threadIdx.x + j * T;
+        uint64_t k = kKeyNone;
+        bool take = false;
+        if (i < n) {
+            k = keyf(i);
+            take = k <= cut;
+        }
+        const unsigned ball = __ballot_sync(0xffffffffu, take);
+        if (ball == 0) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(cb.cnt + q, __popc(ball));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) {
+            const int at = base + __popc(ball & ((1u << lane) - 1u));
+            if (at < cb.cap) out[at] = k;
+            else atomicExch(cb.overflow, 1);
+        }
+    }
 }
 
 // Next (query, list) pair from the global work counter; -1 when done.

@@ -166,8 +166,6 @@ struct ListStore {             // one cluster-major segment (main index or a del
                                // the positions of the whole index so shards merge exactly
     const uint8_t* rr_u8;      // [n, d] rerank rows (u8), PQ only
     const float* rr_f32;       // [n, d] rerank rows (fp32), PQ only
-    const uint8_t* ring;       // PQ codes in the skewed ring-tile layout (pq.cu), or nullptr
-    const int64_t* ring_off;   // [nlist] byte offset of each list's first ring tile
     int64_t n;
 };
 
@@ -178,6 +176,10 @@ struct WorkList {              // probe inversion for one batch: list-major (que
     int32_t* pair_q;           // [max_pairs] query of each pair
     int32_t* pair_l;           // [max_pairs] (local) list of each pair
     int32_t* n_pairs;          // -> list_off[nlist]
+    int32_t* grp_cnt;          // [nlist+1] query groups per list (optional)
+    int32_t* grp_off;          // [nlist+1] exclusive prefix of grp_cnt
+    int32_t* groups;           // [max_pairs] (first pair << 3) | group size, list-major
+    int32_t* n_groups;         // -> grp_off[nlist]
 };
 
 struct CandBuf {               // per-query candidate buffers of one segment

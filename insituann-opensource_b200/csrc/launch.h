@@ -20,9 +20,12 @@ constexpr int kExactScanChunk = 1024; // vectors per filtered chunk in the exact
 size_t worklist_scan_bytes(int nlist);
 // Builds list-major (query, list) pairs from probes [nq, nprobe] (global list
 // ids; list_map maps them to local lists or -1, nullptr = identity).
+// When wl.groups is set, also packs the pairs of every list into groups of up
+// to kGroupQueries consecutive pairs: groups[g] = (first pair << 3) | size.
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
                            void* scan_tmp, size_t scan_bytes, cudaStream_t st);
+constexpr int kGroupQueries = 4;
 
 // ---- coarse routing (route.cu) --------------------------------------------
 // valid[c] = 1 when the centroid's L2 norm is >= 1e-6, else 0.
@@ -66,13 +69,11 @@ struct PQParams {
     int has_delta;
 };
 bool pq_supported_m(int M);
-// M values scanned by the conflict-free ring kernel (others use the row kernel)
-bool pq_ring_m(int M);
-// bytes of the ring-tile layout of one list of `count` vectors
-int64_t pq_ring_list_bytes(int count, int M);
-// builds the ring-tile layout of every list from row-major codes [n, M]
-cudaError_t pq_build_ring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
-                          const int64_t* ring_off, int nlist, int M, uint8_t* out, cudaStream_t st);
+// true when the query-grouped kernel scans (M, d); other shapes use the row kernel
+bool pq_group_usable(int M, int d);
+// vectors per filtered chunk of the kernel that scans (M, d); each chunk keeps at
+// most R candidates per query, which bounds the candidate buffers
+int pq_scan_chunk(int M, int d);
 cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* work_counter,
                     cudaStream_t st);
 // Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).

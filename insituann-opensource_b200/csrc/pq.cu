@@ -125,194 +125,214 @@ __global__ void __launch_bounds__(kPT) pq_scan_kernel(PQParams p, WorkList wl, C
 
 
 // ---------------------------------------------------------------------------
-// Ring ADC scan (M = 16, 32, 48): conflict-free LUT gathers, same sum order.
+// Query-grouped ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8).
 //
-// A warp runs two 16-lane systolic rings.  Lane j of a ring owns the MPL = M/16
-// consecutive sub-quantizers m = MPL*j .. MPL*j+MPL-1: at step x it takes the
-// partial sum of vector x-j from lane j-1 (shuffle), adds its MPL LUT entries
-// in m order and passes the sum on; lane 15 finishes vector x-15.  Every
-// vector's distance is therefore sum_m LUT[m][code[m]] accumulated in m
-// order, exactly as in the row kernel and the CPU restatement.
-//
-// The LUT is stored as rows of S floats per code value c (S a multiple of 32),
-// holding two copies of the M entries at column positions posA(m) and
-// posB(m).  Ring A reads copy A, ring B copy B; the positions are chosen so
-// that in every step the 32 lanes of a warp touch 32 different banks, for any
-// code values:
-//   M=16: A at m, B at 16+m                   (banks j | 16+j)
-//   M=32: A at m, B at 32+((m+1)&31)          (banks of opposite parity)
-//   M=48: A at m, B at 48+m                   (banks 3j+s | 3j+s+16, disjoint as 3 is odd)
-//
-// Codes are re-laid out once per index (pq_build_ring) into tiles of 16 steps:
-// tile T of a list holds, for lane j, step i and sub-quantizer s, the byte
-// code[16T+i-j][MPL*j+s] (0 outside the list).  A lane reads its 16*MPL bytes
-// of a tile with MPL coalesced 16-byte loads and indexes them statically.
+// One CTA takes one inverted list and up to kGQ = 4 of the queries that probe
+// it (consecutive list-major pairs).  The four LUTs are interleaved as
+// float4 lut[c * P + m] = (LUT_q0[m][c], .., LUT_q3[m][c]), so one 16-byte
+// shared load serves four lookups and every code byte loaded from HBM is used
+// by four queries.  The row pitch P = M + 1 makes the 16-byte bank group of
+// an entry depend on c + m instead of on m alone (with P = M, a multiple of 8,
+// all 32 lanes of a warp would hit the same bank group).  Each thread scans
+// whole vectors and accumulates every query's distance in m order, so the
+// sums are the same as in the row kernel and the CPU restatement.
 // ---------------------------------------------------------------------------
+constexpr int kGQ = 4;      // queries per group
+constexpr int kGT = 512;    // threads per CTA
+constexpr int kGChunk = 1024;
+
 template <int M>
-struct Ring {
-    static constexpr int MPL = M / 16;
-    static constexpr int S = M == 16 ? 32 : (M == 32 ? 64 : 96);
-    static constexpr int kTileBytes = 256 * MPL;
-    static constexpr int kChunk = M == 48 ? 3072 : (M == 32 ? 2048 : 4096);
-    __host__ __device__ static constexpr int posA(int m) { return m; }
-    __host__ __device__ static constexpr int posB(int m) {
-        return M == 16 ? 16 + m : (M == 32 ? 32 + ((m + 1) & 31) : 48 + m);
-    }
+struct Grp {
+    static constexpr int P = M + 1;  // LUT row pitch in float4
+    static constexpr size_t lut_bytes() { return sizeof(float4) * 256 * P; }
 };
 
-__host__ __device__ inline int64_t ring_tiles(int count) { return (int64_t)(count + 15) / 16 + 2; }
-
-constexpr int kRingT = 256;  // 8 warps = 16 rings per CTA
-
 template <int M>
-__global__ void __launch_bounds__(kRingT, 2) pq_ring_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
-                                                            int* counter) {
-    using RC = Ring<M>;
-    constexpr int MPL = RC::MPL, S = RC::S, CH = RC::kChunk;
-    extern __shared__ __align__(16) float smf[];
-    float* lut = smf;                // [256][S]
-    float* dist = lut + 256 * S;     // [CH]; holds the query residual while the LUT is built
-    __shared__ EmitSmem esm;
-    __shared__ int s_item;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ring = lane >> 4, j = lane & 15;
-    const int d = p.d, dsub = p.dsub;
-    const float keep = j == 0 ? 0.f : 1.f;
-    int col[MPL];
+__device__ __forceinline__ void grp_vector(const uint8_t* __restrict__ code, const float4* __restrict__ lut, float& s0,
+                                           float& s1, float& s2, float& s3) {
+    const uint4* c4 = reinterpret_cast<const uint4*>(code);
+    uint4 w[M / 16];
 #pragma unroll
-    for (int s = 0; s < MPL; ++s) col[s] = ring ? RC::posB(MPL * j + s) : RC::posA(MPL * j + s);
-    const int P = *wl.n_pairs;
-    const int total = p.has_delta ? 2 * P : P;
+    for (int i = 0; i < M / 16; ++i) w[i] = __ldg(c4 + i);
+    s0 = s1 = s2 = s3 = 0.f;
+#pragma unroll
+    for (int i = 0; i < M / 16; ++i) {
+        const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+        for (int b = 0; b < 16; ++b) {
+            const int m = i * 16 + b;
+            const uint32_t c = (ww[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+            const float4 f = lut[c * Grp<M>::P + m];
+            s0 = __fadd_rn(s0, f.x);
+            s1 = __fadd_rn(s1, f.y);
+            s2 = __fadd_rn(s2, f.z);
+            s3 = __fadd_rn(s3, f.w);
+        }
+    }
+}
+
+template <int M, int DSUB>
+__global__ void __launch_bounds__(kGT, 1) pq_group_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
+                                                          int* counter) {
+    using G = Grp<M>;
+    constexpr int d = M * DSUB;
+    extern __shared__ __align__(16) float smf[];
+    float4* lut = reinterpret_cast<float4*>(smf);                    // [256][P]
+    float* dist = smf + 4 * 256 * G::P;                               // [kGQ][kGChunk]; residuals during the LUT build
+    __shared__ EmitSmem esm;
+    __shared__ int s_item, s_q[kGQ];
+    const int tid = threadIdx.x;
+    const int NG = *wl.n_groups;
+    const int total = p.has_delta ? 2 * NG : NG;
     for (;;) {
         const int it = next_item(counter, total, &s_item);
         if (it < 0) break;
-        const bool seg_delta = it >= P;
-        const int pi = seg_delta ? it - P : it;
-        const int q = wl.pair_q[pi], l = wl.pair_l[pi];
+        const bool seg_delta = it >= NG;
+        const int gi = seg_delta ? it - NG : it;
+        const int packed = wl.groups[gi];
+        const int p0 = packed >> 3, nqg = packed & 7;
+        const int l = wl.pair_l[p0];
         const ListStore& SG = seg_delta ? p.delta : p.main;
         const CandBuf& cb = seg_delta ? cd : cm;
         const int count = SG.counts[l];
         if (count <= 0) continue;
-        const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
-        const uint8_t* tiles = SG.ring + SG.ring_off[l];
-        const int64_t ntiles = ring_tiles(count);
-        {
-            const float* qv = p.q + (size_t)q * d;
+        const int64_t off = SG.offsets[l];
+        const int64_t koff = SG.key_off ? SG.key_off[l] : off;
+        if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
+        __syncthreads();
+        {   // residuals of the group's queries, then the interleaved LUT
+            float* resid = dist;   // [kGQ][d]
             const float* cv = p.cent + (size_t)l * d;
-            float* resid = dist;
-            for (int e = tid; e < d; e += kRingT) resid[e] = __fsub_rn(qv[e], cv[e]);
+            for (int e = tid; e < kGQ * d; e += kGT) {
+                const int k = e / d, x = e - k * d;
+                const int qk = s_q[k];
+                resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
+            }
             __syncthreads();
-            for (int mm = lane; mm < M; mm += 32) {
-                const float* rv = resid + mm * dsub;
-                for (int c = warp; c < kCodes; c += kRingT / 32) {
-                    const float* cbv = p.codebook_t + ((size_t)c * M + mm) * dsub;
-                    float acc = 0.f;
-                    for (int e = 0; e < dsub; ++e) {
-                        const float x = __fsub_rn(rv[e], __ldg(cbv + e));
-                        acc = __fadd_rn(acc, __fmul_rn(x, x));
+            // thread t owns sub-quantizer m = t % M for codes c = t / M, t / M + kGT / M, ...
+            constexpr int kCStep = kGT / M;
+            if (tid < kCStep * M) {
+                const int m = tid % M, c0 = tid / M;
+                float r[kGQ][DSUB];
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k)
+#pragma unroll
+                    for (int u = 0; u < DSUB; ++u) r[k][u] = resid[k * d + m * DSUB + u];
+                for (int c = c0; c < 256; c += kCStep) {
+                    float cbv[DSUB];
+                    const float* src = p.codebook_t + ((size_t)c * M + m) * DSUB;
+                    if constexpr (DSUB % 4 == 0) {
+#pragma unroll
+                        for (int u = 0; u < DSUB; u += 4) {
+                            const float4 t4 = __ldg(reinterpret_cast<const float4*>(src + u));
+                            cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < DSUB; u += 2) {
+                            const float2 t2 = __ldg(reinterpret_cast<const float2*>(src + u));
+                            cbv[u] = t2.x; cbv[u + 1] = t2.y;
+                        }
                     }
-                    lut[c * S + RC::posA(mm)] = acc;
-                    lut[c * S + RC::posB(mm)] = acc;
+                    float acc[kGQ];
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k) {
+                        const float x0 = __fsub_rn(r[k][0], cbv[0]);
+                        float a = __fmul_rn(x0, x0);   // == 0 + x0*x0 exactly
+#pragma unroll
+                        for (int u = 1; u < DSUB; ++u) {
+                            const float x = __fsub_rn(r[k][u], cbv[u]);
+                            a = __fadd_rn(a, __fmul_rn(x, x));
+                        }
+                        acc[k] = a;
+                    }
+                    lut[c * G::P + m] = make_float4(acc[0], acc[1], acc[2], acc[3]);
                 }
             }
             __syncthreads();
         }
-        for (int cs = 0; cs < count; cs += CH) {
-            const int len = min(CH, count - cs);
-            const int Lr = (((len + 15) / 16) + 15) & ~15;  // vectors per ring, multiple of 16
-            const int a = cs + (warp * 2 + ring) * Lr;     // this ring's list-relative range [a, b)
-            const int b = min(a + Lr, cs + len);
-            if (cs + warp * 2 * Lr < cs + len) {           // ring A of this warp has work
-                float sv = 0.f, carry = 0.f;
-                const int T0 = a / 16;
-                const int ntr = Lr / 16 + 1;
-                for (int tt = 0; tt < ntr; ++tt) {
-                    const int64_t T = min((int64_t)(T0 + tt), ntiles - 1);
-                    const uint4* tp = reinterpret_cast<const uint4*>(tiles + T * RC::kTileBytes + j * 16 * MPL);
-                    uint32_t w[4 * MPL];
-#pragma unroll
-                    for (int u = 0; u < MPL; ++u) {
-                        const uint4 x = __ldg(tp + u);
-                        w[4 * u + 0] = x.x;
-                        w[4 * u + 1] = x.y;
-                        w[4 * u + 2] = x.z;
-                        w[4 * u + 3] = x.w;
-                    }
-                    float o[16];
-                    o[0] = carry;
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float sin = __shfl_up_sync(0xffffffffu, sv, 1, 16);
-#pragma unroll
-                        for (int s = 0; s < MPL; ++s) {
-                            const int byte = i * MPL + s;
-                            const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
-                            const float v = lut[c * S + col[s]];
-                            sv = (s == 0) ? fmaf(sin, keep, v) : __fadd_rn(sv, v);
-                        }
-                        if (i < 15) o[i + 1] = sv;
-                        else carry = sv;
-                    }
-                    if (j == 15) {
-                        const int gb = 16 * (T0 + tt) - 16;   // list-relative vectors gb .. gb+15
-                        if (gb >= a && gb + 16 <= b) {
-                            float4* dp = reinterpret_cast<float4*>(dist + (gb - cs));
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) dp[e] = make_float4(o[4 * e], o[4 * e + 1], o[4 * e + 2], o[4 * e + 3]);
-                        } else {
-#pragma unroll
-                            for (int e = 0; e < 16; ++e)
-                                if (gb + e >= a && gb + e < b) dist[gb + e - cs] = o[e];
-                        }
-                    }
+        for (int cs = 0; cs < count; cs += kGChunk) {
+            const int len = min(kGChunk, count - cs);
+            const uint8_t* codes = SG.data + (size_t)(off + cs) * M;
+            for (int v = tid; v < len; v += 2 * kGT) {
+                const int v2 = v + kGT;
+                float a0, a1, a2, a3, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+                grp_vector<M>(codes + (size_t)v * M, lut, a0, a1, a2, a3);
+                if (v2 < len) grp_vector<M>(codes + (size_t)v2 * M, lut, b0, b1, b2, b3);
+                dist[v] = a0;
+                dist[kGChunk + v] = a1;
+                dist[2 * kGChunk + v] = a2;
+                dist[3 * kGChunk + v] = a3;
+                if (v2 < len) {
+                    dist[v2] = b0;
+                    dist[kGChunk + v2] = b1;
+                    dist[2 * kGChunk + v2] = b2;
+                    dist[3 * kGChunk + v2] = b3;
                 }
             }
             __syncthreads();
             const uint32_t kbase = (uint32_t)(koff + cs);
-            auto keyf = [&](int i) -> uint64_t { return make_key(__float_as_uint(dist[i]), kbase + (uint32_t)i); };
-            block_filter_emit<kRingT>(keyf, len, cb, q, esm);
+            // one block reduction gives the four queries' survivor counts
+            uint64_t thr[kGQ];
+            int cnt4[kGQ];
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k) {
+                thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_q[k])) : 0ull;
+                cnt4[k] = 0;
+            }
+#pragma unroll
+            for (int jj = 0; jj < kGChunk / kGT; ++jj) {
+                const int i = tid + jj * kGT;
+                if (i < len) {
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k)
+                        cnt4[k] += (k < nqg && make_key(__float_as_uint(dist[k * kGChunk + i]), kbase + (uint32_t)i) <= thr[k]) ? 1 : 0;
+                }
+            }
+            const int4 tot = block_sum4<kGT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
+            const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k) {
+                if (k >= nqg || totk[k] == 0) continue;
+                const float* dk = dist + k * kGChunk;
+                auto keyf = [&](int i) -> uint64_t { return make_key(__float_as_uint(dk[i]), kbase + (uint32_t)i); };
+                uint64_t cut = thr[k];
+                if (totk[k] > cb.R) {   // more survivors than the rank budget: keep only the R best
+                    const uint64_t kap = block_kth_key<kGT>(keyf, len, cb.R, thr[k], esm.hist, esm.bc);
+                    cut = kap < thr[k] ? kap : thr[k];
+                    if (tid == 0) atomicMin(cb.thr + s_q[k], (unsigned long long)cut);
+                }
+                warp_append<kGT, kGChunk / kGT>(keyf, len, cut, cb, s_q[k]);
+            }
+            __syncthreads();
         }
     }
 }
 
-template <int M>
-cudaError_t launch_ring(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* counter,
-                        cudaStream_t st) {
-    using RC = Ring<M>;
-    const size_t smem = sizeof(float) * ((size_t)256 * RC::S + RC::kChunk);
-    if ((size_t)p.d > RC::kChunk) return cudaErrorInvalidValue;  // the residual is staged in the distance array
-    cudaError_t e = cudaFuncSetAttribute(pq_ring_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+template <int M, int DSUB>
+size_t group_smem_bytes() {
+    return Grp<M>::lut_bytes() + sizeof(float) * kGQ * kGChunk;
+}
+
+template <int M, int DSUB>
+cudaError_t launch_group(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
+                         cudaStream_t st) {
+    const size_t smem = group_smem_bytes<M, DSUB>();
+    cudaError_t e =
+        cudaFuncSetAttribute(pq_group_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_ring_kernel<M>, kRingT, smem);
-    if (per_sm < 1) per_sm = 1;
-    long long items = (long long)max_pairs * (p.has_delta ? 2 : 1);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_group_kernel<M, DSUB>, kGT, smem);
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    long long items = (long long)max_groups * (p.has_delta ? 2 : 1);
     long long grid = (long long)sms * per_sm;
     if (grid > items) grid = items;
     if (grid < 1) grid = 1;
     note_launch();
-    pq_ring_kernel<M><<<(int)grid, kRingT, smem, st>>>(p, wl, cm, cd, counter);
+    pq_group_kernel<M, DSUB><<<(int)grid, kGT, smem, st>>>(p, wl, cm, cd, counter);
     return cudaGetLastError();
-}
-
-template <int MPL>
-__global__ void ring_layout_kernel(const uint8_t* __restrict__ codes, const int64_t* __restrict__ offsets,
-                                   const int32_t* __restrict__ counts, const int64_t* __restrict__ ring_off,
-                                   int nlist, int M, uint8_t* __restrict__ out) {
-    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
-        const int cnt = counts[l];
-        const int64_t off = offsets[l];
-        const int64_t total = ring_tiles(cnt) * 256 * MPL;
-        uint8_t* dst = out + ring_off[l];
-        for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
-            const int64_t T = e / (256 * MPL);
-            const int r = (int)(e % (256 * MPL));
-            const int jj = r / (16 * MPL), r2 = r % (16 * MPL), i = r2 / MPL, s = r2 % MPL;
-            const int64_t v = 16 * T + i - jj;
-            dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
-        }
-    }
 }
 
 template <int M>
@@ -510,22 +530,12 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
 
 bool pq_supported_m(int M) { return M > 0 && M <= 64 && M % 8 == 0; }
 
-bool pq_ring_m(int M) { return M == 16 || M == 32 || M == 48; }
+int pq_scan_chunk(int M, int d) { return pq_group_usable(M, d) ? kGChunk : kPChunk; }
 
-int64_t pq_ring_list_bytes(int count, int M) { return ring_tiles(count) * 256 * (M / 16); }
-
-cudaError_t pq_build_ring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
-                          const int64_t* ring_off, int nlist, int M, uint8_t* out, cudaStream_t st) {
-    if (!pq_ring_m(M)) return cudaErrorInvalidValue;
-    if (nlist <= 0) return cudaSuccess;
-    const int grid = nlist < 4096 ? nlist : 4096;
-    note_launch();
-    switch (M / 16) {
-        case 1: ring_layout_kernel<1><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
-        case 2: ring_layout_kernel<2><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
-        default: ring_layout_kernel<3><<<grid, 256, 0, st>>>(codes, offsets, counts, ring_off, nlist, M, out); break;
-    }
-    return cudaGetLastError();
+bool pq_group_usable(int M, int d) {
+    if (M <= 0 || d % M != 0) return false;
+    const int dsub = d / M;
+    return (M == 16 || M == 32 || M == 48) && (dsub == 2 || dsub == 4 || dsub == 8);
 }
 
 cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* counter,
@@ -534,13 +544,14 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
     if (max_pairs <= 0) return cudaSuccess;
     cudaError_t e = cudaMemsetAsync(counter, 0, sizeof(int), st);
     if (e) return e;
-    const bool ring = pq_ring_m(p.M) && p.main.ring && (!p.has_delta || p.delta.ring) && p.codebook_t;
-    if (ring) {
-        switch (p.M) {
-            case 16: return launch_ring<16>(p, wl, max_pairs, cm, cd, counter, st);
-            case 32: return launch_ring<32>(p, wl, max_pairs, cm, cd, counter, st);
-            default: return launch_ring<48>(p, wl, max_pairs, cm, cd, counter, st);
-        }
+    if (pq_group_usable(p.M, p.d) && wl.groups && p.codebook_t) {
+        const int ds = p.d / p.M;
+#define ISB_GROUP(MM, DS) \
+    if (p.M == MM && ds == DS) return launch_group<MM, DS>(p, wl, max_pairs, cm, cd, counter, st);
+        ISB_GROUP(16, 2) ISB_GROUP(16, 4) ISB_GROUP(16, 8)
+        ISB_GROUP(32, 2) ISB_GROUP(32, 4) ISB_GROUP(32, 8)
+        ISB_GROUP(48, 2) ISB_GROUP(48, 4)
+#undef ISB_GROUP
     }
     switch (p.M) {
         case 8: return launch_scan<8>(p, wl, max_pairs, cm, cd, counter, st);

@@ -44,6 +44,23 @@ __global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprob
     }
 }
 
+__global__ void group_count_kernel(const int32_t* list_cnt, int nlist, int32_t* grp_cnt) {
+    int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l < nlist) grp_cnt[l] = (list_cnt[l] + kGroupQueries - 1) / kGroupQueries;
+    else if (l == nlist) grp_cnt[l] = 0;
+}
+
+__global__ void group_fill_kernel(const int32_t* list_off, const int32_t* grp_off, int nlist, int32_t* groups) {
+    int l = blockIdx.x * blockDim.x + threadIdx.x;
+    if (l >= nlist) return;
+    const int first = list_off[l], n = list_off[l + 1] - first;
+    int g = grp_off[l];
+    for (int o = 0; o < n; o += kGroupQueries) {
+        const int sz = n - o < kGroupQueries ? n - o : kGroupQueries;
+        groups[g++] = ((first + o) << 3) | sz;
+    }
+}
+
 int grid_for(size_t total, int threads) {
     size_t b = (total + threads - 1) / threads;
     if (b < 1) b = 1;
@@ -78,6 +95,16 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
         note_launch();
         fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, nlist_global, list_map,
                                                                 wl.list_off, wl.cursor, wl.pair_q, wl.pair_l);
+        if ((e = cudaGetLastError())) return e;
+    }
+    if (wl.groups) {
+        note_launch();
+        group_count_kernel<<<(nlist_local + 256) / 256, 256, 0, st>>>(wl.list_cnt, nlist_local, wl.grp_cnt);
+        if ((e = cudaGetLastError())) return e;
+        if ((e = cub::DeviceScan::ExclusiveSum(scan_tmp, scan_bytes, wl.grp_cnt, wl.grp_off, nlist_local + 1, st)))
+            return e;
+        note_launch();
+        group_fill_kernel<<<(nlist_local + 255) / 256, 256, 0, st>>>(wl.list_off, wl.grp_off, nlist_local, wl.groups);
         if ((e = cudaGetLastError())) return e;
     }
     return cudaSuccess;
