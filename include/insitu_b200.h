@@ -266,6 +266,31 @@ int ivf_u8_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
 int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int k);
 
 /* ======================================================================
+ * Allocation-free search (no counterpart in the reference)
+ * ====================================================================== */
+/*
+ * Exact uint8 search for callers that must not allocate device memory while
+ * they serve queries (a database worker whose device memory is budgeted up
+ * front, a real-time service that must avoid the allocator and its implicit
+ * synchronisation, a caller that brings its own stream and buffer pool).
+ * Same results as ivf_u8_search on the probe table d_probes; every argument
+ * is a device pointer on the index's device and the work is queued on
+ * `stream` (a cudaStream_t; NULL = legacy default stream), so the outputs are
+ * ready once that stream has synchronised.
+ *
+ * All scratch comes from one fixed 16 MiB array compiled into the library,
+ * held by every GPU that loads the library until the process exits.  The
+ * call allocates nothing; a batch whose scratch would exceed 16 MiB is
+ * rejected with IVF_EINVAL (message in ivf_global_last_error()) -- split it
+ * into smaller batches.  The first call on each device looks up the array's
+ * device address; make that first call before any stream capture.  Calls
+ * share the array: two calls that overlap on the GPU race, so order them on
+ * one stream or synchronise between them.
+ */
+int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, const int* d_probes, int n_query, int n_probes,
+                          int k, int* d_out_ids, int* d_out_dist, void* stream);
+
+/* ======================================================================
  * observability
  * ====================================================================== */
 /* number of kernels this library has launched in this process (all devices) */

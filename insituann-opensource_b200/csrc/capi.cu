@@ -525,6 +525,22 @@ thread_local CoarseTimingBreakdown g_coarse_timing;
 
 namespace isb {
 void note_launch(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+bool u8_index_view(void* idx_ctx, ListStore* ls, int* nlist, int* nlist_global, const int32_t** g2l, int* d,
+                   int* max_count, int* device) {
+    auto* x = static_cast<IndexCtx*>(idx_ctx);
+    if (!x || x->magic != kIdxMagic || x->kind != kKindU8) return false;
+    *ls = x->main.view();
+    *nlist = x->nlist;
+    *nlist_global = x->nlist_global;
+    *g2l = x->g2l;
+    *d = x->d;
+    *max_count = x->main.max_count;
+    *device = x->device;
+    return true;
+}
+
+void set_global_error(const std::string& msg) { g_err = msg; }
 }  // namespace isb
 
 // ===========================================================================

@@ -40,7 +40,7 @@ EXPORTS = [
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
     "ivf_route_keys", "ivf_route_merge", "ivf_pq_search_shard", "ivf_pq_merge_shards",
     "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_last_error", "ivf_global_last_error",
-    "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms",
+    "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms", "ivf_u8_search_noalloc",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
     "cuda_pipeline_init", "cuda_pipeline_flush", "cuda_pipeline_flush_vectors_only", "cuda_pipeline_free",
@@ -95,6 +95,7 @@ _SIGS = {
     "ivf_kernel_launches": ([], C.c_ulonglong),
     "ivf_batch_profile": ([vp, i32], i32),
     "ivf_batch_stage_ms": ([vp, vp, i32], i32),
+    "ivf_u8_search_noalloc": ([vp, vp, vp, i32, i32, i32, vp, vp, vp], i32),
 }
 
 STAGES = ("route", "worklist", "scan", "select", "rerank")
