@@ -43,8 +43,9 @@ METRIC = "QPS @ recall@10≥0.9 vs nprobe; scanned GB/s vs 8 TB/s HBM; at 1/2/4/
 
 CONFIGS = {
     # BASELINE.json configs[1]
+    # nprobe: the smallest sweep point whose recall@10 is >= 0.9 on this data (0.99998 measured at 8)
     "c1": dict(kind="f32", n=10_000_000, d=96, ncomp=4096, sigma=0.05, nlist=4096, M=48, train_n=500_000,
-               nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(8, 16, 32, 64, 128), seed=20260601,
+               nq=10_000, k=10, rerank_n=512, nprobe=8, sweep=(8, 16, 32, 64, 128), seed=20260601,
                desc="c1: residual-PQ IVF, 10M x 96 fp32 unit-norm (4096-comp mixture, sigma 0.05), nlist 4096, "
                     "M=48 x 8b, 10k queries, k=10, rerank_n=512 (fp32 rerank)"),
     # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
@@ -262,7 +263,7 @@ def main():
     if N > 1:
         from datetime import timedelta
 
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     nq, d, k, R, M = cfg["nq"], cfg["d"], cfg["k"], cfg["rerank_n"], cfg["M"]
     nlist = cfg["nlist"]
     nprobe = args.nprobe or cfg["nprobe"]
@@ -479,11 +480,13 @@ def main():
     peak, peak_kind = peaks()
     achieved = bytes_per_launch / (scan_ms / 1000.0) / 1e9
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", "pq_scan_c1_traffic.json")
-    if os.path.exists(prof_path) and args.config == "c1" and N == 1:
-        traffic = json.load(open(prof_path)).get("dram_bytes_per_launch")
+    prof_path = os.path.join(ROOT, "profiles", f"pq_group_kernel_{args.config}_nprobe{nprobe}.md")
+    if os.path.exists(prof_path) and N == 1:
+        for line in open(prof_path):
+            if line.startswith("dram_bytes_per_launch:"):
+                traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "pq_scan_kernel<48>", "peak_source": peak_kind,
+                "traffic": traffic, "kernel": "pq_group_kernel<48,2>", "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_ms_per_launch": scan_ms}
 
     cpu = None
@@ -502,7 +505,8 @@ def main():
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": cfg["desc"], "n_base": cfg["n"], "d": d, "nlist": nlist, "M": M,
                        "nq": nq, "nprobe": nprobe, "k": k, "rerank_n": R,
-                       "recall@10": synth.recall_at_k(ids_g, gt, k), "parity_vs_oracle_64q": parity,
+                       "recall@10": synth.recall_at_k(ids_g, gt, k), "recall_target_met": bool(
+                           synth.recall_at_k(ids_g, gt, k) >= 0.9), "parity_vs_oracle_64q": parity,
                        "inputs_exceed_l2": True, "l2_note": "480 MB of codes and 3.84 GB of rerank rows per step",
                        "parallelism": "single GPU" if N == 1 else f"lists sharded x{N} (LPT by bytes), NCCL"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
