@@ -225,7 +225,7 @@ def run_reference_arm(args, cfg):
                                    f"cpu_fine_kernel_pq_resid stage 1 + fp32 rerank ({r['lib']})"},
         "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(out))
+    print(json.dumps(out), flush=True)
 
 
 # ----------------------------------------------------------------------------
@@ -262,6 +262,9 @@ def main():
     dev = torch.device("cuda", local)
     if N > 1:
         from datetime import timedelta
+
+        # NCCL logs to stdout by default; rank 0's stdout must be the JSON line alone
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     nq, d, k, R, M = cfg["nq"], cfg["d"], cfg["k"], cfg["rerank_n"], cfg["M"]
@@ -514,12 +517,17 @@ def main():
             "gbs_scanned_logical": bytes_total / (ms_step / 1000.0) / 1e9,
             "sweep": sweep,
         }
-        print(json.dumps(out))
-    batch.close()
-    index.close()
+        print(json.dumps(out), flush=True)
+    torch.cuda.synchronize()
     if N > 1:
+        # tensors that took part in collectives on the batch stream keep references to it
+        # until the interpreter frees them, so that stream must outlive them: the batch
+        # context is left to process exit
         dist.barrier()
         dist.destroy_process_group()
+        return
+    batch.close()
+    index.close()
 
 
 if __name__ == "__main__":
