@@ -151,18 +151,6 @@ def algorithmic_bytes(probes, counts, M):
     return int(counts[p].astype(np.int64).sum()) * M
 
 
-def lpt_shards(counts, row_bytes, n_shards):
-    """Longest-processing-time assignment of lists to shards by bytes."""
-    order = np.argsort(-(counts.astype(np.int64) * row_bytes), kind="stable")
-    load = np.zeros(n_shards, np.int64)
-    owner = np.empty(len(counts), np.int32)
-    for l in order:
-        s = int(np.argmin(load))
-        owner[l] = s
-        load[s] += int(counts[l]) * row_bytes
-    return owner
-
-
 # ----------------------------------------------------------------------------
 # reference arm / CPU baseline
 # ----------------------------------------------------------------------------
@@ -252,6 +240,7 @@ def main():
 
     import insitu_b200 as ib
     import oracle
+    import shard
     import synth
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -305,12 +294,9 @@ def main():
                       base_f32=idx["base_rr"])
         my_lists = np.arange(nlist)
     else:
-        owner = lpt_shards(counts, M + 4 * d, N)
+        owner = shard.lpt_shards(counts, M + 4 * d, N)
         my_lists = np.where(owner == rank)[0].astype(np.int32)
-        rows = np.concatenate([np.arange(offsets[l], offsets[l] + counts[l]) for l in my_lists])
-        cnt = counts[my_lists]
-        off = np.zeros(len(my_lists), np.int64)
-        off[1:] = np.cumsum(cnt, dtype=np.int64)[:-1]
+        rows, off, cnt = shard.shard_rows(offsets, counts, my_lists)
         index.load_pq(idx["centroids"][my_lists], idx["codebook"], idx["codes"][rows], off, cnt, idx["r2o"][rows],
                       base_f32=idx["base_rr"][rows])
         index.set_shard(nlist, my_lists, offsets[my_lists])
@@ -322,15 +308,15 @@ def main():
         assert nq % N == 0, "nq must divide by the GPU count"
         qo = nq // N
         keys_l = torch.empty((nq, nprobe), dtype=torch.int64, device=dev)
-        keys_all = torch.empty((N, nq, nprobe), dtype=torch.int64, device=dev)
+        keys_all = torch.empty((N * nq, nprobe), dtype=torch.int64, device=dev)
         adc = torch.empty((nq, R), dtype=torch.int64, device=dev)
         exa = torch.empty((nq, R), dtype=torch.int64, device=dev)
         adc_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
         exa_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
         out_ids = torch.empty((qo, k), dtype=torch.int32, device=dev)
         out_dist = torch.empty((qo, k), dtype=torch.float32, device=dev)
-        all_ids = torch.empty((N, qo, k), dtype=torch.int32, device=dev)
-        all_dist = torch.empty((N, qo, k), dtype=torch.float32, device=dev)
+        all_ids = torch.empty((N * qo, k), dtype=torch.int32, device=dev)
+        all_dist = torch.empty((N * qo, k), dtype=torch.float32, device=dev)
 
     def step(np_=nprobe):
         batch.stage1_prepare_device(q_dev.data_ptr(), nq)
@@ -339,18 +325,14 @@ def main():
             return
         with torch.cuda.stream(ext):
             batch.route_keys(index, nq, np_, keys_l.data_ptr())
-            dist.all_gather_into_tensor(keys_all, keys_l)
-            kt = keys_all.permute(1, 0, 2).contiguous()
+            kt = shard.gather_route_keys(dist, keys_l, keys_all)
             batch.route_merge(kt.data_ptr(), N * np_, nq, np_)
             batch.pq_search_shard(index, nq, np_, R, 0, adc.data_ptr(), exa.data_ptr())
-            dist.all_to_all_single(adc_r, adc.view(N, qo, R))
-            dist.all_to_all_single(exa_r, exa.view(N, qo, R))
-            A = adc_r.permute(1, 0, 2).contiguous()
-            E = exa_r.permute(1, 0, 2).contiguous()
+            A = shard.to_owners(dist, N, adc, adc_r)
+            E = shard.to_owners(dist, N, exa, exa_r)
             batch.pq_merge_shards(A.data_ptr(), E.data_ptr(), N * R, R, None, None, 0, 0, qo, k, False)
             batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
-            dist.all_gather_into_tensor(all_ids, out_ids)
-            dist.all_gather_into_tensor(all_dist, out_dist)
+            shard.gather_results(dist, out_ids, out_dist, all_ids, all_dist)
 
     def results():
         if N == 1:

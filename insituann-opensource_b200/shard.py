@@ -1,0 +1,68 @@
+"""Cluster-sharded multi-GPU exchange for the IVF query path.
+
+The reference searches on one GPU only (updates/pq_update.cu:676); this module
+is the host side of the sharded path: inverted lists are placed on ranks by
+bytes (LPT), and one query batch moves through three collectives:
+
+  1. every rank's local routing keys (distance bits << 32 | global list id,
+     [nq, nprobe], sorted) are all-gathered, so every rank can form the
+     global top-nprobe (ivf_route_merge);
+  2. every rank's per-query stage-1 lists (ADC key, exact key) are sent to the
+     rank that owns the query (block partition of the batch) with one
+     all-to-all, and the owner merges them (ivf_pq_merge_shards);
+  3. the owners' top-k are all-gathered.
+
+The functions take torch tensors and a process group, so the same code runs
+over NCCL with device tensors (bench.py) and over gloo with CPU tensors
+(tests/test_shard_gloo.py).
+"""
+from __future__ import annotations
+
+import numpy as np
+
+
+def lpt_shards(counts: np.ndarray, row_bytes: int, n_shards: int) -> np.ndarray:
+    """Owner rank of every list: longest-processing-time placement by bytes."""
+    order = np.argsort(-(np.asarray(counts, np.int64) * row_bytes), kind="stable")
+    load = np.zeros(n_shards, np.int64)
+    owner = np.empty(len(counts), np.int32)
+    for l in order:
+        s = int(np.argmin(load))
+        owner[l] = s
+        load[s] += int(counts[l]) * row_bytes
+    return owner
+
+
+def shard_rows(offsets: np.ndarray, counts: np.ndarray, lists: np.ndarray):
+    """Rows (cluster-major positions) of the given lists and their local offsets."""
+    rows = np.concatenate([np.arange(offsets[l], offsets[l] + counts[l], dtype=np.int64) for l in lists]) \
+        if len(lists) else np.zeros(0, np.int64)
+    cnt = np.asarray(counts)[lists].astype(np.int32)
+    off = np.zeros(len(lists), np.int64)
+    if len(lists):
+        off[1:] = np.cumsum(cnt, dtype=np.int64)[:-1]
+    return rows, off, cnt
+
+
+def gather_route_keys(dist, keys_local, keys_all):
+    """keys_local [nq, nprobe] -> [nq, world * nprobe] (contiguous), via all-gather.
+
+    keys_all is the receive buffer, [world * nq, nprobe] (ranks concatenated)."""
+    nq, nprobe = keys_local.shape
+    dist.all_gather_into_tensor(keys_all, keys_local)
+    return keys_all.reshape(-1, nq, nprobe).permute(1, 0, 2).contiguous().reshape(nq, -1)
+
+
+def to_owners(dist, world, per_query, recv):
+    """per_query [nq, R] (nq = world * qo, block-partitioned) -> owners' [qo, world * R]."""
+    nq, R = per_query.shape
+    qo = nq // world
+    dist.all_to_all_single(recv, per_query.reshape(world, qo, R))  # recv [world (source), qo, R]
+    return recv.permute(1, 0, 2).contiguous().reshape(qo, world * R)
+
+
+def gather_results(dist, ids_local, dist_local, ids_all, dist_all):
+    """owners' [qo, k] results -> [world * qo, k] on every rank (buffers [world * qo, k])."""
+    dist.all_gather_into_tensor(ids_all, ids_local)
+    dist.all_gather_into_tensor(dist_all, dist_local)
+    return ids_all.reshape(-1, ids_local.shape[1]), dist_all.reshape(-1, dist_local.shape[1])
