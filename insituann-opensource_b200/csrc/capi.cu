@@ -75,6 +75,8 @@ struct Segment {
     int64_t* key_off = nullptr;
     uint8_t* rr_u8 = nullptr;
     float* rr_f32 = nullptr;
+    uint8_t* gring = nullptr;      // PQ codes in the grouped-ring tile layout
+    int64_t* gring_off = nullptr;  // [nlist] byte offset of each list's tiles
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -84,7 +86,7 @@ struct Segment {
         *this = Segment();
     }
     ListStore view() const {
-        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, n};
+        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, gring, gring_off, n};
     }
 };
 
@@ -250,6 +252,28 @@ void load_lists(IndexCtx* x, Segment& s, const uint8_t* data, size_t row_bytes, 
     s.key_off = key_off ? dcopy(reinterpret_cast<const int64_t*>(key_off), (size_t)nlist, s.owned) : nullptr;
     s.n = n;
     s.max_count = max_count;
+}
+
+// Re-lays a segment's PQ codes out as grouped-ring tiles when the grouped
+// kernel scans this shape; the row-major copy is then dropped from the device.
+void build_gring(Segment& s, const int* counts, int nlist, int M, int d) {
+    if (!pq_group_usable(M, d)) return;
+    std::vector<int64_t> toff((size_t)nlist);
+    int64_t acc = 0;
+    for (int l = 0; l < nlist; ++l) {
+        toff[(size_t)l] = acc;
+        acc += pq_gring_list_bytes(counts[l], M);
+    }
+    s.gring_off = dcopy(toff.data(), toff.size(), s.owned);
+    s.gring = dalloc<uint8_t>((size_t)acc + 64, s.owned);
+    ck(pq_build_gring(s.data, s.offsets, s.counts, s.gring_off, nlist, M, s.gring, 0), "pq_build_gring");
+    ck(cudaDeviceSynchronize(), "pq_build_gring");
+    auto it = std::find(s.owned.begin(), s.owned.end(), (void*)s.data);
+    if (it != s.owned.end()) {
+        cudaFree(*it);
+        s.owned.erase(it);
+    }
+    s.data = nullptr;
 }
 
 void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
@@ -438,18 +462,26 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
+        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
         {
             StageScope stage(b, IVF_STAGE_WORKLIST);
-            ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
-                              tmp, tmp_bytes, b->st),
-               "build_worklist");
             ck(reset_candidates(cm, n, b->st), "reset_candidates");
             if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
         }
-        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
-        {
+        // Two passes over the probe table: every query's nearest list first, which
+        // sets a tight rank-R bound, then the other probes, which then emit few
+        // candidates.  The result does not depend on the order.
+        const int npass = nprobe > 1 ? 2 : 1;
+        for (int pass = 0; pass < npass; ++pass) {
+            const int col0 = pass == 0 ? 0 : 1, ncol = npass == 1 ? nprobe : (pass == 0 ? 1 : nprobe - 1);
+            {
+                StageScope stage(b, IVF_STAGE_WORKLIST);
+                ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
+                                  tmp, tmp_bytes, b->st, col0, ncol),
+                   "build_worklist");
+            }
             StageScope stage(b, IVF_STAGE_SCAN);
-            ck(pq_scan(p, wl, n * nprobe, cm, cd, b->counter, b->st), "pq_scan");
+            ck(pq_scan(p, wl, n * ncol, cm, cd, b->counter, b->st), "pq_scan");
         }
         uint64_t* m_out = adc ? adc + (size_t)s * R : s1m;
         uint64_t* d_out = nullptr;
@@ -843,6 +875,7 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
                     for (int e = 0; e < dsub; ++e)
                         cbt[((size_t)c * M + m) * dsub + e] = codebook[((size_t)m * K + c) * dsub + e];
             x->codebook_t = dcopy(cbt.data(), cbt.size(), x->owned);
+            build_gring(x->main, counts, nlist, M, d);
         } catch (...) {
             x->main.release();
             free_all(x->owned);
@@ -908,6 +941,7 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
             load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
             if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
             else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
+            build_gring(s, counts, x->nlist, x->M, x->d);
         } catch (...) {
             s.release();
             throw;

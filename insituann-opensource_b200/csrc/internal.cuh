@@ -166,6 +166,8 @@ struct ListStore {             // one cluster-major segment (main index or a del
                                // the positions of the whole index so shards merge exactly
     const uint8_t* rr_u8;      // [n, d] rerank rows (u8), PQ only
     const float* rr_f32;       // [n, d] rerank rows (fp32), PQ only
+    const uint8_t* gring;      // PQ codes in the grouped-ring tile layout (pq.cu), or nullptr
+    const int64_t* gring_off;  // [nlist] byte offset of each list's first tile
     int64_t n;
 };
 

@@ -22,9 +22,10 @@ size_t worklist_scan_bytes(int nlist);
 // ids; list_map maps them to local lists or -1, nullptr = identity).
 // When wl.groups is set, also packs the pairs of every list into groups of up
 // to kGroupQueries consecutive pairs: groups[g] = (first pair << 3) | size.
+// Only probe-table columns col0 .. col0+ncol-1 are used (ncol <= 0: to the end).
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
-                           void* scan_tmp, size_t scan_bytes, cudaStream_t st);
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0 = 0, int ncol = 0);
 constexpr int kGroupQueries = 4;
 
 // ---- coarse routing (route.cu) --------------------------------------------
@@ -71,6 +72,11 @@ struct PQParams {
 bool pq_supported_m(int M);
 // true when the query-grouped kernel scans (M, d); other shapes use the row kernel
 bool pq_group_usable(int M, int d);
+// bytes of the grouped-ring tile layout of one list of `count` vectors
+int64_t pq_gring_list_bytes(int count, int M);
+// builds the grouped-ring tile layout of every list from row-major codes [n, M]
+cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
+                           const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st);
 // vectors per filtered chunk of the kernel that scans (M, d); each chunk keeps at
 // most R candidates per query, which bounds the candidate buffers
 int pq_scan_chunk(int M, int d);

@@ -309,6 +309,269 @@ __global__ void __launch_bounds__(kGT, 1) pq_group_kernel(PQParams p, WorkList w
     }
 }
 
+// ---------------------------------------------------------------------------
+// Grouped ring ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8): the kernel the
+// search uses for these shapes.
+//
+// As in pq_group_kernel, a CTA takes one list and up to 4 probing queries and
+// the four LUTs are interleaved as float4.  Instead of one thread summing a
+// whole vector, a warp runs four systolic rings of 8 lanes: lane j of a ring
+// owns the MPL = M/8 consecutive sub-quantizers m = MPL*j .. MPL*j+MPL-1.  At
+// step x it receives the four partial sums of vector x-j from lane j-1
+// (shuffles), adds its MPL entries in m order and passes them on; lane 7
+// finishes vector x-7.  The distance of every query is therefore still the
+// sum over m in m order.
+//
+// LUT row c holds entry m at float4 position p(m) = m/MPL + 8*(m%MPL), so in
+// every gather lane j of a ring reads bank group j: each quarter-warp (one
+// ring) touches 8 distinct 16-byte bank groups and the gather is
+// conflict-free whatever the code values.
+//
+// Codes are re-laid out once per index (pq_build_gring) into tiles of 16
+// steps: tile T of a list holds, for lane j, step i and sub-quantizer s, the
+// byte code[16T+i-j][MPL*j+s] (0 outside the list), so a lane reads its
+// 16*MPL bytes of a tile with MPL coalesced 16-byte loads and indexes them
+// statically.
+// ---------------------------------------------------------------------------
+constexpr int kRW = 8;                 // warps per CTA
+constexpr int kRT = 32 * kRW;          // threads per CTA
+constexpr int kRChunk = 2048;          // vectors per filtered chunk
+constexpr int kRRings = 4 * kRW;       // 8-lane rings per CTA
+
+__host__ __device__ inline int64_t gring_tiles(int count) { return (int64_t)(count + 7) / 16 + 3; }
+
+template <int M>
+struct GRing {
+    static constexpr int MPL = M / 8;
+    static constexpr int kTileBytes = 128 * MPL;
+    __host__ __device__ static constexpr int pos(int m) { return m / MPL + 8 * (m % MPL); }
+    __host__ __device__ static constexpr int inv(int p) { return MPL * (p % 8) + p / 8; }
+    static constexpr size_t smem_bytes() { return sizeof(float4) * ((size_t)256 * M + kRChunk); }
+};
+
+template <int M, int DSUB>
+__global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
+                                                          int* counter) {
+    using RG = GRing<M>;
+    constexpr int MPL = RG::MPL;
+    constexpr int d = M * DSUB;
+    extern __shared__ __align__(16) float smf[];
+    float4* lut = reinterpret_cast<float4*>(smf);          // [256][M], entry m at pos(m)
+    float4* dist4 = lut + 256 * M;                          // [kRChunk] four queries per vector
+    float* resid = reinterpret_cast<float*>(dist4);         // [kGQ][d] while the LUT is built
+    __shared__ EmitSmem esm;
+    __shared__ int s_item, s_q[kGQ];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ring = lane >> 3, j = lane & 7;
+    const float keep = j == 0 ? 0.f : 1.f;
+    const int NG = *wl.n_groups;
+    const int total = p.has_delta ? 2 * NG : NG;
+    for (;;) {
+        const int it = next_item(counter, total, &s_item);
+        if (it < 0) break;
+        const bool seg_delta = it >= NG;
+        const int gi = seg_delta ? it - NG : it;
+        const int packed = wl.groups[gi];
+        const int p0 = packed >> 3, nqg = packed & 7;
+        const int l = wl.pair_l[p0];
+        const ListStore& SG = seg_delta ? p.delta : p.main;
+        const CandBuf& cb = seg_delta ? cd : cm;
+        const int count = SG.counts[l];
+        if (count <= 0) continue;
+        const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
+        const uint8_t* tiles = SG.gring + SG.gring_off[l];
+        const int64_t ntiles = gring_tiles(count);
+        if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
+        __syncthreads();
+        {
+            const float* cv = p.cent + (size_t)l * d;
+            for (int e = tid; e < kGQ * d; e += kRT) {
+                const int k = e / d, x = e - k * d;
+                const int qk = s_q[k];
+                resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
+            }
+            __syncthreads();
+            // thread t owns LUT column pos = t % M (sub-quantizer inv(pos)) for codes c = t / M + kRT / M * i
+            constexpr int kCStep = kRT / M > 0 ? kRT / M : 1;
+            if (tid < kCStep * M) {
+                const int ps = tid % M, m = RG::inv(ps), c0 = tid / M;
+                float r[kGQ][DSUB];
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k)
+#pragma unroll
+                    for (int u = 0; u < DSUB; ++u) r[k][u] = resid[k * d + m * DSUB + u];
+                for (int c = c0; c < 256; c += kCStep) {
+                    float cbv[DSUB];
+                    const float* src = p.codebook_t + ((size_t)c * M + m) * DSUB;
+                    if constexpr (DSUB % 4 == 0) {
+#pragma unroll
+                        for (int u = 0; u < DSUB; u += 4) {
+                            const float4 t4 = __ldg(reinterpret_cast<const float4*>(src + u));
+                            cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < DSUB; u += 2) {
+                            const float2 t2 = __ldg(reinterpret_cast<const float2*>(src + u));
+                            cbv[u] = t2.x; cbv[u + 1] = t2.y;
+                        }
+                    }
+                    float acc[kGQ];
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k) {
+                        const float x0 = __fsub_rn(r[k][0], cbv[0]);
+                        float a = __fmul_rn(x0, x0);
+#pragma unroll
+                        for (int u = 1; u < DSUB; ++u) {
+                            const float x = __fsub_rn(r[k][u], cbv[u]);
+                            a = __fadd_rn(a, __fmul_rn(x, x));
+                        }
+                        acc[k] = a;
+                    }
+                    lut[c * M + ps] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                }
+            }
+            __syncthreads();
+        }
+        // this lane's LUT columns: pos(MPL*j + s) = j + 8*s
+        const float4* lutj = lut + j;
+        for (int cs = 0; cs < count; cs += kRChunk) {
+            const int len = min(kRChunk, count - cs);
+            const int Lr = (((len + kRRings - 1) / kRRings) + 15) & ~15;   // vectors per ring, multiple of 16
+            const int a = cs + (warp * 4 + ring) * Lr;                      // list-relative range [a, b)
+            const int b = min(a + Lr, cs + len);
+            if (cs + warp * 4 * Lr < cs + len) {                            // ring 0 of this warp has work
+                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
+                const int T0 = a / 16;
+                const int ntr = Lr / 16 + 1;
+                const uint8_t* lanebase = tiles + j * 16 * MPL;
+                uint32_t w[4 * MPL], wn[4 * MPL];
+                {
+                    const int64_t T = min((int64_t)T0, ntiles - 1);
+                    const uint4* tp = reinterpret_cast<const uint4*>(lanebase + T * RG::kTileBytes);
+#pragma unroll
+                    for (int u = 0; u < MPL; ++u) {
+                        const uint4 x = __ldg(tp + u);
+                        w[4 * u] = x.x; w[4 * u + 1] = x.y; w[4 * u + 2] = x.z; w[4 * u + 3] = x.w;
+                    }
+                }
+                for (int tt = 0; tt < ntr; ++tt) {
+                    {
+                        const int64_t T = min((int64_t)(T0 + tt + 1), ntiles - 1);
+                        const uint4* tp = reinterpret_cast<const uint4*>(lanebase + T * RG::kTileBytes);
+#pragma unroll
+                        for (int u = 0; u < MPL; ++u) {
+                            const uint4 x = __ldg(tp + u);
+                            wn[4 * u] = x.x; wn[4 * u + 1] = x.y; wn[4 * u + 2] = x.z; wn[4 * u + 3] = x.w;
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float i0 = __shfl_up_sync(0xffffffffu, s0, 1, 8);
+                        const float i1 = __shfl_up_sync(0xffffffffu, s1, 1, 8);
+                        const float i2 = __shfl_up_sync(0xffffffffu, s2, 1, 8);
+                        const float i3 = __shfl_up_sync(0xffffffffu, s3, 1, 8);
+#pragma unroll
+                        for (int s = 0; s < MPL; ++s) {
+                            const int byte = i * MPL + s;
+                            const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
+                            const float4 f = lutj[c * M + 8 * s];
+                            if (s == 0) {
+                                s0 = fmaf(i0, keep, f.x);
+                                s1 = fmaf(i1, keep, f.y);
+                                s2 = fmaf(i2, keep, f.z);
+                                s3 = fmaf(i3, keep, f.w);
+                            } else {
+                                s0 = __fadd_rn(s0, f.x);
+                                s1 = __fadd_rn(s1, f.y);
+                                s2 = __fadd_rn(s2, f.z);
+                                s3 = __fadd_rn(s3, f.w);
+                            }
+                        }
+                        const int v = 16 * (T0 + tt) + i - 7;   // vector finished by lane 7 at this step
+                        if (j == 7 && v >= a && v < b) dist4[v - cs] = make_float4(s0, s1, s2, s3);
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
+                }
+            }
+            __syncthreads();
+            const uint32_t kbase = (uint32_t)(koff + cs);
+            uint64_t thr[kGQ];
+            int cnt4[kGQ];
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k) {
+                thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_q[k])) : 0ull;
+                cnt4[k] = 0;
+            }
+            for (int i = tid; i < len; i += kRT) {
+                const float4 f = dist4[i];
+                const float fk[kGQ] = {f.x, f.y, f.z, f.w};
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k)
+                    cnt4[k] += (k < nqg && make_key(__float_as_uint(fk[k]), kbase + (uint32_t)i) <= thr[k]) ? 1 : 0;
+            }
+            const int4 tot = block_sum4<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
+            const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
+            const float* dflat = reinterpret_cast<const float*>(dist4);
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k) {
+                if (k >= nqg || totk[k] == 0) continue;
+                auto keyf = [&](int i) -> uint64_t {
+                    return make_key(__float_as_uint(dflat[4 * i + k]), kbase + (uint32_t)i);
+                };
+                uint64_t cut = thr[k];
+                if (totk[k] > cb.R) {
+                    const uint64_t kap = block_kth_key<kRT>(keyf, len, cb.R, thr[k], esm.hist, esm.bc);
+                    cut = kap < thr[k] ? kap : thr[k];
+                    if (tid == 0) atomicMin(cb.thr + s_q[k], (unsigned long long)cut);
+                }
+                warp_append<kRT, kRChunk / kRT>(keyf, len, cut, cb, s_q[k]);
+            }
+            __syncthreads();
+        }
+    }
+}
+
+template <int M, int DSUB>
+cudaError_t launch_gring(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
+                         cudaStream_t st) {
+    const size_t smem = GRing<M>::smem_bytes();
+    cudaError_t e =
+        cudaFuncSetAttribute(pq_gring_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_gring_kernel<M, DSUB>, kRT, smem);
+    if (per_sm < 1) return cudaErrorInvalidConfiguration;
+    long long items = (long long)max_groups * (p.has_delta ? 2 : 1);
+    long long grid = (long long)sms * per_sm;
+    if (grid > items) grid = items;
+    if (grid < 1) grid = 1;
+    note_launch();
+    pq_gring_kernel<M, DSUB><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
+    return cudaGetLastError();
+}
+
+template <int MPL>
+__global__ void gring_layout_kernel(const uint8_t* __restrict__ codes, const int64_t* __restrict__ offsets,
+                                    const int32_t* __restrict__ counts, const int64_t* __restrict__ tile_off,
+                                    int nlist, int M, uint8_t* __restrict__ out) {
+    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
+        const int cnt = counts[l];
+        const int64_t off = offsets[l];
+        const int64_t total = gring_tiles(cnt) * 128 * MPL;
+        uint8_t* dst = out + tile_off[l];
+        for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
+            const int64_t T = e / (128 * MPL);
+            const int r = (int)(e % (128 * MPL));
+            const int jj = r / (16 * MPL), r2 = r % (16 * MPL), i = r2 / MPL, s = r2 % MPL;
+            const int64_t v = 16 * T + i - jj;
+            dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
+        }
+    }
+}
+
 template <int M, int DSUB>
 size_t group_smem_bytes() {
     return Grp<M>::lut_bytes() + sizeof(float) * kGQ * kGChunk;
@@ -530,7 +793,23 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
 
 bool pq_supported_m(int M) { return M > 0 && M <= 64 && M % 8 == 0; }
 
-int pq_scan_chunk(int M, int d) { return pq_group_usable(M, d) ? kGChunk : kPChunk; }
+int pq_scan_chunk(int M, int d) { return pq_group_usable(M, d) ? kRChunk : kPChunk; }
+
+int64_t pq_gring_list_bytes(int count, int M) { return gring_tiles(count) * 128 * (M / 8); }
+
+cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
+                           const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st) {
+    if (M != 16 && M != 32 && M != 48) return cudaErrorInvalidValue;
+    if (nlist <= 0) return cudaSuccess;
+    const int grid = nlist < 4096 ? nlist : 4096;
+    note_launch();
+    switch (M / 8) {
+        case 2: gring_layout_kernel<2><<<grid, 256, 0, st>>>(codes, offsets, counts, tile_off, nlist, M, out); break;
+        case 4: gring_layout_kernel<4><<<grid, 256, 0, st>>>(codes, offsets, counts, tile_off, nlist, M, out); break;
+        default: gring_layout_kernel<6><<<grid, 256, 0, st>>>(codes, offsets, counts, tile_off, nlist, M, out); break;
+    }
+    return cudaGetLastError();
+}
 
 bool pq_group_usable(int M, int d) {
     if (M <= 0 || d % M != 0) return false;
@@ -546,8 +825,9 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
     if (e) return e;
     if (pq_group_usable(p.M, p.d) && wl.groups && p.codebook_t) {
         const int ds = p.d / p.M;
+        if (!p.main.gring || (p.has_delta && !p.delta.gring)) return cudaErrorInvalidValue;
 #define ISB_GROUP(MM, DS) \
-    if (p.M == MM && ds == DS) return launch_group<MM, DS>(p, wl, max_pairs, cm, cd, counter, st);
+    if (p.M == MM && ds == DS) return launch_gring<MM, DS>(p, wl, max_pairs, cm, cd, counter, st);
         ISB_GROUP(16, 2) ISB_GROUP(16, 4) ISB_GROUP(16, 8)
         ISB_GROUP(32, 2) ISB_GROUP(32, 4) ISB_GROUP(32, 8)
         ISB_GROUP(48, 2) ISB_GROUP(48, 4)

@@ -14,6 +14,11 @@ namespace isb {
 
 namespace {
 
+// pair index i (over nq x ncol) -> probe table entry: query i / ncol, column col0 + i % ncol
+__device__ __forceinline__ size_t probe_at(size_t i, int nprobe, int col0, int ncol) {
+    return (i / (size_t)ncol) * (size_t)nprobe + (size_t)col0 + i % (size_t)ncol;
+}
+
 __device__ __forceinline__ int local_list(const int32_t* probes, size_t i, int nlist_global,
                                           const int32_t* list_map) {
     int g = probes[i];
@@ -21,25 +26,25 @@ __device__ __forceinline__ int local_list(const int32_t* probes, size_t i, int n
     return list_map ? list_map[g] : g;
 }
 
-__global__ void count_pairs_kernel(const int32_t* probes, size_t total, int nlist_global,
-                                   const int32_t* list_map, int32_t* list_cnt) {
+__global__ void count_pairs_kernel(const int32_t* probes, size_t total, int nprobe, int col0, int ncol,
+                                   int nlist_global, const int32_t* list_map, int32_t* list_cnt) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
          i += (size_t)gridDim.x * blockDim.x) {
-        int l = local_list(probes, i, nlist_global, list_map);
+        int l = local_list(probes, probe_at(i, nprobe, col0, ncol), nlist_global, list_map);
         if (l >= 0) atomicAdd(&list_cnt[l], 1);
     }
 }
 
-__global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprobe, int nlist_global,
-                                  const int32_t* list_map, const int32_t* list_off, int32_t* cursor,
-                                  int32_t* pair_q, int32_t* pair_l) {
+__global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprobe, int col0, int ncol,
+                                  int nlist_global, const int32_t* list_map, const int32_t* list_off,
+                                  int32_t* cursor, int32_t* pair_q, int32_t* pair_l) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
          i += (size_t)gridDim.x * blockDim.x) {
-        int l = local_list(probes, i, nlist_global, list_map);
+        int l = local_list(probes, probe_at(i, nprobe, col0, ncol), nlist_global, list_map);
         if (l < 0) continue;
         int slot = atomicAdd(&cursor[l], 1);
         int p = list_off[l] + slot;
-        pair_q[p] = (int32_t)(i / (size_t)nprobe);
+        pair_q[p] = (int32_t)(i / (size_t)ncol);
         pair_l[p] = l;
     }
 }
@@ -78,23 +83,25 @@ size_t worklist_scan_bytes(int nlist) {
 
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
-                           void* scan_tmp, size_t scan_bytes, cudaStream_t st) {
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0, int ncol) {
     cudaError_t e;
+    if (ncol <= 0) ncol = nprobe - col0;
     if ((e = cudaMemsetAsync(wl.list_cnt, 0, sizeof(int32_t) * (nlist_local + 1), st))) return e;
     if ((e = cudaMemsetAsync(wl.cursor, 0, sizeof(int32_t) * nlist_local, st))) return e;
-    size_t total = (size_t)nq * nprobe;
+    size_t total = (size_t)nq * (ncol > 0 ? ncol : 0);
     if (total > 0) {
         note_launch();
-        count_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nlist_global, list_map,
-                                                                 wl.list_cnt);
+        count_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, col0, ncol, nlist_global,
+                                                                 list_map, wl.list_cnt);
         if ((e = cudaGetLastError())) return e;
     }
     if ((e = cub::DeviceScan::ExclusiveSum(scan_tmp, scan_bytes, wl.list_cnt, wl.list_off, nlist_local + 1, st)))
         return e;
     if (total > 0) {
         note_launch();
-        fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, nlist_global, list_map,
-                                                                wl.list_off, wl.cursor, wl.pair_q, wl.pair_l);
+        fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, col0, ncol, nlist_global,
+                                                                list_map, wl.list_off, wl.cursor, wl.pair_q,
+                                                                wl.pair_l);
         if ((e = cudaGetLastError())) return e;
     }
     if (wl.groups) {
