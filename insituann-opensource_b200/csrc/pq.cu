@@ -124,190 +124,7 @@ __global__ void __launch_bounds__(kPT) pq_scan_kernel(PQParams p, WorkList wl, C
 }
 
 
-// ---------------------------------------------------------------------------
-// Query-grouped ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8).
-//
-// One CTA takes one inverted list and up to kGQ = 4 of the queries that probe
-// it (consecutive list-major pairs).  The four LUTs are interleaved as
-// float4 lut[c * P + m] = (LUT_q0[m][c], .., LUT_q3[m][c]), so one 16-byte
-// shared load serves four lookups and every code byte loaded from HBM is used
-// by four queries.  The row pitch P = M + 1 makes the 16-byte bank group of
-// an entry depend on c + m instead of on m alone (with P = M, a multiple of 8,
-// all 32 lanes of a warp would hit the same bank group).  Each thread scans
-// whole vectors and accumulates every query's distance in m order, so the
-// sums are the same as in the row kernel and the CPU restatement.
-// ---------------------------------------------------------------------------
 constexpr int kGQ = 4;      // queries per group
-constexpr int kGT = 512;    // threads per CTA
-constexpr int kGChunk = 1024;
-
-template <int M>
-struct Grp {
-    static constexpr int P = M + 1;  // LUT row pitch in float4
-    static constexpr size_t lut_bytes() { return sizeof(float4) * 256 * P; }
-};
-
-template <int M>
-__device__ __forceinline__ void grp_vector(const uint8_t* __restrict__ code, const float4* __restrict__ lut, float& s0,
-                                           float& s1, float& s2, float& s3) {
-    const uint4* c4 = reinterpret_cast<const uint4*>(code);
-    uint4 w[M / 16];
-#pragma unroll
-    for (int i = 0; i < M / 16; ++i) w[i] = __ldg(c4 + i);
-    s0 = s1 = s2 = s3 = 0.f;
-#pragma unroll
-    for (int i = 0; i < M / 16; ++i) {
-        const uint32_t ww[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-#pragma unroll
-        for (int b = 0; b < 16; ++b) {
-            const int m = i * 16 + b;
-            const uint32_t c = (ww[b >> 2] >> (8 * (b & 3))) & 0xFFu;
-            const float4 f = lut[c * Grp<M>::P + m];
-            s0 = __fadd_rn(s0, f.x);
-            s1 = __fadd_rn(s1, f.y);
-            s2 = __fadd_rn(s2, f.z);
-            s3 = __fadd_rn(s3, f.w);
-        }
-    }
-}
-
-template <int M, int DSUB>
-__global__ void __launch_bounds__(kGT, 1) pq_group_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
-                                                          int* counter) {
-    using G = Grp<M>;
-    constexpr int d = M * DSUB;
-    extern __shared__ __align__(16) float smf[];
-    float4* lut = reinterpret_cast<float4*>(smf);                    // [256][P]
-    float* dist = smf + 4 * 256 * G::P;                               // [kGQ][kGChunk]; residuals during the LUT build
-    __shared__ EmitSmem esm;
-    __shared__ int s_item, s_q[kGQ];
-    const int tid = threadIdx.x;
-    const int NG = *wl.n_groups;
-    const int total = p.has_delta ? 2 * NG : NG;
-    for (;;) {
-        const int it = next_item(counter, total, &s_item);
-        if (it < 0) break;
-        const bool seg_delta = it >= NG;
-        const int gi = seg_delta ? it - NG : it;
-        const int packed = wl.groups[gi];
-        const int p0 = packed >> 3, nqg = packed & 7;
-        const int l = wl.pair_l[p0];
-        const ListStore& SG = seg_delta ? p.delta : p.main;
-        const CandBuf& cb = seg_delta ? cd : cm;
-        const int count = SG.counts[l];
-        if (count <= 0) continue;
-        const int64_t off = SG.offsets[l];
-        const int64_t koff = SG.key_off ? SG.key_off[l] : off;
-        if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
-        __syncthreads();
-        {   // residuals of the group's queries, then the interleaved LUT
-            float* resid = dist;   // [kGQ][d]
-            const float* cv = p.cent + (size_t)l * d;
-            for (int e = tid; e < kGQ * d; e += kGT) {
-                const int k = e / d, x = e - k * d;
-                const int qk = s_q[k];
-                resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
-            }
-            __syncthreads();
-            // thread t owns sub-quantizer m = t % M for codes c = t / M, t / M + kGT / M, ...
-            constexpr int kCStep = kGT / M;
-            if (tid < kCStep * M) {
-                const int m = tid % M, c0 = tid / M;
-                float r[kGQ][DSUB];
-#pragma unroll
-                for (int k = 0; k < kGQ; ++k)
-#pragma unroll
-                    for (int u = 0; u < DSUB; ++u) r[k][u] = resid[k * d + m * DSUB + u];
-                for (int c = c0; c < 256; c += kCStep) {
-                    float cbv[DSUB];
-                    const float* src = p.codebook_t + ((size_t)c * M + m) * DSUB;
-                    if constexpr (DSUB % 4 == 0) {
-#pragma unroll
-                        for (int u = 0; u < DSUB; u += 4) {
-                            const float4 t4 = __ldg(reinterpret_cast<const float4*>(src + u));
-                            cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < DSUB; u += 2) {
-                            const float2 t2 = __ldg(reinterpret_cast<const float2*>(src + u));
-                            cbv[u] = t2.x; cbv[u + 1] = t2.y;
-                        }
-                    }
-                    float acc[kGQ];
-#pragma unroll
-                    for (int k = 0; k < kGQ; ++k) {
-                        const float x0 = __fsub_rn(r[k][0], cbv[0]);
-                        float a = __fmul_rn(x0, x0);   // == 0 + x0*x0 exactly
-#pragma unroll
-                        for (int u = 1; u < DSUB; ++u) {
-                            const float x = __fsub_rn(r[k][u], cbv[u]);
-                            a = __fadd_rn(a, __fmul_rn(x, x));
-                        }
-                        acc[k] = a;
-                    }
-                    lut[c * G::P + m] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-                }
-            }
-            __syncthreads();
-        }
-        for (int cs = 0; cs < count; cs += kGChunk) {
-            const int len = min(kGChunk, count - cs);
-            const uint8_t* codes = SG.data + (size_t)(off + cs) * M;
-            for (int v = tid; v < len; v += 2 * kGT) {
-                const int v2 = v + kGT;
-                float a0, a1, a2, a3, b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-                grp_vector<M>(codes + (size_t)v * M, lut, a0, a1, a2, a3);
-                if (v2 < len) grp_vector<M>(codes + (size_t)v2 * M, lut, b0, b1, b2, b3);
-                dist[v] = a0;
-                dist[kGChunk + v] = a1;
-                dist[2 * kGChunk + v] = a2;
-                dist[3 * kGChunk + v] = a3;
-                if (v2 < len) {
-                    dist[v2] = b0;
-                    dist[kGChunk + v2] = b1;
-                    dist[2 * kGChunk + v2] = b2;
-                    dist[3 * kGChunk + v2] = b3;
-                }
-            }
-            __syncthreads();
-            const uint32_t kbase = (uint32_t)(koff + cs);
-            // one block reduction gives the four queries' survivor counts
-            uint64_t thr[kGQ];
-            int cnt4[kGQ];
-#pragma unroll
-            for (int k = 0; k < kGQ; ++k) {
-                thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_q[k])) : 0ull;
-                cnt4[k] = 0;
-            }
-#pragma unroll
-            for (int jj = 0; jj < kGChunk / kGT; ++jj) {
-                const int i = tid + jj * kGT;
-                if (i < len) {
-#pragma unroll
-                    for (int k = 0; k < kGQ; ++k)
-                        cnt4[k] += (k < nqg && make_key(__float_as_uint(dist[k * kGChunk + i]), kbase + (uint32_t)i) <= thr[k]) ? 1 : 0;
-                }
-            }
-            const int4 tot = block_sum4<kGT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
-            const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
-#pragma unroll
-            for (int k = 0; k < kGQ; ++k) {
-                if (k >= nqg || totk[k] == 0) continue;
-                const float* dk = dist + k * kGChunk;
-                auto keyf = [&](int i) -> uint64_t { return make_key(__float_as_uint(dk[i]), kbase + (uint32_t)i); };
-                uint64_t cut = thr[k];
-                if (totk[k] > cb.R) {   // more survivors than the rank budget: keep only the R best
-                    const uint64_t kap = block_kth_key<kGT>(keyf, len, cb.R, thr[k], esm.hist, esm.bc);
-                    cut = kap < thr[k] ? kap : thr[k];
-                    if (tid == 0) atomicMin(cb.thr + s_q[k], (unsigned long long)cut);
-                }
-                warp_append<kGT, kGChunk / kGT>(keyf, len, cut, cb, s_q[k]);
-            }
-            __syncthreads();
-        }
-    }
-}
 
 // ---------------------------------------------------------------------------
 // Grouped ring ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8): the kernel the
@@ -570,32 +387,6 @@ __global__ void gring_layout_kernel(const uint8_t* __restrict__ codes, const int
             dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
         }
     }
-}
-
-template <int M, int DSUB>
-size_t group_smem_bytes() {
-    return Grp<M>::lut_bytes() + sizeof(float) * kGQ * kGChunk;
-}
-
-template <int M, int DSUB>
-cudaError_t launch_group(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
-                         cudaStream_t st) {
-    const size_t smem = group_smem_bytes<M, DSUB>();
-    cudaError_t e =
-        cudaFuncSetAttribute(pq_group_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e) return e;
-    int dev = 0, sms = 148, per_sm = 1;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_group_kernel<M, DSUB>, kGT, smem);
-    if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    long long items = (long long)max_groups * (p.has_delta ? 2 : 1);
-    long long grid = (long long)sms * per_sm;
-    if (grid > items) grid = items;
-    if (grid < 1) grid = 1;
-    note_launch();
-    pq_group_kernel<M, DSUB><<<(int)grid, kGT, smem, st>>>(p, wl, cm, cd, counter);
-    return cudaGetLastError();
 }
 
 template <int M>
