@@ -333,7 +333,7 @@ WorkList worklist_for(BatchCtx* b, IndexCtx* x, int nsub, int nprobe, void** tmp
     if (groups) {
         wl.grp_cnt = ensure<int32_t>(b, b->grp_cnt, (size_t)x->nlist + 1);
         wl.grp_off = ensure<int32_t>(b, b->grp_off, (size_t)x->nlist + 1);
-        wl.groups = ensure<int32_t>(b, b->groups, (size_t)nsub * nprobe);
+        wl.groups = ensure<int64_t>(b, b->groups, (size_t)nsub * nprobe);
         wl.n_groups = wl.grp_off + x->nlist;
     }
     wl.list_cnt = ensure<int32_t>(b, b->wl_cnt, (size_t)x->nlist + 1);
@@ -432,10 +432,18 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     const bool use_delta = overlay && x->has_delta && delta_topk > 0;
     const int Rd = use_delta ? delta_topk : 0;
     require(R <= 4096 && R + Rd <= 4096, "rerank_n + delta_topk must be <= 4096");
-    const int chunk = pq_scan_chunk(x->M, x->d);
-    const int cap_m = nprobe * ceil_div(std::max(x->main.max_count, 1), chunk) * std::min(R, chunk);
-    const int cap_d = use_delta ? nprobe * ceil_div(std::max(x->delta.max_count, 1), chunk) * std::min(Rd, chunk)
-                                : 0;
+    // every filtered chunk of a probed list appends at most min(R, chunk items) keys
+    const int items = pq_scan_chunk_items(x->M, x->d);
+    const int slack_m = pq_chunk_slack(x->M, x->d, R), slack_d = pq_chunk_slack(x->M, x->d, Rd);
+    const int64_t cap_m64 = (int64_t)nprobe * std::max(1, pq_scan_chunks(x->M, x->d, x->main.max_count)) *
+                            std::min(R + slack_m, items);
+    const int64_t cap_d64 = use_delta ? (int64_t)nprobe *
+                                            std::max(1, pq_scan_chunks(x->M, x->d, x->delta.max_count)) *
+                                            std::min(Rd + slack_d, items)
+                                      : 0;
+    require(cap_m64 <= (1ll << 30) && cap_d64 <= (1ll << 30),
+            "candidate buffer of one query would exceed 2^30 keys (lists too long for this nprobe)", IVF_EOVERFLOW);
+    const int cap_m = (int)cap_m64, cap_d = (int)cap_d64;
     size_t per_q = ((size_t)cap_m + cap_d + R + Rd) * 8 + 32;
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
     void* tmp;
@@ -448,6 +456,7 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     cm.overflow = b->overflow;
     cm.cap = cap_m;
     cm.R = R;
+    cm.slack = slack_m;
     uint64_t* s1m = ensure<uint64_t>(b, b->s1m, (size_t)nsub * R);
     uint64_t* s1d = nullptr;
     if (use_delta) {
@@ -457,6 +466,7 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
         cd.overflow = b->overflow;
         cd.cap = cap_d;
         cd.R = Rd;
+        cd.slack = slack_d;
         s1d = ensure<uint64_t>(b, b->s1d, (size_t)nsub * Rd);
     }
     ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");

@@ -18,8 +18,9 @@ namespace isb {
 struct EmitSmem {
     int hist[256];
     int scratch[4 * 33];
-    int bc[4];
+    int bc[16];
     int base;
+    unsigned long long mm[64];
 };
 
 template <int T, class KeyFn>
@@ -110,6 +111,168 @@ __device__ __forceinline__ void warp_append(KeyFn keyf, int n, uint64_t cut, con
             const int at = base + __popc(ball & ((1u << lane) - 1u));
             if (at < cb.cap) out[at] = k;
             else atomicExch(cb.overflow, 1);
+        }
+    }
+}
+
+// warp_append over ITEMS keys per thread held in registers: keyj(j) is the
+// thread's j-th key (kKeyNone for none); j is a compile-time index after
+// unrolling, so register arrays behind keyj stay in registers.
+template <int ITEMS, class KeyJ>
+__device__ __forceinline__ void warp_append_items(KeyJ keyj, uint64_t cut, const CandBuf& cb, int q) {
+    const int lane = threadIdx.x & 31;
+    uint64_t* out = cb.keys + (size_t)q * cb.cap;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint64_t k = keyj(j);
+        const bool take = k <= cut;
+        const unsigned ball = __ballot_sync(0xffffffffu, take);
+        if (ball == 0) continue;
+        int base = 0;
+        if (lane == 0) base = atomicAdd(cb.cnt + q, __popc(ball));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) {
+            const int at = base + __popc(ball & ((1u << lane) - 1u));
+            if (at < cb.cap) out[at] = k;
+            else atomicExch(cb.overflow, 1);
+        }
+    }
+}
+
+// Cut keys for up to Q = 4 queries at once, over ITEMS keys per thread in
+// registers (key(e, q); all threads call it together).  For every query q in
+// `active` (bit q), among its participants (keys <= upper[q], at least R of
+// them) it finds cut[q] such that at least R participants are <= cut[q] and
+// at most R + slack are: a valid new rank-R bound whose keys the caller can
+// append without exceeding R + slack per call.
+//
+// A radix descent as in block_kth_each, but all queries share each pass's
+// barriers, the first digit is the 8 bits just below the highest bit in which
+// the query's participants differ (block min and max), and a query stops as
+// soon as the bin holding its R-th key is small enough (so the cut is the end
+// of that bin, not necessarily the R-th key itself).  hist: Q * 256 ints of
+// shared memory the caller may reuse afterwards only after a barrier;
+// bc: 4 * Q ints; mm: 2 * Q * (T / 32) uint64.
+template <int T, int ITEMS, int Q, class KeyF>
+__device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, const uint64_t (&upper)[Q],
+                                int* hist, int* bc, unsigned long long* mm, uint64_t (&cut)[Q]) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int W = T / 32;
+    uint64_t lo[Q], hi[Q];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+        lo[q] = kKeyNone;
+        hi[q] = 0;
+        if (!((active >> q) & 1u)) continue;
+#pragma unroll
+        for (int e = 0; e < ITEMS; ++e) {
+            const uint64_t k = key(e, q);
+            if (k <= upper[q]) {
+                lo[q] = k < lo[q] ? k : lo[q];
+                hi[q] = k > hi[q] ? k : hi[q];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t l2 = __shfl_xor_sync(0xffffffffu, lo[q], o);
+            const uint64_t h2 = __shfl_xor_sync(0xffffffffu, hi[q], o);
+            lo[q] = l2 < lo[q] ? l2 : lo[q];
+            hi[q] = h2 > hi[q] ? h2 : hi[q];
+        }
+        if (lane == 0) {
+            mm[(2 * q) * W + warp] = lo[q];
+            mm[(2 * q + 1) * W + warp] = hi[q];
+        }
+    }
+    __syncthreads();
+    int shift[Q], need[Q];
+    uint64_t prefix[Q], mask[Q];
+    unsigned todo = 0;
+#pragma unroll
+    for (int q = 0; q < Q; ++q) {
+        shift[q] = 0;
+        need[q] = R;
+        prefix[q] = 0;
+        mask[q] = 0;
+        if (!((active >> q) & 1u)) continue;
+#pragma unroll
+        for (int w = 0; w < W; ++w) {
+            const uint64_t l2 = mm[(2 * q) * W + w], h2 = mm[(2 * q + 1) * W + w];
+            lo[q] = l2 < lo[q] ? l2 : lo[q];
+            hi[q] = h2 > hi[q] ? h2 : hi[q];
+        }
+        if (lo[q] == hi[q]) {          // every participant holds the same key
+            cut[q] = lo[q];
+            continue;
+        }
+        const int top = 63 - __clzll((long long)(lo[q] ^ hi[q]));
+        shift[q] = top >= 7 ? top - 7 : 0;
+        mask[q] = top >= 63 ? 0ull : ~((2ull << top) - 1ull);
+        prefix[q] = lo[q] & mask[q];
+        todo |= 1u << q;
+    }
+    while (todo) {
+        for (int b = tid; b < Q * 256; b += T) hist[b] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < ITEMS; ++e) {
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+                if (!((todo >> q) & 1u)) continue;       // uniform over the block
+                const uint64_t k = key(e, q);
+                const bool part = k <= upper[q] && (k & mask[q]) == prefix[q];
+                const int bin = part ? q * 256 + (int)((k >> shift[q]) & 255u) : Q * 256 + lane;
+                const unsigned peers = __match_any_sync(0xffffffffu, bin);
+                if (part && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], __popc(peers));
+            }
+        }
+        __syncthreads();
+        if (warp < Q && ((todo >> warp) & 1u)) {      // warp q finds the bin of query q's need-th key
+            const int q = warp;
+            int needq = 0;
+#pragma unroll
+            for (int qq = 0; qq < Q; ++qq) needq = qq == q ? need[qq] : needq;   // no dynamic register index
+            int loc[8];
+            int sum = 0;
+#pragma unroll
+            for (int jj = 0; jj < 8; ++jj) {
+                loc[jj] = hist[q * 256 + lane * 8 + jj];
+                sum += loc[jj];
+            }
+            const int incl = warp_incl_scan(sum);
+            const unsigned ball = __ballot_sync(0xffffffffu, incl >= needq);
+            const int src = __ffs(ball) - 1;
+            if (lane == src) {
+                int acc = incl - sum;
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj) {
+                    if (acc + loc[jj] >= needq) {
+                        bc[4 * q] = lane * 8 + jj;
+                        bc[4 * q + 1] = acc;
+                        bc[4 * q + 2] = loc[jj];
+                        break;
+                    }
+                    acc += loc[jj];
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int q = 0; q < Q; ++q) {
+            if (!((todo >> q) & 1u)) continue;
+            const int b = bc[4 * q], below = bc[4 * q + 1], cnt = bc[4 * q + 2];
+            need[q] -= below;
+            prefix[q] |= (uint64_t)b << shift[q];
+            mask[q] |= (uint64_t)0xFFu << shift[q];
+            if (cnt - need[q] <= slack) {          // keys <= end of this bin: R - need + cnt <= R + slack
+                cut[q] = prefix[q] | ~mask[q];
+                todo &= ~(1u << q);
+            } else if (shift[q] == 0) {            // several participants share the final key
+                cut[q] = prefix[q];
+                todo &= ~(1u << q);
+            } else {
+                shift[q] = shift[q] >= 8 ? shift[q] - 8 : 0;
+            }
         }
     }
 }

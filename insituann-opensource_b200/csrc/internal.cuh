@@ -72,25 +72,121 @@ __device__ __forceinline__ int block_sum(int v, int* scratch) {
 }
 
 // ---------------------------------------------------------------------------
-// Radix selection of the need-th smallest 64-bit key (1-based) among the keys
-// k(i), i < n, with k(i) <= upper.  The caller guarantees at least `need`
-// participants.  Returns kappa such that exactly `need` participants satisfy
-// key <= min(kappa, upper) when keys are distinct; when several participants
-// share the final key, returns that key (the caller takes copies as needed).
-// 8 bits per pass from the most significant byte, early exit as soon as the
-// bucket that holds the need-th key is needed in full.
+// Radix selection of the need-th smallest 64-bit key (1-based) among the
+// participants: the keys <= upper that each(fn) hands to fn(key) (every
+// thread passes its own share of the keys).  The caller guarantees at least
+// `need` participants.  Returns kappa such that exactly `need` participants
+// satisfy key <= min(kappa, upper) when keys are distinct; when several
+// participants share the final key, returns that key (the caller takes
+// copies as needed).  8 bits per pass from the most significant byte, early
+// exit as soon as the bucket that holds the need-th key is needed in full.
 // hist: 256 ints of shared memory; bc: 4 ints of shared memory.
 // ---------------------------------------------------------------------------
-template <int T, class KeyFn>
-__device__ uint64_t block_kth_key(KeyFn keyf, int n, int need, uint64_t upper, int* hist, int* bc) {
+template <int T, class EachFn>
+__device__ uint64_t block_kth_each(EachFn each, int need, uint64_t upper, int* hist, int* bc) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     uint64_t prefix = 0, mask = 0;
     for (int shift = 56; shift >= 0; shift -= 8) {
         for (int b = tid; b < 256; b += T) hist[b] = 0;
         __syncthreads();
-        for (int i = tid; i < n; i += T) {
-            uint64_t k = keyf(i);
+        each([&](uint64_t k) {
             if (k <= upper && (k & mask) == prefix) atomicAdd(&hist[(int)((k >> shift) & 255u)], 1);
+        });
+        __syncthreads();
+        if (warp == 0) {
+            int loc[8];
+            int s = 0;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                loc[j] = hist[lane * 8 + j];
+                s += loc[j];
+            }
+            int incl = warp_incl_scan(s);
+            int excl = incl - s;
+            unsigned ball = __ballot_sync(0xffffffffu, incl >= need);
+            int src = __ffs(ball) - 1;
+            if (lane == src) {
+                int acc = excl;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (acc + loc[j] >= need) {
+                        bc[0] = lane * 8 + j;
+                        bc[1] = acc;
+                        bc[2] = loc[j];
+                        break;
+                    }
+                    acc += loc[j];
+                }
+            }
+        }
+        __syncthreads();
+        const int b = bc[0], below = bc[1], cnt = bc[2];
+        __syncthreads();
+        need -= below;
+        prefix |= (uint64_t)b << shift;
+        mask |= (uint64_t)0xFFu << shift;
+        if (cnt == need) return prefix | ~mask;
+    }
+    return prefix;
+}
+
+// The selection of block_kth_each over ITEMS keys per thread held in
+// registers (keyj(j) for j < ITEMS, kKeyNone for none; all threads call it
+// together).  Two things make it cheap on the clustered keys of one chunk:
+//   * the first pass starts at the highest byte in which the participants
+//     differ (block-wide min and max), skipping the bytes they all share;
+//   * histogram increments are combined per warp (__match_any_sync), so a bin
+//     that many keys fall into costs one shared atomic per warp and item.
+// mm: 2 * 32 uint64 of shared memory.
+template <int T, int ITEMS, class KeyJ>
+__device__ uint64_t block_kth_items(KeyJ keyj, int need, uint64_t upper, int* hist, int* bc,
+                                    unsigned long long* mm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    constexpr int W = T / 32;
+    uint64_t lo = kKeyNone, hi = 0;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        const uint64_t k = keyj(j);
+        if (k <= upper) {
+            lo = k < lo ? k : lo;
+            hi = k > hi ? k : hi;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const uint64_t l2 = __shfl_xor_sync(0xffffffffu, lo, o), h2 = __shfl_xor_sync(0xffffffffu, hi, o);
+        lo = l2 < lo ? l2 : lo;
+        hi = h2 > hi ? h2 : hi;
+    }
+    if (lane == 0) {
+        mm[warp] = lo;
+        mm[32 + warp] = hi;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < W; ++w) {
+        const uint64_t l2 = mm[w], h2 = mm[32 + w];
+        lo = l2 < lo ? l2 : lo;
+        hi = h2 > hi ? h2 : hi;
+    }
+    if (lo == hi) {               // every participant holds the same key
+        __syncthreads();          // mm is read by all before a later call rewrites it
+        return lo;
+    }
+    const int top = 63 - __clzll((long long)(lo ^ hi));
+    int shift = (top / 8) * 8;
+    uint64_t mask = shift + 8 >= 64 ? 0ull : ~((1ull << (shift + 8)) - 1ull);
+    uint64_t prefix = lo & mask;
+    for (; shift >= 0; shift -= 8) {
+        for (int b = tid; b < 256; b += T) hist[b] = 0;
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < ITEMS; ++j) {
+            const uint64_t k = keyj(j);
+            const bool part = k <= upper && (k & mask) == prefix;
+            const int bin = part ? (int)((k >> shift) & 255u) : 256 + lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (part && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], __popc(peers));
         }
         __syncthreads();
         if (warp == 0) {
@@ -128,6 +224,16 @@ __device__ uint64_t block_kth_key(KeyFn keyf, int n, int need, uint64_t upper, i
         if (cnt == need) return prefix | ~mask;
     }
     return prefix;
+}
+
+// the same over the keys k(i), i < n, strided over the block
+template <int T, class KeyFn>
+__device__ uint64_t block_kth_key(KeyFn keyf, int n, int need, uint64_t upper, int* hist, int* bc) {
+    return block_kth_each<T>(
+        [&](auto fn) {
+            for (int i = threadIdx.x; i < n; i += T) fn(keyf(i));
+        },
+        need, upper, hist, bc);
 }
 
 // ---------------------------------------------------------------------------
@@ -180,7 +286,7 @@ struct WorkList {              // probe inversion for one batch: list-major (que
     int32_t* n_pairs;          // -> list_off[nlist]
     int32_t* grp_cnt;          // [nlist+1] query groups per list (optional)
     int32_t* grp_off;          // [nlist+1] exclusive prefix of grp_cnt
-    int32_t* groups;           // [max_pairs] (first pair << 3) | group size, list-major
+    int64_t* groups;           // [max_pairs] (list << 32) | (first pair << 3) | group size, list-major
     int32_t* n_groups;         // -> grp_off[nlist]
 };
 
@@ -191,6 +297,7 @@ struct CandBuf {               // per-query candidate buffers of one segment
     int32_t* overflow;         // set when a query's buffer would overflow
     int cap;
     int R;                     // rank budget (rerank_n or delta top-k)
+    int slack;                 // a filtered chunk may append up to R + slack keys (0: exactly R)
 };
 
 }  // namespace isb

@@ -21,7 +21,7 @@ size_t worklist_scan_bytes(int nlist);
 // Builds list-major (query, list) pairs from probes [nq, nprobe] (global list
 // ids; list_map maps them to local lists or -1, nullptr = identity).
 // When wl.groups is set, also packs the pairs of every list into groups of up
-// to kGroupQueries consecutive pairs: groups[g] = (first pair << 3) | size.
+// to kGroupQueries consecutive pairs: groups[g] = (list << 32) | (first pair << 3) | size.
 // Only probe-table columns col0 .. col0+ncol-1 are used (ncol <= 0: to the end).
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
@@ -79,7 +79,14 @@ cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const i
                            const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st);
 // vectors per filtered chunk of the kernel that scans (M, d); each chunk keeps at
 // most R candidates per query, which bounds the candidate buffers
-int pq_scan_chunk(int M, int d);
+// filtered chunks the scan of one list of `count` vectors takes, and the most
+// vectors one chunk holds: a query's candidates from one probed list number at
+// most chunks * min(R + slack, chunk items)
+int pq_scan_chunks(int M, int d, int count);
+int pq_scan_chunk_items(int M, int d);
+// keys beyond R one filtered chunk of the PQ scan may append (its cut is a
+// bound that admits between R and R + slack keys)
+int pq_chunk_slack(int M, int d, int R);
 cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, CandBuf cd, int* work_counter,
                     cudaStream_t st);
 // Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).

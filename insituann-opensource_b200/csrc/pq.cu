@@ -130,8 +130,8 @@ constexpr int kGQ = 4;      // queries per group
 // Grouped ring ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8): the kernel the
 // search uses for these shapes.
 //
-// As in pq_group_kernel, a CTA takes one list and up to 4 probing queries and
-// the four LUTs are interleaved as float4.  Instead of one thread summing a
+// A CTA takes one list and up to 4 probing queries (a group of the work list)
+// and the four queries' LUTs are interleaved as float4.  Instead of one thread summing a
 // whole vector, a warp runs four systolic rings of 8 lanes: lane j of a ring
 // owns the MPL = M/8 consecutive sub-quantizers m = MPL*j .. MPL*j+MPL-1.  At
 // step x it receives the four partial sums of vector x-j from lane j-1
@@ -145,33 +145,113 @@ constexpr int kGQ = 4;      // queries per group
 // conflict-free whatever the code values.
 //
 // Codes are re-laid out once per index (pq_build_gring) into tiles of 16
-// steps: tile T of a list holds, for lane j, step i and sub-quantizer s, the
-// byte code[16T+i-j][MPL*j+s] (0 outside the list), so a lane reads its
-// 16*MPL bytes of a tile with MPL coalesced 16-byte loads and indexes them
-// statically.
+// steps.  Lane j's stream of a tile is the 16*MPL bytes b = i*MPL + s (step i,
+// sub-quantizer s) holding code[16T+i-j][MPL*j+s] (0 outside the list); its
+// 16-byte piece u = b/16 sits at tile offset (8u + j)*16, so each of a ring's
+// MPL 16-byte loads reads one whole 128-byte line, and the lane indexes the
+// bytes statically.
+//
+// The sums of queries (0,1) and (2,3) are float2 pairs added with the packed
+// fp32x2 instructions (__fadd2_rn: two independent round-to-nearest adds).
 // ---------------------------------------------------------------------------
 constexpr int kRW = 8;                 // warps per CTA
 constexpr int kRT = 32 * kRW;          // threads per CTA
 constexpr int kRChunk = 2048;          // vectors per filtered chunk
 constexpr int kRRings = 4 * kRW;       // 8-lane rings per CTA
+constexpr int kRSteps = kRChunk / kRRings;   // ring steps per filtered chunk (a multiple of 16)
+static_assert(kRSteps % 16 == 0, "a chunk is whole tiles");
 
 __host__ __device__ inline int64_t gring_tiles(int count) { return (int64_t)(count + 7) / 16 + 3; }
+// vectors per ring stripe: count / kRRings rounded up to whole tiles
+__host__ __device__ inline int gring_stripe(int count) {
+    return (int)(((int64_t)count + 16 * kRRings - 1) / (16 * kRRings)) * 16;
+}
+// filtered chunks of one list: ring 0 runs min(S, count) + 7 steps
+__host__ __device__ inline int gring_chunks(int count) {
+    if (count <= 0) return 0;
+    const int S = gring_stripe(count);
+    return ((S < count ? S : count) + 7 + kRSteps - 1) / kRSteps;
+}
 
 template <int M>
 struct GRing {
     static constexpr int MPL = M / 8;
-    static constexpr int kTileBytes = 128 * MPL;
     __host__ __device__ static constexpr int pos(int m) { return m / MPL + 8 * (m % MPL); }
     __host__ __device__ static constexpr int inv(int p) { return MPL * (p % 8) + p / 8; }
     static constexpr size_t smem_bytes() { return sizeof(float4) * ((size_t)256 * M + kRChunk); }
 };
 
+// NST steps (NST = 16: a whole tile; otherwise the first nst < 16) of one
+// lane of a ring.  Lane 0 starts a vector's four sums with its first entry
+// (keep2 = 0 there: its shuffle returns its own stale sums, times 0), every
+// other lane continues the sums received from lane j-1; lane 7 stores the
+// finished sums of step i to out[i * kRRings].
+template <int M, int NST>
+__device__ __forceinline__ void gring_tile(const float4* __restrict__ lutj, const uint32_t (&w)[M / 2], int nst,
+                                           float2 keep2, int j, float2& s01, float2& s23, float4* out) {
+    constexpr int MPL = M / 8;
+#pragma unroll
+    for (int i = 0; i < NST; ++i) {
+        if (NST < 16 && i >= nst) break;
+        const float2 i01 = make_float2(__shfl_up_sync(0xffffffffu, s01.x, 1, 8),
+                                       __shfl_up_sync(0xffffffffu, s01.y, 1, 8));
+        const float2 i23 = make_float2(__shfl_up_sync(0xffffffffu, s23.x, 1, 8),
+                                       __shfl_up_sync(0xffffffffu, s23.y, 1, 8));
+#pragma unroll
+        for (int s = 0; s < MPL; ++s) {
+            const int byte = i * MPL + s;
+            const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
+            const float4 f = lutj[c * M + 8 * s];
+            if (s == 0) {
+                s01 = __ffma2_rn(i01, keep2, make_float2(f.x, f.y));
+                s23 = __ffma2_rn(i23, keep2, make_float2(f.z, f.w));
+            } else {
+                s01 = __fadd2_rn(s01, make_float2(f.x, f.y));
+                s23 = __fadd2_rn(s23, make_float2(f.z, f.w));
+            }
+        }
+        if (j == 7) out[i * kRRings] = make_float4(s01.x, s01.y, s23.x, s23.y);
+    }
+}
+
+// 16-byte read-only load issued where it stands: the tile prefetch must leave
+// a whole tile of steps between its issue and its use, so it is not left to
+// the compiler to move it next to the use.
+__device__ __forceinline__ uint4 ldg_v4_here(const uint4* ptr) {
+    uint4 r;
+    asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(ptr)
+                 : "memory");
+    return r;
+}
+
+template <int MPL>
+__device__ __forceinline__ void load_tile(const uint4* lanebase, int64_t T, uint32_t (&w)[4 * MPL]) {
+    const uint4* tp = lanebase + T * (8 * MPL);   // a tile is 128*MPL bytes = 8*MPL uint4
+#pragma unroll
+    for (int u = 0; u < MPL; ++u) {
+        const uint4 x = ldg_v4_here(tp + 8 * u);
+        w[4 * u] = x.x; w[4 * u + 1] = x.y; w[4 * u + 2] = x.z; w[4 * u + 3] = x.w;
+    }
+}
+
+// Persistent CTA loop over the work list's groups.  Latency that does not
+// depend on the group is taken off the group's critical path:
+//   * the next work item is claimed (atomic) while this group runs;
+//   * the codebook rows a thread needs for its LUT column are requested
+//     before the group is even decoded (they are the same for every group);
+//   * the first code tile is requested before the LUT is built, each next
+//     tile one tile ahead, and each chunk's query bounds before its steps.
 template <int M, int DSUB>
 __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
                                                           int* counter) {
     using RG = GRing<M>;
     constexpr int MPL = RG::MPL;
     constexpr int d = M * DSUB;
+    constexpr int kCStep = kRT / M;                              // codes a LUT builder thread strides by
+    constexpr int kNC = (256 + kCStep - 1) / kCStep;             // codes per LUT builder thread, at most
+    constexpr int kLB = kNC < 64 / DSUB ? kNC : 64 / DSUB;       // codebook rows in flight per thread
     extern __shared__ __align__(16) float smf[];
     float4* lut = reinterpret_cast<float4*>(smf);          // [256][M], entry m at pos(m)
     float4* dist4 = lut + 256 * M;                          // [kRChunk] four queries per vector
@@ -179,173 +259,200 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
     __shared__ EmitSmem esm;
     __shared__ int s_item, s_q[kGQ];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ring = lane >> 3, j = lane & 7;
-    const float keep = j == 0 ? 0.f : 1.f;
+    const float2 keep2 = j == 0 ? make_float2(0.f, 0.f) : make_float2(1.f, 1.f);
+    // LUT builders: thread t owns LUT column ps = t % M (sub-quantizer inv(ps)) for codes t / M + kCStep * i
+    const bool builder = tid < kCStep * M;
+    const int ps = tid % M, mcol = RG::inv(ps), c0 = tid / M;
     const int NG = *wl.n_groups;
     const int total = p.has_delta ? 2 * NG : NG;
+    const int rid = warp * 4 + ring;
+    if (tid == 0) s_item = atomicAdd(counter, 1);
+    __syncthreads();
+    float cbv[kLB][DSUB];
+    auto load_cb = [&](int cbase) {
+#pragma unroll
+        for (int b = 0; b < kLB; ++b) {
+            const int c = min(cbase + b * kCStep, 255);
+            const float* src = p.codebook_t + ((size_t)c * M + mcol) * DSUB;
+            if constexpr (DSUB % 4 == 0) {
+#pragma unroll
+                for (int u = 0; u < DSUB; u += 4) {
+                    const float4 t4 = __ldg(reinterpret_cast<const float4*>(src + u));
+                    cbv[b][u] = t4.x; cbv[b][u + 1] = t4.y; cbv[b][u + 2] = t4.z; cbv[b][u + 3] = t4.w;
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < DSUB; u += 2) {
+                    const float2 t2 = __ldg(reinterpret_cast<const float2*>(src + u));
+                    cbv[b][u] = t2.x; cbv[b][u + 1] = t2.y;
+                }
+            }
+        }
+    };
     for (;;) {
-        const int it = next_item(counter, total, &s_item);
-        if (it < 0) break;
+        const int it = s_item;
+        if (it >= total) break;
+        int nxt = 0;
+        if (tid == 0) nxt = atomicAdd(counter, 1);       // used at the end of this group
+        if (builder) load_cb(c0);
         const bool seg_delta = it >= NG;
         const int gi = seg_delta ? it - NG : it;
-        const int packed = wl.groups[gi];
-        const int p0 = packed >> 3, nqg = packed & 7;
-        const int l = wl.pair_l[p0];
+        const int64_t packed = wl.groups[gi];
+        const int l = (int)(packed >> 32), p0 = ((int)packed) >> 3, nqg = ((int)packed) & 7;
         const ListStore& SG = seg_delta ? p.delta : p.main;
         const CandBuf& cb = seg_delta ? cd : cm;
         const int count = SG.counts[l];
-        if (count <= 0) continue;
-        const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
-        const uint8_t* tiles = SG.gring + SG.gring_off[l];
-        const int64_t ntiles = gring_tiles(count);
-        if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
-        __syncthreads();
-        {
-            const float* cv = p.cent + (size_t)l * d;
-            for (int e = tid; e < kGQ * d; e += kRT) {
-                const int k = e / d, x = e - k * d;
-                const int qk = s_q[k];
-                resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
-            }
-            __syncthreads();
-            // thread t owns LUT column pos = t % M (sub-quantizer inv(pos)) for codes c = t / M + kRT / M * i
-            constexpr int kCStep = kRT / M > 0 ? kRT / M : 1;
-            if (tid < kCStep * M) {
-                const int ps = tid % M, m = RG::inv(ps), c0 = tid / M;
-                float r[kGQ][DSUB];
-#pragma unroll
-                for (int k = 0; k < kGQ; ++k)
-#pragma unroll
-                    for (int u = 0; u < DSUB; ++u) r[k][u] = resid[k * d + m * DSUB + u];
-                for (int c = c0; c < 256; c += kCStep) {
-                    float cbv[DSUB];
-                    const float* src = p.codebook_t + ((size_t)c * M + m) * DSUB;
-                    if constexpr (DSUB % 4 == 0) {
-#pragma unroll
-                        for (int u = 0; u < DSUB; u += 4) {
-                            const float4 t4 = __ldg(reinterpret_cast<const float4*>(src + u));
-                            cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
-                        }
-                    } else {
-#pragma unroll
-                        for (int u = 0; u < DSUB; u += 2) {
-                            const float2 t2 = __ldg(reinterpret_cast<const float2*>(src + u));
-                            cbv[u] = t2.x; cbv[u + 1] = t2.y;
-                        }
-                    }
-                    float acc[kGQ];
-#pragma unroll
-                    for (int k = 0; k < kGQ; ++k) {
-                        const float x0 = __fsub_rn(r[k][0], cbv[0]);
-                        float a = __fmul_rn(x0, x0);
-#pragma unroll
-                        for (int u = 1; u < DSUB; ++u) {
-                            const float x = __fsub_rn(r[k][u], cbv[u]);
-                            a = __fadd_rn(a, __fmul_rn(x, x));
-                        }
-                        acc[k] = a;
-                    }
-                    lut[c * M + ps] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        if (count > 0) {
+            const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
+            const uint8_t* tiles = SG.gring + SG.gring_off[l];
+            const int64_t ntiles = gring_tiles(count);
+            // Ring r owns the stripe [r*S, r*S + S) of the list (S a multiple
+            // of 16, so a stripe starts on a tile) and runs through it without
+            // draining: its lane 7 finishes vector r*S + x - 7 at step x.
+            // Steps are cut into chunks of kRSteps; after each chunk the CTA
+            // filters the kRRings * kRSteps finished slots.  The longest
+            // stripe (ring 0) takes min(S, count) + 7 steps.
+            const int S = gring_stripe(count);
+            const int a = rid * S < count ? rid * S : count;
+            const int wa = warp * 4 * S;
+            const int wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its ring 0)
+            const int nchunks = gring_chunks(count);
+            const uint4* lanebase = reinterpret_cast<const uint4*>(tiles) + j;
+            const int64_t T0 = a / 16;
+            uint32_t w[4 * MPL], wn[4 * MPL];
+            load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+            if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
+            {
+                const float* cv = p.cent + (size_t)l * d;
+                for (int e = tid; e < kGQ * d; e += kRT) {
+                    const int k = e / d, x = e - k * d;
+                    const int qk = k < nqg ? wl.pair_q[p0 + k] : -1;
+                    resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
                 }
             }
             __syncthreads();
-        }
-        // this lane's LUT columns: pos(MPL*j + s) = j + 8*s
-        const float4* lutj = lut + j;
-        for (int cs = 0; cs < count; cs += kRChunk) {
-            const int len = min(kRChunk, count - cs);
-            const int Lr = (((len + kRRings - 1) / kRRings) + 15) & ~15;   // vectors per ring, multiple of 16
-            const int a = cs + (warp * 4 + ring) * Lr;                      // list-relative range [a, b)
-            const int b = min(a + Lr, cs + len);
-            if (cs + warp * 4 * Lr < cs + len) {                            // ring 0 of this warp has work
-                float s0 = 0.f, s1 = 0.f, s2 = 0.f, s3 = 0.f;
-                const int T0 = a / 16;
-                const int ntr = Lr / 16 + 1;
-                const uint8_t* lanebase = tiles + j * 16 * MPL;
-                uint32_t w[4 * MPL], wn[4 * MPL];
-                {
-                    const int64_t T = min((int64_t)T0, ntiles - 1);
-                    const uint4* tp = reinterpret_cast<const uint4*>(lanebase + T * RG::kTileBytes);
+            if (builder) {
+                float2 r01[DSUB], r23[DSUB];
 #pragma unroll
-                    for (int u = 0; u < MPL; ++u) {
-                        const uint4 x = __ldg(tp + u);
-                        w[4 * u] = x.x; w[4 * u + 1] = x.y; w[4 * u + 2] = x.z; w[4 * u + 3] = x.w;
-                    }
+                for (int u = 0; u < DSUB; ++u) {
+                    r01[u] = make_float2(resid[mcol * DSUB + u], resid[d + mcol * DSUB + u]);
+                    r23[u] = make_float2(resid[2 * d + mcol * DSUB + u], resid[3 * d + mcol * DSUB + u]);
                 }
-                for (int tt = 0; tt < ntr; ++tt) {
-                    {
-                        const int64_t T = min((int64_t)(T0 + tt + 1), ntiles - 1);
-                        const uint4* tp = reinterpret_cast<const uint4*>(lanebase + T * RG::kTileBytes);
+                for (int cb0 = c0;; cb0 += kLB * kCStep) {
 #pragma unroll
-                        for (int u = 0; u < MPL; ++u) {
-                            const uint4 x = __ldg(tp + u);
-                            wn[4 * u] = x.x; wn[4 * u + 1] = x.y; wn[4 * u + 2] = x.z; wn[4 * u + 3] = x.w;
-                        }
-                    }
+                    for (int b = 0; b < kLB; ++b) {
+                        const int c = cb0 + b * kCStep;
+                        if (c >= 256) break;
+                        // queries (0,1) and (2,3) as packed pairs; x - y is x + (-y) exactly
+                        float2 a01, a23;
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float i0 = __shfl_up_sync(0xffffffffu, s0, 1, 8);
-                        const float i1 = __shfl_up_sync(0xffffffffu, s1, 1, 8);
-                        const float i2 = __shfl_up_sync(0xffffffffu, s2, 1, 8);
-                        const float i3 = __shfl_up_sync(0xffffffffu, s3, 1, 8);
-#pragma unroll
-                        for (int s = 0; s < MPL; ++s) {
-                            const int byte = i * MPL + s;
-                            const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
-                            const float4 f = lutj[c * M + 8 * s];
-                            if (s == 0) {
-                                s0 = fmaf(i0, keep, f.x);
-                                s1 = fmaf(i1, keep, f.y);
-                                s2 = fmaf(i2, keep, f.z);
-                                s3 = fmaf(i3, keep, f.w);
+                        for (int u = 0; u < DSUB; ++u) {
+                            const float2 nc = make_float2(-cbv[b][u], -cbv[b][u]);
+                            const float2 x01 = __fadd2_rn(r01[u], nc), x23 = __fadd2_rn(r23[u], nc);
+                            if (u == 0) {
+                                a01 = __fmul2_rn(x01, x01);
+                                a23 = __fmul2_rn(x23, x23);
                             } else {
-                                s0 = __fadd_rn(s0, f.x);
-                                s1 = __fadd_rn(s1, f.y);
-                                s2 = __fadd_rn(s2, f.z);
-                                s3 = __fadd_rn(s3, f.w);
+                                a01 = __fadd2_rn(a01, __fmul2_rn(x01, x01));
+                                a23 = __fadd2_rn(a23, __fmul2_rn(x23, x23));
                             }
                         }
-                        const int v = 16 * (T0 + tt) + i - 7;   // vector finished by lane 7 at this step
-                        if (j == 7 && v >= a && v < b) dist4[v - cs] = make_float4(s0, s1, s2, s3);
+                        lut[c * M + ps] = make_float4(a01.x, a01.y, a23.x, a23.y);
                     }
+                    if (cb0 + kLB * kCStep >= 256) break;
+                    load_cb(cb0 + kLB * kCStep);
+                }
+            }
+            __syncthreads();
+            int qid[kGQ];
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k) qid[k] = s_q[k];
+            // this lane's LUT columns: pos(MPL*j + s) = j + 8*s
+            const float4* lutj = lut + j;
+            float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
+            const uint32_t kbase = (uint32_t)koff;
+            for (int t = 0; t < nchunks; ++t) {
+                uint64_t thr[kGQ];    // read now, used after the steps: a bound only ever decreases
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k)
+                    thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
+#pragma unroll 1
+                for (int tl = 0; tl < kRSteps / 16; ++tl) {
+                    const int x0 = t * kRSteps + 16 * tl;
+                    if (x0 >= wsteps) break;
+                    load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
+                    // slot of (step s of the chunk, ring r) = s * kRRings + r: the
+                    // four rings of a warp store 64 contiguous bytes per step
+                    float4* out = dist4 + 16 * tl * kRRings + rid;
+                    if (wsteps - x0 >= 16)
+                        gring_tile<M, 16>(lutj, w, 16, keep2, j, s01, s23, out);
+                    else
+                        gring_tile<M, 15>(lutj, w, wsteps - x0, keep2, j, s01, s23, out);
 #pragma unroll
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
-            }
-            __syncthreads();
-            const uint32_t kbase = (uint32_t)(koff + cs);
-            uint64_t thr[kGQ];
-            int cnt4[kGQ];
+                __syncthreads();
+                // thread t reads the slots t + kRT*e: ring t % 32 (= lane), chunk
+                // steps warp + 8e, i.e. vectors lane*S + t*kRSteps + warp + 8e - 7.
+                // All of them are read into registers before block_sum4's
+                // barriers, so the next chunk may overwrite the slots as soon as
+                // those have passed.
+                constexpr int kE = kRRings * kRSteps / kRT;
+                float4 f[kE];
+                uint32_t vid[kE];     // list position, or 0xFFFFFFFF for no vector
 #pragma unroll
-            for (int k = 0; k < kGQ; ++k) {
-                thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_q[k])) : 0ull;
-                cnt4[k] = 0;
-            }
-            for (int i = tid; i < len; i += kRT) {
-                const float4 f = dist4[i];
-                const float fk[kGQ] = {f.x, f.y, f.z, f.w};
+                for (int e = 0; e < kE; ++e) {
+                    const int x = t * kRSteps + warp + 8 * e;
+                    const int v = lane * S + x - 7;
+                    vid[e] = (x >= 7 && x - 7 < S && v < count) ? (uint32_t)v : 0xFFFFFFFFu;
+                    f[e] = vid[e] != 0xFFFFFFFFu ? dist4[tid + kRT * e] : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+                int cnt4[kGQ];
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k) {
+                    thr[k] = thr[k] < kKeyNone - 1 ? thr[k] : kKeyNone - 1;    // never admits kKeyNone
+                    cnt4[k] = 0;
+                }
+                auto key_of = [&](int e, int k) -> uint64_t {
+                    const float dk = k == 0 ? f[e].x : k == 1 ? f[e].y : k == 2 ? f[e].z : f[e].w;
+                    return vid[e] != 0xFFFFFFFFu ? make_key(__float_as_uint(dk), kbase + vid[e]) : kKeyNone;
+                };
+#pragma unroll
+                for (int e = 0; e < kE; ++e)
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k) cnt4[k] += (k < nqg && key_of(e, k) <= thr[k]) ? 1 : 0;
+                const int4 tot = block_sum4<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
+                const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
+                // queries with more than R keys under their bound get a new
+                // bound that admits R .. R + slack of them (one shared descent
+                // whose histograms use the slots, already in registers)
+                unsigned sel = 0;
+                uint64_t cut[kGQ];
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k) {
+                    cut[k] = thr[k];
+                    if (k < nqg && totk[k] > cb.R) sel |= 1u << k;
+                }
+                if (sel) {
+                    uint64_t cs[kGQ];
+                    block_cut_items<kRT, kE, kGQ>(key_of, sel, cb.R, cb.slack, thr, reinterpret_cast<int*>(dist4),
+                                                  esm.bc, esm.mm, cs);
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k) {
+                        if (!((sel >> k) & 1u)) continue;
+                        cut[k] = cs[k] < thr[k] ? cs[k] : thr[k];
+                        if (tid == 0) atomicMin(cb.thr + qid[k], (unsigned long long)cut[k]);
+                    }
+                }
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
-                    cnt4[k] += (k < nqg && make_key(__float_as_uint(fk[k]), kbase + (uint32_t)i) <= thr[k]) ? 1 : 0;
+                    if (k < nqg && totk[k] > 0)
+                        warp_append_items<kE>([&](int e) { return key_of(e, k); }, cut[k], cb, qid[k]);
+                if (sel) __syncthreads();     // the histograms lived in the slots
             }
-            const int4 tot = block_sum4<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
-            const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
-            const float* dflat = reinterpret_cast<const float*>(dist4);
-#pragma unroll
-            for (int k = 0; k < kGQ; ++k) {
-                if (k >= nqg || totk[k] == 0) continue;
-                auto keyf = [&](int i) -> uint64_t {
-                    return make_key(__float_as_uint(dflat[4 * i + k]), kbase + (uint32_t)i);
-                };
-                uint64_t cut = thr[k];
-                if (totk[k] > cb.R) {
-                    const uint64_t kap = block_kth_key<kRT>(keyf, len, cb.R, thr[k], esm.hist, esm.bc);
-                    cut = kap < thr[k] ? kap : thr[k];
-                    if (tid == 0) atomicMin(cb.thr + s_q[k], (unsigned long long)cut);
-                }
-                warp_append<kRT, kRChunk / kRT>(keyf, len, cut, cb, s_q[k]);
-            }
-            __syncthreads();
         }
+        if (tid == 0) s_item = nxt;
+        __syncthreads();
     }
 }
 
@@ -382,7 +489,7 @@ __global__ void gring_layout_kernel(const uint8_t* __restrict__ codes, const int
         for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
             const int64_t T = e / (128 * MPL);
             const int r = (int)(e % (128 * MPL));
-            const int jj = r / (16 * MPL), r2 = r % (16 * MPL), i = r2 / MPL, s = r2 % MPL;
+            const int u = r / 128, jj = (r % 128) / 16, b = 16 * u + r % 16, i = b / MPL, s = b % MPL;
             const int64_t v = 16 * T + i - jj;
             dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
         }
@@ -584,7 +691,14 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
 
 bool pq_supported_m(int M) { return M > 0 && M <= 64 && M % 8 == 0; }
 
-int pq_scan_chunk(int M, int d) { return pq_group_usable(M, d) ? kRChunk : kPChunk; }
+int pq_scan_chunks(int M, int d, int count) {
+    if (count <= 0) return 0;
+    return pq_group_usable(M, d) ? gring_chunks(count) : (count + kPChunk - 1) / kPChunk;
+}
+
+int pq_scan_chunk_items(int M, int d) { return pq_group_usable(M, d) ? kRRings * kRSteps : kPChunk; }
+
+int pq_chunk_slack(int M, int d, int R) { return pq_group_usable(M, d) ? R / 4 : 0; }
 
 int64_t pq_gring_list_bytes(int count, int M) { return gring_tiles(count) * 128 * (M / 8); }
 

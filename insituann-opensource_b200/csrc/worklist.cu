@@ -55,14 +55,14 @@ __global__ void group_count_kernel(const int32_t* list_cnt, int nlist, int32_t* 
     else if (l == nlist) grp_cnt[l] = 0;
 }
 
-__global__ void group_fill_kernel(const int32_t* list_off, const int32_t* grp_off, int nlist, int32_t* groups) {
+__global__ void group_fill_kernel(const int32_t* list_off, const int32_t* grp_off, int nlist, int64_t* groups) {
     int l = blockIdx.x * blockDim.x + threadIdx.x;
     if (l >= nlist) return;
     const int first = list_off[l], n = list_off[l + 1] - first;
     int g = grp_off[l];
     for (int o = 0; o < n; o += kGroupQueries) {
         const int sz = n - o < kGroupQueries ? n - o : kGroupQueries;
-        groups[g++] = ((first + o) << 3) | sz;
+        groups[g++] = ((int64_t)l << 32) | (int64_t)(((first + o) << 3) | sz);
     }
 }
 
