@@ -115,28 +115,54 @@ __device__ __forceinline__ void warp_append(KeyFn keyf, int n, uint64_t cut, con
     }
 }
 
-// warp_append over ITEMS keys per thread held in registers: keyj(j) is the
-// thread's j-th key (kKeyNone for none); j is a compile-time index after
-// unrolling, so register arrays behind keyj stay in registers.
+// Appends every key <= cut among ITEMS keys per thread held in registers
+// (keyj(j), kKeyNone for none; j is a compile-time index after unrolling, so
+// register arrays behind keyj stay in registers) with one atomic per warp:
+// the warp's takes are counted by ballots first, then placed item by item.
 template <int ITEMS, class KeyJ>
 __device__ __forceinline__ void warp_append_items(KeyJ keyj, uint64_t cut, const CandBuf& cb, int q) {
     const int lane = threadIdx.x & 31;
-    uint64_t* out = cb.keys + (size_t)q * cb.cap;
+    unsigned ball[ITEMS];
+    int n = 0;
 #pragma unroll
     for (int j = 0; j < ITEMS; ++j) {
-        const uint64_t k = keyj(j);
-        const bool take = k <= cut;
-        const unsigned ball = __ballot_sync(0xffffffffu, take);
-        if (ball == 0) continue;
-        int base = 0;
-        if (lane == 0) base = atomicAdd(cb.cnt + q, __popc(ball));
-        base = __shfl_sync(0xffffffffu, base, 0);
-        if (take) {
-            const int at = base + __popc(ball & ((1u << lane) - 1u));
-            if (at < cb.cap) out[at] = k;
+        ball[j] = __ballot_sync(0xffffffffu, keyj(j) <= cut);
+        n += __popc(ball[j]);
+    }
+    if (n == 0) return;
+    int base = 0;
+    if (lane == 0) base = atomicAdd(cb.cnt + q, n);
+    base = __shfl_sync(0xffffffffu, base, 0);
+    uint64_t* out = cb.keys + (size_t)q * cb.cap;
+    const unsigned below = (1u << lane) - 1u;
+#pragma unroll
+    for (int j = 0; j < ITEMS; ++j) {
+        if ((ball[j] >> lane) & 1u) {
+            const int at = base + __popc(ball[j] & below);
+            if (at < cb.cap) out[at] = keyj(j);
             else atomicExch(cb.overflow, 1);
         }
+        base += __popc(ball[j]);
     }
+}
+
+// Block-wide totals of four per-thread counts with one barrier: each warp
+// reduces in hardware and adds into cnt[4] (shared), which the caller zeroed
+// before the previous barrier; every thread reads the four totals.
+template <int T>
+__device__ __forceinline__ int4 block_sum4_once(int4 v, int* cnt) {
+    const unsigned a = __reduce_add_sync(0xffffffffu, (unsigned)v.x);
+    const unsigned b = __reduce_add_sync(0xffffffffu, (unsigned)v.y);
+    const unsigned c = __reduce_add_sync(0xffffffffu, (unsigned)v.z);
+    const unsigned d = __reduce_add_sync(0xffffffffu, (unsigned)v.w);
+    if ((threadIdx.x & 31) == 0) {
+        if (a) atomicAdd(cnt, (int)a);
+        if (b) atomicAdd(cnt + 1, (int)b);
+        if (c) atomicAdd(cnt + 2, (int)c);
+        if (d) atomicAdd(cnt + 3, (int)d);
+    }
+    __syncthreads();
+    return make_int4(cnt[0], cnt[1], cnt[2], cnt[3]);
 }
 
 // Cut keys for up to Q = 4 queries at once, over ITEMS keys per thread in
@@ -150,14 +176,16 @@ __device__ __forceinline__ void warp_append_items(KeyJ keyj, uint64_t cut, const
 // barriers, the first digit is the 8 bits just below the highest bit in which
 // the query's participants differ (block min and max), and a query stops as
 // soon as the bin holding its R-th key is small enough (so the cut is the end
-// of that bin, not necessarily the R-th key itself).  hist: Q * 256 ints of
-// shared memory the caller may reuse afterwards only after a barrier;
+// of that bin, not necessarily the R-th key itself).  Passes alternate
+// between two histogram buffers so each takes two barriers.  hist: 2 * Q * 256
+// ints of shared memory the caller may reuse afterwards only after a barrier;
 // bc: 4 * Q ints; mm: 2 * Q * (T / 32) uint64.
 template <int T, int ITEMS, int Q, class KeyF>
 __device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, const uint64_t (&upper)[Q],
                                 int* hist, int* bc, unsigned long long* mm, uint64_t (&cut)[Q]) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     constexpr int W = T / 32;
+    for (int b = tid; b < Q * 256; b += T) hist[b] = 0;
     uint64_t lo[Q], hi[Q];
 #pragma unroll
     for (int q = 0; q < Q; ++q) {
@@ -211,9 +239,8 @@ __device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, con
         prefix[q] = lo[q] & mask[q];
         todo |= 1u << q;
     }
-    while (todo) {
-        for (int b = tid; b < Q * 256; b += T) hist[b] = 0;
-        __syncthreads();
+    for (int pass = 0; todo; ++pass) {
+        int* h = hist + (pass & 1) * (Q * 256);              // zeroed before the last barrier
 #pragma unroll
         for (int e = 0; e < ITEMS; ++e) {
 #pragma unroll
@@ -223,10 +250,14 @@ __device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, con
                 const bool part = k <= upper[q] && (k & mask[q]) == prefix[q];
                 const int bin = part ? q * 256 + (int)((k >> shift[q]) & 255u) : Q * 256 + lane;
                 const unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (part && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], __popc(peers));
+                if (part && (__ffs(peers) - 1) == lane) atomicAdd(&h[bin], __popc(peers));
             }
         }
         __syncthreads();
+        {
+            int* hn = hist + ((pass + 1) & 1) * (Q * 256);   // the next pass's buffer
+            for (int b = tid; b < Q * 256; b += T) hn[b] = 0;
+        }
         if (warp < Q && ((todo >> warp) & 1u)) {      // warp q finds the bin of query q's need-th key
             const int q = warp;
             int needq = 0;
@@ -236,7 +267,7 @@ __device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, con
             int sum = 0;
 #pragma unroll
             for (int jj = 0; jj < 8; ++jj) {
-                loc[jj] = hist[q * 256 + lane * 8 + jj];
+                loc[jj] = h[q * 256 + lane * 8 + jj];
                 sum += loc[jj];
             }
             const int incl = warp_incl_scan(sum);

@@ -127,46 +127,50 @@ __global__ void __launch_bounds__(kPT) pq_scan_kernel(PQParams p, WorkList wl, C
 constexpr int kGQ = 4;      // queries per group
 
 // ---------------------------------------------------------------------------
-// Grouped ring ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8): the kernel the
-// search uses for these shapes.
+// Grouped phase-staggered ADC scan (M = 16, 32, 48 with dsub = 2, 4 or 8):
+// the kernel the search uses for these shapes.
 //
 // A CTA takes one list and up to 4 probing queries (a group of the work list)
-// and the four queries' LUTs are interleaved as float4.  Instead of one thread summing a
-// whole vector, a warp runs four systolic rings of 8 lanes: lane j of a ring
-// owns the MPL = M/8 consecutive sub-quantizers m = MPL*j .. MPL*j+MPL-1.  At
-// step x it receives the four partial sums of vector x-j from lane j-1
-// (shuffles), adds its MPL entries in m order and passes them on; lane 7
-// finishes vector x-7.  The distance of every query is therefore still the
-// sum over m in m order.
+// and the four queries' LUTs are interleaved as float4.  The M sub-quantizers
+// form 8 blocks of MPL = M/8.  A warp is four groups of 8 lanes; lane j of a
+// group sums the vectors 8k + j of its stripe, one block per step, blocks in
+// order, so a vector takes 8 steps and is started at step 8k + j: at step x
+// lane j works on block (x - j) mod 8, the 8 lanes of a group always on 8
+// different blocks, and the lane whose block is 7 finishes vector x - 7.  A
+// sum never leaves its lane (no shuffles), and every distance is the sum over
+// m in m order.
 //
-// LUT row c holds entry m at float4 position p(m) = m/MPL + 8*(m%MPL), so in
-// every gather lane j of a ring reads bank group j: each quarter-warp (one
-// ring) touches 8 distinct 16-byte bank groups and the gather is
+// LUT row c holds entry m at float4 position p(m) = m/MPL + 8*(m%MPL): block
+// b lies in the 16-byte bank group b of every row, so the 8 lanes of a group
+// (one quarter-warp) read 8 distinct bank groups and each gather is
 // conflict-free whatever the code values.
 //
 // Codes are re-laid out once per index (pq_build_gring) into tiles of 16
-// steps.  Lane j's stream of a tile is the 16*MPL bytes b = i*MPL + s (step i,
-// sub-quantizer s) holding code[16T+i-j][MPL*j+s] (0 outside the list); its
-// 16-byte piece u = b/16 sits at tile offset (8u + j)*16, so each of a ring's
-// MPL 16-byte loads reads one whole 128-byte line, and the lane indexes the
-// bytes statically.
+// steps.  Lane j's stream of tile T is the 16*MPL bytes b = i*MPL + s (step i,
+// sub-quantizer s of the block) holding code[v][MPL*blk + s] with
+// g = 16T + i - j, v = 8*floor(g/8) + j, blk = g mod 8 (0 outside the list);
+// its 16-byte piece u = b/16 sits at tile offset (8u + j)*16, so each of a
+// group's MPL 16-byte loads reads one whole 128-byte line, and the lane
+// indexes the bytes statically.
 //
 // The sums of queries (0,1) and (2,3) are float2 pairs added with the packed
-// fp32x2 instructions (__fadd2_rn: two independent round-to-nearest adds).
+// fp32x2 instructions (__fadd2_rn: two independent round-to-nearest adds).  A
+// lane starts a vector with an FMA by 0 of its previous sum, which assumes
+// finite LUT entries (an entry overflows only for |q - c| above 1e19).
 // ---------------------------------------------------------------------------
 constexpr int kRW = 8;                 // warps per CTA
 constexpr int kRT = 32 * kRW;          // threads per CTA
 constexpr int kRChunk = 2048;          // vectors per filtered chunk
-constexpr int kRRings = 4 * kRW;       // 8-lane rings per CTA
-constexpr int kRSteps = kRChunk / kRRings;   // ring steps per filtered chunk (a multiple of 16)
+constexpr int kRRings = 4 * kRW;       // 8-lane groups (stripes) per CTA
+constexpr int kRSteps = kRChunk / kRRings;   // steps per filtered chunk (a multiple of 16)
 static_assert(kRSteps % 16 == 0, "a chunk is whole tiles");
 
 __host__ __device__ inline int64_t gring_tiles(int count) { return (int64_t)(count + 7) / 16 + 3; }
-// vectors per ring stripe: count / kRRings rounded up to whole tiles
+// vectors per stripe: count / kRRings rounded up to whole tiles
 __host__ __device__ inline int gring_stripe(int count) {
     return (int)(((int64_t)count + 16 * kRRings - 1) / (16 * kRRings)) * 16;
 }
-// filtered chunks of one list: ring 0 runs min(S, count) + 7 steps
+// filtered chunks of one list: stripe 0 takes min(S, count) + 7 steps
 __host__ __device__ inline int gring_chunks(int count) {
     if (count <= 0) return 0;
     const int S = gring_stripe(count);
@@ -182,35 +186,33 @@ struct GRing {
 };
 
 // NST steps (NST = 16: a whole tile; otherwise the first nst < 16) of one
-// lane of a ring.  Lane 0 starts a vector's four sums with its first entry
-// (keep2 = 0 there: its shuffle returns its own stale sums, times 0), every
-// other lane continues the sums received from lane j-1; lane 7 stores the
-// finished sums of step i to out[i * kRRings].
+// lane: at step i of the tile the lane is on block (i - j) mod 8 (tiles start
+// on multiples of 16 steps); the lane whose block is 7 stores the finished
+// sums of step i to out[i * kRRings].
 template <int M, int NST>
-__device__ __forceinline__ void gring_tile(const float4* __restrict__ lutj, const uint32_t (&w)[M / 2], int nst,
-                                           float2 keep2, int j, float2& s01, float2& s23, float4* out) {
+__device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, const uint32_t (&w)[M / 2], int nst,
+                                             int j, float2& s01, float2& s23, float4* out) {
     constexpr int MPL = M / 8;
 #pragma unroll
     for (int i = 0; i < NST; ++i) {
         if (NST < 16 && i >= nst) break;
-        const float2 i01 = make_float2(__shfl_up_sync(0xffffffffu, s01.x, 1, 8),
-                                       __shfl_up_sync(0xffffffffu, s01.y, 1, 8));
-        const float2 i23 = make_float2(__shfl_up_sync(0xffffffffu, s23.x, 1, 8),
-                                       __shfl_up_sync(0xffffffffu, s23.y, 1, 8));
+        const int blk = (i - j) & 7;
+        const float4* lb = lut + blk;               // entries MPL*blk + s at positions blk + 8*s
+        const float2 k2 = blk == 0 ? make_float2(0.f, 0.f) : make_float2(1.f, 1.f);
 #pragma unroll
         for (int s = 0; s < MPL; ++s) {
             const int byte = i * MPL + s;
             const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
-            const float4 f = lutj[c * M + 8 * s];
+            const float4 f = lb[c * M + 8 * s];
             if (s == 0) {
-                s01 = __ffma2_rn(i01, keep2, make_float2(f.x, f.y));
-                s23 = __ffma2_rn(i23, keep2, make_float2(f.z, f.w));
+                s01 = __ffma2_rn(s01, k2, make_float2(f.x, f.y));
+                s23 = __ffma2_rn(s23, k2, make_float2(f.z, f.w));
             } else {
                 s01 = __fadd2_rn(s01, make_float2(f.x, f.y));
                 s23 = __fadd2_rn(s23, make_float2(f.z, f.w));
             }
         }
-        if (j == 7) out[i * kRRings] = make_float4(s01.x, s01.y, s23.x, s23.y);
+        if (blk == 7) out[i * kRRings] = make_float4(s01.x, s01.y, s23.x, s23.y);
     }
 }
 
@@ -244,7 +246,7 @@ __device__ __forceinline__ void load_tile(const uint4* lanebase, int64_t T, uint
 //   * the first code tile is requested before the LUT is built, each next
 //     tile one tile ahead, and each chunk's query bounds before its steps.
 template <int M, int DSUB>
-__global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
+__global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
                                                           int* counter) {
     using RG = GRing<M>;
     constexpr int MPL = RG::MPL;
@@ -258,16 +260,18 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
     float* resid = reinterpret_cast<float*>(dist4);         // [kGQ][d] while the LUT is built
     __shared__ EmitSmem esm;
     __shared__ int s_item, s_q[kGQ];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, ring = lane >> 3, j = lane & 7;
-    const float2 keep2 = j == 0 ? make_float2(0.f, 0.f) : make_float2(1.f, 1.f);
+    __shared__ int s_cnt[2][kGQ];       // per-chunk totals, alternating buffers
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, grp = lane >> 3, j = lane & 7;
     // LUT builders: thread t owns LUT column ps = t % M (sub-quantizer inv(ps)) for codes t / M + kCStep * i
     const bool builder = tid < kCStep * M;
     const int ps = tid % M, mcol = RG::inv(ps), c0 = tid / M;
     const int NG = *wl.n_groups;
     const int total = p.has_delta ? 2 * NG : NG;
-    const int rid = warp * 4 + ring;
+    const int rid = warp * 4 + grp;          // stripe of this lane group
+    if (tid < 2 * kGQ) s_cnt[tid / kGQ][tid % kGQ] = 0;
     if (tid == 0) s_item = atomicAdd(counter, 1);
     __syncthreads();
+    int cpar = 0;                       // buffer of s_cnt the next chunk adds into
     float cbv[kLB][DSUB];
     auto load_cb = [&](int cbase) {
 #pragma unroll
@@ -306,16 +310,16 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
             const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
             const uint8_t* tiles = SG.gring + SG.gring_off[l];
             const int64_t ntiles = gring_tiles(count);
-            // Ring r owns the stripe [r*S, r*S + S) of the list (S a multiple
-            // of 16, so a stripe starts on a tile) and runs through it without
-            // draining: its lane 7 finishes vector r*S + x - 7 at step x.
+            // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
+            // multiple of 16, so a stripe starts on a tile) and runs through it
+            // without draining: it finishes vector r*S + x - 7 at step x.
             // Steps are cut into chunks of kRSteps; after each chunk the CTA
             // filters the kRRings * kRSteps finished slots.  The longest
-            // stripe (ring 0) takes min(S, count) + 7 steps.
+            // stripe (group 0) takes min(S, count) + 7 steps.
             const int S = gring_stripe(count);
             const int a = rid * S < count ? rid * S : count;
             const int wa = warp * 4 * S;
-            const int wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its ring 0)
+            const int wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its group 0)
             const int nchunks = gring_chunks(count);
             const uint4* lanebase = reinterpret_cast<const uint4*>(tiles) + j;
             const int64_t T0 = a / 16;
@@ -367,8 +371,6 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
             int qid[kGQ];
 #pragma unroll
             for (int k = 0; k < kGQ; ++k) qid[k] = s_q[k];
-            // this lane's LUT columns: pos(MPL*j + s) = j + 8*s
-            const float4* lutj = lut + j;
             float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
             const uint32_t kbase = (uint32_t)koff;
             for (int t = 0; t < nchunks; ++t) {
@@ -381,22 +383,25 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
                     const int x0 = t * kRSteps + 16 * tl;
                     if (x0 >= wsteps) break;
                     load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
-                    // slot of (step s of the chunk, ring r) = s * kRRings + r: the
-                    // four rings of a warp store 64 contiguous bytes per step
+                    // slot of (step s of the chunk, group r) = s * kRRings + r: the
+                    // four groups of a warp store 64 contiguous bytes per step
                     float4* out = dist4 + 16 * tl * kRRings + rid;
                     if (wsteps - x0 >= 16)
-                        gring_tile<M, 16>(lutj, w, 16, keep2, j, s01, s23, out);
+                        stagger_tile<M, 16>(lut, w, 16, j, s01, s23, out);
                     else
-                        gring_tile<M, 15>(lutj, w, wsteps - x0, keep2, j, s01, s23, out);
+                        stagger_tile<M, 15>(lut, w, wsteps - x0, j, s01, s23, out);
 #pragma unroll
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
                 __syncthreads();
-                // thread t reads the slots t + kRT*e: ring t % 32 (= lane), chunk
+                // every thread has finished the previous chunk: its totals
+                // buffer is free for the chunk after this one
+                if (tid < kGQ) s_cnt[cpar ^ 1][tid] = 0;
+                // thread t reads the slots t + kRT*e: group t % 32 (= lane), chunk
                 // steps warp + 8e, i.e. vectors lane*S + t*kRSteps + warp + 8e - 7.
-                // All of them are read into registers before block_sum4's
-                // barriers, so the next chunk may overwrite the slots as soon as
-                // those have passed.
+                // All of them are read into registers before the totals'
+                // barrier, so the next chunk may overwrite the slots as soon as
+                // that has passed.
                 constexpr int kE = kRRings * kRSteps / kRT;
                 float4 f[kE];
                 uint32_t vid[kE];     // list position, or 0xFFFFFFFF for no vector
@@ -421,7 +426,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_gring_kernel(PQParams p, WorkList w
                 for (int e = 0; e < kE; ++e)
 #pragma unroll
                     for (int k = 0; k < kGQ; ++k) cnt4[k] += (k < nqg && key_of(e, k) <= thr[k]) ? 1 : 0;
-                const int4 tot = block_sum4<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), esm.scratch);
+                const int4 tot = block_sum4_once<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), s_cnt[cpar]);
+                cpar ^= 1;
                 const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
                 // queries with more than R keys under their bound get a new
                 // bound that admits R .. R + slack of them (one shared descent
@@ -461,19 +467,19 @@ cudaError_t launch_gring(const PQParams& p, WorkList wl, int max_groups, CandBuf
                          cudaStream_t st) {
     const size_t smem = GRing<M>::smem_bytes();
     cudaError_t e =
-        cudaFuncSetAttribute(pq_gring_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(pq_stagger_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_gring_kernel<M, DSUB>, kRT, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_stagger_kernel<M, DSUB>, kRT, smem);
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     long long items = (long long)max_groups * (p.has_delta ? 2 : 1);
     long long grid = (long long)sms * per_sm;
     if (grid > items) grid = items;
     if (grid < 1) grid = 1;
     note_launch();
-    pq_gring_kernel<M, DSUB><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
+    pq_stagger_kernel<M, DSUB><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
     return cudaGetLastError();
 }
 
@@ -490,8 +496,11 @@ __global__ void gring_layout_kernel(const uint8_t* __restrict__ codes, const int
             const int64_t T = e / (128 * MPL);
             const int r = (int)(e % (128 * MPL));
             const int u = r / 128, jj = (r % 128) / 16, b = 16 * u + r % 16, i = b / MPL, s = b % MPL;
-            const int64_t v = 16 * T + i - jj;
-            dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * jj + s] : (uint8_t)0;
+            const int64_t g = 16 * T + i - jj;
+            const int64_t g8 = g >= 0 ? g / 8 : -((7 - g) / 8);      // floor(g / 8)
+            const int blk = (int)(g - 8 * g8);
+            const int64_t v = 8 * g8 + jj;
+            dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * blk + s] : (uint8_t)0;
         }
     }
 }
