@@ -247,10 +247,7 @@ __device__ void block_cut_items(KeyF key, unsigned active, int R, int slack, con
             for (int q = 0; q < Q; ++q) {
                 if (!((todo >> q) & 1u)) continue;       // uniform over the block
                 const uint64_t k = key(e, q);
-                const bool part = k <= upper[q] && (k & mask[q]) == prefix[q];
-                const int bin = part ? q * 256 + (int)((k >> shift[q]) & 255u) : Q * 256 + lane;
-                const unsigned peers = __match_any_sync(0xffffffffu, bin);
-                if (part && (__ffs(peers) - 1) == lane) atomicAdd(&h[bin], __popc(peers));
+                if (k <= upper[q] && (k & mask[q]) == prefix[q]) atomicAdd(&h[q * 256 + (int)((k >> shift[q]) & 255u)], 1);
             }
         }
         __syncthreads();

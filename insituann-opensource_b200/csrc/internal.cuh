@@ -132,12 +132,9 @@ __device__ uint64_t block_kth_each(EachFn each, int need, uint64_t upper, int* h
 
 // The selection of block_kth_each over ITEMS keys per thread held in
 // registers (keyj(j) for j < ITEMS, kKeyNone for none; all threads call it
-// together).  Two things make it cheap on the clustered keys of one chunk:
-//   * the first pass starts at the highest byte in which the participants
-//     differ (block-wide min and max), skipping the bytes they all share;
-//   * histogram increments are combined per warp (__match_any_sync), so a bin
-//     that many keys fall into costs one shared atomic per warp and item.
-// mm: 2 * 32 uint64 of shared memory.
+// together).  The first pass starts at the highest byte in which the
+// participants differ (block-wide min and max), skipping the bytes they all
+// share.  mm: 2 * 32 uint64 of shared memory.
 template <int T, int ITEMS, class KeyJ>
 __device__ uint64_t block_kth_items(KeyJ keyj, int need, uint64_t upper, int* hist, int* bc,
                                     unsigned long long* mm) {
@@ -183,10 +180,7 @@ __device__ uint64_t block_kth_items(KeyJ keyj, int need, uint64_t upper, int* hi
 #pragma unroll
         for (int j = 0; j < ITEMS; ++j) {
             const uint64_t k = keyj(j);
-            const bool part = k <= upper && (k & mask) == prefix;
-            const int bin = part ? (int)((k >> shift) & 255u) : 256 + lane;
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (part && (__ffs(peers) - 1) == lane) atomicAdd(&hist[bin], __popc(peers));
+            if (k <= upper && (k & mask) == prefix) atomicAdd(&hist[(int)((k >> shift) & 255u)], 1);
         }
         __syncthreads();
         if (warp == 0) {

@@ -23,59 +23,71 @@ __global__ void centroid_valid_kernel(const float* __restrict__ cent, int nlist,
     valid[c] = (sqrtf(s) >= 1e-6f) ? 1 : 0;
 }
 
-// 64 queries x 64 centroids per CTA, 256 threads, 4x4 pairs per thread,
-// 32 dimensions staged per step.  Zero padding beyond d adds exact zeros.
-constexpr int kRB = 64, kRK = 32;
+// 128 queries x 128 centroids per CTA, 256 threads, 8x8 pairs per thread, 16
+// dimensions staged per step.  The centroid tile is staged negated, so
+// q - c is one packed add (x + (-y) is x - y exactly); a thread's pairs are
+// float2 accumulators of two centroids updated with the packed fp32x2
+// instructions (two independent round-to-nearest operations each).  Zero
+// padding beyond d adds exact zeros.
+constexpr int kRB = 128, kRK = 16;
 
 __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict__ q, int nq,
                                                          const float* __restrict__ cent,
                                                          const uint8_t* __restrict__ valid, int nlist,
                                                          int d, uint32_t* __restrict__ out) {
-    __shared__ float sq[kRK][kRB + 4];
-    __shared__ float sc[kRK][kRB + 4];
+    __shared__ __align__(16) float sq[kRK][kRB + 4];
+    __shared__ __align__(16) float sc[kRK][kRB + 4];     // -centroid
     const int tid = threadIdx.x;
     const int tx = tid & 15, ty = tid >> 4;
     const int q0 = blockIdx.y * kRB, c0 = blockIdx.x * kRB;
-    float acc[4][4];
+    float2 acc[8][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+        for (int j = 0; j < 4; ++j) acc[i][j] = make_float2(0.f, 0.f);
 
     for (int k0 = 0; k0 < d; k0 += kRK) {
         for (int e = tid; e < kRB * kRK; e += 256) {
-            int r = e / kRK, kk = e % kRK;
-            int qi = q0 + r, ci = c0 + r, j = k0 + kk;
+            const int r = e / kRK, kk = e % kRK;
+            const int qi = q0 + r, ci = c0 + r, j = k0 + kk;
             sq[kk][r] = (qi < nq && j < d) ? q[(size_t)qi * d + j] : 0.f;
-            sc[kk][r] = (ci < nlist && j < d) ? cent[(size_t)ci * d + j] : 0.f;
+            sc[kk][r] = (ci < nlist && j < d) ? -cent[(size_t)ci * d + j] : 0.f;
         }
         __syncthreads();
-#pragma unroll 8
+#pragma unroll 4
         for (int kk = 0; kk < kRK; ++kk) {
-            float a[4], b[4];
+            const float4 a0 = *reinterpret_cast<const float4*>(&sq[kk][ty * 8]);
+            const float4 a1 = *reinterpret_cast<const float4*>(&sq[kk][ty * 8 + 4]);
+            const float4 b0 = *reinterpret_cast<const float4*>(&sc[kk][tx * 8]);
+            const float4 b1 = *reinterpret_cast<const float4*>(&sc[kk][tx * 8 + 4]);
+            const float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float2 b[4] = {make_float2(b0.x, b0.y), make_float2(b0.z, b0.w), make_float2(b1.x, b1.y),
+                                 make_float2(b1.z, b1.w)};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) a[i] = sq[kk][ty * 4 + i];
-#pragma unroll
-            for (int j = 0; j < 4; ++j) b[j] = sc[kk][tx * 4 + j];
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
+            for (int i = 0; i < 8; ++i) {
+                const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    float x = __fsub_rn(a[i], b[j]);
-                    acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(x, x));
+                    const float2 x = __fadd2_rn(ai, b[j]);
+                    acc[i][j] = __fadd2_rn(acc[i][j], __fmul2_rn(x, x));
                 }
+            }
         }
         __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        int qi = q0 + ty * 4 + i;
+    for (int i = 0; i < 8; ++i) {
+        const int qi = q0 + ty * 8 + i;
         if (qi >= nq) continue;
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            int ci = c0 + tx * 4 + j;
-            if (ci >= nlist) continue;
-            out[(size_t)qi * nlist + ci] = valid[ci] ? __float_as_uint(acc[i][j]) : 0xFFFFFFFFu;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int ci = c0 + tx * 8 + 2 * j + h;
+                if (ci >= nlist) continue;
+                const float v = h ? acc[i][j].y : acc[i][j].x;
+                out[(size_t)qi * nlist + ci] = valid[ci] ? __float_as_uint(v) : 0xFFFFFFFFu;
+            }
         }
     }
 }
@@ -105,6 +117,66 @@ __device__ void select_row_topl(KeyFn keyf, int n, int L, uint64_t* s, int* hist
         for (int i = cl + tid; i < Lp; i += kSelT) s[i] = i < take ? kap : kKeyNone;
     }
     block_bitonic_sort<kSelT>(s, Lp);
+}
+
+// Rows of up to kRowT * kRowItems keys: one CTA of kRowT threads per row, the
+// row's keys in registers, a radix descent for the L-th key, the keys below it
+// compacted and only those L sorted.
+constexpr int kRowT = 256, kRowItems = 16;
+
+__global__ void __launch_bounds__(kRowT) route_select_reg_kernel(const uint32_t* __restrict__ dist_bits, int n,
+                                                                  int L, const int32_t* __restrict__ id_map,
+                                                                  int32_t* out_ids, float* out_dist,
+                                                                  uint64_t* out_keys) {
+    __shared__ uint64_t s[kSelMaxL];
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ unsigned long long mm[64];
+    __shared__ int s_cnt;
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+    const uint32_t* r = dist_bits + (size_t)row * n;
+    int Lp = 1;
+    while (Lp < L) Lp <<= 1;
+    uint64_t v[kRowItems];
+#pragma unroll
+    for (int e = 0; e < kRowItems; ++e) {
+        const int i = tid + kRowT * e;
+        v[e] = i < n ? make_key(r[i], id_map ? (uint32_t)id_map[i] : (uint32_t)i) : kKeyNone;
+    }
+    if (tid == 0) s_cnt = 0;
+    if (n <= L) {
+        __syncthreads();
+#pragma unroll
+        for (int e = 0; e < kRowItems; ++e) {
+            const int i = tid + kRowT * e;
+            if (i < n) s[i] = v[e];
+        }
+        for (int i = n + tid; i < Lp; i += kRowT) s[i] = kKeyNone;
+    } else {
+        const uint64_t kap =
+            block_kth_items<kRowT, kRowItems>([&](int e) { return v[e]; }, L, kKeyNone - 1, hist, bc, mm);
+#pragma unroll
+        for (int e = 0; e < kRowItems; ++e) {
+            const bool take = v[e] < kap;
+            const unsigned ball = __ballot_sync(0xffffffffu, take);
+            if (ball == 0) continue;
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&s_cnt, __popc(ball));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (take) s[base + __popc(ball & ((1u << lane) - 1u))] = v[e];
+        }
+        __syncthreads();
+        const int cl = s_cnt;
+        for (int i = cl + tid; i < Lp; i += kRowT) s[i] = i < L ? kap : kKeyNone;
+    }
+    block_bitonic_sort<kRowT>(s, Lp);
+    for (int i = tid; i < L; i += kRowT) {
+        const uint64_t k = s[i];
+        const bool ok = k != kKeyNone && key_hi(k) != 0xFFFFFFFFu;
+        if (out_ids) out_ids[(size_t)row * L + i] = ok ? (int32_t)key_lo(k) : -1;
+        if (out_dist) out_dist[(size_t)row * L + i] = ok ? __uint_as_float(key_hi(k)) : __int_as_float(0x7f800000);
+        if (out_keys) out_keys[(size_t)row * L + i] = k;
+    }
 }
 
 __global__ void __launch_bounds__(kSelT) route_select_kernel(const uint32_t* __restrict__ dist_bits, int n, int L,
@@ -179,7 +251,10 @@ cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const 
     if (L > kSelMaxL || L <= 0) return cudaErrorInvalidValue;
     if (nq <= 0) return cudaSuccess;
     note_launch();
-    route_select_kernel<<<nq, kSelT, 0, st>>>(dist_bits, n, L, id_map, out_ids, out_dist, out_keys);
+    if (n <= kRowT * kRowItems)
+        route_select_reg_kernel<<<nq, kRowT, 0, st>>>(dist_bits, n, L, id_map, out_ids, out_dist, out_keys);
+    else
+        route_select_kernel<<<nq, kSelT, 0, st>>>(dist_bits, n, L, id_map, out_ids, out_dist, out_keys);
     return cudaGetLastError();
 }
 

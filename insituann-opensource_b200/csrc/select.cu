@@ -3,15 +3,14 @@
 // Replaces the reference's group bitonic merges with host syncs between
 // rounds (updates/pq_update.cu:91-115, 944-967) and the per-thread heap
 // merge of the CPU path (cpu_fine_kernels_v3_u8.cpp:574-592): one CTA per
-// query selects the R smallest keys of its buffer and sorts them.
+// query selects the R smallest keys of its buffer and sorts them (ties at the
+// R-th key are filled with copies of it, as a bounded heap would keep them).
 #include "launch.h"
 
 namespace isb {
 
 namespace {
 
-constexpr int kT = 512;
-constexpr int kSortMax = 4096;   // buffers up to this size are sorted whole
 
 __global__ void reset_kernel(int32_t* cnt, unsigned long long* thr, int nq) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -21,40 +20,68 @@ __global__ void reset_kernel(int32_t* cnt, unsigned long long* thr, int nq) {
     }
 }
 
-__global__ void __launch_bounds__(kT) select_top_r_kernel(const uint64_t* __restrict__ keys,
-                                                          const int32_t* __restrict__ cnt, int cap, int R,
-                                                          uint64_t* __restrict__ out) {
+// One CTA per query.  Buffers of up to kSelT * kSelItems keys go to
+// registers (one coalesced read) and the R-th key is found by a radix descent
+// over the registers; longer buffers are read from global memory on every
+// pass.  The keys below the R-th are compacted to shared memory and only
+// those R are sorted.
+constexpr int kSelT = 256;
+constexpr int kSelItems = 16;
+
+__global__ void __launch_bounds__(kSelT) select_top_r_kernel(const uint64_t* __restrict__ keys,
+                                                             const int32_t* __restrict__ cnt, int cap, int R,
+                                                             uint64_t* __restrict__ out) {
     extern __shared__ uint64_t s[];
     __shared__ int hist[256];
     __shared__ int bc[4];
+    __shared__ unsigned long long mm[64];
     __shared__ int s_cnt;
-    const int q = blockIdx.x, tid = threadIdx.x;
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
     int n = cnt[q];
     if (n > cap) n = cap;
     const uint64_t* kk = keys + (size_t)q * cap;
     int Rp = 1;
     while (Rp < R) Rp <<= 1;
-    if (n <= kSortMax) {
-        int np = 1;
-        while (np < n) np <<= 1;
-        if (np < Rp) np = Rp;
-        for (int i = tid; i < np; i += kT) s[i] = i < n ? kk[i] : kKeyNone;
-        block_bitonic_sort<kT>(s, np);
+    if (n <= R) {                     // every key is kept
+        for (int i = tid; i < Rp; i += kSelT) s[i] = i < n ? kk[i] : kKeyNone;
+        block_bitonic_sort<kSelT>(s, Rp);
+        for (int i = tid; i < R; i += kSelT) out[(size_t)q * R + i] = s[i];
+        return;
+    }
+    if (tid == 0) s_cnt = 0;
+    uint64_t kap;
+    if (n <= kSelT * kSelItems) {
+        uint64_t v[kSelItems];
+#pragma unroll
+        for (int e = 0; e < kSelItems; ++e) {
+            const int i = tid + kSelT * e;
+            v[e] = i < n ? kk[i] : kKeyNone;
+        }
+        kap = block_kth_items<kSelT, kSelItems>([&](int e) { return v[e]; }, R, kKeyNone - 1, hist, bc, mm);
+        // keys below kappa (fewer than R), placed with one shared atomic per warp
+#pragma unroll
+        for (int e = 0; e < kSelItems; ++e) {
+            const bool take = v[e] < kap;
+            const unsigned ball = __ballot_sync(0xffffffffu, take);
+            if (ball == 0) continue;
+            int base = 0;
+            if (lane == 0) base = atomicAdd(&s_cnt, __popc(ball));
+            base = __shfl_sync(0xffffffffu, base, 0);
+            if (take) s[base + __popc(ball & ((1u << lane) - 1u))] = v[e];
+        }
     } else {
-        auto keyf = [&](int i) -> uint64_t { return kk[i]; };
-        uint64_t kap = block_kth_key<kT>(keyf, n, R, kKeyNone, hist, bc);
-        if (tid == 0) s_cnt = 0;
+        kap = block_kth_key<kSelT>([&](int i) -> uint64_t { return kk[i]; }, n, R, kKeyNone, hist, bc);
         __syncthreads();
-        for (int i = tid; i < n; i += kT) {
-            uint64_t k = kk[i];
+        for (int i = tid; i < n; i += kSelT) {
+            const uint64_t k = kk[i];
             if (k < kap) s[atomicAdd(&s_cnt, 1)] = k;
         }
-        __syncthreads();
-        int cl = s_cnt;
-        for (int i = cl + tid; i < Rp; i += kT) s[i] = i < R ? kap : kKeyNone;
-        block_bitonic_sort<kT>(s, Rp);
     }
-    for (int i = tid; i < R; i += kT) out[(size_t)q * R + i] = s[i];
+    __syncthreads();
+    const int cl = s_cnt;
+    for (int i = cl + tid; i < Rp; i += kSelT) s[i] = i < R ? kap : kKeyNone;   // copies of kappa fill to R
+    block_bitonic_sort<kSelT>(s, Rp);
+    for (int i = tid; i < R; i += kSelT) out[(size_t)q * R + i] = s[i];
 }
 
 __global__ void keys_to_exact_kernel(const uint64_t* __restrict__ keys, int total, int32_t* ids, int32_t* dist,
@@ -81,14 +108,13 @@ cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     int Rp = 1;
     while (Rp < cb.R) Rp <<= 1;
-    int elems = Rp > kSortMax ? Rp : kSortMax;
-    size_t smem = sizeof(uint64_t) * (size_t)elems;
+    const size_t smem = sizeof(uint64_t) * (size_t)Rp;
     if (smem > 64 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(select_top_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         64 * 1024);
+    cudaError_t e =
+        cudaFuncSetAttribute(select_top_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
     if (e) return e;
     note_launch();
-    select_top_r_kernel<<<nq, kT, smem, st>>>(cb.keys, cb.cnt, cb.cap, cb.R, out);
+    select_top_r_kernel<<<nq, kSelT, smem, st>>>(cb.keys, cb.cnt, cb.cap, cb.R, out);
     return cudaGetLastError();
 }
 
