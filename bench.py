@@ -469,13 +469,13 @@ def main():
     peak, peak_kind = peaks()
     achieved = bytes_per_launch / (scan_ms / 1000.0) / 1e9
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", f"pq_group_kernel_{args.config}_nprobe{nprobe}.md")
+    prof_path = os.path.join(ROOT, "profiles", f"pq_stagger_kernel_{args.config}_nprobe{nprobe}.md")
     if os.path.exists(prof_path) and N == 1:
         for line in open(prof_path):
-            if line.startswith("dram_bytes_per_launch:"):
+            if line.startswith("dram_bytes_per_search:"):
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "pq_group_kernel<48,2>", "peak_source": peak_kind,
+                "traffic": traffic, "kernel": "pq_stagger_kernel<48,2> (2 launches per search)", "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_ms_per_launch": scan_ms}
 
     cpu = None
