@@ -187,12 +187,15 @@ struct GRing {
 
 // NST steps (NST = 16: a whole tile; otherwise the first nst < 16) of one
 // lane: at step i of the tile the lane is on block (i - j) mod 8 (tiles start
-// on multiples of 16 steps); the lane whose block is 7 stores the finished
-// sums of step i to out[i * kRRings].
+// on multiples of 16 steps).  In each window of 8 steps every lane finishes
+// exactly one vector, at step 8w + ((j + 7) mod 8); the lane keeps its sums
+// and at the window's end (or the tile's last step) all lanes store together,
+// lane j to out[its finishing step]: one 16-byte store per lane per 8 steps.
 template <int M, int NST>
 __device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, const uint32_t (&w)[M / 2], int nst,
                                              int j, float2& s01, float2& s23, float4* out) {
     constexpr int MPL = M / 8;
+    float4 fin = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int i = 0; i < NST; ++i) {
         if (NST < 16 && i >= nst) break;
@@ -212,7 +215,11 @@ __device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, con
                 s23 = __fadd2_rn(s23, make_float2(f.z, f.w));
             }
         }
-        if (blk == 7) out[i * kRRings] = make_float4(s01.x, s01.y, s23.x, s23.y);
+        if (blk == 7) fin = make_float4(s01.x, s01.y, s23.x, s23.y);
+        if ((i & 7) == 7 || (NST < 16 && i == nst - 1)) {
+            const int fstep = (i & ~7) + ((j + 7) & 7);
+            if (fstep <= i) out[fstep] = fin;
+        }
     }
 }
 
@@ -383,9 +390,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     const int x0 = t * kRSteps + 16 * tl;
                     if (x0 >= wsteps) break;
                     load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
-                    // slot of (step s of the chunk, group r) = s * kRRings + r: the
-                    // four groups of a warp store 64 contiguous bytes per step
-                    float4* out = dist4 + 16 * tl * kRRings + rid;
+                    // slot of (group r, step s of the chunk) = r * kRSteps + s
+                    float4* out = dist4 + rid * kRSteps + 16 * tl;
                     if (wsteps - x0 >= 16)
                         stagger_tile<M, 16>(lut, w, 16, j, s01, s23, out);
                     else
@@ -397,8 +403,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 // every thread has finished the previous chunk: its totals
                 // buffer is free for the chunk after this one
                 if (tid < kGQ) s_cnt[cpar ^ 1][tid] = 0;
-                // thread t reads the slots t + kRT*e: group t % 32 (= lane), chunk
-                // steps warp + 8e, i.e. vectors lane*S + t*kRSteps + warp + 8e - 7.
+                // thread t reads the slots t + kRT*e: group t/64 + 4e, chunk step
+                // t % 64, i.e. vectors (t/64 + 4e)*S + t*kRSteps + t%64 - 7.
                 // All of them are read into registers before the totals'
                 // barrier, so the next chunk may overwrite the slots as soon as
                 // that has passed.
@@ -407,8 +413,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 uint32_t vid[kE];     // list position, or 0xFFFFFFFF for no vector
 #pragma unroll
                 for (int e = 0; e < kE; ++e) {
-                    const int x = t * kRSteps + warp + 8 * e;
-                    const int v = lane * S + x - 7;
+                    const int x = t * kRSteps + (tid % kRSteps);
+                    const int v = (tid / kRSteps + (kRT / kRSteps) * e) * S + x - 7;
                     vid[e] = (x >= 7 && x - 7 < S && v < count) ? (uint32_t)v : 0xFFFFFFFFu;
                     f[e] = vid[e] != 0xFFFFFFFFu ? dist4[tid + kRT * e] : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
