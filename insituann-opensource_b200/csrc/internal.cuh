@@ -20,6 +20,20 @@ constexpr uint64_t kKeyNone = ~0ull; // empty slot / "no bound yet"
 __device__ __forceinline__ uint64_t make_key(uint32_t hi, uint32_t lo) {
     return ((uint64_t)hi << 32) | (uint64_t)lo;
 }
+// Packed fp32x2 add with an explicit round-to-nearest modifier in PTX: each
+// half is one IEEE single-precision addition (checked bit for bit against the
+// CPU statement).  There is deliberately no packed multiply helper: a packed
+// multiply feeding a packed add was measured to differ from separately
+// rounded scalar operations in the last bit.
+__device__ __forceinline__ float2 add2_rn(float2 a, float2 b) {
+    float2 r;
+    asm("{\n .reg .b64 ra, rb, rc;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+        " add.rn.f32x2 rc, ra, rb;\n mov.b64 {%0, %1}, rc;\n}"
+        : "=f"(r.x), "=f"(r.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return r;
+}
+
 __device__ __forceinline__ uint32_t key_hi(uint64_t k) { return (uint32_t)(k >> 32); }
 __device__ __forceinline__ uint32_t key_lo(uint64_t k) { return (uint32_t)k; }
 

@@ -354,21 +354,22 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     for (int b = 0; b < kLB; ++b) {
                         const int c = cb0 + b * kCStep;
                         if (c >= 256) break;
-                        // queries (0,1) and (2,3) as packed pairs; x - y is x + (-y) exactly
-                        float2 a01, a23;
+                        // scalar round-to-nearest operations: a packed fp32x2 multiply
+                        // feeding a packed add was measured not to reproduce the
+                        // separately rounded x*x + a of the CPU statement
+                        float acc[kGQ];
 #pragma unroll
-                        for (int u = 0; u < DSUB; ++u) {
-                            const float2 nc = make_float2(-cbv[b][u], -cbv[b][u]);
-                            const float2 x01 = __fadd2_rn(r01[u], nc), x23 = __fadd2_rn(r23[u], nc);
-                            if (u == 0) {
-                                a01 = __fmul2_rn(x01, x01);
-                                a23 = __fmul2_rn(x23, x23);
-                            } else {
-                                a01 = __fadd2_rn(a01, __fmul2_rn(x01, x01));
-                                a23 = __fadd2_rn(a23, __fmul2_rn(x23, x23));
+                        for (int kq = 0; kq < kGQ; ++kq) {
+                            float a = 0.f;
+#pragma unroll
+                            for (int u = 0; u < DSUB; ++u) {
+                                const float r = kq == 0 ? r01[u].x : kq == 1 ? r01[u].y : kq == 2 ? r23[u].x : r23[u].y;
+                                const float x = __fsub_rn(r, cbv[b][u]);
+                                a = u == 0 ? __fmul_rn(x, x) : __fadd_rn(a, __fmul_rn(x, x));
                             }
+                            acc[kq] = a;
                         }
-                        lut[c * M + ps] = make_float4(a01.x, a01.y, a23.x, a23.y);
+                        lut[c * M + ps] = make_float4(acc[0], acc[1], acc[2], acc[3]);
                     }
                     if (cb0 + kLB * kCStep >= 256) break;
                     load_cb(cb0 + kLB * kCStep);

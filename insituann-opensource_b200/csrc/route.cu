@@ -24,11 +24,14 @@ __global__ void centroid_valid_kernel(const float* __restrict__ cent, int nlist,
 }
 
 // 128 queries x 128 centroids per CTA, 256 threads, 8x8 pairs per thread, 16
-// dimensions staged per step.  The centroid tile is staged negated, so
-// q - c is one packed add (x + (-y) is x - y exactly); a thread's pairs are
-// float2 accumulators of two centroids updated with the packed fp32x2
-// instructions (two independent round-to-nearest operations each).  Zero
-// padding beyond d adds exact zeros.
+// dimensions staged per step.  The centroid tile is staged negated, so q - c
+// is an add (x + (-y) is x - y exactly).  A thread's pairs are float2
+// accumulators of two centroids; the subtraction and the accumulation are
+// packed fp32x2 add.rn (PTX), the squares scalar __fmul_rn: a packed multiply
+// feeding a packed add was measured to differ from the separately rounded CPU
+// sums in the last bit, packed adds alone were not.  Packed operations run at
+// the same FP32 lane rate as scalar ones on B200 but take half the issue
+// slots.  Zero padding beyond d adds exact zeros.
 constexpr int kRB = 128, kRK = 16;
 
 __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict__ q, int nq,
@@ -65,11 +68,10 @@ __global__ void __launch_bounds__(256) route_dist_kernel(const float* __restrict
                                  make_float2(b1.z, b1.w)};
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float2 ai = make_float2(a[i], a[i]);
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                    const float2 x = __fadd2_rn(ai, b[j]);
-                    acc[i][j] = __fadd2_rn(acc[i][j], __fmul2_rn(x, x));
+                    const float2 x = add2_rn(make_float2(a[i], a[i]), b[j]);
+                    acc[i][j] = add2_rn(acc[i][j], make_float2(__fmul_rn(x.x, x.x), __fmul_rn(x.y, x.y)));
                 }
             }
         }

@@ -55,6 +55,24 @@ def gpu_pq(p, q, probes, k, R, delta=None, delta_topk=16, f32=False):
     return out
 
 
+def gpu_stage1(p, q, probes, R, f32=False):
+    """stage-1 keys (ADC bits << 32 | position) of every query, sorted, through the shard entry point."""
+    nq, nprobe = probes.shape
+    index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                               base_u8=None if f32 else p["base_u8"], base_f32=p["base_f32"] if f32 else None)
+    b = ib.Batch(nq, q.shape[1], nprobe, 10, len(p["counts"]))
+    b.stage1_prepare(q)
+    b.set_probes(probes)
+    adc = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+    ex = torch.empty((nq, R), dtype=torch.int64, device="cuda")
+    b.pq_search_shard(index, nq, nprobe, R, 0, adc.data_ptr(), ex.data_ptr())
+    b.sync()
+    got = np.sort(adc.cpu().numpy().view(np.uint64), axis=1)
+    b.close()
+    index.close()
+    return got
+
+
 # ---------------------------------------------------------------------------
 # golden fixtures
 # ---------------------------------------------------------------------------
@@ -122,8 +140,16 @@ def test_route_matches_oracle(cuda_ok, pq_medium):
     b.stage1_prepare(q)
     b.route(index, q.shape[0], nprobe)
     got = b.get_probes(q.shape[0], nprobe)
-    exp, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    exp, exp_d = oracle.route_l2(q, p["centroids"], nprobe)
     assert np.array_equal(got, exp)
+    # the routing distances bit for bit (keys = distance bits << 32 | list id)
+    keys = torch.empty((q.shape[0], nprobe), dtype=torch.int64, device="cuda")
+    b.stage1_prepare(q)
+    b.route_keys(index, q.shape[0], nprobe, keys.data_ptr())
+    b.sync()
+    k = keys.cpu().numpy().view(np.uint64)
+    assert np.array_equal((k & np.uint64(0xFFFFFFFF)).astype(np.int32), exp)
+    assert np.array_equal((k >> np.uint64(32)).astype(np.uint32), exp_d.view(np.uint32))
 
 
 @pytest.mark.parametrize("R,k", [(512, 10), (100, 7), (33, 33)])
@@ -132,9 +158,10 @@ def test_pq_medium_routed(cuda_ok, pq_medium, R, k):
     nprobe = 12
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     gi, gd = gpu_pq(p, q, probes, k, R)
-    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
-                              probes, k, rerank_n=R, base_u8=p["base_u8"])
+    oi, od, s1, _ = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                                     q, probes, k, rerank_n=R, base_u8=p["base_u8"], return_stage1=True)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    assert np.array_equal(gpu_stage1(p, q, probes, max(R, k)), np.sort(s1, axis=1))
 
 
 def test_pq_overlay(cuda_ok, pq_medium):
@@ -160,9 +187,10 @@ def test_pq_f32_shapes(cuda_ok, M):
     q = synth.mixture_f32_unit(200, d, 64, 0.05, seed=61, stream_base=1 << 20).numpy()
     probes, _ = oracle.route_l2(q, p["centroids"], 5)
     gi, gd = gpu_pq(p, q, probes, 10, 512, f32=True)
-    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
-                              probes, 10, rerank_n=512, base_f32=p["base_f32"])
+    oi, od, s1, _ = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                                     q, probes, 10, rerank_n=512, base_f32=p["base_f32"], return_stage1=True)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    assert np.array_equal(gpu_stage1(p, q, probes, 512, f32=True), np.sort(s1, axis=1))
 
 
 def test_pq_edge_probes(cuda_ok, pq_medium):
@@ -203,6 +231,26 @@ def test_long_lists_span_many_chunks(cuda_ok):
     gi, gd = gpu_exact(e, qu, probes, 10)
     oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], qu, probes, 10)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+@pytest.mark.parametrize("R", [2048, 700])
+def test_large_candidate_buffers(cuda_ok, R):
+    """long lists and a large rerank_n: with R = 2048 no chunk of the scan ever
+    needs a cut (all its keys pass), so a query's buffer holds whole lists
+    (beyond the 4096 keys the stage-1 selection keeps in registers); with
+    R = 700 chunks are cut to R .. R + R/4 keys."""
+    n, d, nlist, M = 40000, 64, 4, 16
+    base = synth.mixture_u8(n, d, 8, 12.0, seed=43)
+    p = synth.build_pq_index(base, nlist, M, seed=43, kmeans_iters=5, pq_iters=4, train_n=8000)
+    p["base_u8"] = p["base_rr"]
+    q = synth.mixture_u8(24, d, 8, 12.0, seed=43, stream_base=1 << 20).float().numpy()
+    probes, _ = oracle.route_l2(q, p["centroids"], 4)
+    gi, gd = gpu_pq(p, q, probes, 10, R)
+    oi, od, s1, _ = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
+                                     q, probes, 10, rerank_n=R, base_u8=p["base_u8"], return_stage1=True)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    # the stage-1 keys themselves (the shard entry point returns them unmerged)
+    assert np.array_equal(gpu_stage1(p, q, probes, R), np.sort(s1, axis=1))
 
 
 def test_exact_routed_pipeline(cuda_ok):
