@@ -10,6 +10,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <atomic>
 #include <mutex>
@@ -98,6 +99,10 @@ struct IndexCtx {
     int64_t n = 0;
     float* cent = nullptr;
     uint8_t* valid = nullptr;
+    uint16_t* tc_ops = nullptr;  // tensor-core routing operand of the centroids (null: exact kernels only)
+    float* tc_cn = nullptr;      // [nlist] squared centroid norms
+    float* tc_cne = nullptr;     // the same per tile row, +inf for invalid lists and padding
+    float* tc_cnmax = nullptr;   // largest squared norm of a valid centroid
     int M = 0, dsub = 0;
     float* codebook = nullptr;
     float* codebook_t = nullptr;   // [256, M, dsub]
@@ -132,7 +137,7 @@ struct BatchCtx {
     int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
     int res_nq = 0, res_k = 0;
     int probes_nq = 0, probes_np = 0;
-    Grow route_dist, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
+    Grow route_dist, route_rowfb, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
     Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
     std::vector<void*> owned;
     std::string err;
@@ -276,11 +281,34 @@ void build_gring(Segment& s, const int* counts, int nlist, int M, int d) {
     s.data = nullptr;
 }
 
+// tensor-core routing operands of the loaded centroids (when the shape allows)
+void prepare_route_tc(IndexCtx* x, int nlist, int d) {
+    if (!route_tc_usable(d, nlist)) return;
+    x->tc_ops = dalloc<uint16_t>(route_tc_ops_elems(nlist, d), x->owned);
+    x->tc_cn = dalloc<float>((size_t)nlist, x->owned);
+    x->tc_cne = dalloc<float>(route_tc_cne_len(nlist), x->owned);
+    x->tc_cnmax = dalloc<float>(1, x->owned);
+    ck(route_tc_prepare(x->cent, x->valid, nlist, d, x->tc_ops, x->tc_cn, x->tc_cne, x->tc_cnmax, 0),
+       "routing operands");
+}
+
+// Routing kernels (all give the same lists bit for bit): INSITU_ROUTE_TC=0
+// exact CUDA-core kernels only; 1 (default) the fused tensor-core kernel for
+// nprobe <= 8, where it was measured faster, else the exact kernels; 2 the
+// tensor-core kernels for every nprobe (fused up to 32, distance matrix and
+// rescoring above).  Read on every call.
+int route_tc_mode() {
+    const char* v = std::getenv("INSITU_ROUTE_TC");
+    if (!v || !v[0]) return 1;
+    return v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1;
+}
+
 void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
     require(centroids != nullptr, "centroids are required");
     x->cent = dcopy(centroids, (size_t)nlist * d, x->owned);
     x->valid = dalloc<uint8_t>((size_t)nlist, x->owned);
     ck(route_centroid_valid(x->cent, nlist, d, x->valid, 0), "centroid validity");
+    prepare_route_tc(x, nlist, d);
     ck(cudaDeviceSynchronize(), "centroid validity");
     x->nlist = nlist;
     x->nlist_global = nlist;
@@ -308,10 +336,28 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
     uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
     StageScope stage(b, IVF_STAGE_ROUTE);
+    const int mode = x->tc_ops ? route_tc_mode() : 0;
+    const bool tc = mode == 2;
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
-        ck(route_distances(b->q + (size_t)s * x->d, n, x->cent, x->valid, x->nlist, x->d, dist, b->st),
-           "route_distances");
+        const float* qs = b->q + (size_t)s * x->d;
+        if ((mode == 2 || (mode == 1 && nprobe <= 8)) && route_tc_fused_usable(x->d, x->nlist, nprobe)) {
+            int32_t* fb = ensure<int32_t>(b, b->route_rowfb, (size_t)nsub);
+            ck(route_tc_fused(qs, n, x->tc_ops, x->tc_cne, x->tc_cnmax, x->valid, x->nlist, x->d, x->cent, nprobe,
+                              x->l2g, keys ? nullptr : b->probes + (size_t)s * nprobe,
+                              keys ? keys + (size_t)s * nprobe : nullptr, fb, b->overflow, b->st),
+               "route_tc_fused");
+            continue;
+        }
+        if (tc) {
+            ck(route_tc(qs, n, x->tc_ops, x->tc_cn, x->valid, x->nlist, x->d, dist, b->overflow, b->st), "route_tc");
+            ck(route_rescore(dist, qs, n, x->cent, x->tc_cnmax, x->valid, x->nlist, x->d, nprobe, x->l2g,
+                             keys ? nullptr : b->probes + (size_t)s * nprobe, nullptr,
+                             keys ? keys + (size_t)s * nprobe : nullptr, b->st),
+               "route_rescore");
+            continue;
+        }
+        ck(route_distances(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances");
         if (keys) {
             ck(route_select(dist, n, x->nlist, nprobe, x->l2g, nullptr, nullptr, keys + (size_t)s * nprobe, b->st),
                "route_select");
@@ -527,6 +573,7 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
 }
 
 void check_overflow_after_sync(BatchCtx* b) {
+    if (*b->h_overflow & 4) fail(IVF_ECUDA, "a bounded device wait of the tensor-core routing gave up");
     if (*b->h_overflow)
         fail(IVF_EOVERFLOW, "a candidate buffer overflowed; raise INSITU_SCRATCH_MB or lower n_probes");
 }
@@ -639,6 +686,7 @@ int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vector
         x->owned.push_back(d_cluster_centers);
         x->valid = dalloc<uint8_t>((size_t)n_total_clusters, x->owned);
         ck(route_centroid_valid(x->cent, n_total_clusters, n_dim, x->valid, 0), "centroid validity");
+        prepare_route_tc(x, n_total_clusters, n_dim);
         ck(cudaDeviceSynchronize(), "centroid validity");
         x->nlist = x->nlist_global = n_total_clusters;
         x->d = n_dim;
@@ -692,7 +740,8 @@ void ivf_destroy_batch_context(void* batch_ctx) {
     if (b->magic != kBatMagic) return;
     cudaSetDevice(b->device);
     cudaStreamSynchronize(b->st);
-    Grow* gs[] = {&b->route_dist, &b->wl_cnt, &b->wl_off, &b->wl_cursor, &b->pair_q, &b->pair_l, &b->scan_tmp,
+    Grow* gs[] = {&b->route_dist, &b->route_rowfb, &b->wl_cnt, &b->wl_off, &b->wl_cursor, &b->pair_q, &b->pair_l,
+                  &b->scan_tmp,
                   &b->grp_cnt, &b->grp_off, &b->groups,
                   &b->cand_m, &b->cand_d, &b->cnt_m, &b->cnt_d, &b->thr_m, &b->thr_d, &b->s1m, &b->s1d, &b->exk};
     for (Grow* g : gs)

@@ -44,6 +44,32 @@ cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const 
 cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist, int32_t* out_ids,
                        float* out_dist, int32_t* out_idist, cudaStream_t st);
 // out[i] = clamp(round(q[i]), 0, 255) (updates/exact_update.cu:410-418)
+// Tensor-core routing (route_tc.cu): approximate distances from one tcgen05
+// GEMM over bf16 hi/lo splits, then exact rescoring of the candidates within
+// the error bound of the approximation -- the same top-L as route_distances +
+// route_select.  Usable for d % 16 == 0, d <= 144.
+bool route_tc_usable(int d, int nlist);
+int route_tc_tile(int d);
+size_t route_tc_ops_elems(int nlist, int d);     // bf16 elements of the centroid operand
+// cn: [nlist] squared norms; cne: [route_tc_cne_len] the same, +inf for
+// invalid lists and tile padding
+size_t route_tc_cne_len(int nlist);
+cudaError_t route_tc_prepare(const float* cent, const uint8_t* valid, int nlist, int d, uint16_t* ops, float* cn,
+                             float* cne, float* cn_max, cudaStream_t st);
+// approximate distance bits [nq, nlist] (invalid lists 0xFFFFFFFF); flag bit 2
+// is raised when a bounded wait gave up
+cudaError_t route_tc(const float* q, int nq, const uint16_t* ops, const float* cn, const uint8_t* valid, int nlist,
+                     int d, uint32_t* out, int* flag, cudaStream_t st);
+// nprobe <= 32: one fused kernel (one tcgen05 sweep over the split operands,
+// candidates and exact rescoring on chip) plus an exact pass over the rare
+// rows it hands back
+bool route_tc_fused_usable(int d, int nlist, int L);
+cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const float* cne, const float* cn_max,
+                           const uint8_t* valid, int nlist, int d, const float* cent, int L, const int32_t* id_map,
+                           int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, int* flag, cudaStream_t st);
+cudaError_t route_rescore(const uint32_t* approx, const float* q, int nq, const float* cent, const float* cn_max,
+                          const uint8_t* valid, int nlist, int d, int L, const int32_t* id_map, int32_t* out_ids,
+                          float* out_dist, uint64_t* out_keys, cudaStream_t st);
 cudaError_t make_query_u8(const float* q, size_t n, uint8_t* out, cudaStream_t st);
 
 // ---- candidate selection (select.cu) ---------------------------------------

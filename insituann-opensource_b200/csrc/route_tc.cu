@@ -1,0 +1,950 @@
+// route_tc.cu -- coarse routing on the tensor cores (tcgen05) with exact rescoring.
+//
+// The routing result is defined by the exact fp32 direct-difference distance
+// sum_j (q_j - c_j)^2 (route.cu).  This file gets the same top-nprobe lists
+// faster in two steps:
+//
+//  1. route_tc_kernel: an approximate distance of every (query, centroid)
+//     pair, D~ = ||q||^2 + ||c||^2 - 2 q.c, with q.c from one tcgen05 GEMM.
+//     Each fp32 value x is split into bf16 parts hi = bf16(x), lo =
+//     bf16(x - hi); the GEMM runs over K' = 3d with A = [q_hi | q_hi | q_lo]
+//     and B = [c_hi | c_lo | c_hi], i.e. q_hi.c_hi + q_hi.c_lo + q_lo.c_hi,
+//     accumulated in fp32 in tensor memory.  A CTA owns 128 queries (the MMA
+//     M), stages their operand once, streams 64-centroid operand tiles into
+//     shared memory with bulk async copies (two buffers), issues the MMAs
+//     from one thread into two alternating accumulators, and its 4 warps read
+//     each accumulator back (one query row per TMEM lane) and write D~ bits.
+//  2. route_rescore_kernel: per query, the nprobe-th smallest D~ (T~), every
+//     centroid with D~ <= T~ + 2 eps is a candidate, where eps = 2^-11
+//     (||q||^2 + max ||c||^2) bounds |D~ - D| for every centroid (the split
+//     leaves a relative error near 2^-16 in q.c, the fp32 accumulation of 3d
+//     products less than 2^-14; the bound keeps a factor 4 of margin).  The
+//     candidates are rescored with the exact distance and their top-nprobe
+//     by (distance, list id) is the result -- the same set as the exact
+//     routing, because every centroid of the exact top-nprobe has
+//     D~ <= T~ + 2 eps.  A query with more candidates than fit is rescored
+//     over all centroids.
+//
+// Shared-memory operands use the canonical K-major layout without swizzle:
+// 8-row x 16-byte core matrices, the two 8-element halves of one MMA's K = 16
+// 128 bytes apart (LBO), consecutive 8-row groups 256 bytes apart (SBO), and
+// the K blocks of 16 one after another.
+#include <cuda_bf16.h>
+
+#include "launch.h"
+
+namespace isb {
+
+namespace {
+
+constexpr int kTCM = 128;                 // queries per CTA (MMA M)
+constexpr int kTCN = 64;                  // centroids per tile (MMA N)
+constexpr int kTCThreads = 128;           // 4 warps: one TMEM lane (query row) per thread
+constexpr int kTCWaitSpins = 1 << 22;     // bounded mbarrier polls
+constexpr int kPMaxRouteD = 512;          // largest d of the fallback rows
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// byte offset of the 16-byte chunk (row, k8) -- elements k = 8*k8 .. 8*k8+7 --
+// in the canonical layout of an operand of R rows
+__host__ __device__ __forceinline__ size_t tc_chunk_off(int row, int k8, int R) {
+    return (size_t)(k8 >> 1) * ((size_t)R * 32) + (size_t)(row >> 3) * 256 + (size_t)(k8 & 1) * 128 +
+           (size_t)(row & 7) * 16;
+}
+
+__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);          // start address, 16-byte units
+    d |= (uint64_t)(128u >> 4) << 16;                  // leading byte offset: K halves
+    d |= (uint64_t)(256u >> 4) << 32;                  // stride byte offset: 8-row groups
+    d |= (uint64_t)1 << 46;                            // descriptor version of sm_100
+    return d;                                          // base offset 0, no swizzle
+}
+
+// kind::f16 instruction descriptor: bf16 A and B (K-major), fp32 D, M x N
+__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
+    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < kTCWaitSpins; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ uint32_t bf16_bits(__nv_bfloat16 h) { return (uint32_t)__bfloat16_as_ushort(h); }
+
+// the 8 bf16 of chunk k8 of the split row [x_hi | x_hi | x_lo] (hi_lo_hi = false)
+// or [x_hi | x_lo | x_hi] (hi_lo_hi = true) of the fp32 row x[d]; d % 16 == 0,
+// so a chunk never straddles two parts
+__device__ __forceinline__ uint4 split_chunk(const float* x, int d, int k8, bool valid_row, bool hi_lo_hi) {
+    const int k = 8 * k8, part = k / d, j0 = k - part * d;
+    const bool lo = hi_lo_hi ? part == 1 : part == 2;
+    uint32_t w[4];
+#pragma unroll
+    for (int e = 0; e < 8; e += 2) {
+        uint32_t pair = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+            const float v = valid_row ? x[j0 + e + h] : 0.f;
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            const __nv_bfloat16 out = lo ? __float2bfloat16_rn(v - __bfloat162float(hi)) : hi;
+            pair |= bf16_bits(out) << (16 * h);
+        }
+        w[e / 2] = pair;
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// centroid operand tiles [ntiles][64 x 3d] in the canonical layout, split
+// [hi | lo | hi]; squared norms cn, and cne = cn for valid lists, +inf for
+// invalid lists and the padding rows of the last tile
+__global__ void route_tc_prepare_kernel(const float* __restrict__ cent, const uint8_t* __restrict__ valid, int nlist,
+                                        int d, uint16_t* __restrict__ ops, float* __restrict__ cn,
+                                        float* __restrict__ cne) {
+    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t t0 = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+    const int NT = kTCN, K8 = 3 * d / 8;
+    const int ntiles = (nlist + NT - 1) / NT;
+    const size_t tile_bytes = (size_t)NT * 3 * d * 2;
+    for (size_t e = t0; e < (size_t)ntiles * NT * K8; e += stride) {
+        const int t = (int)(e / ((size_t)NT * K8));
+        const int r = (int)((e / K8) % NT), k8 = (int)(e % K8);
+        const int c = t * NT + r;
+        const bool ok = c < nlist && valid[c];
+        const uint4 v = split_chunk(cent + (size_t)(ok ? c : 0) * d, d, k8, ok, true);
+        *reinterpret_cast<uint4*>(reinterpret_cast<unsigned char*>(ops) + (size_t)t * tile_bytes +
+                                  tc_chunk_off(r, k8, NT)) = v;
+    }
+    for (size_t c = t0; c < (size_t)ntiles * NT; c += stride) {
+        float s = __int_as_float(0x7f800000);
+        if (c < (size_t)nlist) {
+            s = 0.f;
+            for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(cent[c * d + j], cent[c * d + j]));
+            cn[c] = s;
+        }
+        cne[c] = c < (size_t)nlist && valid[c] ? s : __int_as_float(0x7f800000);   // +inf: never a candidate
+    }
+}
+
+__global__ void route_tc_cnmax_kernel(const float* __restrict__ cn, const uint8_t* __restrict__ valid, int nlist,
+                                      float* __restrict__ cn_max) {
+    __shared__ float red[256];
+    float m = 0.f;
+    for (int c = threadIdx.x; c < nlist; c += blockDim.x)
+        if (valid[c]) m = fmaxf(m, cn[c]);
+    red[threadIdx.x] = m;
+    __syncthreads();
+    for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+        if (threadIdx.x < s) red[threadIdx.x] = fmaxf(red[threadIdx.x], red[threadIdx.x + s]);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) *cn_max = red[0];
+}
+
+// One CTA: 128 queries x a range of 64-centroid tiles.  Tensor memory holds
+// two 128 x 64 fp32 accumulators: the MMAs of tile t+1 run while the 4 warps
+// read tile t back.  Each warp moves its 32 rows x 32 columns through a
+// padded shared-memory square so that the distance stores are 128-byte rows
+// (one query, 32 consecutive lists per warp store).
+constexpr int kTCStage = 32 * 33;         // floats of one warp's transpose square
+
+__host__ __device__ constexpr size_t route_tc_smem(int d) {
+    return (size_t)kTCM * 3 * d * 2 + 2 * (size_t)kTCN * 3 * d * 2 + sizeof(float) * (4 * kTCStage + kTCM);
+}
+
+__global__ void __launch_bounds__(kTCThreads, 1)
+    route_tc_kernel(const float* __restrict__ q, int nq, int d, const uint16_t* __restrict__ ops,
+                    const float* __restrict__ cn, const uint8_t* __restrict__ valid, int nlist, int tiles_per_cta,
+                    uint32_t* __restrict__ out, int* flag) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    __shared__ __align__(8) uint64_t bar_b[2];
+    __shared__ __align__(8) uint64_t bar_mma[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int K = 3 * d, K8 = K / 8;
+    const uint32_t a_bytes = (uint32_t)kTCM * K * 2, b_bytes = (uint32_t)kTCN * K * 2;
+    unsigned char* sA = sm;
+    unsigned char* sB = sm + a_bytes;                                      // [2][b_bytes]
+    float* stage = reinterpret_cast<float*>(sB + 2 * (size_t)b_bytes);      // [4][32][33]
+    float* s_qn = stage + 4 * kTCStage;                                    // [128]
+    const int q0 = blockIdx.x * kTCM;
+    const int ntiles = (nlist + kTCN - 1) / kTCN;
+    const int t_begin = blockIdx.y * tiles_per_cta;
+    const int t_end = min(ntiles, t_begin + tiles_per_cta);
+    const int n = t_end - t_begin;
+    if (n <= 0) return;                                    // the whole CTA leaves together
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(2 * kTCN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        mbar_init(&bar_b[0], 1);
+        mbar_init(&bar_b[1], 1);
+        mbar_init(&bar_mma[0], 1);
+        mbar_init(&bar_mma[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_fail = 0;
+    }
+    // this thread's query row of A and its squared norm (used by D~ only)
+    const int qi = q0 + tid;
+    const bool qok = qi < nq;
+    const float* qr = q + (size_t)(qok ? qi : 0) * d;
+    float qn = 0.f;
+    if (qok)
+        for (int j = 0; j < d; ++j) qn = __fadd_rn(qn, __fmul_rn(qr[j], qr[j]));
+    s_qn[tid] = qn;
+    for (int k8 = 0; k8 < K8; ++k8)
+        *reinterpret_cast<uint4*>(sA + tc_chunk_off(tid, k8, kTCM)) = split_chunk(qr, d, k8, qok, false);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = s_tmem;
+    const unsigned char* gops = reinterpret_cast<const unsigned char*>(ops);
+    constexpr uint32_t idesc = umma_idesc_bf16(kTCM, kTCN);
+    const uint32_t a_addr = smem_u32(sA);
+    // thread 0: copy tile i of this CTA into buffer i & 1
+    auto copy_tile = [&](int i) {
+        mbar_arrive_expect(&bar_b[i & 1], b_bytes);
+        bulk_g2s(sB + (size_t)(i & 1) * b_bytes, gops + (size_t)(t_begin + i) * b_bytes, b_bytes, &bar_b[i & 1]);
+    };
+    // thread 0: MMAs of tile i into accumulator i & 1; false when its copy did not land
+    auto mma_tile = [&](int i) -> bool {
+        if (!mbar_wait(&bar_b[i & 1], (uint32_t)((i >> 1) & 1))) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t b_addr = smem_u32(sB + (size_t)(i & 1) * b_bytes);
+        const uint32_t dacc = tmem + (uint32_t)((i & 1) * kTCN);
+        for (int kb = 0; kb < K / 16; ++kb) {
+            const uint64_t ad = umma_smem_desc(a_addr + (uint32_t)kb * (kTCM * 32));
+            const uint64_t bd = umma_smem_desc(b_addr + (uint32_t)kb * (kTCN * 32));
+            const uint32_t acc = kb > 0 ? 1u : 0u;
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(dacc),
+                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+                : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&bar_mma[i & 1]))
+                     : "memory");
+        return true;
+    };
+    if (tid == 0) {
+        copy_tile(0);
+        if (n > 1) copy_tile(1);
+        if (!mma_tile(0)) s_fail = 1;
+    }
+    float* st = stage + warp * kTCStage;
+    int it = 0;
+    for (; it < n; ++it) {
+        // the next tile's MMAs go to the other accumulator while this one is read
+        if (tid == 0 && it + 1 < n && !s_fail && !mma_tile(it + 1)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) break;
+        const bool done = mbar_wait(&bar_mma[it & 1], (uint32_t)((it >> 1) & 1));
+        if (__syncthreads_or(!done)) {
+            if (tid == 0) s_fail = 1;
+            break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        // tile it's MMAs are complete: its buffer takes tile it + 2
+        if (tid == 0 && it + 2 < n) copy_tile(it + 2);
+        const int cbase = (t_begin + it) * kTCN;
+        const uint32_t tacc = tmem + (uint32_t)((it & 1) * kTCN) + ((uint32_t)(warp * 32) << 16);
+        for (int c0 = 0; c0 < kTCN; c0 += 32) {
+            uint32_t r[32];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                "%13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, "
+                "[%32];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                  "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                  "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                  "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                  "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                : "r"(tacc + (uint32_t)c0)
+                : "memory");
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            // row = this lane's query, column j: st[lane][j]; read back transposed
+#pragma unroll
+            for (int j = 0; j < 32; ++j) st[lane * 33 + j] = __uint_as_float(r[j]);
+            __syncwarp();
+            const int c = cbase + c0 + lane;
+            const bool cok = c < nlist;
+            const float cnc = cok ? __ldg(cn + c) : 0.f;
+            const bool vc = cok && __ldg(valid + c);
+#pragma unroll 4
+            for (int j = 0; j < 32; ++j) {
+                const int row = warp * 32 + j, qj = q0 + row;
+                if (cok && qj < nq) {
+                    const float dt = fmaxf(s_qn[row] + cnc - 2.f * st[j * 33 + lane], 0.f);
+                    out[(size_t)qj * nlist + c] = vc ? __float_as_uint(dt) : 0xFFFFFFFFu;
+                }
+            }
+            __syncwarp();
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();                      // accumulator it & 1 read before tile it + 2's MMAs reuse it
+    }
+    if (s_fail) {
+        // a wait gave up: report it, give copies and MMAs in flight a last
+        // bounded chance to land, then release the tensor memory
+        if (tid == 0) {
+            atomicOr(flag, 4);
+            for (int b = 0; b < 2; ++b) {
+                mbar_wait(&bar_mma[b], 0);
+                mbar_wait(&bar_b[b], 0);
+            }
+        }
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTCN)
+                     : "memory");
+}
+
+constexpr int kRsT = 256;                 // threads of the rescoring CTA
+constexpr int kRsItems = 16;              // approximate keys per thread in registers
+constexpr int kRsCap = 2048;              // candidates rescored from shared memory
+
+__device__ __forceinline__ float exact_route_dist(const float* __restrict__ sq, const float* __restrict__ c, int d) {
+    float s = 0.f;
+    for (int j = 0; j < d; ++j) {
+        const float x = __fsub_rn(sq[j], __ldg(c + j));
+        s = __fadd_rn(s, __fmul_rn(x, x));
+    }
+    return s;
+}
+
+// one CTA per query: candidates from the approximate distances, exact
+// rescoring, top-L by (exact distance, list id)
+__global__ void __launch_bounds__(kRsT) route_rescore_kernel(const uint32_t* __restrict__ approx,
+                                                             const float* __restrict__ q, const float* __restrict__ cent,
+                                                             const float* __restrict__ cn_max,
+                                                             const uint8_t* __restrict__ valid, int nlist, int d, int L,
+                                                             const int32_t* __restrict__ id_map, int32_t* out_ids,
+                                                             float* out_dist, uint64_t* out_keys) {
+    extern __shared__ __align__(16) unsigned char rs_sm[];
+    float* sq = reinterpret_cast<float*>(rs_sm);                                    // [d]
+    uint64_t* ck = reinterpret_cast<uint64_t*>(rs_sm + sizeof(float) * ((d + 3) & ~3));  // [kRsCap]
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ unsigned long long mm[64];
+    __shared__ int s_cnt;
+    __shared__ float s_qn;
+    const int row = blockIdx.x, tid = threadIdx.x;
+    const uint32_t* ar = approx + (size_t)row * nlist;
+    for (int j = tid; j < d; j += kRsT) sq[j] = q[(size_t)row * d + j];
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    if (tid == 0) {
+        float s = 0.f;
+        for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(sq[j], sq[j]));
+        s_qn = s;
+    }
+    // T~: the L-th smallest approximate key (bits << 32 | local list), or for
+    // L <= 32 an upper bound of it: the smallest over the warps of each warp's
+    // L-th smallest value (that warp alone has L values at or below it)
+    uint64_t tkey;
+    if (L <= 32 && nlist <= kRsT * kRsItems) {
+        float v[kRsItems];
+#pragma unroll
+        for (int e = 0; e < kRsItems; ++e) {
+            const int i = tid + kRsT * e;
+            const uint32_t a = i < nlist ? ar[i] : 0xFFFFFFFFu;
+            v[e] = a != 0xFFFFFFFFu ? __uint_as_float(a) : __int_as_float(0x7f800000);
+        }
+        // sort the lane's values (bitonic network on registers)
+#pragma unroll
+        for (int size = 2; size <= kRsItems; size <<= 1)
+#pragma unroll
+            for (int stride = size >> 1; stride > 0; stride >>= 1)
+#pragma unroll
+                for (int i = 0; i < kRsItems; ++i) {
+                    const int jx = i ^ stride;
+                    if (jx > i) {
+                        const bool up = (i & size) == 0;
+                        const float a = v[i], b = v[jx];
+                        if ((a > b) == up) {
+                            v[i] = b;
+                            v[jx] = a;
+                        }
+                    }
+                }
+        // L rounds of the warp minimum over the lanes' heads
+        float lth = __int_as_float(0x7f800000);
+        for (int r = 0; r < L; ++r) {
+            float m = v[0];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) m = fminf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const unsigned who = __ballot_sync(0xffffffffu, v[0] == m);
+            if ((int)(tid & 31) == __ffs(who) - 1) {
+#pragma unroll
+                for (int e = 0; e + 1 < kRsItems; ++e) v[e] = v[e + 1];
+                v[kRsItems - 1] = __int_as_float(0x7f800000);
+            }
+            lth = m;
+        }
+        if (tid == 0) s_cnt = 0x7f800000;
+        __syncthreads();
+        if ((tid & 31) == 0) atomicMin(&s_cnt, (int)__float_as_uint(lth));   // non-negative: bits order as values
+        __syncthreads();
+        const uint32_t tb = (uint32_t)s_cnt;
+        tkey = tb >= 0x7f800000u ? kKeyNone - 1 : ((uint64_t)tb << 32);
+        __syncthreads();
+        if (tid == 0) s_cnt = 0;
+    } else if (nlist <= kRsT * kRsItems) {
+        uint64_t v[kRsItems];
+#pragma unroll
+        for (int e = 0; e < kRsItems; ++e) {
+            const int i = tid + kRsT * e;
+            v[e] = i < nlist ? make_key(ar[i], (uint32_t)i) : kKeyNone;
+        }
+        tkey = nlist > L ? block_kth_items<kRsT, kRsItems>([&](int e) { return v[e]; }, L, kKeyNone - 1, hist, bc, mm)
+                         : kKeyNone - 1;
+    } else {
+        tkey = block_kth_key<kRsT>([&](int i) -> uint64_t { return make_key(ar[i], (uint32_t)i); }, nlist, L,
+                                   kKeyNone - 1, hist, bc);
+    }
+    __syncthreads();
+    const uint32_t thi = key_hi(tkey);
+    // every list whose approximate distance is within 2 eps of T~ (all valid
+    // lists when fewer than L have a distance)
+    const float eps = ldexpf(s_qn + *cn_max, -11);
+    const float lim = thi == 0xFFFFFFFFu ? __int_as_float(0x7f800000) : __uint_as_float(thi) + 2.f * eps;
+    for (int i = tid; i < nlist; i += kRsT) {
+        const uint32_t a = ar[i];
+        if (a != 0xFFFFFFFFu && __uint_as_float(a) <= lim) {
+            const int at = atomicAdd(&s_cnt, 1);
+            if (at < kRsCap) ck[at] = (uint64_t)i;
+        }
+    }
+    __syncthreads();
+    const int ncand = s_cnt;
+    int Lp = 1;
+    while (Lp < L) Lp <<= 1;
+    if (ncand <= kRsCap) {
+        int np = 1;
+        while (np < ncand) np <<= 1;
+        if (np < Lp) np = Lp;
+        for (int i = tid; i < np; i += kRsT) {     // each thread rewrites only its own entries
+            uint64_t key = kKeyNone;
+            if (i < ncand) {
+                const int c = (int)ck[i];
+                const float dd = exact_route_dist(sq, cent + (size_t)c * d, d);
+                key = make_key(__float_as_uint(dd), id_map ? (uint32_t)id_map[c] : (uint32_t)c);
+            }
+            ck[i] = key;
+        }
+        __syncthreads();
+        block_bitonic_sort<kRsT>(ck, np);
+    } else {
+        // too many near-ties: rescore every valid list
+        auto keyf = [&](int i) -> uint64_t {
+            if (!valid[i]) return kKeyNone;
+            const float dd = exact_route_dist(sq, cent + (size_t)i * d, d);
+            return make_key(__float_as_uint(dd), id_map ? (uint32_t)id_map[i] : (uint32_t)i);
+        };
+        const uint64_t kap = block_kth_key<kRsT>(keyf, nlist, L, kKeyNone - 1, hist, bc);
+        if (tid == 0) s_cnt = 0;
+        __syncthreads();
+        for (int i = tid; i < nlist; i += kRsT) {
+            const uint64_t k = keyf(i);
+            if (k < kap) ck[atomicAdd(&s_cnt, 1)] = k;
+        }
+        __syncthreads();
+        const int cl = s_cnt;
+        for (int i = cl + tid; i < Lp; i += kRsT) ck[i] = i < L ? kap : kKeyNone;
+        block_bitonic_sort<kRsT>(ck, Lp);
+    }
+    for (int i = tid; i < L; i += kRsT) {
+        const uint64_t k = ck[i];
+        const bool ok = k != kKeyNone && key_hi(k) != 0xFFFFFFFFu;
+        if (out_ids) out_ids[(size_t)row * L + i] = ok ? (int32_t)key_lo(k) : -1;
+        if (out_dist) out_dist[(size_t)row * L + i] = ok ? __uint_as_float(key_hi(k)) : __int_as_float(0x7f800000);
+        if (out_keys) out_keys[(size_t)row * L + i] = k;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Fused routing for nprobe <= 32: one sweep, no distance matrix leaves the SM.
+// ---------------------------------------------------------------------------
+// The split operands of route_tc_kernel (K = 3d, 64-centroid tiles), so the
+// same eps = 2^-11 (|q|^2 + max |c|^2) bounds |D~ - D|.  8 warps; TMEM lane
+// quarter w % 4 holds rows 32 (w % 4) .. +31 and warp w reads columns
+// 32 (w / 4) .. +31 of every 64-column tile, so each row is shared by two
+// threads ("halves").  While the tiles stream by, each thread keeps
+//   * lv: the L smallest D~ it has seen (ascending), lmax = lv[L-1];
+//   * a list of (D~, list) with D~ <= lmax + 2 eps at the time it was seen,
+//     pruned to the current bound whenever it fills up (a prune that frees
+//     less than a quarter gives up on the row).
+// lmax only decreases and each half's lmax is at least the row's final L-th
+// smallest D~ (T~), so every list with D~ <= T~ + 2 eps -- a superset of the
+// exact top-L -- is in one of the two lists.  The candidates are rescored
+// exactly, the two halves' keys merged and the row's top-L written; a row
+// whose list overflowed is handed to route_exact_rows_kernel.
+constexpr int kFT = 256;                  // threads
+constexpr int kFLMax = 32;                // largest L of the fused path
+constexpr int kFN = kTCN;                 // centroids per tile (MMA N)
+constexpr int kFList = 48;                // candidate slots per (row, half)
+constexpr int kFStages = 2;               // operand tiles in flight
+
+// the tile region holds the operand tiles, then the L-lists, then the exact keys
+__host__ __device__ constexpr size_t route_fused_region(int d) {
+    const size_t tiles = kFStages * (size_t)kFN * 3 * d * 2;
+    const size_t keys = sizeof(uint64_t) * kFT * (kFList / 2), lists = sizeof(float) * 2 * kTCM * kFLMax;
+    const size_t m = keys > lists ? keys : lists;
+    return tiles > m ? tiles : m;
+}
+
+__host__ __device__ constexpr size_t route_fused_smem(int d) {
+    return (size_t)kTCM * 3 * d * 2 + route_fused_region(d) +                // A, tile region
+           (sizeof(float) + sizeof(uint16_t)) * kFT * kFList +                // candidate lists
+           sizeof(float) * 2 * kTCM + sizeof(int) * kFT;                      // qn, T~, counts
+}
+
+template <int LMAX>
+__global__ void __launch_bounds__(kFT, 1)
+    route_tc_fused_kernel(const float* __restrict__ q, int nq, int d, const uint16_t* __restrict__ ops,
+                          const float* __restrict__ cne, const float* __restrict__ cn_max,
+                          const uint8_t* __restrict__ valid, int nlist, const float* __restrict__ cent, int L,
+                          const int32_t* __restrict__ id_map, int32_t* out_ids, uint64_t* out_keys,
+                          int32_t* __restrict__ row_fallback, int* flag) {
+    extern __shared__ __align__(1024) unsigned char sm[];
+    __shared__ __align__(8) uint64_t bar_b[kFStages];
+    __shared__ __align__(8) uint64_t bar_mma[2];
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_fail;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int quarter = warp & 3, half = warp >> 2;
+    const int row = quarter * 32 + lane;                  // TMEM lane = query row of this thread
+    const int K = 3 * d, K8 = K / 8;
+    const uint32_t a_bytes = (uint32_t)kTCM * K * 2, b_bytes = (uint32_t)kFN * K * 2;
+    unsigned char* sA = sm;
+    unsigned char* sB = sm + a_bytes;                          // tiles [kFStages][b_bytes], later s_lv, s_key
+    float* s_lv = reinterpret_cast<float*>(sB);                                   // [2][128][kFLMax]
+    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [kFT][kFList / 2]
+    float* s_lval = reinterpret_cast<float*>(sB + route_fused_region(d));         // [kFT][kFList]
+    uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * kFList);        // [kFT][kFList]
+    float* s_qn = reinterpret_cast<float*>(s_lcol + kFT * kFList);                // [128]
+    float* s_T = s_qn + kTCM;                                                     // [128]
+    int* s_nc = reinterpret_cast<int*>(s_T + kTCM);                               // [kFT]
+    const int q0 = blockIdx.x * kTCM;
+    const int ntiles = (nlist + kFN - 1) / kFN;
+    const float INF = __int_as_float(0x7f800000);
+
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(2 * kFN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    if (tid == 0) {
+        for (int b = 0; b < kFStages; ++b) mbar_init(&bar_b[b], 1);
+        mbar_init(&bar_mma[0], 1);
+        mbar_init(&bar_mma[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        s_fail = 0;
+    }
+    // A operand [q_hi | q_hi | q_lo]: thread t builds row t % 128, chunks of its half
+    {
+        const int r = tid & (kTCM - 1), qi = q0 + r;
+        const bool qok = qi < nq;
+        const float* qr = q + (size_t)(qok ? qi : 0) * d;
+        for (int k8 = tid >> 7; k8 < K8; k8 += kFT / kTCM)
+            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, k8, kTCM)) = split_chunk(qr, d, k8, qok, false);
+        if (tid < kTCM) {
+            float qn = 0.f;
+            if (qok)
+                for (int j = 0; j < d; ++j) qn = __fadd_rn(qn, __fmul_rn(qr[j], qr[j]));
+            s_qn[tid] = qn;
+        }
+    }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    const uint32_t tmem = s_tmem;
+    const unsigned char* gops = reinterpret_cast<const unsigned char*>(ops);
+    constexpr uint32_t idesc = umma_idesc_bf16(kTCM, kFN);
+    const uint32_t a_addr = smem_u32(sA);
+    const float qn = s_qn[row];
+    const float eps2 = 2.f * ldexpf(qn + *cn_max, -11);
+    auto copy_tile = [&](int g) {
+        const int b = g % kFStages;
+        mbar_arrive_expect(&bar_b[b], b_bytes);
+        bulk_g2s(sB + (size_t)b * b_bytes, gops + (size_t)g * b_bytes, b_bytes, &bar_b[b]);
+    };
+    auto mma_tile = [&](int g) -> bool {
+        const int b = g % kFStages;
+        if (!mbar_wait(&bar_b[b], (uint32_t)((g / kFStages) & 1))) return false;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        const uint32_t b_addr = smem_u32(sB + (size_t)b * b_bytes);
+        const uint32_t dacc = tmem + (uint32_t)((g & 1) * kFN);
+        for (int kb = 0; kb < K / 16; ++kb) {
+            const uint64_t ad = umma_smem_desc(a_addr + (uint32_t)kb * (kTCM * 32));
+            const uint64_t bd = umma_smem_desc(b_addr + (uint32_t)kb * (kFN * 32));
+            const uint32_t acc = kb > 0 ? 1u : 0u;
+            asm volatile(
+                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(dacc),
+                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+                : "memory");
+        }
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(&bar_mma[g & 1]))
+                     : "memory");
+        return true;
+    };
+    if (tid == 0) {
+        for (int i = 0; i < kFStages && i < ntiles; ++i) copy_tile(i);
+        if (!mma_tile(0)) s_fail = 1;
+    }
+    float lv[LMAX];
+#pragma unroll
+    for (int i = 0; i < LMAX; ++i) lv[i] = INF;
+    float lmax = INF, lim = INF;           // lim = lmax + 2 eps1
+    int nc = 0;                            // entries in this thread's list
+    bool over = false;                     // the list overflowed within the bound
+    float* myval = s_lval + tid * kFList;
+    uint16_t* mycol = s_lcol + tid * kFList;
+    int g = 0;
+    for (; g < ntiles; ++g) {
+        if (tid == 0 && g + 1 < ntiles && !s_fail && !mma_tile(g + 1)) s_fail = 1;
+        __syncthreads();
+        if (s_fail) break;
+        const bool done = mbar_wait(&bar_mma[g & 1], (uint32_t)((g >> 1) & 1));
+        if (__syncthreads_or(!done)) {
+            if (tid == 0) s_fail = 1;
+            break;
+        }
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (tid == 0 && g + kFStages < ntiles) copy_tile(g + kFStages);   // step g's buffer is free
+        {
+            const int col0 = half * 32;                      // columns of this thread within the tile
+            uint32_t r[32];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+                "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+                "%30, %31}, [%32];"
+                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+                  "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+                  "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+                  "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+                  "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+                : "r"(tmem + (uint32_t)((g & 1) * kFN + col0) + ((uint32_t)(quarter * 32) << 16))
+                : "memory");
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+            const int cb = g * kFN + col0;
+            const float cnl = __ldg(cne + cb + lane);       // lane j: squared norm of column cb + j
+            float x[32];
+            bool any = false;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                x[j] = fmaxf(qn + __shfl_sync(0xffffffffu, cnl, j) - 2.f * __uint_as_float(r[j]), 0.f);
+                any |= x[j] <= lim;
+            }
+            if (any) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (x[j] > lim) continue;
+                    if (over) continue;
+                    if (nc == kFList) {        // full: keep only what is still within the bound
+                        int k2 = 0;
+                        for (int i = 0; i < kFList; ++i)
+                            if (myval[i] <= lim) {
+                                myval[k2] = myval[i];
+                                mycol[k2] = mycol[i];
+                                ++k2;
+                            }
+                        nc = k2;
+                        if (nc > kFList - kFList / 4) {   // the bound no longer thins the list: give up
+                            over = true;
+                            continue;
+                        }
+                    }
+                    myval[nc] = x[j];
+                    mycol[nc] = (uint16_t)(cb + j);
+                    ++nc;
+                    if (x[j] < lmax) {
+                        float v = x[j];
+#pragma unroll
+                        for (int i = 0; i < LMAX; ++i) {
+                            const float a = lv[i];
+                            lv[i] = fminf(a, v);
+                            v = fmaxf(a, v);
+                        }
+#pragma unroll
+                        for (int i = 0; i < LMAX; ++i)
+                            if (i == L - 1) lmax = lv[i];
+                        lim = lmax + eps2;
+                    }
+                }
+            }
+        }
+        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+        __syncthreads();                      // accumulator g & 1 read before step g + 2's MMAs reuse it
+    }
+    const bool failed = s_fail != 0;
+    if (failed && tid == 0) {
+        atomicOr(flag, 4);
+        for (int b = 0; b < 2; ++b) mbar_wait(&bar_mma[b], 0);
+        for (int b = 0; b < kFStages; ++b) mbar_wait(&bar_b[b], 0);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kFN)
+                     : "memory");
+    // T~ of the row: L-th smallest of the two halves' L smallest
+    {
+        float* mine = s_lv + (half * kTCM + row) * kFLMax;
+#pragma unroll
+        for (int i = 0; i < kFLMax; ++i) mine[i] = i < LMAX ? lv[i < LMAX ? i : 0] : INF;
+    }
+    __syncthreads();
+    if (half == 0) {
+        const float* la = s_lv + row * kFLMax;
+        const float* lb = s_lv + (kTCM + row) * kFLMax;
+        float T = INF;
+        for (int i = 0; i < 2 * L; ++i) {
+            const float xv = i < L ? la[i] : lb[i - L];
+            int below = 0, eq_before = 0;
+            for (int k2 = 0; k2 < 2 * L; ++k2) {
+                const float y = k2 < L ? la[k2] : lb[k2 - L];
+                below += y < xv;
+                eq_before += (y == xv && k2 < i);
+            }
+            if (below + eq_before == L - 1) T = xv;
+        }
+        s_T[row] = T;
+    }
+    __syncthreads();
+    // this thread's candidates: list entries within T~ + 2 eps1, rescored exactly
+    const float T = s_T[row];
+    const float climit = T + eps2;
+    const int qi = q0 + row;
+    int nk = 0;
+    bool big = over || T == INF;
+    if (qi < nq && !failed && !big) {
+        const float4* qr = reinterpret_cast<const float4*>(q + (size_t)qi * d);
+        for (int i = 0; i < nc; ++i) {
+            if (myval[i] > climit) continue;
+            if (nk == kFList / 2) {
+                big = true;
+                break;
+            }
+            const int c = mycol[i];
+            const float4* cr = reinterpret_cast<const float4*>(cent + (size_t)c * d);
+            float sdist = 0.f;
+#pragma unroll 4
+            for (int j = 0; j < d / 4; ++j) {
+                const float4 a = __ldg(qr + j), b = __ldg(cr + j);
+                const float x0 = __fsub_rn(a.x, b.x), x1 = __fsub_rn(a.y, b.y);
+                const float x2 = __fsub_rn(a.z, b.z), x3 = __fsub_rn(a.w, b.w);
+                sdist = __fadd_rn(sdist, __fmul_rn(x0, x0));
+                sdist = __fadd_rn(sdist, __fmul_rn(x1, x1));
+                sdist = __fadd_rn(sdist, __fmul_rn(x2, x2));
+                sdist = __fadd_rn(sdist, __fmul_rn(x3, x3));
+            }
+            s_key[tid * (kFList / 2) + nk] =
+                make_key(__float_as_uint(sdist), id_map ? (uint32_t)id_map[c] : (uint32_t)c);
+            ++nk;
+        }
+    }
+    s_nc[tid] = big ? -1 : nk;
+    __syncthreads();
+    if (half == 0 && qi < nq) {
+        const int na = s_nc[tid], nb = s_nc[tid + kTCM];
+        const bool fall = failed || na < 0 || nb < 0;
+        row_fallback[qi] = fall ? 1 : 0;
+        if (!fall) {
+            // top-L of the row's candidate keys: repeated minimum over the two lists
+            const uint64_t* ka = s_key + tid * (kFList / 2);
+            const uint64_t* kb = s_key + (tid + kTCM) * (kFList / 2);
+            uint64_t last = 0;
+            for (int o = 0; o < L; ++o) {
+                uint64_t best = kKeyNone;
+                for (int i = 0; i < na; ++i)
+                    if ((o == 0 || ka[i] > last) && ka[i] < best) best = ka[i];
+                for (int i = 0; i < nb; ++i)
+                    if ((o == 0 || kb[i] > last) && kb[i] < best) best = kb[i];
+                const bool ok = best != kKeyNone;
+                if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(best) : -1;
+                if (out_keys) out_keys[(size_t)qi * L + o] = best;
+                last = best;
+            }
+        }
+    }
+}
+
+// Rows the fused kernel marked: exact distances to every list, top-L.
+__global__ void __launch_bounds__(kRsT) route_exact_rows_kernel(const int32_t* __restrict__ row_fallback,
+                                                                const float* __restrict__ q,
+                                                                const float* __restrict__ cent,
+                                                                const uint8_t* __restrict__ valid, int nlist, int d,
+                                                                int L, const int32_t* __restrict__ id_map,
+                                                                int32_t* out_ids, uint64_t* out_keys) {
+    const int row = blockIdx.x, tid = threadIdx.x;
+    if (!row_fallback[row]) return;
+    __shared__ float sq[kPMaxRouteD];
+    __shared__ uint64_t sk[64];
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ int s_cnt;
+    for (int j = tid; j < d; j += kRsT) sq[j] = q[(size_t)row * d + j];
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    auto keyf = [&](int i) -> uint64_t {
+        if (!valid[i]) return kKeyNone;
+        const float dd = exact_route_dist(sq, cent + (size_t)i * d, d);
+        return make_key(__float_as_uint(dd), id_map ? (uint32_t)id_map[i] : (uint32_t)i);
+    };
+    int nvalid = 0;
+    for (int i = tid; i < nlist; i += kRsT) nvalid += valid[i] ? 1 : 0;
+    nvalid = block_sum<kRsT>(nvalid, hist);
+    const int take = nvalid < L ? nvalid : L;
+    uint64_t kap = kKeyNone;
+    if (take > 0) kap = block_kth_key<kRsT>(keyf, nlist, take, kKeyNone - 1, hist, bc);
+    __syncthreads();
+    for (int i = tid; i < nlist; i += kRsT) {
+        const uint64_t k = keyf(i);
+        if (k < kap) sk[atomicAdd(&s_cnt, 1)] = k;
+    }
+    __syncthreads();
+    const int cl = s_cnt;
+    for (int i = cl + tid; i < 64; i += kRsT) sk[i] = i < take ? kap : kKeyNone;
+    block_bitonic_sort<kRsT>(sk, 64);
+    for (int i = tid; i < L; i += kRsT) {
+        const uint64_t k = sk[i];
+        const bool ok = k != kKeyNone;
+        if (out_ids) out_ids[(size_t)row * L + i] = ok ? (int32_t)key_lo(k) : -1;
+        if (out_keys) out_keys[(size_t)row * L + i] = k;
+    }
+}
+
+}  // namespace
+
+bool route_tc_usable(int d, int nlist) {
+    return d > 0 && d % 16 == 0 && nlist > 0 && route_tc_smem(d) <= 227 * 1024;
+}
+
+int route_tc_tile(int) { return kTCN; }
+
+size_t route_tc_ops_elems(int nlist, int d) { return (size_t)((nlist + kTCN - 1) / kTCN) * kTCN * 3 * d; }
+
+size_t route_tc_cne_len(int nlist) { return (size_t)((nlist + kTCN - 1) / kTCN) * kTCN; }
+
+cudaError_t route_tc_prepare(const float* cent, const uint8_t* valid, int nlist, int d, uint16_t* ops, float* cn,
+                             float* cne, float* cn_max, cudaStream_t st) {
+    if (!route_tc_usable(d, nlist)) return cudaErrorInvalidValue;
+    note_launch();
+    route_tc_prepare_kernel<<<512, 256, 0, st>>>(cent, valid, nlist, d, ops, cn, cne);
+    cudaError_t e = cudaGetLastError();
+    if (e) return e;
+    note_launch();
+    route_tc_cnmax_kernel<<<1, 256, 0, st>>>(cn, valid, nlist, cn_max);
+    return cudaGetLastError();
+}
+
+cudaError_t route_tc(const float* q, int nq, const uint16_t* ops, const float* cn, const uint8_t* valid, int nlist,
+                     int d, uint32_t* out, int* flag, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    if (!route_tc_usable(d, nlist)) return cudaErrorInvalidValue;
+    const size_t smem = route_tc_smem(d);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int gx = (nq + kTCM - 1) / kTCM, ntiles = (nlist + kTCN - 1) / kTCN;
+    int gy = sms / gx;
+    if (gy < 1) gy = 1;
+    if (gy > ntiles) gy = ntiles;
+    const int per = (ntiles + gy - 1) / gy;
+    gy = (ntiles + per - 1) / per;
+    cudaError_t e = cudaFuncSetAttribute(route_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    note_launch();
+    route_tc_kernel<<<dim3(gx, gy), kTCThreads, smem, st>>>(q, nq, d, ops, cn, valid, nlist, per, out, flag);
+    return cudaGetLastError();
+}
+
+bool route_tc_fused_usable(int d, int nlist, int L) {
+    return route_tc_usable(d, nlist) && nlist <= 65536 && L >= 1 && L <= kFLMax && d <= kPMaxRouteD &&
+           route_fused_smem(d) <= 227 * 1024;
+}
+
+cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const float* cne, const float* cn_max,
+                           const uint8_t* valid, int nlist, int d, const float* cent, int L, const int32_t* id_map,
+                           int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, int* flag, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    if (!route_tc_fused_usable(d, nlist, L)) return cudaErrorInvalidValue;
+    const size_t smem = route_fused_smem(d);
+    cudaError_t e = cudaSuccess;
+    note_launch();
+    const int grid = (nq + kTCM - 1) / kTCM;
+#define ISB_FUSED(LM)                                                                                            \
+    {                                                                                                            \
+        e = cudaFuncSetAttribute(route_tc_fused_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+                                 (int)smem);                                                                     \
+        if (e) return e;                                                                                         \
+        route_tc_fused_kernel<LM><<<grid, kFT, smem, st>>>(q, nq, d, ops, cne, cn_max, valid, nlist, cent, L,    \
+                                                            id_map, out_ids, out_keys, row_fallback, flag);      \
+    }
+    if (L <= 8) ISB_FUSED(8) else if (L <= 16) ISB_FUSED(16) else ISB_FUSED(32)
+#undef ISB_FUSED
+    if ((e = cudaGetLastError())) return e;
+    note_launch();
+    route_exact_rows_kernel<<<nq, kRsT, 0, st>>>(row_fallback, q, cent, valid, nlist, d, L, id_map, out_ids,
+                                                 out_keys);
+    return cudaGetLastError();
+}
+
+cudaError_t route_rescore(const uint32_t* approx, const float* q, int nq, const float* cent, const float* cn_max,
+                          const uint8_t* valid, int nlist, int d, int L, const int32_t* id_map, int32_t* out_ids,
+                          float* out_dist, uint64_t* out_keys, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    if (L <= 0 || L > kRsCap) return cudaErrorInvalidValue;
+    const size_t smem = sizeof(float) * ((d + 3) & ~3) + sizeof(uint64_t) * kRsCap;
+    cudaError_t e = cudaFuncSetAttribute(route_rescore_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    note_launch();
+    route_rescore_kernel<<<nq, kRsT, smem, st>>>(approx, q, cent, cn_max, valid, nlist, d, L, id_map, out_ids,
+                                                  out_dist, out_keys);
+    return cudaGetLastError();
+}
+
+}  // namespace isb

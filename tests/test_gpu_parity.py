@@ -152,6 +152,34 @@ def test_route_matches_oracle(cuda_ok, pq_medium):
     assert np.array_equal((k >> np.uint64(32)).astype(np.uint32), exp_d.view(np.uint32))
 
 
+@pytest.mark.parametrize("mode,nprobe", [("0", 8), ("1", 8), ("2", 8), ("2", 12), ("2", 32), ("2", 40)])
+def test_route_kernels_bit_identical(cuda_ok, mode, nprobe, monkeypatch):
+    """every routing kernel (exact CUDA-core, fused tensor-core, tensor-core
+    matrix + rescoring) gives the oracle's lists and distance bits; d = 96
+    and d = 128 shapes (the fused kernel covers d = 96 only)"""
+    monkeypatch.setenv("INSITU_ROUTE_TC", mode)
+    for d, nlist, seed in ((96, 300, 71), (128, 200, 72)):
+        cent = synth.mixture_f32_unit(nlist, d, 40, 0.05, seed=seed).numpy()
+        cent[7] = cent[3]                      # identical centroids: a distance tie broken by id
+        cent[11] = 0.0                         # zero norm: never routed
+        q = synth.mixture_f32_unit(333, d, 40, 0.05, seed=seed, stream_base=1 << 20).numpy()
+        exp, exp_d = oracle.route_l2(q, cent, nprobe)
+        counts = np.full(nlist, 1, np.int32)
+        offsets = np.arange(nlist, dtype=np.int64)
+        rows = np.zeros((nlist, d), np.uint8)
+        index = ib.Index().load_u8(rows, offsets, counts, np.arange(nlist, dtype=np.int32), cent)
+        b = ib.Batch(q.shape[0], d, nprobe, 10, nlist)
+        b.stage1_prepare(q)
+        keys = torch.empty((q.shape[0], nprobe), dtype=torch.int64, device="cuda")
+        b.route_keys(index, q.shape[0], nprobe, keys.data_ptr())
+        b.sync()
+        k = keys.cpu().numpy().view(np.uint64)
+        b.close()
+        index.close()
+        assert np.array_equal((k & np.uint64(0xFFFFFFFF)).astype(np.int32), exp)
+        assert np.array_equal((k >> np.uint64(32)).astype(np.uint32), exp_d.view(np.uint32))
+
+
 @pytest.mark.parametrize("R,k", [(512, 10), (100, 7), (33, 33)])
 def test_pq_medium_routed(cuda_ok, pq_medium, R, k):
     p, q = pq_medium
