@@ -191,9 +191,12 @@ struct GRing {
 // exactly one vector, at step 8w + ((j + 7) mod 8); the lane keeps its sums
 // and at the window's end (or the tile's last step) all lanes store together,
 // lane j to out[its finishing step]: one 16-byte store per lane per 8 steps.
+// A stored sum at or below query k's bound thf sets bit k of maybe (a superset
+// of the keys the chunk's filter can admit).
 template <int M, int NST>
 __device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, const uint32_t (&w)[M / 2], int nst,
-                                             int j, float2& s01, float2& s23, float4* out) {
+                                             int j, float2& s01, float2& s23, float4* out, float4 thf,
+                                             uint32_t& maybe) {
     constexpr int MPL = M / 8;
     float4 fin = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
@@ -218,7 +221,11 @@ __device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, con
         if (blk == 7) fin = make_float4(s01.x, s01.y, s23.x, s23.y);
         if ((i & 7) == 7 || (NST < 16 && i == nst - 1)) {
             const int fstep = (i & ~7) + ((j + 7) & 7);
-            if (fstep <= i) out[fstep] = fin;
+            if (fstep <= i) {
+                out[fstep] = fin;
+                maybe |= (fin.x <= thf.x ? 1u : 0u) | (fin.y <= thf.y ? 2u : 0u) | (fin.z <= thf.z ? 4u : 0u) |
+                         (fin.w <= thf.w ? 8u : 0u);
+            }
         }
     }
 }
@@ -267,7 +274,12 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     float* resid = reinterpret_cast<float*>(dist4);         // [kGQ][d] while the LUT is built
     __shared__ EmitSmem esm;
     __shared__ int s_item, s_q[kGQ];
-    __shared__ int s_cnt[2][kGQ];       // per-chunk totals, alternating buffers
+    // per-chunk totals and "some sum may pass" bits of the 4 queries, three
+    // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
+    // barrier, clears buffer (c + 2) % 3 -- last read in chunk c - 1 (done
+    // before this barrier), next written in chunk c + 2 (after the next one)
+    __shared__ int s_cnt[3][kGQ];
+    __shared__ uint32_t s_any[3];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, grp = lane >> 3, j = lane & 7;
     // LUT builders: thread t owns LUT column ps = t % M (sub-quantizer inv(ps)) for codes t / M + kCStep * i
     const bool builder = tid < kCStep * M;
@@ -275,10 +287,11 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     const int NG = *wl.n_groups;
     const int total = p.has_delta ? 2 * NG : NG;
     const int rid = warp * 4 + grp;          // stripe of this lane group
-    if (tid < 2 * kGQ) s_cnt[tid / kGQ][tid % kGQ] = 0;
+    if (tid < 3 * kGQ) s_cnt[tid / kGQ][tid % kGQ] = 0;
+    if (tid < 3) s_any[tid] = 0;
     if (tid == 0) s_item = atomicAdd(counter, 1);
     __syncthreads();
-    int cpar = 0;                       // buffer of s_cnt the next chunk adds into
+    int cpar = 0;                       // buffer of s_cnt / s_any the next chunk adds into
     float cbv[kLB][DSUB];
     auto load_cb = [&](int cbase) {
 #pragma unroll
@@ -386,6 +399,18 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
+                // float form of the bounds for the stores' pass test; a bound at or
+                // above +inf bits admits everything, its bit is forced on
+                float tf[kGQ];
+                uint32_t force = 0;
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k) {
+                    const uint32_t hi = (uint32_t)(thr[k] >> 32);
+                    tf[k] = k < nqg && hi < 0x7f800000u ? __uint_as_float(hi) : -1.f;
+                    if (k < nqg && hi >= 0x7f800000u) force |= 1u << k;
+                }
+                const float4 thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
+                uint32_t maybe = 0;
 #pragma unroll 1
                 for (int tl = 0; tl < kRSteps / 16; ++tl) {
                     const int x0 = t * kRSteps + 16 * tl;
@@ -394,16 +419,22 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     // slot of (group r, step s of the chunk) = r * kRSteps + s
                     float4* out = dist4 + rid * kRSteps + 16 * tl;
                     if (wsteps - x0 >= 16)
-                        stagger_tile<M, 16>(lut, w, 16, j, s01, s23, out);
+                        stagger_tile<M, 16>(lut, w, 16, j, s01, s23, out, thf, maybe);
                     else
-                        stagger_tile<M, 15>(lut, w, wsteps - x0, j, s01, s23, out);
+                        stagger_tile<M, 15>(lut, w, wsteps - x0, j, s01, s23, out, thf, maybe);
 #pragma unroll
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
+                maybe = __reduce_or_sync(0xffffffffu, maybe);
+                if (lane == 0 && (maybe | force)) atomicOr(&s_any[cpar], maybe | force);
                 __syncthreads();
-                // every thread has finished the previous chunk: its totals
-                // buffer is free for the chunk after this one
-                if (tid < kGQ) s_cnt[cpar ^ 1][tid] = 0;
+                const int cfree = cpar == 0 ? 2 : cpar - 1;      // (cpar + 2) % 3
+                if (tid < kGQ) s_cnt[cfree][tid] = 0;
+                if (tid == 0) s_any[cfree] = 0;
+                if (s_any[cpar] == 0) {          // no sum of the chunk can pass any bound
+                    cpar = cpar == 2 ? 0 : cpar + 1;
+                    continue;
+                }
                 // thread t reads the slots t + kRT*e: group t/64 + 4e, chunk step
                 // t % 64, i.e. vectors (t/64 + 4e)*S + t*kRSteps + t%64 - 7.
                 // All of them are read into registers before the totals'
@@ -434,7 +465,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
 #pragma unroll
                     for (int k = 0; k < kGQ; ++k) cnt4[k] += (k < nqg && key_of(e, k) <= thr[k]) ? 1 : 0;
                 const int4 tot = block_sum4_once<kRT>(make_int4(cnt4[0], cnt4[1], cnt4[2], cnt4[3]), s_cnt[cpar]);
-                cpar ^= 1;
+                cpar = cpar == 2 ? 0 : cpar + 1;
                 const int totk[kGQ] = {tot.x, tot.y, tot.z, tot.w};
                 // queries with more than R keys under their bound get a new
                 // bound that admits R .. R + slack of them (one shared descent
