@@ -317,26 +317,61 @@ def main():
         exa = torch.empty((nq, R), dtype=torch.int64, device=dev)
         adc_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
         exa_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
+        take_o = torch.empty((N, qo), dtype=torch.int32, device=dev)
+        take_r = torch.empty((N, qo), dtype=torch.int32, device=dev)
+
+        class _DevArray:              # a library-owned device array seen as a torch tensor (no copy)
+            def __init__(self, ptr, n):
+                self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False),
+                                                 "version": 3}
         out_ids = torch.empty((qo, k), dtype=torch.int32, device=dev)
         out_dist = torch.empty((qo, k), dtype=torch.float32, device=dev)
         all_ids = torch.empty((N * qo, k), dtype=torch.int32, device=dev)
         all_dist = torch.empty((N * qo, k), dtype=torch.float32, device=dev)
 
-    def step(np_=nprobe):
+    def step(np_=nprobe, marks=None):
         batch.stage1_prepare_device(q_dev.data_ptr(), nq)
         if N == 1:
             batch.pq_search(index, nq, np_, k, rerank_n=R, overlay=False, route=True)
             return
+
+        def mark(name):               # CUDA events between the phases of one step (diagnostics)
+            if marks is not None:
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(ext)
+                marks.append((name, ev))
         with torch.cuda.stream(ext):
+            mark("start")
             batch.route_keys(index, nq, np_, keys_l.data_ptr())
+            mark("route")
             kt = shard.gather_route_keys(dist, keys_l, keys_all)
+            mark("gather keys")
             batch.route_merge(kt.data_ptr(), N * np_, nq, np_)
-            batch.pq_search_shard(index, nq, np_, R, 0, adc.data_ptr(), exa.data_ptr())
-            A = shard.to_owners(dist, N, adc, adc_r)
-            E = shard.to_owners(dist, N, exa, exa_r)
-            batch.pq_merge_shards(A.data_ptr(), E.data_ptr(), N * R, R, None, None, 0, 0, qo, k, False)
+            mark("route merge")
+            # nearest probes, global bounds, the other probes
+            batch.pq_shard_scan(index, nq, np_, R, 0)
+            mark("scan nearest")
+            bounds = torch.as_tensor(_DevArray(batch.pq_shard_bounds(), nq), device=dev)
+            shard.exchange_bounds(dist, bounds)
+            mark("exchange bounds")
+            batch.pq_shard_scan(index, nq, np_, R, 1)
+            mark("scan rest")
+            batch.pq_shard_select(index, nq, np_, R, adc.data_ptr())
+            mark("select")
+            shard.to_owners_raw(dist, N, adc, adc_r)
+            mark("stage 1 to owners")
+            batch.pq_shard_take(adc_r.data_ptr(), N, qo, R, take_o.data_ptr())
+            tk = shard.take_to_sources(dist, N, take_o, take_r)
+            mark("prefixes")
+            batch.pq_shard_rerank(index, nq, R, adc.data_ptr(), tk.data_ptr(), exa.data_ptr())
+            mark("rerank")
+            shard.to_owners_raw(dist, N, exa, exa_r)
+            mark("exact to owners")
+            batch.pq_shard_final(exa_r.data_ptr(), N, qo, R, k, False)
             batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
+            mark("final")
             shard.gather_results(dist, out_ids, out_dist, all_ids, all_dist)
+            mark("gather results")
 
     def results():
         if N == 1:
@@ -349,6 +384,16 @@ def main():
         batch.sync()
         if N > 1:
             dist.barrier()
+
+    # ---- per-phase times of one sharded step (INSITU_BENCH_PHASES=1, stderr) ----
+    if N > 1 and os.environ.get("INSITU_BENCH_PHASES") == "1":
+        for _ in range(3):
+            step()
+        marks = []
+        step(marks=marks)
+        torch.cuda.synchronize()
+        log(f"[bench] rank {rank} phases (ms): " + ", ".join(
+            f"{marks[i][0]} {marks[i - 1][1].elapsed_time(marks[i][1]):.3f}" for i in range(1, len(marks))))
 
     # ---- recall sweep over nprobe (untimed) ----
     sweep = []

@@ -524,16 +524,16 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
             ck(reset_candidates(cm, n, b->st), "reset_candidates");
             if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
         }
-        // Two passes over the probe table: every query's nearest list first, which
-        // sets a tight rank-R bound, then the other probes, which then emit few
-        // candidates.  The result does not depend on the order.
+        // Two passes over the probe table: every query's nearest local list first,
+        // which sets a tight rank-R bound, then its other local probes, which then
+        // emit few candidates.  The result does not depend on the order.
         const int npass = nprobe > 1 ? 2 : 1;
         for (int pass = 0; pass < npass; ++pass) {
-            const int col0 = pass == 0 ? 0 : 1, ncol = npass == 1 ? nprobe : (pass == 0 ? 1 : nprobe - 1);
+            const int ncol = npass == 1 ? nprobe : (pass == 0 ? 1 : nprobe - 1);   // bound on pairs per query
             {
                 StageScope stage(b, IVF_STAGE_WORKLIST);
                 ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
-                                  tmp, tmp_bytes, b->st, col0, ncol),
+                                  tmp, tmp_bytes, b->st, 0, npass == 1 ? nprobe : 0, npass == 1 ? -1 : pass),
                    "build_worklist");
             }
             StageScope stage(b, IVF_STAGE_SCAN);
@@ -635,6 +635,41 @@ void set_global_error(const std::string& msg) { g_err = msg; }
 // ===========================================================================
 // C ABI
 // ===========================================================================
+namespace {
+
+struct ShardPlan {
+    CandBuf cm{};
+    WorkList wl{};
+    void* tmp = nullptr;
+    size_t tmp_bytes = 0;
+};
+
+// the candidate buffers and work list of one phased search (one sub-batch)
+ShardPlan shard_plan(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int R) {
+    require(x->kind == kKindPQ, "index is not a residual-PQ index", IVF_ESTATE);
+    require(R > 0 && R <= 4096, "rerank_n must be in [1, 4096]");
+    const int items = pq_scan_chunk_items(x->M, x->d);
+    const int slack = pq_chunk_slack(x->M, x->d, R);
+    const int64_t cap64 =
+        (int64_t)nprobe * std::max(1, pq_scan_chunks(x->M, x->d, x->main.max_count)) * std::min(R + slack, items);
+    require(cap64 <= (1ll << 30), "candidate buffer of one query would exceed 2^30 keys", IVF_EOVERFLOW);
+    const size_t per_q = (size_t)cap64 * 8 + 32;
+    require((size_t)std::max(nq, 1) <= std::max<size_t>(1, scratch_budget() / per_q),
+            "the phased shard search takes one sub-batch: lower n_query or raise INSITU_SCRATCH_MB");
+    ShardPlan sp;
+    sp.wl = worklist_for(b, x, std::max(nq, 1), nprobe, &sp.tmp, &sp.tmp_bytes, pq_group_usable(x->M, x->d));
+    sp.cm.keys = ensure<uint64_t>(b, b->cand_m, (size_t)std::max(nq, 1) * cap64);
+    sp.cm.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)std::max(nq, 1));
+    sp.cm.thr = ensure<unsigned long long>(b, b->thr_m, (size_t)std::max(nq, 1));
+    sp.cm.overflow = b->overflow;
+    sp.cm.cap = (int)cap64;
+    sp.cm.R = R;
+    sp.cm.slack = slack;
+    return sp;
+}
+
+}  // namespace
+
 extern "C" {
 
 void* ivf_create_index_context(void) {
@@ -1196,6 +1231,133 @@ int ivf_pq_merge_shards(void* batch_ctx, const unsigned long long* d_adc, const 
                            d_dadc ? delta_topk : 0, n_query, k, exact_is_int, b->out_ids, b->out_dist, b->st),
            "pq_merge_shards");
         b->res_nq = n_query;
+        b->res_k = k;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// Sharded residual-PQ search in phases (no counterpart in the reference): the
+// caller exchanges the rank-R bounds after the nearest-probe pass, and the
+// shards rerank only the stage-1 prefix each query's owner asks for.
+// ---------------------------------------------------------------------------
+int ivf_pq_shard_scan(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n, int pass) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, 1);
+        require(pass == 0 || pass == 1, "pass must be 0 (nearest probe) or 1 (the other probes)");
+        require_probes(b, n_query, n_probes);
+        cudaSetDevice(b->device);
+        ShardPlan sp = shard_plan(b, x, n_query, n_probes, rerank_n);
+        PQParams p = pq_params(x, b->q, false);
+        if (pass == 0) {
+            StageScope stage(b, IVF_STAGE_WORKLIST);
+            ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+            ck(reset_candidates(sp.cm, n_query, b->st), "reset_candidates");
+        }
+        const int col0 = pass == 0 ? 0 : 1, ncol = pass == 0 ? 1 : n_probes - 1;
+        if (ncol <= 0 || n_query == 0) return;
+        {
+            StageScope stage(b, IVF_STAGE_WORKLIST);
+            ck(build_worklist(b->probes, n_query, n_probes, x->nlist_global, x->g2l, x->nlist, sp.wl, sp.tmp,
+                              sp.tmp_bytes, b->st, col0, ncol),
+               "build_worklist");
+        }
+        StageScope stage(b, IVF_STAGE_SCAN);
+        CandBuf none{};
+        ck(pq_scan(p, sp.wl, n_query * ncol, sp.cm, none, b->counter, b->st), "pq_scan");
+        queue_overflow_check(b);
+    });
+}
+
+unsigned long long* ivf_pq_shard_bounds(void* batch_ctx) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return nullptr;
+    }
+    return reinterpret_cast<unsigned long long*>(b->thr_m.p);
+}
+
+int ivf_pq_shard_select(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n,
+                        unsigned long long* d_adc) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        check_shape(b, x, n_query, n_probes, 1);
+        require(d_adc != nullptr, "adc output is required");
+        cudaSetDevice(b->device);
+        ShardPlan sp = shard_plan(b, x, n_query, n_probes, rerank_n);
+        StageScope stage(b, IVF_STAGE_SELECT);
+        ck(select_top_r(sp.cm, n_query, reinterpret_cast<uint64_t*>(d_adc), b->st), "select_top_r");
+    });
+}
+
+int ivf_pq_shard_take(void* batch_ctx, const unsigned long long* d_adc_all, int n_shards, int n_owned, int rerank_n,
+                      int* d_take) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_adc_all && d_take && n_shards > 0 && n_owned >= 0 && rerank_n > 0, "bad shard-take arguments");
+        cudaSetDevice(b->device);
+        ck(pq_shard_take(reinterpret_cast<const uint64_t*>(d_adc_all), n_shards, n_owned, rerank_n, d_take, b->st),
+           "pq_shard_take");
+    });
+}
+
+int ivf_pq_shard_rerank(void* batch_ctx, void* idx_ctx, int n_query, int rerank_n,
+                        const unsigned long long* d_adc, const int* d_take, unsigned long long* d_exact) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        require(x->kind == kKindPQ, "index is not a residual-PQ index", IVF_ESTATE);
+        require(d_adc && d_take && d_exact && rerank_n > 0, "bad shard-rerank arguments");
+        require(n_query >= 0 && n_query <= b->max_nq && b->d == x->d, "shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        PQParams p = pq_params(x, b->q, false);
+        StageScope stage(b, IVF_STAGE_RERANK);
+        ck(pq_rerank(p, x->nlist, reinterpret_cast<const uint64_t*>(d_adc), rerank_n, nullptr, 0, n_query, 1, nullptr,
+                     nullptr, reinterpret_cast<uint64_t*>(d_exact), nullptr, b->st, d_take),
+           "pq_rerank");
+    });
+}
+
+int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_exact_all, int n_shards, int n_owned,
+                       int rerank_n, int k, int exact_is_int) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_exact_all && n_shards > 0 && rerank_n > 0, "bad shard-final arguments");
+        require(n_owned >= 0 && n_owned <= b->max_nq && k > 0 && k <= b->max_k, "shape exceeds the batch limits");
+        cudaSetDevice(b->device);
+        ck(pq_shard_final(reinterpret_cast<const uint64_t*>(d_exact_all), n_shards, n_owned, rerank_n, k,
+                          exact_is_int, b->out_ids, b->out_dist, b->st),
+           "pq_shard_final");
+        b->res_nq = n_owned;
         b->res_k = k;
     });
 }

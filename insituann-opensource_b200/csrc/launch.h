@@ -23,9 +23,12 @@ size_t worklist_scan_bytes(int nlist);
 // When wl.groups is set, also packs the pairs of every list into groups of up
 // to kGroupQueries consecutive pairs: groups[g] = (list << 32) | (first pair << 3) | size.
 // Only probe-table columns col0 .. col0+ncol-1 are used (ncol <= 0: to the end).
+// seed_part >= 0 replaces the column range: 0 = each query's first probe whose
+// list is local, 1 = its other local probes.
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
-                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0 = 0, int ncol = 0);
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0 = 0, int ncol = 0,
+                           int seed_part = -1);
 constexpr int kGroupQueries = 4;
 
 // ---- coarse routing (route.cu) --------------------------------------------
@@ -118,9 +121,16 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
 // Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).
 // When out_exact_main is given, the per-candidate exact keys are written instead
 // of (ids, dist) being selected: [nq, R] and [nq, Rd] aligned with the inputs.
+// take (device [nq], may be null): rerank only main keys 0 .. take[q]-1 of each query.
 cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int R, const uint64_t* s1_delta,
                       int Rd, int nq, int k, int32_t* out_ids, float* out_dist, uint64_t* out_exact_main,
-                      uint64_t* out_exact_delta, cudaStream_t st);
+                      uint64_t* out_exact_delta, cudaStream_t st, const int32_t* take = nullptr);
+// Sharded search, owner side: adc_all [G][qo][R] ascending stage-1 lists of the
+// G shards -> take [G][qo], the prefix of each list in the query's stage 1;
+// ex_all [G][qo][R] the shards' exact keys of those prefixes -> top-k.
+cudaError_t pq_shard_take(const uint64_t* adc_all, int G, int qo, int R, int32_t* take, cudaStream_t st);
+cudaError_t pq_shard_final(const uint64_t* ex_all, int G, int qo, int R, int k, int exact_is_int, int32_t* out_ids,
+                           float* out_dist, cudaStream_t st);
 // Final merge of sharded stage-1 results: per query, G shards each give R
 // (ADC key, exact key) pairs for the main segment and Rd for the delta.
 cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main, int n_main, int R,

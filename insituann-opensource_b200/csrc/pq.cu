@@ -588,7 +588,7 @@ __device__ __forceinline__ uint8_t to_u8(float x) {  // updates/exact_update.cu:
 __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, const uint64_t* __restrict__ s1m,
                                                          int R, const uint64_t* __restrict__ s1d, int Rd, int k,
                                                          int32_t* out_ids, float* out_dist, uint64_t* out_exm,
-                                                         uint64_t* out_exd) {
+                                                         uint64_t* out_exd, const int32_t* __restrict__ take) {
     extern __shared__ uint64_t sk[];
     __shared__ float sq[kPMaxD];
     __shared__ __align__(16) uint8_t squ[kPMaxD];
@@ -601,11 +601,12 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     }
     __syncthreads();
     const int nc = R + Rd;
+    const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
     int np = 1;
     while (np < nc) np <<= 1;
     for (int c = tid; c < np; c += kRRT) {
         uint64_t ek = kKeyNone;
-        if (c < nc) {
+        if (c < nc && (c >= R || c < tq)) {
             const bool dl = c >= R;
             const uint64_t* src = dl ? s1d + (size_t)q * Rd : s1m + (size_t)q * R;
             const int j = dl ? c - R : c;
@@ -669,7 +670,7 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
 // ---------------------------------------------------------------------------
 // merge of per-shard (ADC key, exact key) lists
 // ---------------------------------------------------------------------------
-constexpr int kMT = 512;
+constexpr int kMT = 256;
 constexpr int kMMax = 8192;
 
 // sorts (key, payload) pairs ascending by key; n power of two
@@ -695,9 +696,11 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
                                                            const uint64_t* adc_d, const uint64_t* ex_d, int n_d,
                                                            int Rd, int k, int exact_is_int, int32_t* out_ids,
                                                            float* out_dist) {
-    extern __shared__ uint64_t smk[];
-    int* smv = reinterpret_cast<int*>(smk + kMMax);
+    extern __shared__ uint64_t smk[];                 // [npmax] keys, then [npmax] payloads
     __shared__ uint64_t fin[2048];
+    int npmax = 1;
+    while (npmax < (n_m > n_d ? n_m : n_d)) npmax <<= 1;
+    int* smv = reinterpret_cast<int*>(smk + npmax);
     const int q = blockIdx.x, tid = threadIdx.x;
     int nf = 0;
     for (int seg = 0; seg < 2; ++seg) {
@@ -731,6 +734,85 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
         out_ids[(size_t)q * k + j] = ok ? (int32_t)key_lo(ek) : -1;
         out_dist[(size_t)q * k + j] =
             ok ? (exact_is_int ? (float)key_hi(ek) : __uint_as_float(key_hi(ek))) : __int_as_float(0x7f800000);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// sharded search, owner side (one CTA per owned query)
+// ---------------------------------------------------------------------------
+// Each of the G shards sent its stage-1 list of the query: R keys, ascending,
+// kKeyNone-padded.  The query's stage 1 over the whole index is every distinct
+// key <= kappa, the R-th smallest of the union (with multiplicity), so shard s
+// is asked to rerank the prefix of its list up to kappa: take[s][q] = the
+// number of its keys <= kappa (all of them when the union has fewer than R).
+constexpr int kShT = 256;
+
+__global__ void __launch_bounds__(kShT) shard_take_kernel(const uint64_t* __restrict__ adc, int G, int qo, int R,
+                                                          int32_t* __restrict__ take) {
+    __shared__ int hist[256];
+    __shared__ int bc[4];
+    __shared__ int s_valid;
+    const int q = blockIdx.x, tid = threadIdx.x;
+    const int n = G * R;
+    // element i of the union: shard i / R, rank i % R
+    auto keyf = [&](int i) -> uint64_t { return adc[((size_t)(i / R) * qo + q) * R + (i % R)]; };
+    if (tid == 0) s_valid = 0;
+    __syncthreads();
+    int v = 0;
+    for (int i = tid; i < n; i += kShT) v += keyf(i) != kKeyNone ? 1 : 0;
+    if (v) atomicAdd(&s_valid, v);
+    __syncthreads();
+    const int valid = s_valid;
+    uint64_t kap = kKeyNone - 1;
+    if (valid > R) kap = block_kth_key<kShT>(keyf, n, R, kKeyNone - 1, hist, bc);
+    // lists are ascending: the count of keys <= kappa is a binary search
+    for (int g = tid; g < G; g += kShT) {
+        const uint64_t* a = adc + ((size_t)g * qo + q) * R;
+        int lo = 0, hi = R;
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (a[mid] <= kap) lo = mid + 1; else hi = mid;
+        }
+        take[(size_t)g * qo + q] = lo;
+    }
+}
+
+// Final top-k of an owned query over the exact keys the shards returned for
+// their requested prefixes (kKeyNone elsewhere); a position reranked twice
+// (a list probed twice) counts once.
+__global__ void __launch_bounds__(kShT) shard_final_kernel(const uint64_t* __restrict__ ex, int G, int qo, int R,
+                                                           int k, int exact_is_int, int32_t* out_ids,
+                                                           float* out_dist) {
+    extern __shared__ uint64_t fk[];               // [np]
+    __shared__ int s_cnt;
+    const int q = blockIdx.x, tid = threadIdx.x;
+    if (tid == 0) s_cnt = 0;
+    __syncthreads();
+    const int n = G * R;
+    for (int i = tid; i < n; i += kShT) {
+        const uint64_t e = ex[((size_t)(i / R) * qo + q) * R + (i % R)];
+        if (e != kKeyNone) fk[atomicAdd(&s_cnt, 1)] = e;
+    }
+    __syncthreads();
+    const int nv = s_cnt;
+    int np = 1;
+    while (np < nv) np <<= 1;
+    for (int i = nv + tid; i < np; i += kShT) fk[i] = kKeyNone;
+    block_bitonic_sort<kShT>(fk, np);
+    if (tid == 0) {
+        int o = 0;
+        uint64_t last = kKeyNone;
+        for (int i = 0; i < nv && o < k; ++i) {
+            if (fk[i] == last) continue;
+            last = fk[i];
+            out_ids[(size_t)q * k + o] = (int32_t)key_lo(last);
+            out_dist[(size_t)q * k + o] = exact_is_int ? (float)key_hi(last) : __uint_as_float(key_hi(last));
+            ++o;
+        }
+        for (; o < k; ++o) {
+            out_ids[(size_t)q * k + o] = -1;
+            out_dist[(size_t)q * k + o] = __int_as_float(0x7f800000);
+        }
     }
 }
 
@@ -800,7 +882,7 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
 
 cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int R, const uint64_t* s1_delta,
                       int Rd, int nq, int k, int32_t* out_ids, float* out_dist, uint64_t* out_exact_main,
-                      uint64_t* out_exact_delta, cudaStream_t st) {
+                      uint64_t* out_exact_delta, cudaStream_t st, const int32_t* take) {
     if (nq <= 0) return cudaSuccess;
     const int nc = R + Rd;
     if (nc > kRRMax || p.d > kPMaxD || (p.d % 16) != 0) return cudaErrorInvalidValue;
@@ -812,7 +894,7 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
     if (e) return e;
     note_launch();
     pq_rerank_kernel<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist,
-                                             out_exact_main, out_exact_delta);
+                                             out_exact_main, out_exact_delta, take);
     return cudaGetLastError();
 }
 
@@ -821,12 +903,35 @@ cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main
                             int k, int exact_is_int, int32_t* out_ids, float* out_dist, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     if (n_main > kMMax || n_delta > kMMax || R + Rd > 2048 || k > 2048) return cudaErrorInvalidValue;
-    size_t smem = (sizeof(uint64_t) + sizeof(int)) * kMMax;
+    int npmax = 1;
+    while (npmax < (n_main > n_delta ? n_main : n_delta)) npmax <<= 1;
+    size_t smem = (sizeof(uint64_t) + sizeof(int)) * npmax;
     cudaError_t e = cudaFuncSetAttribute(merge_shards_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     note_launch();
     merge_shards_kernel<<<nq, kMT, smem, st>>>(adc_main, exact_main, n_main, R, adc_delta, exact_delta, n_delta, Rd,
                                                k, exact_is_int, out_ids, out_dist);
+    return cudaGetLastError();
+}
+
+cudaError_t pq_shard_take(const uint64_t* adc_all, int G, int qo, int R, int32_t* take, cudaStream_t st) {
+    if (qo <= 0) return cudaSuccess;
+    note_launch();
+    shard_take_kernel<<<qo, kShT, 0, st>>>(adc_all, G, qo, R, take);
+    return cudaGetLastError();
+}
+
+cudaError_t pq_shard_final(const uint64_t* ex_all, int G, int qo, int R, int k, int exact_is_int, int32_t* out_ids,
+                           float* out_dist, cudaStream_t st) {
+    if (qo <= 0) return cudaSuccess;
+    int np = 1;
+    while (np < G * R) np <<= 1;
+    const size_t smem = sizeof(uint64_t) * np;
+    if (smem > 160 * 1024) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(shard_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e) return e;
+    note_launch();
+    shard_final_kernel<<<qo, kShT, smem, st>>>(ex_all, G, qo, R, k, exact_is_int, out_ids, out_dist);
     return cudaGetLastError();
 }
 

@@ -16,7 +16,8 @@ __global__ void reset_kernel(int32_t* cnt, unsigned long long* thr, int nq) {
     int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < nq) {
         cnt[i] = 0;
-        thr[i] = kKeyNone;
+        thr[i] = 0x7FFFFFFFFFFFFFFFull;   // no bound yet: above every key, and ordered as a signed int64
+                                         // so shards can exchange bounds with an int64 minimum
     }
 }
 

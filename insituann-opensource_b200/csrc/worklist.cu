@@ -35,6 +35,46 @@ __global__ void count_pairs_kernel(const int32_t* probes, size_t total, int npro
     }
 }
 
+// Seeded two-pass split by local lists (thread per query): part 0 = the
+// query's first probe column whose list is local, part 1 = its other local
+// probes.  On an unsharded index that is column 0 and the rest.
+__device__ __forceinline__ int first_local_col(const int32_t* probes, int q, int nprobe, int nlist_global,
+                                               const int32_t* list_map) {
+    for (int c = 0; c < nprobe; ++c)
+        if (local_list(probes, (size_t)q * nprobe + c, nlist_global, list_map) >= 0) return c;
+    return nprobe;
+}
+
+__global__ void count_seed_kernel(const int32_t* probes, int nq, int nprobe, int part, int nlist_global,
+                                  const int32_t* list_map, int32_t* list_cnt) {
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += gridDim.x * blockDim.x) {
+        const int c0 = first_local_col(probes, q, nprobe, nlist_global, list_map);
+        if (c0 >= nprobe) continue;
+        const int cb = part == 0 ? c0 : c0 + 1, ce = part == 0 ? c0 + 1 : nprobe;
+        for (int c = cb; c < ce; ++c) {
+            const int l = local_list(probes, (size_t)q * nprobe + c, nlist_global, list_map);
+            if (l >= 0) atomicAdd(&list_cnt[l], 1);
+        }
+    }
+}
+
+__global__ void fill_seed_kernel(const int32_t* probes, int nq, int nprobe, int part, int nlist_global,
+                                 const int32_t* list_map, const int32_t* list_off, int32_t* cursor, int32_t* pair_q,
+                                 int32_t* pair_l) {
+    for (int q = blockIdx.x * blockDim.x + threadIdx.x; q < nq; q += gridDim.x * blockDim.x) {
+        const int c0 = first_local_col(probes, q, nprobe, nlist_global, list_map);
+        if (c0 >= nprobe) continue;
+        const int cb = part == 0 ? c0 : c0 + 1, ce = part == 0 ? c0 + 1 : nprobe;
+        for (int c = cb; c < ce; ++c) {
+            const int l = local_list(probes, (size_t)q * nprobe + c, nlist_global, list_map);
+            if (l < 0) continue;
+            const int p = list_off[l] + atomicAdd(&cursor[l], 1);
+            pair_q[p] = q;
+            pair_l[p] = l;
+        }
+    }
+}
+
 __global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprobe, int col0, int ncol,
                                   int nlist_global, const int32_t* list_map, const int32_t* list_off,
                                   int32_t* cursor, int32_t* pair_q, int32_t* pair_l) {
@@ -83,12 +123,21 @@ size_t worklist_scan_bytes(int nlist) {
 
 cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_global,
                            const int32_t* list_map, int nlist_local, WorkList wl,
-                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0, int ncol) {
+                           void* scan_tmp, size_t scan_bytes, cudaStream_t st, int col0, int ncol, int seed_part) {
     cudaError_t e;
     if (ncol <= 0) ncol = nprobe - col0;
     if ((e = cudaMemsetAsync(wl.list_cnt, 0, sizeof(int32_t) * (nlist_local + 1), st))) return e;
     if ((e = cudaMemsetAsync(wl.cursor, 0, sizeof(int32_t) * nlist_local, st))) return e;
     size_t total = (size_t)nq * (ncol > 0 ? ncol : 0);
+    if (seed_part >= 0) {
+        total = 0;
+        if (nq > 0) {
+            note_launch();
+            count_seed_kernel<<<grid_for(nq, 256), 256, 0, st>>>(probes, nq, nprobe, seed_part, nlist_global,
+                                                                 list_map, wl.list_cnt);
+            if ((e = cudaGetLastError())) return e;
+        }
+    }
     if (total > 0) {
         note_launch();
         count_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, col0, ncol, nlist_global,
@@ -102,6 +151,12 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
         fill_pairs_kernel<<<grid_for(total, 256), 256, 0, st>>>(probes, total, nprobe, col0, ncol, nlist_global,
                                                                 list_map, wl.list_off, wl.cursor, wl.pair_q,
                                                                 wl.pair_l);
+        if ((e = cudaGetLastError())) return e;
+    }
+    if (seed_part >= 0 && nq > 0) {
+        note_launch();
+        fill_seed_kernel<<<grid_for(nq, 256), 256, 0, st>>>(probes, nq, nprobe, seed_part, nlist_global, list_map,
+                                                            wl.list_off, wl.cursor, wl.pair_q, wl.pair_l);
         if ((e = cudaGetLastError())) return e;
     }
     if (wl.groups) {

@@ -39,7 +39,9 @@ EXPORTS = [
     "ivf_route", "ivf_set_probes", "ivf_get_probes", "ivf_u8_search", "ivf_pq_search", "ivf_get_results_i32",
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
     "ivf_route_keys", "ivf_route_merge", "ivf_pq_search_shard", "ivf_pq_merge_shards",
-    "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_last_error", "ivf_global_last_error",
+    "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_pq_shard_scan", "ivf_pq_shard_bounds",
+    "ivf_pq_shard_select", "ivf_pq_shard_take", "ivf_pq_shard_rerank", "ivf_pq_shard_final",
+    "ivf_last_error", "ivf_global_last_error",
     "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms", "ivf_u8_search_noalloc",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
@@ -89,6 +91,12 @@ _SIGS = {
     "ivf_pq_merge_shards": ([vp, vp, vp, i32, i32, vp, vp, i32, i32, i32, i32, i32], i32),
     "ivf_u8_search_shard": ([vp, vp, i32, i32, i32, vp], i32),
     "ivf_u8_merge_shards": ([vp, vp, i32, i32, i32], i32),
+    "ivf_pq_shard_scan": ([vp, vp, i32, i32, i32, i32], i32),
+    "ivf_pq_shard_bounds": ([vp], vp),
+    "ivf_pq_shard_select": ([vp, vp, i32, i32, i32, vp], i32),
+    "ivf_pq_shard_take": ([vp, vp, i32, i32, i32, vp], i32),
+    "ivf_pq_shard_rerank": ([vp, vp, i32, i32, vp, vp, vp], i32),
+    "ivf_pq_shard_final": ([vp, vp, i32, i32, i32, i32, i32], i32),
     "ivf_last_error": ([vp], C.c_char_p),
     "ivf_global_last_error": ([], C.c_char_p),
     "cuda_is_available": ([], C.c_bool),
@@ -335,6 +343,27 @@ class Batch:
                         exact_is_int):
         self._check(self.L.ivf_pq_merge_shards(self.h, d_adc, d_exact, n_main, rerank_n, d_dadc, d_dexact, n_delta,
                                                delta_topk, nq, k, 1 if exact_is_int else 0))
+
+    # phased sharded PQ search (see the header): device pointers as ints
+    def pq_shard_scan(self, index: Index, nq, nprobe, rerank_n, pass_):
+        self._check(self.L.ivf_pq_shard_scan(self.h, index.h, nq, nprobe, rerank_n, pass_))
+
+    def pq_shard_bounds(self) -> int:
+        """device address of the [nq] int64 rank-R bounds"""
+        return int(self.L.ivf_pq_shard_bounds(self.h) or 0)
+
+    def pq_shard_select(self, index: Index, nq, nprobe, rerank_n, d_adc):
+        self._check(self.L.ivf_pq_shard_select(self.h, index.h, nq, nprobe, rerank_n, d_adc))
+
+    def pq_shard_take(self, d_adc_all, n_shards, n_owned, rerank_n, d_take):
+        self._check(self.L.ivf_pq_shard_take(self.h, d_adc_all, n_shards, n_owned, rerank_n, d_take))
+
+    def pq_shard_rerank(self, index: Index, nq, rerank_n, d_adc, d_take, d_exact):
+        self._check(self.L.ivf_pq_shard_rerank(self.h, index.h, nq, rerank_n, d_adc, d_take, d_exact))
+
+    def pq_shard_final(self, d_exact_all, n_shards, n_owned, rerank_n, k, exact_is_int):
+        self._check(self.L.ivf_pq_shard_final(self.h, d_exact_all, n_shards, n_owned, rerank_n, k,
+                                              1 if exact_is_int else 0))
 
     def u8_search_shard(self, index: Index, nq, nprobe, k, d_keys):
         self._check(self.L.ivf_u8_search_shard(self.h, index.h, nq, nprobe, k, d_keys))

@@ -12,6 +12,17 @@ bytes (LPT), and one query batch moves through three collectives:
      all-to-all, and the owner merges them (ivf_pq_merge_shards);
   3. the owners' top-k are all-gathered.
 
+The phased protocol (ivf_pq_shard_* entry points) replaces step 2 by:
+
+  2a. after every shard has scanned each query's nearest probe, the per-query
+      rank-R bounds are reduced with an int64 minimum (exchange_bounds) and
+      every shard scans the other probes with the global bound;
+  2b. the stage-1 lists go to the owners (to_owners_raw); each owner computes
+      per shard the prefix of its list in the query's stage 1, and the prefix
+      lengths go back to the shards (take_to_sources);
+  2c. each shard reranks only that prefix; the exact keys go to the owners
+      (to_owners_raw), which form the top-k.
+
 The functions take torch tensors and a process group, so the same code runs
 over NCCL with device tensors (bench.py) and over gloo with CPU tensors
 (tests/test_shard_gloo.py).
@@ -66,3 +77,22 @@ def gather_results(dist, ids_local, dist_local, ids_all, dist_all):
     dist.all_gather_into_tensor(ids_all, ids_local)
     dist.all_gather_into_tensor(dist_all, dist_local)
     return ids_all.reshape(-1, ids_local.shape[1]), dist_all.reshape(-1, dist_local.shape[1])
+
+
+def exchange_bounds(dist, bounds):
+    """bounds [nq] int64 (no bound: INT64_MAX) -> elementwise minimum over ranks, in place."""
+    dist.all_reduce(bounds, op=dist.ReduceOp.MIN)
+    return bounds
+
+
+def to_owners_raw(dist, world, per_query, recv):
+    """per_query [nq, R] (nq = world * qo, block-partitioned) -> recv [world (source), qo, R]."""
+    nq, R = per_query.shape
+    dist.all_to_all_single(recv, per_query.reshape(world, nq // world, R))
+    return recv
+
+
+def take_to_sources(dist, world, take, recv):
+    """owner's take [world (shard), qo] -> this shard's [world * qo] prefix lengths in global query order."""
+    dist.all_to_all_single(recv, take.contiguous())
+    return recv.reshape(-1)

@@ -371,6 +371,80 @@ def test_sharded_merge_equals_unsharded(cuda_ok, pq_medium):
         o.close()
 
 
+@pytest.mark.parametrize("R,k", [(256, 10), (40, 40)])
+def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
+    """lists split over 3 shards (three index contexts on one GPU), the phased
+    protocol with the exchanges done on the host side: nearest-probe scans,
+    int64 minimum of the bounds, the other probes, stage 1 to the owners,
+    prefix lengths back, prefix reranks, owners' top-k == unsharded search."""
+    p, q = pq_medium
+    nlist = len(p["counts"])
+    G, nprobe = 3, 12
+    nq = q.shape[0] - q.shape[0] % G
+    q = q[:nq]
+    qo = nq // G
+    owner = np.arange(nlist) % G
+    shards = []
+    for s in range(G):
+        lists = np.where(owner == s)[0]
+        rows = np.concatenate([np.arange(p["offsets"][l], p["offsets"][l] + p["counts"][l]) for l in lists])
+        cnt = p["counts"][lists]
+        off = np.zeros(len(lists), np.int64)
+        off[1:] = np.cumsum(cnt)[:-1]
+        idx = ib.Index().load_pq(p["centroids"][lists], p["codebook"], p["codes"][rows], off, cnt, p["r2o"][rows],
+                                 base_u8=p["base_u8"][rows])
+        idx.set_shard(nlist, lists.astype(np.int32), p["offsets"][lists])
+        shards.append(idx)
+    dev = torch.device("cuda")
+    exp_probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    batches = [ib.Batch(nq, q.shape[1], nprobe, k, nlist) for _ in range(G)]
+    adc = torch.empty((G, nq, R), dtype=torch.int64, device=dev)
+    exa = torch.empty((G, nq, R), dtype=torch.int64, device=dev)
+    for s in range(G):
+        batches[s].stage1_prepare(q)
+        batches[s].set_probes(exp_probes)
+        batches[s].pq_shard_scan(shards[s], nq, nprobe, R, 0)
+    for b in batches:
+        b.sync()
+
+    class Dev:
+        def __init__(self, ptr, n):
+            self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<i8", "data": (ptr, False), "version": 3}
+    bounds = [torch.as_tensor(Dev(b.pq_shard_bounds(), nq), device=dev) for b in batches]
+    low = torch.stack(bounds).min(dim=0).values
+    for t in bounds:
+        t.copy_(low)
+    torch.cuda.synchronize()
+    for s in range(G):
+        batches[s].pq_shard_scan(shards[s], nq, nprobe, R, 1)
+        batches[s].pq_shard_select(shards[s], nq, nprobe, R, adc[s].data_ptr())
+    for b in batches:
+        b.sync()
+    # stage 1 to the owners: owner o gets [G][qo][R]
+    adc_o = [adc[:, o * qo:(o + 1) * qo, :].contiguous() for o in range(G)]
+    take_o = [torch.empty((G, qo), dtype=torch.int32, device=dev) for _ in range(G)]
+    for o in range(G):
+        batches[o].pq_shard_take(adc_o[o].data_ptr(), G, qo, R, take_o[o].data_ptr())
+    for b in batches:
+        b.sync()
+    for s in range(G):
+        take_s = torch.cat([take_o[o][s] for o in range(G)]).contiguous()     # [nq], global query order
+        batches[s].pq_shard_rerank(shards[s], nq, R, adc[s].data_ptr(), take_s.data_ptr(), exa[s].data_ptr())
+    for b in batches:
+        b.sync()
+    gi = np.zeros((nq, k), np.int32)
+    gd = np.zeros((nq, k), np.float32)
+    for o in range(G):
+        ex_o = exa[:, o * qo:(o + 1) * qo, :].contiguous()
+        batches[o].pq_shard_final(ex_o.data_ptr(), G, qo, R, k, True)
+        gi[o * qo:(o + 1) * qo], gd[o * qo:(o + 1) * qo] = batches[o].get_results(qo, k)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              exp_probes, k, rerank_n=R, base_u8=p["base_u8"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    for o in batches + shards:
+        o.close()
+
+
 def test_errors_are_reported_not_fatal(cuda_ok, pq_medium):
     p, q = pq_medium
     index = ib.Index()
