@@ -5,7 +5,9 @@ what the device kernels return on a GPU shard: sorted local routing keys,
 stage-1 (ADC key, global position) lists restricted to its lists, and the
 exact key of every candidate.  The collectives of shard.py then move them and
 a NumPy mirror of the device merge forms the result, which must equal the
-unsharded oracle search.  A second test drops a rank and checks that the
+unsharded oracle search.  A second test runs the phased protocol the same
+way (bounds minimum, stage-1 lists to the owners, prefix lengths back, exact
+keys of the prefixes to the owners).  A third drops a rank and checks that the
 survivor gets an error from the process-group timeout instead of hanging.
 """
 import os
@@ -129,6 +131,77 @@ def test_two_rank_exchange_equals_unsharded_oracle():
     assert np.array_equal(probes, exp_p)
     oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"],
                               idx["r2o"], q, exp_p, 10, rerank_n=64, base_u8=idx["base_rr"])
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
+def _phased_worker(rank, world, port, data, out):
+    """the phased protocol: bounds minimum, stage-1 lists to the owners, prefix
+    lengths back, prefix reranks, exact keys to the owners, owners' top-k."""
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
+    idx, q, probes, R, k = data["idx"], data["q"], data["probes"], data["R"], data["k"]
+    owner = np.arange(len(idx["counts"])) % world
+    lists = np.where(owner == rank)[0]
+    nq = q.shape[0]
+    qo = nq // world
+    as_t = lambda a: torch.from_numpy(np.ascontiguousarray(a).view(np.int64))      # noqa: E731
+    # bounds: the minimum over ranks of int64 values (no bound = INT64_MAX)
+    rng = np.random.default_rng(rank)
+    mine = rng.integers(0, 1 << 40, size=nq).astype(np.int64)
+    mine[::7] = np.iinfo(np.int64).max
+    got = shard.exchange_bounds(dist, torch.from_numpy(mine.copy())).numpy()
+    allb = [torch.empty(nq, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(allb, torch.from_numpy(mine))
+    assert np.array_equal(got, np.min(np.stack([t.numpy() for t in allb]), axis=0))
+    # stage 1 of this shard: sorted R keys per query (global positions)
+    s1, ex = _shard_stage1(idx, q, probes, lists, R)
+    o = np.argsort(s1, axis=1, kind="stable")
+    s1, ex = np.take_along_axis(s1, o, 1), np.take_along_axis(ex, o, 1)
+    recv = torch.empty((world, qo, R), dtype=torch.int64)
+    adc_o = shard.to_owners_raw(dist, world, as_t(s1), recv).numpy().view(np.uint64)     # [G][qo][R]
+    take = np.zeros((world, qo), np.int32)                  # owner: prefix of each shard's list
+    for i in range(qo):
+        allk = np.sort(adc_o[:, i, :].reshape(-1))
+        valid = allk[allk != NONE]
+        kap = valid[R - 1] if len(valid) > R else NONE - np.uint64(1)
+        for g in range(world):
+            take[g, i] = int(np.searchsorted(adc_o[g, i], kap, side="right"))
+    rtake = torch.empty((world, qo), dtype=torch.int32)
+    mytake = shard.take_to_sources(dist, world, torch.from_numpy(take), rtake).numpy()   # [nq]
+    # exact keys of the requested prefix only; the rest of the list stays NONE
+    exs = np.where(np.arange(R)[None, :] < mytake[:, None], ex, NONE)
+    recv2 = torch.empty((world, qo, R), dtype=torch.int64)
+    ex_o = shard.to_owners_raw(dist, world, as_t(exs), recv2).numpy().view(np.uint64)
+    ids = np.full((qo, k), -1, np.int32)
+    dd = np.full((qo, k), np.inf, np.float32)
+    for i in range(qo):
+        e = np.unique(ex_o[:, i, :].reshape(-1))
+        e = e[e != NONE][:k]
+        for j, key in enumerate(e):
+            ids[i, j] = int(key & np.uint64(0xFFFFFFFF))
+            dd[i, j] = float(int(key >> np.uint64(32)))
+    ids_all = torch.empty((world * qo, k), dtype=torch.int32)
+    d_all = torch.empty((world * qo, k), dtype=torch.float32)
+    gi, gd = shard.gather_results(dist, torch.from_numpy(ids), torch.from_numpy(dd), ids_all, d_all)
+    if rank == 0:
+        out.put((gi.numpy(), gd.numpy()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_phased_protocol_equals_unsharded_oracle():
+    n, d, nlist, M = 12000, 32, 24, 16
+    base = synth.mixture_u8(n, d, 40, 10.0, seed=83)
+    idx = synth.build_pq_index(base, nlist, M, seed=83, kmeans_iters=5, pq_iters=4, train_n=6000)
+    q = synth.mixture_u8(40, d, 40, 10.0, seed=83, stream_base=1 << 20).float().numpy()
+    probes, _ = oracle.route_l2(q, idx["centroids"], 5)
+    data = dict(idx=idx, q=q, probes=probes, R=48, k=10)
+    ctx = mp.get_context("spawn")
+    out = ctx.SimpleQueue()
+    mp.start_processes(_phased_worker, args=(2, _free_port(), data, out), nprocs=2, join=True, start_method="spawn")
+    gi, gd = out.get()
+    oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"],
+                              idx["r2o"], q, probes, 10, rerank_n=48, base_u8=idx["base_rr"])
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
 
 
