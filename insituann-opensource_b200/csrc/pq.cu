@@ -585,14 +585,26 @@ __device__ __forceinline__ uint8_t to_u8(float x) {  // updates/exact_update.cu:
     return (uint8_t)lroundf(x);
 }
 
+// Exact rerank of one query's stage-1 candidates (CTA per query).  Four threads
+// share a candidate row: for the fp32 distance thread `sub` owns the lanes
+// 4 sub .. 4 sub + 3 of the reference's 16-lane AVX-512 arithmetic
+// (cuda/search/cpu_fine/cpu_fine_kernels_pq_resid.cpp:106-131: per block of 16
+// dimensions acc[l] = fma(q - v, q - v, acc[l]), then the 512-bit horizontal
+// add, a pairwise tree l + 8, + 4, + 2, + 1), so its 16-byte loads of a block
+// are one coalesced 64-byte piece of the row and the tree's first two levels
+// are shuffles inside the group of four.  The u8 distance is an exact int32
+// sum, split the same way.  NB = d / 16 when the row length is a template
+// constant (all loads of a row issued before the arithmetic), 0 for any d.
+template <int NB>
 __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, const uint64_t* __restrict__ s1m,
                                                          int R, const uint64_t* __restrict__ s1d, int Rd, int k,
                                                          int32_t* out_ids, float* out_dist, uint64_t* out_exm,
                                                          uint64_t* out_exd, const int32_t* __restrict__ take) {
     extern __shared__ uint64_t sk[];
-    __shared__ float sq[kPMaxD];
+    __shared__ __align__(16) float sq[kPMaxD];
     __shared__ __align__(16) uint8_t squ[kPMaxD];
     const int q = blockIdx.x, tid = threadIdx.x, d = p.d;
+    const int nb = NB ? NB : d / 16;
     const bool f32 = p.main.rr_f32 != nullptr;
     for (int j = tid; j < d; j += kRRT) {
         float x = p.q[(size_t)q * d + j];
@@ -604,58 +616,85 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
     int np = 1;
     while (np < nc) np <<= 1;
-    for (int c = tid; c < np; c += kRRT) {
-        uint64_t ek = kKeyNone;
+    const int grp = tid >> 2, sub = tid & 3;
+    for (int c0 = 0; c0 < np; c0 += kRRT / 4) {
+        const int c = c0 + grp;
+        bool live = false, dl = false;
+        uint64_t key = kKeyNone;
         if (c < nc && (c >= R || c < tq)) {
-            const bool dl = c >= R;
+            dl = c >= R;
             const uint64_t* src = dl ? s1d + (size_t)q * Rd : s1m + (size_t)q * R;
             const int j = dl ? c - R : c;
-            const uint64_t key = src[j];
+            key = src[j];
             // a list probed twice repeats its keys: rerank each position once,
             // except when the per-candidate keys go to a cross-shard merge
-            if (key != kKeyNone && (out_exm || !(j > 0 && src[j - 1] == key))) {
-                const ListStore& S = dl ? p.delta : p.main;
-                const int64_t lp = local_pos(S, key_lo(key), nlist);
-                uint32_t hi;
-                if (f32) {
-                    const float4* row = reinterpret_cast<const float4*>(S.rr_f32 + (size_t)lp * d);
-                    float s = 0.f;
-                    for (int w = 0; w < d / 4; ++w) {
-                        float4 v = __ldg(row + w);
-                        float x0 = __fsub_rn(sq[4 * w + 0], v.x);
-                        s = __fadd_rn(s, __fmul_rn(x0, x0));
-                        float x1 = __fsub_rn(sq[4 * w + 1], v.y);
-                        s = __fadd_rn(s, __fmul_rn(x1, x1));
-                        float x2 = __fsub_rn(sq[4 * w + 2], v.z);
-                        s = __fadd_rn(s, __fmul_rn(x2, x2));
-                        float x3 = __fsub_rn(sq[4 * w + 3], v.w);
-                        s = __fadd_rn(s, __fmul_rn(x3, x3));
-                    }
-                    hi = __float_as_uint(s);
+            live = key != kKeyNone && (out_exm || !(j > 0 && src[j - 1] == key));
+        }
+        const ListStore& S = dl ? p.delta : p.main;
+        const int64_t lp = live ? local_pos(S, key_lo(key), nlist) : 0;
+        uint32_t hi;
+        if (f32) {
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            if (live) {
+                const float4* row = reinterpret_cast<const float4*>(S.rr_f32 + (size_t)lp * d) + sub;
+                const float4* qv = reinterpret_cast<const float4*>(sq) + sub;
+                auto step = [&](const float4 v, const float4 u) {
+                    const float x0 = __fsub_rn(u.x, v.x), x1 = __fsub_rn(u.y, v.y);
+                    const float x2 = __fsub_rn(u.z, v.z), x3 = __fsub_rn(u.w, v.w);
+                    a0 = __fmaf_rn(x0, x0, a0);
+                    a1 = __fmaf_rn(x1, x1, a1);
+                    a2 = __fmaf_rn(x2, x2, a2);
+                    a3 = __fmaf_rn(x3, x3, a3);
+                };
+                if constexpr (NB > 0) {
+                    float4 v[NB];
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) v[t] = __ldg(row + 4 * t);
+#pragma unroll
+                    for (int t = 0; t < NB; ++t) step(v[t], qv[4 * t]);
                 } else {
-                    const uint4* row = reinterpret_cast<const uint4*>(S.rr_u8 + (size_t)lp * d);
-                    const uint4* qq = reinterpret_cast<const uint4*>(squ);
-                    uint32_t acc = 0;
-                    for (int w = 0; w < d / 16; ++w) {
-                        uint4 v = __ldg(row + w), u = qq[w];
-                        uint32_t a;
-                        a = __vabsdiffu4(v.x, u.x); acc = __dp4a(a, a, acc);
-                        a = __vabsdiffu4(v.y, u.y); acc = __dp4a(a, a, acc);
-                        a = __vabsdiffu4(v.z, u.z); acc = __dp4a(a, a, acc);
-                        a = __vabsdiffu4(v.w, u.w); acc = __dp4a(a, a, acc);
-                    }
-                    hi = acc;
+                    for (int t = 0; t < nb; ++t) step(__ldg(row + 4 * t), qv[4 * t]);
                 }
-                const uint32_t id = S.ids ? (uint32_t)S.ids[lp] : key_lo(key);
-                ek = make_key(hi, id);
             }
+            // lanes l and l + 8 are threads sub and sub ^ 2; l and l + 4 are sub and sub ^ 1
+            a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 2));
+            a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 2));
+            a2 = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, 2));
+            a3 = __fadd_rn(a3, __shfl_xor_sync(0xffffffffu, a3, 2));
+            a0 = __fadd_rn(a0, __shfl_xor_sync(0xffffffffu, a0, 1));
+            a1 = __fadd_rn(a1, __shfl_xor_sync(0xffffffffu, a1, 1));
+            a2 = __fadd_rn(a2, __shfl_xor_sync(0xffffffffu, a2, 1));
+            a3 = __fadd_rn(a3, __shfl_xor_sync(0xffffffffu, a3, 1));
+            hi = __float_as_uint(__fadd_rn(__fadd_rn(a0, a2), __fadd_rn(a1, a3)));
+        } else {
+            uint32_t acc = 0;
+            if (live) {
+                const uint4* row = reinterpret_cast<const uint4*>(S.rr_u8 + (size_t)lp * d);
+                const uint4* qq = reinterpret_cast<const uint4*>(squ);
+                for (int w = sub; w < nb; w += 4) {
+                    const uint4 v = __ldg(row + w), u = qq[w];
+                    uint32_t a;
+                    a = __vabsdiffu4(v.x, u.x); acc = __dp4a(a, a, acc);
+                    a = __vabsdiffu4(v.y, u.y); acc = __dp4a(a, a, acc);
+                    a = __vabsdiffu4(v.z, u.z); acc = __dp4a(a, a, acc);
+                    a = __vabsdiffu4(v.w, u.w); acc = __dp4a(a, a, acc);
+                }
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            hi = acc;
         }
-        if (c < nc && out_exm) {
-            if (c < R) out_exm[(size_t)q * R + c] = ek;
-            else out_exd[(size_t)q * Rd + (c - R)] = ek;
+        if (sub == 0 && c < np) {
+            uint64_t ek = kKeyNone;
+            if (live) ek = make_key(hi, S.ids ? (uint32_t)S.ids[lp] : key_lo(key));
+            if (c < nc && out_exm) {
+                if (c < R) out_exm[(size_t)q * R + c] = ek;
+                else out_exd[(size_t)q * Rd + (c - R)] = ek;
+            }
+            sk[c] = ek;
         }
-        sk[c] = ek;
     }
+    __syncthreads();
     if (out_exm) return;
     block_bitonic_sort<kRRT>(sk, np);
     for (int j = tid; j < k; j += kRRT) {
@@ -890,12 +929,22 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
     while (np < nc) np <<= 1;
     if (!out_exact_main && np < k) return cudaErrorInvalidValue;
     size_t smem = sizeof(uint64_t) * np;
-    cudaError_t e = cudaFuncSetAttribute(pq_rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
-    if (e) return e;
-    note_launch();
-    pq_rerank_kernel<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist,
-                                             out_exact_main, out_exact_delta, take);
-    return cudaGetLastError();
+    auto go = [&](auto kern) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        if (e) return e;
+        note_launch();
+        kern<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist, out_exact_main,
+                                     out_exact_delta, take);
+        return cudaGetLastError();
+    };
+    switch (p.main.rr_f32 ? p.d / 16 : 0) {
+        case 2: return go(pq_rerank_kernel<2>);
+        case 3: return go(pq_rerank_kernel<3>);
+        case 4: return go(pq_rerank_kernel<4>);
+        case 6: return go(pq_rerank_kernel<6>);
+        case 8: return go(pq_rerank_kernel<8>);
+        default: return go(pq_rerank_kernel<0>);
+    }
 }
 
 cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main, int n_main, int R,

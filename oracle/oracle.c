@@ -13,7 +13,9 @@
  *
  * Arithmetic rules (compile with -O2 -ffp-contract=off, never -ffast-math):
  *   - every float sum is sequential in index order, products are rounded
- *     before they are added (no fused multiply-add);
+ *     before they are added (no fused multiply-add), except the fp32 rerank
+ *     distance, which restates the reference's AVX-512 arithmetic (16 lane
+ *     accumulators with explicit fmaf, then a pairwise tree; l2_f32_rerank);
  *   - every top-k / top-R is a total order on (distance, id) pairs, so ties
  *     are broken by the smaller id (or position) and results are
  *     schedule-independent.
@@ -175,6 +177,38 @@ static inline int32_t l2_u8(const uint8_t* a, const uint8_t* b, int d) {
 }
 
 /*
+ * fp32 rerank distance as the reference computes it on AVX-512 hosts
+ * (cuda/search/cpu_fine/cpu_fine_kernels_pq_resid.cpp:106-131, l2_sq_fp32):
+ * for each full block of 16 dimensions, lane l (0..15) accumulates
+ * acc[l] = fma(x, x, acc[l]) with x = q[i + l] - v[i + l] rounded first; the
+ * 16 lanes are then summed as a pairwise tree -- lane l with lane l + 8, then
+ * + 4, + 2, + 1 -- which is the order of the 512-bit horizontal add it calls
+ * (checked bit for bit against that intrinsic, with and without -ffast-math,
+ * over 2M random vectors).  Dimensions past the last full block are added
+ * sequentially with fma (the reference's scalar tail under contraction; the
+ * device library accepts only d % 16 == 0, where there is no tail).
+ */
+static inline float l2_f32_rerank(const float* q, const float* v, int d) {
+    float acc[16];
+    for (int l = 0; l < 16; ++l) acc[l] = 0.0f;
+    int i = 0;
+    for (; i + 16 <= d; i += 16) {
+        for (int l = 0; l < 16; ++l) {
+            float x = q[i + l] - v[i + l];
+            acc[l] = fmaf(x, x, acc[l]);
+        }
+    }
+    for (int w = 8; w >= 1; w >>= 1)
+        for (int l = 0; l < w; ++l) acc[l] = acc[l] + acc[l + w];
+    float s = acc[0];
+    for (; i < d; ++i) {
+        float x = q[i] - v[i];
+        s = fmaf(x, x, s);
+    }
+    return s;
+}
+
+/*
  * Exact int32 L2 over the probed lists -> top-k by (dist, original id).
  * Probe ids outside [0, nlist) are skipped; a list probed twice contributes
  * its vectors twice (as the reference does).  Output: original ids and int32
@@ -289,7 +323,7 @@ static void pq_stage1(const pq_segment* s, const float* q, const float* cent, in
  *  stage 1: main top-rerank_n by (ADC, position); delta top-delta_topk by
  *           (ADC, delta position) when a delta segment is given;
  *  stage 2: unique candidates reranked exactly -- int32 L2 on u8 vectors
- *           (query = make_query_u8(q)) or sequential fp32 L2 -- and the top-k
+ *           (query = make_query_u8(q)) or fp32 L2 (l2_f32_rerank) -- and the top-k
  *           kept by (exact distance, final id).
  *
  * Final ids: main -> r2o[position] (or position), delta -> delta ids[position].
@@ -349,7 +383,7 @@ ORACLE_API int oracle_pq_search(
                 uint32_t id = s->ids ? (uint32_t)s->ids[pos] : pos;
                 float e;
                 if (use_f32_rerank) {
-                    e = l2_f32(qq, s->raw_f32 + (size_t)pos * d, d);
+                    e = l2_f32_rerank(qq, s->raw_f32 + (size_t)pos * d, d);
                 } else {
                     e = (float)l2_u8(qu8, s->raw_u8 + (size_t)pos * d, d);
                 }
