@@ -558,8 +558,8 @@ __global__ void __launch_bounds__(kFT, 1)
     unsigned char* sB = sm + a_bytes;                          // tiles [kFStages][b_bytes], later s_lv, s_key
     float* s_lv = reinterpret_cast<float*>(sB);                                   // [2][128][kFLMax]
     uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [kFT][kFList / 2]
-    float* s_lval = reinterpret_cast<float*>(sB + route_fused_region(d));         // [kFT][kFList]
-    uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * kFList);        // [kFT][kFList]
+    float* s_lval = reinterpret_cast<float*>(sB + route_fused_region(d));         // [kFList][kFT]
+    uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * kFList);        // [kFList][kFT]
     float* s_qn = reinterpret_cast<float*>(s_lcol + kFT * kFList);                // [128]
     float* s_T = s_qn + kTCM;                                                     // [128]
     int* s_nc = reinterpret_cast<int*>(s_T + kTCM);                               // [kFT]
@@ -640,8 +640,10 @@ __global__ void __launch_bounds__(kFT, 1)
     float lmax = INF, lim = INF;           // lim = lmax + 2 eps1
     int nc = 0;                            // entries in this thread's list
     bool over = false;                     // the list overflowed within the bound
-    float* myval = s_lval + tid * kFList;
-    uint16_t* mycol = s_lcol + tid * kFList;
+    // entry i of this thread's list at [i][tid]: the lanes of a warp store to 32
+    // different banks whatever their list lengths
+    float* myval = s_lval + tid;
+    uint16_t* mycol = s_lcol + tid;
     int g = 0;
     for (; g < ntiles; ++g) {
         if (tid == 0 && g + 1 < ntiles && !s_fail && !mma_tile(g + 1)) s_fail = 1;
@@ -671,49 +673,56 @@ __global__ void __launch_bounds__(kFT, 1)
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
             const int cb = g * kFN + col0;
             const float cnl = __ldg(cne + cb + lane);       // lane j: squared norm of column cb + j
-            float x[32];
-            bool any = false;
+            // the 32 columns in pieces of kW; before each piece the list must have room
+            // for all of it, else it is pruned to the current bound, and a bound that
+            // no longer thins it (more than kFList - kW survivors) gives up on the row
+            constexpr int kW = LMAX <= 8 ? 32 : (LMAX <= 16 ? 16 : 8);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                x[j] = fmaxf(qn + __shfl_sync(0xffffffffu, cnl, j) - 2.f * __uint_as_float(r[j]), 0.f);
-                any |= x[j] <= lim;
-            }
-            if (any) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (x[j] > lim) continue;
-                    if (over) continue;
-                    if (nc == kFList) {        // full: keep only what is still within the bound
-                        int k2 = 0;
-                        for (int i = 0; i < kFList; ++i)
-                            if (myval[i] <= lim) {
-                                myval[k2] = myval[i];
-                                mycol[k2] = mycol[i];
-                                ++k2;
-                            }
-                        nc = k2;
-                        if (nc > kFList - kFList / 4) {   // the bound no longer thins the list: give up
-                            over = true;
-                            continue;
+            for (int j0 = 0; j0 < 32; j0 += kW) {
+                if (!over && nc > kFList - kW) {
+                    int k2 = 0;
+                    for (int i = 0; i < nc; ++i) {
+                        const float v = myval[i * kFT];
+                        if (v <= lim) {
+                            myval[k2 * kFT] = v;
+                            mycol[k2 * kFT] = mycol[i * kFT];
+                            ++k2;
                         }
                     }
-                    myval[nc] = x[j];
-                    mycol[nc] = (uint16_t)(cb + j);
-                    ++nc;
-                    if (x[j] < lmax) {
-                        float v = x[j];
+                    nc = k2;
+                    if (nc > kFList - kW) {
+                        over = true;
+                        nc = 0;
+                    }
+                }
+                // every column is written at slot nc, which advances only when the
+                // column is within the bound (an abandoned row keeps rewriting slot 0)
+                const int nc0 = nc, adv = over ? 0 : 1;
 #pragma unroll
-                        for (int i = 0; i < LMAX; ++i) {
-                            const float a = lv[i];
-                            lv[i] = fminf(a, v);
+                for (int j = j0; j < j0 + kW; ++j) {
+                    const float xv =
+                        fmaxf(qn + __shfl_sync(0xffffffffu, cnl, j) - 2.f * __uint_as_float(r[j]), 0.f);
+                    myval[nc * kFT] = xv;
+                    mycol[nc * kFT] = (uint16_t)(cb + j);
+                    nc += xv <= lim ? adv : 0;
+                }
+                // the L smallest: only this thread's new entries, so a warp pays for
+                // its busiest lane rather than for every column some lane kept
+                for (int i = nc0; i < nc; ++i) {
+                    float v = myval[i * kFT];
+                    if (v < lmax) {
+#pragma unroll
+                        for (int e = 0; e < LMAX; ++e) {
+                            const float a = lv[e];
+                            lv[e] = fminf(a, v);
                             v = fmaxf(a, v);
                         }
 #pragma unroll
-                        for (int i = 0; i < LMAX; ++i)
-                            if (i == L - 1) lmax = lv[i];
-                        lim = lmax + eps2;
+                        for (int e = 0; e < LMAX; ++e)
+                            if (e == L - 1) lmax = lv[e];
                     }
                 }
+                lim = lmax + eps2;
             }
         }
         asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -763,12 +772,12 @@ __global__ void __launch_bounds__(kFT, 1)
     if (qi < nq && !failed && !big) {
         const float4* qr = reinterpret_cast<const float4*>(q + (size_t)qi * d);
         for (int i = 0; i < nc; ++i) {
-            if (myval[i] > climit) continue;
+            if (myval[i * kFT] > climit) continue;
             if (nk == kFList / 2) {
                 big = true;
                 break;
             }
-            const int c = mycol[i];
+            const int c = mycol[i * kFT];
             const float4* cr = reinterpret_cast<const float4*>(cent + (size_t)c * d);
             float sdist = 0.f;
 #pragma unroll 4
