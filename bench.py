@@ -52,6 +52,12 @@ CONFIGS = {
     "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
                    nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,
                    desc="c1-shaped lists at 1M vectors (profiling case)"),
+    # the c1 routing shape (10k queries, 4096 centroids, d 96, nprobe 8) over 1M
+    # vectors: the routing kernels' work equals c1's, the device holds ~1.5 GB
+    # (profiling case for the routing kernels)
+    "c1-route": dict(kind="f32", n=1_000_000, d=96, ncomp=4096, sigma=0.05, nlist=4096, M=48, train_n=200_000,
+                     nq=10_000, k=10, rerank_n=512, nprobe=8, sweep=(8,), seed=13,
+                     desc="c1 routing shape over 1M vectors (profiling case)"),
     # reduced copy for quick checks of the harness itself (not a bench line)
     "c1-small": dict(kind="f32", n=400_000, d=96, ncomp=512, sigma=0.05, nlist=512, M=48, train_n=100_000,
                      nq=2000, k=10, rerank_n=512, nprobe=16, sweep=(8, 16, 32), seed=7,

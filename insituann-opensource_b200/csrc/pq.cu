@@ -252,8 +252,47 @@ __device__ __forceinline__ void load_tile(const uint4* lanebase, int64_t T, uint
     }
 }
 
+// small asynchronous global -> shared copies (sizes 4 and 8, naturally aligned)
+__device__ __forceinline__ void cp_async_4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_8(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared-memory descriptor of the group a CTA takes next, fetched by thread 0
+// while the current group runs: the packed group word first (stage A), then
+// what it points to (stage B): the list's count, key offset and tile offset
+// and the group's query ids (-1 past its size).
+struct GroupDesc {
+    int64_t pk, koff, goff;
+    int count, q[kGQ];
+};
+
+__device__ __forceinline__ void desc_stage_a(GroupDesc& g, const WorkList& wl, int it, int NG) {
+    cp_async_8(&g.pk, wl.groups + (it >= NG ? it - NG : it));
+}
+
+__device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, const WorkList& wl, int it, int NG) {
+    const int64_t pk = g.pk;
+    const int l = (int)(pk >> 32), p0 = ((int)pk) >> 3, nqg = ((int)pk) & 7;
+    const ListStore& S = it >= NG ? p.delta : p.main;
+    cp_async_4(&g.count, S.counts + l);
+    cp_async_8(&g.koff, (S.key_off ? S.key_off : S.offsets) + l);
+    cp_async_8(&g.goff, S.gring_off + l);
+#pragma unroll
+    for (int k = 0; k < kGQ; ++k) {
+        if (k < nqg) cp_async_4(&g.q[k], wl.pair_q + p0 + k);
+        else g.q[k] = -1;
+    }
+}
+
 // Persistent CTA loop over the work list's groups.  Latency that does not
 // depend on the group is taken off the group's critical path:
+//   * the next group's descriptor is fetched into shared memory during this group;
 //   * the next work item is claimed (atomic) while this group runs;
 //   * the codebook rows a thread needs for its LUT column are requested
 //     before the group is even decoded (they are the same for every group);
@@ -273,7 +312,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     float4* dist4 = lut + 256 * M;                          // [kRChunk] four queries per vector
     float* resid = reinterpret_cast<float*>(dist4);         // [kGQ][d] while the LUT is built
     __shared__ EmitSmem esm;
-    __shared__ int s_item, s_q[kGQ];
+    __shared__ int s_item;
+    __shared__ __align__(8) GroupDesc s_gd;     // the group this CTA starts next
     // per-chunk totals and "some sum may pass" bits of the 4 queries, three
     // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
     // barrier, clears buffer (c + 2) % 3 -- last read in chunk c - 1 (done
@@ -289,7 +329,15 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     const int rid = warp * 4 + grp;          // stripe of this lane group
     if (tid < 3 * kGQ) s_cnt[tid / kGQ][tid % kGQ] = 0;
     if (tid < 3) s_any[tid] = 0;
-    if (tid == 0) s_item = atomicAdd(counter, 1);
+    if (tid == 0) {
+        s_item = atomicAdd(counter, 1);
+        if (s_item < total) {
+            desc_stage_a(s_gd, wl, s_item, NG);
+            cp_async_wait_all();
+            desc_stage_b(s_gd, p, wl, s_item, NG);
+            cp_async_wait_all();
+        }
+    }
     __syncthreads();
     int cpar = 0;                       // buffer of s_cnt / s_any the next chunk adds into
     float cbv[kLB][DSUB];
@@ -320,15 +368,15 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
         if (tid == 0) nxt = atomicAdd(counter, 1);       // used at the end of this group
         if (builder) load_cb(c0);
         const bool seg_delta = it >= NG;
-        const int gi = seg_delta ? it - NG : it;
-        const int64_t packed = wl.groups[gi];
-        const int l = (int)(packed >> 32), p0 = ((int)packed) >> 3, nqg = ((int)packed) & 7;
+        const int64_t packed = s_gd.pk;
+        const int l = (int)(packed >> 32), nqg = ((int)packed) & 7;
         const ListStore& SG = seg_delta ? p.delta : p.main;
         const CandBuf& cb = seg_delta ? cd : cm;
-        const int count = SG.counts[l];
+        const int count = s_gd.count;
+        bool fetched = false;            // thread 0: stage A of the next descriptor issued
         if (count > 0) {
-            const int64_t koff = SG.key_off ? SG.key_off[l] : SG.offsets[l];
-            const uint8_t* tiles = SG.gring + SG.gring_off[l];
+            const int64_t koff = s_gd.koff;
+            const uint8_t* tiles = SG.gring + s_gd.goff;
             const int64_t ntiles = gring_tiles(count);
             // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
             // multiple of 16, so a stripe starts on a tile) and runs through it
@@ -345,15 +393,19 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             const int64_t T0 = a / 16;
             uint32_t w[4 * MPL], wn[4 * MPL];
             load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
-            if (tid < kGQ) s_q[tid] = tid < nqg ? wl.pair_q[p0 + tid] : -1;
             {
                 const float* cv = p.cent + (size_t)l * d;
                 for (int e = tid; e < kGQ * d; e += kRT) {
                     const int k = e / d, x = e - k * d;
-                    const int qk = k < nqg ? wl.pair_q[p0 + k] : -1;
+                    const int qk = s_gd.q[k];
                     resid[e] = qk >= 0 ? __fsub_rn(p.q[(size_t)qk * d + x], cv[x]) : 0.f;
                 }
             }
+            // the group's bounds, requested before the LUT build and used after it
+            uint64_t thr0[kGQ];
+#pragma unroll
+            for (int k = 0; k < kGQ; ++k)
+                thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_gd.q[k])) : 0ull;
             __syncthreads();
             if (builder) {
                 float2 r01[DSUB], r23[DSUB];
@@ -389,27 +441,40 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
             }
             __syncthreads();
+            // the query ids are read before the next group's fetch rewrites them
+            // (its stage B starts after the first chunk's barrier)
             int qid[kGQ];
 #pragma unroll
-            for (int k = 0; k < kGQ; ++k) qid[k] = s_q[k];
+            for (int k = 0; k < kGQ; ++k) qid[k] = s_gd.q[k];
+            if (tid == 0 && nxt < total) {
+                desc_stage_a(s_gd, wl, nxt, NG);
+                fetched = true;
+            }
             float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
             const uint32_t kbase = (uint32_t)koff;
+            // float form of the bounds for the stores' pass test, taken from bounds
+            // already in registers (the group's first, then each chunk's cut): a
+            // bound only decreases, so an older one only sets more bits.  A bound
+            // at or above +inf bits admits everything: its bit is forced on.
+            float4 thf;
+            uint32_t force;
+            auto set_thf = [&](const uint64_t (&b)[kGQ]) {
+                float tf[kGQ];
+                force = 0;
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k) {
+                    const uint32_t hi = (uint32_t)(b[k] >> 32);
+                    tf[k] = k < nqg && hi < 0x7f800000u ? __uint_as_float(hi) : -1.f;
+                    if (k < nqg && hi >= 0x7f800000u) force |= 1u << k;
+                }
+                thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
+            };
+            set_thf(thr0);
             for (int t = 0; t < nchunks; ++t) {
                 uint64_t thr[kGQ];    // read now, used after the steps: a bound only ever decreases
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
-                // float form of the bounds for the stores' pass test; a bound at or
-                // above +inf bits admits everything, its bit is forced on
-                float tf[kGQ];
-                uint32_t force = 0;
-#pragma unroll
-                for (int k = 0; k < kGQ; ++k) {
-                    const uint32_t hi = (uint32_t)(thr[k] >> 32);
-                    tf[k] = k < nqg && hi < 0x7f800000u ? __uint_as_float(hi) : -1.f;
-                    if (k < nqg && hi >= 0x7f800000u) force |= 1u << k;
-                }
-                const float4 thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
                 uint32_t maybe = 0;
 #pragma unroll 1
                 for (int tl = 0; tl < kRSteps / 16; ++tl) {
@@ -428,11 +493,16 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 maybe = __reduce_or_sync(0xffffffffu, maybe);
                 if (lane == 0 && (maybe | force)) atomicOr(&s_any[cpar], maybe | force);
                 __syncthreads();
+                if (t == 0 && tid == 0 && fetched) {         // stage A landed long ago
+                    cp_async_wait_all();
+                    desc_stage_b(s_gd, p, wl, nxt, NG);
+                }
                 const int cfree = cpar == 0 ? 2 : cpar - 1;      // (cpar + 2) % 3
                 if (tid < kGQ) s_cnt[cfree][tid] = 0;
                 if (tid == 0) s_any[cfree] = 0;
                 if (s_any[cpar] == 0) {          // no sum of the chunk can pass any bound
                     cpar = cpar == 2 ? 0 : cpar + 1;
+                    set_thf(thr);
                     continue;
                 }
                 // thread t reads the slots t + kRT*e: group t/64 + 4e, chunk step
@@ -493,9 +563,18 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     if (k < nqg && totk[k] > 0)
                         warp_append_items<kE>([&](int e) { return key_of(e, k); }, cut[k], cb, qid[k]);
                 if (sel) __syncthreads();     // the histograms lived in the slots
+                set_thf(cut);
             }
         }
-        if (tid == 0) s_item = nxt;
+        if (tid == 0) {
+            if (nxt < total && !fetched) {    // an empty list: fetch the next descriptor now
+                desc_stage_a(s_gd, wl, nxt, NG);
+                cp_async_wait_all();
+                desc_stage_b(s_gd, p, wl, nxt, NG);
+            }
+            cp_async_wait_all();
+            s_item = nxt;
+        }
         __syncthreads();
     }
 }
