@@ -474,12 +474,27 @@ def main():
     h_ids = torch.empty((nq, k), dtype=torch.int32).pin_memory()
     h_dist = torch.empty((nq, k), dtype=torch.float32).pin_memory()
 
-    def e2e_step():
-        batch.stage1_prepare_ptr(hq.data_ptr(), nq)
+    # N = 1: two batch contexts in flight, as the reference's pipeline API is
+    # meant to be driven -- while the host waits for one batch's results
+    # (ivf_pipeline_get_results copies them and synchronises that batch's
+    # stream), the next batch's upload and search are already queued on the
+    # other context's stream.  Every step still uploads its queries from pinned
+    # host memory and reads its results back to the host.
+    batches = [batch, ib.Batch(nq, d, max(nprobe, max(cfg["sweep"])), k, nlist)] if N == 1 else [batch]
+
+    def e2e_issue(b):
+        b.stage1_prepare_ptr(hq.data_ptr(), nq)
+        b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=False, route=True)
+
+    def e2e_run(n):
         if N == 1:
-            batch.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=False, route=True)
-            batch.get_results_into(h_dist.data_ptr(), h_ids.data_ptr(), nq, k)
-        else:
+            e2e_issue(batches[0])
+            for i in range(n):
+                if i + 1 < n:
+                    e2e_issue(batches[(i + 1) % 2])
+                batches[i % 2].get_results_into(h_dist.data_ptr(), h_ids.data_ptr(), nq, k)
+            return
+        for _ in range(n):
             with torch.cuda.stream(ext):
                 q_dev.copy_(hq, non_blocking=True)
             step()
@@ -489,17 +504,21 @@ def main():
                     h_dist.copy_(all_dist.reshape(nq, k), non_blocking=True)
             ext.synchronize()
 
-    for _ in range(args.warmup):
-        e2e_step()
+    e2e_run(args.warmup)
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(ext)
-    for _ in range(args.steps):
-        e2e_step()
+    e2e_run(args.steps)
     e1.record(ext)
     barrier()
     e_ms = e0.elapsed_time(e1)
+    if N == 1:
+        # both contexts searched the same queries: their results must agree
+        ids_b, _ = batches[1].get_results(nq, k)
+        if not np.array_equal(ids_b, h_ids.numpy()):
+            raise RuntimeError("the two batch contexts of the e2e pipeline returned different results")
+        batches[1].close()
     if N > 1:
         t = torch.tensor([e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)

@@ -543,10 +543,11 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
         uint64_t* d_out = nullptr;
         {
             StageScope stage(b, IVF_STAGE_SELECT);
-            ck(select_top_r(cm, n, m_out, b->st), "select_top_r");
+            // sorted stage-1 lists only where they leave the library (shard outputs)
+            ck(select_top_r(cm, n, m_out, b->st, adc != nullptr), "select_top_r");
             if (use_delta) {
                 d_out = dadc ? dadc + (size_t)s * Rd : s1d;
-                ck(select_top_r(cd, n, d_out, b->st), "select_top_r (delta)");
+                ck(select_top_r(cd, n, d_out, b->st, adc != nullptr), "select_top_r (delta)");
             }
         }
         StageScope stage(b, IVF_STAGE_RERANK);

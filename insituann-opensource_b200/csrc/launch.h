@@ -77,8 +77,9 @@ cudaError_t make_query_u8(const float* q, size_t n, uint8_t* out, cudaStream_t s
 
 // ---- candidate selection (select.cu) ---------------------------------------
 cudaError_t reset_candidates(CandBuf cb, int nq, cudaStream_t st);
-// Sorted top-R keys per query from a candidate buffer -> out [nq, R] (padding ~0).
-cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st);
+// Top-R keys per query from a candidate buffer -> out [nq, R] (padding ~0), ascending
+// when sorted, else the same keys in no particular order.
+cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st, bool sorted = true);
 // Sorted exact keys -> (ids, int32 distances): for the exact path.
 cudaError_t keys_to_exact_results(const uint64_t* keys, int nq, int k, int32_t* ids, int32_t* dist,
                                   float* fdist, cudaStream_t st);

@@ -646,6 +646,9 @@ cudaError_t launch_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf c
 // rerank
 // ---------------------------------------------------------------------------
 constexpr int kRRT = 256;
+// slots of the rerank's repeat table for np candidates: at least twice np and
+// room for the per-warp top-k lists (8 warps x 16)
+__host__ __device__ constexpr int rr_table(int np) { return 2 * np > 256 ? 2 * np : 256; }
 constexpr int kRRMax = 4096;  // R + Rd candidates per query
 
 // local position of a ranking-key position (shards rank by global positions)
@@ -664,6 +667,62 @@ __device__ __forceinline__ uint8_t to_u8(float x) {  // updates/exact_update.cu:
     return (uint8_t)lroundf(x);
 }
 
+// Inserts key into an open-addressing table of mask + 1 slots (empty =
+// kKeyNone); true for the first insertion of a key, false for a repeat.  The
+// table has at least twice as many slots as keys, so the probe loop ends.
+__device__ __forceinline__ bool hash_first(unsigned long long* tab, int mask, uint64_t key) {
+    int h = (int)((key * 0x9E3779B97F4A7C15ull) >> 40) & mask;
+    for (int probe = 0; probe <= mask; ++probe) {
+        const unsigned long long old = atomicCAS(&tab[h], (unsigned long long)kKeyNone, (unsigned long long)key);
+        if (old == kKeyNone) return true;
+        if (old == key) return false;
+        h = (h + 1) & mask;
+    }
+    return false;
+}
+
+// The k smallest of src[0 .. n) (n <= 32 E), ascending, into dst[0 .. k)
+// (kKeyNone past the last key), by one warp: k rounds of a warp-wide minimum
+// by (key, slot), each removing exactly one copy, so equal keys of different
+// candidates are all kept.
+template <int E>
+__device__ void warp_smallest_k(const uint64_t* src, int n, int k, uint64_t* dst) {
+    const int lane = threadIdx.x & 31;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = e * 32 + lane < n ? src[e * 32 + lane] : kKeyNone;
+    for (int it = 0; it < k; ++it) {
+        uint64_t m = kKeyNone;
+        int mi = lane;
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+            if (v[e] < m) {
+                m = v[e];
+                mi = e * 32 + lane;
+            }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const uint64_t om = __shfl_xor_sync(0xffffffffu, m, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
+            if (om < m || (om == m && oi < mi)) {
+                m = om;
+                mi = oi;
+            }
+        }
+        if (lane == 0) dst[it] = m;
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+            if (mi == e * 32 + lane) v[e] = kKeyNone;
+    }
+}
+
+// n <= 128
+__device__ __forceinline__ void warp_smallest_k_dispatch(const uint64_t* src, int n, int k, uint64_t* dst) {
+    if (n <= 32) warp_smallest_k<1>(src, n, k, dst);
+    else if (n <= 64) warp_smallest_k<2>(src, n, k, dst);
+    else warp_smallest_k<4>(src, n, k, dst);
+}
+
 // Exact rerank of one query's stage-1 candidates (CTA per query).  Four threads
 // share a candidate row: for the fp32 distance thread `sub` owns the lanes
 // 4 sub .. 4 sub + 3 of the reference's 16-lane AVX-512 arithmetic
@@ -679,22 +738,26 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
                                                          int R, const uint64_t* __restrict__ s1d, int Rd, int k,
                                                          int32_t* out_ids, float* out_dist, uint64_t* out_exm,
                                                          uint64_t* out_exd, const int32_t* __restrict__ take) {
-    extern __shared__ uint64_t sk[];
+    extern __shared__ uint64_t sk[];            // [np] exact keys, then a table of rr_table(np) slots
     __shared__ __align__(16) float sq[kPMaxD];
     __shared__ __align__(16) uint8_t squ[kPMaxD];
-    const int q = blockIdx.x, tid = threadIdx.x, d = p.d;
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, d = p.d;
     const int nb = NB ? NB : d / 16;
     const bool f32 = p.main.rr_f32 != nullptr;
+    const int nc = R + Rd;
+    const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
+    int np = 1;
+    while (np < nc) np <<= 1;
+    unsigned long long* tab = reinterpret_cast<unsigned long long*>(sk + np);
+    const int tmask = rr_table(np) - 1;
     for (int j = tid; j < d; j += kRRT) {
         float x = p.q[(size_t)q * d + j];
         sq[j] = x;
         squ[j] = to_u8(x);
     }
+    if (!out_exm)
+        for (int i = tid; i <= tmask; i += kRRT) tab[i] = kKeyNone;
     __syncthreads();
-    const int nc = R + Rd;
-    const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
-    int np = 1;
-    while (np < nc) np <<= 1;
     const int grp = tid >> 2, sub = tid & 3;
     for (int c0 = 0; c0 < np; c0 += kRRT / 4) {
         const int c = c0 + grp;
@@ -705,10 +768,13 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
             const uint64_t* src = dl ? s1d + (size_t)q * Rd : s1m + (size_t)q * R;
             const int j = dl ? c - R : c;
             key = src[j];
-            // a list probed twice repeats its keys: rerank each position once,
-            // except when the per-candidate keys go to a cross-shard merge
-            live = key != kKeyNone && (out_exm || !(j > 0 && src[j - 1] == key));
+            // the per-candidate keys of a cross-shard merge keep every entry; the
+            // final top-k reranks each position once (a list probed twice repeats
+            // its keys in stage 1; delta keys are told apart by bit 63)
+            if (out_exm) live = key != kKeyNone;
+            else if (sub == 0 && key != kKeyNone) live = hash_first(tab, tmask, dl ? (key | (1ull << 63)) : key);
         }
+        if (!out_exm) live = __shfl_sync(0xffffffffu, live, lane & ~3);
         const ListStore& S = dl ? p.delta : p.main;
         const int64_t lp = live ? local_pos(S, key_lo(key), nlist) : 0;
         uint32_t hi;
@@ -775,6 +841,27 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     }
     __syncthreads();
     if (out_exm) return;
+    if (k <= 16 && np <= 512) {
+        // each warp's k smallest of its slice of at most 64 (into the table
+        // region, free now), then warp 0's k smallest of those (at most 128)
+        uint64_t* cand = reinterpret_cast<uint64_t*>(tab);
+        const int w = tid >> 5, per = (np + kRRT / 32 - 1) / (kRRT / 32);
+        const int lo = w * per, nw = lo < np ? min(per, np - lo) : 0;
+        warp_smallest_k_dispatch(sk + lo, nw, k, cand + w * k);
+        __syncthreads();
+        if (w == 0) {
+            warp_smallest_k_dispatch(cand, (kRRT / 32) * k, k, sk);
+            __syncwarp();
+            if (lane < k) {
+                const uint64_t ek = sk[lane];
+                const bool ok = ek != kKeyNone;
+                out_ids[(size_t)q * k + lane] = ok ? (int32_t)key_lo(ek) : -1;
+                out_dist[(size_t)q * k + lane] =
+                    ok ? (f32 ? __uint_as_float(key_hi(ek)) : (float)key_hi(ek)) : __int_as_float(0x7f800000);
+            }
+        }
+        return;
+    }
     block_bitonic_sort<kRRT>(sk, np);
     for (int j = tid; j < k; j += kRRT) {
         const uint64_t ek = j < np ? sk[j] : kKeyNone;
@@ -1007,9 +1094,9 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
     int np = 1;
     while (np < nc) np <<= 1;
     if (!out_exact_main && np < k) return cudaErrorInvalidValue;
-    size_t smem = sizeof(uint64_t) * np;
+    const size_t smem = sizeof(uint64_t) * ((size_t)np + (out_exact_main ? 0 : rr_table(np)));
     auto go = [&](auto kern) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
         if (e) return e;
         note_launch();
         kern<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist, out_exact_main,

@@ -25,13 +25,15 @@ __global__ void reset_kernel(int32_t* cnt, unsigned long long* thr, int nq) {
 // registers (one coalesced read) and the R-th key is found by a radix descent
 // over the registers; longer buffers are read from global memory on every
 // pass.  The keys below the R-th are compacted to shared memory and only
-// those R are sorted.
+// those R are sorted -- or written as they are when the consumer does not
+// need the order (sorted == 0: the single-GPU rerank, which removes repeated
+// positions by hashing and selects its top-k itself).
 constexpr int kSelT = 256;
 constexpr int kSelItems = 16;
 
 __global__ void __launch_bounds__(kSelT) select_top_r_kernel(const uint64_t* __restrict__ keys,
                                                              const int32_t* __restrict__ cnt, int cap, int R,
-                                                             uint64_t* __restrict__ out) {
+                                                             uint64_t* __restrict__ out, int sorted) {
     extern __shared__ uint64_t s[];
     __shared__ int hist[256];
     __shared__ int bc[4];
@@ -44,6 +46,10 @@ __global__ void __launch_bounds__(kSelT) select_top_r_kernel(const uint64_t* __r
     int Rp = 1;
     while (Rp < R) Rp <<= 1;
     if (n <= R) {                     // every key is kept
+        if (!sorted) {
+            for (int i = tid; i < R; i += kSelT) out[(size_t)q * R + i] = i < n ? kk[i] : kKeyNone;
+            return;
+        }
         for (int i = tid; i < Rp; i += kSelT) s[i] = i < n ? kk[i] : kKeyNone;
         block_bitonic_sort<kSelT>(s, Rp);
         for (int i = tid; i < R; i += kSelT) out[(size_t)q * R + i] = s[i];
@@ -81,7 +87,8 @@ __global__ void __launch_bounds__(kSelT) select_top_r_kernel(const uint64_t* __r
     __syncthreads();
     const int cl = s_cnt;
     for (int i = cl + tid; i < Rp; i += kSelT) s[i] = i < R ? kap : kKeyNone;   // copies of kappa fill to R
-    block_bitonic_sort<kSelT>(s, Rp);
+    if (sorted) block_bitonic_sort<kSelT>(s, Rp);
+    else __syncthreads();
     for (int i = tid; i < R; i += kSelT) out[(size_t)q * R + i] = s[i];
 }
 
@@ -105,7 +112,7 @@ cudaError_t reset_candidates(CandBuf cb, int nq, cudaStream_t st) {
     return cudaGetLastError();
 }
 
-cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st) {
+cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st, bool sorted) {
     if (nq <= 0) return cudaSuccess;
     int Rp = 1;
     while (Rp < cb.R) Rp <<= 1;
@@ -115,7 +122,7 @@ cudaError_t select_top_r(CandBuf cb, int nq, uint64_t* out, cudaStream_t st) {
         cudaFuncSetAttribute(select_top_r_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
     if (e) return e;
     note_launch();
-    select_top_r_kernel<<<nq, kSelT, smem, st>>>(cb.keys, cb.cnt, cb.cap, cb.R, out);
+    select_top_r_kernel<<<nq, kSelT, smem, st>>>(cb.keys, cb.cnt, cb.cap, cb.R, out, sorted ? 1 : 0);
     return cudaGetLastError();
 }
 
