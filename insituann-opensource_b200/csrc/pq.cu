@@ -683,8 +683,10 @@ __device__ __forceinline__ bool hash_first(unsigned long long* tab, int mask, ui
 
 // The k smallest of src[0 .. n) (n <= 32 E), ascending, into dst[0 .. k)
 // (kKeyNone past the last key), by one warp: k rounds of a warp-wide minimum
-// by (key, slot), each removing exactly one copy, so equal keys of different
-// candidates are all kept.
+// (high word, then low word among the lanes that hold the high minimum, both
+// by the warp's min-reduction), each removing exactly one copy -- the lowest
+// lane's first slot holding it -- so equal keys of different candidates are
+// all kept.
 template <int E>
 __device__ void warp_smallest_k(const uint64_t* src, int n, int k, uint64_t* dst) {
     const int lane = threadIdx.x & 31;
@@ -692,27 +694,24 @@ __device__ void warp_smallest_k(const uint64_t* src, int n, int k, uint64_t* dst
 #pragma unroll
     for (int e = 0; e < E; ++e) v[e] = e * 32 + lane < n ? src[e * 32 + lane] : kKeyNone;
     for (int it = 0; it < k; ++it) {
-        uint64_t m = kKeyNone;
-        int mi = lane;
+        uint64_t m = v[0];
+        int ms = 0;
 #pragma unroll
-        for (int e = 0; e < E; ++e)
+        for (int e = 1; e < E; ++e)
             if (v[e] < m) {
                 m = v[e];
-                mi = e * 32 + lane;
+                ms = e;
             }
+        const uint32_t hi = __reduce_min_sync(0xffffffffu, key_hi(m));
+        const uint32_t lo = __reduce_min_sync(0xffffffffu, key_hi(m) == hi ? key_lo(m) : 0xFFFFFFFFu);
+        const uint64_t wm = ((uint64_t)hi << 32) | lo;
+        const unsigned holders = __ballot_sync(0xffffffffu, m == wm);
+        if (lane == 0) dst[it] = wm;
+        if (lane == __ffs(holders) - 1) {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const uint64_t om = __shfl_xor_sync(0xffffffffu, m, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, mi, o);
-            if (om < m || (om == m && oi < mi)) {
-                m = om;
-                mi = oi;
-            }
+            for (int e = 0; e < E; ++e)
+                if (e == ms) v[e] = kKeyNone;
         }
-        if (lane == 0) dst[it] = m;
-#pragma unroll
-        for (int e = 0; e < E; ++e)
-            if (mi == e * 32 + lane) v[e] = kKeyNone;
     }
 }
 
@@ -738,7 +737,7 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
                                                          int R, const uint64_t* __restrict__ s1d, int Rd, int k,
                                                          int32_t* out_ids, float* out_dist, uint64_t* out_exm,
                                                          uint64_t* out_exd, const int32_t* __restrict__ take) {
-    extern __shared__ uint64_t sk[];            // [np] exact keys, then a table of rr_table(np) slots
+    extern __shared__ uint64_t sk[];            // [np] exact keys, [np] stage-1 keys, a table of rr_table(np) slots
     __shared__ __align__(16) float sq[kPMaxD];
     __shared__ __align__(16) uint8_t squ[kPMaxD];
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, d = p.d;
@@ -748,13 +747,19 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
     int np = 1;
     while (np < nc) np <<= 1;
-    unsigned long long* tab = reinterpret_cast<unsigned long long*>(sk + np);
+    uint64_t* s1 = sk + np;
+    unsigned long long* tab = reinterpret_cast<unsigned long long*>(sk + 2 * np);
     const int tmask = rr_table(np) - 1;
     for (int j = tid; j < d; j += kRRT) {
         float x = p.q[(size_t)q * d + j];
         sq[j] = x;
         squ[j] = to_u8(x);
     }
+    // every candidate's stage-1 key in one coalesced pass (kKeyNone past the
+    // shard's requested prefix and past the end)
+    for (int c = tid; c < np; c += kRRT)
+        s1[c] = c < R ? (c < tq ? s1m[(size_t)q * R + c] : kKeyNone)
+                      : (c < nc ? s1d[(size_t)q * Rd + (c - R)] : kKeyNone);
     if (!out_exm)
         for (int i = tid; i <= tmask; i += kRRT) tab[i] = kKeyNone;
     __syncthreads();
@@ -763,11 +768,9 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
         const int c = c0 + grp;
         bool live = false, dl = false;
         uint64_t key = kKeyNone;
-        if (c < nc && (c >= R || c < tq)) {
+        if (c < np) {
             dl = c >= R;
-            const uint64_t* src = dl ? s1d + (size_t)q * Rd : s1m + (size_t)q * R;
-            const int j = dl ? c - R : c;
-            key = src[j];
+            key = s1[c];
             // the per-candidate keys of a cross-shard merge keep every entry; the
             // final top-k reranks each position once (a list probed twice repeats
             // its keys in stage 1; delta keys are told apart by bit 63)
@@ -1094,9 +1097,9 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
     int np = 1;
     while (np < nc) np <<= 1;
     if (!out_exact_main && np < k) return cudaErrorInvalidValue;
-    const size_t smem = sizeof(uint64_t) * ((size_t)np + (out_exact_main ? 0 : rr_table(np)));
+    const size_t smem = sizeof(uint64_t) * (2 * (size_t)np + (out_exact_main ? 0 : rr_table(np)));
     auto go = [&](auto kern) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 112 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 136 * 1024);
         if (e) return e;
         note_launch();
         kern<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist, out_exact_main,
