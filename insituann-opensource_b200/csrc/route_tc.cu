@@ -526,7 +526,8 @@ constexpr int kFStages = 2;               // operand tiles in flight
 // the tile region holds the operand tiles, then the L-lists, then the exact keys
 __host__ __device__ constexpr size_t route_fused_region(int d) {
     const size_t tiles = kFStages * (size_t)kFN * 3 * d * 2;
-    const size_t keys = sizeof(uint64_t) * kFT * (kFList / 2), lists = sizeof(float) * 2 * kTCM * kFLMax;
+    const size_t keys = (sizeof(uint64_t) + sizeof(uint16_t)) * kFT * (kFList / 2),
+                 lists = sizeof(float) * kTCM * kFLMax;
     const size_t m = keys > lists ? keys : lists;
     return tiles > m ? tiles : m;
 }
@@ -549,15 +550,17 @@ __global__ void __launch_bounds__(kFT, 1)
     __shared__ __align__(8) uint64_t bar_mma[2];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
+    __shared__ int s_scan[33];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int quarter = warp & 3, half = warp >> 2;
     const int row = quarter * 32 + lane;                  // TMEM lane = query row of this thread
-    const int K = 3 * d, K8 = K / 8;
+    const int K = 3 * d;
     const uint32_t a_bytes = (uint32_t)kTCM * K * 2, b_bytes = (uint32_t)kFN * K * 2;
     unsigned char* sA = sm;
     unsigned char* sB = sm + a_bytes;                          // tiles [kFStages][b_bytes], later s_lv, s_key
-    float* s_lv = reinterpret_cast<float*>(sB);                                   // [2][128][kFLMax]
-    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [kFT][kFList / 2]
+    float* s_lv = reinterpret_cast<float*>(sB);                                   // [LMAX][128] (half 1)
+    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [kFList / 2][kFT]
+    uint16_t* s_pair = reinterpret_cast<uint16_t*>(s_key + kFT * (kFList / 2));   // [kFT * kFList / 2]
     float* s_lval = reinterpret_cast<float*>(sB + route_fused_region(d));         // [kFList][kFT]
     uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * kFList);        // [kFList][kFT]
     float* s_qn = reinterpret_cast<float*>(s_lcol + kFT * kFList);                // [128]
@@ -580,17 +583,43 @@ __global__ void __launch_bounds__(kFT, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
     }
-    // A operand [q_hi | q_hi | q_lo]: thread t builds row t % 128, chunks of its half
+    // A operand [q_hi | q_hi | q_lo]: thread t builds row t % 128, the 8-element
+    // groups g of its half; each group is read once (two 16-byte loads) and
+    // written as its chunk in all three parts
     {
         const int r = tid & (kTCM - 1), qi = q0 + r;
         const bool qok = qi < nq;
-        const float* qr = q + (size_t)(qok ? qi : 0) * d;
-        for (int k8 = tid >> 7; k8 < K8; k8 += kFT / kTCM)
-            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, k8, kTCM)) = split_chunk(qr, d, k8, qok, false);
+        const float4* qr4 = reinterpret_cast<const float4*>(q + (size_t)(qok ? qi : 0) * d);
+        const int G = d / 8;
+        for (int g = tid >> 7; g < G; g += kFT / kTCM) {
+            const float4 va = qok ? __ldg(qr4 + 2 * g) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 vb = qok ? __ldg(qr4 + 2 * g + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+            auto split2 = [](float x0, float x1, uint32_t& whi, uint32_t& wlo) {
+                const __nv_bfloat16 h0 = __float2bfloat16_rn(x0), h1 = __float2bfloat16_rn(x1);
+                const __nv_bfloat16 l0 = __float2bfloat16_rn(x0 - __bfloat162float(h0));
+                const __nv_bfloat16 l1 = __float2bfloat16_rn(x1 - __bfloat162float(h1));
+                whi = bf16_bits(h0) | (bf16_bits(h1) << 16);
+                wlo = bf16_bits(l0) | (bf16_bits(l1) << 16);
+            };
+            uint4 hi4, lo4;
+            split2(va.x, va.y, hi4.x, lo4.x);
+            split2(va.z, va.w, hi4.y, lo4.y);
+            split2(vb.x, vb.y, hi4.z, lo4.z);
+            split2(vb.z, vb.w, hi4.w, lo4.w);
+            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, g, kTCM)) = hi4;
+            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, G + g, kTCM)) = hi4;
+            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, 2 * G + g, kTCM)) = lo4;
+        }
         if (tid < kTCM) {
             float qn = 0.f;
             if (qok)
-                for (int j = 0; j < d; ++j) qn = __fadd_rn(qn, __fmul_rn(qr[j], qr[j]));
+                for (int w = 0; w < d / 4; ++w) {
+                    const float4 a = __ldg(qr4 + w);
+                    qn = __fadd_rn(qn, __fmul_rn(a.x, a.x));
+                    qn = __fadd_rn(qn, __fmul_rn(a.y, a.y));
+                    qn = __fadd_rn(qn, __fmul_rn(a.z, a.z));
+                    qn = __fadd_rn(qn, __fmul_rn(a.w, a.w));
+                }
             s_qn[tid] = qn;
         }
     }
@@ -739,26 +768,23 @@ __global__ void __launch_bounds__(kFT, 1)
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kFN)
                      : "memory");
-    // T~ of the row: L-th smallest of the two halves' L smallest
-    {
-        float* mine = s_lv + (half * kTCM + row) * kFLMax;
+    // T~ of the row: the L-th smallest of the two halves' ascending L smallest
+    // A (this thread's lv, half 0) and B (half 1's, through s_lv, entry-major
+    // [i][row]: the lanes of a warp read 32 different banks), as
+    // min over i = 0..L of max(A[i-1], B[L-1-i]) with A[-1] = B[-1] = -inf
+    if (half == 1) {
 #pragma unroll
-        for (int i = 0; i < kFLMax; ++i) mine[i] = i < LMAX ? lv[i < LMAX ? i : 0] : INF;
+        for (int i = 0; i < LMAX; ++i) s_lv[i * kTCM + row] = lv[i];
     }
     __syncthreads();
     if (half == 0) {
-        const float* la = s_lv + row * kFLMax;
-        const float* lb = s_lv + (kTCM + row) * kFLMax;
         float T = INF;
-        for (int i = 0; i < 2 * L; ++i) {
-            const float xv = i < L ? la[i] : lb[i - L];
-            int below = 0, eq_before = 0;
-            for (int k2 = 0; k2 < 2 * L; ++k2) {
-                const float y = k2 < L ? la[k2] : lb[k2 - L];
-                below += y < xv;
-                eq_before += (y == xv && k2 < i);
-            }
-            if (below + eq_before == L - 1) T = xv;
+#pragma unroll
+        for (int i = 0; i <= LMAX; ++i) {
+            const float a = i == 0 ? -INF : lv[i == 0 ? 0 : i - 1];
+            const int jb = L - 1 - i;
+            const float b = jb < 0 ? -INF : s_lv[jb * kTCM + row];
+            if (i <= L) T = fminf(T, fmaxf(a, b));
         }
         s_T[row] = T;
     }
@@ -770,29 +796,58 @@ __global__ void __launch_bounds__(kFT, 1)
     int nk = 0;
     bool big = over || T == INF;
     if (qi < nq && !failed && !big) {
-        const float4* qr = reinterpret_cast<const float4*>(q + (size_t)qi * d);
+        // the candidates' columns to the front of this thread's list
         for (int i = 0; i < nc; ++i) {
             if (myval[i * kFT] > climit) continue;
             if (nk == kFList / 2) {
                 big = true;
                 break;
             }
-            const int c = mycol[i * kFT];
-            const float4* cr = reinterpret_cast<const float4*>(cent + (size_t)c * d);
-            float sdist = 0.f;
+            mycol[nk * kFT] = mycol[i * kFT];
+            ++nk;
+        }
+    }
+    // Balanced rescoring: every (thread, slot) candidate of the CTA goes into
+    // one list, which all threads work through two at a time (two independent
+    // exact sums, their loads in flight together); the key lands in the
+    // owner's entry-major slot of s_key, [slot][owner]
+    {
+        const int mine = (qi < nq && !failed && !big) ? nk : 0;
+        int total;
+        const int off = block_excl_scan<kFT>(mine, s_scan, &total);
+        for (int i = 0; i < mine; ++i) s_pair[off + i] = (uint16_t)((i << 8) | tid);
+        __syncthreads();
+        for (int p = tid; p < total; p += 2 * kFT) {
+            const int e0 = s_pair[p], e1 = p + kFT < total ? s_pair[p + kFT] : e0;
+            const int t0 = e0 & 255, i0 = e0 >> 8, t1 = e1 & 255, i1 = e1 >> 8;
+            const int c0 = s_lcol[i0 * kFT + t0], c1 = s_lcol[i1 * kFT + t1];
+            const float4* qa = reinterpret_cast<const float4*>(q + (size_t)(q0 + (t0 & (kTCM - 1))) * d);
+            const float4* qb = reinterpret_cast<const float4*>(q + (size_t)(q0 + (t1 & (kTCM - 1))) * d);
+            const float4* r0 = reinterpret_cast<const float4*>(cent + (size_t)c0 * d);
+            const float4* r1 = reinterpret_cast<const float4*>(cent + (size_t)c1 * d);
+            float s0 = 0.f, s1 = 0.f;
 #pragma unroll 4
             for (int j = 0; j < d / 4; ++j) {
-                const float4 a = __ldg(qr + j), b = __ldg(cr + j);
-                const float x0 = __fsub_rn(a.x, b.x), x1 = __fsub_rn(a.y, b.y);
-                const float x2 = __fsub_rn(a.z, b.z), x3 = __fsub_rn(a.w, b.w);
-                sdist = __fadd_rn(sdist, __fmul_rn(x0, x0));
-                sdist = __fadd_rn(sdist, __fmul_rn(x1, x1));
-                sdist = __fadd_rn(sdist, __fmul_rn(x2, x2));
-                sdist = __fadd_rn(sdist, __fmul_rn(x3, x3));
+                const float4 a0 = __ldg(qa + j), b0 = __ldg(r0 + j), a1 = __ldg(qb + j), b1 = __ldg(r1 + j);
+                float x = __fsub_rn(a0.x, b0.x), y = __fsub_rn(a1.x, b1.x);
+                s0 = __fadd_rn(s0, __fmul_rn(x, x));
+                s1 = __fadd_rn(s1, __fmul_rn(y, y));
+                x = __fsub_rn(a0.y, b0.y);
+                y = __fsub_rn(a1.y, b1.y);
+                s0 = __fadd_rn(s0, __fmul_rn(x, x));
+                s1 = __fadd_rn(s1, __fmul_rn(y, y));
+                x = __fsub_rn(a0.z, b0.z);
+                y = __fsub_rn(a1.z, b1.z);
+                s0 = __fadd_rn(s0, __fmul_rn(x, x));
+                s1 = __fadd_rn(s1, __fmul_rn(y, y));
+                x = __fsub_rn(a0.w, b0.w);
+                y = __fsub_rn(a1.w, b1.w);
+                s0 = __fadd_rn(s0, __fmul_rn(x, x));
+                s1 = __fadd_rn(s1, __fmul_rn(y, y));
             }
-            s_key[tid * (kFList / 2) + nk] =
-                make_key(__float_as_uint(sdist), id_map ? (uint32_t)id_map[c] : (uint32_t)c);
-            ++nk;
+            s_key[i0 * kFT + t0] = make_key(__float_as_uint(s0), id_map ? (uint32_t)id_map[c0] : (uint32_t)c0);
+            if (p + kFT < total)
+                s_key[i1 * kFT + t1] = make_key(__float_as_uint(s1), id_map ? (uint32_t)id_map[c1] : (uint32_t)c1);
         }
     }
     s_nc[tid] = big ? -1 : nk;
@@ -803,15 +858,15 @@ __global__ void __launch_bounds__(kFT, 1)
         row_fallback[qi] = fall ? 1 : 0;
         if (!fall) {
             // top-L of the row's candidate keys: repeated minimum over the two lists
-            const uint64_t* ka = s_key + tid * (kFList / 2);
-            const uint64_t* kb = s_key + (tid + kTCM) * (kFList / 2);
+            const uint64_t* ka = s_key + tid;
+            const uint64_t* kb = s_key + tid + kTCM;
             uint64_t last = 0;
             for (int o = 0; o < L; ++o) {
                 uint64_t best = kKeyNone;
                 for (int i = 0; i < na; ++i)
-                    if ((o == 0 || ka[i] > last) && ka[i] < best) best = ka[i];
+                    if ((o == 0 || ka[i * kFT] > last) && ka[i * kFT] < best) best = ka[i * kFT];
                 for (int i = 0; i < nb; ++i)
-                    if ((o == 0 || kb[i] > last) && kb[i] < best) best = kb[i];
+                    if ((o == 0 || kb[i * kFT] > last) && kb[i * kFT] < best) best = kb[i * kFT];
                 const bool ok = best != kKeyNone;
                 if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(best) : -1;
                 if (out_keys) out_keys[(size_t)qi * L + o] = best;
