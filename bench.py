@@ -320,11 +320,11 @@ def main():
         keys_l = torch.empty((nq, nprobe), dtype=torch.int64, device=dev)
         keys_all = torch.empty((N * nq, nprobe), dtype=torch.int64, device=dev)
         adc = torch.empty((nq, R), dtype=torch.int64, device=dev)
-        exa = torch.empty((nq, R), dtype=torch.int64, device=dev)
+        topk = torch.empty((nq, k), dtype=torch.int64, device=dev)
         adc_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
-        exa_r = torch.empty((N, qo, R), dtype=torch.int64, device=dev)
-        take_o = torch.empty((N, qo), dtype=torch.int32, device=dev)
-        take_r = torch.empty((N, qo), dtype=torch.int32, device=dev)
+        topk_r = torch.empty((N, qo, k), dtype=torch.int64, device=dev)
+        kappa_o = torch.empty((qo,), dtype=torch.int64, device=dev)
+        kappa_all = torch.empty((nq,), dtype=torch.int64, device=dev)
 
         class _DevArray:              # a library-owned device array seen as a torch tensor (no copy)
             def __init__(self, ptr, n):
@@ -350,9 +350,9 @@ def main():
             mark("start")
             batch.route_keys(index, nq, np_, keys_l.data_ptr())
             mark("route")
-            kt = shard.gather_route_keys(dist, keys_l, keys_all)
+            dist.all_gather_into_tensor(keys_all, keys_l)
             mark("gather keys")
-            batch.route_merge(kt.data_ptr(), N * np_, nq, np_)
+            batch.route_merge_shards(keys_all.data_ptr(), N, nq, np_)
             mark("route merge")
             # nearest probes, global bounds, the other probes
             batch.pq_shard_scan(index, nq, np_, R, 0)
@@ -366,14 +366,14 @@ def main():
             mark("select")
             shard.to_owners_raw(dist, N, adc, adc_r)
             mark("stage 1 to owners")
-            batch.pq_shard_take(adc_r.data_ptr(), N, qo, R, take_o.data_ptr())
-            tk = shard.take_to_sources(dist, N, take_o, take_r)
-            mark("prefixes")
-            batch.pq_shard_rerank(index, nq, R, adc.data_ptr(), tk.data_ptr(), exa.data_ptr())
+            batch.pq_shard_kappa(adc_r.data_ptr(), N, qo, R, kappa_o.data_ptr())
+            shard.kappa_to_shards(dist, kappa_o, kappa_all)
+            mark("kappa")
+            batch.pq_shard_rerank(index, nq, R, adc.data_ptr(), kappa_all.data_ptr(), k, topk.data_ptr())
             mark("rerank")
-            shard.to_owners_raw(dist, N, exa, exa_r)
-            mark("exact to owners")
-            batch.pq_shard_final(exa_r.data_ptr(), N, qo, R, k, False)
+            shard.to_owners_raw(dist, N, topk, topk_r)
+            mark("top-k to owners")
+            batch.pq_shard_final(topk_r.data_ptr(), N, qo, k, False)
             batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
             mark("final")
             shard.gather_results(dist, out_ids, out_dist, all_ids, all_dist)

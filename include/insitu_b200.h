@@ -245,6 +245,10 @@ void* ivf_batch_stream(void* batch_ctx);
 int ivf_route_keys(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, unsigned long long* d_keys);
 /* merges n_in keys per query [n_query, n_in] into the batch probe table */
 int ivf_route_merge(void* batch_ctx, const unsigned long long* d_keys, int n_in, int n_query, int n_probes);
+/* merges n_shards sorted key lists laid out as all-gathered, [n_shards][n_query][n_probes]
+ * (no transpose), into the batch probe table; n_probes <= 32, n_shards * n_probes <= 256 */
+int ivf_route_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_shards, int n_query,
+                           int n_probes);
 /*
  * stage 1 + exact scoring of this shard's candidates for the batch probes:
  * d_adc [n_query, rerank_n] sorted (ADC bits << 32 | global position),
@@ -270,35 +274,40 @@ int ivf_u8_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n
  * ====================================================================== */
 /*
  * The same results as ivf_pq_search_shard + ivf_pq_merge_shards, with less
- * work per shard: every shard scans each query's nearest probe first, the
- * shards exchange their rank-R bounds (int64 minimum over shards), then scan
- * the other probes with the exchanged bounds; and each shard reranks only the
- * prefix of its stage-1 list that the query's owner asks for.  Per batch
- * (queries broadcast, block-partitioned owners, G shards):
+ * work and traffic per shard: every shard scans each query's nearest probe
+ * first, the shards exchange their rank-R bounds (int64 minimum over
+ * shards), then scan the other probes with the exchanged bounds; the query's
+ * owner finds kappa, the R-th smallest stage-1 key over all shards, and each
+ * shard reranks only its keys <= kappa and returns its exact top-k.  Per
+ * batch (queries broadcast, block-partitioned owners, G shards):
  *   ivf_pq_shard_scan(pass 0)
  *   all-reduce MIN (int64) over ivf_pq_shard_bounds(batch)[0 .. n_query)
  *   ivf_pq_shard_scan(pass 1)
- *   ivf_pq_shard_select -> d_adc [n_query, rerank_n] (ascending, keys with
- *       global positions);  all-to-all to the owners -> [G][n_owned][R]
- *   ivf_pq_shard_take (owner) -> d_take [G][n_owned];  all-to-all back ->
- *       each shard's [n_query] prefix lengths in global query order
- *   ivf_pq_shard_rerank -> d_exact [n_query, R];  all-to-all to the owners
+ *   ivf_pq_shard_select -> d_adc [n_query, rerank_n] (this shard's stage-1
+ *       keys with global positions, in no particular order);  all-to-all to
+ *       the owners -> [G][n_owned][R]
+ *   ivf_pq_shard_kappa (owner) -> d_kappa [n_owned];  all-to-all back ->
+ *       each shard's [n_query] key limits in global query order
+ *   ivf_pq_shard_rerank -> d_topk [n_query, k] (exact keys, ascending,
+ *       kKeyNone-padded);  all-to-all to the owners -> [G][n_owned][k]
  *   ivf_pq_shard_final (owner) -> the batch results of its n_owned queries
- * Probes come from ivf_set_probes / ivf_route_merge.  One sub-batch only
- * (IVF_EINVAL when the candidate buffers of n_query queries exceed
- * INSITU_SCRATCH_MB).  Main segment only (no overlay).
+ * Probes come from ivf_set_probes / ivf_route_merge / ivf_route_merge_shards.
+ * One sub-batch only (IVF_EINVAL when the candidate buffers of n_query
+ * queries exceed INSITU_SCRATCH_MB).  Main segment only (no overlay);
+ * k <= 32 and G * k <= 256.
  */
 int ivf_pq_shard_scan(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n, int pass);
 /* device array [n_query] of the rank-R bounds, as int64 (no bound: INT64_MAX) */
 unsigned long long* ivf_pq_shard_bounds(void* batch_ctx);
 int ivf_pq_shard_select(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n,
                         unsigned long long* d_adc);
-int ivf_pq_shard_take(void* batch_ctx, const unsigned long long* d_adc_all, int n_shards, int n_owned, int rerank_n,
-                      int* d_take);
+int ivf_pq_shard_kappa(void* batch_ctx, const unsigned long long* d_adc_all, int n_shards, int n_owned,
+                       int rerank_n, unsigned long long* d_kappa);
 int ivf_pq_shard_rerank(void* batch_ctx, void* idx_ctx, int n_query, int rerank_n,
-                        const unsigned long long* d_adc, const int* d_take, unsigned long long* d_exact);
-int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_exact_all, int n_shards, int n_owned,
-                       int rerank_n, int k, int exact_is_int);
+                        const unsigned long long* d_adc, const unsigned long long* d_kappa, int k,
+                        unsigned long long* d_topk);
+int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_topk_all, int n_shards, int n_owned, int k,
+                       int exact_is_int);
 
 /* ======================================================================
  * Allocation-free search (no counterpart in the reference)

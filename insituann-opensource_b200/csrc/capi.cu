@@ -1191,6 +1191,27 @@ int ivf_route_merge(void* batch_ctx, const unsigned long long* d_keys, int n_in,
     });
 }
 
+int ivf_route_merge_shards(void* batch_ctx, const unsigned long long* d_keys, int n_shards, int n_query,
+                           int n_probes) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        require(d_keys != nullptr && n_shards > 0, "bad key input");
+        require(n_query >= 0 && n_query <= b->max_nq && n_probes > 0 && n_probes <= b->max_nprobe,
+                "shape exceeds the batch limits");
+        require(n_probes <= 32 && n_shards * n_probes <= 256, "n_probes <= 32 and n_shards * n_probes <= 256");
+        cudaSetDevice(b->device);
+        ck(merge_shard_keys(reinterpret_cast<const uint64_t*>(d_keys), n_shards, n_query, n_probes, b->probes, b->st),
+           "merge_shard_keys");
+        b->probes_nq = n_query;
+        b->probes_np = n_probes;
+    });
+}
+
 int ivf_pq_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int rerank_n, int delta_topk,
                         unsigned long long* d_adc, unsigned long long* d_exact, unsigned long long* d_dadc,
                         unsigned long long* d_dexact) {
@@ -1301,12 +1322,12 @@ int ivf_pq_shard_select(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
         cudaSetDevice(b->device);
         ShardPlan sp = shard_plan(b, x, n_query, n_probes, rerank_n);
         StageScope stage(b, IVF_STAGE_SELECT);
-        ck(select_top_r(sp.cm, n_query, reinterpret_cast<uint64_t*>(d_adc), b->st), "select_top_r");
+        ck(select_top_r(sp.cm, n_query, reinterpret_cast<uint64_t*>(d_adc), b->st, false), "select_top_r");
     });
 }
 
-int ivf_pq_shard_take(void* batch_ctx, const unsigned long long* d_adc_all, int n_shards, int n_owned, int rerank_n,
-                      int* d_take) {
+int ivf_pq_shard_kappa(void* batch_ctx, const unsigned long long* d_adc_all, int n_shards, int n_owned,
+                       int rerank_n, unsigned long long* d_kappa) {
     BatchCtx* b = nullptr;
     try {
         b = as_batch(batch_ctx);
@@ -1314,15 +1335,17 @@ int ivf_pq_shard_take(void* batch_ctx, const unsigned long long* d_adc_all, int 
         return IVF_EINVAL;
     }
     return guarded(&b->err, [&] {
-        require(d_adc_all && d_take && n_shards > 0 && n_owned >= 0 && rerank_n > 0, "bad shard-take arguments");
+        require(d_adc_all && d_kappa && n_shards > 0 && n_owned >= 0 && rerank_n > 0, "bad shard-kappa arguments");
         cudaSetDevice(b->device);
-        ck(pq_shard_take(reinterpret_cast<const uint64_t*>(d_adc_all), n_shards, n_owned, rerank_n, d_take, b->st),
-           "pq_shard_take");
+        ck(pq_shard_kappa(reinterpret_cast<const uint64_t*>(d_adc_all), n_shards, n_owned, rerank_n,
+                          reinterpret_cast<uint64_t*>(d_kappa), b->st),
+           "pq_shard_kappa");
     });
 }
 
 int ivf_pq_shard_rerank(void* batch_ctx, void* idx_ctx, int n_query, int rerank_n,
-                        const unsigned long long* d_adc, const int* d_take, unsigned long long* d_exact) {
+                        const unsigned long long* d_adc, const unsigned long long* d_kappa, int k,
+                        unsigned long long* d_topk) {
     BatchCtx* b = nullptr;
     try {
         b = as_batch(batch_ctx);
@@ -1332,19 +1355,21 @@ int ivf_pq_shard_rerank(void* batch_ctx, void* idx_ctx, int n_query, int rerank_
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
         require(x->kind == kKindPQ, "index is not a residual-PQ index", IVF_ESTATE);
-        require(d_adc && d_take && d_exact && rerank_n > 0, "bad shard-rerank arguments");
+        require(d_adc && d_kappa && d_topk && rerank_n > 0, "bad shard-rerank arguments");
         require(n_query >= 0 && n_query <= b->max_nq && b->d == x->d, "shape exceeds the batch limits");
+        require(k > 0 && k <= b->max_k && k <= 32, "k must be in 1 .. min(32, the batch k)");
         cudaSetDevice(b->device);
         PQParams p = pq_params(x, b->q, false);
         StageScope stage(b, IVF_STAGE_RERANK);
-        ck(pq_rerank(p, x->nlist, reinterpret_cast<const uint64_t*>(d_adc), rerank_n, nullptr, 0, n_query, 1, nullptr,
-                     nullptr, reinterpret_cast<uint64_t*>(d_exact), nullptr, b->st, d_take),
+        ck(pq_rerank(p, x->nlist, reinterpret_cast<const uint64_t*>(d_adc), rerank_n, nullptr, 0, n_query, k, nullptr,
+                     nullptr, nullptr, nullptr, b->st, reinterpret_cast<const uint64_t*>(d_kappa),
+                     reinterpret_cast<uint64_t*>(d_topk)),
            "pq_rerank");
     });
 }
 
-int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_exact_all, int n_shards, int n_owned,
-                       int rerank_n, int k, int exact_is_int) {
+int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_topk_all, int n_shards, int n_owned, int k,
+                       int exact_is_int) {
     BatchCtx* b = nullptr;
     try {
         b = as_batch(batch_ctx);
@@ -1352,11 +1377,12 @@ int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_exact_all, i
         return IVF_EINVAL;
     }
     return guarded(&b->err, [&] {
-        require(d_exact_all && n_shards > 0 && rerank_n > 0, "bad shard-final arguments");
+        require(d_topk_all && n_shards > 0, "bad shard-final arguments");
         require(n_owned >= 0 && n_owned <= b->max_nq && k > 0 && k <= b->max_k, "shape exceeds the batch limits");
+        require(k <= 32 && n_shards * k <= 256, "k <= 32 and n_shards * k <= 256");
         cudaSetDevice(b->device);
-        ck(pq_shard_final(reinterpret_cast<const uint64_t*>(d_exact_all), n_shards, n_owned, rerank_n, k,
-                          exact_is_int, b->out_ids, b->out_dist, b->st),
+        ck(pq_shard_final(reinterpret_cast<const uint64_t*>(d_topk_all), n_shards, n_owned, k, exact_is_int,
+                          b->out_ids, b->out_dist, b->st),
            "pq_shard_final");
         b->res_nq = n_owned;
         b->res_k = k;

@@ -244,6 +244,56 @@ __device__ uint64_t block_kth_key(KeyFn keyf, int n, int need, uint64_t upper, i
         need, upper, hist, bc);
 }
 
+// One round of a warp-wide minimum over the E keys per lane in v: the
+// smallest key of the warp (high word first, then the low word among the
+// lanes that hold the high minimum, both by the warp's min-reduction) is
+// returned to every lane and exactly one copy of it -- the lowest lane's first
+// slot holding it -- is replaced by kKeyNone, so equal keys of different
+// candidates all come out in later rounds.  All 32 lanes call it together.
+template <int E>
+__device__ __forceinline__ uint64_t warp_take_min(uint64_t (&v)[E]) {
+    const int lane = threadIdx.x & 31;
+    uint64_t m = v[0];
+    int ms = 0;
+#pragma unroll
+    for (int e = 1; e < E; ++e)
+        if (v[e] < m) {
+            m = v[e];
+            ms = e;
+        }
+    const uint32_t hi = __reduce_min_sync(0xffffffffu, key_hi(m));
+    const uint32_t lo = __reduce_min_sync(0xffffffffu, key_hi(m) == hi ? key_lo(m) : 0xFFFFFFFFu);
+    const uint64_t wm = ((uint64_t)hi << 32) | lo;
+    const unsigned holders = __ballot_sync(0xffffffffu, m == wm);
+    if (lane == __ffs(holders) - 1) {
+#pragma unroll
+        for (int e = 0; e < E; ++e)
+            if (e == ms) v[e] = kKeyNone;
+    }
+    return wm;
+}
+
+// The k smallest of src[0 .. n) (n <= 32 E), ascending, into dst[0 .. k)
+// (kKeyNone past the last key), by one warp.
+template <int E>
+__device__ void warp_smallest_k(const uint64_t* src, int n, int k, uint64_t* dst) {
+    const int lane = threadIdx.x & 31;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = e * 32 + lane < n ? src[e * 32 + lane] : kKeyNone;
+    for (int it = 0; it < k; ++it) {
+        const uint64_t wm = warp_take_min<E>(v);
+        if (lane == 0) dst[it] = wm;
+    }
+}
+
+// n <= 128
+__device__ __forceinline__ void warp_smallest_k_dispatch(const uint64_t* src, int n, int k, uint64_t* dst) {
+    if (n <= 32) warp_smallest_k<1>(src, n, k, dst);
+    else if (n <= 64) warp_smallest_k<2>(src, n, k, dst);
+    else warp_smallest_k<4>(src, n, k, dst);
+}
+
 // ---------------------------------------------------------------------------
 // In-place ascending bitonic sort of n (power of two) keys in shared memory.
 // ---------------------------------------------------------------------------

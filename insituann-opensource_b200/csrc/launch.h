@@ -46,6 +46,9 @@ cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const 
 // (int_dist = 0) or as int32 (int_dist = 1, written to out_idist and out_dist).
 cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist, int32_t* out_ids,
                        float* out_dist, int32_t* out_idist, cudaStream_t st);
+// Top-L ids per query from S shards' sorted keys laid out [S][nq][L] (an
+// all-gather of per-shard [nq, L]); L <= 32, S * L <= 256.
+cudaError_t merge_shard_keys(const uint64_t* keys, int S, int nq, int L, int32_t* out_ids, cudaStream_t st);
 // out[i] = clamp(round(q[i]), 0, 255) (updates/exact_update.cu:410-418)
 // Tensor-core routing (route_tc.cu): approximate distances from one tcgen05
 // GEMM over bf16 hi/lo splits, then exact rescoring of the candidates within
@@ -122,15 +125,18 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
 // Exact rerank of the stage-1 keys of both segments -> top-k (ids, dist).
 // When out_exact_main is given, the per-candidate exact keys are written instead
 // of (ids, dist) being selected: [nq, R] and [nq, Rd] aligned with the inputs.
-// take (device [nq], may be null): rerank only main keys 0 .. take[q]-1 of each query.
+// kmax (device [nq], may be null): main keys above kmax[q] are not candidates.
+// out_topk (device [nq, k], may be null): the top-k exact keys instead of (ids, dist).
 cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int R, const uint64_t* s1_delta,
                       int Rd, int nq, int k, int32_t* out_ids, float* out_dist, uint64_t* out_exact_main,
-                      uint64_t* out_exact_delta, cudaStream_t st, const int32_t* take = nullptr);
-// Sharded search, owner side: adc_all [G][qo][R] ascending stage-1 lists of the
-// G shards -> take [G][qo], the prefix of each list in the query's stage 1;
-// ex_all [G][qo][R] the shards' exact keys of those prefixes -> top-k.
-cudaError_t pq_shard_take(const uint64_t* adc_all, int G, int qo, int R, int32_t* take, cudaStream_t st);
-cudaError_t pq_shard_final(const uint64_t* ex_all, int G, int qo, int R, int k, int exact_is_int, int32_t* out_ids,
+                      uint64_t* out_exact_delta, cudaStream_t st, const uint64_t* kmax = nullptr,
+                      uint64_t* out_topk = nullptr);
+// Sharded search, owner side: adc_all [G][qo][R] stage-1 lists of the G shards
+// (any order) -> kappa [qo], the R-th smallest key of their union (kKeyNone
+// when the union has fewer than R keys); top_all [G][qo][k] the shards' exact
+// top-k of their keys <= kappa -> the top-k.
+cudaError_t pq_shard_kappa(const uint64_t* adc_all, int G, int qo, int R, uint64_t* kappa, cudaStream_t st);
+cudaError_t pq_shard_final(const uint64_t* top_all, int G, int qo, int k, int exact_is_int, int32_t* out_ids,
                            float* out_dist, cudaStream_t st);
 // Final merge of sharded stage-1 results: per query, G shards each give R
 // (ADC key, exact key) pairs for the main segment and Rd for the delta.

@@ -681,47 +681,6 @@ __device__ __forceinline__ bool hash_first(unsigned long long* tab, int mask, ui
     return false;
 }
 
-// The k smallest of src[0 .. n) (n <= 32 E), ascending, into dst[0 .. k)
-// (kKeyNone past the last key), by one warp: k rounds of a warp-wide minimum
-// (high word, then low word among the lanes that hold the high minimum, both
-// by the warp's min-reduction), each removing exactly one copy -- the lowest
-// lane's first slot holding it -- so equal keys of different candidates are
-// all kept.
-template <int E>
-__device__ void warp_smallest_k(const uint64_t* src, int n, int k, uint64_t* dst) {
-    const int lane = threadIdx.x & 31;
-    uint64_t v[E];
-#pragma unroll
-    for (int e = 0; e < E; ++e) v[e] = e * 32 + lane < n ? src[e * 32 + lane] : kKeyNone;
-    for (int it = 0; it < k; ++it) {
-        uint64_t m = v[0];
-        int ms = 0;
-#pragma unroll
-        for (int e = 1; e < E; ++e)
-            if (v[e] < m) {
-                m = v[e];
-                ms = e;
-            }
-        const uint32_t hi = __reduce_min_sync(0xffffffffu, key_hi(m));
-        const uint32_t lo = __reduce_min_sync(0xffffffffu, key_hi(m) == hi ? key_lo(m) : 0xFFFFFFFFu);
-        const uint64_t wm = ((uint64_t)hi << 32) | lo;
-        const unsigned holders = __ballot_sync(0xffffffffu, m == wm);
-        if (lane == 0) dst[it] = wm;
-        if (lane == __ffs(holders) - 1) {
-#pragma unroll
-            for (int e = 0; e < E; ++e)
-                if (e == ms) v[e] = kKeyNone;
-        }
-    }
-}
-
-// n <= 128
-__device__ __forceinline__ void warp_smallest_k_dispatch(const uint64_t* src, int n, int k, uint64_t* dst) {
-    if (n <= 32) warp_smallest_k<1>(src, n, k, dst);
-    else if (n <= 64) warp_smallest_k<2>(src, n, k, dst);
-    else warp_smallest_k<4>(src, n, k, dst);
-}
-
 // Exact rerank of one query's stage-1 candidates (CTA per query).  Four threads
 // share a candidate row: for the fp32 distance thread `sub` owns the lanes
 // 4 sub .. 4 sub + 3 of the reference's 16-lane AVX-512 arithmetic
@@ -736,7 +695,8 @@ template <int NB>
 __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, const uint64_t* __restrict__ s1m,
                                                          int R, const uint64_t* __restrict__ s1d, int Rd, int k,
                                                          int32_t* out_ids, float* out_dist, uint64_t* out_exm,
-                                                         uint64_t* out_exd, const int32_t* __restrict__ take) {
+                                                         uint64_t* out_exd, const uint64_t* __restrict__ kmax,
+                                                         uint64_t* out_topk) {
     extern __shared__ uint64_t sk[];            // [np] exact keys, [np] stage-1 keys, a table of rr_table(np) slots
     __shared__ __align__(16) float sq[kPMaxD];
     __shared__ __align__(16) uint8_t squ[kPMaxD];
@@ -744,7 +704,7 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     const int nb = NB ? NB : d / 16;
     const bool f32 = p.main.rr_f32 != nullptr;
     const int nc = R + Rd;
-    const int tq = take ? take[q] : R;           // main keys 0 .. tq-1 only (a shard's requested prefix)
+    const uint64_t km = kmax ? kmax[q] : kKeyNone;   // main keys above it are not candidates (a shard's part)
     int np = 1;
     while (np < nc) np <<= 1;
     uint64_t* s1 = sk + np;
@@ -755,11 +715,13 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
         sq[j] = x;
         squ[j] = to_u8(x);
     }
-    // every candidate's stage-1 key in one coalesced pass (kKeyNone past the
-    // shard's requested prefix and past the end)
-    for (int c = tid; c < np; c += kRRT)
-        s1[c] = c < R ? (c < tq ? s1m[(size_t)q * R + c] : kKeyNone)
+    // every candidate's stage-1 key in one coalesced pass (kKeyNone above the
+    // query's key limit and past the end)
+    for (int c = tid; c < np; c += kRRT) {
+        const uint64_t km1 = c < R ? s1m[(size_t)q * R + c] : kKeyNone;
+        s1[c] = c < R ? (km1 <= km ? km1 : kKeyNone)
                       : (c < nc ? s1d[(size_t)q * Rd + (c - R)] : kKeyNone);
+    }
     if (!out_exm)
         for (int i = tid; i <= tmask; i += kRRT) tab[i] = kKeyNone;
     __syncthreads();
@@ -858,9 +820,13 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
             if (lane < k) {
                 const uint64_t ek = sk[lane];
                 const bool ok = ek != kKeyNone;
-                out_ids[(size_t)q * k + lane] = ok ? (int32_t)key_lo(ek) : -1;
-                out_dist[(size_t)q * k + lane] =
-                    ok ? (f32 ? __uint_as_float(key_hi(ek)) : (float)key_hi(ek)) : __int_as_float(0x7f800000);
+                if (out_topk) {
+                    out_topk[(size_t)q * k + lane] = ek;
+                } else {
+                    out_ids[(size_t)q * k + lane] = ok ? (int32_t)key_lo(ek) : -1;
+                    out_dist[(size_t)q * k + lane] =
+                        ok ? (f32 ? __uint_as_float(key_hi(ek)) : (float)key_hi(ek)) : __int_as_float(0x7f800000);
+                }
             }
         }
         return;
@@ -869,6 +835,10 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
     for (int j = tid; j < k; j += kRRT) {
         const uint64_t ek = j < np ? sk[j] : kKeyNone;
         const bool ok = ek != kKeyNone;
+        if (out_topk) {
+            out_topk[(size_t)q * k + j] = ek;
+            continue;
+        }
         out_ids[(size_t)q * k + j] = ok ? (int32_t)key_lo(ek) : -1;
         out_dist[(size_t)q * k + j] =
             ok ? (f32 ? __uint_as_float(key_hi(ek)) : (float)key_hi(ek)) : __int_as_float(0x7f800000);
@@ -946,23 +916,23 @@ __global__ void __launch_bounds__(kMT) merge_shards_kernel(const uint64_t* adc_m
 }
 
 // ---------------------------------------------------------------------------
-// sharded search, owner side (one CTA per owned query)
+// sharded search, owner side
 // ---------------------------------------------------------------------------
-// Each of the G shards sent its stage-1 list of the query: R keys, ascending,
-// kKeyNone-padded.  The query's stage 1 over the whole index is every distinct
-// key <= kappa, the R-th smallest of the union (with multiplicity), so shard s
-// is asked to rerank the prefix of its list up to kappa: take[s][q] = the
-// number of its keys <= kappa (all of them when the union has fewer than R).
+// Each of the G shards sent its stage-1 list of the query: R keys in any
+// order, kKeyNone-padded.  The query's stage 1 over the whole index is every
+// distinct key <= kappa, the R-th smallest of the union (with multiplicity,
+// as a single stage-1 selection counts a repeated position), so every shard
+// reranks its keys <= kappa.  One CTA per owned query.
 constexpr int kShT = 256;
 
-__global__ void __launch_bounds__(kShT) shard_take_kernel(const uint64_t* __restrict__ adc, int G, int qo, int R,
-                                                          int32_t* __restrict__ take) {
+__global__ void __launch_bounds__(kShT) shard_kappa_kernel(const uint64_t* __restrict__ adc, int G, int qo, int R,
+                                                           uint64_t* __restrict__ kappa) {
     __shared__ int hist[256];
     __shared__ int bc[4];
     __shared__ int s_valid;
     const int q = blockIdx.x, tid = threadIdx.x;
     const int n = G * R;
-    // element i of the union: shard i / R, rank i % R
+    // element i of the union: shard i / R, entry i % R
     auto keyf = [&](int i) -> uint64_t { return adc[((size_t)(i / R) * qo + q) * R + (i % R)]; };
     if (tid == 0) s_valid = 0;
     __syncthreads();
@@ -971,56 +941,35 @@ __global__ void __launch_bounds__(kShT) shard_take_kernel(const uint64_t* __rest
     if (v) atomicAdd(&s_valid, v);
     __syncthreads();
     const int valid = s_valid;
-    uint64_t kap = kKeyNone - 1;
+    uint64_t kap = kKeyNone - 1;                   // fewer than R keys: every key is in stage 1
     if (valid > R) kap = block_kth_key<kShT>(keyf, n, R, kKeyNone - 1, hist, bc);
-    // lists are ascending: the count of keys <= kappa is a binary search
-    for (int g = tid; g < G; g += kShT) {
-        const uint64_t* a = adc + ((size_t)g * qo + q) * R;
-        int lo = 0, hi = R;
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (a[mid] <= kap) lo = mid + 1; else hi = mid;
-        }
-        take[(size_t)g * qo + q] = lo;
-    }
+    if (tid == 0) kappa[q] = kap;
 }
 
-// Final top-k of an owned query over the exact keys the shards returned for
-// their requested prefixes (kKeyNone elsewhere); a position reranked twice
-// (a list probed twice) counts once.
-__global__ void __launch_bounds__(kShT) shard_final_kernel(const uint64_t* __restrict__ ex, int G, int qo, int R,
-                                                           int k, int exact_is_int, int32_t* out_ids,
-                                                           float* out_dist) {
-    extern __shared__ uint64_t fk[];               // [np]
-    __shared__ int s_cnt;
-    const int q = blockIdx.x, tid = threadIdx.x;
-    if (tid == 0) s_cnt = 0;
-    __syncthreads();
-    const int n = G * R;
-    for (int i = tid; i < n; i += kShT) {
-        const uint64_t e = ex[((size_t)(i / R) * qo + q) * R + (i % R)];
-        if (e != kKeyNone) fk[atomicAdd(&s_cnt, 1)] = e;
+// Final top-k of an owned query from the G shards' exact top-k lists (keys of
+// distinct positions), one warp per query: L rounds of the warp minimum.
+template <int E>
+__global__ void __launch_bounds__(256) shard_final_kernel(const uint64_t* __restrict__ top, int G, int qo, int k,
+                                                          int exact_is_int, int32_t* out_ids, float* out_dist) {
+    const int q = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (q >= qo) return;                           // whole warps only
+    const int n = G * k;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = e * 32 + lane;
+        v[e] = i < n ? top[((size_t)(i / k) * qo + q) * k + (i % k)] : kKeyNone;
     }
-    __syncthreads();
-    const int nv = s_cnt;
-    int np = 1;
-    while (np < nv) np <<= 1;
-    for (int i = nv + tid; i < np; i += kShT) fk[i] = kKeyNone;
-    block_bitonic_sort<kShT>(fk, np);
-    if (tid == 0) {
-        int o = 0;
-        uint64_t last = kKeyNone;
-        for (int i = 0; i < nv && o < k; ++i) {
-            if (fk[i] == last) continue;
-            last = fk[i];
-            out_ids[(size_t)q * k + o] = (int32_t)key_lo(last);
-            out_dist[(size_t)q * k + o] = exact_is_int ? (float)key_hi(last) : __uint_as_float(key_hi(last));
-            ++o;
-        }
-        for (; o < k; ++o) {
-            out_ids[(size_t)q * k + o] = -1;
-            out_dist[(size_t)q * k + o] = __int_as_float(0x7f800000);
-        }
+    uint64_t mine = kKeyNone;
+    for (int it = 0; it < k; ++it) {
+        const uint64_t wm = warp_take_min<E>(v);
+        if (lane == it) mine = wm;
+    }
+    if (lane < k) {
+        const bool ok = mine != kKeyNone;
+        out_ids[(size_t)q * k + lane] = ok ? (int32_t)key_lo(mine) : -1;
+        out_dist[(size_t)q * k + lane] =
+            ok ? (exact_is_int ? (float)key_hi(mine) : __uint_as_float(key_hi(mine))) : __int_as_float(0x7f800000);
     }
 }
 
@@ -1090,7 +1039,7 @@ cudaError_t pq_scan(const PQParams& p, WorkList wl, int max_pairs, CandBuf cm, C
 
 cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int R, const uint64_t* s1_delta,
                       int Rd, int nq, int k, int32_t* out_ids, float* out_dist, uint64_t* out_exact_main,
-                      uint64_t* out_exact_delta, cudaStream_t st, const int32_t* take) {
+                      uint64_t* out_exact_delta, cudaStream_t st, const uint64_t* kmax, uint64_t* out_topk) {
     if (nq <= 0) return cudaSuccess;
     const int nc = R + Rd;
     if (nc > kRRMax || p.d > kPMaxD || (p.d % 16) != 0) return cudaErrorInvalidValue;
@@ -1103,7 +1052,7 @@ cudaError_t pq_rerank(const PQParams& p, int nlist, const uint64_t* s1_main, int
         if (e) return e;
         note_launch();
         kern<<<nq, kRRT, smem, st>>>(p, nlist, s1_main, R, s1_delta, Rd, k, out_ids, out_dist, out_exact_main,
-                                     out_exact_delta, take);
+                                     out_exact_delta, kmax, out_topk);
         return cudaGetLastError();
     };
     switch (p.main.rr_f32 ? p.d / 16 : 0) {
@@ -1132,24 +1081,24 @@ cudaError_t pq_merge_shards(const uint64_t* adc_main, const uint64_t* exact_main
     return cudaGetLastError();
 }
 
-cudaError_t pq_shard_take(const uint64_t* adc_all, int G, int qo, int R, int32_t* take, cudaStream_t st) {
+cudaError_t pq_shard_kappa(const uint64_t* adc_all, int G, int qo, int R, uint64_t* kappa, cudaStream_t st) {
     if (qo <= 0) return cudaSuccess;
     note_launch();
-    shard_take_kernel<<<qo, kShT, 0, st>>>(adc_all, G, qo, R, take);
+    shard_kappa_kernel<<<qo, kShT, 0, st>>>(adc_all, G, qo, R, kappa);
     return cudaGetLastError();
 }
 
-cudaError_t pq_shard_final(const uint64_t* ex_all, int G, int qo, int R, int k, int exact_is_int, int32_t* out_ids,
+cudaError_t pq_shard_final(const uint64_t* top_all, int G, int qo, int k, int exact_is_int, int32_t* out_ids,
                            float* out_dist, cudaStream_t st) {
+    if (G <= 0 || k <= 0 || k > 32 || G * k > 256) return cudaErrorInvalidValue;
     if (qo <= 0) return cudaSuccess;
-    int np = 1;
-    while (np < G * R) np <<= 1;
-    const size_t smem = sizeof(uint64_t) * np;
-    if (smem > 160 * 1024) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(shard_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e) return e;
+    const int n = G * k;
+    const unsigned blocks = (unsigned)(((size_t)qo * 32 + 255) / 256);
     note_launch();
-    shard_final_kernel<<<qo, kShT, smem, st>>>(ex_all, G, qo, R, k, exact_is_int, out_ids, out_dist);
+    if (n <= 32) shard_final_kernel<1><<<blocks, 256, 0, st>>>(top_all, G, qo, k, exact_is_int, out_ids, out_dist);
+    else if (n <= 64) shard_final_kernel<2><<<blocks, 256, 0, st>>>(top_all, G, qo, k, exact_is_int, out_ids, out_dist);
+    else if (n <= 128) shard_final_kernel<4><<<blocks, 256, 0, st>>>(top_all, G, qo, k, exact_is_int, out_ids, out_dist);
+    else shard_final_kernel<8><<<blocks, 256, 0, st>>>(top_all, G, qo, k, exact_is_int, out_ids, out_dist);
     return cudaGetLastError();
 }
 

@@ -224,6 +224,32 @@ __global__ void __launch_bounds__(kSelT) merge_keys_kernel(const uint64_t* __res
     }
 }
 
+// One warp per query over the shards' sorted routing keys as all-gathered,
+// [S][nq][L]: the query's S * L keys (at most 32 E) go to registers and L
+// rounds of the warp minimum give its global top-L; lane j writes the j-th.
+template <int E>
+__global__ void __launch_bounds__(256) merge_shard_keys_kernel(const uint64_t* __restrict__ keys, int S, int nq,
+                                                               int L, int32_t* __restrict__ out_ids) {
+    const int q = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (q >= nq) return;                   // whole warps only
+    const int n = S * L;
+    uint64_t v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int i = e * 32 + lane;
+        v[e] = i < n ? keys[((size_t)(i / L) * nq + q) * L + (i % L)] : kKeyNone;
+    }
+    uint64_t mine = kKeyNone;
+    for (int it = 0; it < L; ++it) {
+        const uint64_t wm = warp_take_min<E>(v);
+        if (lane == it) mine = wm;
+    }
+    if (lane < L) {
+        const bool ok = mine != kKeyNone && key_hi(mine) != 0xFFFFFFFFu;
+        out_ids[(size_t)q * L + lane] = ok ? (int32_t)key_lo(mine) : -1;
+    }
+}
+
 __global__ void make_u8_kernel(const float* __restrict__ q, size_t n, uint8_t* __restrict__ out) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         float x = fminf(fmaxf(q[i], 0.f), 255.f);
@@ -266,6 +292,19 @@ cudaError_t merge_keys(const uint64_t* keys, int nq, int n, int L, int int_dist,
     if (nq <= 0) return cudaSuccess;
     note_launch();
     merge_keys_kernel<<<nq, kSelT, 0, st>>>(keys, n, L, int_dist, out_ids, out_dist, out_idist);
+    return cudaGetLastError();
+}
+
+cudaError_t merge_shard_keys(const uint64_t* keys, int S, int nq, int L, int32_t* out_ids, cudaStream_t st) {
+    if (S <= 0 || L <= 0 || L > 32 || S * L > 256) return cudaErrorInvalidValue;
+    if (nq <= 0) return cudaSuccess;
+    const int n = S * L;
+    const unsigned blocks = (unsigned)(((size_t)nq * 32 + 255) / 256);
+    note_launch();
+    if (n <= 32) merge_shard_keys_kernel<1><<<blocks, 256, 0, st>>>(keys, S, nq, L, out_ids);
+    else if (n <= 64) merge_shard_keys_kernel<2><<<blocks, 256, 0, st>>>(keys, S, nq, L, out_ids);
+    else if (n <= 128) merge_shard_keys_kernel<4><<<blocks, 256, 0, st>>>(keys, S, nq, L, out_ids);
+    else merge_shard_keys_kernel<8><<<blocks, 256, 0, st>>>(keys, S, nq, L, out_ids);
     return cudaGetLastError();
 }
 

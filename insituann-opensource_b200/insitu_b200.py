@@ -38,9 +38,9 @@ EXPORTS = [
     "ivf_u8_load", "ivf_pq_load", "ivf_set_shard", "ivf_pq_publish_delta", "ivf_pq_clear_delta",
     "ivf_route", "ivf_set_probes", "ivf_get_probes", "ivf_u8_search", "ivf_pq_search", "ivf_get_results_i32",
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
-    "ivf_route_keys", "ivf_route_merge", "ivf_pq_search_shard", "ivf_pq_merge_shards",
+    "ivf_route_keys", "ivf_route_merge", "ivf_route_merge_shards", "ivf_pq_search_shard", "ivf_pq_merge_shards",
     "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_pq_shard_scan", "ivf_pq_shard_bounds",
-    "ivf_pq_shard_select", "ivf_pq_shard_take", "ivf_pq_shard_rerank", "ivf_pq_shard_final",
+    "ivf_pq_shard_select", "ivf_pq_shard_kappa", "ivf_pq_shard_rerank", "ivf_pq_shard_final",
     "ivf_last_error", "ivf_global_last_error",
     "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms", "ivf_u8_search_noalloc",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
@@ -87,6 +87,7 @@ _SIGS = {
     "ivf_batch_stream": ([vp], vp),
     "ivf_route_keys": ([vp, vp, i32, i32, vp], i32),
     "ivf_route_merge": ([vp, vp, i32, i32, i32], i32),
+    "ivf_route_merge_shards": ([vp, vp, i32, i32, i32], i32),
     "ivf_pq_search_shard": ([vp, vp, i32, i32, i32, i32, vp, vp, vp, vp], i32),
     "ivf_pq_merge_shards": ([vp, vp, vp, i32, i32, vp, vp, i32, i32, i32, i32, i32], i32),
     "ivf_u8_search_shard": ([vp, vp, i32, i32, i32, vp], i32),
@@ -94,9 +95,9 @@ _SIGS = {
     "ivf_pq_shard_scan": ([vp, vp, i32, i32, i32, i32], i32),
     "ivf_pq_shard_bounds": ([vp], vp),
     "ivf_pq_shard_select": ([vp, vp, i32, i32, i32, vp], i32),
-    "ivf_pq_shard_take": ([vp, vp, i32, i32, i32, vp], i32),
-    "ivf_pq_shard_rerank": ([vp, vp, i32, i32, vp, vp, vp], i32),
-    "ivf_pq_shard_final": ([vp, vp, i32, i32, i32, i32, i32], i32),
+    "ivf_pq_shard_kappa": ([vp, vp, i32, i32, i32, vp], i32),
+    "ivf_pq_shard_rerank": ([vp, vp, i32, i32, vp, vp, i32, vp], i32),
+    "ivf_pq_shard_final": ([vp, vp, i32, i32, i32, i32], i32),
     "ivf_last_error": ([vp], C.c_char_p),
     "ivf_global_last_error": ([], C.c_char_p),
     "cuda_is_available": ([], C.c_bool),
@@ -334,6 +335,10 @@ class Batch:
     def route_merge(self, d_keys: int, n_in, nq, nprobe):
         self._check(self.L.ivf_route_merge(self.h, d_keys, n_in, nq, nprobe))
 
+    def route_merge_shards(self, d_keys: int, n_shards, nq, nprobe):
+        """d_keys: the shards' sorted routing keys as all-gathered, [n_shards][nq][nprobe]."""
+        self._check(self.L.ivf_route_merge_shards(self.h, d_keys, n_shards, nq, nprobe))
+
     def pq_search_shard(self, index: Index, nq, nprobe, rerank_n, delta_topk, d_adc, d_exact, d_dadc=None,
                         d_dexact=None):
         self._check(self.L.ivf_pq_search_shard(self.h, index.h, nq, nprobe, rerank_n, delta_topk, d_adc, d_exact,
@@ -355,15 +360,17 @@ class Batch:
     def pq_shard_select(self, index: Index, nq, nprobe, rerank_n, d_adc):
         self._check(self.L.ivf_pq_shard_select(self.h, index.h, nq, nprobe, rerank_n, d_adc))
 
-    def pq_shard_take(self, d_adc_all, n_shards, n_owned, rerank_n, d_take):
-        self._check(self.L.ivf_pq_shard_take(self.h, d_adc_all, n_shards, n_owned, rerank_n, d_take))
+    def pq_shard_kappa(self, d_adc_all, n_shards, n_owned, rerank_n, d_kappa):
+        """owner: d_adc_all [n_shards][n_owned][R] -> d_kappa [n_owned], the R-th smallest key of the union"""
+        self._check(self.L.ivf_pq_shard_kappa(self.h, d_adc_all, n_shards, n_owned, rerank_n, d_kappa))
 
-    def pq_shard_rerank(self, index: Index, nq, rerank_n, d_adc, d_take, d_exact):
-        self._check(self.L.ivf_pq_shard_rerank(self.h, index.h, nq, rerank_n, d_adc, d_take, d_exact))
+    def pq_shard_rerank(self, index: Index, nq, rerank_n, d_adc, d_kappa, k, d_topk):
+        """this shard's exact top-k [nq, k] (keys) of its stage-1 keys <= d_kappa[q]"""
+        self._check(self.L.ivf_pq_shard_rerank(self.h, index.h, nq, rerank_n, d_adc, d_kappa, k, d_topk))
 
-    def pq_shard_final(self, d_exact_all, n_shards, n_owned, rerank_n, k, exact_is_int):
-        self._check(self.L.ivf_pq_shard_final(self.h, d_exact_all, n_shards, n_owned, rerank_n, k,
-                                              1 if exact_is_int else 0))
+    def pq_shard_final(self, d_topk_all, n_shards, n_owned, k, exact_is_int):
+        """owner: d_topk_all [n_shards][n_owned][k] -> the batch results of its n_owned queries"""
+        self._check(self.L.ivf_pq_shard_final(self.h, d_topk_all, n_shards, n_owned, k, 1 if exact_is_int else 0))
 
     def u8_search_shard(self, index: Index, nq, nprobe, k, d_keys):
         self._check(self.L.ivf_u8_search_shard(self.h, index.h, nq, nprobe, k, d_keys))

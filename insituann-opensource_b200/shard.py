@@ -6,7 +6,7 @@ bytes (LPT), and one query batch moves through three collectives:
 
   1. every rank's local routing keys (distance bits << 32 | global list id,
      [nq, nprobe], sorted) are all-gathered, so every rank can form the
-     global top-nprobe (ivf_route_merge);
+     global top-nprobe (ivf_route_merge_shards reads the all-gather layout);
   2. every rank's per-query stage-1 lists (ADC key, exact key) are sent to the
      rank that owns the query (block partition of the batch) with one
      all-to-all, and the owner merges them (ivf_pq_merge_shards);
@@ -18,10 +18,10 @@ The phased protocol (ivf_pq_shard_* entry points) replaces step 2 by:
       rank-R bounds are reduced with an int64 minimum (exchange_bounds) and
       every shard scans the other probes with the global bound;
   2b. the stage-1 lists go to the owners (to_owners_raw); each owner computes
-      per shard the prefix of its list in the query's stage 1, and the prefix
-      lengths go back to the shards (take_to_sources);
-  2c. each shard reranks only that prefix; the exact keys go to the owners
-      (to_owners_raw), which form the top-k.
+      kappa, the R-th smallest key of the union, and the owners' kappas are
+      all-gathered (kappa_to_shards);
+  2c. each shard reranks its keys <= kappa and sends its exact top-k to the
+      owners (to_owners_raw), which merge them.
 
 The functions take torch tensors and a process group, so the same code runs
 over NCCL with device tensors (bench.py) and over gloo with CPU tensors
@@ -92,7 +92,7 @@ def to_owners_raw(dist, world, per_query, recv):
     return recv
 
 
-def take_to_sources(dist, world, take, recv):
-    """owner's take [world (shard), qo] -> this shard's [world * qo] prefix lengths in global query order."""
-    dist.all_to_all_single(recv, take.contiguous())
-    return recv.reshape(-1)
+def kappa_to_shards(dist, kappa_owned, kappa_all):
+    """each owner's key limits [qo] (int64) -> every shard's [world * qo] in global query order."""
+    dist.all_gather_into_tensor(kappa_all, kappa_owned)
+    return kappa_all

@@ -352,13 +352,18 @@ def test_sharded_merge_equals_unsharded(cuda_ok, pq_medium):
         b.sync()
     allk = keys.permute(1, 0, 2).contiguous()          # [nq, 2 * nprobe]
     for s in range(2):
-        batches[s].route_merge(allk.data_ptr(), 2 * nprobe, nq, nprobe)
+        # shard 0 merges the transposed keys, shard 1 the all-gather layout [2][nq][nprobe]
+        if s == 0:
+            batches[s].route_merge(allk.data_ptr(), 2 * nprobe, nq, nprobe)
+        else:
+            batches[s].route_merge_shards(keys.data_ptr(), 2, nq, nprobe)
         batches[s].pq_search_shard(shards[s], nq, nprobe, R, dtk, adc[s].data_ptr(), exa[s].data_ptr(),
                                    dadc[s].data_ptr(), dexa[s].data_ptr())
     for b in batches:
         b.sync()
     exp_probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     assert np.array_equal(batches[0].get_probes(nq, nprobe), exp_probes)
+    assert np.array_equal(batches[1].get_probes(nq, nprobe), exp_probes)
     cat = lambda t: t.permute(1, 0, 2).contiguous()    # noqa: E731
     A, E, DA, DE = cat(adc), cat(exa), cat(dadc), cat(dexa)
     batches[0].pq_merge_shards(A.data_ptr(), E.data_ptr(), 2 * R, R, DA.data_ptr(), DE.data_ptr(), 2 * dtk, dtk,
@@ -371,12 +376,13 @@ def test_sharded_merge_equals_unsharded(cuda_ok, pq_medium):
         o.close()
 
 
-@pytest.mark.parametrize("R,k", [(256, 10), (40, 40)])
+@pytest.mark.parametrize("R,k", [(256, 10), (40, 32)])
 def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
     """lists split over 3 shards (three index contexts on one GPU), the phased
     protocol with the exchanges done on the host side: nearest-probe scans,
-    int64 minimum of the bounds, the other probes, stage 1 to the owners,
-    prefix lengths back, prefix reranks, owners' top-k == unsharded search."""
+    int64 minimum of the bounds, the other probes, unsorted stage 1 to the
+    owners, kappa (R-th key of the union) back, each shard's exact top-k of its
+    keys <= kappa, owners' merge == unsharded search."""
     p, q = pq_medium
     nlist = len(p["counts"])
     G, nprobe = 3, 12
@@ -399,7 +405,7 @@ def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
     exp_probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     batches = [ib.Batch(nq, q.shape[1], nprobe, k, nlist) for _ in range(G)]
     adc = torch.empty((G, nq, R), dtype=torch.int64, device=dev)
-    exa = torch.empty((G, nq, R), dtype=torch.int64, device=dev)
+    topk = torch.empty((G, nq, k), dtype=torch.int64, device=dev)
     for s in range(G):
         batches[s].stage1_prepare(q)
         batches[s].set_probes(exp_probes)
@@ -422,21 +428,21 @@ def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
         b.sync()
     # stage 1 to the owners: owner o gets [G][qo][R]
     adc_o = [adc[:, o * qo:(o + 1) * qo, :].contiguous() for o in range(G)]
-    take_o = [torch.empty((G, qo), dtype=torch.int32, device=dev) for _ in range(G)]
+    kappa_o = [torch.empty((qo,), dtype=torch.int64, device=dev) for _ in range(G)]
     for o in range(G):
-        batches[o].pq_shard_take(adc_o[o].data_ptr(), G, qo, R, take_o[o].data_ptr())
+        batches[o].pq_shard_kappa(adc_o[o].data_ptr(), G, qo, R, kappa_o[o].data_ptr())
     for b in batches:
         b.sync()
+    kappa_all = torch.cat(kappa_o).contiguous()          # [nq], global query order (an all-gather)
     for s in range(G):
-        take_s = torch.cat([take_o[o][s] for o in range(G)]).contiguous()     # [nq], global query order
-        batches[s].pq_shard_rerank(shards[s], nq, R, adc[s].data_ptr(), take_s.data_ptr(), exa[s].data_ptr())
+        batches[s].pq_shard_rerank(shards[s], nq, R, adc[s].data_ptr(), kappa_all.data_ptr(), k, topk[s].data_ptr())
     for b in batches:
         b.sync()
     gi = np.zeros((nq, k), np.int32)
     gd = np.zeros((nq, k), np.float32)
     for o in range(G):
-        ex_o = exa[:, o * qo:(o + 1) * qo, :].contiguous()
-        batches[o].pq_shard_final(ex_o.data_ptr(), G, qo, R, k, True)
+        tk_o = topk[:, o * qo:(o + 1) * qo, :].contiguous()
+        batches[o].pq_shard_final(tk_o.data_ptr(), G, qo, k, True)
         gi[o * qo:(o + 1) * qo], gd[o * qo:(o + 1) * qo] = batches[o].get_results(qo, k)
     oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
                               exp_probes, k, rerank_n=R, base_u8=p["base_u8"])

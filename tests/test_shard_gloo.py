@@ -6,8 +6,8 @@ stage-1 (ADC key, global position) lists restricted to its lists, and the
 exact key of every candidate.  The collectives of shard.py then move them and
 a NumPy mirror of the device merge forms the result, which must equal the
 unsharded oracle search.  A second test runs the phased protocol the same
-way (bounds minimum, stage-1 lists to the owners, prefix lengths back, exact
-keys of the prefixes to the owners).  A third drops a rank and checks that the
+way (bounds minimum, stage-1 lists to the owners, kappa back to the shards,
+each shard's exact top-k of its keys <= kappa to the owners).  A third drops a rank and checks that the
 survivor gets an error from the process-group timeout instead of hanging.
 """
 import os
@@ -135,8 +135,9 @@ def test_two_rank_exchange_equals_unsharded_oracle():
 
 
 def _phased_worker(rank, world, port, data, out):
-    """the phased protocol: bounds minimum, stage-1 lists to the owners, prefix
-    lengths back, prefix reranks, exact keys to the owners, owners' top-k."""
+    """the phased protocol: bounds minimum, stage-1 lists to the owners, kappa
+    (the R-th key of their union) back to every shard, each shard's exact top-k
+    of its keys <= kappa to the owners, owners' merge."""
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=__import__("datetime").timedelta(seconds=60))
     idx, q, probes, R, k = data["idx"], data["q"], data["probes"], data["R"], data["k"]
@@ -153,29 +154,32 @@ def _phased_worker(rank, world, port, data, out):
     allb = [torch.empty(nq, dtype=torch.int64) for _ in range(world)]
     dist.all_gather(allb, torch.from_numpy(mine))
     assert np.array_equal(got, np.min(np.stack([t.numpy() for t in allb]), axis=0))
-    # stage 1 of this shard: sorted R keys per query (global positions)
+    # stage 1 of this shard: R keys per query (global positions), in no particular order
     s1, ex = _shard_stage1(idx, q, probes, lists, R)
-    o = np.argsort(s1, axis=1, kind="stable")
-    s1, ex = np.take_along_axis(s1, o, 1), np.take_along_axis(ex, o, 1)
+    o = np.random.default_rng(7 + rank).permutation(R)
+    s1, ex = s1[:, o], ex[:, o]
     recv = torch.empty((world, qo, R), dtype=torch.int64)
     adc_o = shard.to_owners_raw(dist, world, as_t(s1), recv).numpy().view(np.uint64)     # [G][qo][R]
-    take = np.zeros((world, qo), np.int32)                  # owner: prefix of each shard's list
+    kap = np.zeros(qo, np.uint64)                           # owner: R-th smallest key of the union
     for i in range(qo):
         allk = np.sort(adc_o[:, i, :].reshape(-1))
         valid = allk[allk != NONE]
-        kap = valid[R - 1] if len(valid) > R else NONE - np.uint64(1)
-        for g in range(world):
-            take[g, i] = int(np.searchsorted(adc_o[g, i], kap, side="right"))
-    rtake = torch.empty((world, qo), dtype=torch.int32)
-    mytake = shard.take_to_sources(dist, world, torch.from_numpy(take), rtake).numpy()   # [nq]
-    # exact keys of the requested prefix only; the rest of the list stays NONE
-    exs = np.where(np.arange(R)[None, :] < mytake[:, None], ex, NONE)
-    recv2 = torch.empty((world, qo, R), dtype=torch.int64)
-    ex_o = shard.to_owners_raw(dist, world, as_t(exs), recv2).numpy().view(np.uint64)
+        kap[i] = valid[R - 1] if len(valid) > R else NONE - np.uint64(1)
+    kap_all = torch.empty((world * qo,), dtype=torch.int64)
+    kap_all = shard.kappa_to_shards(dist, torch.from_numpy(kap.view(np.int64)), kap_all).numpy().view(np.uint64)
+    # this shard's exact top-k of its distinct stage-1 keys <= kappa
+    top = np.full((nq, k), NONE, np.uint64)
+    for i in range(nq):
+        sel = (s1[i] != NONE) & (s1[i] <= kap_all[i])
+        _, first = np.unique(s1[i][sel], return_index=True)
+        e = np.sort(ex[i][sel][first])[:k]
+        top[i, :len(e)] = e
+    recv2 = torch.empty((world, qo, k), dtype=torch.int64)
+    top_o = shard.to_owners_raw(dist, world, as_t(top), recv2).numpy().view(np.uint64)     # [G][qo][k]
     ids = np.full((qo, k), -1, np.int32)
     dd = np.full((qo, k), np.inf, np.float32)
     for i in range(qo):
-        e = np.unique(ex_o[:, i, :].reshape(-1))
+        e = np.sort(top_o[:, i, :].reshape(-1))
         e = e[e != NONE][:k]
         for j, key in enumerate(e):
             ids[i, j] = int(key & np.uint64(0xFFFFFFFF))
