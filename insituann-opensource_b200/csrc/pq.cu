@@ -699,6 +699,7 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
                                                          uint64_t* out_topk) {
     extern __shared__ uint64_t sk[];            // [np] exact keys, [np] stage-1 keys, a table of rr_table(np) slots
     __shared__ __align__(16) float sq[kPMaxD];
+    __shared__ int s_live;
     __shared__ __align__(16) uint8_t squ[kPMaxD];
     const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, d = p.d;
     const int nb = NB ? NB : d / 16;
@@ -715,29 +716,55 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
         sq[j] = x;
         squ[j] = to_u8(x);
     }
-    // every candidate's stage-1 key in one coalesced pass (kKeyNone above the
-    // query's key limit and past the end)
-    for (int c = tid; c < np; c += kRRT) {
-        const uint64_t km1 = c < R ? s1m[(size_t)q * R + c] : kKeyNone;
-        s1[c] = c < R ? (km1 <= km ? km1 : kKeyNone)
-                      : (c < nc ? s1d[(size_t)q * Rd + (c - R)] : kKeyNone);
-    }
+    if (tid == 0) s_live = 0;
     if (!out_exm)
         for (int i = tid; i <= tmask; i += kRRT) tab[i] = kKeyNone;
     __syncthreads();
+    // every candidate's stage-1 key in one coalesced pass (kKeyNone above the
+    // query's key limit and past the end).  The per-candidate keys of a
+    // cross-shard merge keep their slots; the final top-k path packs the live
+    // keys to the front (one shared add per warp), delta keys tagged by bit 63
+    // (a distance's sign bit, always clear in a key), and works only on those.
+    for (int c0 = 0; c0 < np; c0 += kRRT) {
+        const int c = c0 + tid;
+        uint64_t key = kKeyNone;
+        if (c < R) {
+            const uint64_t km1 = s1m[(size_t)q * R + c];
+            key = km1 <= km ? km1 : kKeyNone;
+        } else if (c < nc) {
+            key = s1d[(size_t)q * Rd + (c - R)];
+            if (!out_exm && key != kKeyNone) key |= 1ull << 63;
+        }
+        if (out_exm) {
+            if (c < np) s1[c] = key;
+            continue;
+        }
+        const bool ok = key != kKeyNone;
+        const unsigned ball = __ballot_sync(0xffffffffu, ok);
+        int base = 0;
+        if (lane == 0 && ball) base = atomicAdd(&s_live, __popc(ball));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (ok) s1[base + __popc(ball & ((1u << lane) - 1u))] = key;
+    }
+    __syncthreads();
+    const int nlive = out_exm ? np : s_live;
     const int grp = tid >> 2, sub = tid & 3;
-    for (int c0 = 0; c0 < np; c0 += kRRT / 4) {
+    for (int c0 = 0; c0 < nlive; c0 += kRRT / 4) {
         const int c = c0 + grp;
         bool live = false, dl = false;
         uint64_t key = kKeyNone;
-        if (c < np) {
-            dl = c >= R;
+        if (c < nlive) {
             key = s1[c];
-            // the per-candidate keys of a cross-shard merge keep every entry; the
-            // final top-k reranks each position once (a list probed twice repeats
-            // its keys in stage 1; delta keys are told apart by bit 63)
-            if (out_exm) live = key != kKeyNone;
-            else if (sub == 0 && key != kKeyNone) live = hash_first(tab, tmask, dl ? (key | (1ull << 63)) : key);
+            if (out_exm) {
+                dl = c >= R;
+                live = key != kKeyNone;
+            } else {
+                dl = (key >> 63) != 0;
+                // the final top-k reranks each position once (a list probed
+                // twice repeats its keys in stage 1)
+                if (sub == 0) live = hash_first(tab, tmask, key);
+                key &= ~(1ull << 63);
+            }
         }
         if (!out_exm) live = __shfl_sync(0xffffffffu, live, lane & ~3);
         const ListStore& S = dl ? p.delta : p.main;
@@ -804,6 +831,8 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
             sk[c] = ek;
         }
     }
+    if (!out_exm)
+        for (int c = nlive + tid; c < np; c += kRRT) sk[c] = kKeyNone;
     __syncthreads();
     if (out_exm) return;
     if (k <= 16 && np <= 512) {
