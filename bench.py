@@ -42,6 +42,11 @@ for p in (os.path.join(ROOT, "insituann-opensource_b200"), os.path.join(ROOT, "o
 METRIC = "QPS @ recall@10≥0.9 vs nprobe; scanned GB/s vs 8 TB/s HBM; at 1/2/4/8 B200"
 
 CONFIGS = {
+    # the exact uint8 path (ivf_u8_search); one GPU
+    "c0": dict(kind="u8", n=1_000_000, d=128, ncomp=1024, sigma=12.0, nlist=1024, nq=10_000, k=10, nprobe=32,
+               seed=20260600, train_n=0, M=0, rerank_n=0, sweep=(32,),
+               desc="c0: exact IVF, 1M x 128 uint8 (1024-comp mixture, centers U[32,224], sigma 12), nlist 1024, "
+                    "10k queries, nprobe 32, k=10, exact int32 L2"),
     # BASELINE.json configs[1]
     # nprobe: the smallest sweep point whose recall@10 is >= 0.9 on this data (0.99998 measured at 8)
     "c1": dict(kind="f32", n=10_000_000, d=96, ncomp=4096, sigma=0.05, nlist=4096, M=48, train_n=500_000,
@@ -185,6 +190,161 @@ def time_reference(idx, q, probes, cfg, target_s, max_queries):
                 lib=os.path.basename(L.library_path), local_ids=ids)
 
 
+def build_workload_u8(cfg, device):
+    """c0: seeded uint8 data, exact index, exact ground truth (outside any timed region)."""
+    import torch
+
+    import synth
+
+    t0 = time.time()
+    base = synth.mixture_u8(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
+    q = synth.mixture_u8(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
+                         stream_base=1 << 30)
+    idx = synth.build_u8_index(base, cfg["nlist"], cfg["seed"], iters=20, kmeans_sample=64 * cfg["nlist"])
+    log(f"[bench] c0 data + index {time.time() - t0:.1f}s")
+    gt = synth.brute_force_gt(base, q, cfg["k"], batch_rows=1 << 16)
+    del base
+    torch.cuda.empty_cache()
+    return idx, q.float().cpu().numpy(), gt
+
+
+def time_reference_u8(idx, q, probes, cfg, target_s):
+    """Times oracle/_ref's cpu_fine_kernel_v3_u8_touched (all threads) on the batch, repeated to ~target_s."""
+    import oracle
+
+    L = oracle.ref_lib()
+    if L is None:
+        return None
+    threads = os.cpu_count() or 1
+    qu = oracle.make_query_u8(q)
+    oracle.ref_exact_u8_touched(idx["base_cm"], idx["offsets"], idx["counts"], qu[:64], probes[:64], cfg["k"],
+                                threads=threads)
+    done, dt, ids = 0, 0.0, None
+    while dt < target_s:
+        t = time.perf_counter()
+        ids, _ = oracle.ref_exact_u8_touched(idx["base_cm"], idx["offsets"], idx["counts"], qu, probes, cfg["k"],
+                                             threads=threads)
+        dt += time.perf_counter() - t
+        done += q.shape[0]
+    return dict(qps=done / dt, seconds=dt, sample=done, threads=threads, lib=os.path.basename(L.library_path),
+                local_ids=ids)
+
+
+def run_exact(args, cfg):
+    """c0 on one GPU: ivf_u8_search (routing, probe inversion, exact scan, top-k) over a resident batch."""
+    import torch
+
+    import insitu_b200 as ib
+    import oracle
+    import synth
+
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"metric": METRIC, "unavailable": "config c0 is a single-GPU bench line"}))
+        return
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(0)
+    nq, d, k, nlist = cfg["nq"], cfg["d"], cfg["k"], cfg["nlist"]
+    nprobe = args.nprobe or cfg["nprobe"]
+    idx, q_np, gt = build_workload_u8(cfg, dev)
+    index = ib.Index().load_u8(idx["base_cm"], idx["offsets"], idx["counts"], idx["r2o"], idx["centroids"])
+    batch = ib.Batch(nq, d, nprobe, k, nlist)
+    ext = torch.cuda.ExternalStream(batch.stream, device=dev)
+    q_dev = torch.from_numpy(q_np).to(dev)
+
+    def step():
+        batch.stage1_prepare_device(q_dev.data_ptr(), nq)
+        batch.u8_search(index, nq, nprobe, k, route=True)
+
+    step()
+    batch.sync()
+    ids_g, dist_g = batch.get_results(nq, k)
+    probes = batch.get_probes(nq, nprobe)
+    exp_p, _ = oracle.route_l2(q_np[:64], idx["centroids"], nprobe)
+    oi, od = oracle.exact_u8(idx["base_cm"], idx["offsets"], idx["counts"], idx["r2o"],
+                             oracle.make_query_u8(q_np[:64]), exp_p, k)
+    parity = bool(np.array_equal(probes[:64], exp_p) and np.array_equal(ids_g[:64], oi)
+                  and np.array_equal(dist_g[:64], od.astype(np.float32)))
+    recall = synth.recall_at_k(ids_g, gt, k)
+    log(f"[bench] c0 parity(64 queries vs oracle)={parity} recall@10={recall:.4f}")
+    for _ in range(args.warmup):
+        step()
+    batch.sync()
+    batch.profile(True)
+    launches0 = ib.kernel_launches()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(0) as clk:
+        torch.cuda.synchronize()
+        ev0.record(ext)
+        for _ in range(args.steps):
+            step()
+        ev1.record(ext)
+        torch.cuda.synchronize()
+    launches = ib.kernel_launches() - launches0
+    stage = batch.stage_ms()
+    batch.profile(False)
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+    value = nq / (ms_step / 1000.0)
+    # e2e: pinned host queries in, host results out, through the C ABI
+    hq = torch.from_numpy(q_np).pin_memory()
+    h_ids = torch.empty((nq, k), dtype=torch.int32).pin_memory()
+    h_dist = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        batch.stage1_prepare_ptr(hq.data_ptr(), nq)
+        batch.u8_search(index, nq, nprobe, k, route=True)
+        batch.get_results_into(h_dist.data_ptr(), h_ids.data_ptr(), nq, k)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        e2e_step()
+    e_ms = (time.perf_counter() - t0) * 1000.0 / args.steps
+    e2e = {"value": nq / (e_ms / 1000.0), "unit": "queries/s", "h2d_bytes_per_step": int(nq * d * 4),
+           "d2h_bytes_per_step": int(nq * k * 8)}
+    # roofline of the exact scan: sum over (query, probed list) of count * d
+    p = probes[probes >= 0]
+    bytes_search = int(idx["counts"][p].astype(np.int64).sum()) * d
+    scan_ms = stage["scan"] / args.steps
+    peak, peak_kind = peaks()
+    achieved = bytes_search / (scan_ms / 1000.0) / 1e9
+    traffic = None
+    prof_path = os.path.join(ROOT, "profiles", f"exact_scan_kernel_c0_nprobe{nprobe}.md")
+    if os.path.exists(prof_path):
+        for line in open(prof_path):
+            if line.startswith("dram_bytes_per_search:"):
+                traffic = int(line.split(":")[1].strip())
+    roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": traffic, "kernel": "exact_scan_kernel (1 launch per search)", "peak_source": peak_kind,
+                "algorithmic_bytes_per_launch": bytes_search, "kernel_ms_per_launch": scan_ms}
+    cpu = None
+    if not args.no_cpu_baseline:
+        S = 2048
+        r = time_reference_u8(idx, q_np[:S], probes[:S], cfg, target_s=12.0)
+        if r is not None:
+            cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
+                   "sample": f"{r['sample']} query searches ({S} distinct queries of the batch, repeated) with "
+                             f"reference cpu_fine_kernel_v3_u8_touched ({r['lib']}), probe lists given, "
+                             f"{r['seconds']:.1f}s"}
+    out = {
+        "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": {"workload": cfg["desc"], "n_base": cfg["n"], "d": d, "nlist": nlist, "nq": nq,
+                   "nprobe": nprobe, "k": k, "recall@10": recall, "recall_target_met": bool(recall >= 0.9),
+                   "parity_vs_oracle_64q": parity, "inputs_exceed_l2": True,
+                   "l2_note": "the 128 MB of vectors are probed 320k times per step (40 GB logical)",
+                   "parallelism": "single GPU"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
+        "clocks": clk.summary(), "stages_ms_per_step": {s_: v / args.steps for s_, v in stage.items()},
+        "sweep": [],
+    }
+    print(json.dumps(out), flush=True)
+    batch.close()
+    index.close()
+
+
 def run_reference_arm(args, cfg):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -197,6 +357,32 @@ def run_reference_arm(args, cfg):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (needs the reference tree)"}))
         return
     dev = torch.device("cuda", 0) if torch.cuda.is_available() else torch.device("cpu")
+    if cfg["kind"] == "u8":                    # c0: the reference's exact CPU kernel on the whole batch
+        import synth
+
+        idx, q, gt = build_workload_u8(cfg, dev)
+        nprobe = args.nprobe or cfg["nprobe"]
+        probes, _ = oracle.route_l2(q, idx["centroids"], nprobe)
+        times, samples = [], []
+        for step in range(args.warmup + args.steps):
+            r = time_reference_u8(idx, q, probes, cfg, target_s=4.0)
+            if step >= args.warmup:
+                times.append(r["seconds"])
+                samples.append(r["sample"])
+        qps = sum(samples) / sum(times)
+        rec = synth.recall_at_k(idx["r2o"][r["local_ids"]], gt, cfg["k"])
+        print(json.dumps({
+            "impl": "reference", "metric": METRIC, "value": qps, "unit": "queries/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * sum(times) / len(times),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+            "config": {"workload": cfg["desc"], "nprobe": nprobe, "k": cfg["k"], "recall@10": rec,
+                       "routing": "not timed (probe lists from the exact fp32 router)"},
+            "cpu_baseline": {"value": qps, "unit": "queries/s", "cores": r["threads"], "kind": "reference",
+                             "sample": f"{samples[-1]} query searches per step (the {cfg['nq']}-query batch, "
+                                       f"repeated), cpu_fine_kernel_v3_u8_touched ({r['lib']})"},
+            "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
     idx, q, gt = build_workload(cfg, dev)
     nprobe = args.nprobe or cfg["nprobe"]
     probes, _ = oracle.route_l2(q, idx["centroids"], nprobe)
@@ -244,6 +430,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference_arm(args, cfg)
+    if cfg["kind"] == "u8":
+        return run_exact(args, cfg)
 
     import torch
     import torch.distributed as dist
