@@ -413,7 +413,11 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
     void* tmp;
     size_t tmp_bytes;
-    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes);
+    // the grouped kernel reads every list once per 64 queries; its group words
+    // hold pair indices below 2^25
+    const bool grouped = exact_group_usable(x->d, k) && (size_t)nsub * nprobe < ((size_t)1 << 25);
+    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes, grouped);
+    if (grouped) wl.gq = 64;
     CandBuf cb{};
     cb.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap);
     cb.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
@@ -434,9 +438,14 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
         }
         {
             StageScope stage(b, IVF_STAGE_SCAN);
-            ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter,
-                          b->st),
-               "exact_scan");
+            if (grouped)
+                ck(exact_group_scan(b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl, n * nprobe, cb,
+                                    b->counter, b->st),
+                   "exact_group_scan");
+            else
+                ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter,
+                              b->st),
+                   "exact_scan");
         }
         uint64_t* dst = keys_out ? keys_out + (size_t)s * k : topk;
         {

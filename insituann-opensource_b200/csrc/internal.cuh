@@ -344,9 +344,12 @@ struct WorkList {              // probe inversion for one batch: list-major (que
     int32_t* n_pairs;          // -> list_off[nlist]
     int32_t* grp_cnt;          // [nlist+1] query groups per list (optional)
     int32_t* grp_off;          // [nlist+1] exclusive prefix of grp_cnt
-    int64_t* groups;           // [max_pairs] (list << 32) | (first pair << 3) | group size, list-major
+    int64_t* groups;           // [max_pairs] (list << 32) | (first pair << S) | group size, list-major
     int32_t* n_groups;         // -> grp_off[nlist]
+    int gq;                    // queries per group: 0 = kGroupQueries (4, S = 3); up to 127 (S = 7)
 };
+
+__host__ __device__ inline int group_shift(int gq) { return gq <= 7 ? 3 : 7; }
 
 struct CandBuf {               // per-query candidate buffers of one segment
     uint64_t* keys;            // [nq, cap]

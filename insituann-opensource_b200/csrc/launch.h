@@ -21,7 +21,8 @@ size_t worklist_scan_bytes(int nlist);
 // Builds list-major (query, list) pairs from probes [nq, nprobe] (global list
 // ids; list_map maps them to local lists or -1, nullptr = identity).
 // When wl.groups is set, also packs the pairs of every list into groups of up
-// to kGroupQueries consecutive pairs: groups[g] = (list << 32) | (first pair << 3) | size.
+// to wl.gq (0: kGroupQueries) consecutive pairs:
+// groups[g] = (list << 32) | (first pair << group_shift(gq)) | size.
 // Only probe-table columns col0 .. col0+ncol-1 are used (ncol <= 0: to the end).
 // seed_part >= 0 replaces the column range: 0 = each query's first probe whose
 // list is local, 1 = its other local probes.
@@ -88,6 +89,12 @@ cudaError_t keys_to_exact_results(const uint64_t* keys, int nq, int k, int32_t* 
                                   float* fdist, cudaStream_t st);
 
 // ---- exact uint8 fine search (exact.cu) -------------------------------------
+// Grouped exact scan (d = 128 or 256, k <= 16): groups of up to 64 queries per
+// list from wl.groups (wl.gq = 64); every (query, list) pair appends its k
+// smallest keys to the query's candidate buffer.
+bool exact_group_usable(int d, int k);
+cudaError_t exact_group_scan(const uint8_t* q_u8, int d, int k, ListStore ls, WorkList wl, int max_groups,
+                             CandBuf cb, int* work_counter, cudaStream_t st);
 cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkList wl, int max_pairs,
                        CandBuf cb, int* work_counter, cudaStream_t st);
 

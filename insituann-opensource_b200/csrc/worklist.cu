@@ -89,20 +89,21 @@ __global__ void fill_pairs_kernel(const int32_t* probes, size_t total, int nprob
     }
 }
 
-__global__ void group_count_kernel(const int32_t* list_cnt, int nlist, int32_t* grp_cnt) {
+__global__ void group_count_kernel(const int32_t* list_cnt, int nlist, int gq, int32_t* grp_cnt) {
     int l = blockIdx.x * blockDim.x + threadIdx.x;
-    if (l < nlist) grp_cnt[l] = (list_cnt[l] + kGroupQueries - 1) / kGroupQueries;
+    if (l < nlist) grp_cnt[l] = (list_cnt[l] + gq - 1) / gq;
     else if (l == nlist) grp_cnt[l] = 0;
 }
 
-__global__ void group_fill_kernel(const int32_t* list_off, const int32_t* grp_off, int nlist, int64_t* groups) {
+__global__ void group_fill_kernel(const int32_t* list_off, const int32_t* grp_off, int nlist, int gq, int shift,
+                                  int64_t* groups) {
     int l = blockIdx.x * blockDim.x + threadIdx.x;
     if (l >= nlist) return;
     const int first = list_off[l], n = list_off[l + 1] - first;
     int g = grp_off[l];
-    for (int o = 0; o < n; o += kGroupQueries) {
-        const int sz = n - o < kGroupQueries ? n - o : kGroupQueries;
-        groups[g++] = ((int64_t)l << 32) | (int64_t)(((first + o) << 3) | sz);
+    for (int o = 0; o < n; o += gq) {
+        const int sz = n - o < gq ? n - o : gq;
+        groups[g++] = ((int64_t)l << 32) | (int64_t)(((int64_t)(first + o) << shift) | sz);
     }
 }
 
@@ -161,12 +162,14 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
     }
     if (wl.groups) {
         note_launch();
-        group_count_kernel<<<(nlist_local + 256) / 256, 256, 0, st>>>(wl.list_cnt, nlist_local, wl.grp_cnt);
+        const int gq = wl.gq > 0 ? wl.gq : kGroupQueries;
+        group_count_kernel<<<(nlist_local + 256) / 256, 256, 0, st>>>(wl.list_cnt, nlist_local, gq, wl.grp_cnt);
         if ((e = cudaGetLastError())) return e;
         if ((e = cub::DeviceScan::ExclusiveSum(scan_tmp, scan_bytes, wl.grp_cnt, wl.grp_off, nlist_local + 1, st)))
             return e;
         note_launch();
-        group_fill_kernel<<<(nlist_local + 255) / 256, 256, 0, st>>>(wl.list_off, wl.grp_off, nlist_local, wl.groups);
+        group_fill_kernel<<<(nlist_local + 255) / 256, 256, 0, st>>>(wl.list_off, wl.grp_off, nlist_local, gq,
+                                                                       group_shift(gq), wl.groups);
         if ((e = cudaGetLastError())) return e;
     }
     return cudaSuccess;

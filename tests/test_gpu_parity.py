@@ -94,6 +94,38 @@ def test_exact_kat(cuda_ok, case):
     assert np.array_equal(gi, a["ids"]) and np.array_equal(gd, a["dist"])
 
 
+@pytest.mark.parametrize("d", [128, 256])
+@pytest.mark.parametrize("case", [c for c in json.load(open(os.path.join(GOLDEN, "kat.json")))
+                                  if c["kind"] == "exact"], ids=lambda c: f"k{c['k']}")
+def test_exact_kat_grouped(cuda_ok, case, d):
+    """the known-answer cases with rows and queries zero-padded to d = 128 / 256,
+    which leaves every distance unchanged and runs the grouped exact kernel."""
+    a = {k: np.array(v) for k, v in case.items() if isinstance(v, list)}
+    pad = lambda x: np.pad(x.astype(np.uint8), ((0, 0), (0, d - x.shape[1])))   # noqa: E731
+    cent = np.pad(a["centroids"].astype(np.float32), ((0, 0), (0, d - a["centroids"].shape[1])))
+    e = dict(base_cm=pad(a["base_cm"]), offsets=a["offsets"], counts=a["counts"], r2o=a["r2o"], centroids=cent)
+    gi, gd = gpu_exact(e, pad(a["q_u8"]), a["probes"], case["k"])
+    assert np.array_equal(gi, a["ids"]) and np.array_equal(gd, a["dist"])
+
+
+@pytest.mark.parametrize("d,k", [(128, 1), (128, 10), (128, 16), (128, 17), (256, 10)])
+def test_exact_grouped_many_queries(cuda_ok, d, k):
+    """more than 64 queries per list (several groups of one list), lists whose
+    length is no multiple of the tile, repeated and invalid probe ids; k = 17
+    runs the per-pair kernel, the others the grouped one."""
+    n, nlist, nq, nprobe = 9000, 24, 700, 6
+    base = synth.mixture_u8(n, d, 24, 12.0, seed=61)
+    e = synth.build_u8_index(base, nlist, seed=61, iters=5)
+    q = synth.mixture_u8(nq, d, 24, 12.0, seed=61, stream_base=1 << 20).numpy()
+    probes, _ = oracle.route_l2(q.astype(np.float32), e["centroids"], nprobe)
+    probes[::7, 2] = probes[::7, 0]          # a list probed twice
+    probes[::11, 3] = -1                     # an invalid probe id
+    probes[::13, 4] = nlist + 5
+    gi, gd = gpu_exact(e, q, probes, k)
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], q, probes, k)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+
+
 @pytest.mark.parametrize("name", ["pq_u8_small", "pq_f32_small"])
 def test_pq_golden(cuda_ok, name):
     g = load(name + ".npz")
