@@ -310,13 +310,13 @@ def run_exact(args, cfg):
     peak, peak_kind = peaks()
     achieved = bytes_search / (scan_ms / 1000.0) / 1e9
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", f"exact_scan_kernel_c0_nprobe{nprobe}.md")
+    prof_path = os.path.join(ROOT, "profiles", f"exact_group_kernel_c0_nprobe{nprobe}.md")
     if os.path.exists(prof_path):
         for line in open(prof_path):
             if line.startswith("dram_bytes_per_search:"):
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "exact_scan_kernel (1 launch per search)", "peak_source": peak_kind,
+                "traffic": traffic, "kernel": "exact_group_kernel<8> (1 launch per search)", "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": bytes_search, "kernel_ms_per_launch": scan_ms}
     cpu = None
     if not args.no_cpu_baseline:
