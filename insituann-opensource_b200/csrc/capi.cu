@@ -78,6 +78,7 @@ struct Segment {
     float* rr_f32 = nullptr;
     uint8_t* gring = nullptr;      // PQ codes in the grouped-ring tile layout
     int64_t* gring_off = nullptr;  // [nlist] byte offset of each list's tiles
+    int32_t* sqnorm = nullptr;     // [n] squared norm of each uint8 row (exact index)
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -87,7 +88,7 @@ struct Segment {
         *this = Segment();
     }
     ListStore view() const {
-        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, gring, gring_off, n};
+        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, gring, gring_off, n, sqnorm};
     }
 };
 
@@ -415,7 +416,8 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
     size_t tmp_bytes;
     // the grouped kernel reads every list once per 64 queries; its group words
     // hold pair indices below 2^25
-    const bool grouped = exact_group_usable(x->d, k) && (size_t)nsub * nprobe < ((size_t)1 << 25);
+    const bool grouped = exact_group_usable(x->d, k) && x->main.sqnorm != nullptr &&
+                         (size_t)nsub * nprobe < ((size_t)1 << 25);
     WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes, grouped);
     if (grouped) wl.gq = 64;
     CandBuf cb{};
@@ -937,6 +939,11 @@ int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets,
         try {
             load_lists(x, x->main, base_u8, (size_t)d, offsets, counts, reorder_to_original, nullptr, nlist, n);
             load_centroids(x, centroids, nlist, d);
+            if (n > 0) {
+                x->main.sqnorm = dalloc<int32_t>((size_t)n, x->main.owned);
+                ck(u8_row_sqnorms(x->main.data, n, d, x->main.sqnorm, 0), "u8_row_sqnorms");
+                ck(cudaDeviceSynchronize(), "u8_row_sqnorms");
+            }
         } catch (...) {
             x->main.release();
             free_all(x->owned);

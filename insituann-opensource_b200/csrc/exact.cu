@@ -103,30 +103,60 @@ constexpr int kXThreads = 256;
 constexpr int kXKMax = 16;          // largest k of the grouped kernel
 
 __host__ __device__ constexpr size_t exact_group_smem(int nw) {
-    return sizeof(uint4) * (size_t)(kXG + kXT) * nw           // queries, tile
+    return sizeof(uint4) * (size_t)(kXG + 2 * kXT) * nw       // queries, two tiles
            + sizeof(uint64_t) * (size_t)kXG * (kXKMax + kXT)   // top-k, staging
            + sizeof(uint64_t) * kXG                            // k-th key per query
-           + sizeof(int) * (size_t)(kXG + kXG + kXT + kXT);    // staged counts, |q|^2, |x|^2, ids
+           + sizeof(int) * (size_t)(kXG + kXG + 4 * kXT);      // staged counts, |q|^2, two tiles' |x|^2 and ids
+}
+
+__global__ void u8_sqnorm_kernel(const uint8_t* __restrict__ x, int64_t n, int nw, int32_t* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const uint4* r = reinterpret_cast<const uint4*>(x) + i * nw;
+        uint32_t s = 0;
+        for (int c = 0; c < nw; ++c) {
+            const uint4 v = __ldg(r + c);
+            s = __dp4a(v.x, v.x, s);
+            s = __dp4a(v.y, v.y, s);
+            s = __dp4a(v.z, v.z, s);
+            s = __dp4a(v.w, v.w, s);
+        }
+        out[i] = (int32_t)s;
+    }
 }
 
 template <int NW>  // 16-byte chunks per row, d = 16 NW; NW in {8, 16}
-__global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* __restrict__ q_u8, ListStore ls,
+__global__ void __launch_bounds__(kXThreads, 3) exact_group_kernel(const uint8_t* __restrict__ q_u8, ListStore ls,
                                                                 WorkList wl, CandBuf cb, int k, int* counter) {
     extern __shared__ __align__(16) unsigned char xsm[];
     uint4* sQ = reinterpret_cast<uint4*>(xsm);                          // [kXG][NW]
-    uint4* sX = sQ + kXG * NW;                                          // [kXT][NW]
-    uint64_t* sTop = reinterpret_cast<uint64_t*>(sX + kXT * NW);        // [kXG][kXKMax]
+    uint4* sX = sQ + kXG * NW;                                          // [2][kXT][NW]
+    uint64_t* sTop = reinterpret_cast<uint64_t*>(sX + 2 * kXT * NW);    // [kXG][kXKMax]
     uint64_t* sStage = sTop + kXG * kXKMax;                             // [kXG][kXT]
     uint64_t* sTau = sStage + kXG * kXT;                                // [kXG]
     int* sCnt = reinterpret_cast<int*>(sTau + kXG);                     // [kXG]
     int* sQn = sCnt + kXG;                                              // [kXG]
-    int* sXn = sQn + kXG;                                               // [kXT]
-    uint32_t* sId = reinterpret_cast<uint32_t*>(sXn + kXT);             // [kXT]
+    int* sXn = sQn + kXG;                                               // [2][kXT]
+    uint32_t* sId = reinterpret_cast<uint32_t*>(sXn + 2 * kXT);         // [2][kXT]
     __shared__ int s_item;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int qb = tid >> 4, vb = tid & 15;
     constexpr int d = 16 * NW;
     const int NG = *wl.n_groups;
+    // tile t0 of list rows from `off` into buffer b: rows, ids, squared norms
+    auto stage_tile = [&](int64_t off, int t0, int count, int b) {
+        const int nv = min(kXT, count - t0);
+        const uint4* src = reinterpret_cast<const uint4*>(ls.data + (size_t)(off + t0) * d);
+        uint4* dst = sX + b * kXT * NW;
+        for (int e = tid; e < nv * NW; e += kXThreads) {
+            const int r = e / NW, c = e % NW;
+            dst[r * NW + (c ^ (r & 7))] = __ldg(src + e);
+        }
+        if (tid < nv) {
+            const int64_t pos = off + t0 + tid;
+            sId[b * kXT + tid] = ls.ids ? (uint32_t)ls.ids[pos] : (uint32_t)pos;
+            sXn[b * kXT + tid] = ls.sqnorm[pos];
+        }
+    };
     for (;;) {
         __syncthreads();
         if (tid == 0) s_item = atomicAdd(counter, 1);
@@ -153,6 +183,7 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
             sCnt[r] = 0;
         }
         for (int e = tid; e < kXG * kXKMax; e += kXThreads) sTop[e] = kKeyNone;
+        if (count > 0) stage_tile(off, 0, count, 0);
         __syncthreads();
         if (tid < kXG) {
             uint32_t n2 = 0;
@@ -166,28 +197,13 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
             }
             sQn[tid] = (int)n2;
         }
-        for (int t0 = 0; t0 < count; t0 += kXT) {
+        __syncthreads();
+        // tile t in buffer t & 1 while tile t + 1 is staged into the other one;
+        // one barrier per tile
+        for (int t0 = 0, b = 0; t0 < count; t0 += kXT, b ^= 1) {
             const int nv = min(kXT, count - t0);
-            __syncthreads();                               // the previous tile is no longer read
-            const uint4* src = reinterpret_cast<const uint4*>(ls.data + (size_t)(off + t0) * d);
-            for (int e = tid; e < nv * NW; e += kXThreads) {
-                const int r = e / NW, c = e % NW;
-                sX[r * NW + (c ^ (r & 7))] = __ldg(src + e);
-            }
-            if (tid < nv) sId[tid] = ls.ids ? (uint32_t)ls.ids[off + t0 + tid] : (uint32_t)(off + t0 + tid);
-            __syncthreads();
-            if (tid < nv) {
-                uint32_t n2 = 0;
-#pragma unroll
-                for (int c = 0; c < NW; ++c) {
-                    const uint4 v = sX[tid * NW + (c ^ (tid & 7))];
-                    n2 = __dp4a(v.x, v.x, n2);
-                    n2 = __dp4a(v.y, v.y, n2);
-                    n2 = __dp4a(v.z, v.z, n2);
-                    n2 = __dp4a(v.w, v.w, n2);
-                }
-                sXn[tid] = (int)n2;
-            }
+            if (t0 + kXT < count) stage_tile(off, t0 + kXT, count, b ^ 1);
+            const uint4* tile = sX + b * kXT * NW;
             // q.x for this thread's 4 x 4 (query, row) pairs
             uint32_t acc[4][4];
 #pragma unroll
@@ -203,7 +219,7 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
                     qa[i] = sQ[r * NW + (c ^ (r & 7))];
                 }
 #pragma unroll
-                for (int j = 0; j < 4; ++j) xa[j] = sX[(vb + 16 * j) * NW + (c ^ (vb & 7))];
+                for (int j = 0; j < 4; ++j) xa[j] = tile[(vb + 16 * j) * NW + (c ^ (vb & 7))];
 #pragma unroll
                 for (int i = 0; i < 4; ++i)
 #pragma unroll
@@ -214,19 +230,19 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
                         acc[i][j] = __dp4a(qa[i].w, xa[j].w, acc[i][j]);
                     }
             }
-            __syncthreads();                               // |x|^2 of the tile
             // keys below the query's current k-th go to its staging list
             bool any = false;
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 const int r = 4 * qb + i;
                 const uint64_t tau = sTau[r];
+                const int qn = sQn[r];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int v = vb + 16 * j;
                     if (r < nqg && v < nv) {
-                        const uint32_t dist = (uint32_t)(sQn[r] + sXn[v]) - 2u * acc[i][j];
-                        const uint64_t key = make_key(dist, sId[v]);
+                        const uint32_t dist = (uint32_t)(qn + sXn[b * kXT + v]) - 2u * acc[i][j];
+                        const uint64_t key = make_key(dist, sId[b * kXT + v]);
                         if (key < tau) {
                             sStage[r * kXT + atomicAdd(&sCnt[r], 1)] = key;
                             any = true;
@@ -277,6 +293,7 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
                     __syncwarp();
                 }
             }
+            __syncthreads();                               // tile t + 1 staged; tile t no longer read
         }
         __syncthreads();
         // every query's k smallest keys of this list into its candidate buffer
@@ -309,9 +326,19 @@ __global__ void __launch_bounds__(kXThreads) exact_group_kernel(const uint8_t* _
 
 bool exact_group_usable(int d, int k) { return (d == 128 || d == 256) && k > 0 && k <= kXKMax; }
 
+cudaError_t u8_row_sqnorms(const uint8_t* x, int64_t n, int d, int32_t* out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    if (d % 16 != 0) return cudaErrorInvalidValue;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    note_launch();
+    u8_sqnorm_kernel<<<(int)blocks, 256, 0, st>>>(x, n, d / 16, out);
+    return cudaGetLastError();
+}
+
 cudaError_t exact_group_scan(const uint8_t* q_u8, int d, int k, ListStore ls, WorkList wl, int max_groups,
                              CandBuf cb, int* work_counter, cudaStream_t st) {
-    if (!exact_group_usable(d, k) || !wl.groups) return cudaErrorInvalidValue;
+    if (!exact_group_usable(d, k) || !wl.groups || !ls.sqnorm) return cudaErrorInvalidValue;
     if (max_groups <= 0) return cudaSuccess;
     cudaError_t e = cudaMemsetAsync(work_counter, 0, sizeof(int), st);
     if (e) return e;

@@ -333,6 +333,7 @@ struct ListStore {             // one cluster-major segment (main index or a del
     const uint8_t* gring;      // PQ codes in the grouped-ring tile layout (pq.cu), or nullptr
     const int64_t* gring_off;  // [nlist] byte offset of each list's first tile
     int64_t n;
+    const int32_t* sqnorm;     // [n] sum of squares of each uint8 row (exact index), or nullptr
 };
 
 struct WorkList {              // probe inversion for one batch: list-major (query, list) pairs

@@ -89,6 +89,8 @@ cudaError_t keys_to_exact_results(const uint64_t* keys, int nq, int k, int32_t* 
                                   float* fdist, cudaStream_t st);
 
 // ---- exact uint8 fine search (exact.cu) -------------------------------------
+// out[i] = sum_j x[i][j]^2 for n uint8 rows of d bytes (d % 16 == 0), exact int32.
+cudaError_t u8_row_sqnorms(const uint8_t* x, int64_t n, int d, int32_t* out, cudaStream_t st);
 // Grouped exact scan (d = 128 or 256, k <= 16): groups of up to 64 queries per
 // list from wl.groups (wl.gq = 64); every (query, list) pair appends its k
 // smallest keys to the query's candidate buffer.
