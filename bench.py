@@ -53,6 +53,11 @@ CONFIGS = {
                nq=10_000, k=10, rerank_n=512, nprobe=8, sweep=(8, 16, 32, 64, 128), seed=20260601,
                desc="c1: residual-PQ IVF, 10M x 96 fp32 unit-norm (4096-comp mixture, sigma 0.05), nlist 4096, "
                     "M=48 x 8b, 10k queries, k=10, rerank_n=512 (fp32 rerank)"),
+    # BASELINE.json configs[2] on one GPU: 100M x 128 uint8, residual PQ M=32 (dsub 4), uint8 rerank
+    "c2": dict(kind="pq_u8", n=100_000_000, d=128, ncomp=65536, sigma=10.0, nlist=65536, M=32, train_n=500_000,
+               nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16, 32, 64, 128, 256), seed=20260602,
+               desc="c2: residual-PQ IVF, 100M x 128 uint8 (65536-comp mixture, centers U[32,224], sigma 10), "
+                    "nlist 65536, M=32 x 8b, 10k queries, k=10, rerank_n=512 (uint8 rerank)"),
     # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
     "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
                    nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,
@@ -142,9 +147,14 @@ def build_workload(cfg, device):
     import synth
 
     t0 = time.time()
-    base = synth.mixture_f32_unit(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
-    q = synth.mixture_f32_unit(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
-                               stream_base=1 << 30)
+    if cfg["kind"] == "pq_u8":
+        base = synth.mixture_u8(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
+        q = synth.mixture_u8(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
+                             stream_base=1 << 30).float()
+    else:
+        base = synth.mixture_f32_unit(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
+        q = synth.mixture_f32_unit(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
+                                   stream_base=1 << 30)
     log(f"[bench] data {time.time() - t0:.1f}s")
     idx = synth.build_pq_index(base, cfg["nlist"], cfg["M"], cfg["seed"], kmeans_iters=20, pq_iters=12,
                                train_n=cfg["train_n"], kmeans_sample=64 * cfg["nlist"])
@@ -154,6 +164,11 @@ def build_workload(cfg, device):
     del base
     torch.cuda.empty_cache()
     return idx, q.cpu().numpy(), gt
+
+
+def rr_kw(rows):
+    """rerank rows as the loaders and the oracle take them: uint8 or fp32 by dtype."""
+    return {"base_u8": rows} if rows.dtype == np.uint8 else {"base_f32": rows}
 
 
 def algorithmic_bytes(probes, counts, M):
@@ -176,10 +191,13 @@ def time_reference(idx, q, probes, cfg, target_s, max_queries):
     if L is None:
         return None
     threads = os.cpu_count() or 1
-    kw = dict(rerank_n=cfg["rerank_n"], base_f32=idx["base_rr"], threads=threads)
+    kw = dict(rerank_n=cfg["rerank_n"], threads=threads, **rr_kw(idx["base_rr"]))
     args = (idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"])
     S = min(max_queries, q.shape[0])
-    oracle.ref_pq_resid(*args, q[:min(S, 64)], probes[:min(S, 64)], cfg["k"], **kw)   # warm-up
+    if idx["base_rr"].dtype == np.uint8:
+        kw["q_u8"] = oracle.make_query_u8(q[:S])
+    kw64 = dict(kw, q_u8=kw["q_u8"][:min(S, 64)]) if "q_u8" in kw else kw
+    oracle.ref_pq_resid(*args, q[:min(S, 64)], probes[:min(S, 64)], cfg["k"], **kw64)   # warm-up
     done, dt, ids = 0, 0.0, None
     while dt < target_s:
         t = time.perf_counter()
@@ -489,14 +507,14 @@ def main():
     index = ib.Index()
     if N == 1:
         index.load_pq(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
-                      base_f32=idx["base_rr"])
+                      **rr_kw(idx["base_rr"]))
         my_lists = np.arange(nlist)
     else:
-        owner = shard.lpt_shards(counts, M + 4 * d, N)
+        owner = shard.lpt_shards(counts, M + idx["base_rr"].itemsize * d, N)
         my_lists = np.where(owner == rank)[0].astype(np.int32)
         rows, off, cnt = shard.shard_rows(offsets, counts, my_lists)
         index.load_pq(idx["centroids"][my_lists], idx["codebook"], idx["codes"][rows], off, cnt, idx["r2o"][rows],
-                      base_f32=idx["base_rr"][rows])
+                      **rr_kw(idx["base_rr"][rows]))
         index.set_shard(nlist, my_lists, offsets[my_lists])
     batch = ib.Batch(nq, d, max(nprobe, max(cfg["sweep"])), k, nlist)
     ext = torch.cuda.ExternalStream(batch.stream, device=dev)
@@ -621,7 +639,7 @@ def main():
         sub = 64
         probes_o, _ = oracle.route_l2(q_np[:sub], idx["centroids"], nprobe)
         oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
-                                  q_np[:sub], probes_o, k, rerank_n=R, base_f32=idx["base_rr"])
+                                  q_np[:sub], probes_o, k, rerank_n=R, **rr_kw(idx["base_rr"]))
         parity = bool(np.array_equal(oi, ids_g[:sub]) and np.array_equal(od, dist_g[:sub]))
         if probes_g is not None:
             parity = parity and bool(np.array_equal(probes_g[:sub], probes_o))
@@ -733,7 +751,8 @@ def main():
             if line.startswith("dram_bytes_per_search:"):
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "pq_stagger_kernel<48,2> (2 launches per search)", "peak_source": peak_kind,
+                "traffic": traffic, "kernel": f"pq_stagger_kernel<{M},{d // M}> (2 launches per search)",
+                "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": bytes_per_launch, "kernel_ms_per_launch": scan_ms}
 
     cpu = None
@@ -743,7 +762,8 @@ def main():
         if r is not None:
             cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
                    "sample": f"{r['sample']} query searches ({r['distinct']} distinct queries of the batch, "
-                             f"repeated) with reference cpu_fine_kernel_pq_resid (stage 1 + fp32 rerank, "
+                             f"repeated) with reference cpu_fine_kernel_pq_resid (stage 1 + "
+                             f"{'uint8' if idx['base_rr'].dtype == np.uint8 else 'fp32'} rerank, "
                              f"{r['lib']}), probe lists given, {r['seconds']:.1f}s"}
 
     if rank == 0:
@@ -755,7 +775,9 @@ def main():
                        "nq": nq, "nprobe": nprobe, "k": k, "rerank_n": R,
                        "recall@10": synth.recall_at_k(ids_g, gt, k), "recall_target_met": bool(
                            synth.recall_at_k(ids_g, gt, k) >= 0.9), "parity_vs_oracle_64q": parity,
-                       "inputs_exceed_l2": True, "l2_note": "480 MB of codes and 3.84 GB of rerank rows per step",
+                       "inputs_exceed_l2": True,
+                       "l2_note": f"{idx['codes'].nbytes / 1e6:.0f} MB of codes and "
+                                  f"{idx['base_rr'].nbytes / 1e9:.2f} GB of rerank rows per step",
                        "parallelism": "single GPU" if N == 1 else f"lists sharded x{N} (LPT by bytes), NCCL"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks, "stages_ms_per_step": {s: v / args.steps for s, v in stage.items()},

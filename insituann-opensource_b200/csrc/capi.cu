@@ -337,8 +337,11 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
     uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
     StageScope stage(b, IVF_STAGE_ROUTE);
+    // default policy (mode 1): the fused tensor-core kernel for nprobe <= 8 where
+    // it fits; the tensor-core matrix + rescoring for 8192 lists or more (2x the
+    // exact kernels' speed at 65536 lists, d 128); the exact kernels otherwise
     const int mode = x->tc_ops ? route_tc_mode() : 0;
-    const bool tc = mode == 2;
+    const bool tc = mode == 2 || (mode == 1 && x->nlist >= 8192);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
         const float* qs = b->q + (size_t)s * x->d;
