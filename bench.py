@@ -443,6 +443,8 @@ def main():
     ap.add_argument("--nprobe", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--overlay", type=int, default=0,
+                    help="also time the search with a published delta segment of this many vectors (1 GPU)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     args.warmup = max(args.warmup, 3)
@@ -732,6 +734,50 @@ def main():
     e2e = {"value": nq / (e_ms / args.steps / 1000.0), "unit": "queries/s",
            "h2d_bytes_per_step": int(nq * d * 4 * N), "d2h_bytes_per_step": int(nq * k * 8)}
 
+    # ---- update overlay (BASELINE configs[4] style): a published delta segment of
+    # seeded uniform codes (the reference's generators), ids after the base, scanned in
+    # the same launches as the main lists; QPS with and without it ----
+    overlay = None
+    if args.overlay > 0 and N == 1:
+        t_g = time.time()
+        dseg = synth.delta_segment(args.overlay, nlist, M, base_id=cfg["n"], d=d, seed=cfg["seed"] + 1,
+                                   f32=idx["base_rr"].dtype != np.uint8)
+        raw = {"raw_f32": dseg["raw_f32"]} if "raw_f32" in dseg else {"raw_u8": dseg["raw_u8"]}
+        index.publish_delta(dseg["codes"], dseg["ids"], dseg["counts"], dseg["offsets"], **raw)
+        log(f"[bench] delta segment of {args.overlay} vectors published in {time.time() - t_g:.1f}s")
+
+        def ostep(np_, ov):
+            batch.stage1_prepare_device(q_dev.data_ptr(), nq)
+            batch.pq_search(index, nq, np_, k, rerank_n=R, overlay=ov, delta_topk=16, route=True)
+
+        ostep(nprobe, True)
+        batch.sync()
+        oid, odd = batch.get_results(nq, k)
+        po, _ = oracle.route_l2(q_np[:64], idx["centroids"], nprobe)
+        ei, ed = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
+                                  q_np[:64], po, k, rerank_n=R, delta=dseg, delta_topk=16, **rr_kw(idx["base_rr"]))
+        o_par = bool(np.array_equal(ei, oid[:64]) and np.array_equal(ed, odd[:64]))
+        rows = []
+        for np_ in sorted({nprobe, 64}):
+            res = {}
+            for ov in (False, True):
+                for _ in range(args.warmup):
+                    ostep(np_, ov)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                torch.cuda.synchronize()
+                e0.record(ext)
+                for _ in range(args.steps):
+                    ostep(np_, ov)
+                e1.record(ext)
+                torch.cuda.synchronize()
+                res[ov] = nq / (e0.elapsed_time(e1) / args.steps / 1000.0)
+            rows.append({"nprobe": np_, "qps_without": res[False], "qps_with": res[True],
+                         "overhead": 1.0 - res[True] / res[False]})
+        overlay = {"delta_vectors": args.overlay, "delta_topk": 16, "parity_vs_oracle_64q": o_par, "runs": rows}
+        log(f"[bench] overlay parity={o_par} " + ", ".join(
+            f"nprobe {r_['nprobe']}: {r_['qps_without']:.0f} -> {r_['qps_with']:.0f} qps" for r_ in rows))
+        index.clear_delta()
+
     # ---- roofline of the ADC scan kernel (this rank) ----
     if probes_all is None:
         probes_all = batch.get_probes(nq, nprobe)
@@ -783,6 +829,7 @@ def main():
             "clocks": clocks, "stages_ms_per_step": {s: v / args.steps for s, v in stage.items()},
             "gbs_scanned_logical": bytes_total / (ms_step / 1000.0) / 1e9,
             "sweep": sweep,
+            "overlay": overlay,
         }
         print(json.dumps(out), flush=True)
     torch.cuda.synchronize()
