@@ -150,3 +150,30 @@ def test_reorder_is_stable():
     assert r2o.tolist() == [1, 4, 3, 0, 2, 5]
     c2, o2, r2 = oracle.reorder(a, 3)
     assert np.array_equal(c2, counts) and np.array_equal(o2, offsets) and np.array_equal(r2, r2o)
+
+
+@pytest.mark.parametrize("d,M", [(48, 24), (96, 48), (100, 25)])
+def test_fp32_rerank_matches_reference_on_fresh_data(d, M):
+    """the oracle's fp32 rerank distance against the reference kernel compiled with
+    AVX-512 (the build the golden fixtures come from) on freshly generated indexes,
+    including d = 100, whose last 4 dimensions follow the 16-lane blocks."""
+    L = oracle.ref_lib()
+    if L is None or not L.library_path.endswith("libref_cpu_fine.so"):
+        pytest.skip("the reference's AVX-512 build is not available on this host")
+    rng = np.random.default_rng(d)
+    n, nlist, nq, nprobe, k, R = 4000, 16, 50, 4, 10, 64
+    base = rng.standard_normal((n, d)).astype(np.float32)
+    assign = rng.integers(0, nlist, n)
+    counts, offsets, r2o = synth.reorder(assign, nlist)
+    base_cm = base[r2o]
+    cent = np.stack([base[assign == c].mean(0) if (assign == c).any() else np.zeros(d, np.float32)
+                     for c in range(nlist)]).astype(np.float32)
+    codebook = rng.standard_normal((M, 256, d // M)).astype(np.float32)
+    codes = rng.integers(0, 256, size=(n, M), dtype=np.uint8)
+    q = rng.standard_normal((nq, d)).astype(np.float32)
+    probes, _ = oracle.route_l2(q, cent, nprobe)
+    ids, dist = oracle.pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_n=R,
+                                 base_f32=base_cm)
+    r_local, r_dist, _, _ = oracle.ref_pq_resid(cent, codebook, codes, offsets, counts, q, probes, k,
+                                                rerank_n=R, base_f32=base_cm)
+    _compare_to_reference(ids, dist, r2o[r_local], r_dist)
