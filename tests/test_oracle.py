@@ -134,6 +134,9 @@ def test_delta_generators_match_reference_formulas():
         x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & ((1 << 64) - 1)
         return x ^ (x >> 31)
 
+    # the published first output of splitmix64 from state 0 pins the mixing constants
+    assert sm(0) == 0xE220A8397B1DCDAF
+    assert int(synth.splitmix64(np.array([0], np.uint64))[0]) == 0xE220A8397B1DCDAF
     local = np.array([0, 1, 2, 12345, 999999], np.int64)
     lists = synth.delta_list_of(local, 65536)
     codes = synth.delta_codes_of(local, 4)
