@@ -220,7 +220,11 @@ int ivf_u8_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int
 /*
  * residual-PQ search: routing (if route != 0) + stage 1 with rerank_n
  * candidates (+ delta_topk from the delta segment when use_overlay != 0 and
- * one is published; the reference uses 16, pq_update.cu:25) + exact rerank.
+ * one is published; the reference uses 16, pq_update.cu:25) + exact rerank
+ * (int32 on uint8 rows; fp32 rows in the reference's AVX-512 order of
+ * operations, cpu_fine_kernels_pq_resid.cpp:106-131, so distances equal the
+ * reference's bit for bit).  A position that stage 1 holds twice (a list
+ * probed twice) is reranked once.
  */
 int ivf_pq_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k, int rerank_n,
                   int use_overlay, int delta_topk, int route);
