@@ -189,6 +189,18 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
  */
 int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, const long long* key_offsets);
 
+/*
+ * Query-time deletes (the reference applies them inside its runners,
+ * updates/exact_update.cu:54, 89, 354-407 and updates/pq_update.cu:45,
+ * 503-523): deleted [n] holds one byte per cluster-major position of the
+ * loaded index (nonzero = deleted; NULL clears the mask).  The exact search
+ * does not scan deleted positions; the residual-PQ search keeps them in stage
+ * 1 (they take candidate slots, as in the reference) and does not rerank them.
+ * The delta segment has no deletes.  Waits for the device before replacing
+ * the mask.
+ */
+int ivf_set_deleted(void* idx_ctx, const unsigned char* deleted, long long n);
+
 /* ======================================================================
  * Update overlay (new: runner-internal in the reference,
  * updates/pq_update.cu:396-494, 975-1055)

@@ -79,6 +79,7 @@ struct Segment {
     uint8_t* gring = nullptr;      // PQ codes in the grouped-ring tile layout
     int64_t* gring_off = nullptr;  // [nlist] byte offset of each list's tiles
     int32_t* sqnorm = nullptr;     // [n] squared norm of each uint8 row (exact index)
+    uint8_t* deleted = nullptr;    // [n] delete mask by position (ivf_set_deleted), or nullptr
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -88,7 +89,7 @@ struct Segment {
         *this = Segment();
     }
     ListStore view() const {
-        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, gring, gring_off, n, sqnorm};
+        return ListStore{data, offsets, counts, ids, key_off, rr_u8, rr_f32, gring, gring_off, n, sqnorm, deleted};
     }
 };
 
@@ -954,6 +955,33 @@ int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets,
         }
         x->n = n;
         x->kind = kKindU8;
+    });
+}
+
+int ivf_set_deleted(void* idx_ctx, const unsigned char* deleted, long long n) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->kind != kKindEmpty, "no index loaded", IVF_ESTATE);
+        cudaSetDevice(x->device);
+        ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // no search may still read the old mask
+        if (x->main.deleted) {
+            for (auto it = x->main.owned.begin(); it != x->main.owned.end(); ++it)
+                if (*it == x->main.deleted) {
+                    x->main.owned.erase(it);
+                    break;
+                }
+            cudaFree(x->main.deleted);
+            x->main.deleted = nullptr;
+        }
+        if (!deleted) return;
+        require(n == x->main.n, "the delete mask must have one byte per position of the index");
+        x->main.deleted = dcopy(deleted, (size_t)n, x->main.owned);
     });
 }
 

@@ -70,7 +70,8 @@ __global__ void __launch_bounds__(kET) exact_scan_kernel(const uint8_t* __restri
                     }
                 }
                 const uint32_t id = ls.ids ? (uint32_t)ls.ids[pos] : (uint32_t)pos;
-                skeys[v] = make_key(acc, id);
+                // deleted positions are not scanned (exact_update.cu:89)
+                skeys[v] = (ls.deleted && ls.deleted[pos]) ? kKeyNone : make_key(acc, id);
             }
             __syncthreads();
             auto keyf = [&](int i) -> uint64_t { return skeys[i]; };
@@ -153,7 +154,9 @@ __global__ void __launch_bounds__(kXThreads, 3) exact_group_kernel(const uint8_t
         }
         if (tid < nv) {
             const int64_t pos = off + t0 + tid;
-            sId[b * kXT + tid] = ls.ids ? (uint32_t)ls.ids[pos] : (uint32_t)pos;
+            // a deleted position gets the id 0xFFFFFFFF, which no row passes (exact_update.cu:89)
+            sId[b * kXT + tid] = (ls.deleted && ls.deleted[pos]) ? 0xFFFFFFFFu
+                                                                 : (ls.ids ? (uint32_t)ls.ids[pos] : (uint32_t)pos);
             sXn[b * kXT + tid] = ls.sqnorm[pos];
         }
     };
@@ -240,7 +243,7 @@ __global__ void __launch_bounds__(kXThreads, 3) exact_group_kernel(const uint8_t
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
                     const int v = vb + 16 * j;
-                    if (r < nqg && v < nv) {
+                    if (r < nqg && v < nv && sId[b * kXT + v] != 0xFFFFFFFFu) {
                         const uint32_t dist = (uint32_t)(qn + sXn[b * kXT + v]) - 2u * acc[i][j];
                         const uint64_t key = make_key(dist, sId[b * kXT + v]);
                         if (key < tau) {

@@ -334,6 +334,7 @@ struct ListStore {             // one cluster-major segment (main index or a del
     const int64_t* gring_off;  // [nlist] byte offset of each list's first tile
     int64_t n;
     const int32_t* sqnorm;     // [n] sum of squares of each uint8 row (exact index), or nullptr
+    const uint8_t* deleted;    // [n] nonzero = deleted position (not scanned / not reranked), or nullptr
 };
 
 struct WorkList {              // probe inversion for one batch: list-major (query, list) pairs

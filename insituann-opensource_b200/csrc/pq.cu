@@ -768,7 +768,9 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
         }
         if (!out_exm) live = __shfl_sync(0xffffffffu, live, lane & ~3);
         const ListStore& S = dl ? p.delta : p.main;
-        const int64_t lp = live ? local_pos(S, key_lo(key), nlist) : 0;
+        int64_t lp = live ? local_pos(S, key_lo(key), nlist) : 0;
+        // a deleted position keeps its stage-1 slot but is not reranked (pq_update.cu:503-523)
+        if (live && S.deleted && S.deleted[lp]) live = false;
         uint32_t hi;
         if (f32) {
             float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;

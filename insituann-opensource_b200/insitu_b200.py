@@ -38,7 +38,7 @@ EXPORTS = [
     "ivf_u8_load", "ivf_pq_load", "ivf_set_shard", "ivf_pq_publish_delta", "ivf_pq_clear_delta",
     "ivf_route", "ivf_set_probes", "ivf_get_probes", "ivf_u8_search", "ivf_pq_search", "ivf_get_results_i32",
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
-    "ivf_route_keys", "ivf_route_merge", "ivf_route_merge_shards", "ivf_pq_search_shard", "ivf_pq_merge_shards",
+    "ivf_route_keys", "ivf_route_merge", "ivf_route_merge_shards", "ivf_set_deleted", "ivf_pq_search_shard", "ivf_pq_merge_shards",
     "ivf_u8_search_shard", "ivf_u8_merge_shards", "ivf_pq_shard_scan", "ivf_pq_shard_bounds",
     "ivf_pq_shard_select", "ivf_pq_shard_kappa", "ivf_pq_shard_rerank", "ivf_pq_shard_final",
     "ivf_last_error", "ivf_global_last_error",
@@ -88,6 +88,7 @@ _SIGS = {
     "ivf_route_keys": ([vp, vp, i32, i32, vp], i32),
     "ivf_route_merge": ([vp, vp, i32, i32, i32], i32),
     "ivf_route_merge_shards": ([vp, vp, i32, i32, i32], i32),
+    "ivf_set_deleted": ([vp, vp, i64], i32),
     "ivf_pq_search_shard": ([vp, vp, i32, i32, i32, i32, vp, vp, vp, vp], i32),
     "ivf_pq_merge_shards": ([vp, vp, vp, i32, i32, vp, vp, i32, i32, i32, i32, i32], i32),
     "ivf_u8_search_shard": ([vp, vp, i32, i32, i32, vp], i32),
@@ -215,6 +216,12 @@ class Index:
 
     def clear_delta(self):
         self._check(self.L.ivf_pq_clear_delta(self.h))
+
+    def set_deleted(self, deleted=None):
+        """per-position delete mask (uint8 [n], nonzero = deleted), or None to clear it."""
+        m = None if deleted is None else _c(deleted, np.uint8)
+        self._check(self.L.ivf_set_deleted(self.h, _p(m), 0 if m is None else m.shape[0]))
+        return self
 
     def close(self):
         if self.h:

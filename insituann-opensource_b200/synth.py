@@ -53,6 +53,33 @@ def delta_codes_of(local_ids: np.ndarray, M: int) -> np.ndarray:
     return (splitmix64(x ^ salt[None, :]) & np.uint64(255)).astype(np.uint8)
 
 
+def delete_mask(position_ids: np.ndarray, ratio: float, protected_ids=None) -> np.ndarray:
+    """Per-position delete mask (1 = deleted) in the reference's form
+    (updates/exact_update.cu:354-407): an id is deleted when
+    splitmix64(id) < ratio * (2^64 - 1), compared in x86 extended precision
+    (long double), unless it is protected; ratio <= 0 deletes nothing and
+    ratio >= 1 every id >= 0.  position_ids[pos] is the original id of each
+    cluster-major position (reorder_to_original)."""
+    ids = np.asarray(position_ids, dtype=np.int64)
+    out = np.zeros(ids.shape[0], np.uint8)
+    if ratio <= 0.0:
+        return out
+    ok = ids >= 0
+    if ratio >= 1.0:
+        out[ok] = 1
+    else:
+        threshold = np.longdouble(ratio) * np.longdouble(np.iinfo(np.uint64).max)
+        h = splitmix64(ids.astype(np.uint64))
+        out[ok & (h.astype(np.longdouble) < threshold)] = 1
+    if protected_ids is not None:
+        prot = np.zeros(max(int(ids.max(initial=0)) + 1, 1), bool)
+        p = np.asarray(protected_ids, dtype=np.int64)
+        p = p[(p >= 0) & (p < prot.shape[0])]
+        prot[p] = True
+        out[ok & prot[np.clip(ids, 0, prot.shape[0] - 1)]] = 0
+    return out
+
+
 def _gen(seed: int, stream: int, device) -> torch.Generator:
     g = torch.Generator(device=device)
     g.manual_seed(int(splitmix64(np.uint64((seed * 1_000_003 + stream) & MASK64))) & ((1 << 63) - 1))

@@ -211,13 +211,14 @@ static inline float l2_f32_rerank(const float* q, const float* v, int d) {
 /*
  * Exact int32 L2 over the probed lists -> top-k by (dist, original id).
  * Probe ids outside [0, nlist) are skipped; a list probed twice contributes
- * its vectors twice (as the reference does).  Output: original ids and int32
- * distances; empty slots are id -1 / INT32_MAX.
+ * its vectors twice (as the reference does); positions with deleted[pos] != 0
+ * (deleted may be NULL) are not scanned (exact_update.cu:54, 89).  Output:
+ * original ids and int32 distances; empty slots are id -1 / INT32_MAX.
  */
 ORACLE_API int oracle_exact_u8(const uint8_t* base_u8, const int64_t* offsets, const int32_t* counts,
                                const int32_t* r2o, int nlist, int d,
                                const uint8_t* q_u8, const int32_t* probes, int nq, int nprobe, int k,
-                               int32_t* out_ids, int32_t* out_dist) {
+                               const uint8_t* deleted, int32_t* out_ids, int32_t* out_dist) {
     if (k <= 0 || d <= 0) return -1;
     uint64_t* buf = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)k);
     if (!buf) return -2;
@@ -230,6 +231,7 @@ ORACLE_API int oracle_exact_u8(const uint8_t* base_u8, const int64_t* offsets, c
             int64_t off = offsets[c];
             for (int32_t v = 0; v < counts[c]; ++v) {
                 int64_t pos = off + v;
+                if (deleted && deleted[pos]) continue;   /* exact_update.cu:89 */
                 int32_t dist = l2_u8(qq, base_u8 + (size_t)pos * d, d);
                 uint32_t id = r2o ? (uint32_t)r2o[pos] : (uint32_t)pos;
                 kheap_push(&h, ikey(dist, id));
@@ -324,7 +326,9 @@ static void pq_stage1(const pq_segment* s, const float* q, const float* cent, in
  *           (ADC, delta position) when a delta segment is given;
  *  stage 2: unique candidates reranked exactly -- int32 L2 on u8 vectors
  *           (query = make_query_u8(q)) or fp32 L2 (l2_f32_rerank) -- and the top-k
- *           kept by (exact distance, final id).
+ *           kept by (exact distance, final id); main positions with
+ *           deleted[pos] != 0 (deleted may be NULL) keep their stage-1 slots
+ *           but are not reranked.
  *
  * Final ids: main -> r2o[position] (or position), delta -> delta ids[position].
  * Outputs: out_ids/out_dist [nq, k] (empty slots -1 / +inf); optionally the
@@ -337,7 +341,7 @@ ORACLE_API int oracle_pq_search(
     const uint8_t* base_u8, const float* base_f32, int use_f32_rerank,
     const uint8_t* dcodes, const int64_t* doffsets, const int32_t* dcounts, const int32_t* dids,
     const uint8_t* draw_u8, const float* draw_f32, int delta_topk,
-    const float* q, int nq, const int32_t* probes, int nprobe, int rerank_n, int k,
+    const float* q, int nq, const int32_t* probes, int nprobe, int rerank_n, int k, const uint8_t* deleted,
     int32_t* out_ids, float* out_dist, uint64_t* out_stage1, uint64_t* out_delta1) {
     if (M <= 0 || K <= 0 || K > 256 || dsub <= 0 || M * dsub != d || k <= 0) return -1;
     if (rerank_n < k) rerank_n = k;
@@ -380,6 +384,9 @@ ORACLE_API int oracle_pq_search(
                 uint32_t pos = (uint32_t)S->k[j];
                 /* sorted keys: a repeated position (list probed twice) is adjacent */
                 if (j > 0 && (uint32_t)S->k[j - 1] == pos) continue;
+                /* deleted main positions stay in stage 1 but are not reranked
+                 * (pq_update.cu:503-523) */
+                if (seg == 0 && deleted && deleted[pos]) continue;
                 uint32_t id = s->ids ? (uint32_t)s->ids[pos] : pos;
                 float e;
                 if (use_f32_rerank) {

@@ -44,7 +44,7 @@ def lib():
         L.oracle_route_l2.argtypes = [f32p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, i32p, f32p]
         L.oracle_route_l2.restype = C.c_int
         L.oracle_exact_u8.argtypes = [u8p, i64p, i32p, C.c_void_p, C.c_int, C.c_int,
-                                      u8p, i32p, C.c_int, C.c_int, C.c_int, i32p, i32p]
+                                      u8p, i32p, C.c_int, C.c_int, C.c_int, C.c_void_p, i32p, i32p]
         L.oracle_exact_u8.restype = C.c_int
         L.oracle_pq_lut.argtypes = [f32p, f32p, f32p, C.c_int, C.c_int, C.c_int, f32p]
         L.oracle_pq_adc.argtypes = [f32p, u8p, C.c_int, C.c_int]
@@ -56,7 +56,7 @@ def lib():
             u8p, i64p, i32p, vp,
             vp, vp, C.c_int,
             vp, vp, vp, vp, vp, vp, C.c_int,
-            f32p, C.c_int, i32p, C.c_int, C.c_int, C.c_int,
+            f32p, C.c_int, i32p, C.c_int, C.c_int, C.c_int, vp,
             i32p, f32p, vp, vp]
         L.oracle_pq_search.restype = C.c_int
         L.oracle_reorder.argtypes = [i32p, C.c_int64, C.c_int, i32p, i64p, i32p]
@@ -102,8 +102,10 @@ def route_l2(q, cent, nprobe):
     return ids, dist
 
 
-def exact_u8(base_u8, offsets, counts, r2o, q_u8, probes, k):
+def exact_u8(base_u8, offsets, counts, r2o, q_u8, probes, k, deleted=None):
+    """Exact uint8 search; ``deleted`` [n] (per cluster-major position, nonzero = deleted) or None."""
     base_u8 = _c(base_u8, np.uint8)
+    deleted = _c(deleted, np.uint8)
     offsets = _c(offsets, np.int64)
     counts = _c(counts, np.int32)
     r2o = _c(r2o, np.int32)
@@ -113,7 +115,7 @@ def exact_u8(base_u8, offsets, counts, r2o, q_u8, probes, k):
     ids = np.empty((nq, k), np.int32)
     dist = np.empty((nq, k), np.int32)
     rc = lib().oracle_exact_u8(base_u8, offsets, counts, _ptr(r2o), counts.shape[0], base_u8.shape[1],
-                               q_u8, probes, nq, nprobe, k, ids, dist)
+                               q_u8, probes, nq, nprobe, k, _ptr(deleted), ids, dist)
     assert rc == 0, rc
     return ids, dist
 
@@ -129,8 +131,10 @@ def pq_lut(q, centroid, codebook):
 
 
 def pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_n=512,
-              base_u8=None, base_f32=None, delta=None, delta_topk=16, return_stage1=False):
-    """Residual-PQ search; ``delta`` is a dict with codes/offsets/counts/ids/raw_u8|raw_f32."""
+              base_u8=None, base_f32=None, delta=None, delta_topk=16, return_stage1=False, deleted=None):
+    """Residual-PQ search; ``delta`` is a dict with codes/offsets/counts/ids/raw_u8|raw_f32;
+    ``deleted`` [n] (per main position, nonzero = not reranked) or None."""
+    deleted = _c(deleted, np.uint8)
     cent = _c(cent, np.float32)
     codebook = _c(codebook, np.float32)
     codes = _c(codes, np.uint8)
@@ -161,7 +165,7 @@ def pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_
     sd = np.empty((nq, max(dt, 1)), np.uint64) if (return_stage1 and dt) else None
     rc = lib().oracle_pq_search(cent, cent.shape[0], d, codebook, M, K, dsub, codes, offsets, counts,
                                 _ptr(r2o), _ptr(base_u8), _ptr(base_f32), use_f32,
-                                *dargs, dt, q, nq, probes, nprobe, rerank_n, k, ids, dist,
+                                *dargs, dt, q, nq, probes, nprobe, rerank_n, k, _ptr(deleted), ids, dist,
                                 _ptr(s1), _ptr(sd))
     del keep
     assert rc == 0, rc

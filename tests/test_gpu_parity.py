@@ -126,6 +126,55 @@ def test_exact_grouped_many_queries(cuda_ok, d, k):
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
 
 
+@pytest.mark.parametrize("d", [64, 128])
+def test_exact_deletes(cuda_ok, d):
+    """deleted positions are not scanned (d = 64: per-pair kernel, d = 128: grouped)."""
+    n, nlist, nq, nprobe, k = 6000, 20, 300, 5, 10
+    base = synth.mixture_u8(n, d, 20, 12.0, seed=71)
+    e = synth.build_u8_index(base, nlist, seed=71, iters=4)
+    q = synth.mixture_u8(nq, d, 20, 12.0, seed=71, stream_base=1 << 20).numpy()
+    probes, _ = oracle.route_l2(q.astype(np.float32), e["centroids"], nprobe)
+    dele = synth.delete_mask(e["r2o"], 0.3)
+    index = ib.Index().load_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], e["centroids"])
+    index.set_deleted(dele)
+    b = ib.Batch(nq, d, nprobe, k, nlist)
+    b.stage1_prepare(q.astype(np.float32))
+    b.set_probes(probes)
+    b.u8_search(index, nq, nprobe, k, route=False)
+    gi, gd = b.get_results_i32(nq, k)
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], q, probes, k, deleted=dele)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    index.set_deleted(None)                  # cleared: the plain search again
+    b.u8_search(index, nq, nprobe, k, route=False)
+    gi, gd = b.get_results_i32(nq, k)
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], q, probes, k)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    b.close()
+    index.close()
+
+
+@pytest.mark.parametrize("f32", [False, True])
+def test_pq_deletes(cuda_ok, pq_medium, f32):
+    """deleted positions keep their stage-1 slots and are not reranked."""
+    p, q = pq_medium
+    nq, nprobe, k, R = q.shape[0], 8, 10, 64
+    probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    dele = synth.delete_mask(p["r2o"], 0.3)
+    rr = {"base_f32": p["base_u8"].astype(np.float32)} if f32 else {"base_u8": p["base_u8"]}
+    index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], **rr)
+    index.set_deleted(dele)
+    b = ib.Batch(nq, q.shape[1], nprobe, k, len(p["counts"]))
+    b.stage1_prepare(q)
+    b.set_probes(probes)
+    b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=False, route=False)
+    gi, gd = b.get_results(nq, k)
+    oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
+                              probes, k, rerank_n=R, deleted=dele, **rr)
+    assert np.array_equal(gi, oi) and np.array_equal(gd, od)
+    b.close()
+    index.close()
+
+
 @pytest.mark.parametrize("name", ["pq_u8_small", "pq_f32_small"])
 def test_pq_golden(cuda_ok, name):
     g = load(name + ".npz")

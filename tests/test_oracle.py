@@ -180,3 +180,64 @@ def test_fp32_rerank_matches_reference_on_fresh_data(d, M):
     r_local, r_dist, _, _ = oracle.ref_pq_resid(cent, codebook, codes, offsets, counts, q, probes, k,
                                                 rerank_n=R, base_f32=base_cm)
     _compare_to_reference(ids, dist, r2o[r_local], r_dist)
+
+
+def test_delete_mask_matches_reference_formula():
+    """synth.delete_mask against an exact restatement of is_deleted_id
+    (updates/exact_update.cu:354-371): splitmix64(id) < ratio * (2^64 - 1)."""
+    from fractions import Fraction
+
+    def sm(x):
+        x = (x + 0x9E3779B97F4A7C15) & ((1 << 64) - 1)
+        x = ((x ^ (x >> 30)) * 0xBF58476D1CE4E5B9) & ((1 << 64) - 1)
+        x = ((x ^ (x >> 27)) * 0x94D049BB133111EB) & ((1 << 64) - 1)
+        return x ^ (x >> 31)
+
+    ids = np.concatenate([np.arange(3000), np.array([-1, 2**31 - 1])]).astype(np.int64)
+    for ratio in (0.0, 0.1, 0.5, 0.9999, 1.0):
+        m = synth.delete_mask(ids, ratio)
+        for i, v in zip(ids.tolist(), m.tolist()):
+            if ratio <= 0 or i < 0:
+                exp = 0
+            elif ratio >= 1:
+                exp = 1
+            else:
+                exp = int(Fraction(sm(i)) < Fraction(ratio) * ((1 << 64) - 1))
+            assert v == exp, (ratio, i)
+    prot = np.array([0, 1, 2, 5])
+    m = synth.delete_mask(ids, 1.0, protected_ids=prot)
+    assert m[prot].sum() == 0 and m[10] == 1
+
+
+def test_oracle_deletes():
+    """exact: deleted rows are never scanned (== the index without them); PQ: they
+    keep stage-1 slots and are not reranked (a NumPy rerank of the stage-1 keys)."""
+    n, d, nlist, M, nq, nprobe, k, R = 3000, 32, 12, 8, 30, 4, 10, 40
+    base = synth.mixture_u8(n, d, 12, 10.0, seed=21)
+    e = synth.build_u8_index(base, nlist, seed=21, iters=4)
+    q = synth.mixture_u8(nq, d, 12, 10.0, seed=21, stream_base=1 << 20).numpy()
+    probes, _ = oracle.route_l2(q.astype(np.float32), e["centroids"], nprobe)
+    dele = synth.delete_mask(e["r2o"], 0.3)
+    gi, gd = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], q, probes, k, deleted=dele)
+    keep = dele == 0
+    cnt = np.array([keep[e["offsets"][l]:e["offsets"][l] + e["counts"][l]].sum() for l in range(nlist)], np.int32)
+    off = np.zeros(nlist, np.int64)
+    off[1:] = np.cumsum(cnt)[:-1]
+    ri, rd = oracle.exact_u8(e["base_cm"][keep], off, cnt, e["r2o"][keep], q, probes, k)
+    assert np.array_equal(gi, ri) and np.array_equal(gd, rd)
+
+    p = synth.build_pq_index(base, nlist, M, seed=21, kmeans_iters=4, pq_iters=3, train_n=2000)
+    qf = q.astype(np.float32)
+    pr, _ = oracle.route_l2(qf, p["centroids"], nprobe)
+    dp = synth.delete_mask(p["r2o"], 0.3)
+    args = (p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], qf, pr, k)
+    oi, od = oracle.pq_search(*args, rerank_n=R, base_u8=p["base_rr"], deleted=dp)
+    _, _, s1, _ = oracle.pq_search(*args, rerank_n=R, base_u8=p["base_rr"], return_stage1=True)
+    qu = oracle.make_query_u8(qf).astype(np.int64)
+    for i in range(nq):
+        pos = np.unique(s1[i][s1[i] != np.uint64(0xFFFFFFFFFFFFFFFF)] & np.uint64(0xFFFFFFFF)).astype(np.int64)
+        pos = pos[dp[pos] == 0]
+        dd = ((qu[i][None, :] - p["base_rr"][pos].astype(np.int64)) ** 2).sum(1)
+        ids = p["r2o"][pos]
+        o = np.lexsort((ids, dd))[:k]
+        assert np.array_equal(oi[i][:len(o)], ids[o]) and np.array_equal(od[i][:len(o)], dd[o].astype(np.float32))
