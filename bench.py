@@ -1,20 +1,27 @@
 #!/usr/bin/env python3
-"""Benchmark of the IVF residual-PQ query hot path (BASELINE.json configs[1] by default).
+"""Benchmark of the IVF residual-PQ query hot path (BASELINE.json configs[2] by default).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c0|c1|c2|...]
     python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...
 
-Workload c1: 10M x 96 fp32 unit-normalised vectors from a seeded 4096-component
-Gaussian mixture (sigma 0.05), nlist 4096, residual PQ M=48 x 8 bit trained on
-a 500k sample, 10k queries from the same mixture, k=10, rerank_n=512 with fp32
-rerank.  A step is one pass of the hot path over the 10k-query batch: routing,
-probe inversion, ADC scan, top-R selection, exact rerank, top-k.
+Workload c2 (the largest single-GPU config of BASELINE.json): 100M x 128 uint8
+vectors from a seeded 65536-component Gaussian mixture (centers U[32,224],
+sigma 10), nlist 65536, residual PQ M=32 x 8 bit trained on a 500k sample, 10k
+queries from the same mixture, k=10, rerank_n=512 with uint8 rerank.  A step
+is one pass of the hot path over the 10k-query batch: routing, probe
+inversion, ADC scan, top-R selection, exact rerank, top-k.
 
-N>1: inverted lists are sharded over the ranks (LPT by bytes); every rank
-routes over its own centroids, the local routing keys are all-gathered and
-merged, each rank scans its own lists and scores its candidates exactly, the
-per-shard candidate lists go to the owners of the queries with one all-to-all,
-the owners merge on the device and the top-k are all-gathered to rank 0.
+Index build (not timed): every rank generates the seeded rows itself
+(counter-based generators), rank 0 runs k-means and trains the codebook, the
+assignment is split over the ranks, and each rank keeps and encodes only the
+lists it owns (LPT by bytes), so nothing of the index is broadcast.
+
+N>1: inverted lists are sharded over the ranks; every rank routes over its own
+centroids, the local routing keys are all-gathered and merged, each rank scans
+its own lists (nearest probe first, then the others under the exchanged
+bounds), the stage-1 lists go to the owners of the queries, the owners find
+the rank-R key limit, each shard reranks its keys below it and the owners
+merge the shards' exact top-k (the phased protocol in include/insitu_b200.h).
 Total work is fixed, so "scaling" is "strong".
 
 --impl reference times the reference's own CPU kernel
@@ -140,30 +147,102 @@ class Clocks:
 # ----------------------------------------------------------------------------
 # workload
 # ----------------------------------------------------------------------------
-def build_workload(cfg, device):
-    """Seeded data, index and exact ground truth (all outside any timed region)."""
+def pq_build(cfg, dev, rank=0, world=1, dist=None):
+    """Seeded data, this rank's lists of the residual-PQ index, and the exact
+    ground truth over all ranks' rows (all outside any timed region)."""
     import torch
 
     import synth
 
     t0 = time.time()
-    if cfg["kind"] == "pq_u8":
-        base = synth.mixture_u8(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
-        q = synth.mixture_u8(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
-                             stream_base=1 << 30).float()
-    else:
-        base = synth.mixture_f32_unit(cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device)
-        q = synth.mixture_f32_unit(cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], device=device,
-                                   stream_base=1 << 30)
-    log(f"[bench] data {time.time() - t0:.1f}s")
-    idx = synth.build_pq_index(base, cfg["nlist"], cfg["M"], cfg["seed"], kmeans_iters=20, pq_iters=12,
-                               train_n=cfg["train_n"], kmeans_sample=64 * cfg["nlist"])
-    log(f"[bench] index {time.time() - t0:.1f}s")
-    gt = synth.brute_force_gt(base, q, cfg["k"], batch_rows=1 << 16)
-    log(f"[bench] ground truth {time.time() - t0:.1f}s")
-    del base
+    kind = "u8" if cfg["kind"] == "pq_u8" else "f32"
+    src = synth.RowSource(kind, cfg["n"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], dev,
+                          zipf=cfg.get("zipf"))
+    qsrc = synth.RowSource(kind, cfg["nq"], cfg["d"], cfg["ncomp"], cfg["sigma"], cfg["seed"], dev,
+                           zipf=cfg.get("zipf"), stream_base=1 << 30)
+    q = qsrc.rows(0, cfg["nq"]).float()
+
+    def say(what):
+        if rank == 0:
+            log(f"[bench] {what} {time.time() - t0:.1f}s")
+    b = synth.build_pq_shard(src, cfg["nlist"], cfg["M"], cfg["seed"], rank, world, dist, kmeans_iters=20,
+                             pq_iters=12, train_n=cfg["train_n"], kmeans_sample=64 * cfg["nlist"], log=say)
+    keys = synth.gt_keys(b["base_rr"], q, cfg["k"], ids=b["r2o"])
+    if world > 1:
+        allk = torch.empty(world * keys.numel(), dtype=keys.dtype, device=dev)
+        dist.all_gather_into_tensor(allk, keys.reshape(-1))
+        keys = allk.reshape((world,) + tuple(keys.shape))
+    b["gt"] = synth.merge_gt_keys(keys, cfg["k"])
+    say("ground truth")
+    b["q"] = q
+    b["q_np"] = q.cpu().numpy()
     torch.cuda.empty_cache()
-    return idx, q.cpu().numpy(), gt
+    return b
+
+
+def host_index(b):
+    """Host copy of a whole index (one rank owns every list) for the CPU oracle and baselines."""
+    return dict(centroids=b["centroids"].cpu().numpy(), codebook=b["codebook"].cpu().numpy(),
+                codes=b["codes"].cpu().numpy(), offsets=b["offsets_global"], counts=b["counts_global"],
+                r2o=b["r2o"].cpu().numpy(), base_rr=b["base_rr"].cpu().numpy())
+
+
+def gather_lists(b, needed, rank, world, dist, dev):
+    """Rank 0 receives the codes, rerank rows and ids of the lists `needed`
+    (sorted global ids) from the ranks that own them and returns a host index
+    that holds those lists alone, in increasing global order (so cluster-major
+    positions keep their relative order and ties break as in the whole index);
+    the other lists are empty.  Other ranks return None."""
+    import torch
+
+    my = b["my_lists"]
+    pos = np.searchsorted(my, needed)
+    own = (pos < len(my)) & (my[np.minimum(pos, max(len(my) - 1, 0))] == needed) if len(my) else \
+        np.zeros(len(needed), bool)
+    loc = pos[own]
+    rows = (np.concatenate([np.arange(b["offsets"][l], b["offsets"][l] + b["counts"][l], dtype=np.int64)
+                            for l in loc]) if len(loc) else np.zeros(0, np.int64))
+    it = torch.from_numpy(rows).to(dev)
+    part = [torch.from_numpy(needed[own].astype(np.int32)).to(dev), b["codes"][it].contiguous(),
+            b["base_rr"][it].contiguous(), b["r2o"][it].contiguous()]
+    sz = torch.tensor([int(own.sum()), len(rows)], dtype=torch.int64, device=dev)
+    allsz = torch.empty(world * 2, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(allsz, sz)
+    allsz = allsz.reshape(world, 2).cpu().numpy()
+    parts = [part] if rank == 0 else None
+    for r in range(1, world):
+        nl, nr = int(allsz[r, 0]), int(allsz[r, 1])
+        if nl == 0:
+            continue
+        if rank == r:
+            for t in part:
+                dist.send(t, dst=0)
+        elif rank == 0:
+            recv = [torch.empty(nl, dtype=torch.int32, device=dev),
+                    torch.empty((nr,) + tuple(part[1].shape[1:]), dtype=part[1].dtype, device=dev),
+                    torch.empty((nr,) + tuple(part[2].shape[1:]), dtype=part[2].dtype, device=dev),
+                    torch.empty(nr, dtype=torch.int32, device=dev)]
+            for t in recv:
+                dist.recv(t, src=r)
+            parts.append(recv)
+    if rank != 0:
+        return None
+    lists = np.concatenate([p[0].cpu().numpy() for p in parts])
+    codes = torch.cat([p[1] for p in parts]).cpu().numpy()
+    rr = torch.cat([p[2] for p in parts]).cpu().numpy()
+    r2o = torch.cat([p[3] for p in parts]).cpu().numpy()
+    cnt_g = b["counts_global"]
+    src_off = np.zeros(len(lists), np.int64)
+    src_off[1:] = np.cumsum(cnt_g[lists], dtype=np.int64)[:-1]
+    order = np.argsort(lists, kind="stable")
+    idx = (np.concatenate([np.arange(src_off[i], src_off[i] + cnt_g[lists[i]], dtype=np.int64) for i in order])
+           if len(order) else np.zeros(0, np.int64))
+    counts = np.zeros(len(cnt_g), np.int32)
+    counts[lists] = cnt_g[lists]
+    offsets = np.zeros(len(cnt_g), np.int64)
+    offsets[1:] = np.cumsum(counts, dtype=np.int64)[:-1]
+    return dict(centroids=b["centroids"].cpu().numpy(), codebook=b["codebook"].cpu().numpy(), codes=codes[idx],
+                offsets=offsets, counts=counts, r2o=r2o[idx], base_rr=rr[idx])
 
 
 def rr_kw(rows):
@@ -401,9 +480,13 @@ def run_reference_arm(args, cfg):
             "e2e": {"value": qps, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }), flush=True)
         return
-    idx, q, gt = build_workload(cfg, dev)
+    b = pq_build(cfg, dev)
+    idx, q, gt = host_index(b), b["q_np"], b["gt"]
+    del b
+    if torch.cuda.is_available():
+        torch.cuda.empty_cache()
     nprobe = args.nprobe or cfg["nprobe"]
-    probes, _ = oracle.route_l2(q, idx["centroids"], nprobe)
+    probes, _ = oracle.route_l2_par(q, idx["centroids"], nprobe)
     times, samples = [], []
     for step in range(args.warmup + args.steps):
         r = time_reference(idx, q, probes, cfg, target_s=4.0, max_queries=cfg["nq"])
@@ -439,12 +522,15 @@ def main():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="c1", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--parity-queries", type=int, default=1000,
+                    help="queries of the batch checked against the CPU oracle (ids, distances and probes)")
     ap.add_argument("--nprobe", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--overlay", type=int, default=0,
-                    help="also time the search with a published delta segment of this many vectors (1 GPU)")
+    ap.add_argument("--overlay", default="",
+                    help="also time the search with published delta segments of these sizes, e.g. "
+                         "1000000,5000000,10000000 (BASELINE configs[4]; 1 GPU)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     args.warmup = max(args.warmup, 3)
@@ -478,46 +564,31 @@ def main():
     nlist = cfg["nlist"]
     nprobe = args.nprobe or cfg["nprobe"]
 
-    # ---- workload (rank 0 builds, broadcast to the others) ----
-    if rank == 0:
-        idx, q_np, gt = build_workload(cfg, dev)
-    else:
-        idx, q_np, gt = None, None, None
-    if N > 1:
-        shapes = [None]
-        if rank == 0:
-            shapes = [{k_: (v.shape, str(v.dtype)) for k_, v in idx.items()} | {"q": (q_np.shape, "float32")}]
-        dist.broadcast_object_list(shapes, src=0)
-        shapes = shapes[0]
-        tensors = {}
-        for name, (shape, dt) in shapes.items():
-            src = (idx[name] if name != "q" else q_np) if rank == 0 else None
-            t = torch.from_numpy(np.ascontiguousarray(src)).to(dev) if rank == 0 else \
-                torch.empty(shape, dtype=getattr(torch, dt), device=dev)
-            dist.broadcast(t, src=0)
-            tensors[name] = t
-        torch.cuda.synchronize()
-        if rank != 0:
-            idx = {n_: t.cpu().numpy() for n_, t in tensors.items() if n_ != "q"}
-            q_np = tensors["q"].cpu().numpy()
-        del tensors
+    # ---- workload: every rank builds its own lists (nothing of the index is broadcast) ----
+    W = pq_build(cfg, dev, rank, N, dist if N > 1 else None)
+    my_lists, gt, q_np = W["my_lists"], W["gt"], W["q_np"]
+    counts, offsets = W["counts_global"], W["offsets_global"]
+    q_dev = W["q"].contiguous()
+    rr_u8 = W["base_rr"].dtype == torch.uint8
+    rr_bytes = W["base_rr"].element_size()
 
-    counts, offsets = idx["counts"], idx["offsets"]
-    q_dev = torch.from_numpy(q_np).to(dev)
-
-    # ---- load this rank's lists ----
+    # ---- load this rank's lists (device tensors are copied device to device) ----
+    R, k = cfg["rerank_n"], cfg["k"]
     index = ib.Index()
-    if N == 1:
-        index.load_pq(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
-                      **rr_kw(idx["base_rr"]))
-        my_lists = np.arange(nlist)
-    else:
-        owner = shard.lpt_shards(counts, M + idx["base_rr"].itemsize * d, N)
-        my_lists = np.where(owner == rank)[0].astype(np.int32)
-        rows, off, cnt = shard.shard_rows(offsets, counts, my_lists)
-        index.load_pq(idx["centroids"][my_lists], idx["codebook"], idx["codes"][rows], off, cnt, idx["r2o"][rows],
-                      **rr_kw(idx["base_rr"][rows]))
+    cent_np = W["centroids"].cpu().numpy()
+    cb_np = W["codebook"].cpu().numpy()
+    rr_arg = {"base_u8": W["base_rr"]} if rr_u8 else {"base_f32": W["base_rr"]}
+    index.load_pq(cent_np[my_lists], cb_np, W["codes"], W["offsets"], W["counts"], W["r2o"], **rr_arg)
+    if N > 1:
         index.set_shard(nlist, my_lists, offsets[my_lists])
+    # the oracle's view: the whole index on rank 0 when one GPU holds it
+    idx = host_index(W) if (N == 1 and rank == 0) else None
+    codes_mb = W["codes"].numel() / 1e6 * N
+    rr_gb = W["base_rr"].numel() * rr_bytes / 1e9 * N
+    del rr_arg
+    if N == 1:
+        del W["codes"], W["base_rr"]      # sharded runs keep them until the oracle check gathered its lists
+    torch.cuda.empty_cache()
     batch = ib.Batch(nq, d, max(nprobe, max(cfg["sweep"])), k, nlist)
     ext = torch.cuda.ExternalStream(batch.stream, device=dev)
 
@@ -629,24 +700,50 @@ def main():
             if rank == 0:
                 log(f"[bench] nprobe {np_}: recall@10 {rec} qps {nq / dt:.0f}")
 
-    # ---- parity spot check against the CPU oracle (first 64 queries, untimed) ----
+    # ---- parity against the CPU oracle on the first P queries of the batch (untimed):
+    # probe lists, result ids and distances, and (one GPU) the stage-1 keys ----
     step()
     ids_g, dist_g = results()
+    probes_g = batch.get_probes(nq, nprobe)
     barrier()
-    parity = None
+    P = min(args.parity_queries, nq)
+    s1_g = None
+    if N == 1:
+        adc_d = torch.empty((P, R), dtype=torch.int64, device=dev)
+        exa_d = torch.empty((P, R), dtype=torch.int64, device=dev)
+        batch.pq_search_shard(index, P, nprobe, R, 0, adc_d.data_ptr(), exa_d.data_ptr())
+        batch.sync()
+        s1_g = adc_d.cpu().numpy().view(np.uint64)
+        del adc_d, exa_d
+    needed = [None]
+    probes_o = None
+    t_par = time.time()
     if rank == 0:
-        probes_g = None
-        if N == 1:
-            probes_g = batch.get_probes(nq, nprobe)
-        sub = 64
-        probes_o, _ = oracle.route_l2(q_np[:sub], idx["centroids"], nprobe)
-        oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
-                                  q_np[:sub], probes_o, k, rerank_n=R, **rr_kw(idx["base_rr"]))
-        parity = bool(np.array_equal(oi, ids_g[:sub]) and np.array_equal(od, dist_g[:sub]))
-        if probes_g is not None:
-            parity = parity and bool(np.array_equal(probes_g[:sub], probes_o))
-        recall = synth.recall_at_k(ids_g, gt, k)
-        log(f"[bench] parity(64 queries vs oracle)={parity} recall@10={recall:.4f}")
+        probes_o, _ = oracle.route_l2_par(q_np[:P], cent_np, nprobe)
+        needed = [np.unique(probes_o[probes_o >= 0]).astype(np.int64)]
+    if N > 1:
+        dist.broadcast_object_list(needed, src=0)
+    oidx = idx if N == 1 else gather_lists(W, needed[0], rank, N, dist, dev)
+    parity, parity_detail = None, None
+    if rank == 0:
+        oi, od, s1_o, _ = oracle.pq_search_par(oidx["centroids"], oidx["codebook"], oidx["codes"], oidx["offsets"],
+                                               oidx["counts"], oidx["r2o"], q_np[:P], probes_o, k, rerank_n=R,
+                                               return_stage1=True, **rr_kw(oidx["base_rr"]))
+        ok_p = bool(np.array_equal(probes_g[:P], probes_o))
+        ok_i = bool(np.array_equal(oi, ids_g[:P]))
+        ok_d = bool(np.array_equal(od, dist_g[:P]))
+        ok_s = None if s1_g is None else bool(np.array_equal(np.sort(s1_g, axis=1), np.sort(s1_o, axis=1)))
+        bad = ~((oi == ids_g[:P]).all(1) & (od == dist_g[:P]).all(1))
+        parity = ok_p and ok_i and ok_d and (ok_s is not False)
+        parity_detail = {"queries": P, "probes_equal": ok_p, "ids_equal": ok_i, "distances_equal": ok_d,
+                         "stage1_keys_equal": ok_s, "queries_differing": int(bad.sum())}
+        log(f"[bench] parity({P} queries vs oracle)={parity} {parity_detail} "
+            f"recall@10={synth.recall_at_k(ids_g, gt, k):.4f} ({time.time() - t_par:.1f}s)")
+    del oidx
+    if N > 1:
+        del W["codes"], W["base_rr"]
+        torch.cuda.empty_cache()
+    barrier()
 
     # ---- timed region ----
     for _ in range(args.warmup):
@@ -738,45 +835,52 @@ def main():
     # seeded uniform codes (the reference's generators), ids after the base, scanned in
     # the same launches as the main lists; QPS with and without it ----
     overlay = None
-    if args.overlay > 0 and N == 1:
-        t_g = time.time()
-        dseg = synth.delta_segment(args.overlay, nlist, M, base_id=cfg["n"], d=d, seed=cfg["seed"] + 1,
-                                   f32=idx["base_rr"].dtype != np.uint8)
-        raw = {"raw_f32": dseg["raw_f32"]} if "raw_f32" in dseg else {"raw_u8": dseg["raw_u8"]}
-        index.publish_delta(dseg["codes"], dseg["ids"], dseg["counts"], dseg["offsets"], **raw)
-        log(f"[bench] delta segment of {args.overlay} vectors published in {time.time() - t_g:.1f}s")
-
+    sizes = [int(x) for x in str(args.overlay).split(",") if x and int(x) > 0]
+    if sizes and N == 1:
         def ostep(np_, ov):
             batch.stage1_prepare_device(q_dev.data_ptr(), nq)
             batch.pq_search(index, nq, np_, k, rerank_n=R, overlay=ov, delta_topk=16, route=True)
 
-        ostep(nprobe, True)
-        batch.sync()
-        oid, odd = batch.get_results(nq, k)
-        po, _ = oracle.route_l2(q_np[:64], idx["centroids"], nprobe)
-        ei, ed = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts, idx["r2o"],
-                                  q_np[:64], po, k, rerank_n=R, delta=dseg, delta_topk=16, **rr_kw(idx["base_rr"]))
-        o_par = bool(np.array_equal(ei, oid[:64]) and np.array_equal(ed, odd[:64]))
-        rows = []
-        for np_ in sorted({nprobe, 64}):
-            res = {}
-            for ov in (False, True):
-                for _ in range(args.warmup):
-                    ostep(np_, ov)
-                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                torch.cuda.synchronize()
-                e0.record(ext)
-                for _ in range(args.steps):
-                    ostep(np_, ov)
-                e1.record(ext)
-                torch.cuda.synchronize()
-                res[ov] = nq / (e0.elapsed_time(e1) / args.steps / 1000.0)
-            rows.append({"nprobe": np_, "qps_without": res[False], "qps_with": res[True],
-                         "overhead": 1.0 - res[True] / res[False]})
-        overlay = {"delta_vectors": args.overlay, "delta_topk": 16, "parity_vs_oracle_64q": o_par, "runs": rows}
-        log(f"[bench] overlay parity={o_par} " + ", ".join(
-            f"nprobe {r_['nprobe']}: {r_['qps_without']:.0f} -> {r_['qps_with']:.0f} qps" for r_ in rows))
-        index.clear_delta()
+        def timed(np_, ov):
+            for _ in range(args.warmup):
+                ostep(np_, ov)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.synchronize()
+            e0.record(ext)
+            for _ in range(args.steps):
+                ostep(np_, ov)
+            e1.record(ext)
+            torch.cuda.synchronize()
+            return nq / (e0.elapsed_time(e1) / args.steps / 1000.0)
+
+        onp = sorted({nprobe, 64})
+        base_qps = {np_: timed(np_, False) for np_ in onp}
+        runs = []
+        for nd in sizes:
+            t_g = time.time()
+            dseg = synth.delta_segment(nd, nlist, M, base_id=cfg["n"], d=d, seed=cfg["seed"] + 1,
+                                       f32=idx["base_rr"].dtype != np.uint8)
+            raw = {"raw_f32": dseg["raw_f32"]} if "raw_f32" in dseg else {"raw_u8": dseg["raw_u8"]}
+            index.publish_delta(dseg["codes"], dseg["ids"], dseg["counts"], dseg["offsets"], **raw)
+            log(f"[bench] delta segment of {nd} vectors published in {time.time() - t_g:.1f}s")
+            ostep(64, True)
+            batch.sync()
+            oid, odd = batch.get_results(nq, k)
+            Po = min(P, nq)
+            po, _ = oracle.route_l2_par(q_np[:Po], idx["centroids"], 64)
+            ei, ed = oracle.pq_search_par(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts,
+                                          idx["r2o"], q_np[:Po], po, k, rerank_n=R, delta=dseg, delta_topk=16,
+                                          **rr_kw(idx["base_rr"]))
+            o_par = bool(np.array_equal(ei, oid[:Po]) and np.array_equal(ed, odd[:Po]))
+            for np_ in onp:
+                qw = timed(np_, True)
+                runs.append({"delta_vectors": nd, "nprobe": np_, "qps_without": base_qps[np_], "qps_with": qw,
+                             "overhead": 1.0 - qw / base_qps[np_], "parity_vs_oracle": o_par,
+                             "parity_queries": Po})
+                log(f"[bench] overlay {nd}: nprobe {np_}: {base_qps[np_]:.0f} -> {qw:.0f} qps, parity {o_par}")
+            index.clear_delta()
+            del dseg, raw
+        overlay = {"delta_topk": 16, "runs": runs}
 
     # ---- roofline of the ADC scan kernel (this rank) ----
     if probes_all is None:
@@ -803,7 +907,7 @@ def main():
 
     cpu = None
     if rank == 0 and N == 1 and not args.no_cpu_baseline:
-        probes_o, _ = oracle.route_l2(q_np[:4096], idx["centroids"], nprobe)
+        probes_o, _ = oracle.route_l2_par(q_np[:4096], idx["centroids"], nprobe)
         r = time_reference(idx, q_np[:4096], probes_o, cfg, target_s=12.0, max_queries=4096)
         if r is not None:
             cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
@@ -820,10 +924,10 @@ def main():
             "config": {"workload": cfg["desc"], "n_base": cfg["n"], "d": d, "nlist": nlist, "M": M,
                        "nq": nq, "nprobe": nprobe, "k": k, "rerank_n": R,
                        "recall@10": synth.recall_at_k(ids_g, gt, k), "recall_target_met": bool(
-                           synth.recall_at_k(ids_g, gt, k) >= 0.9), "parity_vs_oracle_64q": parity,
+                           synth.recall_at_k(ids_g, gt, k) >= 0.9), "parity_vs_oracle": parity,
+                       "parity_detail": parity_detail,
                        "inputs_exceed_l2": True,
-                       "l2_note": f"{idx['codes'].nbytes / 1e6:.0f} MB of codes and "
-                                  f"{idx['base_rr'].nbytes / 1e9:.2f} GB of rerank rows per step",
+                       "l2_note": f"{codes_mb:.0f} MB of codes and {rr_gb:.2f} GB of rerank rows per step",
                        "parallelism": "single GPU" if N == 1 else f"lists sharded x{N} (LPT by bytes), NCCL"},
             "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
             "clocks": clocks, "stages_ms_per_step": {s: v / args.steps for s, v in stage.items()},

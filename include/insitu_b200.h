@@ -6,9 +6,14 @@
  *
  * Plain C types only.  Every function may be called from any host thread;
  * one batch context is one CUDA stream and must not be used by two threads at
- * once.  Index contexts are immutable after loading (publishing a delta
- * segment excepted), so several batch contexts may search one index
- * concurrently.
+ * once.  Index contexts are immutable after loading except for the delete
+ * mask and the delta segment, so several batch contexts may search one index
+ * concurrently.  ivf_set_deleted, ivf_pq_publish_delta and
+ * ivf_pq_clear_delta may run while other threads search the same index: they
+ * wait until every search that has started reading the index has queued its
+ * work, synchronise the device, and only then free the replaced arrays;
+ * searches that start later see the new arrays.  An index context must not be
+ * destroyed while a search on it is in flight.
  *
  * Return conventions
  *   - names taken from the reference keep the reference's return types and
@@ -156,9 +161,12 @@ const CoarseTimingBreakdown* coarse_get_last_timing(void);
 
 /* ======================================================================
  * Index loading (new: the reference loads these inside its runners,
- * updates/pq_update.cu:676-713 and updates/exact_update.cu:2229).  All
- * arrays are host arrays in the reference file layouts and are copied to
- * the device; positions are cluster-major (stable reorder).
+ * updates/pq_update.cu:676-713 and updates/exact_update.cu:2229).  Arrays
+ * are in the reference file layouts and are copied into memory the index
+ * owns; positions are cluster-major (stable reorder).  offsets, counts,
+ * centroids and the codebook are host arrays; the bulk arrays (base rows,
+ * codes, reorder_to_original, rerank rows) may be host arrays or device
+ * arrays on the index's device (the copy direction is inferred).
  * ====================================================================== */
 
 /*
@@ -345,7 +353,9 @@ int ivf_pq_shard_final(void* batch_ctx, const unsigned long long* d_topk_all, in
  * into smaller batches.  The first call on each device looks up the array's
  * device address; make that first call before any stream capture.  Calls
  * share the array: two calls that overlap on the GPU race, so order them on
- * one stream or synchronise between them.
+ * one stream or synchronise between them.  The call returns with the
+ * caller's current device unchanged; the cached array address is valid for
+ * the life of the device's primary context (no cudaDeviceReset in between).
  */
 int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, const int* d_probes, int n_query, int n_probes,
                           int k, int* d_out_ids, int* d_out_dist, void* stream);

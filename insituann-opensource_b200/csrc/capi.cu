@@ -14,6 +14,7 @@
 #include <cstring>
 #include <atomic>
 #include <mutex>
+#include <shared_mutex>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -56,10 +57,12 @@ T* dalloc(size_t n, std::vector<void*>& owned) {
     return static_cast<T*>(p);
 }
 
+// copies n elements from host or device memory (the runtime infers which from
+// the pointer) into a new device array owned by `owned`
 template <class T>
 T* dcopy(const T* h, size_t n, std::vector<void*>& owned) {
     T* d = dalloc<T>(n, owned);
-    if (n) ck(cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyHostToDevice), "cudaMemcpy H2D");
+    if (n) ck(cudaMemcpy(d, h, n * sizeof(T), cudaMemcpyDefault), "cudaMemcpy to device");
     return d;
 }
 
@@ -115,6 +118,11 @@ struct IndexCtx {
     int32_t* g2l = nullptr;      // [nlist_global] global -> local list id or -1 (shards)
     std::vector<void*> owned;    // centroids, validity, codebook, shard maps, adopted arrays
     std::mutex mu;
+    // Searches hold rw shared from reading the device arrays until their
+    // launches are queued; calls that replace arrays (delete mask, delta
+    // segment, loads) hold it exclusively, then synchronise the device before
+    // freeing, so no queued or later kernel reads freed memory.
+    std::shared_mutex rw;
     std::string err;
 };
 
@@ -646,6 +654,12 @@ bool u8_index_view(void* idx_ctx, ListStore* ls, int* nlist, int* nlist_global, 
 }
 
 void set_global_error(const std::string& msg) { g_err = msg; }
+
+std::shared_lock<std::shared_mutex> index_read_lock(void* idx_ctx) {
+    auto* x = static_cast<IndexCtx*>(idx_ctx);
+    if (!x || x->magic != kIdxMagic) return std::shared_lock<std::shared_mutex>();
+    return std::shared_lock<std::shared_mutex>(x->rw);
+}
 }  // namespace isb
 
 // ===========================================================================
@@ -723,6 +737,7 @@ int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vector
     }
     int st = guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         if (x->kind != kKindEmpty) {
             ret = 0;
             return;
@@ -851,6 +866,7 @@ void ivf_pipeline_stage2_compute(void* batch_ctx, void* idx_ctx, int n_query, in
     }
     guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         require(distance_mode == IVF_DISTANCE_L2, "only distance_mode 0 (L2) is supported", IVF_EUNSUPPORTED);
         check_shape(b, x, n_query, n_probes, k);
         cudaSetDevice(b->device);
@@ -936,6 +952,7 @@ int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets,
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         require(x->kind == kKindEmpty, "index context already holds an index", IVF_ESTATE);
         require(nlist > 0 && n >= 0 && d > 0 && d % 16 == 0 && d <= 512, "need nlist > 0, d % 16 == 0, d <= 512");
         require(base_u8 != nullptr || n == 0, "null base");
@@ -967,6 +984,7 @@ int ivf_set_deleted(void* idx_ctx, const unsigned char* deleted, long long n) {
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         require(x->kind != kKindEmpty, "no index loaded", IVF_ESTATE);
         cudaSetDevice(x->device);
         ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");   // no search may still read the old mask
@@ -996,6 +1014,7 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         require(x->kind == kKindEmpty, "index context already holds an index", IVF_ESTATE);
         require(nlist > 0 && n >= 0 && d > 0 && d <= 512, "bad sizes");
         require(K == 256, "only K = 256 (8-bit codes) is supported");
@@ -1039,6 +1058,7 @@ int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, c
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         require(x->kind == kKindU8 || x->kind == kKindPQ, "load the shard's lists first", IVF_ESTATE);
         require(x->l2g == nullptr, "shard mapping already set", IVF_ESTATE);
         require(nlist_global >= x->nlist && local_to_global, "bad shard mapping");
@@ -1069,6 +1089,7 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         require(x->kind == kKindPQ, "publish needs a residual-PQ index", IVF_ESTATE);
         require(n_delta >= 0, "negative n_delta");
         require(ids != nullptr, "delta ids are required");
@@ -1102,6 +1123,7 @@ int ivf_pq_clear_delta(void* idx_ctx) {
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
         cudaSetDevice(x->device);
         ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
         x->delta.release();
@@ -1121,6 +1143,7 @@ int ivf_route(void* batch_ctx, void* idx_ctx, int n_query, int n_probes) {
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, 1);
         cudaSetDevice(b->device);
         do_route(b, x, n_query, n_probes, nullptr);
@@ -1175,6 +1198,7 @@ int ivf_u8_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, k);
         cudaSetDevice(b->device);
         if (route) do_route(b, x, n_query, n_probes, nullptr);
@@ -1192,6 +1216,7 @@ int ivf_pq_search(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, k);
         require(rerank_n > 0, "rerank_n must be > 0");
         require(delta_topk >= 0, "delta_topk must be >= 0");
@@ -1211,6 +1236,7 @@ int ivf_route_keys(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, un
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, 1);
         require(d_keys != nullptr, "null key output");
         cudaSetDevice(b->device);
@@ -1270,6 +1296,7 @@ int ivf_pq_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, 1);
         require(d_adc && d_exact && rerank_n > 0, "adc and exact outputs are required");
         require(!d_dadc == !d_dexact, "give both or neither delta outputs");
@@ -1318,6 +1345,7 @@ int ivf_pq_shard_scan(void* batch_ctx, void* idx_ctx, int n_query, int n_probes,
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, 1);
         require(pass == 0 || pass == 1, "pass must be 0 (nearest probe) or 1 (the other probes)");
         require_probes(b, n_query, n_probes);
@@ -1364,6 +1392,7 @@ int ivf_pq_shard_select(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, 1);
         require(d_adc != nullptr, "adc output is required");
         cudaSetDevice(b->device);
@@ -1401,6 +1430,7 @@ int ivf_pq_shard_rerank(void* batch_ctx, void* idx_ctx, int n_query, int rerank_
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         require(x->kind == kKindPQ, "index is not a residual-PQ index", IVF_ESTATE);
         require(d_adc && d_kappa && d_topk && rerank_n > 0, "bad shard-rerank arguments");
         require(n_query >= 0 && n_query <= b->max_nq && b->d == x->d, "shape exceeds the batch limits");
@@ -1446,6 +1476,7 @@ int ivf_u8_search_shard(void* batch_ctx, void* idx_ctx, int n_query, int n_probe
     }
     return guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
         check_shape(b, x, n_query, n_probes, k);
         require(d_keys != nullptr, "null key output");
         cudaSetDevice(b->device);

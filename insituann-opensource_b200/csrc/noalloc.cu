@@ -19,10 +19,15 @@
 // any stream capture.  All calls share the array and it keeps the previous
 // call's contents; every counter the search relies on is cleared by the call
 // itself.  Two calls whose work overlaps on the GPU (different streams, or
-// different host threads without ordering) race on the array.
+// different host threads without ordering) race on the array.  The cached
+// address lives as long as the device's primary context: a caller that runs
+// cudaDeviceReset while the library is loaded must not call this entry point
+// again in that process.  The call leaves the caller's current device as it
+// found it.
 #include <cuda_runtime.h>
 
 #include <mutex>
+#include <shared_mutex>
 #include <string>
 
 #include "../../include/insitu_b200.h"
@@ -73,6 +78,9 @@ namespace isb {
 bool u8_index_view(void* idx_ctx, ListStore* ls, int* nlist, int* nlist_global, const int32_t** g2l, int* d,
                    int* max_count, int* device);
 void set_global_error(const std::string& msg);
+// shared hold on the index's arrays: a concurrent call that replaces them
+// (delete mask, delta segment) waits until this call has queued its work
+std::shared_lock<std::shared_mutex> index_read_lock(void* idx_ctx);
 }  // namespace isb
 
 namespace {
@@ -80,6 +88,20 @@ int fail(int code, const std::string& msg) {
     isb::set_global_error(msg);
     return code;
 }
+
+// makes `dev` current for the lifetime of the guard, then restores the
+// caller's device
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
 }  // namespace
 
 extern "C" int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, const int* d_probes, int n_query,
@@ -88,6 +110,7 @@ extern "C" int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, c
     ListStore ls{};
     int nlist = 0, nlist_global = 0, d = 0, max_count = 0, dev = 0;
     const int32_t* g2l = nullptr;
+    auto rd = index_read_lock(idx_ctx);
     if (!u8_index_view(idx_ctx, &ls, &nlist, &nlist_global, &g2l, &d, &max_count, &dev))
         return fail(IVF_ESTATE, "ivf_u8_search_noalloc: not a loaded uint8 exact index");
     if (n_query < 0 || n_probes <= 0 || k <= 0 || k > 4096)
@@ -96,8 +119,11 @@ extern "C" int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, c
         return fail(IVF_EINVAL, "ivf_u8_search_noalloc: null device pointer");
     if (n_query == 0) return IVF_OK;
     if (dev < 0 || dev >= kMaxDevices) return fail(IVF_EINVAL, "ivf_u8_search_noalloc: device index out of range");
-    cudaError_t e = cudaSetDevice(dev);
-    if (e != cudaSuccess) return fail(IVF_ECUDA, std::string("cudaSetDevice: ") + cudaGetErrorString(e));
+    DeviceGuard guard(dev);
+    int cur = -1;
+    cudaError_t e = cudaGetDevice(&cur);
+    if (e != cudaSuccess || cur != dev)
+        return fail(IVF_ECUDA, std::string("could not make the index's device current: ") + cudaGetErrorString(e));
     void* base = nullptr;
     e = scratch_address(dev, &base);
     if (e != cudaSuccess) {
@@ -118,6 +144,18 @@ extern "C" int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, c
     wl.pair_q = cv.take<int32_t>((size_t)n_query * n_probes);
     wl.pair_l = cv.take<int32_t>((size_t)n_query * n_probes);
     wl.n_pairs = wl.list_off + nlist;
+    // the grouped kernel (one read of a list per 64 probing queries) where the
+    // shape allows it, as ivf_u8_search chooses; its group words hold pair
+    // indices below 2^25
+    const bool grouped = exact_group_usable(d, k) && ls.sqnorm != nullptr &&
+                         (size_t)n_query * n_probes < ((size_t)1 << 25);
+    if (grouped) {
+        wl.grp_cnt = cv.take<int32_t>((size_t)nlist + 1);
+        wl.grp_off = cv.take<int32_t>((size_t)nlist + 1);
+        wl.groups = cv.take<int64_t>((size_t)n_query * n_probes);
+        wl.n_groups = wl.grp_off + nlist;
+        wl.gq = 64;
+    }
     const size_t scan_bytes = worklist_scan_bytes(nlist);
     void* scan_tmp = cv.take<unsigned char>(scan_bytes);
     CandBuf cb{};
@@ -138,7 +176,8 @@ extern "C" int ivf_u8_search_noalloc(void* idx_ctx, const uint8_t* d_query_u8, c
     if ((e = cudaMemsetAsync(cb.overflow, 0, sizeof(int32_t), st)) ||
         (e = build_worklist(d_probes, n_query, n_probes, nlist_global, g2l, nlist, wl, scan_tmp, scan_bytes, st)) ||
         (e = reset_candidates(cb, n_query, st)) ||
-        (e = exact_scan(d_query_u8, n_query, d, ls, wl, n_query * n_probes, cb, counter, st)) ||
+        (e = grouped ? exact_group_scan(d_query_u8, d, k, ls, wl, n_query * n_probes, cb, counter, st)
+                     : exact_scan(d_query_u8, n_query, d, ls, wl, n_query * n_probes, cb, counter, st)) ||
         (e = select_top_r(cb, n_query, topk, st)) ||
         (e = keys_to_exact_results(topk, n_query, k, d_out_ids, d_out_dist, nullptr, st))) {
         cudaGetLastError();

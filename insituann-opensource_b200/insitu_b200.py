@@ -146,14 +146,27 @@ def load_library(require_device: bool = False):
 
 
 def _p(a) -> Optional[int]:
-    """Host pointer of a numpy array (None passes NULL)."""
+    """Address of a numpy array or of a torch tensor's data (None passes NULL)."""
     if a is None:
         return None
+    if hasattr(a, "data_ptr"):
+        return a.data_ptr()
     return a.ctypes.data
 
 
+_TORCH_DT = {np.uint8: "uint8", np.int32: "int32", np.int64: "int64", np.float32: "float32"}
+
+
 def _c(a, dt):
-    return None if a is None else np.ascontiguousarray(a, dtype=dt)
+    """C-contiguous array of dtype dt; torch tensors (host or device) stay torch tensors."""
+    if a is None:
+        return None
+    if hasattr(a, "data_ptr"):
+        import torch
+
+        t = a.to(getattr(torch, _TORCH_DT[dt]))
+        return t.contiguous()
+    return np.ascontiguousarray(a, dtype=dt)
 
 
 class Index:

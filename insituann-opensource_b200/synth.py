@@ -97,11 +97,27 @@ def _component_ids(n, ncomp, seed, stream, device, zipf: Optional[float]):
     return torch.multinomial(w.float(), n, replacement=True, generator=g)
 
 
-def mixture_u8(n, d, ncomp, sigma, seed, device="cpu", start=0, zipf=None, lo=32.0, hi=224.0, chunk=1 << 20,
-               stream_base=0):
-    """uint8 rows from a Gaussian mixture: centers U[lo, hi], per-dim sigma, rounded and clipped."""
+def u8_centers(d, ncomp, seed, device="cpu", lo=32.0, hi=224.0):
+    """Mixture centers of mixture_u8: uniform in [lo, hi] per dimension."""
     gc = _gen(seed, 1 << 40, device)
-    centers = lo + (hi - lo) * torch.rand((ncomp, d), generator=gc, device=device)
+    return lo + (hi - lo) * torch.rand((ncomp, d), generator=gc, device=device)
+
+
+def f32_centers(d, ncomp, seed, device="cpu"):
+    """Mixture centers of mixture_f32_unit: Gaussian directions on the unit sphere."""
+    gc = _gen(seed, 1 << 40, device)
+    centers = torch.randn((ncomp, d), generator=gc, device=device)
+    return centers / centers.norm(dim=1, keepdim=True)
+
+
+def mixture_u8(n, d, ncomp, sigma, seed, device="cpu", start=0, zipf=None, lo=32.0, hi=224.0, chunk=1 << 20,
+               stream_base=0, centers=None):
+    """uint8 rows from a Gaussian mixture: centers U[lo, hi], per-dim sigma, rounded and clipped.
+
+    Rows start .. start+n-1 of the seeded sequence (start a multiple of chunk);
+    centers (from u8_centers) may be passed to skip recomputing them."""
+    if centers is None:
+        centers = u8_centers(d, ncomp, seed, device, lo, hi)
     out = torch.empty((n, d), dtype=torch.uint8, device=device)
     for c0 in range(0, n, chunk):
         c1 = min(n, c0 + chunk)
@@ -113,11 +129,11 @@ def mixture_u8(n, d, ncomp, sigma, seed, device="cpu", start=0, zipf=None, lo=32
     return out
 
 
-def mixture_f32_unit(n, d, ncomp, sigma, seed, device="cpu", start=0, chunk=1 << 20, stream_base=0):
+def mixture_f32_unit(n, d, ncomp, sigma, seed, device="cpu", start=0, chunk=1 << 20, stream_base=0,
+                     centers=None):
     """fp32 rows from a Gaussian mixture (centers on the unit sphere, per-dim sigma), unit-normalised."""
-    gc = _gen(seed, 1 << 40, device)
-    centers = torch.randn((ncomp, d), generator=gc, device=device)
-    centers = centers / centers.norm(dim=1, keepdim=True)
+    if centers is None:
+        centers = f32_centers(d, ncomp, seed, device)
     out = torch.empty((n, d), dtype=torch.float32, device=device)
     for c0 in range(0, n, chunk):
         c1 = min(n, c0 + chunk)
@@ -294,22 +310,183 @@ def delta_segment(n_delta: int, nlist: int, M: int, base_id: int, d: int, seed: 
     return out
 
 
-def brute_force_gt(base: torch.Tensor, q: torch.Tensor, k: int, batch_rows: int = 1 << 20) -> np.ndarray:
-    """Exact top-k original ids by L2 (ties by smaller id), for recall."""
-    qf = q.float()
-    qn = (qf * qf).sum(1)
-    best_d = torch.full((q.shape[0], k), float("inf"), device=q.device)
-    best_i = torch.full((q.shape[0], k), -1, dtype=torch.int64, device=q.device)
-    for i in range(0, base.shape[0], batch_rows):
-        xb = base[i:i + batch_rows].float()
-        dd = qn[:, None] + (xb * xb).sum(1)[None, :] - 2.0 * (qf @ xb.T)
-        vd, vi = torch.topk(dd, min(k, xb.shape[0]), dim=1, largest=False)
-        cd = torch.cat([best_d, vd], 1)
-        ci = torch.cat([best_i, vi + i], 1)
-        o = torch.argsort(cd, dim=1, stable=True)[:, :k]
-        best_d = torch.gather(cd, 1, o)
-        best_i = torch.gather(ci, 1, o)
-    return best_i.int().cpu().numpy()
+def gt_keys(base: torch.Tensor, q: torch.Tensor, k: int, ids: Optional[torch.Tensor] = None,
+            batch_rows: int = 1 << 15) -> torch.Tensor:
+    """Exact top-k of q against the rows of base as keys (distance bits << 32) | id, ascending.
+
+    uint8 rows: the distance is the exact integer |q|^2 + |x|^2 - 2 q.x; q.x
+    comes from an fp32 GEMM of integer operands, which is exact (every
+    partial sum is an integer below 128 * 255^2 < 2^24 and TF32 is off), and
+    the three terms are combined in int64.  fp32 rows: fp32 |q|^2 + |x|^2 -
+    2 q.x, clamped at 0.  ids [n] are the rows' original ids (default: the
+    row index).  Ties go to the smaller id."""
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        nq = q.shape[0]
+        is_u8 = base.dtype == torch.uint8
+        qf = q.float()
+        if is_u8:
+            qn = (qf * qf).sum(1).round().long()
+        else:
+            qn = (qf * qf).sum(1)
+        best = torch.full((nq, k), (1 << 63) - 1, dtype=torch.int64, device=q.device)
+        for i in range(0, base.shape[0], batch_rows):
+            xb = base[i:i + batch_rows].float()
+            dot = qf @ xb.T
+            if is_u8:
+                xn = (xb * xb).sum(1).round().long()
+                dd = qn[:, None] + xn[None, :] - 2 * dot.round().long()          # exact, < 2^31
+            else:
+                dd = (qn[:, None] + (xb * xb).sum(1)[None, :] - 2.0 * dot).clamp_min(0.0)
+                dd = dd.view(torch.int32).long()                                 # non-negative: bits order as values
+            rid = (torch.arange(i, i + xb.shape[0], device=q.device) if ids is None
+                   else ids[i:i + xb.shape[0]].long())
+            key = (dd << 32) | rid[None, :]
+            kb = min(k, xb.shape[0])
+            vk, _ = torch.topk(key, kb, dim=1, largest=False)
+            best, _ = torch.sort(torch.cat([best, vk], 1), dim=1)
+            best = best[:, :k].contiguous()
+        return best
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def merge_gt_keys(keys: torch.Tensor, k: int) -> np.ndarray:
+    """keys [..., nq, m] from several parts (e.g. gathered from ranks) -> top-k original ids [nq, k]."""
+    if keys.dim() == 3:
+        keys = keys.permute(1, 0, 2).reshape(keys.shape[1], -1)
+    best, _ = torch.sort(keys, dim=1)
+    best = best[:, :k]
+    ids = (best & 0xFFFFFFFF).int()
+    ids[best == (1 << 63) - 1] = -1
+    return ids.cpu().numpy()
+
+
+def brute_force_gt(base: torch.Tensor, q: torch.Tensor, k: int, batch_rows: int = 1 << 15) -> np.ndarray:
+    """Exact top-k original ids by L2 (ties by smaller id), for recall (see gt_keys)."""
+    return merge_gt_keys(gt_keys(base, q, k, batch_rows=batch_rows), k)
+
+
+# ----------------------------------------------------------------------------
+# shard-local index build (every rank builds only its own lists)
+# ----------------------------------------------------------------------------
+class RowSource:
+    """The seeded rows of one benchmark config, generated chunk by chunk.
+
+    Counter-based: chunk i (rows i*chunk .. ) is drawn from generators keyed by
+    (seed, i) alone, so any rank can produce any chunk without the others; the
+    bytes equal mixture_u8 / mixture_f32_unit over the whole range."""
+
+    def __init__(self, kind: str, n: int, d: int, ncomp: int, sigma: float, seed: int, device,
+                 zipf: Optional[float] = None, chunk: int = 1 << 20, stream_base: int = 0):
+        self.kind, self.n, self.d, self.ncomp, self.sigma, self.seed = kind, n, d, ncomp, sigma, seed
+        self.device, self.zipf, self.chunk, self.stream_base = device, zipf, chunk, stream_base
+        self.centers = (u8_centers(d, ncomp, seed, device) if kind == "u8" else f32_centers(d, ncomp, seed, device))
+        self.nchunks = (n + chunk - 1) // chunk
+
+    def rows(self, start: int, n: int) -> torch.Tensor:
+        """rows start .. start+n-1 (start a multiple of the chunk)."""
+        if self.kind == "u8":
+            return mixture_u8(n, self.d, self.ncomp, self.sigma, self.seed, device=self.device, start=start,
+                              zipf=self.zipf, chunk=self.chunk, stream_base=self.stream_base, centers=self.centers)
+        return mixture_f32_unit(n, self.d, self.ncomp, self.sigma, self.seed, device=self.device, start=start,
+                                chunk=self.chunk, stream_base=self.stream_base, centers=self.centers)
+
+    def chunk_range(self, i: int):
+        return i * self.chunk, min(self.n, (i + 1) * self.chunk)
+
+    def chunk_rows(self, i: int) -> torch.Tensor:
+        r0, r1 = self.chunk_range(i)
+        return self.rows(r0, r1 - r0)
+
+
+def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0, world: int = 1, dist=None,
+                   kmeans_iters: int = 20, pq_iters: int = 12, train_n: int = 500_000,
+                   kmeans_sample: Optional[int] = None, row_bytes: Optional[int] = None, assign_fn=None,
+                   log=None):
+    """Residual-PQ index of src, built so that each rank holds only its own lists.
+
+    1. rank 0 runs k-means on the first kmeans_sample rows (an i.i.d. sample of
+       the mixture) and broadcasts the centroids;
+    2. each rank assigns the chunks i with i % world == rank to their nearest
+       centroid; an all-reduce completes the assignment on every rank;
+    3. rank 0 trains the PQ codebook on the residuals of the first train_n rows
+       and broadcasts it;
+    4. lists go to ranks by LPT on bytes (shard.lpt_shards; one rank owns all
+       at world == 1); every rank regenerates the chunks, keeps the rows of
+       its lists, orders them cluster-major (stable: by list, then original
+       id, as dataset.cuh:559-592) and encodes their residuals.
+    Returns device tensors (centroids, codebook, codes, r2o, base_rr) and
+    numpy maps (my_lists, local offsets/counts, global offsets/counts)."""
+    import shard
+
+    dev = src.device
+    say = log or (lambda *_: None)
+    n, d = src.n, src.d
+    S = min(n, kmeans_sample or 64 * nlist)
+    if rank == 0:
+        xs = src.rows(0, S)
+        cent = kmeans(xs, nlist, kmeans_iters, seed)
+        del xs
+    else:
+        cent = torch.empty((nlist, d), dtype=torch.float32, device=dev)
+    if world > 1:
+        dist.broadcast(cent, src=0)
+    say("k-means")
+    assign_fn = assign_fn or (lambda x, c: assign(x, c))
+    a = torch.zeros(n, dtype=torch.int32, device=dev)
+    for i in range(rank, src.nchunks, world):
+        r0, r1 = src.chunk_range(i)
+        a[r0:r1] = assign_fn(src.chunk_rows(i), cent).int()
+    if world > 1:
+        dist.all_reduce(a)
+    say("assignment")
+    T = min(train_n, n)
+    if rank == 0:
+        resid = src.rows(0, T).float() - cent[a[:T].long()]
+        cb = train_pq(resid, M, pq_iters, seed)
+        del resid
+    else:
+        cb = torch.empty((M, 256, d // M), dtype=torch.float32, device=dev)
+    if world > 1:
+        dist.broadcast(cb, src=0)
+    say("codebook")
+    counts_g = torch.bincount(a.long(), minlength=nlist).cpu().numpy().astype(np.int32)
+    offsets_g = np.zeros(nlist, np.int64)
+    offsets_g[1:] = np.cumsum(counts_g, dtype=np.int64)[:-1]
+    rb = row_bytes or (M + (1 if src.kind == "u8" else 4) * d)
+    owner = shard.lpt_shards(counts_g, rb, world) if world > 1 else np.zeros(nlist, np.int32)
+    my_lists = np.where(owner == rank)[0].astype(np.int32)
+    mine = torch.from_numpy(owner == rank).to(dev)
+    parts, pids = [], []
+    for i in range(src.nchunks):
+        r0, r1 = src.chunk_range(i)
+        sel = torch.nonzero(mine[a[r0:r1].long()]).squeeze(1)
+        if sel.numel():
+            parts.append(src.chunk_rows(i)[sel])
+            pids.append(sel + r0)
+    rows = torch.cat(parts) if parts else torch.empty((0, d), dtype=torch.uint8 if src.kind == "u8" else
+                                                      torch.float32, device=dev)
+    ids = torch.cat(pids) if pids else torch.empty(0, dtype=torch.int64, device=dev)
+    del parts, pids
+    order = torch.argsort((a[ids].long() << 32) | ids)
+    rows = rows[order].contiguous()
+    ids = ids[order]
+    del order
+    say("rows")
+    codes = torch.empty((rows.shape[0], M), dtype=torch.uint8, device=dev)
+    bs = 1 << 20
+    for i in range(0, rows.shape[0], bs):
+        resid = rows[i:i + bs].float() - cent[a[ids[i:i + bs]].long()]
+        codes[i:i + bs] = encode_pq(resid, cb)
+    say("codes")
+    cnt = counts_g[my_lists].astype(np.int32)
+    off = np.zeros(len(my_lists), np.int64)
+    if len(my_lists):
+        off[1:] = np.cumsum(cnt, dtype=np.int64)[:-1]
+    return dict(centroids=cent, codebook=cb, codes=codes, r2o=ids.int(), base_rr=rows, my_lists=my_lists,
+                offsets=off, counts=cnt, offsets_global=offsets_g, counts_global=counts_g)
 
 
 def recall_at_k(ids: np.ndarray, gt: np.ndarray, k: int) -> float:

@@ -174,6 +174,35 @@ def pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_
     return ids, dist
 
 
+def _split_queries(nq, threads):
+    threads = max(1, min(threads or (os.cpu_count() or 1), nq))
+    step = (nq + threads - 1) // threads
+    return [(s, min(nq, s + step)) for s in range(0, nq, step)]
+
+
+def route_l2_par(q, cent, nprobe, threads=0):
+    """route_l2 over query slices on host threads (the C calls release the GIL)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    q = _c(q, np.float32)
+    cent = _c(cent, np.float32)
+    parts = _split_queries(q.shape[0], threads)
+    with ThreadPoolExecutor(len(parts)) as ex:
+        res = list(ex.map(lambda r: route_l2(q[r[0]:r[1]], cent, nprobe), parts))
+    return np.concatenate([a for a, _ in res]), np.concatenate([b for _, b in res])
+
+
+def pq_search_par(cent, codebook, codes, offsets, counts, r2o, q, probes, k, threads=0, **kw):
+    """pq_search over query slices on host threads (results are per query, so equal to one call)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    parts = _split_queries(q.shape[0], threads)
+    with ThreadPoolExecutor(len(parts)) as ex:
+        res = list(ex.map(lambda r: pq_search(cent, codebook, codes, offsets, counts, r2o, q[r[0]:r[1]],
+                                              probes[r[0]:r[1]], k, **kw), parts))
+    return tuple(None if res[0][i] is None else np.concatenate([x[i] for x in res]) for i in range(len(res[0])))
+
+
 def reorder(assign, nlist):
     assign = _c(assign, np.int32)
     n = assign.shape[0]

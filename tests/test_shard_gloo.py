@@ -235,3 +235,50 @@ def test_dropped_rank_is_detected_by_timeout():
     assert all(not p.is_alive() for p in ps)
     what, secs = out.get()
     assert what != "no error" and secs < 30
+
+
+def _build_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+
+        src = synth.RowSource("u8", 40000, 32, 40, 10.0, 5, "cpu", chunk=1 << 13)
+        kw = dict(kmeans_iters=3, pq_iters=2, train_n=5000, kmeans_sample=4000)
+        b = synth.build_pq_shard(src, 48, 8, 5, rank=rank, world=world, dist=dist, **kw)
+        b1 = synth.build_pq_shard(src, 48, 8, 5, **kw)
+        ok = torch.equal(b["centroids"], b1["centroids"]) and torch.equal(b["codebook"], b1["codebook"])
+        for i, l in enumerate(b["my_lists"]):
+            s, c, s1 = b["offsets"][i], b["counts"][i], b1["offsets"][l]
+            ok &= bool(c == b1["counts"][l])
+            ok &= torch.equal(b["codes"][s:s + c], b1["codes"][s1:s1 + c])
+            ok &= torch.equal(b["base_rr"][s:s + c], b1["base_rr"][s1:s1 + c])
+            ok &= torch.equal(b["r2o"][s:s + c], b1["r2o"][s1:s1 + c])
+        needed = np.array([0, 3, 7, 20, 33, 47], np.int64)
+        g = bench.gather_lists(b, needed, rank, world, dist, torch.device("cpu"))
+        if rank == 0:
+            h = bench.host_index(b1)
+            for l in range(48):
+                c = g["counts"][l]
+                if l in needed:
+                    s, s1 = g["offsets"][l], h["offsets"][l]
+                    ok &= bool(c == h["counts"][l])
+                    for key in ("codes", "base_rr", "r2o"):
+                        ok &= bool((g[key][s:s + c] == h[key][s1:s1 + c]).all())
+                else:
+                    ok &= bool(c == 0)
+        out[rank] = bool(ok) and len(b["my_lists"]) > 0
+    finally:
+        dist.destroy_process_group()
+
+
+def test_shard_local_build_and_list_gather():
+    """Two ranks each build only their own lists (rows regenerated from the
+    counter-based seeds, assignment split over the ranks): every owned list
+    equals the single-rank build's, the lists partition the index, and the
+    bench's oracle gather reassembles any set of lists on rank 0."""
+    world = 2
+    mgr = mp.Manager()
+    out = mgr.dict()
+    mp.spawn(_build_worker, args=(world, _free_port(), out), nprocs=world, join=True)
+    assert out.get(0) and out.get(1)

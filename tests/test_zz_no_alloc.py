@@ -36,14 +36,16 @@ def _reference_search(e, q_u8, probes, k):
 
 
 def test_noalloc_matches_ivf_u8_search_twice(cuda_ok):
-    n, d, nlist, k = 40000, 128, 64, 10
+    n, d, nlist = 40000, 128, 64
     base = synth.mixture_u8(n, d, 64, 12.0, seed=71)
     e = synth.build_u8_index(base, nlist, seed=71, iters=6)
     e["base_cm"][300:1400] = e["base_cm"][299]   # distance ties, broken by original id
     L = ib.load_library(require_device=True)
     index = ib.Index().load_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], e["centroids"])
     stream = torch.cuda.Stream()
-    for call, (nq, nprobe, seed) in enumerate([(200, 8, 72), (97, 13, 73)]):
+    # two calls in a row at k = 10 (the grouped kernel: d = 128, k <= 16), then one at
+    # k = 20 (the per-pair kernel); each must equal ivf_u8_search on the same probes
+    for call, (nq, nprobe, seed, k) in enumerate([(200, 8, 72, 10), (97, 13, 73, 10), (64, 8, 75, 20)]):
         q = synth.mixture_u8(nq, d, 64, 12.0, seed=71, stream_base=(1 << 20) + seed).numpy()
         probes, _ = oracle.route_l2(q.astype(np.float32), e["centroids"], nprobe)
         exp_ids, exp_dist = _reference_search(e, q, probes, k)
@@ -55,6 +57,7 @@ def test_noalloc_matches_ivf_u8_search_twice(cuda_ok):
         rc = L.ivf_u8_search_noalloc(index.h, dq.data_ptr(), dp.data_ptr(), nq, nprobe, k, ids.data_ptr(),
                                      dist.data_ptr(), ctypes.c_void_p(stream.cuda_stream))
         assert rc == 0, L.ivf_global_last_error().decode()
+        assert torch.cuda.current_device() == 0          # the caller's device is left as it was
         stream.synchronize()
         assert np.array_equal(ids.cpu().numpy(), exp_ids), f"call {call}: ids differ"
         assert np.array_equal(dist.cpu().numpy(), exp_dist), f"call {call}: distances differ"
