@@ -147,7 +147,7 @@ struct BatchCtx {
     int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
     int res_nq = 0, res_k = 0;
     int probes_nq = 0, probes_np = 0;
-    Grow route_dist, route_rowfb, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
+    Grow route_dist, route_rowfb, route_split, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
     Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
     std::vector<void*> owned;
     std::string err;
@@ -302,15 +302,18 @@ void prepare_route_tc(IndexCtx* x, int nlist, int d) {
        "routing operands");
 }
 
-// Routing kernels (all give the same lists bit for bit): INSITU_ROUTE_TC=0
-// exact CUDA-core kernels only; 1 (default) the fused tensor-core kernel for
-// nprobe <= 8, where it was measured faster, else the exact kernels; 2 the
-// tensor-core kernels for every nprobe (fused up to 32, distance matrix and
-// rescoring above).  Read on every call.
+// Routing kernels (all give the same lists bit for bit), INSITU_ROUTE_TC:
+//   0  the exact CUDA-core kernels only;
+//   1  (default) the fused tensor-core kernel wherever it applies (nprobe <=
+//      32, operands within shared memory), else the tensor-core matrix +
+//      rescoring for 8192 lists or more, else the exact kernels;
+//   2  the fused kernel where it applies, else the tensor-core matrix;
+//   3  the tensor-core matrix + rescoring for every shape it covers.
+// Read on every call.
 int route_tc_mode() {
     const char* v = std::getenv("INSITU_ROUTE_TC");
     if (!v || !v[0]) return 1;
-    return v[0] == '0' ? 0 : v[0] == '2' ? 2 : 1;
+    return (v[0] >= '0' && v[0] <= '3') ? v[0] - '0' : 1;
 }
 
 void load_centroids(IndexCtx* x, const float* centroids, int nlist, int d) {
@@ -342,42 +345,49 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     require(x->nlist_global >= nprobe || keys, "n_probes > n_total_clusters");
     const int L = std::min(nprobe, 2048);
     require(L == nprobe, "n_probes > 2048 is not supported");
-    size_t row = (size_t)x->nlist * sizeof(uint32_t);
-    int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
-    uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
     StageScope stage(b, IVF_STAGE_ROUTE);
-    // default policy (mode 1): the fused tensor-core kernel for nprobe <= 8 where
-    // it fits; the tensor-core matrix + rescoring for 8192 lists or more (2x the
-    // exact kernels' speed at 65536 lists, d 128); the exact kernels otherwise
     const int mode = x->tc_ops ? route_tc_mode() : 0;
-    const bool tc = mode == 2 || (mode == 1 && x->nlist >= 8192);
-    for (int s = 0; s < nq; s += nsub) {
-        int n = std::min(nsub, nq - s);
-        const float* qs = b->q + (size_t)s * x->d;
-        if ((mode == 2 || (mode == 1 && nprobe <= 8)) && route_tc_fused_usable(x->d, x->nlist, nprobe)) {
-            int32_t* fb = ensure<int32_t>(b, b->route_rowfb, (size_t)nsub);
-            ck(route_tc_fused(qs, n, x->tc_ops, x->tc_cne, x->tc_cnmax, x->valid, x->nlist, x->d, x->cent, nprobe,
-                              x->l2g, keys ? nullptr : b->probes + (size_t)s * nprobe,
-                              keys ? keys + (size_t)s * nprobe : nullptr, fb, b->overflow, b->st),
+    if ((mode == 1 || mode == 2) && route_tc_fused_usable(x->d, x->nlist, nprobe)) {
+        // one tcgen05 sweep, no distance matrix; the per-split keys bound the sub-batch
+        const int splits = route_tc_fused_splits(nq, x->nlist);
+        const size_t per_q = (size_t)splits * nprobe * sizeof(uint64_t) + sizeof(int32_t);
+        const int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
+        int32_t* fb = ensure<int32_t>(b, b->route_rowfb, (size_t)nsub);
+        uint64_t* sk = splits > 1 ? ensure<uint64_t>(b, b->route_split, (size_t)nsub * splits * nprobe) : nullptr;
+        for (int s = 0; s < nq; s += nsub) {
+            const int n = std::min(nsub, nq - s);
+            ck(route_tc_fused(b->q + (size_t)s * x->d, n, x->tc_ops, x->tc_cne, x->tc_cnmax, x->valid, x->nlist,
+                              x->d, x->cent, nprobe, x->l2g, keys ? nullptr : b->probes + (size_t)s * nprobe,
+                              keys ? keys + (size_t)s * nprobe : nullptr, fb, sk, splits, b->overflow, b->st),
                "route_tc_fused");
-            continue;
         }
-        if (tc) {
-            ck(route_tc(qs, n, x->tc_ops, x->tc_cn, x->valid, x->nlist, x->d, dist, b->overflow, b->st), "route_tc");
-            ck(route_rescore(dist, qs, n, x->cent, x->tc_cnmax, x->valid, x->nlist, x->d, nprobe, x->l2g,
-                             keys ? nullptr : b->probes + (size_t)s * nprobe, nullptr,
-                             keys ? keys + (size_t)s * nprobe : nullptr, b->st),
-               "route_rescore");
-            continue;
-        }
-        ck(route_distances(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances");
-        if (keys) {
-            ck(route_select(dist, n, x->nlist, nprobe, x->l2g, nullptr, nullptr, keys + (size_t)s * nprobe, b->st),
-               "route_select");
-        } else {
-            ck(route_select(dist, n, x->nlist, nprobe, x->l2g, b->probes + (size_t)s * nprobe, nullptr, nullptr,
-                            b->st),
-               "route_select");
+    } else {
+        size_t row = (size_t)x->nlist * sizeof(uint32_t);
+        int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)nq, scratch_budget() / 4 / row));
+        uint32_t* dist = ensure<uint32_t>(b, b->route_dist, (size_t)nsub * x->nlist);
+        const bool tc = mode >= 2 || (mode == 1 && x->nlist >= 8192);
+        for (int s = 0; s < nq; s += nsub) {
+            int n = std::min(nsub, nq - s);
+            const float* qs = b->q + (size_t)s * x->d;
+            if (tc) {
+                ck(route_tc(qs, n, x->tc_ops, x->tc_cn, x->valid, x->nlist, x->d, dist, b->overflow, b->st),
+                   "route_tc");
+                ck(route_rescore(dist, qs, n, x->cent, x->tc_cnmax, x->valid, x->nlist, x->d, nprobe, x->l2g,
+                                 keys ? nullptr : b->probes + (size_t)s * nprobe, nullptr,
+                                 keys ? keys + (size_t)s * nprobe : nullptr, b->st),
+                   "route_rescore");
+                continue;
+            }
+            ck(route_distances(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances");
+            if (keys) {
+                ck(route_select(dist, n, x->nlist, nprobe, x->l2g, nullptr, nullptr, keys + (size_t)s * nprobe,
+                                b->st),
+                   "route_select");
+            } else {
+                ck(route_select(dist, n, x->nlist, nprobe, x->l2g, b->probes + (size_t)s * nprobe, nullptr,
+                                nullptr, b->st),
+                   "route_select");
+            }
         }
     }
     if (!keys) {

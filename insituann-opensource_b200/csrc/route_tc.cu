@@ -503,90 +503,150 @@ __global__ void __launch_bounds__(kRsT) route_rescore_kernel(const uint32_t* __r
 // ---------------------------------------------------------------------------
 // Fused routing for nprobe <= 32: one sweep, no distance matrix leaves the SM.
 // ---------------------------------------------------------------------------
-// The split operands of route_tc_kernel (K = 3d, 64-centroid tiles), so the
-// same eps = 2^-11 (|q|^2 + max |c|^2) bounds |D~ - D|.  8 warps; TMEM lane
-// quarter w % 4 holds rows 32 (w % 4) .. +31 and warp w reads columns
-// 32 (w / 4) .. +31 of every 64-column tile, so each row is shared by two
-// threads ("halves").  While the tiles stream by, each thread keeps
+// The split operands of route_tc_kernel (64-centroid tiles, parts
+// [c_hi | c_lo | c_hi]), so the same eps = 2^-11 (|q|^2 + max |c|^2) bounds
+// |D~ - D|.  The query operand holds [q_hi | q_lo] once; the MMAs of parts 0
+// and 1 both read q_hi.  A CTA whose 128 queries all have q_lo = 0 (queries
+// that bf16 holds exactly, e.g. integer values below 256) runs parts 0 and 1
+// only: q.c = q_hi.c_hi + q_hi.c_lo then misses only q.(c - c_hi - c_lo).
+//
+// Grid: (query blocks of 128, column splits); CTA (x, y) sweeps the tiles
+// [y * tiles_per_cta, ...) and produces, per query row, the exact top-L of
+// its columns; the splits are merged afterwards (route_split_merge_kernel).
+// The top-L of a union is the top-L of the parts' top-L, so the merged lists
+// equal the exact routing.
+//
+// Warp roles (320 threads, no block-wide barrier inside the sweep):
+//   warp 8  (one thread): bulk async copies of operand tiles into a ring of
+//           stages (as many as fit: 2-5), each stage freed by the commit of
+//           the MMAs that read it;
+//   warp 9  (one thread): tcgen05 MMAs of tile g into one of 4 TMEM
+//           accumulators, committed to the accumulator's "full" barrier;
+//   warps 0-7: TMEM lane quarter w % 4 (rows 32 (w % 4) .. +31), columns
+//           32 (w / 4) .. +31 of every tile (each row is shared by two
+//           threads, "halves"); each reads its 32 values with tcgen05.ld,
+//           frees the accumulator, then filters.
+// While the tiles stream by, each epilogue thread keeps
 //   * lv: the L smallest D~ it has seen (ascending), lmax = lv[L-1];
-//   * a list of (D~, list) with D~ <= lmax + 2 eps at the time it was seen,
-//     pruned to the current bound whenever it fills up (a prune that frees
-//     less than a quarter gives up on the row).
-// lmax only decreases and each half's lmax is at least the row's final L-th
-// smallest D~ (T~), so every list with D~ <= T~ + 2 eps -- a superset of the
-// exact top-L -- is in one of the two lists.  The candidates are rescored
-// exactly, the two halves' keys merged and the row's top-L written; a row
-// whose list overflowed is handed to route_exact_rows_kernel.
-constexpr int kFT = 256;                  // threads
+//   * a list of (D~, column) with D~ <= lmax + 2 eps at the time it was seen,
+//     pruned to the current bound before a piece of columns could overflow it
+//     (a prune that does not make room gives up on the row).
+// The filter tests c_n - 2 q.c <= lmax + 2 eps - |q|^2 (+ a rounding slack)
+// on column pairs with packed fp32 arithmetic; only a pair some lane of the
+// warp keeps takes the append branch.  lmax only decreases and each half's
+// lmax is at least the row's final L-th smallest D~ (T~), so every column
+// with D~ <= T~ + 2 eps -- a superset of the exact top-L -- is in one of the
+// two lists.  The candidates are rescored exactly and the row's top-L of this
+// split is written; a row whose list overflowed is handed to
+// route_exact_rows_kernel.  Every wait is bounded and also gives up once
+// another role has failed.
+constexpr int kFT = 256;                  // epilogue threads
+constexpr int kFBlock = 320;              // + the copy warp and the MMA warp
 constexpr int kFLMax = 32;                // largest L of the fused path
 constexpr int kFN = kTCN;                 // centroids per tile (MMA N)
-constexpr int kFList = 48;                // candidate slots per (row, half)
-constexpr int kFStages = 2;               // operand tiles in flight
+constexpr int kFAcc = 4;                  // TMEM accumulators
+constexpr int kFMaxStages = 8;
+constexpr int kFMaxSplits = 32;           // column splits per query block (one lane each in the merge)
 
-// the tile region holds the operand tiles, then the L-lists, then the exact keys
-__host__ __device__ constexpr size_t route_fused_region(int d) {
-    const size_t tiles = kFStages * (size_t)kFN * 3 * d * 2;
-    const size_t keys = (sizeof(uint64_t) + sizeof(uint16_t)) * kFT * (kFList / 2),
+// candidate slots per (row, half): the L smallest, one piece of kFW columns and a
+// band of near-ties above the running bound
+constexpr int kFW = 8;
+__host__ __device__ constexpr int fused_list(int lmax) { return lmax <= 16 ? lmax + 24 : 48; }
+
+// shared memory besides the stage region: A, candidate lists, qn / T~ / counts
+__host__ __device__ constexpr size_t route_fused_fixed(int d, int list) {
+    return (size_t)kTCM * 2 * d * 2 + (sizeof(float) + sizeof(uint16_t)) * kFT * (size_t)list +
+           sizeof(float) * 2 * kTCM + sizeof(int) * kFBlock;
+}
+// the stage region must hold two full (3-part) tiles, and after the sweep the
+// halves' L-lists and the rescored keys
+__host__ __device__ constexpr size_t route_fused_region_min(int d, int list) {
+    const size_t tiles = 2 * (size_t)kFN * 3 * d * 2;
+    const size_t keys = (sizeof(uint64_t) + sizeof(uint16_t)) * kFT * (list / 2),
                  lists = sizeof(float) * kTCM * kFLMax;
     const size_t m = keys > lists ? keys : lists;
     return tiles > m ? tiles : m;
 }
+constexpr size_t kFSmemCap = 227 * 1024 - 1536;  // dynamic shared memory of one CTA (1 KB static barriers aside)
 
-__host__ __device__ constexpr size_t route_fused_smem(int d) {
-    return (size_t)kTCM * 3 * d * 2 + route_fused_region(d) +                // A, tile region
-           (sizeof(float) + sizeof(uint16_t)) * kFT * kFList +                // candidate lists
-           sizeof(float) * 2 * kTCM + sizeof(int) * kFT;                      // qn, T~, counts
+__host__ __device__ constexpr size_t route_fused_region(int d, int list) {
+    return ((kFSmemCap - route_fused_fixed(d, list)) / 128) * 128;
 }
 
-template <int LMAX>
-__global__ void __launch_bounds__(kFT, 1)
+// wait on an mbarrier phase, bounded; gives up early once *fail is set
+__device__ __forceinline__ bool mbar_wait_or(uint64_t* bar, uint32_t parity, const volatile int* fail) {
+    for (int i = 0; i < kTCWaitSpins; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 31 && *fail) return false;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int LMAX, int LIST>
+__global__ void __launch_bounds__(kFBlock, 1)
     route_tc_fused_kernel(const float* __restrict__ q, int nq, int d, const uint16_t* __restrict__ ops,
                           const float* __restrict__ cne, const float* __restrict__ cn_max,
                           const uint8_t* __restrict__ valid, int nlist, const float* __restrict__ cent, int L,
-                          const int32_t* __restrict__ id_map, int32_t* out_ids, uint64_t* out_keys,
-                          int32_t* __restrict__ row_fallback, int* flag) {
+                          const int32_t* __restrict__ id_map, int tiles_per_cta, int region, int32_t* out_ids,
+                          uint64_t* out_keys, uint64_t* split_keys, int32_t* __restrict__ row_fallback, int* flag) {
     extern __shared__ __align__(1024) unsigned char sm[];
-    __shared__ __align__(8) uint64_t bar_b[kFStages];
-    __shared__ __align__(8) uint64_t bar_mma[2];
+    __shared__ __align__(8) uint64_t bar_full[kFMaxStages];
+    __shared__ __align__(8) uint64_t bar_empty[kFMaxStages];
+    __shared__ __align__(8) uint64_t bar_af[kFAcc];
+    __shared__ __align__(8) uint64_t bar_ae[kFAcc];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
     __shared__ int s_scan[33];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int quarter = warp & 3, half = warp >> 2;
-    const int row = quarter * 32 + lane;                  // TMEM lane = query row of this thread
-    const int K = 3 * d;
-    const uint32_t a_bytes = (uint32_t)kTCM * K * 2, b_bytes = (uint32_t)kFN * K * 2;
+    const bool epi = warp < 8;
+    const int quarter = warp & 3, half = (warp >> 2) & 1;
+    const int row = quarter * 32 + lane;                  // TMEM lane = query row of an epilogue thread
+    const uint32_t part_bytes = (uint32_t)kFN * d * 2;    // one part of one tile
+    const uint32_t a_bytes = (uint32_t)kTCM * 2 * d * 2;
     unsigned char* sA = sm;
-    unsigned char* sB = sm + a_bytes;                          // tiles [kFStages][b_bytes], later s_lv, s_key
-    float* s_lv = reinterpret_cast<float*>(sB);                                   // [LMAX][128] (half 1)
-    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [kFList / 2][kFT]
-    uint16_t* s_pair = reinterpret_cast<uint16_t*>(s_key + kFT * (kFList / 2));   // [kFT * kFList / 2]
-    float* s_lval = reinterpret_cast<float*>(sB + route_fused_region(d));         // [kFList][kFT]
-    uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * kFList);        // [kFList][kFT]
-    float* s_qn = reinterpret_cast<float*>(s_lcol + kFT * kFList);                // [128]
+    unsigned char* sB = sm + a_bytes;                                             // stage region
+    float* s_lval = reinterpret_cast<float*>(sB + region);                       // [LIST][kFT]
+    uint16_t* s_lcol = reinterpret_cast<uint16_t*>(s_lval + kFT * LIST);          // [LIST][kFT]
+    float* s_qn = reinterpret_cast<float*>(s_lcol + kFT * LIST);                  // [128]
     float* s_T = s_qn + kTCM;                                                     // [128]
-    int* s_nc = reinterpret_cast<int*>(s_T + kTCM);                               // [kFT]
+    int* s_nc = reinterpret_cast<int*>(s_T + kTCM);                               // [kFBlock]
+    // after the sweep the stage region holds the halves' L-lists, then the rescored keys
+    float* s_lv = reinterpret_cast<float*>(sB);                                   // [LMAX][128] (half 1)
+    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [LIST / 2][kFT]
+    uint16_t* s_pair = reinterpret_cast<uint16_t*>(s_key + kFT * (LIST / 2));     // [kFT * LIST / 2]
     const int q0 = blockIdx.x * kTCM;
-    const int ntiles = (nlist + kFN - 1) / kFN;
+    const int ntiles_all = (nlist + kFN - 1) / kFN;
+    const int t_begin = blockIdx.y * tiles_per_cta;
+    const int nt = min(ntiles_all, t_begin + tiles_per_cta) - t_begin;           // >= 1 (launch)
+    const int c_begin = t_begin * kFN;
     const float INF = __int_as_float(0x7f800000);
 
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(2 * kFN)
+                     "r"(kFAcc * kFN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     if (tid == 0) {
-        for (int b = 0; b < kFStages; ++b) mbar_init(&bar_b[b], 1);
-        mbar_init(&bar_mma[0], 1);
-        mbar_init(&bar_mma[1], 1);
+        for (int b = 0; b < kFMaxStages; ++b) {
+            mbar_init(&bar_full[b], 1);
+            mbar_init(&bar_empty[b], 1);
+        }
+        for (int a = 0; a < kFAcc; ++a) {
+            mbar_init(&bar_af[a], 1);
+            mbar_init(&bar_ae[a], 8);         // one arrival per epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
     }
-    // A operand [q_hi | q_hi | q_lo]: thread t builds row t % 128, the 8-element
-    // groups g of its half; each group is read once (two 16-byte loads) and
-    // written as its chunk in all three parts
-    {
+    // A operand [q_hi | q_lo]: epilogue thread t builds row t % 128, the 8-element
+    // groups g of its half (two 16-byte loads per group)
+    int has_lo = 0;
+    if (epi) {
         const int r = tid & (kTCM - 1), qi = q0 + r;
         const bool qok = qi < nq;
         const float4* qr4 = reinterpret_cast<const float4*>(q + (size_t)(qok ? qi : 0) * d);
@@ -607,8 +667,8 @@ __global__ void __launch_bounds__(kFT, 1)
             split2(vb.x, vb.y, hi4.z, lo4.z);
             split2(vb.z, vb.w, hi4.w, lo4.w);
             *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, g, kTCM)) = hi4;
-            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, G + g, kTCM)) = hi4;
-            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, 2 * G + g, kTCM)) = lo4;
+            *reinterpret_cast<uint4*>(sA + tc_chunk_off(r, G + g, kTCM)) = lo4;
+            has_lo |= (lo4.x | lo4.y | lo4.z | lo4.w) != 0u;
         }
         if (tid < kTCM) {
             float qn = 0.f;
@@ -625,68 +685,101 @@ __global__ void __launch_bounds__(kFT, 1)
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();
+    const int nparts = __syncthreads_or(has_lo) ? 3 : 2;
     asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
     const uint32_t tmem = s_tmem;
-    const unsigned char* gops = reinterpret_cast<const unsigned char*>(ops);
-    constexpr uint32_t idesc = umma_idesc_bf16(kTCM, kFN);
-    const uint32_t a_addr = smem_u32(sA);
-    const float qn = s_qn[row];
-    const float eps2 = 2.f * ldexpf(qn + *cn_max, -11);
-    auto copy_tile = [&](int g) {
-        const int b = g % kFStages;
-        mbar_arrive_expect(&bar_b[b], b_bytes);
-        bulk_g2s(sB + (size_t)b * b_bytes, gops + (size_t)g * b_bytes, b_bytes, &bar_b[b]);
-    };
-    auto mma_tile = [&](int g) -> bool {
-        const int b = g % kFStages;
-        if (!mbar_wait(&bar_b[b], (uint32_t)((g / kFStages) & 1))) return false;
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        const uint32_t b_addr = smem_u32(sB + (size_t)b * b_bytes);
-        const uint32_t dacc = tmem + (uint32_t)((g & 1) * kFN);
-        for (int kb = 0; kb < K / 16; ++kb) {
-            const uint64_t ad = umma_smem_desc(a_addr + (uint32_t)kb * (kTCM * 32));
-            const uint64_t bd = umma_smem_desc(b_addr + (uint32_t)kb * (kFN * 32));
-            const uint32_t acc = kb > 0 ? 1u : 0u;
-            asm volatile(
-                "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(dacc),
-                "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
-                : "memory");
-        }
-        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                         smem_u32(&bar_mma[g & 1]))
-                     : "memory");
-        return true;
-    };
-    if (tid == 0) {
-        for (int i = 0; i < kFStages && i < ntiles; ++i) copy_tile(i);
-        if (!mma_tile(0)) s_fail = 1;
-    }
+    const uint32_t stage_bytes = (uint32_t)nparts * part_bytes;
+    int nst = (int)((uint32_t)region / stage_bytes);
+    if (nst > kFMaxStages) nst = kFMaxStages;
+    const volatile int* vfail = &s_fail;
+    int issued = 0, mma_issued = 0;
+
+    // the L smallest, ascending, in the last L slots; the slots before them hold
+    // -inf and never change, so lmax = lv[LMAX - 1] needs no runtime index
     float lv[LMAX];
 #pragma unroll
-    for (int i = 0; i < LMAX; ++i) lv[i] = INF;
-    float lmax = INF, lim = INF;           // lim = lmax + 2 eps1
+    for (int i = 0; i < LMAX; ++i) lv[i] = i < LMAX - L ? -INF : INF;
+    float lmax = INF;
     int nc = 0;                            // entries in this thread's list
     bool over = false;                     // the list overflowed within the bound
-    // entry i of this thread's list at [i][tid]: the lanes of a warp store to 32
-    // different banks whatever their list lengths
-    float* myval = s_lval + tid;
+    const float qn = epi ? s_qn[row] : 0.f;
+    const float eps2 = 2.f * ldexpf(qn + *cn_max, -11);
+    float* myval = s_lval + tid;           // entry i at [i][tid]: a warp's stores hit 32 banks
     uint16_t* mycol = s_lcol + tid;
-    int g = 0;
-    for (; g < ntiles; ++g) {
-        if (tid == 0 && g + 1 < ntiles && !s_fail && !mma_tile(g + 1)) s_fail = 1;
-        __syncthreads();
-        if (s_fail) break;
-        const bool done = mbar_wait(&bar_mma[g & 1], (uint32_t)((g >> 1) & 1));
-        if (__syncthreads_or(!done)) {
-            if (tid == 0) s_fail = 1;
-            break;
+
+    if (warp == 8) {
+        if (lane == 0) {
+            // copies: tile g into stage g % nst once the MMAs of tile g - nst are done
+            const unsigned char* gops = reinterpret_cast<const unsigned char*>(ops);
+            const size_t tile_stride = (size_t)3 * part_bytes;
+            for (int g = 0; g < nt; ++g) {
+                const int s = g % nst;
+                if (g >= nst && !mbar_wait_or(&bar_empty[s], (uint32_t)(((g / nst) - 1) & 1), vfail)) {
+                    s_fail = 1;
+                    break;
+                }
+                mbar_arrive_expect(&bar_full[s], stage_bytes);
+                bulk_g2s(sB + (size_t)s * stage_bytes, gops + (size_t)(t_begin + g) * tile_stride, stage_bytes,
+                         &bar_full[s]);
+                issued = g + 1;
+            }
         }
-        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-        if (tid == 0 && g + kFStages < ntiles) copy_tile(g + kFStages);   // step g's buffer is free
-        {
-            const int col0 = half * 32;                      // columns of this thread within the tile
+        __syncwarp();
+    } else if (warp == 9) {
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_bf16(kTCM, kFN);
+            const uint32_t a_addr = smem_u32(sA);
+            const int kbp = d / 16;                  // K blocks of 16 per part
+            for (int g = 0; g < nt; ++g) {
+                const int s = g % nst, a = g % kFAcc;
+                if (g >= kFAcc && !mbar_wait_or(&bar_ae[a], (uint32_t)(((g / kFAcc) - 1) & 1), vfail)) {
+                    s_fail = 1;
+                    break;
+                }
+                if (!mbar_wait_or(&bar_full[s], (uint32_t)((g / nst) & 1), vfail)) {
+                    s_fail = 1;
+                    break;
+                }
+                asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+                const uint32_t b_addr = smem_u32(sB + (size_t)s * stage_bytes);
+                const uint32_t dacc = tmem + (uint32_t)(a * kFN);
+                for (int p = 0; p < nparts; ++p) {
+                    const int ap = p == 2 ? 1 : 0;      // parts 0 and 1 read q_hi, part 2 reads q_lo
+                    for (int kb = 0; kb < kbp; ++kb) {
+                        const uint64_t ad = umma_smem_desc(a_addr + (uint32_t)(ap * kbp + kb) * (kTCM * 32));
+                        const uint64_t bd = umma_smem_desc(b_addr + (uint32_t)(p * kbp + kb) * (kFN * 32));
+                        const uint32_t acc = (p | kb) ? 1u : 0u;
+                        asm volatile(
+                            "{\n .reg .pred pa;\n setp.ne.b32 pa, %4, 0;\n"
+                            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, pa;\n}" ::"r"(dacc),
+                            "l"(ad), "l"(bd), "r"(idesc), "r"(acc)
+                            : "memory");
+                    }
+                }
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_u32(&bar_empty[s]))
+                             : "memory");
+                asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                                 smem_u32(&bar_af[a]))
+                             : "memory");
+                mma_issued = g + 1;
+            }
+        }
+        __syncwarp();
+    } else {
+        // candidate test on (c_n - 2 q.c) against lim - |q|^2, widened by a slack
+        // that covers the rounding of the shifted comparison (far below eps)
+        const float slack = ldexpf(qn + *cn_max, -19);
+        float lq = INF;                    // lmax + 2 eps - |q|^2 + slack
+        constexpr int kW = kFW;
+        for (int g = 0; g < nt; ++g) {
+            const int a = g % kFAcc;
+            const bool got = mbar_wait_or(&bar_af[a], (uint32_t)((g / kFAcc) & 1), vfail);
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) s_fail = 1;
+                break;
+            }
+            asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
             uint32_t r[32];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
@@ -697,18 +790,18 @@ __global__ void __launch_bounds__(kFT, 1)
                   "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
                   "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
                   "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-                : "r"(tmem + (uint32_t)((g & 1) * kFN + col0) + ((uint32_t)(quarter * 32) << 16))
+                : "r"(tmem + (uint32_t)(a * kFN + half * 32) + ((uint32_t)(quarter * 32) << 16))
                 : "memory");
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-            const int cb = g * kFN + col0;
-            const float cnl = __ldg(cne + cb + lane);       // lane j: squared norm of column cb + j
-            // the 32 columns in pieces of kW; before each piece the list must have room
-            // for all of it, else it is pruned to the current bound, and a bound that
-            // no longer thins it (more than kFList - kW survivors) gives up on the row
-            constexpr int kW = LMAX <= 8 ? 32 : (LMAX <= 16 ? 16 : 8);
+            asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_ae[a]);          // the accumulator may be refilled
+            const int rel0 = g * kFN + half * 32;            // column of r[0], relative to c_begin
+            const float4* cn4 = reinterpret_cast<const float4*>(cne + c_begin + rel0);
 #pragma unroll
             for (int j0 = 0; j0 < 32; j0 += kW) {
-                if (!over && nc > kFList - kW) {
+                if (!over && nc > LIST - kW) {
+                    const float lim = lmax + eps2;
                     int k2 = 0;
                     for (int i = 0; i < nc; ++i) {
                         const float v = myval[i * kFT];
@@ -719,87 +812,111 @@ __global__ void __launch_bounds__(kFT, 1)
                         }
                     }
                     nc = k2;
-                    if (nc > kFList - kW) {
-                        over = true;
-                        nc = 0;
+                    if (nc > LIST - kW) over = true;
+                }
+                const int nc0 = nc;
+#pragma unroll
+                for (int j = j0; j < j0 + kW; j += 4) {
+                    const float4 c4 = __ldg(cn4 + j / 4);
+                    const float2 m2 = make_float2(-2.f, -2.f);
+                    const float2 x01 = __ffma2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), m2,
+                                                  make_float2(c4.x, c4.y));
+                    const float2 x23 = __ffma2_rn(make_float2(__uint_as_float(r[j + 2]), __uint_as_float(r[j + 3])),
+                                                  m2, make_float2(c4.z, c4.w));
+                    const bool p0 = x01.x <= lq, p1 = x01.y <= lq, p2 = x23.x <= lq, p3 = x23.y <= lq;
+                    if (__any_sync(0xffffffffu, p0 | p1 | p2 | p3) && !over) {
+                        if (p0) {
+                            myval[nc * kFT] = fmaxf(x01.x + qn, 0.f);
+                            mycol[nc * kFT] = (uint16_t)(rel0 + j);
+                            ++nc;
+                        }
+                        if (p1) {
+                            myval[nc * kFT] = fmaxf(x01.y + qn, 0.f);
+                            mycol[nc * kFT] = (uint16_t)(rel0 + j + 1);
+                            ++nc;
+                        }
+                        if (p2) {
+                            myval[nc * kFT] = fmaxf(x23.x + qn, 0.f);
+                            mycol[nc * kFT] = (uint16_t)(rel0 + j + 2);
+                            ++nc;
+                        }
+                        if (p3) {
+                            myval[nc * kFT] = fmaxf(x23.y + qn, 0.f);
+                            mycol[nc * kFT] = (uint16_t)(rel0 + j + 3);
+                            ++nc;
+                        }
                     }
                 }
-                // every column is written at slot nc, which advances only when the
-                // column is within the bound (an abandoned row keeps rewriting slot 0)
-                const int nc0 = nc, adv = over ? 0 : 1;
-#pragma unroll
-                for (int j = j0; j < j0 + kW; ++j) {
-                    const float xv =
-                        fmaxf(qn + __shfl_sync(0xffffffffu, cnl, j) - 2.f * __uint_as_float(r[j]), 0.f);
-                    myval[nc * kFT] = xv;
-                    mycol[nc * kFT] = (uint16_t)(cb + j);
-                    nc += xv <= lim ? adv : 0;
-                }
-                // the L smallest: only this thread's new entries, so a warp pays for
-                // its busiest lane rather than for every column some lane kept
+                // the L smallest: only this thread's new entries
                 for (int i = nc0; i < nc; ++i) {
                     float v = myval[i * kFT];
                     if (v < lmax) {
 #pragma unroll
                         for (int e = 0; e < LMAX; ++e) {
-                            const float a = lv[e];
-                            lv[e] = fminf(a, v);
-                            v = fmaxf(a, v);
+                            const float a2 = lv[e];
+                            lv[e] = fminf(a2, v);
+                            v = fmaxf(a2, v);
                         }
-#pragma unroll
-                        for (int e = 0; e < LMAX; ++e)
-                            if (e == L - 1) lmax = lv[e];
+                        lmax = lv[LMAX - 1];
                     }
                 }
-                lim = lmax + eps2;
+                lq = lmax + eps2 - qn + slack;
             }
         }
-        asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-        __syncthreads();                      // accumulator g & 1 read before step g + 2's MMAs reuse it
     }
+    __syncthreads();
     const bool failed = s_fail != 0;
-    if (failed && tid == 0) {
-        atomicOr(flag, 4);
-        for (int b = 0; b < 2; ++b) mbar_wait(&bar_mma[b], 0);
-        for (int b = 0; b < kFStages; ++b) mbar_wait(&bar_b[b], 0);
+    if (failed) {
+        // a wait gave up: report it, give copies and MMAs in flight a last
+        // bounded chance to land, then release the tensor memory
+        if (tid == 8 * 32) {
+            atomicOr(flag, 4);
+            for (int g = issued - nst < 0 ? 0 : issued - nst; g < issued; ++g)
+                mbar_wait(&bar_full[g % nst], (uint32_t)((g / nst) & 1));
+        }
+        if (tid == 9 * 32 && mma_issued > 0) {
+            const int g = mma_issued - 1;
+            mbar_wait(&bar_af[g % kFAcc], (uint32_t)((g / kFAcc) & 1));
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kFN)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kFAcc * kFN)
                      : "memory");
     // T~ of the row: the L-th smallest of the two halves' ascending L smallest
     // A (this thread's lv, half 0) and B (half 1's, through s_lv, entry-major
     // [i][row]: the lanes of a warp read 32 different banks), as
-    // min over i = 0..L of max(A[i-1], B[L-1-i]) with A[-1] = B[-1] = -inf
-    if (half == 1) {
+    // min over i = 0..L of max(A[i-1], B[L-1-i]) with A[-1] = B[-1] = -inf;
+    // in the arrays A[i] is slot LMAX - L + i (slot ip = LMAX - L + i - 1 below)
+    if (epi && half == 1) {
 #pragma unroll
         for (int i = 0; i < LMAX; ++i) s_lv[i * kTCM + row] = lv[i];
     }
     __syncthreads();
-    if (half == 0) {
+    if (epi && half == 0) {
         float T = INF;
 #pragma unroll
-        for (int i = 0; i <= LMAX; ++i) {
-            const float a = i == 0 ? -INF : lv[i == 0 ? 0 : i - 1];
-            const int jb = L - 1 - i;
-            const float b = jb < 0 ? -INF : s_lv[jb * kTCM + row];
-            if (i <= L) T = fminf(T, fmaxf(a, b));
+        for (int ip = -1; ip < LMAX; ++ip) {
+            if (ip < LMAX - L - 1) continue;
+            const float a = ip < 0 ? -INF : lv[ip < 0 ? 0 : ip];
+            const int jb = 2 * LMAX - L - 2 - ip;
+            const float b = jb < LMAX - L ? -INF : s_lv[jb * kTCM + row];
+            T = fminf(T, fmaxf(a, b));
         }
         s_T[row] = T;
     }
     __syncthreads();
-    // this thread's candidates: list entries within T~ + 2 eps1, rescored exactly
-    const float T = s_T[row];
+    // this thread's candidates: list entries within T~ + 2 eps, rescored exactly
+    const float T = epi ? s_T[row] : INF;
     const float climit = T + eps2;
     const int qi = q0 + row;
     int nk = 0;
-    bool big = over || T == INF;
-    if (qi < nq && !failed && !big) {
-        // the candidates' columns to the front of this thread's list
+    bool big = !epi || over || T == INF;
+    if (epi && qi < nq && !failed && !big) {
         for (int i = 0; i < nc; ++i) {
             if (myval[i * kFT] > climit) continue;
-            if (nk == kFList / 2) {
+            if (nk == LIST / 2) {
                 big = true;
                 break;
             }
@@ -812,15 +929,15 @@ __global__ void __launch_bounds__(kFT, 1)
     // exact sums, their loads in flight together); the key lands in the
     // owner's entry-major slot of s_key, [slot][owner]
     {
-        const int mine = (qi < nq && !failed && !big) ? nk : 0;
+        const int mine = (epi && qi < nq && !failed && !big) ? nk : 0;
         int total;
-        const int off = block_excl_scan<kFT>(mine, s_scan, &total);
+        const int off = block_excl_scan<kFBlock>(mine, s_scan, &total);
         for (int i = 0; i < mine; ++i) s_pair[off + i] = (uint16_t)((i << 8) | tid);
         __syncthreads();
-        for (int p = tid; p < total; p += 2 * kFT) {
-            const int e0 = s_pair[p], e1 = p + kFT < total ? s_pair[p + kFT] : e0;
+        for (int p = tid; p < total; p += 2 * kFBlock) {
+            const int e0 = s_pair[p], e1 = p + kFBlock < total ? s_pair[p + kFBlock] : e0;
             const int t0 = e0 & 255, i0 = e0 >> 8, t1 = e1 & 255, i1 = e1 >> 8;
-            const int c0 = s_lcol[i0 * kFT + t0], c1 = s_lcol[i1 * kFT + t1];
+            const int c0 = c_begin + s_lcol[i0 * kFT + t0], c1 = c_begin + s_lcol[i1 * kFT + t1];
             const float4* qa = reinterpret_cast<const float4*>(q + (size_t)(q0 + (t0 & (kTCM - 1))) * d);
             const float4* qb = reinterpret_cast<const float4*>(q + (size_t)(q0 + (t1 & (kTCM - 1))) * d);
             const float4* r0 = reinterpret_cast<const float4*>(cent + (size_t)c0 * d);
@@ -846,32 +963,61 @@ __global__ void __launch_bounds__(kFT, 1)
                 s1 = __fadd_rn(s1, __fmul_rn(y, y));
             }
             s_key[i0 * kFT + t0] = make_key(__float_as_uint(s0), id_map ? (uint32_t)id_map[c0] : (uint32_t)c0);
-            if (p + kFT < total)
+            if (p + kFBlock < total)
                 s_key[i1 * kFT + t1] = make_key(__float_as_uint(s1), id_map ? (uint32_t)id_map[c1] : (uint32_t)c1);
         }
     }
     s_nc[tid] = big ? -1 : nk;
     __syncthreads();
-    if (half == 0 && qi < nq) {
+    if (epi && half == 0 && qi < nq) {
         const int na = s_nc[tid], nb = s_nc[tid + kTCM];
         const bool fall = failed || na < 0 || nb < 0;
-        row_fallback[qi] = fall ? 1 : 0;
-        if (!fall) {
-            // top-L of the row's candidate keys: repeated minimum over the two lists
-            const uint64_t* ka = s_key + tid;
-            const uint64_t* kb = s_key + tid + kTCM;
-            uint64_t last = 0;
-            for (int o = 0; o < L; ++o) {
-                uint64_t best = kKeyNone;
+        if (fall) row_fallback[qi] = 1;
+        // top-L of the row's candidate keys: repeated minimum over the two lists
+        const uint64_t* ka = s_key + tid;
+        const uint64_t* kb = s_key + tid + kTCM;
+        uint64_t last = 0;
+        for (int o = 0; o < L; ++o) {
+            uint64_t best = kKeyNone;
+            if (!fall) {
                 for (int i = 0; i < na; ++i)
                     if ((o == 0 || ka[i * kFT] > last) && ka[i * kFT] < best) best = ka[i * kFT];
                 for (int i = 0; i < nb; ++i)
                     if ((o == 0 || kb[i * kFT] > last) && kb[i * kFT] < best) best = kb[i * kFT];
+            }
+            if (split_keys) {
+                split_keys[((size_t)blockIdx.y * nq + qi) * L + o] = best;
+            } else if (!fall) {
                 const bool ok = best != kKeyNone;
                 if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(best) : -1;
                 if (out_keys) out_keys[(size_t)qi * L + o] = best;
-                last = best;
             }
+            last = best;
+        }
+    }
+}
+
+// Top-L per query of the column splits' sorted top-L keys [S][nq][L]: one
+// warp per query, lane s walks split s's list, L rounds of the warp minimum.
+__global__ void __launch_bounds__(256) route_split_merge_kernel(const uint64_t* __restrict__ keys, int S, int nq,
+                                                                int L, int32_t* out_ids, uint64_t* out_keys) {
+    const int qi = (int)((blockIdx.x * (size_t)blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (qi >= nq) return;                  // whole warps only
+    const uint64_t* mine = keys + ((size_t)lane * nq + qi) * L;
+    int pos = 0;
+    for (int o = 0; o < L; ++o) {
+        const uint64_t h = (lane < S && pos < L) ? mine[pos] : kKeyNone;
+        uint64_t m = h;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+            const uint64_t t = __shfl_xor_sync(0xffffffffu, m, off);
+            m = t < m ? t : m;
+        }
+        if (h == m && m != kKeyNone) ++pos;   // keys are distinct: one lane advances
+        if (lane == 0) {
+            const bool ok = m != kKeyNone && key_hi(m) != 0xFFFFFFFFu;
+            if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(m) : -1;
+            if (out_keys) out_keys[(size_t)qi * L + o] = m;
         }
     }
 }
@@ -966,31 +1112,81 @@ cudaError_t route_tc(const float* q, int nq, const uint16_t* ops, const float* c
     return cudaGetLastError();
 }
 
+namespace {
+int fused_lmax(int L) { return L <= 8 ? 8 : (L <= 16 ? 16 : 32); }
+}  // namespace
+
 bool route_tc_fused_usable(int d, int nlist, int L) {
-    return route_tc_usable(d, nlist) && nlist <= 65536 && L >= 1 && L <= kFLMax && d <= kPMaxRouteD &&
-           route_fused_smem(d) <= 227 * 1024;
+    if (!route_tc_usable(d, nlist) || L < 1 || L > kFLMax || d > kPMaxRouteD) return false;
+    const int list = fused_list(fused_lmax(L));
+    if (route_fused_fixed(d, list) + 1024 >= kFSmemCap) return false;
+    if (route_fused_region(d, list) < route_fused_region_min(d, list)) return false;
+    // at most kFMaxSplits column splits of at most 65536 columns (16-bit list entries)
+    const int ntiles = (nlist + kFN - 1) / kFN;
+    return (ntiles + kFMaxSplits - 1) / kFMaxSplits <= 65536 / kFN;
+}
+
+int route_tc_fused_splits(int nq, int nlist) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int ntiles = (nlist + kFN - 1) / kFN, qb = (nq + kTCM - 1) / kTCM;
+    int best = 1;
+    double best_cost = 1e300;
+    // one CTA per SM (shared memory); a CTA costs its tiles plus about 6 tiles
+    // of fixed work (operand build, rescoring), a split launch one merge
+    for (int S = 1; S <= kFMaxSplits && S <= ntiles; ++S) {
+        const int per = (ntiles + S - 1) / S;
+        if (per * kFN > 65536) continue;
+        const int Sr = (ntiles + per - 1) / per;
+        const long long waves = ((long long)qb * Sr + sms - 1) / sms;
+        const double cost = (double)waves * (per + 6) + (Sr > 1 ? 2.0 : 0.0);
+        if (cost < best_cost) {
+            best_cost = cost;
+            best = Sr;
+        }
+    }
+    return best;
 }
 
 cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const float* cne, const float* cn_max,
                            const uint8_t* valid, int nlist, int d, const float* cent, int L, const int32_t* id_map,
-                           int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, int* flag, cudaStream_t st) {
+                           int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, uint64_t* split_keys,
+                           int splits, int* flag, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     if (!route_tc_fused_usable(d, nlist, L)) return cudaErrorInvalidValue;
-    const size_t smem = route_fused_smem(d);
-    cudaError_t e = cudaSuccess;
+    const int ntiles = (nlist + kFN - 1) / kFN;
+    if (splits < 1) splits = 1;
+    const int per = (ntiles + splits - 1) / splits;
+    const int S = (ntiles + per - 1) / per;
+    if (S > kFMaxSplits || per * kFN > 65536 || (S > 1 && !split_keys)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaMemsetAsync(row_fallback, 0, sizeof(int32_t) * (size_t)nq, st);
+    if (e) return e;
+    const int lmax = fused_lmax(L), list = fused_list(lmax);
+    const size_t region = route_fused_region(d, list);
+    const size_t smem = route_fused_fixed(d, list) + region;
+    const dim3 grid((unsigned)((nq + kTCM - 1) / kTCM), (unsigned)S);
+    uint64_t* sk = S > 1 ? split_keys : nullptr;
     note_launch();
-    const int grid = (nq + kTCM - 1) / kTCM;
 #define ISB_FUSED(LM)                                                                                            \
     {                                                                                                            \
-        e = cudaFuncSetAttribute(route_tc_fused_kernel<LM>, cudaFuncAttributeMaxDynamicSharedMemorySize,         \
+        constexpr int LI = fused_list(LM);                                                                       \
+        e = cudaFuncSetAttribute(route_tc_fused_kernel<LM, LI>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
                                  (int)smem);                                                                     \
         if (e) return e;                                                                                         \
-        route_tc_fused_kernel<LM><<<grid, kFT, smem, st>>>(q, nq, d, ops, cne, cn_max, valid, nlist, cent, L,    \
-                                                            id_map, out_ids, out_keys, row_fallback, flag);      \
+        route_tc_fused_kernel<LM, LI><<<grid, kFBlock, smem, st>>>(q, nq, d, ops, cne, cn_max, valid, nlist,     \
+                                                                    cent, L, id_map, per, (int)region, out_ids,  \
+                                                                    out_keys, sk, row_fallback, flag);           \
     }
-    if (L <= 8) ISB_FUSED(8) else if (L <= 16) ISB_FUSED(16) else ISB_FUSED(32)
+    if (lmax == 8) ISB_FUSED(8) else if (lmax == 16) ISB_FUSED(16) else ISB_FUSED(32)
 #undef ISB_FUSED
     if ((e = cudaGetLastError())) return e;
+    if (S > 1) {
+        note_launch();
+        route_split_merge_kernel<<<(unsigned)(((size_t)nq * 32 + 255) / 256), 256, 0, st>>>(sk, S, nq, L, out_ids,
+                                                                                              out_keys);
+        if ((e = cudaGetLastError())) return e;
+    }
     note_launch();
     route_exact_rows_kernel<<<nq, kRsT, 0, st>>>(row_fallback, q, cent, valid, nlist, d, L, id_map, out_ids,
                                                  out_keys);

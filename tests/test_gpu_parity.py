@@ -233,13 +233,14 @@ def test_route_matches_oracle(cuda_ok, pq_medium):
     assert np.array_equal((k >> np.uint64(32)).astype(np.uint32), exp_d.view(np.uint32))
 
 
-@pytest.mark.parametrize("mode,nprobe", [("0", 8), ("1", 8), ("2", 8), ("2", 12), ("2", 32), ("2", 40)])
+@pytest.mark.parametrize("mode,nprobe", [("0", 8), ("1", 8), ("1", 16), ("2", 12), ("2", 32), ("3", 8),
+                                         ("3", 40)])
 def test_route_kernels_bit_identical(cuda_ok, mode, nprobe, monkeypatch):
     """every routing kernel (exact CUDA-core, fused tensor-core, tensor-core
     matrix + rescoring) gives the oracle's lists and distance bits; d = 96
-    and d = 128 shapes (the fused kernel covers d = 96 only)"""
+    and d = 128 shapes, one with enough lists to split the fused sweep"""
     monkeypatch.setenv("INSITU_ROUTE_TC", mode)
-    for d, nlist, seed in ((96, 300, 71), (128, 200, 72)):
+    for d, nlist, seed in ((96, 300, 71), (128, 200, 72), (128, 3000, 73)):
         cent = synth.mixture_f32_unit(nlist, d, 40, 0.05, seed=seed).numpy()
         cent[7] = cent[3]                      # identical centroids: a distance tie broken by id
         cent[11] = 0.0                         # zero norm: never routed
@@ -550,3 +551,46 @@ def test_errors_are_reported_not_fatal(cuda_ok, pq_medium):
     assert (ids >= 0).all()
     b.close()
     index.close()
+
+
+def _route_keys(cent, q, nprobe):
+    nlist, d = cent.shape
+    counts = np.full(nlist, 1, np.int32)
+    offsets = np.arange(nlist, dtype=np.int64)
+    rows = np.zeros((nlist, d), np.uint8)
+    index = ib.Index().load_u8(rows, offsets, counts, np.arange(nlist, dtype=np.int32), cent)
+    b = ib.Batch(q.shape[0], d, nprobe, 10, nlist)
+    b.stage1_prepare(q)
+    keys = torch.empty((q.shape[0], nprobe), dtype=torch.int64, device="cuda")
+    b.route_keys(index, q.shape[0], nprobe, keys.data_ptr())
+    b.sync()
+    b.route(index, q.shape[0], nprobe)
+    probes = b.get_probes(q.shape[0], nprobe)
+    k = keys.cpu().numpy().view(np.uint64)
+    b.close()
+    index.close()
+    return k, probes
+
+
+@pytest.mark.parametrize("nlist", [65536, 262144])
+def test_route_fused_large_nlist_d128(cuda_ok, nlist):
+    """the fused tensor-core routing at the c2 / c3 shapes (d = 128, 65536 and
+    262144 lists, the sweep split over many CTAs per query block and merged):
+    probe lists and distance bits equal the oracle's exact routing, for
+    integer-valued queries (bf16 holds them exactly: two operand parts) and
+    for fractional ones (three parts)"""
+    g = np.random.default_rng(nlist)
+    d = 128
+    cent = (32.0 + 192.0 * g.random((nlist, d))).astype(np.float32)
+    cent[5] = cent[9]                      # a distance tie broken by list id
+    cent[17] = 0.0                         # zero norm: never routed
+    comp = g.integers(0, nlist, 300)
+    q_int = np.clip(np.round(cent[comp] + 10.0 * g.standard_normal((300, d))), 0, 255).astype(np.float32)
+    q_frac = (cent[comp] + 10.0 * g.standard_normal((300, d))).astype(np.float32)
+    for q in (q_int, q_frac):
+        for nprobe in (8, 16):
+            exp, exp_d = oracle.route_l2_par(q, cent, nprobe)
+            k, probes = _route_keys(cent, q, nprobe)
+            assert np.array_equal(probes, exp)
+            assert np.array_equal((k & np.uint64(0xFFFFFFFF)).astype(np.int32), exp)
+            assert np.array_equal((k >> np.uint64(32)).astype(np.uint32), exp_d.view(np.uint32))
