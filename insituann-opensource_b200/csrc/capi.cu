@@ -143,11 +143,11 @@ struct BatchCtx {
     float* out_dist = nullptr;
     int32_t* out_idist = nullptr;
     int* counter = nullptr;
-    int* overflow = nullptr;      // device flag
+    int* overflow = nullptr;      // device flags: [0] candidate overflow, [1] routing wait gave up
     int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
     int res_nq = 0, res_k = 0;
     int probes_nq = 0, probes_np = 0;
-    Grow route_dist, route_rowfb, route_split, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
+    Grow route_dist, route_rowfb, route_split, route_bound, wl_cnt, wl_off, wl_cursor, pair_q, pair_l, scan_tmp, grp_cnt, grp_off, groups;
     Grow cand_m, cand_d, cnt_m, cnt_d, thr_m, thr_d, s1m, s1d, exk;
     std::vector<void*> owned;
     std::string err;
@@ -346,19 +346,24 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     const int L = std::min(nprobe, 2048);
     require(L == nprobe, "n_probes > 2048 is not supported");
     StageScope stage(b, IVF_STAGE_ROUTE);
+    // the routing kernels report a bounded wait that gave up in flag word 1,
+    // which the fine-search stages do not reset
+    int* rflag = b->overflow + 1;
+    ck(cudaMemsetAsync(rflag, 0, sizeof(int), b->st), "memset");
     const int mode = x->tc_ops ? route_tc_mode() : 0;
     if ((mode == 1 || mode == 2) && route_tc_fused_usable(x->d, x->nlist, nprobe)) {
         // one tcgen05 sweep, no distance matrix; the per-split keys bound the sub-batch
         const int splits = route_tc_fused_splits(nq, x->nlist);
-        const size_t per_q = (size_t)splits * nprobe * sizeof(uint64_t) + sizeof(int32_t);
+        const size_t per_q = (size_t)splits * nprobe * sizeof(uint64_t) + 2 * sizeof(int32_t);
         const int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
         int32_t* fb = ensure<int32_t>(b, b->route_rowfb, (size_t)nsub);
+        uint32_t* rbnd = ensure<uint32_t>(b, b->route_bound, (size_t)nsub);
         uint64_t* sk = splits > 1 ? ensure<uint64_t>(b, b->route_split, (size_t)nsub * splits * nprobe) : nullptr;
         for (int s = 0; s < nq; s += nsub) {
             const int n = std::min(nsub, nq - s);
             ck(route_tc_fused(b->q + (size_t)s * x->d, n, x->tc_ops, x->tc_cne, x->tc_cnmax, x->valid, x->nlist,
                               x->d, x->cent, nprobe, x->l2g, keys ? nullptr : b->probes + (size_t)s * nprobe,
-                              keys ? keys + (size_t)s * nprobe : nullptr, fb, sk, splits, b->overflow, b->st),
+                              keys ? keys + (size_t)s * nprobe : nullptr, fb, sk, rbnd, splits, rflag, b->st),
                "route_tc_fused");
         }
     } else {
@@ -370,7 +375,7 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
             int n = std::min(nsub, nq - s);
             const float* qs = b->q + (size_t)s * x->d;
             if (tc) {
-                ck(route_tc(qs, n, x->tc_ops, x->tc_cn, x->valid, x->nlist, x->d, dist, b->overflow, b->st),
+                ck(route_tc(qs, n, x->tc_ops, x->tc_cn, x->valid, x->nlist, x->d, dist, rflag, b->st),
                    "route_tc");
                 ck(route_rescore(dist, qs, n, x->cent, x->tc_cnmax, x->valid, x->nlist, x->d, nprobe, x->l2g,
                                  keys ? nullptr : b->probes + (size_t)s * nprobe, nullptr,
@@ -390,6 +395,7 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
             }
         }
     }
+    ck(cudaMemcpyAsync(b->h_overflow + 1, rflag, sizeof(int), cudaMemcpyDeviceToHost, b->st), "flag D2H");
     if (!keys) {
         b->probes_nq = nq;
         b->probes_np = nprobe;
@@ -607,7 +613,8 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
 }
 
 void check_overflow_after_sync(BatchCtx* b) {
-    if (*b->h_overflow & 4) fail(IVF_ECUDA, "a bounded device wait of the tensor-core routing gave up");
+    if ((b->h_overflow[0] | b->h_overflow[1]) & 4)
+        fail(IVF_ECUDA, "a bounded device wait of the tensor-core routing gave up");
     if (*b->h_overflow)
         fail(IVF_EOVERFLOW, "a candidate buffer overflowed; raise INSITU_SCRATCH_MB or lower n_probes");
 }
@@ -797,7 +804,7 @@ void* ivf_create_batch_context(int max_n_query, int n_dim, int max_n_probes, int
             b->counter = dalloc<int>(4, b->owned);
             b->overflow = dalloc<int>(4, b->owned);
             ck(cudaMallocHost(&b->h_overflow, sizeof(int) * 4), "cudaMallocHost");
-            *b->h_overflow = 0;
+            b->h_overflow[0] = b->h_overflow[1] = 0;
         } catch (...) {
             if (b->st) cudaStreamDestroy(b->st);
             free_all(b->owned);
@@ -1196,6 +1203,7 @@ int ivf_get_probes(void* batch_ctx, int* h_probes, int n_query, int n_probes) {
                            cudaMemcpyDeviceToHost, b->st),
            "probes D2H");
         ck(cudaStreamSynchronize(b->st), "cudaStreamSynchronize");
+        if (b->h_overflow[1] & 4) fail(IVF_ECUDA, "a bounded device wait of the tensor-core routing gave up");
     });
 }
 

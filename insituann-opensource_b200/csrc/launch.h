@@ -71,14 +71,15 @@ cudaError_t route_tc(const float* q, int nq, const uint16_t* ops, const float* c
 // candidates and exact rescoring on chip; the centroids split over `splits`
 // CTAs per 128 queries, whose sorted top-L keys [splits][nq][L] go to
 // split_keys and are merged), plus an exact pass over the rare rows it hands
-// back.  row_fallback: [nq] scratch.
+// back.  row_fallback, row_bound: [nq] scratch (row_bound may be null: then the
+// CTAs of a query do not share their running bounds).
 bool route_tc_fused_usable(int d, int nlist, int L);
 // column splits that balance nq queries x nlist centroids over the device's SMs
 int route_tc_fused_splits(int nq, int nlist);
 cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const float* cne, const float* cn_max,
                            const uint8_t* valid, int nlist, int d, const float* cent, int L, const int32_t* id_map,
                            int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, uint64_t* split_keys,
-                           int splits, int* flag, cudaStream_t st);
+                           uint32_t* row_bound, int splits, int* flag, cudaStream_t st);
 cudaError_t route_rescore(const uint32_t* approx, const float* q, int nq, const float* cent, const float* cn_max,
                           const uint8_t* valid, int nlist, int d, int L, const int32_t* id_map, int32_t* out_ids,
                           float* out_dist, uint64_t* out_keys, cudaStream_t st);

@@ -559,15 +559,13 @@ __host__ __device__ constexpr size_t route_fused_fixed(int d, int list) {
            sizeof(float) * 2 * kTCM + sizeof(int) * kFBlock;
 }
 // the stage region must hold two full (3-part) tiles, and after the sweep the
-// halves' L-lists and the rescored keys
+// halves' L-lists and the rescoring's pair list
 __host__ __device__ constexpr size_t route_fused_region_min(int d, int list) {
     const size_t tiles = 2 * (size_t)kFN * 3 * d * 2;
-    const size_t keys = (sizeof(uint64_t) + sizeof(uint16_t)) * kFT * (list / 2),
-                 lists = sizeof(float) * kTCM * kFLMax;
-    const size_t m = keys > lists ? keys : lists;
-    return tiles > m ? tiles : m;
+    const size_t after = sizeof(float) * kTCM * kFLMax + sizeof(uint16_t) * kFT * (size_t)list;
+    return tiles > after ? tiles : after;
 }
-constexpr size_t kFSmemCap = 227 * 1024 - 1536;  // dynamic shared memory of one CTA (1 KB static barriers aside)
+constexpr size_t kFSmemCap = 227 * 1024 - 2560;  // dynamic shared memory of one CTA (2 KB static aside)
 
 __host__ __device__ constexpr size_t route_fused_region(int d, int list) {
     return ((kFSmemCap - route_fused_fixed(d, list)) / 128) * 128;
@@ -592,7 +590,8 @@ __global__ void __launch_bounds__(kFBlock, 1)
                           const float* __restrict__ cne, const float* __restrict__ cn_max,
                           const uint8_t* __restrict__ valid, int nlist, const float* __restrict__ cent, int L,
                           const int32_t* __restrict__ id_map, int tiles_per_cta, int region, int32_t* out_ids,
-                          uint64_t* out_keys, uint64_t* split_keys, int32_t* __restrict__ row_fallback, int* flag) {
+                          uint64_t* out_keys, uint64_t* split_keys, uint32_t* row_bound,
+                          int32_t* __restrict__ row_fallback, int* flag) {
     extern __shared__ __align__(1024) unsigned char sm[];
     __shared__ __align__(8) uint64_t bar_full[kFMaxStages];
     __shared__ __align__(8) uint64_t bar_empty[kFMaxStages];
@@ -601,6 +600,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail;
     __shared__ int s_scan[33];
+    __shared__ float s_halfb[2][kTCM];     // each half's running (L/2)-th smallest D~ (L == LMAX)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool epi = warp < 8;
     const int quarter = warp & 3, half = (warp >> 2) & 1;
@@ -616,8 +616,6 @@ __global__ void __launch_bounds__(kFBlock, 1)
     int* s_nc = reinterpret_cast<int*>(s_T + kTCM);                               // [kFBlock]
     // after the sweep the stage region holds the halves' L-lists, then the rescored keys
     float* s_lv = reinterpret_cast<float*>(sB);                                   // [LMAX][128] (half 1)
-    uint64_t* s_key = reinterpret_cast<uint64_t*>(sB);                            // [LIST / 2][kFT]
-    uint16_t* s_pair = reinterpret_cast<uint16_t*>(s_key + kFT * (LIST / 2));     // [kFT * LIST / 2]
     const int q0 = blockIdx.x * kTCM;
     const int ntiles_all = (nlist + kFN - 1) / kFN;
     const int t_begin = blockIdx.y * tiles_per_cta;
@@ -643,6 +641,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
     }
+    if (tid < 2 * kTCM) s_halfb[tid >> 7][tid & (kTCM - 1)] = INF;
     // A operand [q_hi | q_lo]: epilogue thread t builds row t % 128, the 8-element
     // groups g of its half (two 16-byte loads per group)
     int has_lo = 0;
@@ -700,10 +699,19 @@ __global__ void __launch_bounds__(kFBlock, 1)
 #pragma unroll
     for (int i = 0; i < LMAX; ++i) lv[i] = i < LMAX - L ? -INF : INF;
     float lmax = INF;
+    float ub = INF;                        // the row's shared bound as last read
     int nc = 0;                            // entries in this thread's list
     bool over = false;                     // the list overflowed within the bound
     const float qn = epi ? s_qn[row] : 0.f;
-    const float eps2 = 2.f * ldexpf(qn + *cn_max, -11);
+    // |D~ - D| <= eps = 2^-13 (|q|^2 + max |c|^2): the split leaves q.c with an
+    // error below 2^-17 sum |q_j c_j| (each bf16 rounding is within 2^-9, so
+    // c - c_hi - c_lo is within 2^-18 |c| and q_lo c_lo within 2^-18 |q| |c|),
+    // the tensor cores' fp32 accumulation of at most 3d <= 384 exact bf16
+    // products adds at most 2 * 384 * 2^-24 sum |q_j c_j| (allowing truncating
+    // adds), the fp32 norms 2^-17 of each, the final fma and add 2^-22 of the
+    // total: with 2 |q| |c| <= |q|^2 + |c|^2, about 2^-14.9 (|q|^2 + |c|^2),
+    // a quarter of eps
+    const float eps2 = 2.f * ldexpf(qn + *cn_max, -13);
     float* myval = s_lval + tid;           // entry i at [i][tid]: a warp's stores hit 32 banks
     uint16_t* mycol = s_lcol + tid;
 
@@ -770,8 +778,18 @@ __global__ void __launch_bounds__(kFBlock, 1)
         // candidate test on (c_n - 2 q.c) against lim - |q|^2, widened by a slack
         // that covers the rounding of the shifted comparison (far below eps)
         const float slack = ldexpf(qn + *cn_max, -19);
-        float lq = INF;                    // lmax + 2 eps - |q|^2 + slack
+        float lq = INF;                    // min(lmax, ub) + 2 eps - |q|^2 + slack
         constexpr int kW = kFW;
+        // the row's bound shared by all CTAs (and both halves) of this query: the
+        // smallest running L-th D~ any of them has published; any such value is
+        // >= the row's final L-th smallest D~, so it is a valid filter bound
+        volatile uint32_t* rb = (row_bound && q0 + row < nq) ? row_bound + (q0 + row) : nullptr;
+        uint32_t ub_next = rb ? *rb : 0x7f800000u;
+        float pub = INF;                   // the last bound this thread published
+        // the column norms of the next tile, loaded one tile ahead
+        float4 cnx[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) cnx[i] = __ldg(reinterpret_cast<const float4*>(cne + c_begin + half * 32) + i);
         for (int g = 0; g < nt; ++g) {
             const int a = g % kFAcc;
             const bool got = mbar_wait_or(&bar_af[a], (uint32_t)((g / kFAcc) & 1), vfail);
@@ -796,12 +814,22 @@ __global__ void __launch_bounds__(kFBlock, 1)
             asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
             __syncwarp();
             if (lane == 0) mbar_arrive(&bar_ae[a]);          // the accumulator may be refilled
+            ub = fminf(ub, __uint_as_float(ub_next));
+            if (rb) ub_next = *rb;                            // for the next tile
+            lq = fminf(lmax, ub) + eps2 - qn + slack;
             const int rel0 = g * kFN + half * 32;            // column of r[0], relative to c_begin
-            const float4* cn4 = reinterpret_cast<const float4*>(cne + c_begin + rel0);
+            float4 cn4[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) cn4[i] = cnx[i];
+            if (g + 1 < nt) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                    cnx[i] = __ldg(reinterpret_cast<const float4*>(cne + c_begin + rel0 + kFN) + i);
+            }
 #pragma unroll
             for (int j0 = 0; j0 < 32; j0 += kW) {
                 if (!over && nc > LIST - kW) {
-                    const float lim = lmax + eps2;
+                    const float lim = fminf(lmax, ub) + eps2;
                     int k2 = 0;
                     for (int i = 0; i < nc; ++i) {
                         const float v = myval[i * kFT];
@@ -817,7 +845,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
                 const int nc0 = nc;
 #pragma unroll
                 for (int j = j0; j < j0 + kW; j += 4) {
-                    const float4 c4 = __ldg(cn4 + j / 4);
+                    const float4 c4 = cn4[j / 4];
                     const float2 m2 = make_float2(-2.f, -2.f);
                     const float2 x01 = __ffma2_rn(make_float2(__uint_as_float(r[j]), __uint_as_float(r[j + 1])), m2,
                                                   make_float2(c4.x, c4.y));
@@ -860,7 +888,20 @@ __global__ void __launch_bounds__(kFBlock, 1)
                         lmax = lv[LMAX - 1];
                     }
                 }
-                lq = lmax + eps2 - qn + slack;
+                lq = fminf(lmax, ub) + eps2 - qn + slack;
+            }
+            // the two halves of a row: L/2 values of each at or below max(A[L/2-1],
+            // B[L/2-1]) make L values at or below it, so it bounds the row's L-th
+            float bnd = lmax;
+            if (L == LMAX) {
+                s_halfb[half][row] = lv[LMAX / 2 - 1];
+                bnd = fminf(bnd, fmaxf(lv[LMAX / 2 - 1], s_halfb[half ^ 1][row]));
+                ub = fminf(ub, bnd);
+                lq = fminf(lmax, ub) + eps2 - qn + slack;
+            }
+            if (rb && bnd < pub) {
+                atomicMin(const_cast<uint32_t*>(rb), __float_as_uint(bnd));    // non-negative: bits order as values
+                pub = bnd;
             }
         }
     }
@@ -905,29 +946,32 @@ __global__ void __launch_bounds__(kFBlock, 1)
             T = fminf(T, fmaxf(a, b));
         }
         s_T[row] = T;
+        // the split's L-th smallest D~ bounds the row for the CTAs that follow
+        if (row_bound && q0 + row < nq && T < INF) atomicMin(row_bound + q0 + row, __float_as_uint(T));
     }
     __syncthreads();
-    // this thread's candidates: list entries within T~ + 2 eps, rescored exactly
+    // this thread's candidates: list entries within T~ + 2 eps, moved to the
+    // front of its list and rescored in place (the exact distance replaces D~)
     const float T = epi ? s_T[row] : INF;
-    const float climit = T + eps2;
+    // candidates: D~ <= min(T~ of this split's lists, the shared bound) + 2 eps,
+    // both >= the row's global L-th smallest D~
+    const float tb = fminf(T, ub);
+    const float climit = tb + eps2;
     const int qi = q0 + row;
     int nk = 0;
-    bool big = !epi || over || T == INF;
+    const bool big = !epi || over || !(tb < 3.0e38f);
     if (epi && qi < nq && !failed && !big) {
         for (int i = 0; i < nc; ++i) {
             if (myval[i * kFT] > climit) continue;
-            if (nk == LIST / 2) {
-                big = true;
-                break;
-            }
             mycol[nk * kFT] = mycol[i * kFT];
             ++nk;
         }
     }
     // Balanced rescoring: every (thread, slot) candidate of the CTA goes into
-    // one list, which all threads work through two at a time (two independent
-    // exact sums, their loads in flight together); the key lands in the
-    // owner's entry-major slot of s_key, [slot][owner]
+    // one pair list (after the halves' L-lists in the stage region), which all
+    // threads work through two at a time (two independent exact sums, their
+    // loads in flight together)
+    uint16_t* s_pair = reinterpret_cast<uint16_t*>(s_lv + LMAX * kTCM);     // [kFT * LIST]
     {
         const int mine = (epi && qi < nq && !failed && !big) ? nk : 0;
         int total;
@@ -962,9 +1006,8 @@ __global__ void __launch_bounds__(kFBlock, 1)
                 s0 = __fadd_rn(s0, __fmul_rn(x, x));
                 s1 = __fadd_rn(s1, __fmul_rn(y, y));
             }
-            s_key[i0 * kFT + t0] = make_key(__float_as_uint(s0), id_map ? (uint32_t)id_map[c0] : (uint32_t)c0);
-            if (p + kFBlock < total)
-                s_key[i1 * kFT + t1] = make_key(__float_as_uint(s1), id_map ? (uint32_t)id_map[c1] : (uint32_t)c1);
+            s_lval[i0 * kFT + t0] = s0;
+            if (p + kFBlock < total) s_lval[i1 * kFT + t1] = s1;
         }
     }
     s_nc[tid] = big ? -1 : nk;
@@ -973,26 +1016,40 @@ __global__ void __launch_bounds__(kFBlock, 1)
         const int na = s_nc[tid], nb = s_nc[tid + kTCM];
         const bool fall = failed || na < 0 || nb < 0;
         if (fall) row_fallback[qi] = 1;
-        // top-L of the row's candidate keys: repeated minimum over the two lists
-        const uint64_t* ka = s_key + tid;
-        const uint64_t* kb = s_key + tid + kTCM;
+        // top-L of the row's candidates by (exact distance, list): repeated
+        // minimum over the two halves' lists; local columns order as the
+        // global ids do (id_map is increasing), so (distance bits, column) keys
+        // rank them and the output keys carry the global ids
+        const float* va = s_lval + tid;
+        const float* vb = s_lval + tid + kTCM;
+        const uint16_t* ca = s_lcol + tid;
+        const uint16_t* cb = s_lcol + tid + kTCM;
         uint64_t last = 0;
         for (int o = 0; o < L; ++o) {
             uint64_t best = kKeyNone;
             if (!fall) {
-                for (int i = 0; i < na; ++i)
-                    if ((o == 0 || ka[i * kFT] > last) && ka[i * kFT] < best) best = ka[i * kFT];
-                for (int i = 0; i < nb; ++i)
-                    if ((o == 0 || kb[i * kFT] > last) && kb[i * kFT] < best) best = kb[i * kFT];
-            }
-            if (split_keys) {
-                split_keys[((size_t)blockIdx.y * nq + qi) * L + o] = best;
-            } else if (!fall) {
-                const bool ok = best != kKeyNone;
-                if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(best) : -1;
-                if (out_keys) out_keys[(size_t)qi * L + o] = best;
+                for (int i = 0; i < na; ++i) {
+                    const uint64_t kk = make_key(__float_as_uint(va[i * kFT]), (uint32_t)ca[i * kFT]);
+                    if ((o == 0 || kk > last) && kk < best) best = kk;
+                }
+                for (int i = 0; i < nb; ++i) {
+                    const uint64_t kk = make_key(__float_as_uint(vb[i * kFT]), (uint32_t)cb[i * kFT]);
+                    if ((o == 0 || kk > last) && kk < best) best = kk;
+                }
             }
             last = best;
+            uint64_t outk = kKeyNone;
+            if (best != kKeyNone) {
+                const int c = c_begin + (int)key_lo(best);
+                outk = make_key(key_hi(best), id_map ? (uint32_t)id_map[c] : (uint32_t)c);
+            }
+            if (split_keys) {
+                split_keys[((size_t)blockIdx.y * nq + qi) * L + o] = outk;
+            } else if (!fall) {
+                const bool ok = outk != kKeyNone;
+                if (out_ids) out_ids[(size_t)qi * L + o] = ok ? (int32_t)key_lo(outk) : -1;
+                if (out_keys) out_keys[(size_t)qi * L + o] = outk;
+            }
         }
     }
 }
@@ -1152,7 +1209,7 @@ int route_tc_fused_splits(int nq, int nlist) {
 cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const float* cne, const float* cn_max,
                            const uint8_t* valid, int nlist, int d, const float* cent, int L, const int32_t* id_map,
                            int32_t* out_ids, uint64_t* out_keys, int32_t* row_fallback, uint64_t* split_keys,
-                           int splits, int* flag, cudaStream_t st) {
+                           uint32_t* row_bound, int splits, int* flag, cudaStream_t st) {
     if (nq <= 0) return cudaSuccess;
     if (!route_tc_fused_usable(d, nlist, L)) return cudaErrorInvalidValue;
     const int ntiles = (nlist + kFN - 1) / kFN;
@@ -1162,6 +1219,8 @@ cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const fl
     if (S > kFMaxSplits || per * kFN > 65536 || (S > 1 && !split_keys)) return cudaErrorInvalidValue;
     cudaError_t e = cudaMemsetAsync(row_fallback, 0, sizeof(int32_t) * (size_t)nq, st);
     if (e) return e;
+    // 0x7f7f7f7f: a float above any distance, "no bound yet"
+    if (row_bound && (e = cudaMemsetAsync(row_bound, 0x7f, sizeof(uint32_t) * (size_t)nq, st))) return e;
     const int lmax = fused_lmax(L), list = fused_list(lmax);
     const size_t region = route_fused_region(d, list);
     const size_t smem = route_fused_fixed(d, list) + region;
@@ -1176,7 +1235,7 @@ cudaError_t route_tc_fused(const float* q, int nq, const uint16_t* ops, const fl
         if (e) return e;                                                                                         \
         route_tc_fused_kernel<LM, LI><<<grid, kFBlock, smem, st>>>(q, nq, d, ops, cne, cn_max, valid, nlist,     \
                                                                     cent, L, id_map, per, (int)region, out_ids,  \
-                                                                    out_keys, sk, row_fallback, flag);           \
+                                                                    out_keys, sk, row_bound, row_fallback, flag); \
     }
     if (lmax == 8) ISB_FUSED(8) else if (lmax == 16) ISB_FUSED(16) else ISB_FUSED(32)
 #undef ISB_FUSED

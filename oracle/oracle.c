@@ -164,6 +164,86 @@ ORACLE_API int oracle_route_l2(const float* q, int nq, const float* cent, int nl
     return 0;
 }
 
+/*
+ * The reference's own routing formula (cuda/search/cpu_fine/ivf_search_cpu_fine.cu:857-944
+ * with cuda/search/coarse/fusion_l2_topk_warpsort.cu:127-135): per query and
+ * centroid, dist = -2 * <q, c> + |q| * |q| + |c| * |c|, the norms as
+ * sqrtf of the sum of squares (cuda/l2norm/l2norm.cu), evaluated left to right
+ * in fp32; centroids with |c| < 1e-6 are skipped.  The reference takes <q, c>
+ * from cuBLAS SGEMM, whose summation order is not documented; here it is the
+ * sequential fp32 sum, one admissible order.  Used only to measure how often
+ * this formula and the direct-difference routing above disagree (near-ties).
+ * Top-nprobe by (dist, list id); negative distances (cancellation) order
+ * below zero.
+ */
+static inline uint64_t fkey_signed(float v, uint32_t id) {
+    uint32_t b;
+    memcpy(&b, &v, 4);
+    b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    return ((uint64_t)b << 32) | id;
+}
+
+static inline float unfkey_signed(uint32_t b) {
+    b = (b & 0x80000000u) ? (b & 0x7fffffffu) : ~b;
+    float v;
+    memcpy(&v, &b, 4);
+    return v;
+}
+
+ORACLE_API int oracle_route_l2_normexp(const float* q, int nq, const float* cent, int nlist, int d,
+                                       int nprobe, int32_t* out_ids, float* out_dist) {
+    if (nq < 0 || nlist <= 0 || d <= 0 || nprobe <= 0) return -1;
+    float* cn = (float*)malloc(sizeof(float) * (size_t)nlist);
+    uint64_t* buf = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)nprobe);
+    if (!cn || !buf) { free(cn); free(buf); return -2; }
+    for (int c = 0; c < nlist; ++c) {
+        float s = 0.0f;
+        for (int j = 0; j < d; ++j) {
+            float p = cent[(size_t)c * d + j] * cent[(size_t)c * d + j];
+            s = s + p;
+        }
+        cn[c] = sqrtf(s);
+    }
+    for (int qi = 0; qi < nq; ++qi) {
+        kheap h = {buf, 0, nprobe};
+        const float* qq = q + (size_t)qi * d;
+        float s = 0.0f;
+        for (int j = 0; j < d; ++j) {
+            float p = qq[j] * qq[j];
+            s = s + p;
+        }
+        const float qn = sqrtf(s);
+        for (int c = 0; c < nlist; ++c) {
+            if (!(cn[c] >= 1e-6f)) continue;
+            const float* cc = cent + (size_t)c * d;
+            float ip = 0.0f;
+            for (int j = 0; j < d; ++j) {
+                float p = qq[j] * cc[j];
+                ip = ip + p;
+            }
+            float t = -2.0f * ip;
+            float qq2 = qn * qn;
+            float cc2 = cn[c] * cn[c];
+            t = t + qq2;
+            t = t + cc2;
+            kheap_push(&h, fkey_signed(t, (uint32_t)c));
+        }
+        kheap_sort(&h);
+        for (int p = 0; p < nprobe; ++p) {
+            if (p < h.n) {
+                out_ids[(size_t)qi * nprobe + p] = (int32_t)(uint32_t)h.k[p];
+                if (out_dist) out_dist[(size_t)qi * nprobe + p] = unfkey_signed((uint32_t)(h.k[p] >> 32));
+            } else {
+                out_ids[(size_t)qi * nprobe + p] = -1;
+                if (out_dist) out_dist[(size_t)qi * nprobe + p] = INFINITY;
+            }
+        }
+    }
+    free(cn);
+    free(buf);
+    return 0;
+}
+
 /* ------------------------------------------------------------------ */
 /* exact uint8 fine search                                              */
 /* ------------------------------------------------------------------ */

@@ -43,6 +43,8 @@ def lib():
         L.oracle_centroid_valid.argtypes = [f32p, C.c_int, C.c_int, u8p]
         L.oracle_route_l2.argtypes = [f32p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, i32p, f32p]
         L.oracle_route_l2.restype = C.c_int
+        L.oracle_route_l2_normexp.argtypes = [f32p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, i32p, f32p]
+        L.oracle_route_l2_normexp.restype = C.c_int
         L.oracle_exact_u8.argtypes = [u8p, i64p, i32p, C.c_void_p, C.c_int, C.c_int,
                                       u8p, i32p, C.c_int, C.c_int, C.c_int, C.c_void_p, i32p, i32p]
         L.oracle_exact_u8.restype = C.c_int
@@ -172,6 +174,61 @@ def pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_
     if return_stage1:
         return ids, dist, s1, sd
     return ids, dist
+
+
+def route_l2_normexp(q, cent, nprobe, threads=0):
+    """Routing by the reference's formula -2 q.c + |q|^2 + |c|^2 (fp32, norms
+    through sqrtf), over query slices on host threads; see oracle.c."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    q = _c(q, np.float32)
+    cent = _c(cent, np.float32)
+
+    def one(r):
+        qs = np.ascontiguousarray(q[r[0]:r[1]])
+        ids = np.empty((qs.shape[0], nprobe), np.int32)
+        dist = np.empty((qs.shape[0], nprobe), np.float32)
+        rc = lib().oracle_route_l2_normexp(qs, qs.shape[0], cent, cent.shape[0], q.shape[1], nprobe, ids, dist)
+        assert rc == 0, rc
+        return ids, dist
+    parts = _split_queries(q.shape[0], threads)
+    with ThreadPoolExecutor(len(parts)) as ex:
+        res = list(ex.map(one, parts))
+    return np.concatenate([a for a, _ in res]), np.concatenate([b for _, b in res])
+
+
+def route_disagreement(q, cent, ours, theirs, d_bound_factor=None):
+    """Compares two top-nprobe probe tables of the same queries.
+
+    Returns (n_queries_differing, max_gap_ratio): for every query whose sets
+    differ, every list only in `theirs` must not be farther (exact fp64
+    distance) than our nprobe-th list by more than B, and every list only in
+    `ours` not nearer than it by more than B, with
+    B = 2 (2 d + 10) 2^-24 (|q|^2 + max |c|^2), the rounding bound of an fp32
+    evaluation of -2 q.c + |q|^2 + |c|^2 in any summation order;
+    max_gap_ratio is the largest such excess over B seen (<= 1 when every
+    disagreement is a rounding-level near-tie)."""
+    q = np.asarray(q, np.float64)
+    cent = np.asarray(cent, np.float64)
+    d = q.shape[1]
+    f = d_bound_factor if d_bound_factor is not None else 2.0 * (2 * d + 10) * 2.0 ** -24
+    cmax = float((cent * cent).sum(1).max())
+    n_diff, worst = 0, 0.0
+    for i in range(q.shape[0]):
+        a, b = set(ours[i][ours[i] >= 0].tolist()), set(theirs[i][theirs[i] >= 0].tolist())
+        if a == b:
+            continue
+        n_diff += 1
+        ids = np.array(sorted(a | b))
+        dd = ((cent[ids] - q[i]) ** 2).sum(1)
+        dist = dict(zip(ids.tolist(), dd.tolist()))
+        T = max(dist[x] for x in a)
+        B = f * (float((q[i] * q[i]).sum()) + cmax)
+        for x in b - a:
+            worst = max(worst, (dist[x] - T) / B)
+        for x in a - b:
+            worst = max(worst, (T - dist[x]) / B if dist[x] < T else 0.0)
+    return n_diff, worst
 
 
 def _split_queries(nq, threads):

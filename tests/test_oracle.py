@@ -241,3 +241,32 @@ def test_oracle_deletes():
         ids = p["r2o"][pos]
         o = np.lexsort((ids, dd))[:k]
         assert np.array_equal(oi[i][:len(o)], ids[o]) and np.array_equal(od[i][:len(o)], dd[o].astype(np.float32))
+
+
+@pytest.mark.parametrize("shape", ["c1", "c2"])
+def test_reference_routing_formula_agrees_up_to_near_ties(shape):
+    """The reference routes by -2 q.c + |q|^2 + |c|^2 (fp32, norms through
+    sqrtf; ivf_search_cpu_fine.cu:857-944, fusion_l2_topk_warpsort.cu:127-135);
+    this library ranks centroids by the exact fp32 direct difference.  On
+    seeded inputs of the c1 and c2 routing shapes the two probe tables agree
+    except for rounding-level near-ties: every list one table has and the
+    other lacks lies within the formula's fp32 rounding bound of the
+    nprobe-th distance (oracle.route_disagreement)."""
+    g = np.random.default_rng(7 if shape == "c1" else 8)
+    if shape == "c1":
+        nq, nlist, d, nprobe = 1000, 4096, 96, 8
+        cent = g.standard_normal((nlist, d)).astype(np.float32)
+        cent /= np.linalg.norm(cent, axis=1, keepdims=True)
+        comp = g.integers(0, nlist, nq)
+        q = cent[comp] + 0.05 * g.standard_normal((nq, d)).astype(np.float32)
+        q = (q / np.linalg.norm(q, axis=1, keepdims=True)).astype(np.float32)
+    else:
+        nq, nlist, d, nprobe = 200, 65536, 128, 16
+        cent = (32.0 + 192.0 * g.random((nlist, d))).astype(np.float32)
+        comp = g.integers(0, nlist, nq)
+        q = np.clip(np.round(cent[comp] + 10.0 * g.standard_normal((nq, d))), 0, 255).astype(np.float32)
+    ours, _ = oracle.route_l2_par(q, cent, nprobe)
+    theirs, _ = oracle.route_l2_normexp(q, cent, nprobe)
+    n_diff, worst = oracle.route_disagreement(q, cent, ours, theirs)
+    assert worst <= 1.0, (n_diff, worst)
+    assert n_diff <= max(2, nq // 20), n_diff
