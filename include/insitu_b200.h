@@ -210,6 +210,45 @@ int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, c
 int ivf_set_deleted(void* idx_ctx, const unsigned char* deleted, long long n);
 
 /* ======================================================================
+ * Index build on the GPU (the reference builds offline: k-means in
+ * cuda/clustering/kmeans/kmeans.cu, the stable reorder in
+ * cuda/dataset/dataset.cuh:559-592, residual PQ with faiss in
+ * scripts/train_ivfpq_residual.py:151-310).  Device pointers; every
+ * reduction runs in a fixed order (fp64 sums, rows in increasing order), so
+ * a build is deterministic.  The calls without a batch context queue their
+ * work on `stream` (a cudaStream_t, NULL = legacy default stream) and may
+ * allocate temporary device memory; they report failures through
+ * ivf_global_last_error().
+ * ====================================================================== */
+/* a routing-only index context: the centroids [nlist, d] (host or device),
+ * for ivf_assign and ivf_route */
+int ivf_load_centroids(void* idx_ctx, const float* centroids, int nlist, int d);
+/* exact nearest centroid of n rows d_x [n, d] (fp32, or uint8 when x_is_u8):
+ * the routing kernels with n_probes = 1 (exact fp32 L2, ties to the smaller
+ * list id), in sub-batches of the batch context's max_n_query rows, on the
+ * batch stream; d_assign [n] int32 */
+int ivf_assign(void* batch_ctx, void* idx_ctx, const void* d_x, int x_is_u8, long long n, int* d_assign);
+/* stable cluster-major order: d_counts [nlist], d_offsets [nlist], d_order
+ * [n] = the row at each position (a list's rows in increasing row order, as
+ * dataset.cuh:559-592 and the reorder_to_original array of the loaders) */
+int ivf_build_reorder(const int* d_assign, long long n, int nlist, int* d_counts, long long* d_offsets, int* d_order,
+                      void* stream);
+/* one k-means update: centroid l = mean of the rows assigned to l (lists
+ * without rows keep their centroid) */
+int ivf_kmeans_update(const void* d_x, int x_is_u8, long long n, int d, const int* d_assign, int nlist,
+                      float* d_centroids, void* stream);
+/* residual-PQ training: `iters` Lloyd iterations per sub-space (K = 256,
+ * dsub = d / M in {1, 2, 4, 8}) on the residuals x_i - centroid[assign_i] of
+ * n sample rows, starting from and updating d_codebook [M, 256, dsub] */
+int ivf_pq_train(const void* d_x, int x_is_u8, long long n, int d, const float* d_centroids, const int* d_assign,
+                 int M, int iters, float* d_codebook, void* stream);
+/* residual-PQ encoding: d_codes [n, M], code m of row d_rows[i] (NULL: i) =
+ * the nearest codeword (squared L2 in dimension order, ties to the smaller
+ * code) of sub-space m to its residual against centroid[assign[row]] */
+int ivf_pq_encode(const void* d_x, int x_is_u8, long long n, int d, const int* d_rows, const float* d_centroids,
+                  const int* d_assign, const float* d_codebook, int M, unsigned char* d_codes, void* stream);
+
+/* ======================================================================
  * Update overlay (new: runner-internal in the reference,
  * updates/pq_update.cu:396-494, 975-1055)
  * ====================================================================== */

@@ -28,7 +28,7 @@ namespace {
 
 constexpr uint32_t kIdxMagic = 0x31584449u;  // "IDX1"
 constexpr uint32_t kBatMagic = 0x31544142u;  // "BAT1"
-constexpr int kKindEmpty = 0, kKindF32 = 1, kKindU8 = 2, kKindPQ = 3;
+constexpr int kKindEmpty = 0, kKindF32 = 1, kKindU8 = 2, kKindPQ = 3, kKindRoute = 4;
 
 struct ApiError : std::runtime_error {
     int code;
@@ -1063,6 +1063,103 @@ int ivf_pq_load(void* idx_ctx, const float* centroids, const float* codebook, in
         x->dsub = dsub;
         x->n = n;
         x->kind = kKindPQ;
+    });
+}
+
+// ---------------------------------------------------------------------------
+// index build (build.cu kernels; assignment through the routing path)
+// ---------------------------------------------------------------------------
+int ivf_load_centroids(void* idx_ctx, const float* centroids, int nlist, int d) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
+        require(x->kind == kKindEmpty, "index context already holds an index", IVF_ESTATE);
+        require(nlist > 0 && d > 0 && d % 4 == 0 && d <= 512, "need nlist > 0, d % 4 == 0, d <= 512");
+        cudaSetDevice(x->device);
+        try {
+            load_centroids(x, centroids, nlist, d);
+        } catch (...) {
+            free_all(x->owned);
+            throw;
+        }
+        x->kind = kKindRoute;
+    });
+}
+
+int ivf_assign(void* batch_ctx, void* idx_ctx, const void* d_x, int x_is_u8, long long n, int* d_assign) {
+    BatchCtx* b = nullptr;
+    try {
+        b = as_batch(batch_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&b->err, [&] {
+        IndexCtx* x = as_index(idx_ctx);
+        std::shared_lock<std::shared_mutex> rd(x->rw);
+        require(x->kind != kKindEmpty, "index context holds no centroids", IVF_ESTATE);
+        require(b->d == x->d, "batch and index dimensions differ");
+        require(n >= 0 && (d_x || n == 0) && (d_assign || n == 0), "bad rows or output");
+        require(x->nlist_global == x->nlist, "assignment needs the whole centroid set, not a shard");
+        cudaSetDevice(b->device);
+        for (long long s = 0; s < n; s += b->max_nq) {
+            const int m = (int)std::min<long long>(b->max_nq, n - s);
+            ck(stage_rows_f32(d_x, x_is_u8, (size_t)s * x->d, (size_t)m * x->d, b->q, b->st), "stage rows");
+            b->probes_nq = 0;
+            do_route(b, x, m, 1, nullptr);
+            ck(cudaMemcpyAsync(d_assign + s, b->probes, sizeof(int32_t) * (size_t)m, cudaMemcpyDeviceToDevice,
+                               b->st),
+               "assign D2D");
+        }
+        b->probes_nq = 0;
+    });
+}
+
+int ivf_build_reorder(const int* d_assign, long long n, int nlist, int* d_counts, long long* d_offsets, int* d_order,
+                      void* stream) {
+    return guarded(nullptr, [&] {
+        require(n >= 0 && n < 2147483647ll && nlist > 0, "need 0 <= n < 2^31, nlist > 0");
+        require(d_assign && d_counts && d_offsets && d_order, "null pointer");
+        ck(build_reorder(d_assign, n, nlist, d_counts, reinterpret_cast<int64_t*>(d_offsets), d_order,
+                         static_cast<cudaStream_t>(stream)),
+           "build_reorder (an assignment outside [0, nlist)?)");
+    });
+}
+
+int ivf_kmeans_update(const void* d_x, int x_is_u8, long long n, int d, const int* d_assign, int nlist,
+                      float* d_centroids, void* stream) {
+    return guarded(nullptr, [&] {
+        require(n >= 0 && n < 2147483647ll && d > 0 && nlist > 0 && d_x && d_assign && d_centroids, "bad arguments");
+        ck(kmeans_update(d_x, x_is_u8, n, d, d_assign, nlist, d_centroids, static_cast<cudaStream_t>(stream)),
+           "kmeans_update (an assignment outside [0, nlist)?)");
+    });
+}
+
+int ivf_pq_train(const void* d_x, int x_is_u8, long long n, int d, const float* d_centroids, const int* d_assign,
+                 int M, int iters, float* d_codebook, void* stream) {
+    return guarded(nullptr, [&] {
+        require(n >= 0 && d > 0 && M > 0 && d % M == 0 && (d / M == 1 || d / M == 2 || d / M == 4 || d / M == 8),
+                "need d % M == 0 and d / M in {1, 2, 4, 8}");
+        require((long long)n * M < 2147483647ll, "n * M must be below 2^31");
+        ck(pq_train(d_x, x_is_u8, n, d, d_centroids, d_assign, M, iters, d_codebook,
+                    static_cast<cudaStream_t>(stream)),
+           "pq_train");
+    });
+}
+
+int ivf_pq_encode(const void* d_x, int x_is_u8, long long n, int d, const int* d_rows, const float* d_centroids,
+                  const int* d_assign, const float* d_codebook, int M, unsigned char* d_codes, void* stream) {
+    return guarded(nullptr, [&] {
+        require(n >= 0 && d > 0 && M > 0 && d % M == 0 && (d / M == 1 || d / M == 2 || d / M == 4 || d / M == 8),
+                "need d % M == 0 and d / M in {1, 2, 4, 8}");
+        ck(pq_encode_rows(d_x, x_is_u8, n, d, d_rows, d_centroids, d_assign, d_codebook, M, d_codes,
+                          static_cast<cudaStream_t>(stream)),
+           "pq_encode");
     });
 }
 

@@ -106,6 +106,25 @@ cudaError_t exact_group_scan(const uint8_t* q_u8, int d, int k, ListStore ls, Wo
 cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkList wl, int max_pairs,
                        CandBuf cb, int* work_counter, cudaStream_t st);
 
+// ---- index build (build.cu) ---------------------------------------------------
+// out[i] = x[offset + i] as fp32 for i < n (x uint8 when is_u8, else fp32)
+cudaError_t stage_rows_f32(const void* x, int is_u8, size_t offset, size_t n, float* out, cudaStream_t st);
+// stable cluster-major order of n rows by assignment: counts / offsets per
+// list, order[p] = row at position p (rows of a list in increasing order);
+// cudaErrorInvalidValue when an assignment is outside [0, nlist)
+cudaError_t build_reorder(const int32_t* assign, int64_t n, int nlist, int32_t* counts, int64_t* offsets,
+                          int32_t* order, cudaStream_t st);
+// cent[l] = mean of the rows assigned to l (fp64 sums in row order; empty lists keep their centroid)
+cudaError_t kmeans_update(const void* x, int is_u8, int64_t n, int d, const int32_t* assign, int nlist, float* cent,
+                          cudaStream_t st);
+// codes[i][m] = nearest of the 256 codewords of sub-space m to the residual of
+// row rows[i] (nullptr: i) against its centroid cent[assign[row]]
+cudaError_t pq_encode_rows(const void* x, int is_u8, int64_t n, int d, const int32_t* rows, const float* cent,
+                           const int32_t* assign, const float* cb, int M, uint8_t* codes, cudaStream_t st);
+// `iters` Lloyd iterations per sub-space on n rows, codebook cb [M, 256, d / M] updated in place
+cudaError_t pq_train(const void* x, int is_u8, int64_t n, int d, const float* cent, const int32_t* assign, int M,
+                     int iters, float* cb, cudaStream_t st);
+
 // ---- residual PQ (pq.cu) -----------------------------------------------------
 struct PQParams {
     const float* q;          // [nq, d] fp32 queries

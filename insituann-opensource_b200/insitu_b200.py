@@ -43,6 +43,7 @@ EXPORTS = [
     "ivf_pq_shard_select", "ivf_pq_shard_kappa", "ivf_pq_shard_rerank", "ivf_pq_shard_final",
     "ivf_last_error", "ivf_global_last_error",
     "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms", "ivf_u8_search_noalloc",
+    "ivf_load_centroids", "ivf_assign", "ivf_build_reorder", "ivf_kmeans_update", "ivf_pq_train", "ivf_pq_encode",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
     "cuda_pipeline_init", "cuda_pipeline_flush", "cuda_pipeline_flush_vectors_only", "cuda_pipeline_free",
@@ -106,6 +107,12 @@ _SIGS = {
     "ivf_batch_profile": ([vp, i32], i32),
     "ivf_batch_stage_ms": ([vp, vp, i32], i32),
     "ivf_u8_search_noalloc": ([vp, vp, vp, i32, i32, i32, vp, vp, vp], i32),
+    "ivf_load_centroids": ([vp, vp, i32, i32], i32),
+    "ivf_assign": ([vp, vp, vp, i32, i64, vp], i32),
+    "ivf_build_reorder": ([vp, i64, i32, vp, vp, vp, vp], i32),
+    "ivf_kmeans_update": ([vp, i32, i64, i32, vp, i32, vp, vp], i32),
+    "ivf_pq_train": ([vp, i32, i64, i32, vp, vp, i32, i32, vp, vp], i32),
+    "ivf_pq_encode": ([vp, i32, i64, i32, vp, vp, vp, vp, i32, vp, vp], i32),
 }
 
 STAGES = ("route", "worklist", "scan", "select", "rerank")
@@ -408,6 +415,100 @@ class Batch:
             self.close()
         except Exception:
             pass
+
+
+class Builder:
+    """GPU index build through the C ABI (device tensors in and out).
+
+    ``assign`` is the exact routing with n_probes = 1; ``kmeans`` runs Lloyd
+    iterations of assign + ivf_kmeans_update; ``reorder``, ``pq_train`` and
+    ``pq_encode`` wrap the other build entry points.  Work runs on the current
+    torch stream of the tensors' device."""
+
+    def __init__(self, d: int, batch_rows: int = 65536):
+        self.L = load_library(require_device=True)
+        self.d = d
+        self.batch_rows = batch_rows
+
+    def _stream(self):
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+
+    def _check(self, rc, ctx=None):
+        if rc != IVF_OK:
+            msg = (self.L.ivf_last_error(ctx) if ctx else self.L.ivf_global_last_error()).decode()
+            raise InsituError(rc, msg)
+
+    def assign(self, x, centroids):
+        """nearest centroid (int32 [n]) of the rows of x (uint8 or fp32 device tensor)."""
+        import torch
+
+        n = x.shape[0]
+        nlist = centroids.shape[0]
+        out = torch.empty(n, dtype=torch.int32, device=x.device)
+        idx = self.L.ivf_create_index_context()
+        b = self.L.ivf_create_batch_context(min(self.batch_rows, max(n, 1)), self.d, 1, 1, nlist)
+        try:
+            c = centroids.float().contiguous()
+            self._check(self.L.ivf_load_centroids(idx, c.data_ptr(), nlist, self.d), idx)
+            torch.cuda.current_stream().synchronize()
+            self._check(self.L.ivf_assign(b, idx, x.contiguous().data_ptr(), 1 if x.dtype == torch.uint8 else 0,
+                                          n, out.data_ptr()), b)
+            self.L.ivf_pipeline_sync_batch(b)
+        finally:
+            self.L.ivf_destroy_batch_context(b)
+            self.L.ivf_destroy_index_context(idx)
+        return out
+
+    def kmeans_update(self, x, assign, centroids):
+        import torch
+
+        self._check(self.L.ivf_kmeans_update(x.contiguous().data_ptr(), 1 if x.dtype == torch.uint8 else 0,
+                                             x.shape[0], self.d, assign.data_ptr(), centroids.shape[0],
+                                             centroids.data_ptr(), self._stream()))
+        return centroids
+
+    def kmeans(self, x, init_centroids, iters):
+        """Lloyd k-means from init_centroids (fp32 [nlist, d], updated copy returned)."""
+        cent = init_centroids.float().clone().contiguous()
+        for _ in range(iters):
+            a = self.assign(x, cent)
+            self.kmeans_update(x, a, cent)
+        return cent
+
+    def reorder(self, assign, nlist):
+        """(counts int32 [nlist], offsets int64 [nlist], order int32 [n]) as device tensors."""
+        import torch
+
+        n = assign.shape[0]
+        counts = torch.empty(nlist, dtype=torch.int32, device=assign.device)
+        offsets = torch.empty(nlist, dtype=torch.int64, device=assign.device)
+        order = torch.empty(max(n, 1), dtype=torch.int32, device=assign.device)
+        self._check(self.L.ivf_build_reorder(assign.data_ptr(), n, nlist, counts.data_ptr(), offsets.data_ptr(),
+                                             order.data_ptr(), self._stream()))
+        return counts, offsets, order[:n]
+
+    def pq_train(self, x, centroids, assign, codebook, iters):
+        import torch
+
+        M = codebook.shape[0]
+        self._check(self.L.ivf_pq_train(x.contiguous().data_ptr(), 1 if x.dtype == torch.uint8 else 0, x.shape[0],
+                                        self.d, centroids.data_ptr(), assign.data_ptr(), M, iters,
+                                        codebook.data_ptr(), self._stream()))
+        return codebook
+
+    def pq_encode(self, x, centroids, assign, codebook, rows=None):
+        import torch
+
+        M = codebook.shape[0]
+        n = rows.shape[0] if rows is not None else x.shape[0]
+        codes = torch.empty((n, M), dtype=torch.uint8, device=x.device)
+        self._check(self.L.ivf_pq_encode(x.contiguous().data_ptr(), 1 if x.dtype == torch.uint8 else 0, n, self.d,
+                                         None if rows is None else rows.data_ptr(), centroids.data_ptr(),
+                                         assign.data_ptr(), codebook.data_ptr(), M, codes.data_ptr(),
+                                         self._stream()))
+        return codes
 
 
 class CoarseTiming(C.Structure):

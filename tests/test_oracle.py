@@ -270,3 +270,30 @@ def test_reference_routing_formula_agrees_up_to_near_ties(shape):
     n_diff, worst = oracle.route_disagreement(q, cent, ours, theirs)
     assert worst <= 1.0, (n_diff, worst)
     assert n_diff <= max(2, nq // 20), n_diff
+
+
+def _route_fixture():
+    path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "route_ref.npz")
+    if not os.path.exists(path):
+        pytest.skip("route_ref.npz not generated (tests/golden/make_route_golden.py, needs a GPU)")
+    return np.load(path)
+
+
+@pytest.mark.parametrize("name", ["c1", "c2"])
+def test_oracle_routing_vs_reference_coarse_search(name):
+    """The oracle's exact routing (which the GPU kernels equal bit for bit)
+    against the reference's own coarse_search (cuBLAS SGEMM + warpsort top-k,
+    recorded on a GPU into golden/route_ref.npz): the probe sets agree except
+    for rounding-level near-ties (oracle.route_disagreement), on the first 500
+    queries of the seeded c1 / c2 routing cases."""
+    import route_cases
+
+    fx = _route_fixture()
+    cent, q = route_cases.make(name)
+    P = 500
+    for nprobe in route_cases.CASES[name]["nprobes"]:
+        ref = fx[f"{name}_nprobe{nprobe}"][:P]
+        ours, _ = oracle.route_l2_par(q[:P], cent, nprobe)
+        n_diff, worst = oracle.route_disagreement(q[:P], cent, ours, ref)
+        assert worst <= 1.0, (nprobe, n_diff, worst)
+        assert n_diff <= P // 50, (nprobe, n_diff)
