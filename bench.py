@@ -65,6 +65,18 @@ CONFIGS = {
                nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16, 32, 64, 128, 256), seed=20260602,
                desc="c2: residual-PQ IVF, 100M x 128 uint8 (65536-comp mixture, centers U[32,224], sigma 10), "
                     "nlist 65536, M=32 x 8b, 10k queries, k=10, rerank_n=512 (uint8 rerank)"),
+    # 1B x 128 uint8 with Zipf(1.1) component weights, nlist 262144, sharded
+    # over the GPUs (run it with --gpus 8); k-means on a 4.2M-row sample, 10 iterations
+    "c3": dict(kind="pq_u8", n=1_000_000_000, d=128, ncomp=262144, sigma=10.0, zipf=1.1, nlist=262144, M=32,
+               train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(32, 64, 128), seed=20260603,
+               kmeans_iters=10, kmeans_sample=16 * 262144,
+               desc="c3: residual-PQ IVF, 1B x 128 uint8 (262144-comp mixture, Zipf(1.1) weights, sigma 10), "
+                    "nlist 262144, M=32 x 8b, 10k queries, k=10, rerank_n=512 (uint8 rerank), lists sharded"),
+    # c2 at a tenth of the rows (the c2 list count and shapes): a quick check of the c2 path
+    "c2-small": dict(kind="pq_u8", n=10_000_000, d=128, ncomp=65536, sigma=10.0, nlist=65536, M=32,
+                     train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=20260602,
+                     kmeans_iters=6, kmeans_sample=16 * 65536,
+                     desc="c2 shapes at 10M rows (quick checks)"),
     # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
     "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
                    nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,
@@ -165,8 +177,14 @@ def pq_build(cfg, dev, rank=0, world=1, dist=None):
     def say(what):
         if rank == 0:
             log(f"[bench] {what} {time.time() - t0:.1f}s")
-    b = synth.build_pq_shard(src, cfg["nlist"], cfg["M"], cfg["seed"], rank, world, dist, kmeans_iters=20,
-                             pq_iters=12, train_n=cfg["train_n"], kmeans_sample=64 * cfg["nlist"], log=say)
+    builder = None
+    if dev.type == "cuda":
+        import insitu_b200 as ib
+
+        builder = ib.Builder(cfg["d"], batch_rows=65536)     # the library's GPU index build
+    b = synth.build_pq_shard(src, cfg["nlist"], cfg["M"], cfg["seed"], rank, world, dist,
+                             kmeans_iters=cfg.get("kmeans_iters", 20), pq_iters=12, train_n=cfg["train_n"],
+                             kmeans_sample=cfg.get("kmeans_sample", 64 * cfg["nlist"]), log=say, builder=builder)
     keys = synth.gt_keys(b["base_rr"], q, cfg["k"], ids=b["r2o"])
     if world > 1:
         allk = torch.empty(world * keys.numel(), dtype=keys.dtype, device=dev)

@@ -558,10 +558,12 @@ __host__ __device__ constexpr size_t route_fused_fixed(int d, int list) {
     return (size_t)kTCM * 2 * d * 2 + (sizeof(float) + sizeof(uint16_t)) * kFT * (size_t)list +
            sizeof(float) * 2 * kTCM + sizeof(int) * kFBlock;
 }
-// the stage region must hold two full (3-part) tiles, and after the sweep the
-// halves' L-lists and the rescoring's pair list
+// the stage region must hold two 2-part tiles (queries bf16 holds exactly)
+// and one 3-part tile (a single stage serialises copy and MMA but works), and
+// after the sweep the halves' L-lists and the rescoring's pair list
 __host__ __device__ constexpr size_t route_fused_region_min(int d, int list) {
-    const size_t tiles = 2 * (size_t)kFN * 3 * d * 2;
+    const size_t part = (size_t)kFN * d * 2;
+    const size_t tiles = 4 * part > 3 * part ? 4 * part : 3 * part;
     const size_t after = sizeof(float) * kTCM * kFLMax + sizeof(uint16_t) * kFT * (size_t)list;
     return tiles > after ? tiles : after;
 }

@@ -4,9 +4,12 @@ The reference measures on SIFT1B / DEEP / SPACEV, which are not available
 here; seeded Gaussian mixtures with the shapes, sizes and value ranges of the
 benchmark configs stand in for them.  Index building (k-means, stable
 cluster-major reorder, residual-PQ training and encoding) is the offline
-part of the reference (cuda/clustering/, scripts/train_ivfpq_residual.py); it
-is written here with torch so it runs on the GPU box in seconds, and it is
-not part of the measured query path.
+part of the reference (cuda/clustering/, scripts/train_ivfpq_residual.py).
+The torch functions here serve the small CPU-side cases of the tests;
+build_pq_shard can instead drive the library's GPU build entry points
+(insitu_b200.Builder: exact assignment by the routing kernels, fixed-order
+means), which the benchmark uses.  None of it is part of the measured query
+path.
 
 Counter-based seeding: every chunk of rows draws from its own generator
 seeded by (seed, chunk index), so any shard can generate its rows alone.
@@ -404,7 +407,7 @@ class RowSource:
 def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0, world: int = 1, dist=None,
                    kmeans_iters: int = 20, pq_iters: int = 12, train_n: int = 500_000,
                    kmeans_sample: Optional[int] = None, row_bytes: Optional[int] = None, assign_fn=None,
-                   log=None):
+                   log=None, builder=None):
     """Residual-PQ index of src, built so that each rank holds only its own lists.
 
     1. rank 0 runs k-means on the first kmeans_sample rows (an i.i.d. sample of
@@ -417,6 +420,9 @@ def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0,
        at world == 1); every rank regenerates the chunks, keeps the rows of
        its lists, orders them cluster-major (stable: by list, then original
        id, as dataset.cuh:559-592) and encodes their residuals.
+    builder: an insitu_b200.Builder -- k-means, assignment, PQ training and
+    encoding then run in the library's GPU build kernels (exact nearest
+    centroids, fixed-order means) instead of torch.
     Returns device tensors (centroids, codebook, codes, r2o, base_rr) and
     numpy maps (my_lists, local offsets/counts, global offsets/counts)."""
     import shard
@@ -427,14 +433,20 @@ def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0,
     S = min(n, kmeans_sample or 64 * nlist)
     if rank == 0:
         xs = src.rows(0, S)
-        cent = kmeans(xs, nlist, kmeans_iters, seed)
+        if builder is not None:
+            g = _gen(seed, 7, dev)
+            init = torch.randperm(S, generator=g, device=dev)[:nlist]
+            cent = builder.kmeans(xs, xs[init].float(), kmeans_iters)
+        else:
+            cent = kmeans(xs, nlist, kmeans_iters, seed)
         del xs
     else:
         cent = torch.empty((nlist, d), dtype=torch.float32, device=dev)
     if world > 1:
         dist.broadcast(cent, src=0)
     say("k-means")
-    assign_fn = assign_fn or (lambda x, c: assign(x, c))
+    if assign_fn is None:
+        assign_fn = (lambda x, c: builder.assign(x, c)) if builder is not None else (lambda x, c: assign(x, c))
     a = torch.zeros(n, dtype=torch.int32, device=dev)
     for i in range(rank, src.nchunks, world):
         r0, r1 = src.chunk_range(i)
@@ -444,9 +456,17 @@ def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0,
     say("assignment")
     T = min(train_n, n)
     if rank == 0:
-        resid = src.rows(0, T).float() - cent[a[:T].long()]
-        cb = train_pq(resid, M, pq_iters, seed)
-        del resid
+        if builder is not None:
+            xt = src.rows(0, T)
+            g = _gen(seed, 11, dev)
+            init = torch.randperm(T, generator=g, device=dev)[:256]
+            cb = (xt[init].float() - cent[a[init].long()]).reshape(256, M, -1).permute(1, 0, 2).contiguous()
+            cb = builder.pq_train(xt, cent, a[:T].contiguous(), cb, pq_iters)
+            del xt
+        else:
+            resid = src.rows(0, T).float() - cent[a[:T].long()]
+            cb = train_pq(resid, M, pq_iters, seed)
+            del resid
     else:
         cb = torch.empty((M, 256, d // M), dtype=torch.float32, device=dev)
     if world > 1:
@@ -475,11 +495,17 @@ def build_pq_shard(src: RowSource, nlist: int, M: int, seed: int, rank: int = 0,
     ids = ids[order]
     del order
     say("rows")
-    codes = torch.empty((rows.shape[0], M), dtype=torch.uint8, device=dev)
-    bs = 1 << 20
-    for i in range(0, rows.shape[0], bs):
-        resid = rows[i:i + bs].float() - cent[a[ids[i:i + bs]].long()]
-        codes[i:i + bs] = encode_pq(resid, cb)
+    if builder is not None:
+        la = a[ids].contiguous()
+        codes = builder.pq_encode(rows, cent, la, cb) if rows.shape[0] else \
+            torch.empty((0, M), dtype=torch.uint8, device=dev)
+        del la
+    else:
+        codes = torch.empty((rows.shape[0], M), dtype=torch.uint8, device=dev)
+        bs = 1 << 20
+        for i in range(0, rows.shape[0], bs):
+            resid = rows[i:i + bs].float() - cent[a[ids[i:i + bs]].long()]
+            codes[i:i + bs] = encode_pq(resid, cb)
     say("codes")
     cnt = counts_g[my_lists].astype(np.int32)
     off = np.zeros(len(my_lists), np.int64)

@@ -588,7 +588,7 @@ def test_route_fused_large_nlist_d128(cuda_ok, nlist):
     q_int = np.clip(np.round(cent[comp] + 10.0 * g.standard_normal((300, d))), 0, 255).astype(np.float32)
     q_frac = (cent[comp] + 10.0 * g.standard_normal((300, d))).astype(np.float32)
     for q in (q_int, q_frac):
-        for nprobe in (8, 16):
+        for nprobe in (1, 8, 16, 32):
             exp, exp_d = oracle.route_l2_par(q, cent, nprobe)
             k, probes = _route_keys(cent, q, nprobe)
             assert np.array_equal(probes, exp)
