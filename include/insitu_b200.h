@@ -123,7 +123,13 @@ void ivf_unregister_index_instance(unsigned int index_oid);
 /* ======================================================================
  * Coarse routing handle -- cuda/search/cpu_fine/cpu_fine.h:232-278
  * (C++ linkage there; C linkage here, same layout and argument meaning).
+ * The library exports both: C callers use these declarations, C++ runners
+ * the reference's own cpu_fine.h or cpu_fine_b200.h.  A C++ file that
+ * includes cpu_fine_b200.h (or the reference's cpu_fine.h) and this header
+ * defines INSITU_B200_NO_COARSE first, since a function cannot be declared
+ * with both linkages.
  * ====================================================================== */
+#ifndef INSITU_B200_NO_COARSE
 typedef struct CoarseHandle {
     const float* d_centers;   /* borrowed device centroids [n_total_clusters, dim] */
     float* d_centers_norm;    /* owned: here the per-centroid validity (norm >= 1e-6) */
@@ -158,6 +164,7 @@ void coarse_search(const CoarseHandle* h, const float* h_query, int n_query_batc
                    int* h_cluster_ids_out, double* out_coarse_ms, double* out_h2d_ms, double* out_d2h_ms);
 /* cpu_fine.h:278 -- timing of the calling thread's last coarse_search. */
 const CoarseTimingBreakdown* coarse_get_last_timing(void);
+#endif /* INSITU_B200_NO_COARSE */
 
 /* ======================================================================
  * Index loading (new: the reference loads these inside its runners,
@@ -208,6 +215,37 @@ int ivf_set_shard(void* idx_ctx, int nlist_global, const int* local_to_global, c
  * the mask.
  */
 int ivf_set_deleted(void* idx_ctx, const unsigned char* deleted, long long n);
+
+/* ======================================================================
+ * The reference's index file formats (host code):
+ *   centroids [nlist:i32][dim:i32][f32 ...]            updates/pq_update.cu:46
+ *   assign    [n:i64][i32 ...]                         updates/pq_update.cu:47
+ *   codebook  [M:i32][K:i32][dsub:i32][pad:i32][f32 M*K*dsub]
+ *                                        scripts/train_ivfpq_residual.py:209-213
+ *   codes     [n:i64][M:i32][pad:i32][u8 n*M], cluster-major  (:304-307)
+ *   u8bin / fbin [n:i32][d:i32][payload]  (DiskANN)    updates/io.h:183-294
+ *   gt        [n:i32][k:i32][i32 n*k]                  scripts/gen_gt_fast.py:34-38
+ * Readers return the payload's element count; with out == NULL they read the
+ * header only, else out must hold cap >= count elements.  -1 on error
+ * (message in ivf_global_last_error()).  Writers return IVF_OK or -1.
+ * ====================================================================== */
+long long ivf_read_centroids(const char* path, float* out, long long cap, int* nlist, int* dim);
+long long ivf_read_assign(const char* path, int* out, long long cap, long long* n);
+long long ivf_read_codebook(const char* path, float* out, long long cap, int* M, int* K, int* dsub);
+long long ivf_read_codes(const char* path, unsigned char* out, long long cap, long long* n, int* M);
+long long ivf_read_u8bin(const char* path, unsigned char* out, long long cap, long long* n, int* d);
+long long ivf_read_fbin(const char* path, float* out, long long cap, long long* n, int* d);
+long long ivf_read_gt(const char* path, int* out, long long cap, long long* n, int* k);
+int ivf_write_centroids(const char* path, const float* centroids, int nlist, int dim);
+int ivf_write_assign(const char* path, const int* assign, long long n);
+int ivf_write_codebook(const char* path, const float* codebook, int M, int K, int dsub);
+int ivf_write_codes(const char* path, const unsigned char* codes, long long n, int M);
+/* residual-PQ index straight from the reference's files: centroids, codebook,
+ * cluster-major codes, assignment and the uint8 base rows (u8bin, original
+ * order), laid out by the stable reorder of the assignment -- what
+ * updates/pq_update.cu:676-713 loads; reported ids are original ids */
+int ivf_pq_load_files(void* idx_ctx, const char* centroids_path, const char* codebook_path, const char* codes_path,
+                      const char* assign_path, const char* base_u8bin_path);
 
 /* ======================================================================
  * Index build on the GPU (the reference builds offline: k-means in

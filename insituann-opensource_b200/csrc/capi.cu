@@ -1764,6 +1764,8 @@ void coarse_handle_init(CoarseHandle* h, const float* d_centers, int n_total_clu
             rs->x->nlist = rs->x->nlist_global = n_total_clusters;
             rs->x->d = dim;
             rs->x->kind = kKindF32;
+            prepare_route_tc(rs->x, n_total_clusters, dim);      // tensor-core routing where the shape allows
+            ck(cudaDeviceSynchronize(), "routing operands");
             for (auto& e : rs->ev) ck(cudaEventCreate(&e), "cudaEventCreate");
         } catch (...) {
             if (rs->x) {
@@ -1844,5 +1846,23 @@ void coarse_search(const CoarseHandle* h, const float* h_query, int n_query_batc
 }
 
 const CoarseTimingBreakdown* coarse_get_last_timing(void) { return &g_coarse_timing; }
+
+}  // extern "C"
+
+// The C++-linkage names of the same functions (cpp_abi.cu) forward here; the
+// handle and timing structs have the same layout in both headers.
+namespace isb {
+void coarse_init_fwd(void* h, const float* d_centers, int n, int dim) {
+    coarse_handle_init(static_cast<CoarseHandle*>(h), d_centers, n, dim);
+}
+void coarse_release_fwd(void* h) { coarse_handle_release(static_cast<CoarseHandle*>(h)); }
+void coarse_search_fwd(const void* h, const float* q, int nq, int np, int mode, int* out, double* a, double* b2,
+                       double* c) {
+    coarse_search(static_cast<const CoarseHandle*>(h), q, nq, np, mode, out, a, b2, c);
+}
+const void* coarse_timing_fwd() { return coarse_get_last_timing(); }
+}  // namespace isb
+
+extern "C" {
 
 }  // extern "C"

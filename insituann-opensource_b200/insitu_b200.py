@@ -44,6 +44,9 @@ EXPORTS = [
     "ivf_last_error", "ivf_global_last_error",
     "ivf_kernel_launches", "ivf_batch_profile", "ivf_batch_stage_ms", "ivf_u8_search_noalloc",
     "ivf_load_centroids", "ivf_assign", "ivf_build_reorder", "ivf_kmeans_update", "ivf_pq_train", "ivf_pq_encode",
+    "ivf_read_centroids", "ivf_read_assign", "ivf_read_codebook", "ivf_read_codes", "ivf_read_u8bin",
+    "ivf_read_fbin", "ivf_read_gt", "ivf_write_centroids", "ivf_write_assign", "ivf_write_codebook",
+    "ivf_write_codes", "ivf_pq_load_files",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
     "cuda_pipeline_init", "cuda_pipeline_flush", "cuda_pipeline_flush_vectors_only", "cuda_pipeline_free",
@@ -113,6 +116,18 @@ _SIGS = {
     "ivf_kmeans_update": ([vp, i32, i64, i32, vp, i32, vp, vp], i32),
     "ivf_pq_train": ([vp, i32, i64, i32, vp, vp, i32, i32, vp, vp], i32),
     "ivf_pq_encode": ([vp, i32, i64, i32, vp, vp, vp, vp, i32, vp, vp], i32),
+    "ivf_read_centroids": ([C.c_char_p, vp, i64, vp, vp], i64),
+    "ivf_read_assign": ([C.c_char_p, vp, i64, vp], i64),
+    "ivf_read_codebook": ([C.c_char_p, vp, i64, vp, vp, vp], i64),
+    "ivf_read_codes": ([C.c_char_p, vp, i64, vp, vp], i64),
+    "ivf_read_u8bin": ([C.c_char_p, vp, i64, vp, vp], i64),
+    "ivf_read_fbin": ([C.c_char_p, vp, i64, vp, vp], i64),
+    "ivf_read_gt": ([C.c_char_p, vp, i64, vp, vp], i64),
+    "ivf_write_centroids": ([C.c_char_p, vp, i32, i32], i32),
+    "ivf_write_assign": ([C.c_char_p, vp, i64], i32),
+    "ivf_write_codebook": ([C.c_char_p, vp, i32, i32, i32], i32),
+    "ivf_write_codes": ([C.c_char_p, vp, i64, i32], i32),
+    "ivf_pq_load_files": ([vp, C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p], i32),
 }
 
 STAGES = ("route", "worklist", "scan", "select", "rerank")
@@ -216,6 +231,13 @@ class Index:
         self._check(self.L.ivf_pq_load(self.h, _p(cent), _p(cb), M, K, dsub, _p(codes), _p(offsets), _p(counts),
                                        _p(r2o), _p(bu), _p(bf), counts.shape[0], n, d))
         self.kind, self.d, self.nlist, self.f32 = "pq", d, counts.shape[0], bf is not None
+        return self
+
+    def load_pq_files(self, centroids_path, codebook_path, codes_path, assign_path, base_u8bin_path):
+        """a residual-PQ index from the reference's files (ivf_pq_load_files)"""
+        self._check(self.L.ivf_pq_load_files(self.h, centroids_path.encode(), codebook_path.encode(),
+                                             codes_path.encode(), assign_path.encode(), base_u8bin_path.encode()))
+        self.kind = "pq"
         return self
 
     def set_shard(self, nlist_global, local_to_global, key_offsets=None):
@@ -415,6 +437,99 @@ class Batch:
             self.close()
         except Exception:
             pass
+
+
+# ---- the reference's index file formats (host code, no device needed) ----
+def _err(L):
+    return L.ivf_global_last_error().decode()
+
+
+def read_centroids(path):
+    L = load_library()
+    nl, d = C.c_int(0), C.c_int(0)
+    if L.ivf_read_centroids(path.encode(), None, 0, C.byref(nl), C.byref(d)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty((nl.value, d.value), np.float32)
+    if L.ivf_read_centroids(path.encode(), _p(out), out.size, C.byref(nl), C.byref(d)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def read_assign(path):
+    L = load_library()
+    n = C.c_longlong(0)
+    if L.ivf_read_assign(path.encode(), None, 0, C.byref(n)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty(n.value, np.int32)
+    if L.ivf_read_assign(path.encode(), _p(out), out.size, C.byref(n)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def read_codebook(path):
+    L = load_library()
+    M, K, ds = C.c_int(0), C.c_int(0), C.c_int(0)
+    if L.ivf_read_codebook(path.encode(), None, 0, C.byref(M), C.byref(K), C.byref(ds)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty((M.value, K.value, ds.value), np.float32)
+    if L.ivf_read_codebook(path.encode(), _p(out), out.size, C.byref(M), C.byref(K), C.byref(ds)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def read_codes(path):
+    L = load_library()
+    n, M = C.c_longlong(0), C.c_int(0)
+    if L.ivf_read_codes(path.encode(), None, 0, C.byref(n), C.byref(M)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty((n.value, M.value), np.uint8)
+    if L.ivf_read_codes(path.encode(), _p(out), out.size, C.byref(n), C.byref(M)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def read_bin(path, dtype=np.uint8):
+    """DiskANN u8bin (dtype uint8) or fbin (float32) [n, d]"""
+    L = load_library()
+    n, d = C.c_longlong(0), C.c_int(0)
+    fn = L.ivf_read_u8bin if dtype == np.uint8 else L.ivf_read_fbin
+    if fn(path.encode(), None, 0, C.byref(n), C.byref(d)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty((n.value, d.value), dtype)
+    if fn(path.encode(), _p(out), out.size, C.byref(n), C.byref(d)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def read_gt(path):
+    L = load_library()
+    n, k = C.c_longlong(0), C.c_int(0)
+    if L.ivf_read_gt(path.encode(), None, 0, C.byref(n), C.byref(k)) < 0:
+        raise InsituError(-1, _err(L))
+    out = np.empty((n.value, k.value), np.int32)
+    if L.ivf_read_gt(path.encode(), _p(out), out.size, C.byref(n), C.byref(k)) < 0:
+        raise InsituError(-1, _err(L))
+    return out
+
+
+def write_index_files(prefix, centroids=None, assign=None, codebook=None, codes=None):
+    """writes the given arrays in the reference formats as prefix + {centroids,assign,codebook,codes}.bin"""
+    L = load_library()
+    rc = 0
+    if centroids is not None:
+        c = _c(centroids, np.float32)
+        rc |= L.ivf_write_centroids((prefix + "centroids.bin").encode(), _p(c), c.shape[0], c.shape[1])
+    if assign is not None:
+        a = _c(assign, np.int32)
+        rc |= L.ivf_write_assign((prefix + "assign.bin").encode(), _p(a), a.shape[0])
+    if codebook is not None:
+        cb = _c(codebook, np.float32)
+        rc |= L.ivf_write_codebook((prefix + "codebook.bin").encode(), _p(cb), *cb.shape)
+    if codes is not None:
+        cd = _c(codes, np.uint8)
+        rc |= L.ivf_write_codes((prefix + "codes.bin").encode(), _p(cd), cd.shape[0], cd.shape[1])
+    if rc:
+        raise InsituError(-1, _err(L))
 
 
 class Builder:
