@@ -629,8 +629,8 @@ def main():
                                                  "version": 3}
         out_ids = torch.empty((qo, k), dtype=torch.int32, device=dev)
         out_dist = torch.empty((qo, k), dtype=torch.float32, device=dev)
-        all_ids = torch.empty((N * qo, k), dtype=torch.int32, device=dev)
-        all_dist = torch.empty((N * qo, k), dtype=torch.float32, device=dev)
+        own_packed = torch.empty((qo, k), dtype=torch.int64, device=dev)
+        all_packed = torch.empty((N * qo, k), dtype=torch.int64, device=dev)
 
     def step(np_=nprobe, marks=None):
         batch.stage1_prepare_device(q_dev.data_ptr(), nq)
@@ -673,14 +673,14 @@ def main():
             batch.pq_shard_final(topk_r.data_ptr(), N, qo, k, False)
             batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
             mark("final")
-            shard.gather_results(dist, out_ids, out_dist, all_ids, all_dist)
+            shard.gather_results_packed(dist, out_ids, out_dist, own_packed, all_packed)
             mark("gather results")
 
     def results():
         if N == 1:
             return batch.get_results(nq, k)
         torch.cuda.synchronize()
-        return all_ids.reshape(nq, k).cpu().numpy(), all_dist.reshape(nq, k).cpu().numpy()
+        return shard.unpack_results(all_packed.reshape(nq, k).cpu().numpy())
 
     def barrier():
         torch.cuda.synchronize()
@@ -796,6 +796,7 @@ def main():
     hq = torch.from_numpy(q_np).pin_memory()
     h_ids = torch.empty((nq, k), dtype=torch.int32).pin_memory()
     h_dist = torch.empty((nq, k), dtype=torch.float32).pin_memory()
+    h_packed = torch.empty((nq, k), dtype=torch.int64).pin_memory() if N > 1 else None
 
     # N = 1: two batch contexts in flight, as the reference's pipeline API is
     # meant to be driven -- while the host waits for one batch's results
@@ -823,8 +824,7 @@ def main():
             step()
             if rank == 0:
                 with torch.cuda.stream(ext):
-                    h_ids.copy_(all_ids.reshape(nq, k), non_blocking=True)
-                    h_dist.copy_(all_dist.reshape(nq, k), non_blocking=True)
+                    h_packed.copy_(all_packed.reshape(nq, k), non_blocking=True)
             ext.synchronize()
 
     e2e_run(args.warmup)

@@ -10,7 +10,8 @@ bytes (LPT), and one query batch moves through three collectives:
   2. every rank's per-query stage-1 lists (ADC key, exact key) are sent to the
      rank that owns the query (block partition of the batch) with one
      all-to-all, and the owner merges them (ivf_pq_merge_shards);
-  3. the owners' top-k are all-gathered.
+  3. the owners' top-k are all-gathered, one int64 per result
+     ((distance bits << 32) | id, gather_results_packed).
 
 The phased protocol (ivf_pq_shard_* entry points) replaces step 2 by:
 
@@ -77,6 +78,25 @@ def gather_results(dist, ids_local, dist_local, ids_all, dist_all):
     dist.all_gather_into_tensor(ids_all, ids_local)
     dist.all_gather_into_tensor(dist_all, dist_local)
     return ids_all.reshape(-1, ids_local.shape[1]), dist_all.reshape(-1, dist_local.shape[1])
+
+
+def gather_results_packed(dist, ids_local, dist_local, packed_local, packed_all):
+    """owners' [qo, k] results -> [world * qo, k] on every rank with one
+    all-gather: each result travels as (distance bits << 32) | id (int64)."""
+    import torch
+
+    packed_local.copy_((dist_local.view(torch.int32).to(torch.int64) << 32) |
+                       (ids_local.to(torch.int64) & 0xFFFFFFFF))
+    dist.all_gather_into_tensor(packed_all, packed_local)
+    return packed_all
+
+
+def unpack_results(packed):
+    """int64 (distance bits << 32) | id -> (ids int32, distances float32), NumPy"""
+    p = np.asarray(packed, np.int64)
+    ids = (p & 0xFFFFFFFF).astype(np.uint32).view(np.int32)
+    dd = ((p >> 32) & 0xFFFFFFFF).astype(np.uint32).view(np.float32)
+    return ids, dd
 
 
 def exchange_bounds(dist, bounds):

@@ -317,10 +317,11 @@ def gt_keys(base: torch.Tensor, q: torch.Tensor, k: int, ids: Optional[torch.Ten
             batch_rows: int = 1 << 15) -> torch.Tensor:
     """Exact top-k of q against the rows of base as keys (distance bits << 32) | id, ascending.
 
-    uint8 rows: the distance is the exact integer |q|^2 + |x|^2 - 2 q.x; q.x
-    comes from an fp32 GEMM of integer operands, which is exact (every
-    partial sum is an integer below 128 * 255^2 < 2^24 and TF32 is off), and
-    the three terms are combined in int64.  fp32 rows: fp32 |q|^2 + |x|^2 -
+    uint8 rows: the distance is the exact integer |q|^2 + |x|^2 - 2 q.x; on a
+    GPU q.x comes from an int8 tensor-core GEMM of the values shifted by -128
+    (exact int32), elsewhere from an fp32 GEMM of integer operands, which is
+    exact too (every partial sum is an integer below 128 * 255^2 < 2^24 and
+    TF32 is off); the terms are combined in int64.  fp32 rows: fp32 |q|^2 + |x|^2 -
     2 q.x, clamped at 0.  ids [n] are the rows' original ids (default: the
     row index).  Ties go to the smaller id."""
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -328,6 +329,14 @@ def gt_keys(base: torch.Tensor, q: torch.Tensor, k: int, ids: Optional[torch.Ten
     try:
         nq = q.shape[0]
         is_u8 = base.dtype == torch.uint8
+        d = q.shape[1]
+        # uint8 on a GPU: q.x from an int8 tensor-core GEMM of the values shifted
+        # by -128, exact in int32: q.x = q'.x' + 128 (sum q' + sum x') + 128^2 d
+        int8 = (is_u8 and q.is_cuda and hasattr(torch, "_int_mm") and nq > 16 and d % 8 == 0
+                and bool((q == q.round()).all()) and batch_rows % 8 == 0)
+        if int8:
+            q8 = (q.round().clamp(0, 255).to(torch.int32) - 128).to(torch.int8).contiguous()
+            sq = q8.to(torch.int64).sum(1)
         qf = q.float()
         if is_u8:
             qn = (qf * qf).sum(1).round().long()
@@ -335,18 +344,25 @@ def gt_keys(base: torch.Tensor, q: torch.Tensor, k: int, ids: Optional[torch.Ten
             qn = (qf * qf).sum(1)
         best = torch.full((nq, k), (1 << 63) - 1, dtype=torch.int64, device=q.device)
         for i in range(0, base.shape[0], batch_rows):
-            xb = base[i:i + batch_rows].float()
-            dot = qf @ xb.T
-            if is_u8:
-                xn = (xb * xb).sum(1).round().long()
-                dd = qn[:, None] + xn[None, :] - 2 * dot.round().long()          # exact, < 2^31
+            nb = min(batch_rows, base.shape[0] - i)
+            if int8 and nb % 8 == 0:
+                x8 = (base[i:i + nb].to(torch.int32) - 128).to(torch.int8).contiguous()
+                sx = x8.to(torch.int64).sum(1)
+                dot = torch._int_mm(q8, x8.T).to(torch.int64) + 128 * (sq[:, None] + sx[None, :]) + 128 * 128 * d
+                xw = base[i:i + nb].to(torch.int64)
+                dd = qn[:, None] + (xw * xw).sum(1)[None, :] - 2 * dot
             else:
-                dd = (qn[:, None] + (xb * xb).sum(1)[None, :] - 2.0 * dot).clamp_min(0.0)
-                dd = dd.view(torch.int32).long()                                 # non-negative: bits order as values
-            rid = (torch.arange(i, i + xb.shape[0], device=q.device) if ids is None
-                   else ids[i:i + xb.shape[0]].long())
+                xb = base[i:i + nb].float()
+                dot = qf @ xb.T
+                if is_u8:
+                    xn = (xb * xb).sum(1).round().long()
+                    dd = qn[:, None] + xn[None, :] - 2 * dot.round().long()          # exact, < 2^31
+                else:
+                    dd = (qn[:, None] + (xb * xb).sum(1)[None, :] - 2.0 * dot).clamp_min(0.0)
+                    dd = dd.view(torch.int32).long()                             # non-negative: bits order as values
+            rid = (torch.arange(i, i + nb, device=q.device) if ids is None else ids[i:i + nb].long())
             key = (dd << 32) | rid[None, :]
-            kb = min(k, xb.shape[0])
+            kb = min(k, nb)
             vk, _ = torch.topk(key, kb, dim=1, largest=False)
             best, _ = torch.sort(torch.cat([best, vk], 1), dim=1)
             best = best[:, :k].contiguous()

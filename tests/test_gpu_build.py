@@ -100,3 +100,14 @@ def test_pq_encode_and_train(cuda_ok, d, M):
             if len(rows):
                 exp[m, c] = (resid[rows, m, :].astype(np.float64).sum(0) / len(rows)).astype(np.float32)
     np.testing.assert_allclose(cb1, exp, rtol=1e-6, atol=1e-6)
+
+
+def test_ground_truth_int8_path_equals_exact(cuda_ok):
+    """synth.gt_keys on a GPU (int8 tensor-core q.x) equals the CPU keys
+    (fp32 products of integers) bit for bit, ties included."""
+    base = synth.mixture_u8(20000, 128, 20, 10.0, seed=91)
+    base[100:140] = base[99]
+    q = synth.mixture_u8(64, 128, 20, 10.0, seed=91, stream_base=1 << 20).float()
+    cpu = synth.gt_keys(base, q, 10, batch_rows=4096)
+    gpu = synth.gt_keys(base.cuda(), q.cuda(), 10, batch_rows=4096).cpu()
+    assert torch.equal(cpu, gpu)

@@ -184,11 +184,13 @@ def _phased_worker(rank, world, port, data, out):
         for j, key in enumerate(e):
             ids[i, j] = int(key & np.uint64(0xFFFFFFFF))
             dd[i, j] = float(int(key >> np.uint64(32)))
-    ids_all = torch.empty((world * qo, k), dtype=torch.int32)
-    d_all = torch.empty((world * qo, k), dtype=torch.float32)
-    gi, gd = shard.gather_results(dist, torch.from_numpy(ids), torch.from_numpy(dd), ids_all, d_all)
+    # the results travel as one int64 per entry (bench.py's sharded step)
+    own = torch.empty((qo, k), dtype=torch.int64)
+    allp = torch.empty((world * qo, k), dtype=torch.int64)
+    shard.gather_results_packed(dist, torch.from_numpy(ids), torch.from_numpy(dd), own, allp)
+    gi, gd = shard.unpack_results(allp.numpy())
     if rank == 0:
-        out.put((gi.numpy(), gd.numpy()))
+        out.put((gi, gd))
     dist.barrier()
     dist.destroy_process_group()
 
