@@ -569,6 +569,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     N = world
+    if N > 1:
+        # the phased sharded search keeps a whole 10k-query batch in one
+        # sub-batch; at c2 its candidate buffers pass the 6 GB default scratch
+        os.environ.setdefault("INSITU_SCRATCH_MB", "24576")
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if N > 1:

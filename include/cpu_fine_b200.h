@@ -7,6 +7,8 @@
  *   coarse_search, coarse_get_last_timing  -- cuda/search/cpu_fine/cpu_fine.h:232-278
  *   ivftensor::cpu_fine::cpu_fine_kernel_v3_u8[_touched]  -- cpu_fine_u8.h:47-77
  *   ivftensor::cpu_fine::cpu_fine_kernel_pq_resid          -- cpu_fine_pq_resid.h:69-94
+ *   ivf_init_streaming_upload, ivf_append_cluster_data,
+ *   ivf_finalize_streaming_upload                          -- cuda/search/ivf_search.cuh:330-355
  *
  * Same names, argument order, types and return meaning as the reference
  * (the C++ symbols are mangled identically).  The routing and the fine
@@ -62,6 +64,16 @@ void coarse_handle_release(CoarseHandle* h);
 void coarse_search(const CoarseHandle* h, const float* h_query, int n_query_batch, int n_probes, int distance_mode,
                    int* h_cluster_ids_out, double* out_coarse_ms, double* out_h2d_ms, double* out_d2h_ms);
 const CoarseTimingBreakdown* coarse_get_last_timing();
+
+/* Streaming upload of an fp32 index -- cuda/search/ivf_search.cuh:330-355 (C++
+ * linkage there and here): the rows arrive cluster by cluster from the host,
+ * finalize takes the centroids.  The index then serves
+ * ivf_pipeline_stage2_compute with distance_mode 0 (L2) or 1 (cosine), routed
+ * by cosine as the reference routes this path. */
+void ivf_init_streaming_upload(void* idx_ctx_ptr, int n_total_clusters, int n_total_vectors, int n_dim);
+void ivf_append_cluster_data(void* idx_ctx_ptr, int cluster_id, float* host_vector_data, int count,
+                             int start_offset_idx);
+void ivf_finalize_streaming_upload(void* idx_ctx_ptr, float* center_data_flat, int total_vectors_check);
 
 namespace ivftensor {
 namespace cpu_fine {

@@ -64,11 +64,14 @@ void ivf_destroy_index_context(void* idx_ctx);
 
 /*
  * ivf_search.cuh:236-244 -- adopt caller-allocated device arrays of an fp32
- * index (ownership passes to the context, as in ivf_search_separated.cu:141-143).
- * Returns 1 when loaded, 0 when the context already holds an index.  The
- * fp32 fine-search path behind it is outside this library's hot path: the
- * data is adopted and routing works, but ivf_pipeline_stage2_compute on such
- * an index records IVF_EUNSUPPORTED.
+ * index (ownership passes to the context, as in ivf_search_separated.cu:141-143):
+ * list sizes [nlist], cluster-major rows [n, d] (list l starts at the sum of
+ * the sizes before it), centroids [nlist, d].  Returns 1 when loaded, 0 when
+ * the context already holds an index.  ivf_pipeline_stage2_compute on such an
+ * index routes by cosine (as the reference does on this path) and scans by
+ * exact L2 (distance_mode 0) or 1 - cosine (distance_mode 1); results are
+ * row positions.  The streaming upload (cpu_fine_b200.h) builds the same index
+ * from host data.
  */
 int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vectors, float* d_cluster_centers,
                      int n_total_clusters, int n_total_vectors, int n_dim);
@@ -86,7 +89,9 @@ void ivf_pipeline_stage1_prepare(void* batch_ctx, float* query_batch_host, int n
  *   uint8 index: exact int32 search, top-k by (distance, original id);
  *   PQ index:    residual-PQ stage 1 (rerank_n = 512) + exact rerank, with
  *                the published delta segment when one exists.
- * distance_mode must be IVF_DISTANCE_L2 (cosine records IVF_EUNSUPPORTED).
+ *   fp32 index:  cosine routing, exact L2 or cosine scan (see ivf_load_dataset).
+ * distance_mode IVF_DISTANCE_COSINE is served on fp32 indexes only (the others
+ * record IVF_EUNSUPPORTED).
  */
 void ivf_pipeline_stage2_compute(void* batch_ctx, void* idx_ctx, int n_query, int n_probes, int k,
                                  int distance_mode);
@@ -302,6 +307,18 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
                          const long long* offsets, const long long* key_offsets, const uint8_t* raw_u8,
                          const float* raw_f32, long long n_delta);
 int ivf_pq_clear_delta(void* idx_ctx);
+/*
+ * Online insert (the pipeline the reference's README describes as not
+ * released, README.md:16-24): n new vectors d_x [n, d] -- device rows, uint8
+ * (x_is_u8 = 1) or fp32 as the index's rerank rows -- with reported ids
+ * (host [n]) join the delta segment.  Each row is assigned to its nearest
+ * centroid by the exact routing (n_probes = 1), its residual is encoded with
+ * the index's codebook (the build kernels of ivf_pq_encode), and the grown
+ * segment is published in one step: a concurrent search sees all of an
+ * insert or none of it.  Within a list, older delta rows come first, then
+ * the new ones in insertion order.  Whole (unsharded) indexes only.
+ */
+int ivf_pq_insert(void* idx_ctx, const void* d_x, int x_is_u8, const int* ids, long long n);
 
 /* ======================================================================
  * Search (new, explicit parameters)

@@ -109,10 +109,21 @@ struct IndexCtx {
     float* tc_cne = nullptr;     // the same per tile row, +inf for invalid lists and padding
     float* tc_cnmax = nullptr;   // largest squared norm of a valid centroid
     int M = 0, dsub = 0;
+    float* f32_rows = nullptr;   // fp32 index (ivf_load_dataset / streaming upload): cluster-major rows
+    float* f32_norms = nullptr;  // and their L2 norms (cosine)
+    // streaming upload in progress (ivf_init_streaming_upload .. finalize)
+    bool su_active = false;
+    std::vector<int32_t> su_counts;
+    std::vector<int64_t> su_offsets;
     float* codebook = nullptr;
     float* codebook_t = nullptr;   // [256, M, dsub]
     Segment main, delta;
     bool has_delta = false;
+    // host copy of the published delta segment in delta-position order (list
+    // major), kept so ivf_pq_insert can grow it
+    std::vector<uint8_t> h_dcodes, h_draw_u8;
+    std::vector<float> h_draw_f32;
+    std::vector<int32_t> h_dids, h_dcounts;
     int nlist_global = 0;        // == nlist unless the index is a shard
     int32_t* l2g = nullptr;      // [nlist] local -> global list id (shards)
     int32_t* g2l = nullptr;      // [nlist_global] global -> local list id or -1 (shards)
@@ -341,7 +352,7 @@ void check_shape(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k) {
 
 // top-nprobe of the staged queries over the index's (local) centroids.
 // keys != nullptr: write sorted keys with global list ids instead of probes.
-void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
+void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys, bool cosine = false) {
     require(x->nlist_global >= nprobe || keys, "n_probes > n_total_clusters");
     const int L = std::min(nprobe, 2048);
     require(L == nprobe, "n_probes > 2048 is not supported");
@@ -350,7 +361,7 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
     // which the fine-search stages do not reset
     int* rflag = b->overflow + 1;
     ck(cudaMemsetAsync(rflag, 0, sizeof(int), b->st), "memset");
-    const int mode = x->tc_ops ? route_tc_mode() : 0;
+    const int mode = (x->tc_ops && !cosine) ? route_tc_mode() : 0;
     if ((mode == 1 || mode == 2) && route_tc_fused_usable(x->d, x->nlist, nprobe)) {
         // one tcgen05 sweep, no distance matrix; the per-split keys bound the sub-batch
         const int splits = route_tc_fused_splits(nq, x->nlist);
@@ -383,7 +394,10 @@ void do_route(BatchCtx* b, IndexCtx* x, int nq, int nprobe, uint64_t* keys) {
                    "route_rescore");
                 continue;
             }
-            ck(route_distances(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances");
+            if (cosine)
+                ck(route_distances_cos(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances_cos");
+            else
+                ck(route_distances(qs, n, x->cent, x->valid, x->nlist, x->d, dist, b->st), "route_distances");
             if (keys) {
                 ck(route_select(dist, n, x->nlist, nprobe, x->l2g, nullptr, nullptr, keys + (size_t)s * nprobe,
                                 b->st),
@@ -486,6 +500,52 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
                                          b->out_dist + (size_t)s * k, b->st),
                    "keys_to_exact_results");
         }
+    }
+    queue_overflow_check(b);
+    b->res_nq = nq;
+    b->res_k = k;
+}
+
+// exact fp32 search (L2, or cosine) on the batch probes of an fp32 index
+void run_f32(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, bool cosine) {
+    require(x->kind == kKindF32 && x->f32_rows, "index is not an fp32 index", IVF_ESTATE);
+    require(x->d <= 512, "fp32 search needs d <= 512");
+    require_probes(b, nq, nprobe);
+    const int cap = nprobe * ceil_div(std::max(x->main.max_count, 1), kExactScanChunk) *
+                    std::min(k, kExactScanChunk);
+    size_t per_q = (size_t)cap * 8 + (size_t)k * 8 + 16;
+    int nsub = (int)std::max<size_t>(1, std::min<size_t>((size_t)std::max(nq, 1), scratch_budget() / per_q));
+    void* tmp;
+    size_t tmp_bytes;
+    WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes, false);
+    CandBuf cb{};
+    cb.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap);
+    cb.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
+    cb.thr = ensure<unsigned long long>(b, b->thr_m, (size_t)nsub);
+    cb.overflow = b->overflow;
+    cb.cap = cap;
+    cb.R = k;
+    uint64_t* topk = ensure<uint64_t>(b, b->exk, (size_t)nsub * k);
+    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    for (int s = 0; s < nq; s += nsub) {
+        int n = std::min(nsub, nq - s);
+        {
+            StageScope stage(b, IVF_STAGE_WORKLIST);
+            ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
+                              tmp, tmp_bytes, b->st),
+               "build_worklist");
+            ck(reset_candidates(cb, n, b->st), "reset_candidates");
+        }
+        {
+            StageScope stage(b, IVF_STAGE_SCAN);
+            ck(f32_scan(b->q + (size_t)s * x->d, x->d, x->f32_rows, x->f32_norms, x->main.view(), cosine ? 1 : 0, wl,
+                        n * nprobe, cb, b->counter, b->st),
+               "f32_scan");
+        }
+        StageScope stage(b, IVF_STAGE_SELECT);
+        ck(select_top_r(cb, n, topk, b->st), "select_top_r");
+        ck(merge_keys(topk, n, k, k, 0, b->out_ids + (size_t)s * k, b->out_dist + (size_t)s * k, nullptr, b->st),
+           "merge_keys");
     }
     queue_overflow_check(b);
     b->res_nq = nq;
@@ -717,6 +777,100 @@ ShardPlan shard_plan(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int R) {
 
 }  // namespace
 
+namespace {
+
+// An fp32 index over cluster-major rows already on the device (the reference's
+// ivf_load_dataset / streaming upload): counts [nlist] (device, adopted),
+// offsets as the running sum of counts, per-row norms, centroid validity and
+// the routing operands.
+void adopt_f32_lists(IndexCtx* x, int* d_counts, float* d_rows, int nlist, long long n, int d,
+                     const int64_t* h_offsets = nullptr) {
+    std::vector<int32_t> hc((size_t)nlist);
+    ck(cudaMemcpy(hc.data(), d_counts, sizeof(int32_t) * hc.size(), cudaMemcpyDeviceToHost), "counts D2H");
+    std::vector<int64_t> off((size_t)nlist, 0);
+    int maxc = 0;
+    for (int l = 0; l < nlist; ++l) {
+        require(hc[l] >= 0, "negative list size");
+        if (h_offsets) off[l] = h_offsets[l];
+        else if (l) off[l] = off[l - 1] + hc[l - 1];
+        require(off[l] >= 0 && off[l] + hc[l] <= n, "a list lies outside [0, n_total_vectors)");
+        maxc = std::max(maxc, hc[l]);
+    }
+    x->main.counts = d_counts;
+    x->main.offsets = dcopy(off.data(), off.size(), x->owned);
+    x->main.n = n;
+    x->main.max_count = maxc;
+    x->f32_rows = d_rows;
+    x->f32_norms = dalloc<float>((size_t)std::max<long long>(n, 1), x->owned);
+    ck(f32_row_norms(d_rows, n, d, x->f32_norms, 0), "row norms");
+    x->valid = dalloc<uint8_t>((size_t)nlist, x->owned);
+    ck(route_centroid_valid(x->cent, nlist, d, x->valid, 0), "centroid validity");
+    prepare_route_tc(x, nlist, d);
+    ck(cudaDeviceSynchronize(), "fp32 index");
+    x->nlist = x->nlist_global = nlist;
+    x->d = d;
+    x->n = n;
+    x->kind = kKindF32;
+}
+
+// Publishes a delta segment (the caller holds x->mu): the new segment is built
+// in full first, then swapped in under the exclusive index lock after the
+// device has finished every queued search, so a search sees either the old
+// segment or the new one.  Keeps a host copy for ivf_pq_insert (the arrays may
+// be host or device pointers).
+void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, const int* counts,
+                          const long long* offsets, const long long* key_offsets, const uint8_t* raw_u8,
+                          const float* raw_f32, long long n_delta) {
+    require(x->kind == kKindPQ, "publish needs a residual-PQ index", IVF_ESTATE);
+    require(n_delta >= 0, "negative n_delta");
+    require(ids != nullptr || n_delta == 0, "delta ids are required");
+    require(counts && offsets, "delta counts and offsets are required");
+    const bool f32 = x->main.rr_f32 != nullptr;
+    require(n_delta == 0 || (f32 ? raw_f32 != nullptr : raw_u8 != nullptr),
+            "delta rerank rows must match the base type");
+    cudaSetDevice(x->device);
+    Segment s;
+    std::vector<uint8_t> hc((size_t)n_delta * x->M), hu;
+    std::vector<float> hf;
+    std::vector<int32_t> hi((size_t)n_delta), hcnt(counts, counts + x->nlist);
+    try {
+        load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
+        if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
+        else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
+        if (n_delta) {
+            ck(cudaMemcpy(hc.data(), s.data, hc.size(), cudaMemcpyDeviceToHost), "delta copy");
+            ck(cudaMemcpy(hi.data(), s.ids, sizeof(int32_t) * hi.size(), cudaMemcpyDeviceToHost), "delta copy");
+            if (f32) {
+                hf.resize((size_t)n_delta * x->d);
+                ck(cudaMemcpy(hf.data(), s.rr_f32, sizeof(float) * hf.size(), cudaMemcpyDeviceToHost), "delta copy");
+            } else {
+                hu.resize((size_t)n_delta * x->d);
+                ck(cudaMemcpy(hu.data(), s.rr_u8, hu.size(), cudaMemcpyDeviceToHost), "delta copy");
+            }
+        }
+        build_gring(s, counts, x->nlist, x->M, x->d);
+    } catch (...) {
+        s.release();
+        throw;
+    }
+    std::unique_lock<std::shared_mutex> wr(x->rw);
+    cudaError_t e = cudaDeviceSynchronize();                // no queued search still reads the old segment
+    if (e != cudaSuccess) {
+        s.release();
+        ck(e, "cudaDeviceSynchronize");
+    }
+    x->delta.release();
+    x->delta = std::move(s);
+    x->has_delta = n_delta > 0;
+    x->h_dcodes.swap(hc);
+    x->h_dids.swap(hi);
+    x->h_dcounts.swap(hcnt);
+    x->h_draw_u8.swap(hu);
+    x->h_draw_f32.swap(hf);
+}
+
+}  // namespace
+
 extern "C" {
 
 void* ivf_create_index_context(void) {
@@ -767,14 +921,7 @@ int ivf_load_dataset(void* idx_ctx, int* d_cluster_size, float* d_cluster_vector
         x->owned.push_back(d_cluster_vectors);
         x->cent = d_cluster_centers;
         x->owned.push_back(d_cluster_centers);
-        x->valid = dalloc<uint8_t>((size_t)n_total_clusters, x->owned);
-        ck(route_centroid_valid(x->cent, n_total_clusters, n_dim, x->valid, 0), "centroid validity");
-        prepare_route_tc(x, n_total_clusters, n_dim);
-        ck(cudaDeviceSynchronize(), "centroid validity");
-        x->nlist = x->nlist_global = n_total_clusters;
-        x->d = n_dim;
-        x->n = n_total_vectors;
-        x->kind = kKindF32;
+        adopt_f32_lists(x, d_cluster_size, d_cluster_vectors, n_total_clusters, n_total_vectors, n_dim);
         ret = 1;
     });
     return st == IVF_OK ? ret : 0;
@@ -884,10 +1031,18 @@ void ivf_pipeline_stage2_compute(void* batch_ctx, void* idx_ctx, int n_query, in
     guarded(&b->err, [&] {
         IndexCtx* x = as_index(idx_ctx);
         std::shared_lock<std::shared_mutex> rd(x->rw);
-        require(distance_mode == IVF_DISTANCE_L2, "only distance_mode 0 (L2) is supported", IVF_EUNSUPPORTED);
+        require(distance_mode == IVF_DISTANCE_L2 || distance_mode == IVF_DISTANCE_COSINE, "bad distance_mode");
         check_shape(b, x, n_query, n_probes, k);
         cudaSetDevice(b->device);
-        if (x->kind == kKindF32) fail(IVF_EUNSUPPORTED, "fp32 fine search is outside this library");
+        if (x->kind == kKindF32) {
+            // the reference routes this path by cosine in both modes
+            // (ivf_search_separated.cu:477-512), then scans by L2 or cosine
+            do_route(b, x, n_query, n_probes, nullptr, true);
+            run_f32(b, x, n_query, n_probes, k, distance_mode == IVF_DISTANCE_COSINE);
+            return;
+        }
+        require(distance_mode == IVF_DISTANCE_L2, "cosine is served on fp32 indexes (ivf_load_dataset) only",
+                IVF_EUNSUPPORTED);
         do_route(b, x, n_query, n_probes, nullptr);
         if (x->kind == kKindU8) run_u8(b, x, n_query, n_probes, k, nullptr);
         else run_pq(b, x, n_query, n_probes, k, 512, true, 16, nullptr, nullptr, nullptr, nullptr);
@@ -1203,28 +1358,7 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
     }
     return guarded(&x->err, [&] {
         std::lock_guard<std::mutex> lk(x->mu);
-        std::unique_lock<std::shared_mutex> wr(x->rw);
-        require(x->kind == kKindPQ, "publish needs a residual-PQ index", IVF_ESTATE);
-        require(n_delta >= 0, "negative n_delta");
-        require(ids != nullptr, "delta ids are required");
-        const bool f32 = x->main.rr_f32 != nullptr;
-        require(f32 ? raw_f32 != nullptr : raw_u8 != nullptr, "delta rerank rows must match the base type");
-        cudaSetDevice(x->device);
-        ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");  // no search may still read the old segment
-        x->delta.release();
-        x->has_delta = false;
-        Segment s;
-        try {
-            load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
-            if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
-            else s.rr_u8 = dcopy(raw_u8, (size_t)n_delta * x->d, s.owned);
-            build_gring(s, counts, x->nlist, x->M, x->d);
-        } catch (...) {
-            s.release();
-            throw;
-        }
-        x->delta = std::move(s);
-        x->has_delta = n_delta > 0;
+        publish_delta_locked(x, codes, ids, counts, offsets, key_offsets, raw_u8, raw_f32, n_delta);
     });
 }
 
@@ -1242,6 +1376,108 @@ int ivf_pq_clear_delta(void* idx_ctx) {
         ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
         x->delta.release();
         x->has_delta = false;
+        x->h_dcodes.clear();
+        x->h_dids.clear();
+        x->h_dcounts.clear();
+        x->h_draw_u8.clear();
+        x->h_draw_f32.clear();
+    });
+}
+
+int ivf_pq_insert(void* idx_ctx, const void* d_x, int x_is_u8, const int* ids, long long n) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    return guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);          // one insert or publish at a time
+        require(x->kind == kKindPQ, "insert needs a residual-PQ index", IVF_ESTATE);
+        require(x->nlist_global == x->nlist, "insert into a shard is not supported: insert into the whole index");
+        require(n >= 0 && (n == 0 || (d_x && ids)), "bad rows or ids");
+        const bool f32 = x->main.rr_f32 != nullptr;
+        require(f32 ? !x_is_u8 : x_is_u8 != 0, "inserted rows must have the type of the index's rerank rows");
+        if (n == 0) return;
+        cudaSetDevice(x->device);
+        const int d = x->d, M = x->M, nlist = x->nlist;
+        // 1. exact nearest centroid (the routing kernels, n_probes = 1) and 2. the
+        // residual codes, on a private stream; searches keep running meanwhile
+        std::vector<void*> tmp;
+        int32_t* d_assign = dalloc<int32_t>((size_t)n, tmp);
+        uint8_t* d_codes = dalloc<uint8_t>((size_t)n * M, tmp);
+        void* b = ivf_create_batch_context((int)std::min<long long>(n, 65536), d, 1, 1, nlist);
+        std::vector<int32_t> ha((size_t)n);
+        std::vector<uint8_t> hc((size_t)n * M);
+        try {
+            require(b != nullptr, "batch context: " + g_err, IVF_ENOMEM);
+            BatchCtx* bc = static_cast<BatchCtx*>(b);
+            {
+                std::shared_lock<std::shared_mutex> rd(x->rw);
+                for (long long s0 = 0; s0 < n; s0 += bc->max_nq) {
+                    const int m = (int)std::min<long long>(bc->max_nq, n - s0);
+                    ck(stage_rows_f32(d_x, x_is_u8, (size_t)s0 * d, (size_t)m * d, bc->q, bc->st), "stage rows");
+                    do_route(bc, x, m, 1, nullptr);
+                    ck(cudaMemcpyAsync(d_assign + s0, bc->probes, sizeof(int32_t) * (size_t)m,
+                                       cudaMemcpyDeviceToDevice, bc->st),
+                       "assign D2D");
+                }
+                ck(pq_encode_rows(d_x, x_is_u8, n, d, nullptr, x->cent, d_assign, x->codebook, M, d_codes, bc->st),
+                   "pq_encode");
+                ck(cudaMemcpyAsync(ha.data(), d_assign, sizeof(int32_t) * ha.size(), cudaMemcpyDeviceToHost,
+                                   bc->st),
+                   "assign D2H");
+                ck(cudaMemcpyAsync(hc.data(), d_codes, hc.size(), cudaMemcpyDeviceToHost, bc->st), "codes D2H");
+                ck(cudaStreamSynchronize(bc->st), "cudaStreamSynchronize");
+                check_overflow_after_sync(bc);
+            }
+        } catch (...) {
+            if (b) ivf_destroy_batch_context(b);
+            free_all(tmp);
+            throw;
+        }
+        ivf_destroy_batch_context(b);
+        free_all(tmp);
+        const size_t rb = f32 ? sizeof(float) : 1;
+        std::vector<uint8_t> hraw((size_t)n * d * rb);
+        ck(cudaMemcpy(hraw.data(), d_x, hraw.size(), cudaMemcpyDefault), "rows D2H");
+        // 3. the grown segment, list-major; a list keeps its older delta rows
+        // first, then the new ones in insertion order
+        const long long n_old = (long long)x->h_dids.size();
+        std::vector<int32_t> cnt((size_t)nlist, 0);
+        if (n_old) cnt = x->h_dcounts;
+        std::vector<long long> old_off((size_t)nlist, 0);
+        for (int l = 1; l < nlist; ++l) old_off[l] = old_off[l - 1] + cnt[l - 1];
+        std::vector<int32_t> add((size_t)nlist, 0);
+        for (long long i = 0; i < n; ++i) add[ha[i]]++;
+        std::vector<int32_t> ncnt((size_t)nlist);
+        std::vector<long long> noff((size_t)nlist, 0);
+        for (int l = 0; l < nlist; ++l) ncnt[l] = cnt[l] + add[l];
+        for (int l = 1; l < nlist; ++l) noff[l] = noff[l - 1] + ncnt[l - 1];
+        const long long nt = n_old + n;
+        require(nt < (1ll << 31), "delta segment above 2^31 rows");
+        std::vector<uint8_t> codes((size_t)nt * M), raw((size_t)nt * d * rb);
+        std::vector<int32_t> nid((size_t)nt);
+        const uint8_t* oraw = f32 ? reinterpret_cast<const uint8_t*>(x->h_draw_f32.data()) : x->h_draw_u8.data();
+        for (int l = 0; l < nlist; ++l) {
+            const size_t src = (size_t)old_off[l], dst = (size_t)noff[l], c = (size_t)cnt[l];
+            if (!c) continue;
+            std::memcpy(&codes[dst * M], &x->h_dcodes[src * M], c * M);
+            std::memcpy(&raw[dst * d * rb], &oraw[src * d * rb], c * d * rb);
+            std::memcpy(&nid[dst], &x->h_dids[src], c * sizeof(int32_t));
+        }
+        std::vector<long long> cur(noff);
+        for (int l = 0; l < nlist; ++l) cur[l] += cnt[l];
+        for (long long i = 0; i < n; ++i) {
+            const size_t dst = (size_t)cur[ha[i]]++;
+            std::memcpy(&codes[dst * M], &hc[(size_t)i * M], M);
+            std::memcpy(&raw[dst * d * rb], &hraw[(size_t)i * d * rb], d * rb);
+            nid[dst] = ids[i];
+        }
+        // 4. published in one step
+        publish_delta_locked(x, codes.data(), nid.data(), ncnt.data(), noff.data(), nullptr,
+                             f32 ? nullptr : raw.data(), f32 ? reinterpret_cast<const float*>(raw.data()) : nullptr,
+                             nt);
     });
 }
 
@@ -1866,3 +2102,81 @@ const void* coarse_timing_fwd() { return coarse_get_last_timing(); }
 extern "C" {
 
 }  // extern "C"
+
+// ===========================================================================
+// Streaming upload of an fp32 index, cuda/search/ivf_search.cuh:330-355 and
+// ivf_search_separated.cu:166-270 (C++ linkage, as in the reference).  The
+// functions return nothing; failures are recorded on the index context
+// (ivf_last_error) and in ivf_global_last_error().
+// ===========================================================================
+__attribute__((visibility("default"))) void ivf_init_streaming_upload(void* idx_ctx_ptr, int n_total_clusters, int n_total_vectors, int n_dim) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx_ptr);
+    } catch (...) {
+        g_err = "not an index context";
+        return;
+    }
+    guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
+        require(x->kind == kKindEmpty && !x->su_active, "index context already holds an index", IVF_ESTATE);
+        require(n_total_clusters > 0 && n_total_vectors >= 0 && n_dim > 0 && n_dim <= 512, "bad sizes");
+        cudaSetDevice(x->device);
+        x->f32_rows = dalloc<float>((size_t)n_total_vectors * n_dim, x->owned);
+        x->su_counts.assign((size_t)n_total_clusters, 0);
+        x->su_offsets.assign((size_t)n_total_clusters, 0);
+        x->nlist = x->nlist_global = n_total_clusters;
+        x->d = n_dim;
+        x->n = n_total_vectors;
+        x->su_active = true;
+    });
+}
+
+__attribute__((visibility("default"))) void ivf_append_cluster_data(void* idx_ctx_ptr, int cluster_id, float* host_vector_data, int count,
+                             int start_offset_idx) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx_ptr);
+    } catch (...) {
+        g_err = "not an index context";
+        return;
+    }
+    guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        require(x->su_active, "no streaming upload in progress", IVF_ESTATE);
+        require(cluster_id >= 0 && cluster_id < x->nlist, "cluster_id outside [0, n_total_clusters)");
+        require(start_offset_idx >= 0, "negative start offset");
+        const int c = (count > 0 && host_vector_data) ? count : 0;    // no data: an empty cluster
+        require((long long)start_offset_idx + c <= x->n, "cluster data beyond n_total_vectors");
+        cudaSetDevice(x->device);
+        if (c)
+            ck(cudaMemcpy(x->f32_rows + (size_t)start_offset_idx * x->d, host_vector_data,
+                          sizeof(float) * (size_t)c * x->d, cudaMemcpyHostToDevice),
+               "cluster data H2D");
+        x->su_counts[(size_t)cluster_id] = c;
+        x->su_offsets[(size_t)cluster_id] = start_offset_idx;
+    });
+}
+
+__attribute__((visibility("default"))) void ivf_finalize_streaming_upload(void* idx_ctx_ptr, float* center_data_flat, int total_vectors_check) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx_ptr);
+    } catch (...) {
+        g_err = "not an index context";
+        return;
+    }
+    guarded(&x->err, [&] {
+        std::lock_guard<std::mutex> lk(x->mu);
+        std::unique_lock<std::shared_mutex> wr(x->rw);
+        require(x->su_active, "no streaming upload in progress", IVF_ESTATE);
+        require(center_data_flat != nullptr, "null centroids");
+        require(total_vectors_check >= 0 && total_vectors_check <= x->n, "total_vectors_check beyond n_total_vectors");
+        cudaSetDevice(x->device);
+        x->cent = dcopy(center_data_flat, (size_t)x->nlist * x->d, x->owned);
+        int32_t* d_counts = dcopy(x->su_counts.data(), x->su_counts.size(), x->owned);
+        adopt_f32_lists(x, d_counts, x->f32_rows, x->nlist, x->n, x->d, x->su_offsets.data());
+        x->su_active = false;
+    });
+}

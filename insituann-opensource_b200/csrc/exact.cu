@@ -81,6 +81,80 @@ __global__ void __launch_bounds__(kET) exact_scan_kernel(const uint8_t* __restri
 }
 
 // ---------------------------------------------------------------------------
+// fp32 exact fine search (the reference's GPU path for indexes loaded with
+// ivf_load_dataset: cuda/search/ivf_search_separated.cu:417-650,
+// fine/indexed_gemm_{l2,cos}.cu): for every vector of every probed list,
+//   L2:     sum_j (q_j - x_j)^2 in dimension order (fp32, separately rounded);
+//   cosine: 1 - <q, x> / (|q| |x|), <q, x> summed in dimension order, norms as
+//           sqrtf of the sequential sum of squares; clamped at 0, and a vector
+//           or query of zero norm is at distance 1 (cosine 0);
+// keys (distance bits, position) through the shared block filter, so the top-k
+// is by (distance, position).
+// ---------------------------------------------------------------------------
+__global__ void f32_norms_kernel(const float* __restrict__ x, int64_t n, int d, float* __restrict__ out) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float* r = x + (size_t)i * d;
+        float s = 0.f;
+        for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(r[j], r[j]));
+        out[i] = sqrtf(s);
+    }
+}
+
+__global__ void __launch_bounds__(kET) f32_scan_kernel(const float* __restrict__ q, int d, const float* __restrict__ x,
+                                                       const float* __restrict__ xnorm, ListStore ls, int cosine,
+                                                       WorkList wl, CandBuf cb, int* counter) {
+    __shared__ float sq[kEMaxD];
+    __shared__ uint64_t skeys[kEChunk];
+    __shared__ EmitSmem esm;
+    __shared__ int s_item;
+    __shared__ float s_qn;
+    const int tid = threadIdx.x;
+    const int P = *wl.n_pairs;
+    for (;;) {
+        const int it = next_item(counter, P, &s_item);
+        if (it < 0) break;
+        const int qi = wl.pair_q[it], l = wl.pair_l[it];
+        const int count = ls.counts[l];
+        if (count <= 0) continue;
+        const int64_t off = ls.offsets[l];
+        for (int j = tid; j < d; j += kET) sq[j] = q[(size_t)qi * d + j];
+        __syncthreads();
+        if (tid == 0) {
+            float s = 0.f;
+            for (int j = 0; j < d; ++j) s = __fadd_rn(s, __fmul_rn(sq[j], sq[j]));
+            s_qn = sqrtf(s);
+        }
+        __syncthreads();
+        const float qn = s_qn;
+        for (int cs = 0; cs < count; cs += kEChunk) {
+            const int len = min(kEChunk, count - cs);
+            for (int v = tid; v < len; v += kET) {
+                const int64_t pos = off + cs + v;
+                const float* row = x + (size_t)pos * d;
+                float dist;
+                if (cosine) {
+                    float dot = 0.f;
+                    for (int j = 0; j < d; ++j) dot = __fadd_rn(dot, __fmul_rn(sq[j], __ldg(row + j)));
+                    const float den = __fmul_rn(qn, xnorm[pos]);
+                    dist = den > 0.f ? fmaxf(__fsub_rn(1.f, __fdiv_rn(dot, den)), 0.f) : 1.f;
+                } else {
+                    float acc = 0.f;
+                    for (int j = 0; j < d; ++j) {
+                        const float t = __fsub_rn(sq[j], __ldg(row + j));
+                        acc = __fadd_rn(acc, __fmul_rn(t, t));
+                    }
+                    dist = acc;
+                }
+                skeys[v] = (ls.deleted && ls.deleted[pos]) ? kKeyNone : make_key(__float_as_uint(dist), (uint32_t)pos);
+            }
+            __syncthreads();
+            auto keyf = [&](int i) -> uint64_t { return skeys[i]; };
+            block_filter_emit<kET>(keyf, len, cb, qi, esm);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Grouped exact scan: one CTA works on a list and up to kXG queries that probe
 // it, so every list row is read once per group instead of once per query.
 // With |q|^2, |x|^2 and q.x all exact in int32, sum_j (q_j - x_j)^2 =
@@ -383,6 +457,31 @@ cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkLis
         case 16: note_launch(); exact_scan_kernel<16><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
         default: note_launch(); exact_scan_kernel<0><<<grid, kET, 0, st>>>(q_u8, d, ls, wl, cb, work_counter); break;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t f32_row_norms(const float* x, int64_t n, int d, float* out, cudaStream_t st) {
+    if (n <= 0) return cudaSuccess;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 32) blocks = 148 * 32;
+    note_launch();
+    f32_norms_kernel<<<(int)blocks, 256, 0, st>>>(x, n, d, out);
+    return cudaGetLastError();
+}
+
+cudaError_t f32_scan(const float* q, int d, const float* x, const float* xnorm, ListStore ls, int cosine, WorkList wl,
+                     int max_pairs, CandBuf cb, int* work_counter, cudaStream_t st) {
+    if (d <= 0 || d > kEMaxD) return cudaErrorInvalidValue;
+    if (max_pairs <= 0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(work_counter, 0, sizeof(int), st);
+    if (e) return e;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    int grid = sms * 4;
+    if (grid > max_pairs) grid = max_pairs;
+    note_launch();
+    f32_scan_kernel<<<grid, kET, 0, st>>>(q, d, x, xnorm, ls, cosine, wl, cb, work_counter);
     return cudaGetLastError();
 }
 

@@ -39,6 +39,9 @@ cudaError_t route_centroid_valid(const float* cent, int nlist, int d, uint8_t* v
 // (0xFFFFFFFF for centroids that are not valid): out [nq, nlist].
 cudaError_t route_distances(const float* q, int nq, const float* cent, const uint8_t* valid,
                             int nlist, int d, uint32_t* out, cudaStream_t st);
+// the same for the cosine distance 1 - <q, c> / (|q| |c|) (clamped at 0)
+cudaError_t route_distances_cos(const float* q, int nq, const float* cent, const uint8_t* valid, int nlist, int d,
+                                uint32_t* out, cudaStream_t st);
 // Top-L (dist, id) per row of dist_bits [nq, n] -> ids [nq, L] (+ dist [nq, L] and/or
 // sorted keys [nq, L], each optional).  Column c has id id_map[c] (nullptr: c).
 cudaError_t route_select(const uint32_t* dist_bits, int nq, int n, int L, const int32_t* id_map,
@@ -105,6 +108,12 @@ cudaError_t exact_group_scan(const uint8_t* q_u8, int d, int k, ListStore ls, Wo
                              CandBuf cb, int* work_counter, cudaStream_t st);
 cudaError_t exact_scan(const uint8_t* q_u8, int nq, int d, ListStore ls, WorkList wl, int max_pairs,
                        CandBuf cb, int* work_counter, cudaStream_t st);
+// fp32 rows: out[i] = sqrtf(sum_j x[i][j]^2) (sequential fp32 sum)
+cudaError_t f32_row_norms(const float* x, int64_t n, int d, float* out, cudaStream_t st);
+// exact fp32 fine search over the probed lists of x (cluster-major [n, d]):
+// L2 or (cosine != 0) 1 - cos, keys (distance, position) into cb
+cudaError_t f32_scan(const float* q, int d, const float* x, const float* xnorm, ListStore ls, int cosine, WorkList wl,
+                     int max_pairs, CandBuf cb, int* work_counter, cudaStream_t st);
 
 // ---- index build (build.cu) ---------------------------------------------------
 // out[i] = x[offset + i] as fp32 for i < n (x uint8 when is_u8, else fp32)

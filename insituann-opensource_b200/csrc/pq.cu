@@ -270,6 +270,8 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 struct GroupDesc {
     int64_t pk, koff, goff;
     int count, q[kGQ];
+    int64_t dkoff, dgoff;    // the same list's delta segment (when one is published)
+    int dcount;
 };
 
 __device__ __forceinline__ void desc_stage_a(GroupDesc& g, const WorkList& wl, int it, int NG) {
@@ -283,6 +285,14 @@ __device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, co
     cp_async_4(&g.count, S.counts + l);
     cp_async_8(&g.koff, (S.key_off ? S.key_off : S.offsets) + l);
     cp_async_8(&g.goff, S.gring_off + l);
+    if (p.has_delta) {
+        const ListStore& D = p.delta;
+        cp_async_4(&g.dcount, D.counts + l);
+        cp_async_8(&g.dkoff, (D.key_off ? D.key_off : D.offsets) + l);
+        cp_async_8(&g.dgoff, D.gring_off + l);
+    } else {
+        g.dcount = 0;
+    }
 #pragma unroll
     for (int k = 0; k < kGQ; ++k) {
         if (k < nqg) cp_async_4(&g.q[k], wl.pair_q + p0 + k);
@@ -298,7 +308,7 @@ __device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, co
 //     before the group is even decoded (they are the same for every group);
 //   * the first code tile is requested before the LUT is built, each next
 //     tile one tile ahead, and each chunk's query bounds before its steps.
-template <int M, int DSUB>
+template <int M, int DSUB, bool DELTA>
 __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
                                                           int* counter) {
     using RG = GRing<M>;
@@ -314,6 +324,10 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     __shared__ EmitSmem esm;
     __shared__ int s_item;
     __shared__ __align__(8) GroupDesc s_gd;     // the group this CTA starts next
+    // the current group's main and delta list (count, key offset, tile offset),
+    // kept past the next group's descriptor fetch
+    __shared__ int64_t s_skoff[2], s_sgoff[2];
+    __shared__ int s_scount[2];
     // per-chunk totals and "some sum may pass" bits of the 4 queries, three
     // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
     // barrier, clears buffer (c + 2) % 3 -- last read in chunk c - 1 (done
@@ -325,7 +339,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     const bool builder = tid < kCStep * M;
     const int ps = tid % M, mcol = RG::inv(ps), c0 = tid / M;
     const int NG = *wl.n_groups;
-    const int total = p.has_delta ? 2 * NG : NG;
+    const int total = NG;                    // a group scans its list's main and delta rows
     const int rid = warp * 4 + grp;          // stripe of this lane group
     if (tid < 3 * kGQ) s_cnt[tid / kGQ][tid % kGQ] = 0;
     if (tid < 3) s_any[tid] = 0;
@@ -367,31 +381,51 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
         int nxt = 0;
         if (tid == 0) nxt = atomicAdd(counter, 1);       // used at the end of this group
         if (builder) load_cb(c0);
-        const bool seg_delta = it >= NG;
         const int64_t packed = s_gd.pk;
         const int l = (int)(packed >> 32), nqg = ((int)packed) & 7;
-        const ListStore& SG = seg_delta ? p.delta : p.main;
-        const CandBuf& cb = seg_delta ? cd : cm;
-        const int count = s_gd.count;
+        // the group's list in the main segment and, with the overlay, the same
+        // list's delta rows: both are scanned here with the one LUT (read out of
+        // s_gd before the next group's descriptor rewrites it)
+        const int count_m = s_gd.count, count_d = DELTA ? s_gd.dcount : 0;
+        if (tid == 0) {
+            s_scount[0] = count_m;
+            s_scount[1] = count_d;
+            s_skoff[0] = s_gd.koff;
+            s_sgoff[0] = s_gd.goff;
+            s_skoff[1] = s_gd.dkoff;
+            s_sgoff[1] = s_gd.dgoff;
+        }
         bool fetched = false;            // thread 0: stage A of the next descriptor issued
-        if (count > 0) {
-            const int64_t koff = s_gd.koff;
-            const uint8_t* tiles = SG.gring + s_gd.goff;
-            const int64_t ntiles = gring_tiles(count);
-            // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
-            // multiple of 16, so a stripe starts on a tile) and runs through it
-            // without draining: it finishes vector r*S + x - 7 at step x.
-            // Steps are cut into chunks of kRSteps; after each chunk the CTA
-            // filters the kRRings * kRSteps finished slots.  The longest
-            // stripe (group 0) takes min(S, count) + 7 steps.
-            const int S = gring_stripe(count);
-            const int a = rid * S < count ? rid * S : count;
-            const int wa = warp * 4 * S;
-            const int wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its group 0)
-            const int nchunks = gring_chunks(count);
-            const uint4* lanebase = reinterpret_cast<const uint4*>(tiles) + j;
-            const int64_t T0 = a / 16;
+        bool staged = false;             // thread 0: its stage B issued
+        if (count_m > 0 || count_d > 0) {
             uint32_t w[4 * MPL], wn[4 * MPL];
+            // segment seg's stripes and tiles (from s_gd for the first segment,
+            // before the barrier that publishes the shared copies)
+            auto seg_setup = [&](int seg, bool from_desc, const uint4*& lanebase, int64_t& ntiles, int& S,
+                                 int64_t& T0, int& wsteps, int& nchunks) {
+                const int count = seg ? count_d : count_m;
+                const int64_t goff = from_desc ? (seg ? s_gd.dgoff : s_gd.goff) : s_sgoff[seg];
+                const uint8_t* tiles = (seg ? p.delta.gring : p.main.gring) + goff;
+                ntiles = gring_tiles(count);
+                // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
+                // multiple of 16, so a stripe starts on a tile) and runs through it
+                // without draining: it finishes vector r*S + x - 7 at step x.
+                // Steps are cut into chunks of kRSteps; after each chunk the CTA
+                // filters the kRRings * kRSteps finished slots.  The longest
+                // stripe (group 0) takes min(S, count) + 7 steps.
+                S = gring_stripe(count);
+                const int a = rid * S < count ? rid * S : count;
+                const int wa = warp * 4 * S;
+                wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its group 0)
+                nchunks = gring_chunks(count);
+                lanebase = reinterpret_cast<const uint4*>(tiles) + j;
+                T0 = a / 16;
+            };
+            const uint4* lanebase;
+            int64_t ntiles, T0;
+            int S, wsteps, nchunks;
+            const int seg0 = count_m > 0 ? 0 : 1;
+            seg_setup(seg0, true, lanebase, ntiles, S, T0, wsteps, nchunks);
             load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
             {
                 const float* cv = p.cent + (size_t)l * d;
@@ -403,9 +437,12 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             }
             // the group's bounds, requested before the LUT build and used after it
             uint64_t thr0[kGQ];
+            {
+                const CandBuf& cb0 = seg0 ? cd : cm;
 #pragma unroll
-            for (int k = 0; k < kGQ; ++k)
-                thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + s_gd.q[k])) : 0ull;
+                for (int k = 0; k < kGQ; ++k)
+                    thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb0.thr + s_gd.q[k])) : 0ull;
+            }
             __syncthreads();
             if (builder) {
                 float2 r01[DSUB], r23[DSUB];
@@ -451,7 +488,6 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 fetched = true;
             }
             float2 s01 = make_float2(0.f, 0.f), s23 = make_float2(0.f, 0.f);
-            const uint32_t kbase = (uint32_t)koff;
             // float form of the bounds for the stores' pass test, taken from bounds
             // already in registers (the group's first, then each chunk's cut): a
             // bound only decreases, so an older one only sets more bits.  A bound
@@ -469,6 +505,20 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
                 thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
             };
+            for (int seg = seg0; seg < (DELTA ? 2 : 1); ++seg) {
+            const int count = s_scount[seg];
+            if (count == 0) continue;
+            const CandBuf& cb = seg ? cd : cm;
+            const uint32_t kbase = (uint32_t)s_skoff[seg];
+            if (seg != seg0) {                 // the delta rows after the main list: same LUT
+                seg_setup(seg, false, lanebase, ntiles, S, T0, wsteps, nchunks);
+                load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+#pragma unroll
+                for (int k = 0; k < kGQ; ++k)
+                    thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
+                s01 = make_float2(0.f, 0.f);
+                s23 = make_float2(0.f, 0.f);
+            }
             set_thf(thr0);
             for (int t = 0; t < nchunks; ++t) {
                 uint64_t thr[kGQ];    // read now, used after the steps: a bound only ever decreases
@@ -493,9 +543,10 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 maybe = __reduce_or_sync(0xffffffffu, maybe);
                 if (lane == 0 && (maybe | force)) atomicOr(&s_any[cpar], maybe | force);
                 __syncthreads();
-                if (t == 0 && tid == 0 && fetched) {         // stage A landed long ago
+                if (tid == 0 && fetched && !staged) {         // stage A landed long ago
                     cp_async_wait_all();
                     desc_stage_b(s_gd, p, wl, nxt, NG);
+                    staged = true;
                 }
                 const int cfree = cpar == 0 ? 2 : cpar - 1;      // (cpar + 2) % 3
                 if (tid < kGQ) s_cnt[cfree][tid] = 0;
@@ -565,8 +616,13 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 if (sel) __syncthreads();     // the histograms lived in the slots
                 set_thf(cut);
             }
+            }
         }
         if (tid == 0) {
+            if (fetched && !staged) {          // lists too short for a chunk barrier after the fetch
+                cp_async_wait_all();
+                desc_stage_b(s_gd, p, wl, nxt, NG);
+            }
             if (nxt < total && !fetched) {    // an empty list: fetch the next descriptor now
                 desc_stage_a(s_gd, wl, nxt, NG);
                 cp_async_wait_all();
@@ -579,25 +635,34 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     }
 }
 
-template <int M, int DSUB>
-cudaError_t launch_gring(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
-                         cudaStream_t st) {
+// one launch per search pass: with a published delta segment every group also
+// scans its list's delta rows (the DELTA instantiation)
+template <int M, int DSUB, bool DELTA>
+cudaError_t launch_gring_seg(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
+                             cudaStream_t st) {
     const size_t smem = GRing<M>::smem_bytes();
-    cudaError_t e =
-        cudaFuncSetAttribute(pq_stagger_kernel<M, DSUB>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(pq_stagger_kernel<M, DSUB, DELTA>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_stagger_kernel<M, DSUB>, kRT, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_stagger_kernel<M, DSUB, DELTA>, kRT, smem);
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
-    long long items = (long long)max_groups * (p.has_delta ? 2 : 1);
+    long long items = (long long)max_groups;
     long long grid = (long long)sms * per_sm;
     if (grid > items) grid = items;
     if (grid < 1) grid = 1;
     note_launch();
-    pq_stagger_kernel<M, DSUB><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
+    pq_stagger_kernel<M, DSUB, DELTA><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
     return cudaGetLastError();
+}
+
+template <int M, int DSUB>
+cudaError_t launch_gring(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
+                         cudaStream_t st) {
+    if (p.has_delta) return launch_gring_seg<M, DSUB, true>(p, wl, max_groups, cm, cd, counter, st);
+    return launch_gring_seg<M, DSUB, false>(p, wl, max_groups, cm, cd, counter, st);
 }
 
 template <int MPL>

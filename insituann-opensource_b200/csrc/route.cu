@@ -23,6 +23,31 @@ __global__ void centroid_valid_kernel(const float* __restrict__ cent, int nlist,
     valid[c] = (sqrtf(s) >= 1e-6f) ? 1 : 0;
 }
 
+// Cosine routing distance of the reference's fp32 pipeline
+// (cuda/search/ivf_search_separated.cu:477-512 with
+// coarse/fusion_cos_topk_warpsort.cu:125-135): 1 - <q, c> / (|q| |c|) in fp32,
+// <q, c> summed in dimension order, norms sqrtf of the sequential sums;
+// centroids below 1e-6 norm are not routed; clamped at 0 so that the bits of
+// the distance order as its values.  One thread per (query, centroid); the
+// query row of the CTA's queries is read through L1.
+__global__ void route_cos_kernel(const float* __restrict__ q, int nq, const float* __restrict__ cent,
+                                 const uint8_t* __restrict__ valid, int nlist, int d, uint32_t* __restrict__ out) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, qi = blockIdx.y;
+    if (c >= nlist || qi >= nq) return;
+    const float* qr = q + (size_t)qi * d;
+    const float* cr = cent + (size_t)c * d;
+    float dot = 0.f, qs = 0.f, cs = 0.f;
+    for (int j = 0; j < d; ++j) {
+        const float a = __ldg(qr + j), b = __ldg(cr + j);
+        dot = __fadd_rn(dot, __fmul_rn(a, b));
+        qs = __fadd_rn(qs, __fmul_rn(a, a));
+        cs = __fadd_rn(cs, __fmul_rn(b, b));
+    }
+    const float den = __fmul_rn(sqrtf(qs), sqrtf(cs));
+    const float dist = den > 0.f ? fmaxf(__fsub_rn(1.f, __fdiv_rn(dot, den)), 0.f) : 1.f;
+    out[(size_t)qi * nlist + c] = valid[c] ? __float_as_uint(dist) : 0xFFFFFFFFu;
+}
+
 // 128 queries x 128 centroids per CTA, 256 threads, 8x8 pairs per thread, 16
 // dimensions staged per step.  The centroid tile is staged negated, so q - c
 // is an add (x + (-y) is x - y exactly).  A thread's pairs are float2
@@ -271,6 +296,15 @@ cudaError_t route_distances(const float* q, int nq, const float* cent, const uin
     dim3 grid((nlist + kRB - 1) / kRB, (nq + kRB - 1) / kRB);
     note_launch();
     route_dist_kernel<<<grid, 256, 0, st>>>(q, nq, cent, valid, nlist, d, out);
+    return cudaGetLastError();
+}
+
+cudaError_t route_distances_cos(const float* q, int nq, const float* cent, const uint8_t* valid, int nlist, int d,
+                                uint32_t* out, cudaStream_t st) {
+    if (nq <= 0) return cudaSuccess;
+    dim3 grid((nlist + 255) / 256, nq);
+    note_launch();
+    route_cos_kernel<<<grid, 256, 0, st>>>(q, nq, cent, valid, nlist, d, out);
     return cudaGetLastError();
 }
 

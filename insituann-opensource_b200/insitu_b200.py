@@ -46,7 +46,7 @@ EXPORTS = [
     "ivf_load_centroids", "ivf_assign", "ivf_build_reorder", "ivf_kmeans_update", "ivf_pq_train", "ivf_pq_encode",
     "ivf_read_centroids", "ivf_read_assign", "ivf_read_codebook", "ivf_read_codes", "ivf_read_u8bin",
     "ivf_read_fbin", "ivf_read_gt", "ivf_write_centroids", "ivf_write_assign", "ivf_write_codebook",
-    "ivf_write_codes", "ivf_pq_load_files",
+    "ivf_write_codes", "ivf_pq_load_files", "ivf_pq_insert",
     "cuda_is_available", "cuda_malloc", "cuda_alloc_pinned", "cuda_free_pinned", "cuda_free", "cuda_memcpy_h2d",
     "cuda_memcpy_d2h", "cuda_memcpy_async_h2d", "cuda_memcpy_async_d2h", "cuda_cleanup_memory",
     "cuda_pipeline_init", "cuda_pipeline_flush", "cuda_pipeline_flush_vectors_only", "cuda_pipeline_free",
@@ -128,6 +128,7 @@ _SIGS = {
     "ivf_write_codebook": ([C.c_char_p, vp, i32, i32, i32], i32),
     "ivf_write_codes": ([C.c_char_p, vp, i64, i32], i32),
     "ivf_pq_load_files": ([vp, C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p, C.c_char_p], i32),
+    "ivf_pq_insert": ([vp, vp, i32, vp, i64], i32),
 }
 
 STAGES = ("route", "worklist", "scan", "select", "rerank")
@@ -258,6 +259,16 @@ class Index:
 
     def clear_delta(self):
         self._check(self.L.ivf_pq_clear_delta(self.h))
+
+    def insert(self, rows, ids):
+        """online insert of device rows (torch uint8 / float32 [n, d]) with ids (int32 [n]) into the delta"""
+        import torch
+
+        rows = rows.contiguous()
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        self._check(self.L.ivf_pq_insert(self.h, rows.data_ptr(), 1 if rows.dtype == torch.uint8 else 0, _p(ids),
+                                         rows.shape[0]))
+        return self
 
     def set_deleted(self, deleted=None):
         """per-position delete mask (uint8 [n], nonzero = deleted), or None to clear it."""

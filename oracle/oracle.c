@@ -244,6 +244,95 @@ ORACLE_API int oracle_route_l2_normexp(const float* q, int nq, const float* cent
     return 0;
 }
 
+/*
+ * The reference's fp32 pipeline (ivf_load_dataset + ivf_pipeline_stage2_compute,
+ * cuda/search/ivf_search_separated.cu:417-650): routing by cosine distance
+ * 1 - <q, c> / (|q| |c|) in both distance modes (:477-512,
+ * coarse/fusion_cos_topk_warpsort.cu:125-135; centroids below 1e-6 norm are
+ * skipped), then an exact scan of the probed lists by L2 (mode 0) or 1 - cosine
+ * (mode 1, fine/indexed_gemm_cos.cu:114-116).  Sums in dimension order, norms
+ * sqrtf of sequential sums, cosine distances clamped at 0 and 1 for a zero
+ * norm; ties by list id (routing) and by row position (scan).
+ */
+static inline float cos_dist(const float* a, const float* b, int d, float an, float bn) {
+    float dot = 0.0f;
+    for (int j = 0; j < d; ++j) {
+        float p = a[j] * b[j];
+        dot = dot + p;
+    }
+    float den = an * bn;
+    if (!(den > 0.0f)) return 1.0f;
+    float v = 1.0f - dot / den;
+    return v > 0.0f ? v : 0.0f;
+}
+
+static inline float norm_f32(const float* a, int d) {
+    float s = 0.0f;
+    for (int j = 0; j < d; ++j) {
+        float p = a[j] * a[j];
+        s = s + p;
+    }
+    return sqrtf(s);
+}
+
+ORACLE_API int oracle_f32_search(const float* rows, const int64_t* offsets, const int32_t* counts, int nlist, int d,
+                                 const float* cent, const float* q, int nq, int nprobe, int k, int cosine,
+                                 int32_t* out_probes, int32_t* out_ids, float* out_dist) {
+    if (nq < 0 || nlist <= 0 || d <= 0 || nprobe <= 0 || k <= 0) return -1;
+    uint64_t* pb = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)nprobe);
+    uint64_t* kb = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)k);
+    float* cn = (float*)malloc(sizeof(float) * (size_t)nlist);
+    if (!pb || !kb || !cn) { free(pb); free(kb); free(cn); return -2; }
+    for (int c = 0; c < nlist; ++c) cn[c] = norm_f32(cent + (size_t)c * d, d);
+    for (int qi = 0; qi < nq; ++qi) {
+        const float* qq = q + (size_t)qi * d;
+        const float qn = norm_f32(qq, d);
+        kheap hp = {pb, 0, nprobe};
+        for (int c = 0; c < nlist; ++c) {
+            if (!(cn[c] >= 1e-6f)) continue;
+            kheap_push(&hp, fkey(cos_dist(qq, cent + (size_t)c * d, d, qn, cn[c]), (uint32_t)c));
+        }
+        kheap_sort(&hp);
+        kheap hk = {kb, 0, k};
+        for (int p = 0; p < nprobe; ++p) {
+            const int l = p < hp.n ? (int)(uint32_t)hp.k[p] : -1;
+            out_probes[(size_t)qi * nprobe + p] = l;
+            if (l < 0) continue;
+            for (int v = 0; v < counts[l]; ++v) {
+                const int64_t pos = offsets[l] + v;
+                const float* x = rows + (size_t)pos * d;
+                float dist;
+                if (cosine) {
+                    dist = cos_dist(qq, x, d, qn, norm_f32(x, d));
+                } else {
+                    float s = 0.0f;
+                    for (int j = 0; j < d; ++j) {
+                        float t = qq[j] - x[j];
+                        float p2 = t * t;
+                        s = s + p2;
+                    }
+                    dist = s;
+                }
+                kheap_push(&hk, fkey(dist, (uint32_t)pos));
+            }
+        }
+        kheap_sort(&hk);
+        for (int j = 0; j < k; ++j) {
+            if (j < hk.n) {
+                out_ids[(size_t)qi * k + j] = (int32_t)(uint32_t)hk.k[j];
+                out_dist[(size_t)qi * k + j] = bitsf((uint32_t)(hk.k[j] >> 32));
+            } else {
+                out_ids[(size_t)qi * k + j] = -1;
+                out_dist[(size_t)qi * k + j] = INFINITY;
+            }
+        }
+    }
+    free(pb);
+    free(kb);
+    free(cn);
+    return 0;
+}
+
 /* ------------------------------------------------------------------ */
 /* exact uint8 fine search                                              */
 /* ------------------------------------------------------------------ */

@@ -44,6 +44,9 @@ def lib():
         L.oracle_route_l2.argtypes = [f32p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, i32p, f32p]
         L.oracle_route_l2.restype = C.c_int
         L.oracle_route_l2_normexp.argtypes = [f32p, C.c_int, f32p, C.c_int, C.c_int, C.c_int, i32p, f32p]
+        L.oracle_f32_search.argtypes = [f32p, i64p, i32p, C.c_int, C.c_int, f32p, f32p, C.c_int, C.c_int,
+                                        C.c_int, C.c_int, i32p, i32p, f32p]
+        L.oracle_f32_search.restype = C.c_int
         L.oracle_route_l2_normexp.restype = C.c_int
         L.oracle_exact_u8.argtypes = [u8p, i64p, i32p, C.c_void_p, C.c_int, C.c_int,
                                       u8p, i32p, C.c_int, C.c_int, C.c_int, C.c_void_p, i32p, i32p]
@@ -174,6 +177,21 @@ def pq_search(cent, codebook, codes, offsets, counts, r2o, q, probes, k, rerank_
     if return_stage1:
         return ids, dist, s1, sd
     return ids, dist
+
+
+def f32_search(rows, offsets, counts, cent, q, nprobe, k, cosine=False):
+    """The reference's fp32 pipeline restated: cosine routing, exact L2 / cosine
+    scan; returns (probes, ids = row positions, distances)."""
+    rows, cent, q = _c(rows, np.float32), _c(cent, np.float32), _c(q, np.float32)
+    offsets, counts = _c(offsets, np.int64), _c(counts, np.int32)
+    nq, d = q.shape
+    probes = np.empty((nq, nprobe), np.int32)
+    ids = np.empty((nq, k), np.int32)
+    dist = np.empty((nq, k), np.float32)
+    rc = lib().oracle_f32_search(rows, offsets, counts, counts.shape[0], d, cent, q, nq, nprobe, k,
+                                 1 if cosine else 0, probes, ids, dist)
+    assert rc == 0, rc
+    return probes, ids, dist
 
 
 def route_l2_normexp(q, cent, nprobe, threads=0):

@@ -111,3 +111,60 @@ def test_ground_truth_int8_path_equals_exact(cuda_ok):
     cpu = synth.gt_keys(base, q, 10, batch_rows=4096)
     gpu = synth.gt_keys(base.cuda(), q.cuda(), 10, batch_rows=4096).cpu()
     assert torch.equal(cpu, gpu)
+
+
+def _np_encode(x, cent, a, cb):
+    """residual PQ codes in the kernel's arithmetic: fp32 terms in dimension order, first minimum"""
+    M, _, dsub = cb.shape
+    resid = (x.astype(np.float32) - cent[a]).reshape(x.shape[0], M, dsub)
+    s = np.zeros((x.shape[0], M, 256), np.float32)
+    for e in range(dsub):
+        t = resid[:, :, e][:, :, None] - cb[None, :, :, e]
+        s = s + t * t
+    return s.argmin(-1).astype(np.uint8)
+
+
+def test_online_insert_matches_the_oracle(cuda_ok):
+    """ivf_pq_insert: three batches of new uint8 rows are assigned, encoded
+    and published into the delta segment; after each, the overlay search
+    equals the oracle on the delta built in NumPy (list-major, older rows
+    first, new rows in insertion order)."""
+    n, d, nlist, M, nq, nprobe, k, R = 8000, 64, 32, 16, 60, 6, 10, 64
+    base = synth.mixture_u8(n, d, 30, 10.0, seed=101)
+    idx = synth.build_pq_index(base, nlist, M, seed=101, kmeans_iters=5, pq_iters=4, train_n=5000)
+    q = synth.mixture_u8(nq, d, 30, 10.0, seed=101, stream_base=1 << 20).float().numpy()
+    index = ib.Index().load_pq(idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"],
+                               idx["r2o"], base_u8=idx["base_rr"])
+    b = ib.Batch(nq, d, nprobe, k, nlist)
+    probes, _ = oracle.route_l2(q, idx["centroids"], nprobe)
+    rows_all, ids_all, lists_all = [], [], []
+    next_id = n
+    for step, m in enumerate((500, 1, 1300)):
+        new = synth.mixture_u8(m, d, 30, 10.0, seed=101, stream_base=(1 << 21) + step).numpy()
+        ids = np.arange(next_id, next_id + m, dtype=np.int32)
+        next_id += m
+        index.insert(torch.from_numpy(new).cuda(), ids)
+        a, _ = oracle.route_l2(new.astype(np.float32), idx["centroids"], 1)
+        rows_all.append(new)
+        ids_all.append(ids)
+        lists_all.append(a[:, 0])
+        rows = np.concatenate(rows_all)
+        lists = np.concatenate(lists_all)
+        order = np.argsort(lists, kind="stable")               # older inserts first within a list
+        counts = np.bincount(lists, minlength=nlist).astype(np.int32)
+        offsets = np.zeros(nlist, np.int64)
+        offsets[1:] = np.cumsum(counts)[:-1]
+        codes = _np_encode(rows, idx["centroids"], lists, idx["codebook"])
+        delta = dict(codes=codes[order], offsets=offsets, counts=counts, ids=np.concatenate(ids_all)[order],
+                     raw_u8=rows[order])
+        b.stage1_prepare(q)
+        b.set_probes(probes)
+        b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=True, delta_topk=16, route=False)
+        gi, gd = b.get_results(nq, k)
+        oi, od = oracle.pq_search(idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"],
+                                  idx["r2o"], q, probes, k, rerank_n=R, base_u8=idx["base_rr"], delta=delta,
+                                  delta_topk=16)
+        assert np.array_equal(gi, oi) and np.array_equal(gd, od), f"after insert {step}"
+    assert (gi >= n).any()                      # inserted vectors reach the results
+    b.close()
+    index.close()

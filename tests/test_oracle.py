@@ -297,3 +297,49 @@ def test_oracle_routing_vs_reference_coarse_search(name):
         n_diff, worst = oracle.route_disagreement(q[:P], cent, ours, ref)
         assert worst <= 1.0, (nprobe, n_diff, worst)
         assert n_diff <= P // 50, (nprobe, n_diff)
+
+
+@pytest.mark.parametrize("cosine", [False, True])
+def test_oracle_f32_pipeline_against_python_loops(cosine):
+    """oracle.f32_search (the reference's fp32 pipeline: cosine routing, exact
+    L2 / 1 - cosine scan) against plain Python loops in float32, in the same
+    order of operations; an empty list included."""
+    g = np.random.default_rng(3)
+    nlist, d, n = 6, 8, 60
+    rows = g.standard_normal((n, d)).astype(np.float32)
+    counts = np.array([10, 0, 15, 5, 20, 10], np.int32)
+    offsets = np.concatenate([[0], np.cumsum(counts)[:-1]]).astype(np.int64)
+    cent = g.standard_normal((nlist, d)).astype(np.float32)
+    q = g.standard_normal((4, d)).astype(np.float32)
+    f = np.float32
+
+    def nrm(a):
+        s = f(0)
+        for v in a:
+            s = f(s + f(v * v))
+        return f(np.sqrt(s))
+
+    def cosd(a, b):
+        dot = f(0)
+        for x, y in zip(a, b):
+            dot = f(dot + f(x * y))
+        return max(f(f(1) - f(dot / f(nrm(a) * nrm(b)))), f(0))
+
+    pr, ids, dd = oracle.f32_search(rows, offsets, counts, cent, q, 3, 5, cosine=cosine)
+    for i in range(q.shape[0]):
+        assert [c for _, c in sorted((cosd(q[i], cent[c]), c) for c in range(nlist))[:3]] == list(pr[i])
+        cand = []
+        for l in pr[i]:
+            for v in range(counts[l]):
+                p = offsets[l] + v
+                if cosine:
+                    dist = cosd(q[i], rows[p])
+                else:
+                    dist = f(0)
+                    for x, y in zip(q[i], rows[p]):
+                        t = f(x - y)
+                        dist = f(dist + f(t * t))
+                cand.append((dist, p))
+        cand.sort()
+        assert [p for _, p in cand[:5]] == list(ids[i])
+        assert np.array_equal(np.array([x for x, _ in cand[:5]], np.float32), dd[i])
