@@ -277,18 +277,19 @@ def algorithmic_bytes(probes, counts, M):
 # ----------------------------------------------------------------------------
 # reference arm / CPU baseline
 # ----------------------------------------------------------------------------
-def time_reference(idx, q, probes, cfg, target_s, max_queries):
+def time_reference(idx, q, probes, cfg, target_s, max_queries, stock=True):
     """Times oracle/_ref (the reference's cpu_fine_kernel_pq_resid) on a query sample.
 
     The sample (at most max_queries queries, with their probe lists) is searched
-    repeatedly until about target_s seconds of CPU work have been timed."""
+    repeatedly until about target_s seconds of CPU work have been timed.
+    stock: the reference's own compiler flags (else the build that pins the oracle)."""
     import oracle
 
-    L = oracle.ref_lib()
+    L = oracle.ref_lib(stock)
     if L is None:
         return None
     threads = os.cpu_count() or 1
-    kw = dict(rerank_n=cfg["rerank_n"], threads=threads, **rr_kw(idx["base_rr"]))
+    kw = dict(rerank_n=cfg["rerank_n"], threads=threads, stock=stock, **rr_kw(idx["base_rr"]))
     args = (idx["centroids"], idx["codebook"], idx["codes"], idx["offsets"], idx["counts"])
     S = min(max_queries, q.shape[0])
     if idx["base_rr"].dtype == np.uint8:
@@ -323,22 +324,22 @@ def build_workload_u8(cfg, device):
     return idx, q.float().cpu().numpy(), gt
 
 
-def time_reference_u8(idx, q, probes, cfg, target_s):
+def time_reference_u8(idx, q, probes, cfg, target_s, stock=True):
     """Times oracle/_ref's cpu_fine_kernel_v3_u8_touched (all threads) on the batch, repeated to ~target_s."""
     import oracle
 
-    L = oracle.ref_lib()
+    L = oracle.ref_lib(stock)
     if L is None:
         return None
     threads = os.cpu_count() or 1
     qu = oracle.make_query_u8(q)
     oracle.ref_exact_u8_touched(idx["base_cm"], idx["offsets"], idx["counts"], qu[:64], probes[:64], cfg["k"],
-                                threads=threads)
+                                threads=threads, stock=stock)
     done, dt, ids = 0, 0.0, None
     while dt < target_s:
         t = time.perf_counter()
         ids, _ = oracle.ref_exact_u8_touched(idx["base_cm"], idx["offsets"], idx["counts"], qu, probes, cfg["k"],
-                                             threads=threads)
+                                             threads=threads, stock=stock)
         dt += time.perf_counter() - t
         done += q.shape[0]
     return dict(qps=done / dt, seconds=dt, sample=done, threads=threads, lib=os.path.basename(L.library_path),
@@ -437,11 +438,13 @@ def run_exact(args, cfg):
     if not args.no_cpu_baseline:
         S = 2048
         r = time_reference_u8(idx, q_np[:S], probes[:S], cfg, target_s=12.0)
+        r2 = time_reference_u8(idx, q_np[:S], probes[:S], cfg, target_s=4.0, stock=False)
         if r is not None:
             cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
                    "sample": f"{r['sample']} query searches ({S} distinct queries of the batch, repeated) with "
-                             f"reference cpu_fine_kernel_v3_u8_touched ({r['lib']}), probe lists given, "
-                             f"{r['seconds']:.1f}s"}
+                             f"reference cpu_fine_kernel_v3_u8_touched ({r['lib']}: the reference's flags -O3 "
+                             f"-ffast-math -funroll-loops, AVX-512), probe lists given, {r['seconds']:.1f}s",
+                   "without_fast_math": None if r2 is None else {"value": r2["qps"], "lib": r2["lib"]}}
     out = {
         "metric": METRIC, "value": value, "unit": "queries/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
@@ -931,12 +934,15 @@ def main():
     if rank == 0 and N == 1 and not args.no_cpu_baseline:
         probes_o, _ = oracle.route_l2_par(q_np[:4096], idx["centroids"], nprobe)
         r = time_reference(idx, q_np[:4096], probes_o, cfg, target_s=12.0, max_queries=4096)
+        r2 = time_reference(idx, q_np[:4096], probes_o, cfg, target_s=4.0, max_queries=4096, stock=False)
         if r is not None:
             cpu = {"value": r["qps"], "unit": "queries/s", "cores": r["threads"], "kind": "reference",
                    "sample": f"{r['sample']} query searches ({r['distinct']} distinct queries of the batch, "
                              f"repeated) with reference cpu_fine_kernel_pq_resid (stage 1 + "
                              f"{'uint8' if idx['base_rr'].dtype == np.uint8 else 'fp32'} rerank, "
-                             f"{r['lib']}), probe lists given, {r['seconds']:.1f}s"}
+                             f"{r['lib']}: the reference's flags -O3 -ffast-math -funroll-loops, AVX-512), "
+                             f"probe lists given, {r['seconds']:.1f}s",
+                   "without_fast_math": None if r2 is None else {"value": r2["qps"], "lib": r2["lib"]}}
 
     if rank == 0:
         out = {

@@ -306,15 +306,34 @@ def _cpu_has_avx512bw() -> bool:
         return False
 
 
-def ref_lib():
-    """The reference's CPU kernels, or None when oracle/_ref was not built."""
-    global _REF
+_REF_STOCK = None
+
+
+def ref_lib(stock=False):
+    """The reference's CPU kernels, or None when oracle/_ref was not built.
+
+    stock=False: the build without -ffast-math that pins the oracle;
+    stock=True: the reference's own flags (-O3 -ffast-math -funroll-loops,
+    AVX-512), the timed baseline (AVX-512 hosts; else the first build)."""
+    global _REF, _REF_STOCK
+    if stock:
+        if _REF_STOCK is None:
+            path = os.path.join(HERE, "_ref", "libref_cpu_fine_stock.so")
+            if not (_cpu_has_avx512bw() and os.path.exists(path)):
+                return ref_lib(False)
+            _REF_STOCK = _bind_ref(C.CDLL(path), path)
+        return _REF_STOCK
     if _REF is None:
         name = "libref_cpu_fine.so" if _cpu_has_avx512bw() else "libref_cpu_fine_avx2.so"
         path = os.path.join(HERE, "_ref", name)
         if not os.path.exists(path):
             return None
-        L = C.CDLL(path)
+        _REF = _bind_ref(C.CDLL(path), path)
+    return _REF
+
+
+def _bind_ref(L, path):
+    if True:
         L.ref_cpu_fine_kernel_v3_u8_touched.argtypes = [
             u8p, i64p, i32p, u8p, i32p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, i32p, f32p]
         L.ref_cpu_fine_kernel_v3_u8_touched.restype = C.c_longlong
@@ -325,13 +344,12 @@ def ref_lib():
             i32p, f32p, C.POINTER(C.c_double), C.POINTER(C.c_double)]
         L.ref_cpu_fine_kernel_pq_resid.restype = C.c_longlong
         L.library_path = path
-        _REF = L
-    return _REF
+    return L
 
 
-def ref_exact_u8_touched(base_u8, offsets, counts, q_u8, probes, k, threads=0):
+def ref_exact_u8_touched(base_u8, offsets, counts, q_u8, probes, k, threads=0, stock=False):
     """Reference cpu_fine_kernel_v3_u8_touched: returns (local positions, float dists)."""
-    L = ref_lib()
+    L = ref_lib(stock)
     assert L is not None, "oracle/_ref not built"
     base_u8 = _c(base_u8, np.uint8)
     offsets = _c(offsets, np.int64)
@@ -347,9 +365,9 @@ def ref_exact_u8_touched(base_u8, offsets, counts, q_u8, probes, k, threads=0):
 
 
 def ref_pq_resid(cent, codebook, codes, offsets, counts, q_f32, probes, k, rerank_n=512,
-                 base_u8=None, q_u8=None, base_f32=None, threads=0):
+                 base_u8=None, q_u8=None, base_f32=None, threads=0, stock=False):
     """Reference cpu_fine_kernel_pq_resid: returns (local positions, float exact dists, s1_ms, s2_ms)."""
-    L = ref_lib()
+    L = ref_lib(stock)
     assert L is not None, "oracle/_ref not built"
     cent = _c(cent, np.float32)
     codebook = _c(codebook, np.float32)
