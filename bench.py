@@ -156,6 +156,29 @@ class Clocks:
                 "samples": len(rows), "reasons": reasons}
 
 
+def clock_soak(step, sync, seconds=1.0, dist=None, dev=None):
+    """Untimed steps of the same work, run under the clock sampler right before
+    the timed region: nvidia-smi samples every 100 ms, so a timed region of a
+    few hundred ms alone would give it one or two samples.  Every rank runs the
+    same number of steps (the maximum over ranks), since a step may hold
+    collectives."""
+    sync()
+    t0 = time.perf_counter()
+    step()
+    sync()
+    dt = time.perf_counter() - t0
+    n = min(200, max(0, int(seconds / max(dt, 1e-4)) + 1))
+    if dist is not None:
+        import torch
+
+        t = torch.tensor([n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n = int(t.item())
+    for _ in range(n):
+        step()
+    sync()
+
+
 # ----------------------------------------------------------------------------
 # workload
 # ----------------------------------------------------------------------------
@@ -376,20 +399,22 @@ def run_exact(args, cfg):
     batch.sync()
     ids_g, dist_g = batch.get_results(nq, k)
     probes = batch.get_probes(nq, nprobe)
-    exp_p, _ = oracle.route_l2(q_np[:64], idx["centroids"], nprobe)
+    P = min(args.parity_queries, nq)
+    exp_p, _ = oracle.route_l2_par(q_np[:P], idx["centroids"], nprobe)
     oi, od = oracle.exact_u8(idx["base_cm"], idx["offsets"], idx["counts"], idx["r2o"],
-                             oracle.make_query_u8(q_np[:64]), exp_p, k)
-    parity = bool(np.array_equal(probes[:64], exp_p) and np.array_equal(ids_g[:64], oi)
-                  and np.array_equal(dist_g[:64], od.astype(np.float32)))
+                             oracle.make_query_u8(q_np[:P]), exp_p, k)
+    parity = bool(np.array_equal(probes[:P], exp_p) and np.array_equal(ids_g[:P], oi)
+                  and np.array_equal(dist_g[:P], od.astype(np.float32)))
     recall = synth.recall_at_k(ids_g, gt, k)
-    log(f"[bench] c0 parity(64 queries vs oracle)={parity} recall@10={recall:.4f}")
+    log(f"[bench] c0 parity({P} queries vs oracle)={parity} recall@10={recall:.4f}")
     for _ in range(args.warmup):
         step()
     batch.sync()
-    batch.profile(True)
-    launches0 = ib.kernel_launches()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(0) as clk:
+        clock_soak(step, batch.sync)
+        batch.profile(True)
+        launches0 = ib.kernel_launches()
         torch.cuda.synchronize()
         ev0.record(ext)
         for _ in range(args.steps):
@@ -451,7 +476,7 @@ def run_exact(args, cfg):
         "vs_baseline": None, "dtype": "u8", "data": "synthetic",
         "config": {"workload": cfg["desc"], "n_base": cfg["n"], "d": d, "nlist": nlist, "nq": nq,
                    "nprobe": nprobe, "k": k, "recall@10": recall, "recall_target_met": bool(recall >= 0.9),
-                   "parity_vs_oracle_64q": parity, "inputs_exceed_l2": True,
+                   "parity_vs_oracle": parity, "parity_queries": P, "inputs_exceed_l2": True,
                    "l2_note": "the 128 MB of vectors are probed 320k times per step (40 GB logical)",
                    "parallelism": "single GPU"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": int(launches),
@@ -764,6 +789,23 @@ def main():
                          "stage1_keys_equal": ok_s, "queries_differing": int(bad.sum())}
         log(f"[bench] parity({P} queries vs oracle)={parity} {parity_detail} "
             f"recall@10={synth.recall_at_k(ids_g, gt, k):.4f} ({time.time() - t_par:.1f}s)")
+    # ---- routing against the reference's own coarse_search (cuBLAS SGEMM, norm expansion) on
+    # the same P queries, when that build is present: how many probe sets differ, and the
+    # recall@10 of the search run on the reference's probe lists instead of this library's ----
+    route_vs_ref = None
+    if N == 1 and rank == 0 and oracle.ref_coarse_lib() is not None:
+        rp = oracle.ref_coarse_search(cent_np, q_np[:P], nprobe)
+        diff = ~(np.sort(rp, axis=1) == np.sort(probes_g[:P], axis=1)).all(1)
+        batch.stage1_prepare_device(q_dev.data_ptr(), P)
+        batch.set_probes(rp)
+        batch.pq_search(index, P, nprobe, k, rerank_n=R, overlay=False, route=False)
+        ids_r, _ = batch.get_results(P, k)
+        rec_own = synth.recall_at_k(ids_g[:P], gt[:P], k)
+        rec_ref = synth.recall_at_k(ids_r, gt[:P], k)
+        route_vs_ref = {"queries": P, "probe_sets_differing": int(diff.sum()),
+                        "recall@10_own_probes": rec_own, "recall@10_reference_probes": rec_ref,
+                        "recall_delta": rec_own - rec_ref}
+        log(f"[bench] routing vs reference coarse_search: {route_vs_ref}")
     del oidx
     if N > 1:
         del W["codes"], W["base_rr"]
@@ -775,11 +817,12 @@ def main():
         step()
     barrier()
     probes_all = batch.get_probes(nq, nprobe) if N == 1 else None
-    batch.profile(True)
-    launches0 = ib.kernel_launches()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        clock_soak(step, barrier, dist=dist if N > 1 else None, dev=dev)
+        batch.profile(True)
+        launches0 = ib.kernel_launches()
         barrier()
         ev0.record(ext)
         for _ in range(args.steps):
@@ -953,7 +996,7 @@ def main():
                        "nq": nq, "nprobe": nprobe, "k": k, "rerank_n": R,
                        "recall@10": synth.recall_at_k(ids_g, gt, k), "recall_target_met": bool(
                            synth.recall_at_k(ids_g, gt, k) >= 0.9), "parity_vs_oracle": parity,
-                       "parity_detail": parity_detail,
+                       "parity_detail": parity_detail, "routing_vs_reference": route_vs_ref,
                        "inputs_exceed_l2": True,
                        "l2_note": f"{codes_mb:.0f} MB of codes and {rr_gb:.2f} GB of rerank rows per step",
                        "parallelism": "single GPU" if N == 1 else f"lists sharded x{N} (LPT by bytes), NCCL"},

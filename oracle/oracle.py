@@ -15,6 +15,11 @@ import subprocess
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def ref_root() -> str:
+    """The reference checkout: $REF_ROOT, else `reference` beside this repository's checkout."""
+    return os.environ.get("REF_ROOT") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
 _LIB = None
 _REF = None
 
@@ -28,8 +33,8 @@ u64p = np.ctypeslib.ndpointer(dtype=np.uint64, flags="C_CONTIGUOUS")
 def build(ref: bool = False) -> None:
     """Compile liboracle.so (and, when the reference tree exists, the reference kernels)."""
     subprocess.run(["make", "-s", "-C", HERE], check=True)
-    if ref and os.path.isdir(os.environ.get("REF_ROOT", "/root/reference")):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+    if ref and os.path.isdir(ref_root()):
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF_ROOT={ref_root()}"], check=True)
 
 
 def lib():
@@ -345,6 +350,38 @@ def _bind_ref(L, path):
         L.ref_cpu_fine_kernel_pq_resid.restype = C.c_longlong
         L.library_path = path
     return L
+
+
+_REF_COARSE = None
+
+
+def ref_coarse_lib():
+    """The reference's GPU coarse_search (oracle/_ref/libref_coarse.so, built by
+    `make ref-coarse`), or None when it was not built.  Needs a CUDA device."""
+    global _REF_COARSE
+    if _REF_COARSE is None:
+        path = os.path.join(HERE, "_ref", "libref_coarse.so")
+        if not os.path.exists(path):
+            return None
+        L = C.CDLL(path)
+        L.ref_coarse_search.argtypes = [f32p, C.c_int, C.c_int, f32p, C.c_int, C.c_int, i32p]
+        L.ref_coarse_search.restype = C.c_int
+        _REF_COARSE = L
+    return _REF_COARSE
+
+
+def ref_coarse_search(cent, q_f32, nprobe):
+    """Probe lists [nq, nprobe] of the reference's own coarse_search
+    (cuda/search/cpu_fine/ivf_search_cpu_fine.cu:764-1361: norms, cuBLAS SGEMM
+    ||q||^2 + ||c||^2 - 2 q.c, warp-sort top-nprobe) run on the GPU."""
+    L = ref_coarse_lib()
+    assert L is not None, "oracle/_ref/libref_coarse.so not built"
+    cent = _c(cent, np.float32)
+    q_f32 = _c(q_f32, np.float32)
+    ids = np.full((q_f32.shape[0], nprobe), -1, np.int32)
+    rc = L.ref_coarse_search(cent, cent.shape[0], cent.shape[1], q_f32, q_f32.shape[0], nprobe, ids)
+    assert rc == 0, f"ref_coarse_search returned {rc}"
+    return ids
 
 
 def ref_exact_u8_touched(base_u8, offsets, counts, q_u8, probes, k, threads=0, stock=False):
