@@ -77,6 +77,11 @@ CONFIGS = {
                      train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=20260602,
                      kmeans_iters=6, kmeans_sample=16 * 65536,
                      desc="c2 shapes at 10M rows (quick checks)"),
+    # c2-shaped lists (about 1526 vectors each, 2.4 probing queries per list at nprobe 16) at a
+    # tenth of the rows and queries: the scan's per-group work equals c2's (profiling case)
+    "c2-mid": dict(kind="pq_u8", n=10_000_000, d=128, ncomp=6554, sigma=10.0, nlist=6554, M=32,
+                   train_n=500_000, nq=1000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=17,
+                   desc="c2-shaped lists at 10M rows, 1k queries (profiling case)"),
     # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
     "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
                    nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,

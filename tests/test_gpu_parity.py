@@ -153,23 +153,31 @@ def test_exact_deletes(cuda_ok, d):
     index.close()
 
 
-@pytest.mark.parametrize("f32", [False, True])
-def test_pq_deletes(cuda_ok, pq_medium, f32):
-    """deleted positions keep their stage-1 slots and are not reranked."""
+@pytest.mark.parametrize("f32,overlay", [(False, False), (True, False), (False, True), (True, True)])
+def test_pq_deletes(cuda_ok, pq_medium, f32, overlay):
+    """deleted positions keep their stage-1 slots and are not reranked; with a
+    published delta, main keys are masked and delta keys are not."""
     p, q = pq_medium
     nq, nprobe, k, R = q.shape[0], 8, 10, 64
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     dele = synth.delete_mask(p["r2o"], 0.3)
     rr = {"base_f32": p["base_u8"].astype(np.float32)} if f32 else {"base_u8": p["base_u8"]}
+    delta = None
+    if overlay:
+        delta = synth.delta_segment(20000, len(p["counts"]), p["codebook"].shape[0], base_id=p["codes"].shape[0],
+                                    d=q.shape[1], seed=5, f32=f32)
     index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], **rr)
     index.set_deleted(dele)
+    if delta is not None:
+        index.publish_delta(delta["codes"], delta["ids"], delta["counts"], delta["offsets"],
+                            raw_u8=delta.get("raw_u8"), raw_f32=delta.get("raw_f32"))
     b = ib.Batch(nq, q.shape[1], nprobe, k, len(p["counts"]))
     b.stage1_prepare(q)
     b.set_probes(probes)
-    b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=False, route=False)
+    b.pq_search(index, nq, nprobe, k, rerank_n=R, overlay=overlay, delta_topk=16, route=False)
     gi, gd = b.get_results(nq, k)
     oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
-                              probes, k, rerank_n=R, deleted=dele, **rr)
+                              probes, k, rerank_n=R, deleted=dele, delta=delta, delta_topk=16, **rr)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
     b.close()
     index.close()
@@ -458,14 +466,16 @@ def test_sharded_merge_equals_unsharded(cuda_ok, pq_medium):
         o.close()
 
 
-@pytest.mark.parametrize("R,k", [(256, 10), (40, 32)])
-def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
+@pytest.mark.parametrize("R,k,masked", [(256, 10, False), (40, 32, False), (256, 10, True)])
+def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k, masked):
     """lists split over 3 shards (three index contexts on one GPU), the phased
     protocol with the exchanges done on the host side: nearest-probe scans,
     int64 minimum of the bounds, the other probes, unsorted stage 1 to the
     owners, kappa (R-th key of the union) back, each shard's exact top-k of its
-    keys <= kappa, owners' merge == unsharded search."""
+    keys <= kappa, owners' merge == unsharded search.  masked: a delete mask
+    (30% of the rows), each shard holding its rows' part of it."""
     p, q = pq_medium
+    dele = synth.delete_mask(p["r2o"], 0.3) if masked else None
     nlist = len(p["counts"])
     G, nprobe = 3, 12
     nq = q.shape[0] - q.shape[0] % G
@@ -482,6 +492,8 @@ def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
         idx = ib.Index().load_pq(p["centroids"][lists], p["codebook"], p["codes"][rows], off, cnt, p["r2o"][rows],
                                  base_u8=p["base_u8"][rows])
         idx.set_shard(nlist, lists.astype(np.int32), p["offsets"][lists])
+        if dele is not None:
+            idx.set_deleted(dele[rows])
         shards.append(idx)
     dev = torch.device("cuda")
     exp_probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
@@ -527,7 +539,7 @@ def test_phased_shard_protocol_equals_unsharded(cuda_ok, pq_medium, R, k):
         batches[o].pq_shard_final(tk_o.data_ptr(), G, qo, k, True)
         gi[o * qo:(o + 1) * qo], gd[o * qo:(o + 1) * qo] = batches[o].get_results(qo, k)
     oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
-                              exp_probes, k, rerank_n=R, base_u8=p["base_u8"])
+                              exp_probes, k, rerank_n=R, base_u8=p["base_u8"], deleted=dele)
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
     for o in batches + shards:
         o.close()
