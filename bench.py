@@ -707,7 +707,7 @@ def main():
             mark("rerank")
             shard.to_owners_raw(dist, N, topk, topk_r)
             mark("top-k to owners")
-            batch.pq_shard_final(topk_r.data_ptr(), N, qo, k, False)
+            batch.pq_shard_final(topk_r.data_ptr(), N, qo, k, rr_u8)    # uint8 rerank: int32 distances
             batch.get_results_device(out_dist.data_ptr(), out_ids.data_ptr(), qo, k)
             mark("final")
             shard.gather_results_packed(dist, out_ids, out_dist, own_packed, all_packed)
