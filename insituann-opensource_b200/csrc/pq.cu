@@ -131,7 +131,9 @@ constexpr int kGQ = 4;      // queries per group
 // the kernel the search uses for these shapes.
 //
 // A CTA takes one list and up to 4 probing queries (a group of the work list)
-// and the four queries' LUTs are interleaved as float4.  The M sub-quantizers
+// and the four queries' LUTs are interleaved as float4 (a group of two or one
+// query uses bank-shifted copies of a float2 or float table instead, so its
+// gathers move only the entries it sums; see stagger_tile).  The M sub-quantizers
 // form 8 blocks of MPL = M/8.  A warp is four groups of 8 lanes; lane j of a
 // group sums the vectors 8k + j of its stripe, one block per step, blocks in
 // order, so a vector takes 8 steps and is started at step 8k + j: at step x
@@ -193,38 +195,58 @@ struct GRing {
 // lane j to out[its finishing step]: one 16-byte store per lane per 8 steps.
 // A stored sum at or below query k's bound thf sets bit k of maybe (a superset
 // of the keys the chunk's filter can admit).
-template <int M, int NST>
-__device__ __forceinline__ void stagger_tile(const float4* __restrict__ lut, const uint32_t (&w)[M / 2], int nst,
-                                             int j, float2& s01, float2& s23, float4* out, float4 thf,
+//
+// Q = queries per LUT entry.  Q = 4: one table of float4 entries; a
+// quarter-warp (one lane group) reads 8 distinct 16-byte bank groups.  Q = 2
+// (M a multiple of 16): two copies of a float2 table, copy 1 with entry
+// position p XOR 8; lane group g reads copy g & 1, so the two groups of a
+// half-warp read disjoint halves of the banks.  Q = 1 (M = 32): four copies
+// of a float table, copy g with position p XOR 8g; the four groups of a warp
+// read four disjoint bank octets.  Each layout is conflict-free, and a gather
+// costs 4, 2 or 1 wavefronts per warp.  In copy x entry m = MPL*blk + s sits
+// at (blk + 8s) XOR 8x = blk + 8 (s XOR x).
+template <int M, int NST, int Q>
+__device__ __forceinline__ void stagger_tile(const float* __restrict__ lutf, const uint32_t (&w)[M / 2], int nst,
+                                             int j, int g, float2& s01, float2& s23, float4* out, float4 thf,
                                              uint32_t& maybe) {
     constexpr int MPL = M / 8;
+    static_assert(Q == 4 || (Q == 2 && M % 16 == 0) || (Q == 1 && M == 32), "LUT layout");
     float4 fin = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int cp = Q == 4 ? 0 : (Q == 2 ? (g & 1) : g);             // the copy this lane group reads
 #pragma unroll
     for (int i = 0; i < NST; ++i) {
         if (NST < 16 && i >= nst) break;
         const int blk = (i - j) & 7;
-        const float4* lb = lut + blk;               // entries MPL*blk + s at positions blk + 8*s
         const float2 k2 = blk == 0 ? make_float2(0.f, 0.f) : make_float2(1.f, 1.f);
 #pragma unroll
         for (int s = 0; s < MPL; ++s) {
             const int byte = i * MPL + s;
             const uint32_t c = (w[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
-            const float4 f = lb[c * M + 8 * s];
-            if (s == 0) {
-                s01 = __ffma2_rn(s01, k2, make_float2(f.x, f.y));
-                s23 = __ffma2_rn(s23, k2, make_float2(f.z, f.w));
+            if constexpr (Q == 4) {
+                const float4 f = reinterpret_cast<const float4*>(lutf)[c * M + blk + 8 * s];
+                if (s == 0) {
+                    s01 = __ffma2_rn(s01, k2, make_float2(f.x, f.y));
+                    s23 = __ffma2_rn(s23, k2, make_float2(f.z, f.w));
+                } else {
+                    s01 = __fadd2_rn(s01, make_float2(f.x, f.y));
+                    s23 = __fadd2_rn(s23, make_float2(f.z, f.w));
+                }
+            } else if constexpr (Q == 2) {
+                const float2 f = reinterpret_cast<const float2*>(lutf)[(cp * 256 + c) * M + blk + 8 * (s ^ cp)];
+                s01 = s == 0 ? __ffma2_rn(s01, k2, f) : __fadd2_rn(s01, f);
             } else {
-                s01 = __fadd2_rn(s01, make_float2(f.x, f.y));
-                s23 = __fadd2_rn(s23, make_float2(f.z, f.w));
+                const float f = lutf[(cp * 256 + c) * M + blk + 8 * (s ^ cp)];
+                s01.x = s == 0 ? __fmaf_rn(s01.x, k2.x, f) : __fadd_rn(s01.x, f);
             }
         }
-        if (blk == 7) fin = make_float4(s01.x, s01.y, s23.x, s23.y);
+        if (blk == 7) fin = make_float4(s01.x, Q >= 2 ? s01.y : 0.f, Q == 4 ? s23.x : 0.f, Q == 4 ? s23.y : 0.f);
         if ((i & 7) == 7 || (NST < 16 && i == nst - 1)) {
             const int fstep = (i & ~7) + ((j + 7) & 7);
             if (fstep <= i) {
                 out[fstep] = fin;
-                maybe |= (fin.x <= thf.x ? 1u : 0u) | (fin.y <= thf.y ? 2u : 0u) | (fin.z <= thf.z ? 4u : 0u) |
-                         (fin.w <= thf.w ? 8u : 0u);
+                maybe |= (fin.x <= thf.x ? 1u : 0u);
+                if (Q >= 2) maybe |= (fin.y <= thf.y ? 2u : 0u);
+                if (Q == 4) maybe |= (fin.z <= thf.z ? 4u : 0u) | (fin.w <= thf.w ? 8u : 0u);
             }
         }
     }
@@ -328,6 +350,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     // kept past the next group's descriptor fetch
     __shared__ int64_t s_skoff[2], s_sgoff[2];
     __shared__ int s_scount[2];
+    __shared__ unsigned long long s_thr1[kGQ];   // the second segment's bounds, read before the LUT build
     // per-chunk totals and "some sum may pass" bits of the 4 queries, three
     // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
     // barrier, clears buffer (c + 2) % 3 -- last read in chunk c - 1 (done
@@ -383,6 +406,9 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
         if (builder) load_cb(c0);
         const int64_t packed = s_gd.pk;
         const int l = (int)(packed >> 32), nqg = ((int)packed) & 7;
+        // queries per LUT entry for this group (stagger_tile): 4, or 2 / 1 for
+        // groups of two / one query (1 needs M = 32, else 2)
+        const int qmode = nqg >= 3 ? 4 : (nqg == 2 || M != 32) ? 2 : 1;
         // the group's list in the main segment and, with the overlay, the same
         // list's delta rows: both are scanned here with the one LUT (read out of
         // s_gd before the next group's descriptor rewrites it)
@@ -424,9 +450,30 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             const uint4* lanebase;
             int64_t ntiles, T0;
             int S, wsteps, nchunks;
-            const int seg0 = count_m > 0 ? 0 : 1;
+            // With a delta segment the (short) delta rows go first and the
+            // main rows second: the second segment's first tile is then
+            // prefetched during the first segment's last tile (or, for a warp
+            // with no steps in the first segment, right away), and its bounds
+            // are read before the LUT build, so switching segments exposes no
+            // global-memory latency.
+            const int seg0 = DELTA ? (count_d > 0 ? 1 : 0) : 0;
+            const int seg1 = DELTA && seg0 == 1 && count_m > 0 ? 0 : -1;
             seg_setup(seg0, true, lanebase, ntiles, S, T0, wsteps, nchunks);
-            load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+            const uint4* pre1 = nullptr;     // first tile of seg1 for this lane (null: none)
+            if (DELTA && seg1 >= 0) {
+                const uint4* lb1;
+                int64_t nt1, T01;
+                int S1, ws1, nc1;
+                seg_setup(seg1, true, lb1, nt1, S1, T01, ws1, nc1);
+                pre1 = lb1 + min(T01, nt1 - 1) * (8 * MPL);
+            }
+            bool have1 = false;              // w already holds seg1's first tile
+            if (DELTA && pre1 && wsteps == 0) {
+                load_tile<MPL>(pre1, 0, w);
+                have1 = true;
+            } else {
+                load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+            }
             {
                 const float* cv = p.cent + (size_t)l * d;
                 for (int e = tid; e < kGQ * d; e += kRT) {
@@ -436,12 +483,15 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
             }
             // the group's bounds, requested before the LUT build and used after it
+            // (the second segment's into shared memory, read when it starts)
             uint64_t thr0[kGQ];
             {
                 const CandBuf& cb0 = seg0 ? cd : cm;
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb0.thr + s_gd.q[k])) : 0ull;
+                if (DELTA && seg1 >= 0 && tid < nqg)
+                    s_thr1[tid] = *((volatile unsigned long long*)(cm.thr + s_gd.q[tid]));
             }
             __syncthreads();
             if (builder) {
@@ -459,10 +509,17 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                         // scalar round-to-nearest operations: a packed fp32x2 multiply
                         // feeding a packed add was measured not to reproduce the
                         // separately rounded x*x + a of the CPU statement
+                        // entries of the group's absent queries are left 0 (their
+                        // sums are never compared): a group of one or two queries
+                        // builds a quarter or half of the table
                         float acc[kGQ];
 #pragma unroll
                         for (int kq = 0; kq < kGQ; ++kq) {
                             float a = 0.f;
+                            if (kq > 0 && kq >= nqg) {
+                                acc[kq] = 0.f;
+                                continue;
+                            }
 #pragma unroll
                             for (int u = 0; u < DSUB; ++u) {
                                 const float r = kq == 0 ? r01[u].x : kq == 1 ? r01[u].y : kq == 2 ? r23[u].x : r23[u].y;
@@ -471,7 +528,17 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                             }
                             acc[kq] = a;
                         }
-                        lut[c * M + ps] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                        if (qmode == 4) {
+                            lut[c * M + ps] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+                        } else if (qmode == 2) {        // copies 0 and 1 (position XOR 8)
+                            float2* l2 = reinterpret_cast<float2*>(smf);
+                            const float2 v = make_float2(acc[0], acc[1]);
+                            l2[c * M + ps] = v;
+                            l2[(256 + c) * M + (ps ^ 8)] = v;
+                        } else if constexpr (M == 32) {  // copies 0..3 (position XOR 8x)
+#pragma unroll
+                            for (int x = 0; x < 4; ++x) smf[(256 * x + c) * M + (ps ^ (8 * x))] = acc[0];
+                        }
                     }
                     if (cb0 + kLB * kCStep >= 256) break;
                     load_cb(cb0 + kLB * kCStep);
@@ -505,17 +572,19 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
                 thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
             };
-            for (int seg = seg0; seg < (DELTA ? 2 : 1); ++seg) {
+            for (int si = 0; si < (DELTA ? 2 : 1); ++si) {
+            const int seg = si == 0 ? seg0 : seg1;
+            if (seg < 0) break;
             const int count = s_scount[seg];
             if (count == 0) continue;
             const CandBuf& cb = seg ? cd : cm;
             const uint32_t kbase = (uint32_t)s_skoff[seg];
-            if (seg != seg0) {                 // the delta rows after the main list: same LUT
+            if (si == 1) {                     // the main rows after the delta rows: same LUT
                 seg_setup(seg, false, lanebase, ntiles, S, T0, wsteps, nchunks);
-                load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+                if (!have1) load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+                pre1 = nullptr;
 #pragma unroll
-                for (int k = 0; k < kGQ; ++k)
-                    thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
+                for (int k = 0; k < kGQ; ++k) thr0[k] = k < nqg ? s_thr1[k] : 0ull;
                 s01 = make_float2(0.f, 0.f);
                 s23 = make_float2(0.f, 0.f);
             }
@@ -530,13 +599,26 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 for (int tl = 0; tl < kRSteps / 16; ++tl) {
                     const int x0 = t * kRSteps + 16 * tl;
                     if (x0 >= wsteps) break;
-                    load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
+                    if (DELTA && pre1 && x0 + 16 >= wsteps) {     // this warp's last tile of seg0
+                        load_tile<MPL>(pre1, 0, wn);
+                        have1 = true;
+                    } else {
+                        load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
+                    }
                     // slot of (group r, step s of the chunk) = r * kRSteps + s
                     float4* out = dist4 + rid * kRSteps + 16 * tl;
-                    if (wsteps - x0 >= 16)
-                        stagger_tile<M, 16>(lut, w, 16, j, s01, s23, out, thf, maybe);
-                    else
-                        stagger_tile<M, 15>(lut, w, wsteps - x0, j, s01, s23, out, thf, maybe);
+                    const bool full = wsteps - x0 >= 16;
+                    if (qmode == 4) {
+                        if (full) stagger_tile<M, 16, 4>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
+                        else stagger_tile<M, 15, 4>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, maybe);
+                    } else if (M != 32 || qmode == 2) {
+                        if (full) stagger_tile<M, 16, 2>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
+                        else stagger_tile<M, 15, 2>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, maybe);
+                    } else {
+                        if (full) stagger_tile<M, 16, (M == 32 ? 1 : 2)>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
+                        else stagger_tile<M, 15, (M == 32 ? 1 : 2)>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf,
+                                                                   maybe);
+                    }
 #pragma unroll
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
