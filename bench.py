@@ -82,6 +82,12 @@ CONFIGS = {
     "c2-mid": dict(kind="pq_u8", n=10_000_000, d=128, ncomp=6554, sigma=10.0, nlist=6554, M=32,
                    train_n=500_000, nq=1000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=17,
                    desc="c2-shaped lists at 10M rows, 1k queries (profiling case)"),
+    # the c2 routing shape (10k queries, 65536 centroids, d 128, nprobe 16) over 1M rows:
+    # the routing kernels' work equals c2's (profiling case for the routing kernels)
+    "c2-route": dict(kind="pq_u8", n=1_000_000, d=128, ncomp=65536, sigma=10.0, nlist=65536, M=32,
+                     train_n=200_000, nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=19,
+                     kmeans_iters=4, kmeans_sample=16 * 65536,
+                     desc="c2 routing shape over 1M rows (profiling case)"),
     # c1-shaped lists (about 2440 vectors each) at a size small enough for a full ncu capture
     "c1-mid": dict(kind="f32", n=1_000_000, d=96, ncomp=410, sigma=0.05, nlist=410, M=48, train_n=200_000,
                    nq=2000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=11,

@@ -23,6 +23,16 @@
  *     read with ivf_last_error().
  * No function aborts, exits or resets the device.
  *
+ * Environment (read on every call; every choice gives the same results bit
+ * for bit):
+ *   INSITU_SCRATCH_MB   per-batch scratch budget (default 6144); larger
+ *                       batches run in query sub-batches inside one call
+ *   INSITU_ROUTE_TC     routing kernels: 1 (default) fused tensor-core
+ *                       kernel where it applies, 2 fused or tensor-core
+ *                       matrix, 3 tensor-core matrix, 0 CUDA cores only
+ *   INSITU_EXACT_TC     exact uint8 groups (d = 128 / 256, k <= 16): 1
+ *                       (default) on the tensor cores, 0 on the CUDA cores
+ *
  * Citations are paths inside the reference project
  * (mindtravel/InSituANN-OpenSource).
  */

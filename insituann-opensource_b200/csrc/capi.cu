@@ -108,6 +108,10 @@ struct IndexCtx {
     float* tc_cn = nullptr;      // [nlist] squared centroid norms
     float* tc_cne = nullptr;     // the same per tile row, +inf for invalid lists and padding
     float* tc_cnmax = nullptr;   // largest squared norm of a valid centroid
+    // tensor map over the uint8 rows of an exact index (exact_tc.cu); tc_rows_ok
+    // false: the exact search uses the CUDA-core kernels
+    alignas(64) unsigned char tc_rows_map[128] = {};
+    bool tc_rows_ok = false;
     int M = 0, dsub = 0;
     float* f32_rows = nullptr;   // fp32 index (ivf_load_dataset / streaming upload): cluster-major rows
     float* f32_norms = nullptr;  // and their L2 norms (cosine)
@@ -154,7 +158,8 @@ struct BatchCtx {
     float* out_dist = nullptr;
     int32_t* out_idist = nullptr;
     int* counter = nullptr;
-    int* overflow = nullptr;      // device flags: [0] candidate overflow, [1] routing wait gave up
+    int* overflow = nullptr;      // device flags: [0] candidate overflow, [1] routing wait gave up,
+                                  // [2] fine-search (tensor-core) wait gave up
     int* h_overflow = nullptr;    // pinned mirror, read after the stream syncs
     int res_nq = 0, res_k = 0;
     int probes_nq = 0, probes_np = 0;
@@ -321,6 +326,13 @@ void prepare_route_tc(IndexCtx* x, int nlist, int d) {
 //   2  the fused kernel where it applies, else the tensor-core matrix;
 //   3  the tensor-core matrix + rescoring for every shape it covers.
 // Read on every call.
+// Exact uint8 groups, INSITU_EXACT_TC: 1 (default) the tensor-core kernel
+// where it applies, 0 the CUDA-core grouped kernel.  Read on every call.
+int exact_tc_mode() {
+    const char* v = std::getenv("INSITU_EXACT_TC");
+    return (v && v[0] == '0') ? 0 : 1;
+}
+
 int route_tc_mode() {
     const char* v = std::getenv("INSITU_ROUTE_TC");
     if (!v || !v[0]) return 1;
@@ -441,8 +453,16 @@ void require_probes(BatchCtx* b, int nq, int nprobe) {
             "no probe table for this (n_query, n_probes): route or set probes first", IVF_ESTATE);
 }
 
+// clears the flags a fine search raises (candidate overflow, tensor-core wait)
+void reset_fine_flags(BatchCtx* b) {
+    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    ck(cudaMemsetAsync(b->overflow + 2, 0, sizeof(int), b->st), "memset");
+}
+
 void queue_overflow_check(BatchCtx* b) {
     ck(cudaMemcpyAsync(b->h_overflow, b->overflow, sizeof(int), cudaMemcpyDeviceToHost, b->st), "overflow D2H");
+    ck(cudaMemcpyAsync(b->h_overflow + 2, b->overflow + 2, sizeof(int), cudaMemcpyDeviceToHost, b->st),
+       "flag D2H");
 }
 
 // exact uint8 search on the batch probes; keys_out: per-query sorted top-k keys instead of results
@@ -462,6 +482,8 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
                          (size_t)nsub * nprobe < ((size_t)1 << 25);
     WorkList wl = worklist_for(b, x, nsub, nprobe, &tmp, &tmp_bytes, grouped);
     if (grouped) wl.gq = 64;
+    // groups on the tensor cores (exact_tc.cu) unless INSITU_EXACT_TC=0
+    const bool use_tc = grouped && x->tc_rows_ok && exact_tc_usable(x->d, k) && exact_tc_mode() != 0;
     CandBuf cb{};
     cb.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap);
     cb.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);
@@ -470,7 +492,7 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
     cb.cap = cap;
     cb.R = k;
     uint64_t* topk = ensure<uint64_t>(b, b->exk, (size_t)nsub * k);
-    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    reset_fine_flags(b);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
         {
@@ -482,7 +504,11 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
         }
         {
             StageScope stage(b, IVF_STAGE_SCAN);
-            if (grouped)
+            if (use_tc)
+                ck(exact_tc_scan(x->tc_rows_map, b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl,
+                                 n * nprobe, cb, b->counter, b->overflow + 2, b->st),
+                   "exact_tc_scan");
+            else if (grouped)
                 ck(exact_group_scan(b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl, n * nprobe, cb,
                                     b->counter, b->st),
                    "exact_group_scan");
@@ -526,7 +552,7 @@ void run_f32(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, bool cosine) {
     cb.cap = cap;
     cb.R = k;
     uint64_t* topk = ensure<uint64_t>(b, b->exk, (size_t)nsub * k);
-    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    reset_fine_flags(b);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
         {
@@ -614,7 +640,7 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
         cd.slack = slack_d;
         s1d = ensure<uint64_t>(b, b->s1d, (size_t)nsub * Rd);
     }
-    ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+    reset_fine_flags(b);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
         PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
@@ -673,8 +699,8 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
 }
 
 void check_overflow_after_sync(BatchCtx* b) {
-    if ((b->h_overflow[0] | b->h_overflow[1]) & 4)
-        fail(IVF_ECUDA, "a bounded device wait of the tensor-core routing gave up");
+    if ((b->h_overflow[0] | b->h_overflow[1] | b->h_overflow[2]) & 4)
+        fail(IVF_ECUDA, "a bounded device wait of a tensor-core kernel gave up");
     if (*b->h_overflow)
         fail(IVF_EOVERFLOW, "a candidate buffer overflowed; raise INSITU_SCRATCH_MB or lower n_probes");
 }
@@ -950,8 +976,9 @@ void* ivf_create_batch_context(int max_n_query, int n_dim, int max_n_probes, int
             b->out_idist = dalloc<int32_t>((size_t)max_n_query * max_k, b->owned);
             b->counter = dalloc<int>(4, b->owned);
             b->overflow = dalloc<int>(4, b->owned);
+            ck(cudaMemset(b->overflow, 0, sizeof(int) * 4), "memset");
             ck(cudaMallocHost(&b->h_overflow, sizeof(int) * 4), "cudaMallocHost");
-            b->h_overflow[0] = b->h_overflow[1] = 0;
+            b->h_overflow[0] = b->h_overflow[1] = b->h_overflow[2] = 0;
         } catch (...) {
             if (b->st) cudaStreamDestroy(b->st);
             free_all(b->owned);
@@ -1136,6 +1163,9 @@ int ivf_u8_load(void* idx_ctx, const uint8_t* base_u8, const long long* offsets,
                 x->main.sqnorm = dalloc<int32_t>((size_t)n, x->main.owned);
                 ck(u8_row_sqnorms(x->main.data, n, d, x->main.sqnorm, 0), "u8_row_sqnorms");
                 ck(cudaDeviceSynchronize(), "u8_row_sqnorms");
+                x->tc_rows_ok =
+                    exact_tc_usable(d, 1) && exact_tc_map(x->main.data, n, d, x->tc_rows_map) == cudaSuccess;
+                cudaGetLastError();
             }
         } catch (...) {
             x->main.release();
@@ -1705,7 +1735,7 @@ int ivf_pq_shard_scan(void* batch_ctx, void* idx_ctx, int n_query, int n_probes,
         PQParams p = pq_params(x, b->q, false);
         if (pass == 0) {
             StageScope stage(b, IVF_STAGE_WORKLIST);
-            ck(cudaMemsetAsync(b->overflow, 0, sizeof(int), b->st), "memset");
+            reset_fine_flags(b);
             ck(reset_candidates(sp.cm, n_query, b->st), "reset_candidates");
         }
         const int col0 = pass == 0 ? 0 : 1, ncol = pass == 0 ? 1 : n_probes - 1;

@@ -32,6 +32,17 @@ cudaError_t build_worklist(const int32_t* probes, int nq, int nprobe, int nlist_
                            int seed_part = -1);
 constexpr int kGroupQueries = 4;
 
+// ---- exact uint8 search on the tensor cores (exact_tc.cu) ------------------
+// d in {128, 256}, 0 < k <= 16
+bool exact_tc_usable(int d, int k);
+// the tensor map (128 bytes, 64-byte aligned) over rows [n, d] of an exact index
+cudaError_t exact_tc_map(const uint8_t* rows, int64_t n, int d, void* map_out);
+// the grouped exact search (groups of up to 64 queries, wl.gq = 64) with q.x
+// on the tensor cores; the same candidate keys as exact_group_scan.  flag is
+// raised (4) when a bounded wait gave up.
+cudaError_t exact_tc_scan(const void* map, const uint8_t* q_u8, int d, int k, ListStore ls, WorkList wl,
+                          int max_groups, CandBuf cb, int* work_counter, int* flag, cudaStream_t st);
+
 // ---- coarse routing (route.cu) --------------------------------------------
 // valid[c] = 1 when the centroid's L2 norm is >= 1e-6, else 0.
 cudaError_t route_centroid_valid(const float* cent, int nlist, int d, uint8_t* valid, cudaStream_t st);

@@ -32,6 +32,7 @@
 #include <cuda_bf16.h>
 
 #include "launch.h"
+#include "tc.cuh"
 
 namespace isb {
 
@@ -40,65 +41,7 @@ namespace {
 constexpr int kTCM = 128;                 // queries per CTA (MMA M)
 constexpr int kTCN = 64;                  // centroids per tile (MMA N)
 constexpr int kTCThreads = 128;           // 4 warps: one TMEM lane (query row) per thread
-constexpr int kTCWaitSpins = 1 << 22;     // bounded mbarrier polls
 constexpr int kPMaxRouteD = 512;          // largest d of the fallback rows
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-// byte offset of the 16-byte chunk (row, k8) -- elements k = 8*k8 .. 8*k8+7 --
-// in the canonical layout of an operand of R rows
-__host__ __device__ __forceinline__ size_t tc_chunk_off(int row, int k8, int R) {
-    return (size_t)(k8 >> 1) * ((size_t)R * 32) + (size_t)(row >> 3) * 256 + (size_t)(k8 & 1) * 128 +
-           (size_t)(row & 7) * 16;
-}
-
-__device__ __forceinline__ uint64_t umma_smem_desc(uint32_t saddr) {
-    uint64_t d = 0;
-    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);          // start address, 16-byte units
-    d |= (uint64_t)(128u >> 4) << 16;                  // leading byte offset: K halves
-    d |= (uint64_t)(256u >> 4) << 32;                  // stride byte offset: 8-row groups
-    d |= (uint64_t)1 << 46;                            // descriptor version of sm_100
-    return d;                                          // base offset 0, no swizzle
-}
-
-// kind::f16 instruction descriptor: bf16 A and B (K-major), fp32 D, M x N
-__host__ __device__ constexpr uint32_t umma_idesc_bf16(int M, int N) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, int count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_arrive_expect(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (int i = 0; i < kTCWaitSpins; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
-}
-
-__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
 
 __device__ __forceinline__ uint32_t bf16_bits(__nv_bfloat16 h) { return (uint32_t)__bfloat16_as_ushort(h); }
 
@@ -571,19 +514,6 @@ constexpr size_t kFSmemCap = 227 * 1024 - 2560;  // dynamic shared memory of one
 
 __host__ __device__ constexpr size_t route_fused_region(int d, int list) {
     return ((kFSmemCap - route_fused_fixed(d, list)) / 128) * 128;
-}
-
-// wait on an mbarrier phase, bounded; gives up early once *fail is set
-__device__ __forceinline__ bool mbar_wait_or(uint64_t* bar, uint32_t parity, const volatile int* fail) {
-    for (int i = 0; i < kTCWaitSpins; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 31) == 31 && *fail) return false;
-    }
-    return false;
-}
-
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
 template <int LMAX, int LIST>

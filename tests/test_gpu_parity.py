@@ -126,6 +126,40 @@ def test_exact_grouped_many_queries(cuda_ok, d, k):
     assert np.array_equal(gi, oi) and np.array_equal(gd, od)
 
 
+@pytest.mark.parametrize("d,k,deleted", [(128, 10, False), (128, 16, True), (256, 1, False), (256, 7, True)])
+def test_exact_tensor_core_kernel_equals_cuda_core_kernel(cuda_ok, d, k, deleted, monkeypatch):
+    """the tcgen05 (kind::i8) grouped exact kernel and the dp4a grouped kernel
+    give the oracle's results: lists of several 128-row tiles and ragged
+    last tiles, more than 64 queries per list, a list probed twice, invalid
+    probe ids, exact distance ties and (optionally) deleted rows."""
+    n, nlist, nq, nprobe = 30000, 12, 500, 5
+    base = synth.mixture_u8(n, d, 12, 12.0, seed=81)
+    e = synth.build_u8_index(base, nlist, seed=81, iters=4)
+    e["base_cm"][500:900] = e["base_cm"][499]            # ties, broken by original id
+    q = synth.mixture_u8(nq, d, 12, 12.0, seed=81, stream_base=1 << 20).numpy()
+    probes, _ = oracle.route_l2(q.astype(np.float32), e["centroids"], nprobe)
+    probes[::9, 1] = probes[::9, 0]
+    probes[::13, 2] = -1
+    dele = synth.delete_mask(e["r2o"], 0.2) if deleted else None
+    out = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("INSITU_EXACT_TC", mode)
+        index = ib.Index().load_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], e["centroids"])
+        if dele is not None:
+            index.set_deleted(dele)
+        b = ib.Batch(nq, d, nprobe, k, nlist)
+        b.stage1_prepare(q.astype(np.float32))
+        b.set_probes(probes)
+        b.u8_search(index, nq, nprobe, k, route=False)
+        out[mode] = b.get_results_i32(nq, k)
+        b.close()
+        index.close()
+    oi, od = oracle.exact_u8(e["base_cm"], e["offsets"], e["counts"], e["r2o"], q, probes, k, deleted=dele)
+    for mode in ("1", "0"):
+        gi, gd = out[mode]
+        assert np.array_equal(gi, oi) and np.array_equal(gd, od), f"INSITU_EXACT_TC={mode}"
+
+
 @pytest.mark.parametrize("d", [64, 128])
 def test_exact_deletes(cuda_ok, d):
     """deleted positions are not scanned (d = 64: per-pair kernel, d = 128: grouped)."""
