@@ -462,13 +462,15 @@ def run_exact(args, cfg):
     peak, peak_kind = peaks()
     achieved = bytes_search / (scan_ms / 1000.0) / 1e9
     traffic = None
-    prof_path = os.path.join(ROOT, "profiles", f"exact_group_kernel_c0_nprobe{nprobe}.md")
+    # the grouped exact search runs on the tensor cores unless INSITU_EXACT_TC=0
+    kname = "exact_group_kernel" if os.environ.get("INSITU_EXACT_TC", "1").startswith("0") else "exact_tc_kernel"
+    prof_path = os.path.join(ROOT, "profiles", f"{kname}_c0_nprobe{nprobe}.md")
     if os.path.exists(prof_path):
         for line in open(prof_path):
             if line.startswith("dram_bytes_per_search:"):
                 traffic = int(line.split(":")[1].strip())
     roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": traffic, "kernel": "exact_group_kernel<8> (1 launch per search)", "peak_source": peak_kind,
+                "traffic": traffic, "kernel": f"{kname} (d = 128; 1 launch per search)", "peak_source": peak_kind,
                 "algorithmic_bytes_per_launch": bytes_search, "kernel_ms_per_launch": scan_ms}
     cpu = None
     if not args.no_cpu_baseline:
@@ -925,15 +927,19 @@ def main():
                 ostep(np_, ov)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             torch.cuda.synchronize()
+            batch.profile(True)
             e0.record(ext)
             for _ in range(args.steps):
                 ostep(np_, ov)
             e1.record(ext)
             torch.cuda.synchronize()
-            return nq / (e0.elapsed_time(e1) / args.steps / 1000.0)
+            st = {s_: round(v / args.steps, 4) for s_, v in batch.stage_ms().items()}
+            batch.profile(False)
+            return nq / (e0.elapsed_time(e1) / args.steps / 1000.0), st
 
         onp = sorted({nprobe, 64})
-        base_qps = {np_: timed(np_, False) for np_ in onp}
+        base = {np_: timed(np_, False) for np_ in onp}
+        base_qps = {np_: v[0] for np_, v in base.items()}
         runs = []
         for nd in sizes:
             t_g = time.time()
@@ -952,11 +958,17 @@ def main():
                                           **rr_kw(idx["base_rr"]))
             o_par = bool(np.array_equal(ei, oid[:Po]) and np.array_equal(ed, odd[:Po]))
             for np_ in onp:
-                qw = timed(np_, True)
+                qw, st_w = timed(np_, True)
+                # the delta's share of the scanned bytes: delta rows over all rows of the probed lists
+                pr = batch.get_probes(nq, np_)
+                dsum = float(dseg["counts"][pr].sum())
+                share = dsum / (dsum + float(counts[pr].sum()))
                 runs.append({"delta_vectors": nd, "nprobe": np_, "qps_without": base_qps[np_], "qps_with": qw,
-                             "overhead": 1.0 - qw / base_qps[np_], "parity_vs_oracle": o_par,
-                             "parity_queries": Po})
-                log(f"[bench] overlay {nd}: nprobe {np_}: {base_qps[np_]:.0f} -> {qw:.0f} qps, parity {o_par}")
+                             "overhead": 1.0 - qw / base_qps[np_], "delta_share_of_scanned": share,
+                             "stages_ms_without": base[np_][1], "stages_ms_with": st_w,
+                             "parity_vs_oracle": o_par, "parity_queries": Po})
+                log(f"[bench] overlay {nd}: nprobe {np_}: {base_qps[np_]:.0f} -> {qw:.0f} qps "
+                    f"(delta share {share:.3f}), parity {o_par}; stages {base[np_][1]} -> {st_w}")
             index.clear_delta()
             del dseg, raw
         overlay = {"delta_topk": 16, "runs": runs}
