@@ -71,7 +71,15 @@ CONFIGS = {
                train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(32, 64, 128), seed=20260603,
                kmeans_iters=10, kmeans_sample=16 * 262144,
                desc="c3: residual-PQ IVF, 1B x 128 uint8 (262144-comp mixture, Zipf(1.1) weights, sigma 10), "
-                    "nlist 262144, M=32 x 8b, 10k queries, k=10, rerank_n=512 (uint8 rerank), lists sharded"),
+                    "nlist 262144, M=32 x 8b, 10k queries, k=10, rerank_n=512 (uint8 rerank), lists sharded",
+               # Zipf-skewed lists (the largest about 10x the mean after k-means) need larger
+               # candidate buffers for a whole 10k-query batch in one sub-batch
+               scratch_mb=65536),
+    # c3's shapes (Zipf(1.1) weights, nlist 262144, nprobe 32) at 100M rows: a 2-GPU check of c3's path
+    "c3-small": dict(kind="pq_u8", n=100_000_000, d=128, ncomp=262144, sigma=10.0, zipf=1.1, nlist=262144, M=32,
+                     train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=32, sweep=(32,), seed=20260603,
+                     kmeans_iters=6, kmeans_sample=8 * 262144, scratch_mb=49152,
+                     desc="c3 shapes at 100M rows (Zipf(1.1), nlist 262144)"),
     # c2 at a tenth of the rows (the c2 list count and shapes): a quick check of the c2 path
     "c2-small": dict(kind="pq_u8", n=10_000_000, d=128, ncomp=65536, sigma=10.0, nlist=65536, M=32,
                      train_n=500_000, nq=10_000, k=10, rerank_n=512, nprobe=16, sweep=(16,), seed=20260602,
@@ -613,7 +621,7 @@ def main():
     if N > 1:
         # the phased sharded search keeps a whole 10k-query batch in one
         # sub-batch; at c2 its candidate buffers pass the 6 GB default scratch
-        os.environ.setdefault("INSITU_SCRATCH_MB", "24576")
+        os.environ.setdefault("INSITU_SCRATCH_MB", str(cfg.get("scratch_mb", 24576)))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     if N > 1:
