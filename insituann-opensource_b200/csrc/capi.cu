@@ -484,6 +484,7 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
     if (grouped) wl.gq = 64;
     // groups on the tensor cores (exact_tc.cu) unless INSITU_EXACT_TC=0
     const bool use_tc = grouped && x->tc_rows_ok && exact_tc_usable(x->d, k) && exact_tc_mode() != 0;
+    if (use_tc) wl.gq = 127;     // the tensor-core kernel takes up to 127 queries per group
     CandBuf cb{};
     cb.keys = ensure<uint64_t>(b, b->cand_m, (size_t)nsub * cap);
     cb.cnt = ensure<int32_t>(b, b->cnt_m, (size_t)nsub);

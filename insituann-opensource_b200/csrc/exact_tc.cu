@@ -2,12 +2,18 @@
 // kind::i8).
 //
 // The same work as exact_group_kernel (exact.cu): one CTA takes a list and up
-// to 64 queries that probe it (a group of the work list), and every query
+// to 127 queries that probe it (a group of the work list), and every query
 // keeps the k smallest keys (distance, original id) of the list.  q.x comes
 // from the tensor cores: u8 x u8 products accumulated in s32 in tensor memory,
 // exact (a row of d <= 256 bytes sums at most 256 * 255^2 < 2^31), so
 // |q|^2 + |x|^2 - 2 q.x is the reference's integer sum of squared differences
 // (updates/exact_update.cu:632-666, cpu_fine_kernels_v3_u8.cpp:356-595).
+//
+// The MMA has the group's queries as M (128 rows of A, in shared memory) and
+// a tile of 128 list rows as N (B), so accumulator lane i holds query i's dot
+// products with the tile's rows: each epilogue thread owns one query and half
+// of the tile's columns and keeps that query's k smallest keys in registers,
+// with no exchange between threads until the list is done.
 //
 // A CTA is 10 warps:
 //   warp 0, one lane   tensor copies: tiles of 128 list rows (d bytes each)
@@ -17,19 +23,21 @@
 //                      list or lie past the tensor (read as zeros) and are
 //                      masked by the epilogue;
 //   warp 1             allocates tensor memory; one lane issues, per tile,
-//                      d / 32 MMAs (M = 128 rows, N = 64 queries, K = 32)
-//                      into one of 4 accumulators of 64 columns;
-//   warps 2..9         epilogue: warp w reads the accumulator's lanes
-//                      32 (w % 4) .. + 31 (tile rows) and columns
-//                      32 ((w - 2) / 4) .. + 31 (queries); a key below its
-//                      query's running k-th is staged in shared memory (one
-//                      atomic per warp and query); a query whose staging area
-//                      may not hold another tile, and every query after the
-//                      list's last tile, merges its staged keys into its k
-//                      smallest (one warp per 8 queries).
-// The queries of a group sit in shared memory in the same swizzled layout
-// (the MMA's B operand).  Every wait is bounded; a wait that gives up sets
-// the error flag, the CTA drains its own copies and MMAs and returns.
+//                      d / 32 MMAs (M = 128 queries, N = 128 rows, K = 32)
+//                      into one of 2 accumulators of 128 columns;
+//   warps 2..9         epilogue: warp w reads lanes 32 (w % 4) .. + 31
+//                      (queries) and columns 64 ((w - 2) / 4) .. + 63 (tile
+//                      rows); a row whose distance is at most the query's
+//                      running k-th (or its bound from lists done before) is
+//                      kept in the thread's slots in shared memory, and the
+//                      slots are then inserted into the thread's sorted k
+//                      smallest (a compare-exchange chain in registers).
+// After the list's last tile the two threads of a query merge their k
+// smallest and append them to the query's candidate buffer.  Keys are ranked
+// by (distance, position) while scanning: a list's rows are stored in
+// increasing original id, so within a list that is the (distance, id) order.
+// Every wait is bounded; a wait that gives up sets the error flag, the CTA
+// drains its own copies and MMAs and returns.
 #include <cstring>
 #include <mutex>
 
@@ -40,46 +48,47 @@ namespace isb {
 
 namespace {
 
-constexpr int kTM = 128;               // list rows per tile (MMA M)
-constexpr int kTQ = 64;                // queries per group (MMA N)
-constexpr int kTAcc = 4;               // tensor-memory accumulators
+constexpr int kTQ = 128;               // queries per group (MMA M; groups hold up to 127)
+constexpr int kTN = 128;               // list rows per tile (MMA N)
+constexpr int kTAcc = 2;               // tensor-memory accumulators of kTN columns
 constexpr int kTWarps = 10;
 constexpr int kTThreads = 32 * kTWarps;
 constexpr int kTEpi = 256;             // epilogue threads (warps 2..9)
 constexpr int kTKMax = 16;             // largest k
-constexpr int kTCap = 160;             // staged keys per query (>= 128 + 32)
+constexpr int kTSlots = 32;            // kept rows per thread between insertions
 constexpr int kTMaxStages = 6;
 
 __host__ __device__ constexpr size_t exact_tc_fixed(int d) {
-    return (size_t)kTQ * d                              // queries (B operand)
-           + sizeof(uint64_t) * kTQ * kTKMax            // k smallest per query
-           + sizeof(uint64_t) * kTQ * kTCap;            // staged keys
+    return (size_t)kTQ * d                              // queries (A operand)
+           + sizeof(uint32_t) * kTSlots * kTEpi         // kept rows (also the final exchange)
+           + sizeof(uint2) * 8 * 64;                    // per epilogue warp: its rows' |x|^2 and position
 }
 
 // stages of list tiles that fit beside the fixed arrays (1 KB kept for
-// aligning the base to the swizzle atom)
+// aligning the base to the swizzle atom, 2 KB for static shared memory)
 __host__ __device__ inline int exact_tc_stages(int d) {
-    const size_t cap = 227 * 1024 - 1024 - 2048;       // 2 KB of static shared memory aside
-    const int st = (int)((cap - exact_tc_fixed(d)) / ((size_t)kTM * d));
+    const size_t cap = 227 * 1024 - 1024 - 2048;
+    const int st = (int)((cap - exact_tc_fixed(d)) / ((size_t)kTN * d));
     return st > kTMaxStages ? kTMaxStages : st;
 }
 
 __host__ __device__ inline size_t exact_tc_smem(int d) {
-    return (size_t)exact_tc_stages(d) * kTM * d + exact_tc_fixed(d) + 1024;
+    return (size_t)exact_tc_stages(d) * kTN * d + exact_tc_fixed(d) + 1024;
 }
 
 // barrier of the 8 epilogue warps (named barrier 1)
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory"); }
 
-// the same barrier, returning whether any epilogue thread passed v = true
-__device__ __forceinline__ bool epi_sync_any(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "n"(kTEpi)
-        : "memory");
-    return r != 0;
+// inserts key into the ascending list lv (one compare-exchange per slot; the
+// list's first kTKMax - k slots hold 0 and never move)
+__device__ __forceinline__ void topk_insert(uint64_t (&lv)[kTKMax], uint64_t key) {
+#pragma unroll
+    for (int e = 0; e < kTKMax; ++e) {
+        const uint64_t a = lv[e];
+        const bool lt = key < a;
+        lv[e] = lt ? key : a;
+        key = lt ? a : key;
+    }
 }
 
 template <int NKB>   // 128-byte K blocks per row: d = 128 NKB
@@ -96,19 +105,16 @@ __global__ void __launch_bounds__(kTThreads, 1)
     __shared__ __align__(8) uint64_t bar_ae[kTAcc];
     __shared__ uint32_t s_tmem;
     __shared__ int s_fail, s_item;
-    __shared__ unsigned long long s_tau[kTQ];
-    __shared__ int s_cnt[kTQ], s_qn[kTQ], s_qid[kTQ];
-    const size_t tile_bytes = (size_t)kTM * d;
-    unsigned char* sA = sm;
-    unsigned char* sB = sm + (size_t)stages * tile_bytes;
-    uint64_t* sTop = reinterpret_cast<uint64_t*>(sB + (size_t)kTQ * d);     // [kTQ][kTKMax]
-    uint64_t* sStage = sTop + kTQ * kTKMax;                                  // [kTQ][kTCap]
+    const size_t tile_bytes = (size_t)kTN * d;
+    unsigned char* sA = sm + (size_t)stages * tile_bytes;                       // queries [kTQ][d], swizzled
+    uint32_t* sSlot = reinterpret_cast<uint32_t*>(sA + (size_t)kTQ * d);         // [kTSlots][kTEpi]
+    uint2* sRow = reinterpret_cast<uint2*>(sSlot + kTSlots * kTEpi);             // [8 warps][64]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const volatile int* vfail = &s_fail;
 
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(kTAcc * kTQ)
+                     "r"(kTAcc * kTN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -142,38 +148,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
         const int l = (int)(pk >> 32), p0 = (int)((pk >> 7) & 0x1FFFFFF), nqg = (int)(pk & 127);
         const int count = ls.counts[l];
         const int64_t off = ls.offsets[l];
-        const int ntiles = (count + kTM - 1) / kTM;
-        // the group's queries in the swizzled B layout (rows past nqg are zero)
+        const int ntiles = (count + kTN - 1) / kTN;
+        // the group's queries in the swizzled A layout (rows past nqg are zero)
         for (int e = tid; e < kTQ * 8 * NKB; e += kTThreads) {
             const int r = e / (8 * NKB), c = e % (8 * NKB), kb = c >> 3, cc = c & 7;
             uint4 v = make_uint4(0u, 0u, 0u, 0u);
             if (r < nqg) v = __ldg(reinterpret_cast<const uint4*>(q_u8 + (size_t)wl.pair_q[p0 + r] * d) + c);
-            *reinterpret_cast<uint4*>(sB + (size_t)kb * kTQ * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+            *reinterpret_cast<uint4*>(sA + (size_t)kb * kTQ * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
         }
-        if (tid < kTQ) {
-            const int r = tid;
-            const int q = r < nqg ? wl.pair_q[p0 + r] : -1;
-            uint32_t n2 = 0;
-            if (q >= 0) {
-                const uint4* qr = reinterpret_cast<const uint4*>(q_u8 + (size_t)q * d);
-#pragma unroll
-                for (int c = 0; c < 8 * NKB; ++c) {
-                    const uint4 v = __ldg(qr + c);
-                    n2 = __dp4a(v.x, v.x, n2);
-                    n2 = __dp4a(v.y, v.y, n2);
-                    n2 = __dp4a(v.z, v.z, n2);
-                    n2 = __dp4a(v.w, v.w, n2);
-                }
-            }
-            s_qn[r] = (int)n2;
-            s_qid[r] = q;
-            s_cnt[r] = 0;
-            // a query starts from its bound over the lists done so far (the k-th
-            // of k keys already in its buffer): a key at or above it cannot be
-            // among the query's k smallest
-            s_tau[r] = q >= 0 ? *((volatile unsigned long long*)(cb.thr + q)) : kKeyNone;
-        }
-        for (int e = tid; e < kTQ * kTKMax; e += kTThreads) sTop[e] = kKeyNone;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         tc_fence_before();
         __syncthreads();
@@ -189,10 +171,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
                         break;
                     }
                     mbar_arrive_expect(&bar_full[s], (uint32_t)tile_bytes);
-                    const int y = (int)(off + (int64_t)t * kTM);
+                    const int y = (int)(off + (int64_t)t * kTN);
 #pragma unroll
                     for (int kb = 0; kb < NKB; ++kb)
-                        tma_load_2d(sA + (size_t)s * tile_bytes + (size_t)kb * kTM * 128, &tmap, 128 * kb, y,
+                        tma_load_2d(sm + (size_t)s * tile_bytes + (size_t)kb * kTN * 128, &tmap, 128 * kb, y,
                                     &bar_full[s]);
                     issued = g + 1;
                 }
@@ -200,8 +182,8 @@ __global__ void __launch_bounds__(kTThreads, 1)
             __syncwarp();
         } else if (warp == 1) {
             if (lane == 0) {
-                constexpr uint32_t idesc = umma_idesc_u8(kTM, kTQ);
-                const uint32_t b_addr = smem_u32(sB);
+                constexpr uint32_t idesc = umma_idesc_u8(kTQ, kTN);
+                const uint32_t a_addr = smem_u32(sA);
                 for (int t = 0; t < ntiles; ++t) {
                     const int64_t g = gt + t;
                     const int s = (int)(g % stages), a = (int)(g % kTAcc);
@@ -214,15 +196,15 @@ __global__ void __launch_bounds__(kTThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(sA + (size_t)s * tile_bytes);
-                    const uint32_t dacc = tmem + (uint32_t)(a * kTQ);
+                    const uint32_t b_addr = smem_u32(sm + (size_t)s * tile_bytes);
+                    const uint32_t dacc = tmem + (uint32_t)(a * kTN);
 #pragma unroll
                     for (int kk = 0; kk < 4 * NKB; ++kk) {
-                        // K block kk / 4 of the rows, 32 bytes kk % 4 inside its swizzled 128
-                        const uint32_t ko = (uint32_t)(kk >> 2) * (kTM * 128) + (uint32_t)(kk & 3) * 32;
-                        const uint32_t kq = (uint32_t)(kk >> 2) * (kTQ * 128) + (uint32_t)(kk & 3) * 32;
-                        const uint64_t ad = umma_smem_desc_sw128(a_addr + ko);
-                        const uint64_t bd = umma_smem_desc_sw128(b_addr + kq);
+                        // K block kk / 4, 32 bytes kk % 4 inside its swizzled 128
+                        const uint32_t ka = (uint32_t)(kk >> 2) * (kTQ * 128) + (uint32_t)(kk & 3) * 32;
+                        const uint32_t kr = (uint32_t)(kk >> 2) * (kTN * 128) + (uint32_t)(kk & 3) * 32;
+                        const uint64_t ad = umma_smem_desc_sw128(a_addr + ka);
+                        const uint64_t bd = umma_smem_desc_sw128(b_addr + kr);
                         const uint32_t acc = kk ? 1u : 0u;
                         asm volatile(
                             "{\n .reg .pred pa;\n setp.ne.b32 pa, %4, 0;\n"
@@ -238,114 +220,114 @@ __global__ void __launch_bounds__(kTThreads, 1)
             __syncwarp();
         } else {
             const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
-            const int trow = quarter * 32 + lane;             // TMEM lane = tile row
+            const int qi = quarter * 32 + lane;               // TMEM lane = the thread's query
+            const bool live = qi < nqg;
+            const int q = live ? wl.pair_q[p0 + qi] : -1;
+            // |q|^2 and the bound over the lists done before: a key above it cannot be
+            // among the query's k smallest (the buffer already holds k keys at or below it)
+            uint32_t qn = 0;
+            uint32_t tau = 0xFFFFFFFFu;
+            if (live) {
+                const uint4* qr = reinterpret_cast<const uint4*>(q_u8 + (size_t)q * d);
+#pragma unroll
+                for (int c = 0; c < 8 * NKB; ++c) {
+                    const uint4 v = __ldg(qr + c);
+                    qn = __dp4a(v.x, v.x, qn);
+                    qn = __dp4a(v.y, v.y, qn);
+                    qn = __dp4a(v.z, v.z, qn);
+                    qn = __dp4a(v.w, v.w, qn);
+                }
+                tau = (uint32_t)(*((volatile unsigned long long*)(cb.thr + q)) >> 32);
+            }
+            uint64_t lv[kTKMax];
+#pragma unroll
+            for (int i = 0; i < kTKMax; ++i) lv[i] = i < kTKMax - k ? 0ull : kKeyNone;
+            uint32_t lim = tau;                                // distances above it are not kept
+            uint2* myrows = sRow + ew * 64;
+            uint32_t* myslot = sSlot + (tid - 64);             // slot c at [c][kTEpi]
             for (int t = 0; t < ntiles; ++t) {
                 const int64_t g = gt + t;
                 const int a = (int)(g % kTAcc);
-                // this row's id and |x|^2 (a deleted position has id 0xFFFFFFFF: skipped)
-                const int v = t * kTM + trow;
-                uint32_t id = 0xFFFFFFFFu;
-                int xn = 0;
-                if (v < count) {
-                    const int64_t pos = off + v;
-                    if (!(ls.deleted && ls.deleted[pos])) id = ls.ids ? (uint32_t)ls.ids[pos] : (uint32_t)pos;
-                    xn = ls.sqnorm[pos];
+                // |x|^2 and position of this warp's 64 rows (0xFFFFFFFF: past the list or deleted)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int v = t * kTN + half * 64 + 32 * h + lane;
+                    uint2 rw = make_uint2(0u, 0xFFFFFFFFu);
+                    if (v < count) {
+                        const int64_t pos = off + v;
+                        if (!(ls.deleted && ls.deleted[pos])) rw = make_uint2((uint32_t)ls.sqnorm[pos], (uint32_t)pos);
+                    }
+                    myrows[32 * h + lane] = rw;
                 }
-                // a wait that gave up is acted on at the barrier after the filter,
-                // which all epilogue warps reach (the values read are then discarded)
                 const bool got = mbar_wait_or(&bar_af[a], (uint32_t)((g / kTAcc) & 1), vfail);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) s_fail = 1;
+                    break;
+                }
                 tc_fence_after();
-                uint32_t dot[32];
-                tmem_ld32(tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * kTQ + half * 32), dot);
+                uint32_t dot[2][32];
+                const uint32_t ta = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(a * kTN + half * 64);
+                tmem_ld32(ta, dot[0]);
+                tmem_ld32(ta + 32, dot[1]);
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&bar_ae[a]);
-                // keys below their query's k-th go to its staging area
 #pragma unroll
-                for (int i = 0; i < 32; ++i) {
-                    const int r = half * 32 + i;
-                    if (r >= nqg) break;
-                    const uint32_t dist = (uint32_t)(s_qn[r] + xn) - 2u * dot[i];
-                    const uint64_t key = make_key(dist, id);
-                    const bool pass = id != 0xFFFFFFFFu && key < s_tau[r];
-                    const unsigned ball = __ballot_sync(0xffffffffu, pass);
-                    if (ball) {
-                        int base = 0;
-                        if (lane == 0) base = atomicAdd(&s_cnt[r], __popc(ball));
-                        base = __shfl_sync(0xffffffffu, base, 0);
-                        if (pass) sStage[r * kTCap + base + __popc(ball & ((1u << lane) - 1u))] = key;
-                    }
-                }
-                if (epi_sync_any(!got)) {
-                    if (tid == 64) s_fail = 1;
-                    break;
-                }
-                // merges: a query whose staging area could overflow in the next
-                // tile, and every query after the last tile
-                const bool last = t == ntiles - 1;
-                for (int rr = 0; rr < 8; ++rr) {
-                    const int r = 8 * ew + rr;
-                    if (r >= nqg) break;
-                    const int ns = s_cnt[r];
-                    if (ns == 0 || (!last && ns <= kTCap - kTM)) continue;
-                    const int m = k + ns;
-                    if (m <= 32) {
-                        // lane i takes element i of (k smallest, staged) and writes it
-                        // at its rank among all m, ties by element index
-                        const uint64_t mine = lane < k ? sTop[r * kTKMax + lane]
-                                                       : (lane < m ? sStage[r * kTCap + (lane - k)] : kKeyNone);
-                        int rank = 0;
-                        for (int j = 0; j < m; ++j) {
-                            const uint64_t o = __shfl_sync(0xffffffffu, mine, j);
-                            rank += (o < mine || (o == mine && j < lane)) ? 1 : 0;
-                        }
-                        __syncwarp();
-                        if (lane < m && rank < k) sTop[r * kTKMax + rank] = mine;
-                        if (lane < m && rank == k - 1 && mine != kKeyNone && mine < s_tau[r]) s_tau[r] = mine;
-                    } else {
-                        constexpr int E = (kTKMax + kTCap + 31) / 32;
-                        uint64_t v6[E];
+                for (int h = 0; h < 2; ++h) {
+                    // rows within the limit go to the slots, then into the k smallest
+                    int nk = 0;
 #pragma unroll
-                        for (int e = 0; e < E; ++e) {
-                            const int i = e * 32 + lane;
-                            v6[e] = i < k ? sTop[r * kTKMax + i]
-                                          : (i - k < ns ? sStage[r * kTCap + (i - k)] : kKeyNone);
+                    for (int j = 0; j < 32; ++j) {
+                        const uint2 rw = myrows[32 * h + j];
+                        const uint32_t dist = qn + rw.x - 2u * dot[h][j];
+                        if (live && rw.y != 0xFFFFFFFFu && dist <= lim) {
+                            myslot[nk * kTEpi] = (dist << 6) | (uint32_t)(32 * h + j);
+                            ++nk;
                         }
-                        uint64_t kth = kKeyNone;
-                        for (int o = 0; o < k; ++o) {
-                            const uint64_t mm = warp_take_min<E>(v6);
-                            if (lane == o) sTop[r * kTKMax + o] = mm;
-                            kth = mm;
-                        }
-                        __syncwarp();
-                        if (lane == 0 && kth != kKeyNone && kth < s_tau[r]) s_tau[r] = kth;
                     }
-                    __syncwarp();
-                    if (lane == 0) s_cnt[r] = 0;
+                    for (int c = 0; c < nk; ++c) {
+                        const uint32_t e = myslot[c * kTEpi];
+                        const uint64_t key = make_key(e >> 6, myrows[e & 63].y);
+                        if (key < lv[kTKMax - 1]) topk_insert(lv, key);
+                    }
+                    const uint32_t kd = (uint32_t)(lv[kTKMax - 1] >> 32);
+                    lim = kd < tau ? kd : tau;
                 }
-                epi_sync();
+                __syncwarp();                              // the rows of the next tile overwrite myrows
             }
-            // every query's k smallest keys of this list into its candidate buffer
-            if (!*vfail) {
-                for (int rr = 0; rr < 8; ++rr) {
-                    const int r = 8 * ew + rr;
-                    if (r >= nqg) break;
-                    const uint64_t key = lane < k ? sTop[r * kTKMax + lane] : kKeyNone;
-                    const bool ok = key != kKeyNone;
-                    const unsigned ball = __ballot_sync(0xffffffffu, ok);
-                    if (!ball) continue;
-                    const int q = s_qid[r];
-                    int base = 0;
-                    if (lane == 0) {
-                        base = atomicAdd(cb.cnt + q, __popc(ball));
-                        const uint64_t kth = sTop[r * kTKMax + k - 1];
-                        if (kth != kKeyNone) atomicMin(cb.thr + q, (unsigned long long)kth);
-                    }
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (ok) {
-                        const int at = base + __popc(ball & ((1u << lane) - 1u));
-                        if (at < cb.cap) cb.keys[(size_t)q * cb.cap + at] = key;
+            // the two threads of a query: half 1 hands its k smallest to half 0,
+            // which merges them and appends the result to the query's buffer
+            epi_sync();
+            uint64_t* xch = reinterpret_cast<uint64_t*>(sSlot);      // [kTQ][kTKMax]
+            if (half == 1) {
+#pragma unroll
+                for (int i = 0; i < kTKMax; ++i) xch[qi * kTKMax + i] = lv[i];
+            }
+            epi_sync();
+            if (half == 0 && live && !*vfail) {
+                for (int i = kTKMax - k; i < kTKMax; ++i) {
+                    const uint64_t o = xch[qi * kTKMax + i];
+                    if (o >= lv[kTKMax - 1]) break;              // the other list is ascending
+                    topk_insert(lv, o);
+                }
+                // the list's keys are slots kTKMax - k .. kTKMax - k + nk - 1 (ascending);
+                // the slots are indexed statically so that lv stays in registers
+                int nk = 0;
+#pragma unroll
+                for (int i = 0; i < kTKMax; ++i) nk += (i >= kTKMax - k && lv[i] != kKeyNone) ? 1 : 0;
+                if (nk > 0) {
+                    const int base = atomicAdd(cb.cnt + q, nk);
+#pragma unroll
+                    for (int i = 0; i < kTKMax; ++i) {
+                        const int r = i - (kTKMax - k);
+                        if (r < 0 || r >= nk) continue;
+                        const uint64_t kp = lv[i];
+                        const uint32_t pos = (uint32_t)kp;
+                        const uint64_t key = make_key((uint32_t)(kp >> 32), ls.ids ? (uint32_t)ls.ids[pos] : pos);
+                        if (base + r < cb.cap) cb.keys[(size_t)q * cb.cap + base + r] = key;
                         else atomicExch(cb.overflow, 1);
+                        // k keys of this list: their k-th bounds the query's k smallest
+                        if (r == k - 1) atomicMin(cb.thr + q, (unsigned long long)key);
                     }
                 }
             }
@@ -374,7 +356,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTAcc * kTQ)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTAcc * kTN)
                      : "memory");
 }
 
@@ -404,14 +386,14 @@ EncodeTiledFn encode_fn() {
 bool exact_tc_usable(int d, int k) { return (d == 128 || d == 256) && k > 0 && k <= kTKMax; }
 
 cudaError_t exact_tc_map(const uint8_t* rows, int64_t n, int d, void* map_out) {
-    if (!rows || n <= 0 || n >= ((int64_t)1 << 31) - kTM || (d != 128 && d != 256) ||
+    if (!rows || n <= 0 || n >= ((int64_t)1 << 31) - kTN || (d != 128 && d != 256) ||
         (reinterpret_cast<uintptr_t>(rows) & 15))
         return cudaErrorInvalidValue;
     EncodeTiledFn fn = encode_fn();
     if (!fn) return cudaErrorNotSupported;
     const cuuint64_t dims[2] = {(cuuint64_t)d, (cuuint64_t)n};
     const cuuint64_t strides[1] = {(cuuint64_t)d};
-    const cuuint32_t box[2] = {128, (cuuint32_t)kTM};
+    const cuuint32_t box[2] = {128, (cuuint32_t)kTN};
     const cuuint32_t estr[2] = {1, 1};
     const CUresult r = fn(static_cast<CUtensorMap*>(map_out), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
                           const_cast<uint8_t*>(rows), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,

@@ -37,7 +37,7 @@ constexpr int kGroupQueries = 4;
 bool exact_tc_usable(int d, int k);
 // the tensor map (128 bytes, 64-byte aligned) over rows [n, d] of an exact index
 cudaError_t exact_tc_map(const uint8_t* rows, int64_t n, int d, void* map_out);
-// the grouped exact search (groups of up to 64 queries, wl.gq = 64) with q.x
+// the grouped exact search (groups of up to 127 queries, wl.gq = 127) with q.x
 // on the tensor cores; the same candidate keys as exact_group_scan.  flag is
 // raised (4) when a bounded wait gave up.
 cudaError_t exact_tc_scan(const void* map, const uint8_t* q_u8, int d, int k, ListStore ls, WorkList wl,
