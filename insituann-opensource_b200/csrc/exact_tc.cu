@@ -166,7 +166,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 for (int t = 0; t < ntiles; ++t) {
                     const int64_t g = gt + t;
                     const int s = (int)(g % stages);
-                    if (g >= stages && !mbar_wait_or(&bar_empty[s], (uint32_t)(((g / stages) - 1) & 1), vfail)) {
+                    if (g >= stages && !mbar_wait_timed(&bar_empty[s], (uint32_t)(((g / stages) - 1) & 1), vfail)) {
                         s_fail = 1;
                         break;
                     }
@@ -187,11 +187,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 for (int t = 0; t < ntiles; ++t) {
                     const int64_t g = gt + t;
                     const int s = (int)(g % stages), a = (int)(g % kTAcc);
-                    if (g >= kTAcc && !mbar_wait_or(&bar_ae[a], (uint32_t)(((g / kTAcc) - 1) & 1), vfail)) {
+                    if (g >= kTAcc && !mbar_wait_timed(&bar_ae[a], (uint32_t)(((g / kTAcc) - 1) & 1), vfail)) {
                         s_fail = 1;
                         break;
                     }
-                    if (!mbar_wait_or(&bar_full[s], (uint32_t)((g / stages) & 1), vfail)) {
+                    if (!mbar_wait_timed(&bar_full[s], (uint32_t)((g / stages) & 1), vfail)) {
                         s_fail = 1;
                         break;
                     }
@@ -245,21 +245,28 @@ __global__ void __launch_bounds__(kTThreads, 1)
             uint32_t lim = tau;                                // distances above it are not kept
             uint2* myrows = sRow + ew * 64;
             uint32_t* myslot = sSlot + (tid - 64);             // slot c at [c][kTEpi]
+            // |x|^2 and position of this warp's 64 rows of tile t (0xFFFFFFFF: past the
+            // list or deleted), read one tile ahead
+            auto row_info = [&](int t, int h) {
+                const int v = t * kTN + half * 64 + 32 * h + lane;
+                uint2 rw = make_uint2(0u, 0xFFFFFFFFu);
+                if (v < count) {
+                    const int64_t pos = off + v;
+                    if (!(ls.deleted && ls.deleted[pos])) rw = make_uint2((uint32_t)ls.sqnorm[pos], (uint32_t)pos);
+                }
+                return rw;
+            };
+            uint2 nrw0 = row_info(0, 0), nrw1 = row_info(0, 1);
             for (int t = 0; t < ntiles; ++t) {
                 const int64_t g = gt + t;
                 const int a = (int)(g % kTAcc);
-                // |x|^2 and position of this warp's 64 rows (0xFFFFFFFF: past the list or deleted)
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int v = t * kTN + half * 64 + 32 * h + lane;
-                    uint2 rw = make_uint2(0u, 0xFFFFFFFFu);
-                    if (v < count) {
-                        const int64_t pos = off + v;
-                        if (!(ls.deleted && ls.deleted[pos])) rw = make_uint2((uint32_t)ls.sqnorm[pos], (uint32_t)pos);
-                    }
-                    myrows[32 * h + lane] = rw;
+                myrows[lane] = nrw0;
+                myrows[32 + lane] = nrw1;
+                if (t + 1 < ntiles) {
+                    nrw0 = row_info(t + 1, 0);
+                    nrw1 = row_info(t + 1, 1);
                 }
-                const bool got = mbar_wait_or(&bar_af[a], (uint32_t)((g / kTAcc) & 1), vfail);
+                const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((g / kTAcc) & 1), vfail);
                 if (!__all_sync(0xffffffffu, got)) {
                     if (lane == 0) s_fail = 1;
                     break;
@@ -344,11 +351,11 @@ __global__ void __launch_bounds__(kTThreads, 1)
     if (s_fail) {
         if (warp == 0 && lane == 0) {
             for (int64_t g = issued - stages > 0 ? issued - stages : 0; g < issued; ++g)
-                mbar_wait(&bar_full[g % stages], (uint32_t)((g / stages) & 1));
+                mbar_wait_timed(&bar_full[g % stages], (uint32_t)((g / stages) & 1), nullptr);
         }
         if (warp == 1 && lane == 0 && mma_done > 0) {
             const int64_t g = mma_done - 1;
-            mbar_wait(&bar_af[g % kTAcc], (uint32_t)((g / kTAcc) & 1));
+            mbar_wait_timed(&bar_af[g % kTAcc], (uint32_t)((g / kTAcc) & 1), nullptr);
         }
         if (tid == 0) atomicOr(flag, 4);
     }

@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
     };
     // thread 0: MMAs of tile i into accumulator i & 1; false when its copy did not land
     auto mma_tile = [&](int i) -> bool {
-        if (!mbar_wait(&bar_b[i & 1], (uint32_t)((i >> 1) & 1))) return false;
+        if (!mbar_wait_timed(&bar_b[i & 1], (uint32_t)((i >> 1) & 1), nullptr)) return false;
         asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
         const uint32_t b_addr = smem_u32(sB + (size_t)(i & 1) * b_bytes);
         const uint32_t dacc = tmem + (uint32_t)((i & 1) * kTCN);
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(kTCThreads, 1)
         if (tid == 0 && it + 1 < n && !s_fail && !mma_tile(it + 1)) s_fail = 1;
         __syncthreads();
         if (s_fail) break;
-        const bool done = mbar_wait(&bar_mma[it & 1], (uint32_t)((it >> 1) & 1));
+        const bool done = mbar_wait_timed(&bar_mma[it & 1], (uint32_t)((it >> 1) & 1), nullptr);
         if (__syncthreads_or(!done)) {
             if (tid == 0) s_fail = 1;
             break;
@@ -268,8 +268,8 @@ __global__ void __launch_bounds__(kTCThreads, 1)
         if (tid == 0) {
             atomicOr(flag, 4);
             for (int b = 0; b < 2; ++b) {
-                mbar_wait(&bar_mma[b], 0);
-                mbar_wait(&bar_b[b], 0);
+                mbar_wait_timed(&bar_mma[b], 0, nullptr);
+                mbar_wait_timed(&bar_b[b], 0, nullptr);
             }
         }
     }
@@ -654,7 +654,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
             const size_t tile_stride = (size_t)3 * part_bytes;
             for (int g = 0; g < nt; ++g) {
                 const int s = g % nst;
-                if (g >= nst && !mbar_wait_or(&bar_empty[s], (uint32_t)(((g / nst) - 1) & 1), vfail)) {
+                if (g >= nst && !mbar_wait_timed(&bar_empty[s], (uint32_t)(((g / nst) - 1) & 1), vfail)) {
                     s_fail = 1;
                     break;
                 }
@@ -672,11 +672,11 @@ __global__ void __launch_bounds__(kFBlock, 1)
             const int kbp = d / 16;                  // K blocks of 16 per part
             for (int g = 0; g < nt; ++g) {
                 const int s = g % nst, a = g % kFAcc;
-                if (g >= kFAcc && !mbar_wait_or(&bar_ae[a], (uint32_t)(((g / kFAcc) - 1) & 1), vfail)) {
+                if (g >= kFAcc && !mbar_wait_timed(&bar_ae[a], (uint32_t)(((g / kFAcc) - 1) & 1), vfail)) {
                     s_fail = 1;
                     break;
                 }
-                if (!mbar_wait_or(&bar_full[s], (uint32_t)((g / nst) & 1), vfail)) {
+                if (!mbar_wait_timed(&bar_full[s], (uint32_t)((g / nst) & 1), vfail)) {
                     s_fail = 1;
                     break;
                 }
@@ -724,7 +724,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
         for (int i = 0; i < 8; ++i) cnx[i] = __ldg(reinterpret_cast<const float4*>(cne + c_begin + half * 32) + i);
         for (int g = 0; g < nt; ++g) {
             const int a = g % kFAcc;
-            const bool got = mbar_wait_or(&bar_af[a], (uint32_t)((g / kFAcc) & 1), vfail);
+            const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((g / kFAcc) & 1), vfail);
             if (!__all_sync(0xffffffffu, got)) {
                 if (lane == 0) s_fail = 1;
                 break;
@@ -845,11 +845,11 @@ __global__ void __launch_bounds__(kFBlock, 1)
         if (tid == 8 * 32) {
             atomicOr(flag, 4);
             for (int g = issued - nst < 0 ? 0 : issued - nst; g < issued; ++g)
-                mbar_wait(&bar_full[g % nst], (uint32_t)((g / nst) & 1));
+                mbar_wait_timed(&bar_full[g % nst], (uint32_t)((g / nst) & 1), nullptr);
         }
         if (tid == 9 * 32 && mma_issued > 0) {
             const int g = mma_issued - 1;
-            mbar_wait(&bar_af[g % kFAcc], (uint32_t)((g / kFAcc) & 1));
+            mbar_wait_timed(&bar_af[g % kFAcc], (uint32_t)((g / kFAcc) & 1), nullptr);
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");

@@ -1,8 +1,10 @@
 // tc.cuh -- building blocks of the tensor-core kernels (tcgen05, mbarriers,
 // bulk and tensor copies), shared by route_tc.cu and exact_tc.cu.
 //
-// Every wait here is bounded (kTCWaitSpins polls): a kernel whose wait gives
-// up reports it through its error flag instead of hanging the device.
+// Every wait here is bounded (kTCWaitNs of wall time, read from the global
+// timer; the polls suspend the waiting thread in between, so that waiting
+// warps do not take issue slots): a kernel whose wait gives up reports it
+// through its error flag instead of hanging the device.
 #pragma once
 
 #include <cuda.h>
@@ -10,8 +12,6 @@
 #include <stdint.h>
 
 namespace isb {
-
-constexpr int kTCWaitSpins = 1 << 22;     // bounded mbarrier polls
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -86,19 +86,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    for (int i = 0; i < kTCWaitSpins; ++i)
-        if (mbar_try_wait(bar, parity)) return true;
-    return false;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
 }
 
-// wait on an mbarrier phase, bounded; gives up early once *fail is set
-__device__ __forceinline__ bool mbar_wait_or(uint64_t* bar, uint32_t parity, const volatile int* fail) {
-    for (int i = 0; i < kTCWaitSpins; ++i) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((i & 31) == 31 && *fail) return false;
+// one try_wait that may suspend the thread (until the phase completes or
+// about hint_ns pass), so that a waiting warp does not take issue slots
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint64_t kTCWaitNs = 2000000000ull;   // a wait gives up after 2 s
+
+// wait on an mbarrier phase with suspending polls, bounded by kTCWaitNs of
+// wall time; gives up early once *fail is set (fail may be null)
+__device__ __forceinline__ bool mbar_wait_timed(uint64_t* bar, uint32_t parity, const volatile int* fail) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
+        if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+        if (fail && *fail) return false;
+        if (globaltimer_ns() - t0 > kTCWaitNs) return false;
     }
-    return false;
 }
 
 // untiled bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0)
