@@ -498,23 +498,32 @@ void run_u8(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, uint64_t* keys_
         int n = std::min(nsub, nq - s);
         {
             StageScope stage(b, IVF_STAGE_WORKLIST);
-            ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
-                              tmp, tmp_bytes, b->st),
-               "build_worklist");
             ck(reset_candidates(cb, n, b->st), "reset_candidates");
         }
-        {
+        // Two passes over the probe table, as in the residual-PQ search: every
+        // query's nearest list first, whose k smallest bound the query tightly,
+        // then its other probes, of which few rows then pass.  The result does
+        // not depend on the order.
+        const int npass = nprobe > 1 ? 2 : 1;
+        for (int pass = 0; pass < npass; ++pass) {
+            const int ncol = npass == 1 ? nprobe : (pass == 0 ? 1 : nprobe - 1);   // bound on pairs per query
+            {
+                StageScope stage(b, IVF_STAGE_WORKLIST);
+                ck(build_worklist(b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, x->nlist, wl,
+                                  tmp, tmp_bytes, b->st, 0, npass == 1 ? nprobe : 0, npass == 1 ? -1 : pass),
+                   "build_worklist");
+            }
             StageScope stage(b, IVF_STAGE_SCAN);
             if (use_tc)
                 ck(exact_tc_scan(x->tc_rows_map, b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl,
-                                 n * nprobe, cb, b->counter, b->overflow + 2, b->st),
+                                 n * ncol, cb, b->counter, b->overflow + 2, b->st),
                    "exact_tc_scan");
             else if (grouped)
-                ck(exact_group_scan(b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl, n * nprobe, cb,
+                ck(exact_group_scan(b->q_u8 + (size_t)s * x->d, x->d, k, x->main.view(), wl, n * ncol, cb,
                                     b->counter, b->st),
                    "exact_group_scan");
             else
-                ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * nprobe, cb, b->counter,
+                ck(exact_scan(b->q_u8 + (size_t)s * x->d, n, x->d, x->main.view(), wl, n * ncol, cb, b->counter,
                               b->st),
                    "exact_scan");
         }
