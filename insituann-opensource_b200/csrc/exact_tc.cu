@@ -15,8 +15,12 @@
 // of the tile's columns and keeps that query's k smallest keys in registers,
 // with no exchange between threads until the list is done.
 //
-// A CTA is 10 warps:
-//   warp 0, one lane   tensor copies: tiles of 128 list rows (d bytes each)
+// A CTA is 10 warps, working on up to two groups at once (two query slots):
+//   warp 0             claims the next group, stages its queries (the MMA's
+//                      A operand), their norms and bounds into a free slot
+//                      while the epilogue still works on the previous group;
+//                      one lane issues the tensor copies: tiles of 128 list
+//                      rows (d bytes each)
 //                      into a ring of stages, 128-byte swizzled, through a
 //                      tensor map over the index's rows in this GPU's memory
 //                      (no multicast); rows past the list belong to the next
@@ -59,15 +63,15 @@ constexpr int kTSlots = 32;            // kept rows per thread between insertion
 constexpr int kTMaxStages = 6;
 
 __host__ __device__ constexpr size_t exact_tc_fixed(int d) {
-    return (size_t)kTQ * d                              // queries (A operand)
+    return 2 * (size_t)kTQ * d                          // queries of two groups (A operand)
            + sizeof(uint32_t) * kTSlots * kTEpi         // kept rows (also the final exchange)
            + sizeof(uint2) * 8 * 64;                    // per epilogue warp: its rows' |x|^2 and position
 }
 
 // stages of list tiles that fit beside the fixed arrays (1 KB kept for
-// aligning the base to the swizzle atom, 2 KB for static shared memory)
+// aligning the base to the swizzle atom, 4 KB for static shared memory)
 __host__ __device__ inline int exact_tc_stages(int d) {
-    const size_t cap = 227 * 1024 - 1024 - 2048;
+    const size_t cap = 227 * 1024 - 1024 - 4096;
     const int st = (int)((cap - exact_tc_fixed(d)) / ((size_t)kTN * d));
     return st > kTMaxStages ? kTMaxStages : st;
 }
@@ -78,6 +82,18 @@ __host__ __device__ inline size_t exact_tc_smem(int d) {
 
 // barrier of the 8 epilogue warps (named barrier 1)
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kTEpi) : "memory"); }
+
+// the same barrier, returning whether any epilogue thread passed v = true
+// (so that all epilogue warps take the same branch after a bounded wait)
+__device__ __forceinline__ bool epi_sync_any(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kTEpi)
+        : "memory");
+    return r != 0;
+}
 
 // inserts key into the ascending list lv (one compare-exchange per slot; the
 // list's first kTKMax - k slots hold 0 and never move)
@@ -91,6 +107,14 @@ __device__ __forceinline__ void topk_insert(uint64_t (&lv)[kTKMax], uint64_t key
     }
 }
 
+// One group in flight per slot (two slots): what the copy warp decoded and
+// staged for it, read by the MMA thread and the epilogue.
+struct TcGroup {
+    int64_t off;     // first position of the list
+    int count;       // rows of the list
+    int nqg;         // queries of the group (0: no more groups)
+};
+
 template <int NKB>   // 128-byte K blocks per row: d = 128 NKB
 __global__ void __launch_bounds__(kTThreads, 1)
     exact_tc_kernel(const __grid_constant__ CUtensorMap tmap, const uint8_t* __restrict__ q_u8, ListStore ls,
@@ -103,12 +127,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
     __shared__ __align__(8) uint64_t bar_empty[kTMaxStages];
     __shared__ __align__(8) uint64_t bar_af[kTAcc];
     __shared__ __align__(8) uint64_t bar_ae[kTAcc];
+    __shared__ __align__(8) uint64_t bar_qready[2];   // a slot's queries and descriptor are staged
+    __shared__ __align__(8) uint64_t bar_qfree[2];    // the MMAs and the epilogue are done with a slot
     __shared__ uint32_t s_tmem;
-    __shared__ int s_fail, s_item;
+    __shared__ int s_fail;
+    __shared__ TcGroup s_grp[2];
+    __shared__ int s_qn[2][kTQ], s_qid[2][kTQ];
+    __shared__ uint32_t s_tau[2][kTQ];
     const size_t tile_bytes = (size_t)kTN * d;
-    unsigned char* sA = sm + (size_t)stages * tile_bytes;                       // queries [kTQ][d], swizzled
-    uint32_t* sSlot = reinterpret_cast<uint32_t*>(sA + (size_t)kTQ * d);         // [kTSlots][kTEpi]
-    uint2* sRow = reinterpret_cast<uint2*>(sSlot + kTSlots * kTEpi);             // [8 warps][64]
+    const size_t a_bytes = (size_t)kTQ * d;
+    unsigned char* sA0 = sm + (size_t)stages * tile_bytes;                      // queries [2][kTQ][d], swizzled
+    uint32_t* sSlot = reinterpret_cast<uint32_t*>(sA0 + 2 * a_bytes);           // [kTSlots][kTEpi]
+    uint2* sRow = reinterpret_cast<uint2*>(sSlot + kTSlots * kTEpi);            // [8 warps][64]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const volatile int* vfail = &s_fail;
 
@@ -127,6 +157,10 @@ __global__ void __launch_bounds__(kTThreads, 1)
             mbar_init(&bar_af[a], 1);
             mbar_init(&bar_ae[a], kTEpi / 32);     // one arrival per epilogue warp
         }
+        for (int q = 0; q < 2; ++q) {
+            mbar_init(&bar_qready[q], 1);
+            mbar_init(&bar_qfree[q], 1 + kTEpi / 32);   // the MMA thread's commit + each epilogue warp
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_fail = 0;
     }
@@ -135,64 +169,110 @@ __global__ void __launch_bounds__(kTThreads, 1)
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     const int NG = *wl.n_groups;
-    int64_t gt = 0;             // tiles this CTA has started so far (mbarrier phases)
-    int64_t issued = 0;         // warp 0: tiles whose copies were issued
-    int64_t mma_done = 0;       // warp 1: tiles whose MMAs were issued
 
-    for (;;) {
-        if (tid == 0) s_item = s_fail ? NG : atomicAdd(counter, 1);
-        __syncthreads();
-        const int it = s_item;
-        if (it >= NG) break;
-        const int64_t pk = wl.groups[it];
-        const int l = (int)(pk >> 32), p0 = (int)((pk >> 7) & 0x1FFFFFF), nqg = (int)(pk & 127);
-        const int count = ls.counts[l];
-        const int64_t off = ls.offsets[l];
-        const int ntiles = (count + kTN - 1) / kTN;
-        // the group's queries in the swizzled A layout (rows past nqg are zero)
-        for (int e = tid; e < kTQ * 8 * NKB; e += kTThreads) {
-            const int r = e / (8 * NKB), c = e % (8 * NKB), kb = c >> 3, cc = c & 7;
-            uint4 v = make_uint4(0u, 0u, 0u, 0u);
-            if (r < nqg) v = __ldg(reinterpret_cast<const uint4*>(q_u8 + (size_t)wl.pair_q[p0 + r] * d) + c);
-            *reinterpret_cast<uint4*>(sA + (size_t)kb * kTQ * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
-        }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-
-        if (warp == 0) {
+    if (warp == 0) {
+        // ---- copy warp: claims the groups, stages their queries (all lanes), and
+        // issues the list tiles (lane 0) ----
+        int64_t gt = 0;          // tiles issued so far
+        for (int gi = 0;; ++gi) {
+            const int slot = gi & 1;
+            if (gi >= 2 && !mbar_wait_timed(&bar_qfree[slot], (uint32_t)(((gi >> 1) - 1) & 1), vfail)) {
+                if (lane == 0) s_fail = 1;
+                break;
+            }
+            int it = 0;
+            if (lane == 0) it = *vfail ? NG : atomicAdd(counter, 1);
+            it = __shfl_sync(0xffffffffu, it, 0);
+            TcGroup grp{0, 0, 0};
+            int p0 = 0;
+            if (it < NG) {
+                const int64_t pk = wl.groups[it];
+                const int l = (int)(pk >> 32);
+                p0 = (int)((pk >> 7) & 0x1FFFFFF);
+                grp.nqg = (int)(pk & 127);
+                grp.count = ls.counts[l];
+                grp.off = ls.offsets[l];
+            }
+            unsigned char* sA = sA0 + (size_t)slot * a_bytes;
+            if (grp.nqg > 0) {
+                // the group's queries in the swizzled A layout (rows past nqg are zero)
+                for (int e = lane; e < kTQ * 8 * NKB; e += 32) {
+                    const int r = e / (8 * NKB), c = e % (8 * NKB), kb = c >> 3, cc = c & 7;
+                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+                    if (r < grp.nqg) v = __ldg(reinterpret_cast<const uint4*>(q_u8 + (size_t)wl.pair_q[p0 + r] * d) + c);
+                    *reinterpret_cast<uint4*>(sA + (size_t)kb * kTQ * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
+                }
+                // |q|^2, the query id and its bound over the lists done before (a key
+                // above the bound cannot be among the query's k smallest)
+                for (int r = lane; r < kTQ; r += 32) {
+                    const int q = r < grp.nqg ? wl.pair_q[p0 + r] : -1;
+                    uint32_t n2 = 0, tau = 0xFFFFFFFFu;
+                    if (q >= 0) {
+                        const uint4* qr = reinterpret_cast<const uint4*>(q_u8 + (size_t)q * d);
+#pragma unroll
+                        for (int c = 0; c < 8 * NKB; ++c) {
+                            const uint4 v = __ldg(qr + c);
+                            n2 = __dp4a(v.x, v.x, n2);
+                            n2 = __dp4a(v.y, v.y, n2);
+                            n2 = __dp4a(v.z, v.z, n2);
+                            n2 = __dp4a(v.w, v.w, n2);
+                        }
+                        tau = (uint32_t)(*((volatile unsigned long long*)(cb.thr + q)) >> 32);
+                    }
+                    s_qn[slot][r] = (int)n2;
+                    s_qid[slot][r] = q;
+                    s_tau[slot][r] = tau;
+                }
+            }
+            if (lane == 0) s_grp[slot] = grp;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_qready[slot]);
+            if (grp.nqg == 0) break;
             if (lane == 0) {
-                for (int t = 0; t < ntiles; ++t) {
-                    const int64_t g = gt + t;
-                    const int s = (int)(g % stages);
-                    if (g >= stages && !mbar_wait_timed(&bar_empty[s], (uint32_t)(((g / stages) - 1) & 1), vfail)) {
+                const int ntiles = (grp.count + kTN - 1) / kTN;
+                for (int t = 0; t < ntiles; ++t, ++gt) {
+                    const int s = (int)(gt % stages);
+                    if (gt >= stages && !mbar_wait_timed(&bar_empty[s], (uint32_t)(((gt / stages) - 1) & 1), vfail)) {
                         s_fail = 1;
                         break;
                     }
                     mbar_arrive_expect(&bar_full[s], (uint32_t)tile_bytes);
-                    const int y = (int)(off + (int64_t)t * kTN);
+                    const int y = (int)(grp.off + (int64_t)t * kTN);
 #pragma unroll
                     for (int kb = 0; kb < NKB; ++kb)
                         tma_load_2d(sm + (size_t)s * tile_bytes + (size_t)kb * kTN * 128, &tmap, 128 * kb, y,
                                     &bar_full[s]);
-                    issued = g + 1;
                 }
             }
             __syncwarp();
-        } else if (warp == 1) {
-            if (lane == 0) {
-                constexpr uint32_t idesc = umma_idesc_u8(kTQ, kTN);
-                const uint32_t a_addr = smem_u32(sA);
-                for (int t = 0; t < ntiles; ++t) {
-                    const int64_t g = gt + t;
-                    const int s = (int)(g % stages), a = (int)(g % kTAcc);
-                    if (g >= kTAcc && !mbar_wait_timed(&bar_ae[a], (uint32_t)(((g / kTAcc) - 1) & 1), vfail)) {
-                        s_fail = 1;
-                        break;
-                    }
-                    if (!mbar_wait_timed(&bar_full[s], (uint32_t)((g / stages) & 1), vfail)) {
-                        s_fail = 1;
+            if (*vfail) break;
+        }
+        // the copies in flight land before the CTA's shared memory is released
+        if (lane == 0)
+            for (int64_t g = gt - stages > 0 ? gt - stages : 0; g < gt; ++g)
+                mbar_wait_timed(&bar_full[g % stages], (uint32_t)((g / stages) & 1), nullptr);
+    } else if (warp == 1) {
+        // ---- MMA thread ----
+        if (lane == 0) {
+            constexpr uint32_t idesc = umma_idesc_u8(kTQ, kTN);
+            int64_t gt = 0;
+            for (int gi = 0;; ++gi) {
+                const int slot = gi & 1;
+                if (!mbar_wait_timed(&bar_qready[slot], (uint32_t)((gi >> 1) & 1), vfail)) {
+                    s_fail = 1;
+                    break;
+                }
+                const TcGroup grp = s_grp[slot];
+                if (grp.nqg == 0) break;
+                const uint32_t a_addr = smem_u32(sA0 + (size_t)slot * a_bytes);
+                const int ntiles = (grp.count + kTN - 1) / kTN;
+                bool ok = true;
+                for (int t = 0; t < ntiles; ++t, ++gt) {
+                    const int s = (int)(gt % stages), a = (int)(gt % kTAcc);
+                    if ((gt >= kTAcc && !mbar_wait_timed(&bar_ae[a], (uint32_t)(((gt / kTAcc) - 1) & 1), vfail)) ||
+                        !mbar_wait_timed(&bar_full[s], (uint32_t)((gt / stages) & 1), vfail)) {
+                        ok = false;
                         break;
                     }
                     tc_fence_after();
@@ -214,37 +294,44 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                     tc_commit(&bar_empty[s]);
                     tc_commit(&bar_af[a]);
-                    mma_done = g + 1;
                 }
-            }
-            __syncwarp();
-        } else {
-            const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
-            const int qi = quarter * 32 + lane;               // TMEM lane = the thread's query
-            const bool live = qi < nqg;
-            const int q = live ? wl.pair_q[p0 + qi] : -1;
-            // |q|^2 and the bound over the lists done before: a key above it cannot be
-            // among the query's k smallest (the buffer already holds k keys at or below it)
-            uint32_t qn = 0;
-            uint32_t tau = 0xFFFFFFFFu;
-            if (live) {
-                const uint4* qr = reinterpret_cast<const uint4*>(q_u8 + (size_t)q * d);
-#pragma unroll
-                for (int c = 0; c < 8 * NKB; ++c) {
-                    const uint4 v = __ldg(qr + c);
-                    qn = __dp4a(v.x, v.x, qn);
-                    qn = __dp4a(v.y, v.y, qn);
-                    qn = __dp4a(v.z, v.z, qn);
-                    qn = __dp4a(v.w, v.w, qn);
+                if (!ok) {
+                    s_fail = 1;
+                    break;
                 }
-                tau = (uint32_t)(*((volatile unsigned long long*)(cb.thr + q)) >> 32);
+                tc_commit(&bar_qfree[slot]);      // the slot's queries are no longer read
             }
+            // the MMAs in flight are done before tensor memory is released
+            if (gt > 0) mbar_wait_timed(&bar_af[(gt - 1) % kTAcc], (uint32_t)(((gt - 1) / kTAcc) & 1), nullptr);
+        }
+        __syncwarp();
+    } else {
+        // ---- epilogue ----
+        const int ew = warp - 2, quarter = warp & 3, half = ew >> 2;
+        const int qi = quarter * 32 + lane;               // TMEM lane = the thread's query
+        uint2* myrows = sRow + ew * 64;
+        uint32_t* myslot = sSlot + (tid - 64);             // slot c at [c][kTEpi]
+        int64_t gt = 0;
+        for (int gi = 0;; ++gi) {
+            const int slot = gi & 1;
+            const bool ready = mbar_wait_timed(&bar_qready[slot], (uint32_t)((gi >> 1) & 1), vfail);
+            if (epi_sync_any(!ready)) {                    // every epilogue warp leaves together
+                if (tid == 64) s_fail = 1;
+                break;
+            }
+            const TcGroup grp = s_grp[slot];
+            if (grp.nqg == 0) break;
+            const int count = grp.count;
+            const int64_t off = grp.off;
+            const int ntiles = (count + kTN - 1) / kTN;
+            const bool live = qi < grp.nqg;
+            const int q = s_qid[slot][qi];
+            const uint32_t qn = (uint32_t)s_qn[slot][qi];
+            const uint32_t tau = s_tau[slot][qi];
             uint64_t lv[kTKMax];
 #pragma unroll
             for (int i = 0; i < kTKMax; ++i) lv[i] = i < kTKMax - k ? 0ull : kKeyNone;
             uint32_t lim = tau;                                // distances above it are not kept
-            uint2* myrows = sRow + ew * 64;
-            uint32_t* myslot = sSlot + (tid - 64);             // slot c at [c][kTEpi]
             // |x|^2 and position of this warp's 64 rows of tile t (0xFFFFFFFF: past the
             // list or deleted), read one tile ahead
             auto row_info = [&](int t, int h) {
@@ -257,18 +344,18 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 return rw;
             };
             uint2 nrw0 = row_info(0, 0), nrw1 = row_info(0, 1);
-            for (int t = 0; t < ntiles; ++t) {
-                const int64_t g = gt + t;
-                const int a = (int)(g % kTAcc);
+            bool ok = true;
+            for (int t = 0; t < ntiles; ++t, ++gt) {
+                const int a = (int)(gt % kTAcc);
                 myrows[lane] = nrw0;
                 myrows[32 + lane] = nrw1;
                 if (t + 1 < ntiles) {
                     nrw0 = row_info(t + 1, 0);
                     nrw1 = row_info(t + 1, 1);
                 }
-                const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((g / kTAcc) & 1), vfail);
+                const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((gt / kTAcc) & 1), vfail);
                 if (!__all_sync(0xffffffffu, got)) {
-                    if (lane == 0) s_fail = 1;
+                    ok = false;
                     break;
                 }
                 tc_fence_after();
@@ -301,6 +388,9 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     lim = kd < tau ? kd : tau;
                 }
                 __syncwarp();                              // the rows of the next tile overwrite myrows
+            }
+            if (!ok) {
+                if (lane == 0) s_fail = 1;
             }
             // the two threads of a query: half 1 hands its k smallest to half 0,
             // which merges them and appends the result to the query's buffer
@@ -338,27 +428,14 @@ __global__ void __launch_bounds__(kTThreads, 1)
                     }
                 }
             }
+            epi_sync();                                    // xch is free for the next group
+            if (lane == 0) mbar_arrive(&bar_qfree[slot]);
+            if (*vfail) break;
         }
-        gt += ntiles;
-        tc_fence_before();
-        __syncthreads();
-        tc_fence_after();
-        if (s_fail) break;
     }
 
-    // drain: the copies and MMAs this CTA issued are complete before its shared
-    // and tensor memory are released (only a wait that gave up leaves any)
-    if (s_fail) {
-        if (warp == 0 && lane == 0) {
-            for (int64_t g = issued - stages > 0 ? issued - stages : 0; g < issued; ++g)
-                mbar_wait_timed(&bar_full[g % stages], (uint32_t)((g / stages) & 1), nullptr);
-        }
-        if (warp == 1 && lane == 0 && mma_done > 0) {
-            const int64_t g = mma_done - 1;
-            mbar_wait_timed(&bar_af[g % kTAcc], (uint32_t)((g / kTAcc) & 1), nullptr);
-        }
-        if (tid == 0) atomicOr(flag, 4);
-    }
+    __syncthreads();
+    if (s_fail && tid == 0) atomicOr(flag, 4);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
