@@ -430,7 +430,7 @@ __global__ void __launch_bounds__(kTThreads, 1)
             }
             epi_sync();                                    // xch is free for the next group
             if (lane == 0) mbar_arrive(&bar_qfree[slot]);
-            if (*vfail) break;
+            // (a failure seen now ends the loop at the next group's collective check)
         }
     }
 
