@@ -195,33 +195,54 @@ __global__ void __launch_bounds__(kTThreads, 1)
             }
             unsigned char* sA = sA0 + (size_t)slot * a_bytes;
             if (grp.nqg > 0) {
-                // the group's queries in the swizzled A layout (rows past nqg are zero)
-                for (int e = lane; e < kTQ * 8 * NKB; e += 32) {
-                    const int r = e / (8 * NKB), c = e % (8 * NKB), kb = c >> 3, cc = c & 7;
-                    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                    if (r < grp.nqg) v = __ldg(reinterpret_cast<const uint4*>(q_u8 + (size_t)wl.pair_q[p0 + r] * d) + c);
-                    *reinterpret_cast<uint4*>(sA + (size_t)kb * kTQ * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = v;
-                }
-                // |q|^2, the query id and its bound over the lists done before (a key
-                // above the bound cannot be among the query's k smallest)
-                for (int r = lane; r < kTQ; r += 32) {
-                    const int q = r < grp.nqg ? wl.pair_q[p0 + r] : -1;
-                    uint32_t n2 = 0, tau = 0xFFFFFFFFu;
-                    if (q >= 0) {
-                        const uint4* qr = reinterpret_cast<const uint4*>(q_u8 + (size_t)q * d);
+                // the group's queries in the swizzled A layout by asynchronous 16-byte
+                // copies, all in flight at once (rows past nqg are zero); lane L
+                // stages rows L, L + 32, ... and keeps their query ids
+                int qids[kTQ / 32];
 #pragma unroll
-                        for (int c = 0; c < 8 * NKB; ++c) {
-                            const uint4 v = __ldg(qr + c);
-                            n2 = __dp4a(v.x, v.x, n2);
-                            n2 = __dp4a(v.y, v.y, n2);
-                            n2 = __dp4a(v.z, v.z, n2);
-                            n2 = __dp4a(v.w, v.w, n2);
-                        }
-                        tau = (uint32_t)(*((volatile unsigned long long*)(cb.thr + q)) >> 32);
+                for (int i = 0; i < kTQ / 32; ++i) {
+                    const int r = lane + 32 * i;
+                    qids[i] = r < grp.nqg ? wl.pair_q[p0 + r] : -1;
+                }
+#pragma unroll
+                for (int i = 0; i < kTQ / 32; ++i) {
+                    const int r = lane + 32 * i;
+#pragma unroll
+                    for (int c = 0; c < 8 * NKB; ++c) {
+                        unsigned char* dst = sA + (size_t)(c >> 3) * kTQ * 128 + r * 128 + (((c & 7) ^ (r & 7)) << 4);
+                        if (qids[i] >= 0)
+                            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)),
+                                         "l"(q_u8 + (size_t)qids[i] * d + 16 * c)
+                                         : "memory");
+                        else
+                            *reinterpret_cast<uint4*>(dst) = make_uint4(0u, 0u, 0u, 0u);
+                    }
+                }
+                // the bounds over the lists done before (a key above the bound cannot be
+                // among the query's k smallest), read while the copies land
+                uint32_t taus[kTQ / 32];
+#pragma unroll
+                for (int i = 0; i < kTQ / 32; ++i)
+                    taus[i] = qids[i] >= 0 ? (uint32_t)(*((volatile unsigned long long*)(cb.thr + qids[i])) >> 32)
+                                           : 0xFFFFFFFFu;
+                asm volatile("cp.async.wait_all;" ::: "memory");
+                // |q|^2 of this lane's rows, from the staged copy
+#pragma unroll
+                for (int i = 0; i < kTQ / 32; ++i) {
+                    const int r = lane + 32 * i;
+                    uint32_t n2 = 0;
+#pragma unroll
+                    for (int c = 0; c < 8 * NKB; ++c) {
+                        const uint4 v = *reinterpret_cast<const uint4*>(sA + (size_t)(c >> 3) * kTQ * 128 + r * 128 +
+                                                                       (((c & 7) ^ (r & 7)) << 4));
+                        n2 = __dp4a(v.x, v.x, n2);
+                        n2 = __dp4a(v.y, v.y, n2);
+                        n2 = __dp4a(v.z, v.z, n2);
+                        n2 = __dp4a(v.w, v.w, n2);
                     }
                     s_qn[slot][r] = (int)n2;
-                    s_qid[slot][r] = q;
-                    s_tau[slot][r] = tau;
+                    s_qid[slot][r] = qids[i];
+                    s_tau[slot][r] = taus[i];
                 }
             }
             if (lane == 0) s_grp[slot] = grp;

@@ -984,12 +984,12 @@ __global__ void __launch_bounds__(kRRT) pq_rerank_kernel(PQParams p, int nlist, 
         for (int c = nlive + tid; c < np; c += kRRT) sk[c] = kKeyNone;
     __syncthreads();
     if (out_exm) return;
-    if (k <= 16 && np <= 512) {
-        // each warp's k smallest of its slice of at most 64 (into the table
-        // region, free now), then warp 0's k smallest of those (at most 128)
+    if (k <= 16 && nlive <= (kRRT / 32) * 128) {
+        // each warp's k smallest of its slice of the live keys (at most 128; into
+        // the table region, free now), then warp 0's k smallest of those (at most 128)
         uint64_t* cand = reinterpret_cast<uint64_t*>(tab);
-        const int w = tid >> 5, per = (np + kRRT / 32 - 1) / (kRRT / 32);
-        const int lo = w * per, nw = lo < np ? min(per, np - lo) : 0;
+        const int w = tid >> 5, per = (nlive + kRRT / 32 - 1) / (kRRT / 32);
+        const int lo = w * per, nw = lo < nlive ? min(per, nlive - lo) : 0;
         warp_smallest_k_dispatch(sk + lo, nw, k, cand + w * k);
         __syncthreads();
         if (w == 0) {

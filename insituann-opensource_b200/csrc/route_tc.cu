@@ -510,7 +510,7 @@ __host__ __device__ constexpr size_t route_fused_region_min(int d, int list) {
     const size_t after = sizeof(float) * kTCM * kFLMax + sizeof(uint16_t) * kFT * (size_t)list;
     return tiles > after ? tiles : after;
 }
-constexpr size_t kFSmemCap = 227 * 1024 - 2560;  // dynamic shared memory of one CTA (2 KB static aside)
+constexpr size_t kFSmemCap = 227 * 1024 - 4608;  // dynamic shared memory of one CTA (4.5 KB static aside)
 
 __host__ __device__ constexpr size_t route_fused_region(int d, int list) {
     return ((kFSmemCap - route_fused_fixed(d, list)) / 128) * 128;
@@ -533,6 +533,7 @@ __global__ void __launch_bounds__(kFBlock, 1)
     __shared__ int s_fail;
     __shared__ int s_scan[33];
     __shared__ float s_halfb[2][kTCM];     // each half's running (L/2)-th smallest D~ (L == LMAX)
+    __shared__ __align__(16) float s_cn[8][2][32];   // per epilogue warp: its columns' norms, two tiles
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const bool epi = warp < 8;
     const int quarter = warp & 3, half = (warp >> 2) & 1;
@@ -718,10 +719,10 @@ __global__ void __launch_bounds__(kFBlock, 1)
         volatile uint32_t* rb = (row_bound && q0 + row < nq) ? row_bound + (q0 + row) : nullptr;
         uint32_t ub_next = rb ? *rb : 0x7f800000u;
         float pub = INF;                   // the last bound this thread published
-        // the column norms of the next tile, loaded one tile ahead
-        float4 cnx[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) cnx[i] = __ldg(reinterpret_cast<const float4*>(cne + c_begin + half * 32) + i);
+        // the column norms of this warp's 32 columns of a tile: one coalesced load
+        // per lane (issued a tile ahead) into the warp's buffer, read back as
+        // broadcasts
+        float cnn = __ldg(cne + c_begin + half * 32 + lane);
         for (int g = 0; g < nt; ++g) {
             const int a = g % kFAcc;
             const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((g / kFAcc) & 1), vfail);
@@ -750,14 +751,12 @@ __global__ void __launch_bounds__(kFBlock, 1)
             if (rb) ub_next = *rb;                            // for the next tile
             lq = fminf(lmax, ub) + eps2 - qn + slack;
             const int rel0 = g * kFN + half * 32;            // column of r[0], relative to c_begin
+            s_cn[warp][g & 1][lane] = cnn;
+            __syncwarp();
+            if (g + 1 < nt) cnn = __ldg(cne + c_begin + rel0 + kFN + lane);
             float4 cn4[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) cn4[i] = cnx[i];
-            if (g + 1 < nt) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i)
-                    cnx[i] = __ldg(reinterpret_cast<const float4*>(cne + c_begin + rel0 + kFN) + i);
-            }
+            for (int i = 0; i < 8; ++i) cn4[i] = reinterpret_cast<const float4*>(s_cn[warp][g & 1])[i];
 #pragma unroll
             for (int j0 = 0; j0 < 32; j0 += kW) {
                 if (!over && nc > LIST - kW) {
