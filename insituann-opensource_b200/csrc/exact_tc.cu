@@ -364,20 +364,34 @@ __global__ void __launch_bounds__(kTThreads, 1)
                 }
                 return rw;
             };
-            uint2 nrw0 = row_info(0, 0), nrw1 = row_info(0, 1);
+            // a warp none of whose 32 queries is in the group only hands the
+            // accumulators back (after they are written, to keep the phases)
+            const bool warp_live = __any_sync(0xffffffffu, live);
+            uint2 nrw0 = make_uint2(0u, 0xFFFFFFFFu), nrw1 = nrw0;
+            if (warp_live) {
+                nrw0 = row_info(0, 0);
+                nrw1 = row_info(0, 1);
+            }
             bool ok = true;
             for (int t = 0; t < ntiles; ++t, ++gt) {
                 const int a = (int)(gt % kTAcc);
+                const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((gt / kTAcc) & 1), vfail);
+                if (!__all_sync(0xffffffffu, got)) {
+                    ok = false;
+                    break;
+                }
+                if (!warp_live) {
+                    tc_fence_after();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&bar_ae[a]);
+                    continue;
+                }
                 myrows[lane] = nrw0;
                 myrows[32 + lane] = nrw1;
                 if (t + 1 < ntiles) {
                     nrw0 = row_info(t + 1, 0);
                     nrw1 = row_info(t + 1, 1);
-                }
-                const bool got = mbar_wait_timed(&bar_af[a], (uint32_t)((gt / kTAcc) & 1), vfail);
-                if (!__all_sync(0xffffffffu, got)) {
-                    ok = false;
-                    break;
                 }
                 tc_fence_after();
                 uint32_t dot[2][32];
