@@ -83,6 +83,10 @@ struct Segment {
     int64_t* gring_off = nullptr;  // [nlist] byte offset of each list's tiles
     int32_t* sqnorm = nullptr;     // [n] squared norm of each uint8 row (exact index)
     uint8_t* deleted = nullptr;    // [n] delete mask by position (ivf_set_deleted), or nullptr
+    // delta segment only: each list's main rows then its delta rows as one
+    // grouped-ring tile stream (pq_build_gring_mix), or nullptr
+    uint8_t* mix = nullptr;
+    int64_t* mix_off = nullptr;
     int64_t n = 0;
     int max_count = 0;
     std::vector<void*> owned;
@@ -600,6 +604,8 @@ PQParams pq_params(IndexCtx* x, const float* q, bool use_delta) {
     p.main = x->main.view();
     p.delta = x->delta.view();
     p.has_delta = use_delta ? 1 : 0;
+    p.mix = use_delta ? x->delta.mix : nullptr;
+    p.mix_off = use_delta ? x->delta.mix_off : nullptr;
     return p;
 }
 
@@ -618,10 +624,12 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     const int slack_m = pq_chunk_slack(x->M, x->d, R), slack_d = pq_chunk_slack(x->M, x->d, Rd);
     const int64_t cap_m64 = (int64_t)nprobe * std::max(1, pq_scan_chunks(x->M, x->d, x->main.max_count)) *
                             std::min(R + slack_m, items);
-    const int64_t cap_d64 = use_delta ? (int64_t)nprobe *
-                                            std::max(1, pq_scan_chunks(x->M, x->d, x->delta.max_count)) *
-                                            std::min(Rd + slack_d, items)
-                                      : 0;
+    // with the combined tile stream a probed list appends all of its delta rows
+    const int64_t cap_d64 =
+        use_delta ? (int64_t)nprobe * std::max<int64_t>(x->delta.mix ? x->delta.max_count : 0,
+                                                        std::max(1, pq_scan_chunks(x->M, x->d, x->delta.max_count)) *
+                                                            std::min(Rd + slack_d, items))
+                  : 0;
     require(cap_m64 <= (1ll << 30) && cap_d64 <= (1ll << 30),
             "candidate buffer of one query would exceed 2^30 keys (lists too long for this nprobe)", IVF_EOVERFLOW);
     const int cap_m = (int)cap_m64, cap_d = (int)cap_d64;
@@ -849,6 +857,33 @@ void adopt_f32_lists(IndexCtx* x, int* d_counts, float* d_rows, int nlist, long 
     x->kind = kKindF32;
 }
 
+// INSITU_PQ_MIX=0 keeps a published delta's rows in their own tile stream
+// (scanned after each list's main rows) instead of the combined one
+bool mix_mode() {
+    const char* e = std::getenv("INSITU_PQ_MIX");
+    return !(e && e[0] == '0');
+}
+
+// Lays out every list's main rows followed by its delta rows (the delta
+// segment s, already in grouped-ring tiles) as one tile stream, so that a
+// search scans both in one pass over the list.
+void build_mix(IndexCtx* x, Segment& s, const int* dcounts) {
+    std::vector<int32_t> mc((size_t)x->nlist);
+    ck(cudaMemcpy(mc.data(), x->main.counts, sizeof(int32_t) * mc.size(), cudaMemcpyDeviceToHost), "main counts");
+    std::vector<int64_t> off((size_t)x->nlist);
+    int64_t acc = 0;
+    for (int l = 0; l < x->nlist; ++l) {
+        off[(size_t)l] = acc;
+        acc += pq_gring_list_bytes(mc[(size_t)l] + dcounts[l], x->M);
+    }
+    s.mix_off = dcopy(off.data(), off.size(), s.owned);
+    s.mix = dalloc<uint8_t>((size_t)acc + 64, s.owned);
+    ck(pq_build_gring_mix(x->main.gring, x->main.gring_off, x->main.counts, s.gring, s.gring_off, s.counts, s.mix_off,
+                          x->nlist, x->M, s.mix, 0),
+       "pq_build_gring_mix");
+    ck(cudaDeviceSynchronize(), "pq_build_gring_mix");
+}
+
 // Publishes a delta segment (the caller holds x->mu): the new segment is built
 // in full first, then swapped in under the exclusive index lock after the
 // device has finished every queued search, so a search sees either the old
@@ -885,6 +920,7 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
             }
         }
         build_gring(s, counts, x->nlist, x->M, x->d);
+        if (n_delta > 0 && s.gring && x->main.gring && mix_mode()) build_mix(x, s, counts);
     } catch (...) {
         s.release();
         throw;

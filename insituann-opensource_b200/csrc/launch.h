@@ -155,6 +155,10 @@ struct PQParams {
     ListStore main;
     ListStore delta;
     int has_delta;
+    // with a delta: every list's main rows followed by its delta rows in one
+    // grouped-ring tile stream (pq_build_gring_mix), or nullptr
+    const uint8_t* mix;
+    const int64_t* mix_off;  // [nlist] byte offset of each list's combined tiles
 };
 bool pq_supported_m(int M);
 // true when the query-grouped kernel scans (M, d); other shapes use the row kernel
@@ -164,6 +168,12 @@ int64_t pq_gring_list_bytes(int count, int M);
 // builds the grouped-ring tile layout of every list from row-major codes [n, M]
 cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
                            const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st);
+// the combined tile stream of every list: its main rows (count_m, from the
+// main tiles) then its delta rows (count_d, from the delta tiles), laid out as
+// one list of count_m + count_d rows at mix_off[l]
+cudaError_t pq_build_gring_mix(const uint8_t* main_tiles, const int64_t* main_off, const int32_t* main_counts,
+                               const uint8_t* delta_tiles, const int64_t* delta_off, const int32_t* delta_counts,
+                               const int64_t* mix_off, int nlist, int M, uint8_t* out, cudaStream_t st);
 // vectors per filtered chunk of the kernel that scans (M, d); each chunk keeps at
 // most R candidates per query, which bounds the candidate buffers
 // filtered chunks the scan of one list of `count` vectors takes, and the most

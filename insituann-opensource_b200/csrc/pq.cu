@@ -293,6 +293,7 @@ struct GroupDesc {
     int64_t pk, koff, goff;
     int count, q[kGQ];
     int64_t dkoff, dgoff;    // the same list's delta segment (when one is published)
+    int64_t mgoff;           // the list's main and delta rows in one tile stream (PQParams::mix)
     int dcount;
 };
 
@@ -312,6 +313,7 @@ __device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, co
         cp_async_4(&g.dcount, D.counts + l);
         cp_async_8(&g.dkoff, (D.key_off ? D.key_off : D.offsets) + l);
         cp_async_8(&g.dgoff, D.gring_off + l);
+        if (p.mix) cp_async_8(&g.mgoff, p.mix_off + l);
     } else {
         g.dcount = 0;
     }
@@ -348,8 +350,9 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     __shared__ __align__(8) GroupDesc s_gd;     // the group this CTA starts next
     // the current group's main and delta list (count, key offset, tile offset),
     // kept past the next group's descriptor fetch
-    __shared__ int64_t s_skoff[2], s_sgoff[2];
-    __shared__ int s_scount[2];
+    // [0] main rows, [1] delta rows, [2] both in one tile stream (PQParams::mix)
+    __shared__ int64_t s_skoff[3], s_sgoff[3];
+    __shared__ int s_scount[3];
     __shared__ unsigned long long s_thr1[kGQ];   // the second segment's bounds, read before the LUT build
     // per-chunk totals and "some sum may pass" bits of the 4 queries, three
     // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
@@ -420,6 +423,9 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             s_sgoff[0] = s_gd.goff;
             s_skoff[1] = s_gd.dkoff;
             s_sgoff[1] = s_gd.dgoff;
+            s_scount[2] = count_m + count_d;
+            s_skoff[2] = s_gd.koff;
+            s_sgoff[2] = DELTA && p.mix ? s_gd.mgoff : 0;
         }
         bool fetched = false;            // thread 0: stage A of the next descriptor issued
         bool staged = false;             // thread 0: its stage B issued
@@ -429,9 +435,10 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // before the barrier that publishes the shared copies)
             auto seg_setup = [&](int seg, bool from_desc, const uint4*& lanebase, int64_t& ntiles, int& S,
                                  int64_t& T0, int& wsteps, int& nchunks) {
-                const int count = seg ? count_d : count_m;
-                const int64_t goff = from_desc ? (seg ? s_gd.dgoff : s_gd.goff) : s_sgoff[seg];
-                const uint8_t* tiles = (seg ? p.delta.gring : p.main.gring) + goff;
+                const int count = seg == 2 ? count_m + count_d : (seg ? count_d : count_m);
+                const int64_t goff =
+                    from_desc ? (seg == 2 ? s_gd.mgoff : (seg ? s_gd.dgoff : s_gd.goff)) : s_sgoff[seg];
+                const uint8_t* tiles = (seg == 2 ? p.mix : (seg ? p.delta.gring : p.main.gring)) + goff;
                 ntiles = gring_tiles(count);
                 // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
                 // multiple of 16, so a stripe starts on a tile) and runs through it
@@ -456,7 +463,12 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // with no steps in the first segment, right away), and its bounds
             // are read before the LUT build, so switching segments exposes no
             // global-memory latency.
-            const int seg0 = DELTA ? (count_d > 0 ? 1 : 0) : 0;
+            // With the combined tile stream of a list's main and delta rows
+            // (built when the delta is published) both are scanned in one pass,
+            // over stripes of the combined list: positions below the main count
+            // are main rows, the others delta rows (segment 2).
+            const bool mixed = DELTA && p.mix != nullptr && count_m > 0 && count_d > 0;
+            const int seg0 = DELTA ? (mixed ? 2 : (count_d > 0 ? 1 : 0)) : 0;
             const int seg1 = DELTA && seg0 == 1 && count_m > 0 ? 0 : -1;
             seg_setup(seg0, true, lanebase, ntiles, S, T0, wsteps, nchunks);
             const uint4* pre1 = nullptr;     // first tile of seg1 for this lane (null: none)
@@ -486,7 +498,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // (the second segment's into shared memory, read when it starts)
             uint64_t thr0[kGQ];
             {
-                const CandBuf& cb0 = seg0 ? cd : cm;
+                const CandBuf& cb0 = seg0 == 1 ? cd : cm;
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb0.thr + s_gd.q[k])) : 0ull;
@@ -577,8 +589,11 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             if (seg < 0) break;
             const int count = s_scount[seg];
             if (count == 0) continue;
-            const CandBuf& cb = seg ? cd : cm;
+            const CandBuf& cb = seg == 1 ? cd : cm;
             const uint32_t kbase = (uint32_t)s_skoff[seg];
+            // combined stream: positions from cmain on are the delta's (key base dkbase)
+            const uint32_t cmain = seg == 2 ? (uint32_t)count_m : 0xFFFFFFFFu;
+            const uint32_t dkbase = (uint32_t)s_skoff[1];
             if (si == 1) {                     // the main rows after the delta rows: same LUT
                 seg_setup(seg, false, lanebase, ntiles, S, T0, wsteps, nchunks);
                 if (!have1) load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
@@ -623,6 +638,15 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
                 maybe = __reduce_or_sync(0xffffffffu, maybe);
+                bool cdelta = false;             // the chunk finishes delta rows of the combined stream
+                if (DELTA && seg == 2) {
+                    // a chunk that finishes delta rows is always filtered (the store
+                    // test compares with the main bounds only)
+                    const int va = t * kRSteps >= 7 ? t * kRSteps - 7 : 0, vb = min(S, t * kRSteps + kRSteps - 7);
+                    for (int r = 0; r < kRRings; ++r)
+                        cdelta |= r * S + va < count && r * S + vb > (int)cmain;
+                    if (cdelta) maybe |= (1u << nqg) - 1u;
+                }
                 if (lane == 0 && (maybe | force)) atomicOr(&s_any[cpar], maybe | force);
                 __syncthreads();
                 if (tid == 0 && fetched && !staged) {         // stage A landed long ago
@@ -661,7 +685,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
                 auto key_of = [&](int e, int k) -> uint64_t {
                     const float dk = k == 0 ? f[e].x : k == 1 ? f[e].y : k == 2 ? f[e].z : f[e].w;
-                    return vid[e] != 0xFFFFFFFFu ? make_key(__float_as_uint(dk), kbase + vid[e]) : kKeyNone;
+                    return vid[e] < cmain ? make_key(__float_as_uint(dk), kbase + vid[e]) : kKeyNone;
                 };
 #pragma unroll
                 for (int e = 0; e < kE; ++e)
@@ -695,6 +719,22 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 for (int k = 0; k < kGQ; ++k)
                     if (k < nqg && totk[k] > 0)
                         warp_append_items<kE>([&](int e) { return key_of(e, k); }, cut[k], cb, qid[k]);
+                if (DELTA && cdelta) {
+                    // the delta rows of the chunk: every key goes to the delta buffer
+                    // (a list's delta rows are few; the buffer holds all of them)
+#pragma unroll
+                    for (int k = 0; k < kGQ; ++k) {
+                        if (k >= nqg) break;
+                        warp_append_items<kE>(
+                            [&](int e) -> uint64_t {
+                                const float dk = k == 0 ? f[e].x : k == 1 ? f[e].y : k == 2 ? f[e].z : f[e].w;
+                                return vid[e] != 0xFFFFFFFFu && vid[e] >= cmain
+                                           ? make_key(__float_as_uint(dk), dkbase + vid[e] - cmain)
+                                           : kKeyNone;
+                            },
+                            kKeyNone - 1, cd, qid[k]);
+                    }
+                }
                 if (sel) __syncthreads();     // the histograms lived in the slots
                 set_thf(cut);
             }
@@ -765,6 +805,48 @@ __global__ void gring_layout_kernel(const uint8_t* __restrict__ codes, const int
             const int blk = (int)(g - 8 * g8);
             const int64_t v = 8 * g8 + jj;
             dst[e] = (v >= 0 && v < cnt) ? codes[(size_t)(off + v) * M + MPL * blk + s] : (uint8_t)0;
+        }
+    }
+}
+
+// byte offset, inside a list's tiles, of sub-quantizer byte s of block b of
+// vector v (the inverse of gring_layout_kernel's mapping; v >= 0)
+template <int MPL>
+__device__ __forceinline__ int64_t gring_byte(int64_t v, int b, int s) {
+    const int j = (int)(v & 7);
+    const int64_t g = (v - j) + b + j;          // 16T + i
+    const int64_t T = g / 16;
+    const int i = (int)(g % 16), byte = i * MPL + s;
+    return T * 128 * MPL + (int64_t)(8 * (byte / 16) + j) * 16 + byte % 16;
+}
+
+// combined tiles of list l: positions below count_m copy the main tiles byte
+// for byte (the layout of a position does not depend on the list's length),
+// positions count_m .. count_m + count_d - 1 take the delta's rows in order
+template <int MPL>
+__global__ void gring_mix_kernel(const uint8_t* __restrict__ mt, const int64_t* __restrict__ moff,
+                                 const int32_t* __restrict__ mcnt, const uint8_t* __restrict__ dt,
+                                 const int64_t* __restrict__ doff, const int32_t* __restrict__ dcnt,
+                                 const int64_t* __restrict__ xoff, int nlist, uint8_t* __restrict__ out) {
+    for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
+        const int cm = mcnt[l], cdl = dcnt[l];
+        const int64_t mtotal = gring_tiles(cm) * 128 * MPL;
+        const int64_t total = gring_tiles(cm + cdl) * 128 * MPL;
+        const uint8_t* src_m = mt + moff[l];
+        const uint8_t* src_d = dt + doff[l];
+        uint8_t* dst = out + xoff[l];
+        for (int64_t e = threadIdx.x; e < total; e += blockDim.x) {
+            const int64_t T = e / (128 * MPL);
+            const int r = (int)(e % (128 * MPL));
+            const int u = r / 128, jj = (r % 128) / 16, b = 16 * u + r % 16, i = b / MPL, s = b % MPL;
+            const int64_t g = 16 * T + i - jj;
+            const int64_t g8 = g >= 0 ? g / 8 : -((7 - g) / 8);      // floor(g / 8)
+            const int blk = (int)(g - 8 * g8);
+            const int64_t v = 8 * g8 + jj;
+            uint8_t val = 0;
+            if (v >= 0 && v < cm) val = e < mtotal ? src_m[e] : (uint8_t)0;
+            else if (v >= cm && v < cm + cdl) val = src_d[gring_byte<MPL>(v - cm, blk, s)];
+            dst[e] = val;
         }
     }
 }
@@ -1177,6 +1259,25 @@ cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const i
         case 4: gring_layout_kernel<4><<<grid, 256, 0, st>>>(codes, offsets, counts, tile_off, nlist, M, out); break;
         default: gring_layout_kernel<6><<<grid, 256, 0, st>>>(codes, offsets, counts, tile_off, nlist, M, out); break;
     }
+    return cudaGetLastError();
+}
+
+cudaError_t pq_build_gring_mix(const uint8_t* main_tiles, const int64_t* main_off, const int32_t* main_counts,
+                               const uint8_t* delta_tiles, const int64_t* delta_off, const int32_t* delta_counts,
+                               const int64_t* mix_off, int nlist, int M, uint8_t* out, cudaStream_t st) {
+    if (M != 16 && M != 32 && M != 48) return cudaErrorInvalidValue;
+    if (nlist <= 0) return cudaSuccess;
+    const int grid = nlist < 4096 ? nlist : 4096;
+    note_launch();
+#define ISB_MIX(MPL)                                                                                           \
+    gring_mix_kernel<MPL><<<grid, 256, 0, st>>>(main_tiles, main_off, main_counts, delta_tiles, delta_off,      \
+                                                 delta_counts, mix_off, nlist, out)
+    switch (M / 8) {
+        case 2: ISB_MIX(2); break;
+        case 4: ISB_MIX(4); break;
+        default: ISB_MIX(6); break;
+    }
+#undef ISB_MIX
     return cudaGetLastError();
 }
 

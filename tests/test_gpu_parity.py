@@ -188,9 +188,11 @@ def test_exact_deletes(cuda_ok, d):
 
 
 @pytest.mark.parametrize("f32,overlay", [(False, False), (True, False), (False, True), (True, True)])
-def test_pq_deletes(cuda_ok, pq_medium, f32, overlay):
+def test_pq_deletes(cuda_ok, pq_medium, f32, overlay, monkeypatch):
     """deleted positions keep their stage-1 slots and are not reranked; with a
-    published delta, main keys are masked and delta keys are not."""
+    published delta, main keys are masked and delta keys are not (f32: the
+    delta rows in their own tile stream, u8: in the combined one)."""
+    monkeypatch.setenv("INSITU_PQ_MIX", "0" if f32 else "1")
     p, q = pq_medium
     nq, nprobe, k, R = q.shape[0], 8, 10, 64
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
@@ -316,12 +318,21 @@ def test_pq_medium_routed(cuda_ok, pq_medium, R, k):
     assert np.array_equal(gpu_stage1(p, q, probes, max(R, k)), np.sort(s1, axis=1))
 
 
-def test_pq_overlay(cuda_ok, pq_medium):
+@pytest.mark.parametrize("mix", ["1", "0"])
+def test_pq_overlay(cuda_ok, pq_medium, mix, monkeypatch):
+    """main + delta search; mix "1" scans each list's main and delta rows as one
+    combined tile stream, "0" as two.  One list has no main rows (delta only)."""
+    monkeypatch.setenv("INSITU_PQ_MIX", mix)
     p, q = pq_medium
+    p = dict(p)
+    counts = p["counts"].copy()
+    counts[3] = 0
+    p["counts"] = counts
     nprobe, k, R = 12, 10, 256
     n = p["codes"].shape[0]
     delta = synth.delta_segment(20000, len(p["counts"]), p["codebook"].shape[0], base_id=n, d=q.shape[1], seed=3)
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
+    probes[::7, 0] = 3
     for dtk in (16, 5):
         gi, gd = gpu_pq(p, q, probes, k, R, delta=delta, delta_topk=dtk)
         oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
