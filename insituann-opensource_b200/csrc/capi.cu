@@ -290,8 +290,9 @@ void load_lists(IndexCtx* x, Segment& s, const uint8_t* data, size_t row_bytes, 
 }
 
 // Re-lays a segment's PQ codes out as grouped-ring tiles when the grouped
-// kernel scans this shape; the row-major copy is then dropped from the device.
-void build_gring(Segment& s, const int* counts, int nlist, int M, int d) {
+// kernel scans this shape; the row-major copy is then dropped from the device
+// unless keep_rows (a delta segment scanned by pq_delta_direct).
+void build_gring(Segment& s, const int* counts, int nlist, int M, int d, bool keep_rows = false) {
     if (!pq_group_usable(M, d)) return;
     std::vector<int64_t> toff((size_t)nlist);
     int64_t acc = 0;
@@ -303,6 +304,7 @@ void build_gring(Segment& s, const int* counts, int nlist, int M, int d) {
     s.gring = dalloc<uint8_t>((size_t)acc + 64, s.owned);
     ck(pq_build_gring(s.data, s.offsets, s.counts, s.gring_off, nlist, M, s.gring, 0), "pq_build_gring");
     ck(cudaDeviceSynchronize(), "pq_build_gring");
+    if (keep_rows) return;
     auto it = std::find(s.owned.begin(), s.owned.end(), (void*)s.data);
     if (it != s.owned.end()) {
         cudaFree(*it);
@@ -618,6 +620,10 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     const int R = std::max(rerank_n, adc ? 1 : k);
     const bool use_delta = overlay && x->has_delta && delta_topk > 0;
     const int Rd = use_delta ? delta_topk : 0;
+    // the delta rows by their own kernel after the main scan (row-major delta
+    // codes kept at publish), or in the scan's launches (candidate buffer cd)
+    const bool direct = use_delta && x->delta.data != nullptr && pq_delta_direct_usable(x->M, x->d, Rd);
+    const bool scan_delta = use_delta && !direct;
     require(R <= 4096 && R + Rd <= 4096, "rerank_n + delta_topk must be <= 4096");
     // every filtered chunk of a probed list appends at most min(R, chunk items) keys
     const int items = pq_scan_chunk_items(x->M, x->d);
@@ -626,7 +632,7 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
                             std::min(R + slack_m, items);
     // with the combined tile stream a probed list appends all of its delta rows
     const int64_t cap_d64 =
-        use_delta ? (int64_t)nprobe * std::max<int64_t>(x->delta.mix ? x->delta.max_count : 0,
+        scan_delta ? (int64_t)nprobe * std::max<int64_t>(x->delta.mix ? x->delta.max_count : 0,
                                                         std::max(1, pq_scan_chunks(x->M, x->d, x->delta.max_count)) *
                                                             std::min(Rd + slack_d, items))
                   : 0;
@@ -647,8 +653,8 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
     cm.R = R;
     cm.slack = slack_m;
     uint64_t* s1m = ensure<uint64_t>(b, b->s1m, (size_t)nsub * R);
-    uint64_t* s1d = nullptr;
-    if (use_delta) {
+    uint64_t* s1d = use_delta ? ensure<uint64_t>(b, b->s1d, (size_t)nsub * Rd) : nullptr;
+    if (scan_delta) {
         cd.keys = ensure<uint64_t>(b, b->cand_d, (size_t)nsub * cap_d);
         cd.cnt = ensure<int32_t>(b, b->cnt_d, (size_t)nsub);
         cd.thr = ensure<unsigned long long>(b, b->thr_d, (size_t)nsub);
@@ -656,16 +662,15 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
         cd.cap = cap_d;
         cd.R = Rd;
         cd.slack = slack_d;
-        s1d = ensure<uint64_t>(b, b->s1d, (size_t)nsub * Rd);
     }
     reset_fine_flags(b);
     for (int s = 0; s < nq; s += nsub) {
         int n = std::min(nsub, nq - s);
-        PQParams p = pq_params(x, b->q + (size_t)s * x->d, use_delta);
+        PQParams p = pq_params(x, b->q + (size_t)s * x->d, scan_delta);
         {
             StageScope stage(b, IVF_STAGE_WORKLIST);
             ck(reset_candidates(cm, n, b->st), "reset_candidates");
-            if (use_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
+            if (scan_delta) ck(reset_candidates(cd, n, b->st), "reset_candidates");
         }
         // Two passes over the probe table: every query's nearest local list first,
         // which sets a tight rank-R bound, then its other local probes, which then
@@ -683,15 +688,19 @@ void run_pq(BatchCtx* b, IndexCtx* x, int nq, int nprobe, int k, int rerank_n, b
             ck(pq_scan(p, wl, n * ncol, cm, cd, b->counter, b->st), "pq_scan");
         }
         uint64_t* m_out = adc ? adc + (size_t)s * R : s1m;
-        uint64_t* d_out = nullptr;
+        uint64_t* d_out = use_delta ? (dadc ? dadc + (size_t)s * Rd : s1d) : nullptr;
+        if (direct) {
+            StageScope stage(b, IVF_STAGE_SCAN);
+            const PQParams pd = pq_params(x, b->q + (size_t)s * x->d, true);
+            ck(pq_delta_direct(pd, b->probes + (size_t)s * nprobe, n, nprobe, x->nlist_global, x->g2l, Rd, d_out,
+                               b->st),
+               "pq_delta_direct");
+        }
         {
             StageScope stage(b, IVF_STAGE_SELECT);
             // sorted stage-1 lists only where they leave the library (shard outputs)
             ck(select_top_r(cm, n, m_out, b->st, adc != nullptr), "select_top_r");
-            if (use_delta) {
-                d_out = dadc ? dadc + (size_t)s * Rd : s1d;
-                ck(select_top_r(cd, n, d_out, b->st, adc != nullptr), "select_top_r (delta)");
-            }
+            if (scan_delta) ck(select_top_r(cd, n, d_out, b->st, adc != nullptr), "select_top_r (delta)");
         }
         StageScope stage(b, IVF_STAGE_RERANK);
         if (adc) {
@@ -857,11 +866,18 @@ void adopt_f32_lists(IndexCtx* x, int* d_counts, float* d_rows, int nlist, long 
     x->kind = kKindF32;
 }
 
-// INSITU_PQ_MIX=0 keeps a published delta's rows in their own tile stream
-// (scanned after each list's main rows) instead of the combined one
-bool mix_mode() {
-    const char* e = std::getenv("INSITU_PQ_MIX");
-    return !(e && e[0] == '0');
+// How a published delta segment is searched (INSITU_PQ_DELTA, read when the
+// delta is published): "direct" (default) -- its rows by pq_delta_direct, a
+// kernel of its own after the main scan (delta ranks above 32 fall back to
+// "seg"); "mix" -- each list's main and delta rows in one combined tile
+// stream, scanned in one pass with one LUT; "seg" -- the delta rows in their
+// own tiles, scanned after each list's main rows with the same LUT.
+enum DeltaMode { kDeltaDirect = 0, kDeltaMix = 1, kDeltaSeg = 2 };
+DeltaMode delta_mode() {
+    const char* e = std::getenv("INSITU_PQ_DELTA");
+    if (e && std::strcmp(e, "mix") == 0) return kDeltaMix;
+    if (e && std::strcmp(e, "seg") == 0) return kDeltaSeg;
+    return kDeltaDirect;
 }
 
 // Lays out every list's main rows followed by its delta rows (the delta
@@ -919,8 +935,9 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
                 ck(cudaMemcpy(hu.data(), s.rr_u8, hu.size(), cudaMemcpyDeviceToHost), "delta copy");
             }
         }
-        build_gring(s, counts, x->nlist, x->M, x->d);
-        if (n_delta > 0 && s.gring && x->main.gring && mix_mode()) build_mix(x, s, counts);
+        const DeltaMode mode = delta_mode();
+        build_gring(s, counts, x->nlist, x->M, x->d, mode == kDeltaDirect);
+        if (n_delta > 0 && s.gring && x->main.gring && mode == kDeltaMix) build_mix(x, s, counts);
     } catch (...) {
         s.release();
         throw;

@@ -115,6 +115,21 @@ __device__ __forceinline__ void warp_append(KeyFn keyf, int n, uint64_t cut, con
     }
 }
 
+// Ascending bitonic sort of one 64-bit key per lane across the warp.
+__device__ __forceinline__ uint64_t warp_sort32(uint64_t v) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+            const bool up = (lane & k) == 0, lower = (lane & j) == 0;
+            v = lower == up ? (o < v ? o : v) : (o > v ? o : v);
+        }
+    }
+    return v;
+}
+
 // Appends every key <= cut among ITEMS keys per thread held in registers
 // (keyj(j), kKeyNone for none; j is a compile-time index after unrolling, so
 // register arrays behind keyj stay in registers) with one atomic per warp:

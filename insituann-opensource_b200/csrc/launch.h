@@ -168,6 +168,13 @@ int64_t pq_gring_list_bytes(int count, int M);
 // builds the grouped-ring tile layout of every list from row-major codes [n, M]
 cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
                            const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st);
+// the Rd (<= 32) smallest delta keys of each query over the delta rows of its
+// probed lists, sorted, computed directly from the row-major delta codes
+// (PQParams::delta.data) without LUTs; probes [nq, nprobe] hold global list
+// ids mapped through list_map (nullptr: identity) like build_worklist's
+bool pq_delta_direct_usable(int M, int d, int Rd);
+cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, int nprobe, int nlist_global,
+                            const int32_t* list_map, int Rd, uint64_t* out, cudaStream_t st);
 // the combined tile stream of every list: its main rows (count_m, from the
 // main tiles) then its delta rows (count_d, from the delta tiles), laid out as
 // one list of count_m + count_d rows at mix_off[l]

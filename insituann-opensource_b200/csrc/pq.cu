@@ -194,7 +194,9 @@ struct GRing {
 // and at the window's end (or the tile's last step) all lanes store together,
 // lane j to out[its finishing step]: one 16-byte store per lane per 8 steps.
 // A stored sum at or below query k's bound thf sets bit k of maybe (a superset
-// of the keys the chunk's filter can admit).
+// of the keys the chunk's filter can admit), except at the steps from xdr on
+// (the delta rows of a combined main + delta stream, which the warp filters
+// itself; xdr past the tile: none).
 //
 // Q = queries per LUT entry.  Q = 4: one table of float4 entries; a
 // quarter-warp (one lane group) reads 8 distinct 16-byte bank groups.  Q = 2
@@ -208,7 +210,7 @@ struct GRing {
 template <int M, int NST, int Q>
 __device__ __forceinline__ void stagger_tile(const float* __restrict__ lutf, const uint32_t (&w)[M / 2], int nst,
                                              int j, int g, float2& s01, float2& s23, float4* out, float4 thf,
-                                             uint32_t& maybe) {
+                                             int xdr, uint32_t& maybe) {
     constexpr int MPL = M / 8;
     static_assert(Q == 4 || (Q == 2 && M % 16 == 0) || (Q == 1 && M == 32), "LUT layout");
     float4 fin = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -244,9 +246,11 @@ __device__ __forceinline__ void stagger_tile(const float* __restrict__ lutf, con
             const int fstep = (i & ~7) + ((j + 7) & 7);
             if (fstep <= i) {
                 out[fstep] = fin;
-                maybe |= (fin.x <= thf.x ? 1u : 0u);
-                if (Q >= 2) maybe |= (fin.y <= thf.y ? 2u : 0u);
-                if (Q == 4) maybe |= (fin.z <= thf.z ? 4u : 0u) | (fin.w <= thf.w ? 8u : 0u);
+                if (fstep < xdr) {
+                    maybe |= (fin.x <= thf.x ? 1u : 0u);
+                    if (Q >= 2) maybe |= (fin.y <= thf.y ? 2u : 0u);
+                    if (Q == 4) maybe |= (fin.z <= thf.z ? 4u : 0u) | (fin.w <= thf.w ? 8u : 0u);
+                }
             }
         }
     }
@@ -312,8 +316,8 @@ __device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, co
         const ListStore& D = p.delta;
         cp_async_4(&g.dcount, D.counts + l);
         cp_async_8(&g.dkoff, (D.key_off ? D.key_off : D.offsets) + l);
-        cp_async_8(&g.dgoff, D.gring_off + l);
         if (p.mix) cp_async_8(&g.mgoff, p.mix_off + l);
+        else cp_async_8(&g.dgoff, D.gring_off + l);
     } else {
         g.dcount = 0;
     }
@@ -332,7 +336,7 @@ __device__ __forceinline__ void desc_stage_b(GroupDesc& g, const PQParams& p, co
 //     before the group is even decoded (they are the same for every group);
 //   * the first code tile is requested before the LUT is built, each next
 //     tile one tile ahead, and each chunk's query bounds before its steps.
-template <int M, int DSUB, bool DELTA>
+template <int M, int DSUB, int DM>
 __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList wl, CandBuf cm, CandBuf cd,
                                                           int* counter) {
     using RG = GRing<M>;
@@ -354,6 +358,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
     __shared__ int64_t s_skoff[3], s_sgoff[3];
     __shared__ int s_scount[3];
     __shared__ unsigned long long s_thr1[kGQ];   // the second segment's bounds, read before the LUT build
+    __shared__ unsigned long long s_thd[3][kGQ]; // each chunk's delta bounds (combined stream), buffers as s_cnt
     // per-chunk totals and "some sum may pass" bits of the 4 queries, three
     // buffers in rotation: chunk c adds into buffer c % 3 and, after its first
     // barrier, clears buffer (c + 2) % 3 -- last read in chunk c - 1 (done
@@ -415,7 +420,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
         // the group's list in the main segment and, with the overlay, the same
         // list's delta rows: both are scanned here with the one LUT (read out of
         // s_gd before the next group's descriptor rewrites it)
-        const int count_m = s_gd.count, count_d = DELTA ? s_gd.dcount : 0;
+        const int count_m = s_gd.count, count_d = DM ? s_gd.dcount : 0;
         if (tid == 0) {
             s_scount[0] = count_m;
             s_scount[1] = count_d;
@@ -425,7 +430,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             s_sgoff[1] = s_gd.dgoff;
             s_scount[2] = count_m + count_d;
             s_skoff[2] = s_gd.koff;
-            s_sgoff[2] = DELTA && p.mix ? s_gd.mgoff : 0;
+            s_sgoff[2] = DM == 2 ? s_gd.mgoff : 0;
         }
         bool fetched = false;            // thread 0: stage A of the next descriptor issued
         bool staged = false;             // thread 0: its stage B issued
@@ -467,12 +472,11 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // (built when the delta is published) both are scanned in one pass,
             // over stripes of the combined list: positions below the main count
             // are main rows, the others delta rows (segment 2).
-            const bool mixed = DELTA && p.mix != nullptr && count_m > 0 && count_d > 0;
-            const int seg0 = DELTA ? (mixed ? 2 : (count_d > 0 ? 1 : 0)) : 0;
-            const int seg1 = DELTA && seg0 == 1 && count_m > 0 ? 0 : -1;
+            const int seg0 = DM == 2 ? 2 : DM == 1 && count_d > 0 ? 1 : 0;
+            const int seg1 = DM == 1 && seg0 == 1 && count_m > 0 ? 0 : -1;
             seg_setup(seg0, true, lanebase, ntiles, S, T0, wsteps, nchunks);
             const uint4* pre1 = nullptr;     // first tile of seg1 for this lane (null: none)
-            if (DELTA && seg1 >= 0) {
+            if (DM == 1 && seg1 >= 0) {
                 const uint4* lb1;
                 int64_t nt1, T01;
                 int S1, ws1, nc1;
@@ -480,7 +484,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 pre1 = lb1 + min(T01, nt1 - 1) * (8 * MPL);
             }
             bool have1 = false;              // w already holds seg1's first tile
-            if (DELTA && pre1 && wsteps == 0) {
+            if (DM == 1 && pre1 && wsteps == 0) {
                 load_tile<MPL>(pre1, 0, w);
                 have1 = true;
             } else {
@@ -502,7 +506,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr0[k] = k < nqg ? *((volatile unsigned long long*)(cb0.thr + s_gd.q[k])) : 0ull;
-                if (DELTA && seg1 >= 0 && tid < nqg)
+                if (DM == 1 && seg1 >= 0 && tid < nqg)
                     s_thr1[tid] = *((volatile unsigned long long*)(cm.thr + s_gd.q[tid]));
             }
             __syncthreads();
@@ -584,7 +588,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
                 thf = make_float4(tf[0], tf[1], tf[2], tf[3]);
             };
-            for (int si = 0; si < (DELTA ? 2 : 1); ++si) {
+            for (int si = 0; si < (DM == 1 ? 2 : 1); ++si) {
             const int seg = si == 0 ? seg0 : seg1;
             if (seg < 0) break;
             const int count = s_scount[seg];
@@ -592,7 +596,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             const CandBuf& cb = seg == 1 ? cd : cm;
             const uint32_t kbase = (uint32_t)s_skoff[seg];
             // combined stream: positions from cmain on are the delta's (key base dkbase)
-            const uint32_t cmain = seg == 2 ? (uint32_t)count_m : 0xFFFFFFFFu;
+            const uint32_t cmain = DM == 2 ? (uint32_t)count_m : 0xFFFFFFFFu;
             const uint32_t dkbase = (uint32_t)s_skoff[1];
             if (si == 1) {                     // the main rows after the delta rows: same LUT
                 seg_setup(seg, false, lanebase, ntiles, S, T0, wsteps, nchunks);
@@ -604,17 +608,23 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 s23 = make_float2(0.f, 0.f);
             }
             set_thf(thr0);
+            // first step (of the segment) at which this lane group finishes a
+            // delta row of the combined stream: position rid*S + x - 7 >= cmain
+            const int xd = DM == 2 ? (int)cmain - rid * S + 7 : 0x7FFFFFFF;
             for (int t = 0; t < nchunks; ++t) {
                 uint64_t thr[kGQ];    // read now, used after the steps: a bound only ever decreases
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k)
                     thr[k] = k < nqg ? *((volatile unsigned long long*)(cb.thr + qid[k])) : 0ull;
+                // the delta bounds land in shared memory during the steps (an older
+                // copy of a bound is only a looser one)
+                if (DM == 2 && warp == 1 && lane < nqg) cp_async_8(&s_thd[cpar][lane], cd.thr + (lane == 0 ? qid[0] : lane == 1 ? qid[1] : lane == 2 ? qid[2] : qid[3]));
                 uint32_t maybe = 0;
 #pragma unroll 1
                 for (int tl = 0; tl < kRSteps / 16; ++tl) {
                     const int x0 = t * kRSteps + 16 * tl;
                     if (x0 >= wsteps) break;
-                    if (DELTA && pre1 && x0 + 16 >= wsteps) {     // this warp's last tile of seg0
+                    if (DM == 1 && pre1 && x0 + 16 >= wsteps) {     // this warp's last tile of seg0
                         load_tile<MPL>(pre1, 0, wn);
                         have1 = true;
                     } else {
@@ -624,31 +634,132 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     float4* out = dist4 + rid * kRSteps + 16 * tl;
                     const bool full = wsteps - x0 >= 16;
                     if (qmode == 4) {
-                        if (full) stagger_tile<M, 16, 4>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
-                        else stagger_tile<M, 15, 4>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, maybe);
+                        if (full) stagger_tile<M, 16, 4>(smf, w, 16, j, grp, s01, s23, out, thf, xd - x0, maybe);
+                        else stagger_tile<M, 15, 4>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, xd - x0, maybe);
                     } else if (M != 32 || qmode == 2) {
-                        if (full) stagger_tile<M, 16, 2>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
-                        else stagger_tile<M, 15, 2>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, maybe);
+                        if (full) stagger_tile<M, 16, 2>(smf, w, 16, j, grp, s01, s23, out, thf, xd - x0, maybe);
+                        else stagger_tile<M, 15, 2>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf, xd - x0, maybe);
                     } else {
-                        if (full) stagger_tile<M, 16, (M == 32 ? 1 : 2)>(smf, w, 16, j, grp, s01, s23, out, thf, maybe);
+                        if (full) stagger_tile<M, 16, (M == 32 ? 1 : 2)>(smf, w, 16, j, grp, s01, s23, out, thf, xd - x0, maybe);
                         else stagger_tile<M, 15, (M == 32 ? 1 : 2)>(smf, w, wsteps - x0, j, grp, s01, s23, out, thf,
-                                                                   maybe);
+                                                                   xd - x0, maybe);
                     }
 #pragma unroll
                     for (int u = 0; u < 4 * MPL; ++u) w[u] = wn[u];
                 }
                 maybe = __reduce_or_sync(0xffffffffu, maybe);
-                bool cdelta = false;             // the chunk finishes delta rows of the combined stream
-                if (DELTA && seg == 2) {
-                    // a chunk that finishes delta rows is always filtered (the store
-                    // test compares with the main bounds only)
-                    const int va = t * kRSteps >= 7 ? t * kRSteps - 7 : 0, vb = min(S, t * kRSteps + kRSteps - 7);
-                    for (int r = 0; r < kRRings; ++r)
-                        cdelta |= r * S + va < count && r * S + vb > (int)cmain;
-                    if (cdelta) maybe |= (1u << nqg) - 1u;
-                }
                 if (lane == 0 && (maybe | force)) atomicOr(&s_any[cpar], maybe | force);
+                if (DM == 2 && warp == 1) cp_async_wait_all();
                 __syncthreads();
+                if (DM == 2) {
+                    // The delta rows of the combined stream that this warp's stripes
+                    // finished in the chunk, against the delta bounds.  The warp
+                    // wrote their slots itself (no block barrier is needed to read
+                    // them, and the next writes to them are its own); lane i takes
+                    // the warp's i-th such row (a list's delta rows are few, so
+                    // usually one pass of 32).  A query with more passing keys than
+                    // the delta rank Rd gets a new bound: the Rd-th smallest of any
+                    // Rd or more existing keys bounds the rank-Rd key from above.
+                    const int va = t * kRSteps >= 7 ? t * kRSteps - 7 : 0, vb = min(S, t * kRSteps + kRSteps - 7);
+                    int lo[4], ln[4], m = 0;
+#pragma unroll
+                    for (int g4 = 0; g4 < 4; ++g4) {
+                        const int r = 4 * warp + g4;
+                        const int a = max((int)cmain, r * S + va), b = min(count, r * S + vb);
+                        lo[g4] = a;
+                        ln[g4] = va < vb && b > a ? b - a : 0;
+                        m += ln[g4];
+                    }
+                    if (m > 0) {
+                        // item i of the warp's rows: its four sums and delta position
+                        auto item = [&](int i, float4& fv, uint32_t& dp) -> bool {
+                            if (i >= m) return false;
+                            int g4 = 0, a = lo[0];
+                            if (i >= ln[0]) {
+                                i -= ln[0]; g4 = 1; a = lo[1];
+                                if (i >= ln[1]) {
+                                    i -= ln[1]; g4 = 2; a = lo[2];
+                                    if (i >= ln[2]) { i -= ln[2]; g4 = 3; a = lo[3]; }
+                                }
+                            }
+                            const int v = a + i, r = 4 * warp + g4;
+                            fv = dist4[r * kRSteps + (v - r * S + 7 - t * kRSteps)];
+                            dp = (uint32_t)v - cmain;
+                            return true;
+                        };
+                        auto dkey = [&](bool ok, const float4& fv, uint32_t dp, int k) -> uint64_t {
+                            const float dk = k == 0 ? fv.x : k == 1 ? fv.y : k == 2 ? fv.z : fv.w;
+                            return ok ? make_key(__float_as_uint(dk), dkbase + dp) : kKeyNone;
+                        };
+                        uint64_t bnd[kGQ];
+                        int nk[kGQ];
+                        auto count_pass = [&]() {
+#pragma unroll
+                            for (int k = 0; k < kGQ; ++k) nk[k] = 0;
+                            for (int i0 = 0; i0 < m; i0 += 32) {
+                                float4 fv;
+                                uint32_t dp;
+                                const bool ok = item(i0 + lane, fv, dp);
+#pragma unroll
+                                for (int k = 0; k < kGQ; ++k)
+                                    if (k < nqg) nk[k] += __popc(__ballot_sync(0xffffffffu, dkey(ok, fv, dp, k) <= bnd[k]));
+                            }
+                        };
+#pragma unroll
+                        for (int k = 0; k < kGQ; ++k) {
+                            const unsigned long long b = k < nqg ? s_thd[cpar][k] : 0ull;
+                            bnd[k] = b < kKeyNone - 1 ? b : kKeyNone - 1;
+                        }
+                        count_pass();
+                        if (cd.R <= 32) {
+                            float4 fv;
+                            uint32_t dp;
+                            const bool ok = item(lane, fv, dp);
+                            bool cut = false;
+#pragma unroll
+                            for (int k = 0; k < kGQ; ++k) {
+                                if (k >= nqg || nk[k] <= cd.R) continue;
+                                const uint64_t kk = dkey(ok, fv, dp, k);
+                                const bool pass = kk <= bnd[k];
+                                if (__popc(__ballot_sync(0xffffffffu, pass)) < cd.R) continue;
+                                const uint64_t mk = warp_sort32(pass ? kk : kKeyNone);
+                                const uint64_t c = __shfl_sync(0xffffffffu, mk, cd.R - 1);
+                                if (c < bnd[k]) {
+                                    bnd[k] = c;
+                                    cut = true;
+                                    if (lane == 0) atomicMin(cd.thr + qid[k], (unsigned long long)c);
+                                }
+                            }
+                            if (cut) count_pass();
+                        }
+                        // one atomic per query, the queries' in flight together
+                        const int myn = lane == 0 ? nk[0] : lane == 1 ? nk[1] : lane == 2 ? nk[2] : nk[3];
+                        const int myq = lane == 0 ? qid[0] : lane == 1 ? qid[1] : lane == 2 ? qid[2] : qid[3];
+                        int mybase = 0;
+                        if (lane < nqg && myn > 0) mybase = atomicAdd(cd.cnt + myq, myn);
+                        int at[kGQ];
+#pragma unroll
+                        for (int k = 0; k < kGQ; ++k) at[k] = __shfl_sync(0xffffffffu, mybase, k);
+                        for (int i0 = 0; i0 < m; i0 += 32) {
+                            float4 fv;
+                            uint32_t dp;
+                            const bool ok = item(i0 + lane, fv, dp);
+#pragma unroll
+                            for (int k = 0; k < kGQ; ++k) {
+                                if (k >= nqg || nk[k] == 0) continue;
+                                const uint64_t kk = dkey(ok, fv, dp, k);
+                                const bool pass = kk <= bnd[k];
+                                const unsigned ball = __ballot_sync(0xffffffffu, pass);
+                                if (pass) {
+                                    const int i = at[k] + __popc(ball & ((1u << lane) - 1u));
+                                    if (i < cd.cap) cd.keys[(size_t)qid[k] * cd.cap + i] = kk;
+                                    else atomicExch(cd.overflow, 1);
+                                }
+                                at[k] += __popc(ball);
+                            }
+                        }
+                    }
+                }
                 if (tid == 0 && fetched && !staged) {         // stage A landed long ago
                     cp_async_wait_all();
                     desc_stage_b(s_gd, p, wl, nxt, NG);
@@ -719,22 +830,6 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 for (int k = 0; k < kGQ; ++k)
                     if (k < nqg && totk[k] > 0)
                         warp_append_items<kE>([&](int e) { return key_of(e, k); }, cut[k], cb, qid[k]);
-                if (DELTA && cdelta) {
-                    // the delta rows of the chunk: every key goes to the delta buffer
-                    // (a list's delta rows are few; the buffer holds all of them)
-#pragma unroll
-                    for (int k = 0; k < kGQ; ++k) {
-                        if (k >= nqg) break;
-                        warp_append_items<kE>(
-                            [&](int e) -> uint64_t {
-                                const float dk = k == 0 ? f[e].x : k == 1 ? f[e].y : k == 2 ? f[e].z : f[e].w;
-                                return vid[e] != 0xFFFFFFFFu && vid[e] >= cmain
-                                           ? make_key(__float_as_uint(dk), dkbase + vid[e] - cmain)
-                                           : kKeyNone;
-                            },
-                            kKeyNone - 1, cd, qid[k]);
-                    }
-                }
                 if (sel) __syncthreads();     // the histograms lived in the slots
                 set_thf(cut);
             }
@@ -758,33 +853,35 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
 }
 
 // one launch per search pass: with a published delta segment every group also
-// scans its list's delta rows (the DELTA instantiation)
-template <int M, int DSUB, bool DELTA>
+// scans its list's delta rows, in the combined tile stream (DM = 2) or after
+// the main rows from the delta's own tiles (DM = 1)
+template <int M, int DSUB, int DM>
 cudaError_t launch_gring_seg(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
                              cudaStream_t st) {
     const size_t smem = GRing<M>::smem_bytes();
-    cudaError_t e = cudaFuncSetAttribute(pq_stagger_kernel<M, DSUB, DELTA>,
+    cudaError_t e = cudaFuncSetAttribute(pq_stagger_kernel<M, DSUB, DM>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e) return e;
     int dev = 0, sms = 148, per_sm = 1;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_stagger_kernel<M, DSUB, DELTA>, kRT, smem);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, pq_stagger_kernel<M, DSUB, DM>, kRT, smem);
     if (per_sm < 1) return cudaErrorInvalidConfiguration;
     long long items = (long long)max_groups;
     long long grid = (long long)sms * per_sm;
     if (grid > items) grid = items;
     if (grid < 1) grid = 1;
     note_launch();
-    pq_stagger_kernel<M, DSUB, DELTA><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
+    pq_stagger_kernel<M, DSUB, DM><<<(int)grid, kRT, smem, st>>>(p, wl, cm, cd, counter);
     return cudaGetLastError();
 }
 
 template <int M, int DSUB>
 cudaError_t launch_gring(const PQParams& p, WorkList wl, int max_groups, CandBuf cm, CandBuf cd, int* counter,
                          cudaStream_t st) {
-    if (p.has_delta) return launch_gring_seg<M, DSUB, true>(p, wl, max_groups, cm, cd, counter, st);
-    return launch_gring_seg<M, DSUB, false>(p, wl, max_groups, cm, cd, counter, st);
+    if (p.has_delta && p.mix) return launch_gring_seg<M, DSUB, 2>(p, wl, max_groups, cm, cd, counter, st);
+    if (p.has_delta) return launch_gring_seg<M, DSUB, 1>(p, wl, max_groups, cm, cd, counter, st);
+    return launch_gring_seg<M, DSUB, 0>(p, wl, max_groups, cm, cd, counter, st);
 }
 
 template <int MPL>
@@ -1279,6 +1376,129 @@ cudaError_t pq_build_gring_mix(const uint8_t* main_tiles, const int64_t* main_of
     }
 #undef ISB_MIX
     return cudaGetLastError();
+}
+
+namespace {
+
+constexpr int kDW = 8;      // warps per CTA of the direct delta kernel
+
+// The delta rows of every list a query probes, scanned without LUTs: each
+// lane takes one row and computes its ADC distance from the residual and the
+// codebook with the operations of the LUT build and the stagger sum in their
+// order (entry m = sum over u of (r_u - c_u)^2, products and sums rounded
+// separately; distance = entries added in m order), so every key equals the
+// one the LUT scan would form.  A warp keeps its 32 smallest keys (one per
+// lane, ascending) and merges each batch of 32 rows into them only when some
+// row beats its largest; the CTA (one query) merges its warps' lists and
+// writes the Rd <= 32 smallest, sorted, kKeyNone past the available keys.  A
+// repeated probe scans its list again (its keys count twice, as in the
+// candidate-buffer path).  Replaces, for small deltas, the per-list delta
+// scan of build_delta_pq_mutable_publish / the overlay search
+// (updates/pq_update.cu:448-523).
+template <int M, int DSUB>
+__global__ void __launch_bounds__(kDW * 32) delta_direct_kernel(PQParams p, const int32_t* __restrict__ probes,
+                                                               int nprobe, int nlist_global,
+                                                               const int32_t* __restrict__ list_map, int Rd,
+                                                               uint64_t* __restrict__ out) {
+    constexpr int d = M * DSUB;
+    __shared__ float s_res[kDW][d];
+    __shared__ uint64_t s_top[kDW * 32];
+    const int q = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const ListStore& D = p.delta;
+    uint64_t top = kKeyNone;
+    for (int c = warp; c < nprobe; c += kDW) {
+        const int g = probes[(size_t)q * nprobe + c];
+        if (g < 0 || g >= nlist_global) continue;
+        const int l = list_map ? list_map[g] : g;
+        if (l < 0) continue;
+        const int cnt = D.counts[l];
+        if (cnt <= 0) continue;
+        const int64_t off = D.offsets[l];
+        const uint32_t kb = (uint32_t)(D.key_off ? D.key_off[l] : off);
+        const float* cv = p.cent + (size_t)l * d;
+        for (int x = lane; x < d; x += 32) s_res[warp][x] = __fsub_rn(p.q[(size_t)q * d + x], cv[x]);
+        __syncwarp();
+        for (int r0 = 0; r0 < cnt; r0 += 32) {
+            const int r = r0 + lane;
+            uint64_t key = kKeyNone;
+            if (r < cnt) {
+                const uint4* cp = reinterpret_cast<const uint4*>(D.data + (size_t)(off + r) * M);
+                float dist = 0.f;
+#pragma unroll
+                for (int h = 0; h < M / 16; ++h) {
+                    const uint4 w4 = __ldg(cp + h);
+                    const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int b = 0; b < 16; ++b) {
+                        const int m = 16 * h + b;
+                        const uint32_t code = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+                        const float* cb = p.codebook_t + ((size_t)code * M + m) * DSUB;
+                        float cbv[DSUB];
+                        if constexpr (DSUB % 4 == 0) {
+#pragma unroll
+                            for (int u = 0; u < DSUB; u += 4) {
+                                const float4 t4 = __ldg(reinterpret_cast<const float4*>(cb + u));
+                                cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
+                            }
+                        } else {
+                            const float2 t2 = __ldg(reinterpret_cast<const float2*>(cb));
+                            cbv[0] = t2.x; cbv[1] = t2.y;
+                        }
+                        float a = 0.f;
+#pragma unroll
+                        for (int u = 0; u < DSUB; ++u) {
+                            const float x = __fsub_rn(s_res[warp][m * DSUB + u], cbv[u]);
+                            a = u == 0 ? __fmul_rn(x, x) : __fadd_rn(a, __fmul_rn(x, x));
+                        }
+                        dist = m == 0 ? a : __fadd_rn(dist, a);
+                    }
+                }
+                key = make_key(__float_as_uint(dist), kb + (uint32_t)r);
+            }
+            const uint64_t worst = __shfl_sync(0xffffffffu, top, 31);
+            if (__any_sync(0xffffffffu, key < worst)) {
+                // the batch sorted and reversed against the ascending list: their
+                // lane-wise minima are the 32 smallest of both, a bitonic sequence
+                uint64_t b = warp_sort32(key);
+                b = __shfl_sync(0xffffffffu, b, 31 - lane);
+                uint64_t v = b < top ? b : top;
+#pragma unroll
+                for (int j = 16; j > 0; j >>= 1) {
+                    const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+                    v = (lane & j) == 0 ? (o < v ? o : v) : (o > v ? o : v);
+                }
+                top = v;
+            }
+        }
+        __syncwarp();     // the residual is rewritten for the next probe
+    }
+    s_top[warp * 32 + lane] = top;
+    block_bitonic_sort<kDW * 32>(s_top, kDW * 32);
+    for (int i = threadIdx.x; i < Rd; i += kDW * 32) out[(size_t)q * Rd + i] = s_top[i];
+}
+
+}  // namespace
+
+bool pq_delta_direct_usable(int M, int d, int Rd) {
+    return Rd >= 1 && Rd <= 32 && pq_group_usable(M, d) && d <= kPMaxD;
+}
+
+cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, int nprobe, int nlist_global,
+                            const int32_t* list_map, int Rd, uint64_t* out, cudaStream_t st) {
+    if (!pq_delta_direct_usable(p.M, p.d, Rd) || !p.delta.data || !p.codebook_t) return cudaErrorInvalidValue;
+    if (nq <= 0) return cudaSuccess;
+    const int ds = p.d / p.M;
+    note_launch();
+#define ISB_DIRECT(MM, DS)                                                                                    \
+    if (p.M == MM && ds == DS) {                                                                              \
+        delta_direct_kernel<MM, DS><<<nq, kDW * 32, 0, st>>>(p, probes, nprobe, nlist_global, list_map, Rd, out); \
+        return cudaGetLastError();                                                                            \
+    }
+    ISB_DIRECT(16, 2) ISB_DIRECT(16, 4) ISB_DIRECT(16, 8)
+    ISB_DIRECT(32, 2) ISB_DIRECT(32, 4) ISB_DIRECT(32, 8)
+    ISB_DIRECT(48, 2) ISB_DIRECT(48, 4)
+#undef ISB_DIRECT
+    return cudaErrorInvalidValue;
 }
 
 bool pq_group_usable(int M, int d) {

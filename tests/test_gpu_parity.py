@@ -191,8 +191,8 @@ def test_exact_deletes(cuda_ok, d):
 def test_pq_deletes(cuda_ok, pq_medium, f32, overlay, monkeypatch):
     """deleted positions keep their stage-1 slots and are not reranked; with a
     published delta, main keys are masked and delta keys are not (f32: the
-    delta rows in their own tile stream, u8: in the combined one)."""
-    monkeypatch.setenv("INSITU_PQ_MIX", "0" if f32 else "1")
+    delta rows in the combined tile stream, u8: by the direct delta kernel)."""
+    monkeypatch.setenv("INSITU_PQ_DELTA", "mix" if f32 else "direct")
     p, q = pq_medium
     nq, nprobe, k, R = q.shape[0], 8, 10, 64
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
@@ -318,11 +318,14 @@ def test_pq_medium_routed(cuda_ok, pq_medium, R, k):
     assert np.array_equal(gpu_stage1(p, q, probes, max(R, k)), np.sort(s1, axis=1))
 
 
-@pytest.mark.parametrize("mix", ["1", "0"])
-def test_pq_overlay(cuda_ok, pq_medium, mix, monkeypatch):
-    """main + delta search; mix "1" scans each list's main and delta rows as one
-    combined tile stream, "0" as two.  One list has no main rows (delta only)."""
-    monkeypatch.setenv("INSITU_PQ_MIX", mix)
+@pytest.mark.parametrize("mode", ["direct", "mix", "seg"])
+def test_pq_overlay(cuda_ok, pq_medium, mode, monkeypatch):
+    """main + delta search with the delta rows scanned by their own kernel
+    (direct; its rank limit 32 sends delta_topk 48 to seg), in one combined
+    tile stream with each list's main rows (mix), or in their own tiles after
+    the main rows (seg).  One list has no main rows (delta only), and every
+    seventh query probes it twice."""
+    monkeypatch.setenv("INSITU_PQ_DELTA", mode)
     p, q = pq_medium
     p = dict(p)
     counts = p["counts"].copy()
@@ -333,7 +336,7 @@ def test_pq_overlay(cuda_ok, pq_medium, mix, monkeypatch):
     delta = synth.delta_segment(20000, len(p["counts"]), p["codebook"].shape[0], base_id=n, d=q.shape[1], seed=3)
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     probes[::7, 0] = 3
-    for dtk in (16, 5):
+    for dtk in (16, 5, 48):
         gi, gd = gpu_pq(p, q, probes, k, R, delta=delta, delta_topk=dtk)
         oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
                                   probes, k, rerank_n=R, base_u8=p["base_u8"], delta=delta, delta_topk=dtk)
