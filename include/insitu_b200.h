@@ -34,10 +34,12 @@
  *                       (default) on the tensor cores, 0 on the CUDA cores
  *   INSITU_PQ_DELTA     read by ivf_pq_publish_delta / ivf_pq_insert: how
  *                       the published delta rows are searched -- "direct"
- *                       (default) by a kernel of their own after the main
- *                       scan (delta_topk above 32 as "seg"), "mix" in one
- *                       tile stream with each list's main rows, "seg" in
- *                       their own tiles after each list's main rows
+ *                       by a kernel of their own after the main scan
+ *                       (delta_topk above 32 as "seg"), "mix" in one tile
+ *                       stream with each list's main rows, "seg" in their
+ *                       own tiles after each list's main rows; unset:
+ *                       "direct" up to 48 delta rows per list on average,
+ *                       else "mix"
  *
  * Citations are paths inside the reference project
  * (mindtravel/InSituANN-OpenSource).

@@ -867,17 +867,22 @@ void adopt_f32_lists(IndexCtx* x, int* d_counts, float* d_rows, int nlist, long 
 }
 
 // How a published delta segment is searched (INSITU_PQ_DELTA, read when the
-// delta is published): "direct" (default) -- its rows by pq_delta_direct, a
-// kernel of its own after the main scan (delta ranks above 32 fall back to
-// "seg"); "mix" -- each list's main and delta rows in one combined tile
-// stream, scanned in one pass with one LUT; "seg" -- the delta rows in their
-// own tiles, scanned after each list's main rows with the same LUT.
-enum DeltaMode { kDeltaDirect = 0, kDeltaMix = 1, kDeltaSeg = 2 };
+// delta is published): "direct" -- its rows by pq_delta_direct, a kernel of
+// its own after the main scan, which computes each row's distance without a
+// LUT (delta ranks above 32 fall back to "seg"); "mix" -- each list's main and
+// delta rows in one combined tile stream, scanned in one pass with the main
+// rows' LUT (a second copy of the main tiles); "seg" -- the delta rows in
+// their own tiles, scanned after each list's main rows with the same LUT.
+// Unset: "direct" for deltas of at most kDirectRowsPerList rows per list on
+// average (a LUT would cost more than it saves), else "mix".
+enum DeltaMode { kDeltaAuto = -1, kDeltaDirect = 0, kDeltaMix = 1, kDeltaSeg = 2 };
+constexpr long long kDirectRowsPerList = 48;
 DeltaMode delta_mode() {
     const char* e = std::getenv("INSITU_PQ_DELTA");
+    if (e && std::strcmp(e, "direct") == 0) return kDeltaDirect;
     if (e && std::strcmp(e, "mix") == 0) return kDeltaMix;
     if (e && std::strcmp(e, "seg") == 0) return kDeltaSeg;
-    return kDeltaDirect;
+    return kDeltaAuto;
 }
 
 // Lays out every list's main rows followed by its delta rows (the delta
@@ -935,7 +940,8 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
                 ck(cudaMemcpy(hu.data(), s.rr_u8, hu.size(), cudaMemcpyDeviceToHost), "delta copy");
             }
         }
-        const DeltaMode mode = delta_mode();
+        DeltaMode mode = delta_mode();
+        if (mode == kDeltaAuto) mode = n_delta <= kDirectRowsPerList * x->nlist ? kDeltaDirect : kDeltaMix;
         build_gring(s, counts, x->nlist, x->M, x->d, mode == kDeltaDirect);
         if (n_delta > 0 && s.gring && x->main.gring && mode == kDeltaMix) build_mix(x, s, counts);
     } catch (...) {

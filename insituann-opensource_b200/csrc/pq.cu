@@ -168,9 +168,9 @@ constexpr int kRSteps = kRChunk / kRRings;   // steps per filtered chunk (a mult
 static_assert(kRSteps % 16 == 0, "a chunk is whole tiles");
 
 __host__ __device__ inline int64_t gring_tiles(int count) { return (int64_t)(count + 7) / 16 + 3; }
-// vectors per stripe: count / kRRings rounded up to whole tiles
+// vectors per stripe: count / kRRings rounded up to a multiple of 8 (half a tile)
 __host__ __device__ inline int gring_stripe(int count) {
-    return (int)(((int64_t)count + 16 * kRRings - 1) / (16 * kRRings)) * 16;
+    return (int)(((int64_t)count + 8 * kRRings - 1) / (8 * kRRings)) * 8;
 }
 // filtered chunks of one list: stripe 0 takes min(S, count) + 7 steps
 __host__ __device__ inline int gring_chunks(int count) {
@@ -268,9 +268,14 @@ __device__ __forceinline__ uint4 ldg_v4_here(const uint4* ptr) {
     return r;
 }
 
+// The 16 steps of a lane from half-tile H on (tile H/2, or the second half of
+// tile (H-1)/2 and the first half of the next for odd H): a tile's bytes are
+// its lanes' 16-byte pieces u = 0..MPL-1 one after another (steps 8u/MPL ..
+// of the lane in piece u), so the pieces from half a tile on are the same
+// pieces 64*MPL bytes further, read with the same static byte indexing.
 template <int MPL>
-__device__ __forceinline__ void load_tile(const uint4* lanebase, int64_t T, uint32_t (&w)[4 * MPL]) {
-    const uint4* tp = lanebase + T * (8 * MPL);   // a tile is 128*MPL bytes = 8*MPL uint4
+__device__ __forceinline__ void load_tile(const uint4* lanebase, int64_t H, uint32_t (&w)[4 * MPL]) {
+    const uint4* tp = lanebase + H * (4 * MPL);   // half a tile is 64*MPL bytes = 4*MPL uint4
 #pragma unroll
     for (int u = 0; u < MPL; ++u) {
         const uint4 x = ldg_v4_here(tp + 8 * u);
@@ -438,16 +443,17 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             uint32_t w[4 * MPL], wn[4 * MPL];
             // segment seg's stripes and tiles (from s_gd for the first segment,
             // before the barrier that publishes the shared copies)
-            auto seg_setup = [&](int seg, bool from_desc, const uint4*& lanebase, int64_t& ntiles, int& S,
-                                 int64_t& T0, int& wsteps, int& nchunks) {
+            auto seg_setup = [&](int seg, bool from_desc, const uint4*& lanebase, int64_t& hmax, int& S,
+                                 int64_t& H0, int& wsteps, int& nchunks) {
                 const int count = seg == 2 ? count_m + count_d : (seg ? count_d : count_m);
                 const int64_t goff =
                     from_desc ? (seg == 2 ? s_gd.mgoff : (seg ? s_gd.dgoff : s_gd.goff)) : s_sgoff[seg];
                 const uint8_t* tiles = (seg == 2 ? p.mix : (seg ? p.delta.gring : p.main.gring)) + goff;
-                ntiles = gring_tiles(count);
+                hmax = 2 * gring_tiles(count) - 2;    // last half tile a 16-step load may start on
                 // Lane group r owns the stripe [r*S, r*S + S) of the list (S a
-                // multiple of 16, so a stripe starts on a tile) and runs through it
-                // without draining: it finishes vector r*S + x - 7 at step x.
+                // multiple of 8, so a stripe starts on a tile or half way into
+                // one: half tile H0) and runs through it without draining: it
+                // finishes vector r*S + x - 7 at step x.
                 // Steps are cut into chunks of kRSteps; after each chunk the CTA
                 // filters the kRRings * kRSteps finished slots.  The longest
                 // stripe (group 0) takes min(S, count) + 7 steps.
@@ -457,10 +463,10 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 wsteps = wa < count ? min(S, count - wa) + 7 : 0;    // steps of this warp (its group 0)
                 nchunks = gring_chunks(count);
                 lanebase = reinterpret_cast<const uint4*>(tiles) + j;
-                T0 = a / 16;
+                H0 = a / 8;
             };
             const uint4* lanebase;
-            int64_t ntiles, T0;
+            int64_t hmax, H0;
             int S, wsteps, nchunks;
             // With a delta segment the (short) delta rows go first and the
             // main rows second: the second segment's first tile is then
@@ -474,21 +480,21 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // are main rows, the others delta rows (segment 2).
             const int seg0 = DM == 2 ? 2 : DM == 1 && count_d > 0 ? 1 : 0;
             const int seg1 = DM == 1 && seg0 == 1 && count_m > 0 ? 0 : -1;
-            seg_setup(seg0, true, lanebase, ntiles, S, T0, wsteps, nchunks);
+            seg_setup(seg0, true, lanebase, hmax, S, H0, wsteps, nchunks);
             const uint4* pre1 = nullptr;     // first tile of seg1 for this lane (null: none)
             if (DM == 1 && seg1 >= 0) {
                 const uint4* lb1;
-                int64_t nt1, T01;
+                int64_t hm1, H01;
                 int S1, ws1, nc1;
-                seg_setup(seg1, true, lb1, nt1, S1, T01, ws1, nc1);
-                pre1 = lb1 + min(T01, nt1 - 1) * (8 * MPL);
+                seg_setup(seg1, true, lb1, hm1, S1, H01, ws1, nc1);
+                pre1 = lb1 + min(H01, hm1) * (4 * MPL);
             }
             bool have1 = false;              // w already holds seg1's first tile
             if (DM == 1 && pre1 && wsteps == 0) {
                 load_tile<MPL>(pre1, 0, w);
                 have1 = true;
             } else {
-                load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+                load_tile<MPL>(lanebase, min(H0, hmax), w);
             }
             {
                 const float* cv = p.cent + (size_t)l * d;
@@ -599,8 +605,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             const uint32_t cmain = DM == 2 ? (uint32_t)count_m : 0xFFFFFFFFu;
             const uint32_t dkbase = (uint32_t)s_skoff[1];
             if (si == 1) {                     // the main rows after the delta rows: same LUT
-                seg_setup(seg, false, lanebase, ntiles, S, T0, wsteps, nchunks);
-                if (!have1) load_tile<MPL>(lanebase, min(T0, ntiles - 1), w);
+                seg_setup(seg, false, lanebase, hmax, S, H0, wsteps, nchunks);
+                if (!have1) load_tile<MPL>(lanebase, min(H0, hmax), w);
                 pre1 = nullptr;
 #pragma unroll
                 for (int k = 0; k < kGQ; ++k) thr0[k] = k < nqg ? s_thr1[k] : 0ull;
@@ -628,7 +634,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                         load_tile<MPL>(pre1, 0, wn);
                         have1 = true;
                     } else {
-                        load_tile<MPL>(lanebase, min(T0 + x0 / 16 + 1, ntiles - 1), wn);
+                        load_tile<MPL>(lanebase, min(H0 + 2 * (x0 / 16 + 1), hmax), wn);
                     }
                     // slot of (group r, step s of the chunk) = r * kRSteps + s
                     float4* out = dist4 + rid * kRSteps + 16 * tl;
