@@ -895,7 +895,7 @@ void build_mix(IndexCtx* x, Segment& s, const int* dcounts) {
     int64_t acc = 0;
     for (int l = 0; l < x->nlist; ++l) {
         off[(size_t)l] = acc;
-        acc += pq_gring_list_bytes(mc[(size_t)l] + dcounts[l], x->M);
+        acc += pq_mix_list_bytes(mc[(size_t)l], dcounts[l], x->M);
     }
     s.mix_off = dcopy(off.data(), off.size(), s.owned);
     s.mix = dalloc<uint8_t>((size_t)acc + 64, s.owned);

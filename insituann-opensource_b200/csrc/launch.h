@@ -175,9 +175,11 @@ cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const i
 bool pq_delta_direct_usable(int M, int d, int Rd);
 cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, int nprobe, int nlist_global,
                             const int32_t* list_map, int Rd, uint64_t* out, cudaStream_t st);
-// the combined tile stream of every list: its main rows (count_m, from the
-// main tiles) then its delta rows (count_d, from the delta tiles), laid out as
-// one list of count_m + count_d rows at mix_off[l]
+// the combined tile stream of every list (pq.cu, mix_stripes): each of the
+// 32 stripes holds its share of the list's main rows, then its share of the
+// delta rows, from the main and delta tiles; list l's bytes at mix_off[l],
+// pq_mix_list_bytes of them
+int64_t pq_mix_list_bytes(int count_main, int count_delta, int M);
 cudaError_t pq_build_gring_mix(const uint8_t* main_tiles, const int64_t* main_off, const int32_t* main_counts,
                                const uint8_t* delta_tiles, const int64_t* delta_off, const int32_t* delta_counts,
                                const int64_t* mix_off, int nlist, int M, uint8_t* out, cudaStream_t st);

@@ -172,6 +172,21 @@ __host__ __device__ inline int64_t gring_tiles(int count) { return (int64_t)(cou
 __host__ __device__ inline int gring_stripe(int count) {
     return (int)(((int64_t)count + 8 * kRRings - 1) / (8 * kRRings)) * 8;
 }
+// The combined main + delta tile stream of a list (PQParams::mix): stripe r
+// holds the main rows r*Sm .. r*Sm + Sm - 1 at its steps 0 .. Sm - 1 and the
+// delta rows r*Sd .. r*Sd + Sd - 1 at its steps Sm .. Sm + Sd - 1 (each part
+// only below its count), S = Sm + Sd rounded up to 8, kRRings * S positions in
+// all: every warp takes a share of the delta rows in the same steps.
+struct MixStripes {
+    int Sm, Sd, S;
+};
+__host__ __device__ inline MixStripes mix_stripes(int cm, int cd) {
+    MixStripes m;
+    m.Sm = (cm + kRRings - 1) / kRRings;
+    m.Sd = (cd + kRRings - 1) / kRRings;
+    m.S = (m.Sm + m.Sd + 7) / 8 * 8;
+    return m;
+}
 // filtered chunks of one list: stripe 0 takes min(S, count) + 7 steps
 __host__ __device__ inline int gring_chunks(int count) {
     if (count <= 0) return 0;
@@ -433,7 +448,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             s_sgoff[0] = s_gd.goff;
             s_skoff[1] = s_gd.dkoff;
             s_sgoff[1] = s_gd.dgoff;
-            s_scount[2] = count_m + count_d;
+            s_scount[2] = kRRings * mix_stripes(count_m, count_d).S;
             s_skoff[2] = s_gd.koff;
             s_sgoff[2] = DM == 2 ? s_gd.mgoff : 0;
         }
@@ -445,7 +460,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             // before the barrier that publishes the shared copies)
             auto seg_setup = [&](int seg, bool from_desc, const uint4*& lanebase, int64_t& hmax, int& S,
                                  int64_t& H0, int& wsteps, int& nchunks) {
-                const int count = seg == 2 ? count_m + count_d : (seg ? count_d : count_m);
+                const int count = seg == 2 ? kRRings * mix_stripes(count_m, count_d).S : (seg ? count_d : count_m);
                 const int64_t goff =
                     from_desc ? (seg == 2 ? s_gd.mgoff : (seg ? s_gd.dgoff : s_gd.goff)) : s_sgoff[seg];
                 const uint8_t* tiles = (seg == 2 ? p.mix : (seg ? p.delta.gring : p.main.gring)) + goff;
@@ -601,8 +616,8 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
             if (count == 0) continue;
             const CandBuf& cb = seg == 1 ? cd : cm;
             const uint32_t kbase = (uint32_t)s_skoff[seg];
-            // combined stream: positions from cmain on are the delta's (key base dkbase)
-            const uint32_t cmain = DM == 2 ? (uint32_t)count_m : 0xFFFFFFFFu;
+            // combined stream: each stripe's main rows, then its delta rows (key base dkbase)
+            const MixStripes ms = mix_stripes(DM == 2 ? count_m : 0, DM == 2 ? count_d : 0);
             const uint32_t dkbase = (uint32_t)s_skoff[1];
             if (si == 1) {                     // the main rows after the delta rows: same LUT
                 seg_setup(seg, false, lanebase, hmax, S, H0, wsteps, nchunks);
@@ -614,9 +629,9 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 s23 = make_float2(0.f, 0.f);
             }
             set_thf(thr0);
-            // first step (of the segment) at which this lane group finishes a
-            // delta row of the combined stream: position rid*S + x - 7 >= cmain
-            const int xd = DM == 2 ? (int)cmain - rid * S + 7 : 0x7FFFFFFF;
+            // first step at which a lane group finishes a delta row of the
+            // combined stream (stripe step Sm, finished 7 steps later)
+            const int xd = DM == 2 ? ms.Sm + 7 : 0x7FFFFFFF;
             for (int t = 0; t < nchunks; ++t) {
                 uint64_t thr[kGQ];    // read now, used after the steps: a bound only ever decreases
 #pragma unroll
@@ -662,18 +677,20 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                     // finished in the chunk, against the delta bounds.  The warp
                     // wrote their slots itself (no block barrier is needed to read
                     // them, and the next writes to them are its own); lane i takes
-                    // the warp's i-th such row (a list's delta rows are few, so
-                    // usually one pass of 32).  A query with more passing keys than
-                    // the delta rank Rd gets a new bound: the Rd-th smallest of any
-                    // Rd or more existing keys bounds the rank-Rd key from above.
+                    // the warp's i-th such row (each stripe holds about 1/32 of the
+                    // list's delta rows, so usually one pass of 32).  A query with
+                    // more passing keys than the delta rank Rd gets a new bound: the
+                    // Rd-th smallest of any Rd or more existing keys bounds the
+                    // rank-Rd key from above.
                     const int va = t * kRSteps >= 7 ? t * kRSteps - 7 : 0, vb = min(S, t * kRSteps + kRSteps - 7);
                     int lo[4], ln[4], m = 0;
 #pragma unroll
                     for (int g4 = 0; g4 < 4; ++g4) {
                         const int r = 4 * warp + g4;
-                        const int a = max((int)cmain, r * S + va), b = min(count, r * S + vb);
+                        const int dl = min(ms.Sd, max(0, count_d - r * ms.Sd));     // delta rows of stripe r
+                        const int a = max(ms.Sm, va), b = min(ms.Sm + dl, vb);     // stripe steps, less 7
                         lo[g4] = a;
-                        ln[g4] = va < vb && b > a ? b - a : 0;
+                        ln[g4] = b > a ? b - a : 0;
                         m += ln[g4];
                     }
                     if (m > 0) {
@@ -688,9 +705,9 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                                     if (i >= ln[2]) { i -= ln[2]; g4 = 3; a = lo[3]; }
                                 }
                             }
-                            const int v = a + i, r = 4 * warp + g4;
-                            fv = dist4[r * kRSteps + (v - r * S + 7 - t * kRSteps)];
-                            dp = (uint32_t)v - cmain;
+                            const int xs = a + i, r = 4 * warp + g4;
+                            fv = dist4[r * kRSteps + (xs + 7 - t * kRSteps)];
+                            dp = (uint32_t)(r * ms.Sd + xs - ms.Sm);
                             return true;
                         };
                         auto dkey = [&](bool ok, const float4& fv, uint32_t dp, int k) -> uint64_t {
@@ -789,9 +806,14 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 uint32_t vid[kE];     // list position, or 0xFFFFFFFF for no vector
 #pragma unroll
                 for (int e = 0; e < kE; ++e) {
-                    const int x = t * kRSteps + (tid % kRSteps);
-                    const int v = (tid / kRSteps + (kRT / kRSteps) * e) * S + x - 7;
-                    vid[e] = (x >= 7 && x - 7 < S && v < count) ? (uint32_t)v : 0xFFFFFFFFu;
+                    const int x = t * kRSteps + (tid % kRSteps), rr = tid / kRSteps + (kRT / kRSteps) * e;
+                    if (DM == 2) {           // the main rows of the combined stream
+                        const int mi = rr * ms.Sm + x - 7;
+                        vid[e] = (x >= 7 && x - 7 < ms.Sm && mi < count_m) ? (uint32_t)mi : 0xFFFFFFFFu;
+                    } else {
+                        const int v = rr * S + x - 7;
+                        vid[e] = (x >= 7 && x - 7 < S && v < count) ? (uint32_t)v : 0xFFFFFFFFu;
+                    }
                     f[e] = vid[e] != 0xFFFFFFFFu ? dist4[tid + kRT * e] : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
                 int cnt4[kGQ];
@@ -802,7 +824,7 @@ __global__ void __launch_bounds__(kRT, 1) pq_stagger_kernel(PQParams p, WorkList
                 }
                 auto key_of = [&](int e, int k) -> uint64_t {
                     const float dk = k == 0 ? f[e].x : k == 1 ? f[e].y : k == 2 ? f[e].z : f[e].w;
-                    return vid[e] < cmain ? make_key(__float_as_uint(dk), kbase + vid[e]) : kKeyNone;
+                    return vid[e] != 0xFFFFFFFFu ? make_key(__float_as_uint(dk), kbase + vid[e]) : kKeyNone;
                 };
 #pragma unroll
                 for (int e = 0; e < kE; ++e)
@@ -923,9 +945,10 @@ __device__ __forceinline__ int64_t gring_byte(int64_t v, int b, int s) {
     return T * 128 * MPL + (int64_t)(8 * (byte / 16) + j) * 16 + byte % 16;
 }
 
-// combined tiles of list l: positions below count_m copy the main tiles byte
-// for byte (the layout of a position does not depend on the list's length),
-// positions count_m .. count_m + count_d - 1 take the delta's rows in order
+// combined tiles of list l (mix_stripes): position p = r*S + x of stripe r
+// holds main row r*Sm + x for x < Sm, delta row r*Sd + x - Sm for Sm <= x <
+// Sm + Sd (each below its count), zeros otherwise; bytes come from the main
+// and delta grouped-ring tiles
 template <int MPL>
 __global__ void gring_mix_kernel(const uint8_t* __restrict__ mt, const int64_t* __restrict__ moff,
                                  const int32_t* __restrict__ mcnt, const uint8_t* __restrict__ dt,
@@ -933,8 +956,9 @@ __global__ void gring_mix_kernel(const uint8_t* __restrict__ mt, const int64_t* 
                                  const int64_t* __restrict__ xoff, int nlist, uint8_t* __restrict__ out) {
     for (int l = blockIdx.x; l < nlist; l += gridDim.x) {
         const int cm = mcnt[l], cdl = dcnt[l];
-        const int64_t mtotal = gring_tiles(cm) * 128 * MPL;
-        const int64_t total = gring_tiles(cm + cdl) * 128 * MPL;
+        const MixStripes ms = mix_stripes(cm, cdl);
+        const int64_t np = (int64_t)kRRings * ms.S;
+        const int64_t total = gring_tiles((int)np) * 128 * MPL;
         const uint8_t* src_m = mt + moff[l];
         const uint8_t* src_d = dt + doff[l];
         uint8_t* dst = out + xoff[l];
@@ -947,8 +971,16 @@ __global__ void gring_mix_kernel(const uint8_t* __restrict__ mt, const int64_t* 
             const int blk = (int)(g - 8 * g8);
             const int64_t v = 8 * g8 + jj;
             uint8_t val = 0;
-            if (v >= 0 && v < cm) val = e < mtotal ? src_m[e] : (uint8_t)0;
-            else if (v >= cm && v < cm + cdl) val = src_d[gring_byte<MPL>(v - cm, blk, s)];
+            if (v >= 0 && v < np) {
+                const int st = (int)(v / ms.S), x = (int)(v % ms.S);
+                if (x < ms.Sm) {
+                    const int64_t mi = (int64_t)st * ms.Sm + x;
+                    if (mi < cm) val = src_m[gring_byte<MPL>(mi, blk, s)];
+                } else if (x < ms.Sm + ms.Sd) {
+                    const int64_t di = (int64_t)st * ms.Sd + (x - ms.Sm);
+                    if (di < cdl) val = src_d[gring_byte<MPL>(di, blk, s)];
+                }
+            }
             dst[e] = val;
         }
     }
@@ -1350,6 +1382,10 @@ int pq_scan_chunk_items(int M, int d) { return pq_group_usable(M, d) ? kRRings *
 int pq_chunk_slack(int M, int d, int R) { return pq_group_usable(M, d) ? R / 4 : 0; }
 
 int64_t pq_gring_list_bytes(int count, int M) { return gring_tiles(count) * 128 * (M / 8); }
+
+int64_t pq_mix_list_bytes(int count_main, int count_delta, int M) {
+    return gring_tiles(kRRings * mix_stripes(count_main, count_delta).S) * 128 * (M / 8);
+}
 
 cudaError_t pq_build_gring(const uint8_t* codes, const int64_t* offsets, const int32_t* counts,
                            const int64_t* tile_off, int nlist, int M, uint8_t* out, cudaStream_t st) {
