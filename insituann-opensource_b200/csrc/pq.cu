@@ -1438,7 +1438,7 @@ constexpr int kDW = 8;      // warps per CTA of the direct delta kernel
 // scan of build_delta_pq_mutable_publish / the overlay search
 // (updates/pq_update.cu:448-523).
 template <int M, int DSUB>
-__global__ void __launch_bounds__(kDW * 32) delta_direct_kernel(PQParams p, const int32_t* __restrict__ probes,
+__global__ void __launch_bounds__(kDW * 32, 1) delta_direct_kernel(PQParams p, const int32_t* __restrict__ probes,
                                                                int nprobe, int nlist_global,
                                                                const int32_t* __restrict__ list_map, int Rd,
                                                                uint64_t* __restrict__ out) {
@@ -1519,6 +1519,107 @@ __global__ void __launch_bounds__(kDW * 32) delta_direct_kernel(PQParams p, cons
     for (int i = threadIdx.x; i < Rd; i += kDW * 32) out[(size_t)q * Rd + i] = s_top[i];
 }
 
+// The same search with the codebook staged in shared memory, sub-quantizer
+// major ([m][c][u]: a warp's 32 gathers of one sub-quantizer fall on 32
+// random 16-byte slots of one 4 KB row instead of 32 L1 lines), by persistent
+// CTAs of kDW2 warps, each CTA taking queries q = blockIdx.x + i * gridDim.x.
+constexpr int kDW2 = 16;
+template <int M, int DSUB>
+constexpr size_t delta_smem_bytes() {
+    return sizeof(float) * ((size_t)M * 256 * DSUB + (size_t)kDW2 * M * DSUB) + sizeof(uint64_t) * kDW2 * 32;
+}
+
+template <int M, int DSUB>
+__global__ void __launch_bounds__(kDW2 * 32, 1) delta_direct_smem_kernel(PQParams p, const int32_t* __restrict__ probes,
+                                                                    int nq, int nprobe, int nlist_global,
+                                                                    const int32_t* __restrict__ list_map, int Rd,
+                                                                    uint64_t* __restrict__ out) {
+    constexpr int d = M * DSUB;
+    extern __shared__ __align__(16) float smd[];
+    float* s_cb = smd;                                   // [M][256][DSUB]
+    float* s_res = s_cb + (size_t)M * 256 * DSUB;        // [kDW2][d]
+    uint64_t* s_top = reinterpret_cast<uint64_t*>(s_res + kDW2 * d);   // [kDW2 * 32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < M * 256 * DSUB; i += kDW2 * 32) {
+        const int c = i / (M * DSUB), m = (i / DSUB) % M, u = i % DSUB;
+        s_cb[((size_t)m * 256 + c) * DSUB + u] = p.codebook_t[i];
+    }
+    __syncthreads();
+    const ListStore& D = p.delta;
+    float* res = s_res + warp * d;
+    for (int q = blockIdx.x; q < nq; q += gridDim.x) {
+        uint64_t top = kKeyNone;
+        for (int c = warp; c < nprobe; c += kDW2) {
+            const int g = probes[(size_t)q * nprobe + c];
+            if (g < 0 || g >= nlist_global) continue;
+            const int l = list_map ? list_map[g] : g;
+            if (l < 0) continue;
+            const int cnt = D.counts[l];
+            if (cnt <= 0) continue;
+            const int64_t off = D.offsets[l];
+            const uint32_t kb = (uint32_t)(D.key_off ? D.key_off[l] : off);
+            const float* cv = p.cent + (size_t)l * d;
+            for (int x = lane; x < d; x += 32) res[x] = __fsub_rn(p.q[(size_t)q * d + x], cv[x]);
+            __syncwarp();
+            for (int r0 = 0; r0 < cnt; r0 += 32) {
+                const int r = r0 + lane;
+                uint64_t key = kKeyNone;
+                if (r < cnt) {
+                    const uint4* cp = reinterpret_cast<const uint4*>(D.data + (size_t)(off + r) * M);
+                    float dist = 0.f;
+#pragma unroll
+                    for (int h = 0; h < M / 16; ++h) {
+                        const uint4 w4 = __ldg(cp + h);
+                        const uint32_t w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                        for (int b = 0; b < 16; ++b) {
+                            const int m = 16 * h + b;
+                            const uint32_t code = (w[b >> 2] >> (8 * (b & 3))) & 0xFFu;
+                            const float* cb = s_cb + ((size_t)m * 256 + code) * DSUB;
+                            float cbv[DSUB];
+                            if constexpr (DSUB % 4 == 0) {
+#pragma unroll
+                                for (int u = 0; u < DSUB; u += 4) {
+                                    const float4 t4 = *reinterpret_cast<const float4*>(cb + u);
+                                    cbv[u] = t4.x; cbv[u + 1] = t4.y; cbv[u + 2] = t4.z; cbv[u + 3] = t4.w;
+                                }
+                            } else {
+                                const float2 t2 = *reinterpret_cast<const float2*>(cb);
+                                cbv[0] = t2.x; cbv[1] = t2.y;
+                            }
+                            float a = 0.f;
+#pragma unroll
+                            for (int u = 0; u < DSUB; ++u) {
+                                const float x = __fsub_rn(res[m * DSUB + u], cbv[u]);
+                                a = u == 0 ? __fmul_rn(x, x) : __fadd_rn(a, __fmul_rn(x, x));
+                            }
+                            dist = m == 0 ? a : __fadd_rn(dist, a);
+                        }
+                    }
+                    key = make_key(__float_as_uint(dist), kb + (uint32_t)r);
+                }
+                const uint64_t worst = __shfl_sync(0xffffffffu, top, 31);
+                if (__any_sync(0xffffffffu, key < worst)) {
+                    uint64_t b = warp_sort32(key);
+                    b = __shfl_sync(0xffffffffu, b, 31 - lane);
+                    uint64_t v = b < top ? b : top;
+#pragma unroll
+                    for (int j = 16; j > 0; j >>= 1) {
+                        const uint64_t o = __shfl_xor_sync(0xffffffffu, v, j);
+                        v = (lane & j) == 0 ? (o < v ? o : v) : (o > v ? o : v);
+                    }
+                    top = v;
+                }
+            }
+            __syncwarp();
+        }
+        s_top[warp * 32 + lane] = top;
+        block_bitonic_sort<kDW2 * 32>(s_top, kDW2 * 32);
+        for (int i = threadIdx.x; i < Rd; i += kDW2 * 32) out[(size_t)q * Rd + i] = s_top[i];
+        __syncthreads();      // s_top is rewritten for the next query
+    }
+}
+
 }  // namespace
 
 bool pq_delta_direct_usable(int M, int d, int Rd) {
@@ -1530,10 +1631,26 @@ cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, in
     if (!pq_delta_direct_usable(p.M, p.d, Rd) || !p.delta.data || !p.codebook_t) return cudaErrorInvalidValue;
     if (nq <= 0) return cudaSuccess;
     const int ds = p.d / p.M;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     note_launch();
+    // the shared-memory codebook where it fits in one CTA, else the codebook
+    // gathered through L1
 #define ISB_DIRECT(MM, DS)                                                                                    \
     if (p.M == MM && ds == DS) {                                                                              \
-        delta_direct_kernel<MM, DS><<<nq, kDW * 32, 0, st>>>(p, probes, nprobe, nlist_global, list_map, Rd, out); \
+        constexpr size_t smem = delta_smem_bytes<MM, DS>();                                                   \
+        if constexpr (smem <= 220 * 1024) {                                                                   \
+            cudaError_t e = cudaFuncSetAttribute(delta_direct_smem_kernel<MM, DS>,                            \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
+            if (e) return e;                                                                                  \
+            const int grid = nq < sms ? nq : sms;                                                             \
+            delta_direct_smem_kernel<MM, DS><<<grid, kDW2 * 32, smem, st>>>(p, probes, nq, nprobe, nlist_global, \
+                                                                            list_map, Rd, out);               \
+        } else {                                                                                              \
+            delta_direct_kernel<MM, DS><<<nq, kDW * 32, 0, st>>>(p, probes, nprobe, nlist_global, list_map, Rd, \
+                                                                 out);                                        \
+        }                                                                                                     \
         return cudaGetLastError();                                                                            \
     }
     ISB_DIRECT(16, 2) ISB_DIRECT(16, 4) ISB_DIRECT(16, 8)
