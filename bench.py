@@ -595,9 +595,12 @@ def main():
     ap.add_argument("--nprobe", type=int, default=0)
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--overlay", default="",
+    ap.add_argument("--overlay", default="auto",
                     help="also time the search with published delta segments of these sizes, e.g. "
-                         "1000000,5000000,10000000 (BASELINE configs[4]; 1 GPU)")
+                         "1000000,5000000,10000000 (BASELINE configs[4]; 1 GPU); 'auto' (default): "
+                         "those three on c2 at N=1, none otherwise; 'none' for none")
+    ap.add_argument("--overlay-nprobe", default="64",
+                    help="nprobe values of the overlay runs (BASELINE configs[4]: 64)")
     args = ap.parse_args()
     cfg = CONFIGS[args.config]
     args.warmup = max(args.warmup, 3)
@@ -924,7 +927,10 @@ def main():
     # seeded uniform codes (the reference's generators), ids after the base, scanned in
     # the same launches as the main lists; QPS with and without it ----
     overlay = None
-    sizes = [int(x) for x in str(args.overlay).split(",") if x and int(x) > 0]
+    ov_arg = str(args.overlay)
+    if ov_arg == "auto":
+        ov_arg = "1000000,5000000,10000000" if args.config == "c2" else ""
+    sizes = [int(x) for x in ov_arg.split(",") if x and x != "none" and int(x) > 0]
     if sizes and N == 1:
         def ostep(np_, ov):
             batch.stage1_prepare_device(q_dev.data_ptr(), nq)
@@ -945,7 +951,7 @@ def main():
             batch.profile(False)
             return nq / (e0.elapsed_time(e1) / args.steps / 1000.0), st
 
-        onp = sorted({nprobe, 64})
+        onp = sorted({int(x) for x in str(args.overlay_nprobe).split(",") if x})
         base = {np_: timed(np_, False) for np_ in onp}
         base_qps = {np_: v[0] for np_, v in base.items()}
         runs = []
@@ -959,7 +965,7 @@ def main():
             ostep(64, True)
             batch.sync()
             oid, odd = batch.get_results(nq, k)
-            Po = min(P, nq)
+            Po = min(P, nq, 500)
             po, _ = oracle.route_l2_par(q_np[:Po], idx["centroids"], 64)
             ei, ed = oracle.pq_search_par(idx["centroids"], idx["codebook"], idx["codes"], offsets, counts,
                                           idx["r2o"], q_np[:Po], po, k, rerank_n=R, delta=dseg, delta_topk=16,
@@ -971,8 +977,12 @@ def main():
                 pr = batch.get_probes(nq, np_)
                 dsum = float(dseg["counts"][pr].sum())
                 share = dsum / (dsum + float(counts[pr].sum()))
-                runs.append({"delta_vectors": nd, "nprobe": np_, "qps_without": base_qps[np_], "qps_with": qw,
+                # how the library searches this delta (INSITU_PQ_DELTA, else its size rule)
+                mode = os.environ.get("INSITU_PQ_DELTA") or ("direct" if nd <= 100 * nlist else "mix")
+                runs.append({"delta_vectors": nd, "nprobe": np_, "delta_search": mode,
+                             "qps_without": base_qps[np_], "qps_with": qw,
                              "overhead": 1.0 - qw / base_qps[np_], "delta_share_of_scanned": share,
+                             "overhead_within_share_plus_5pct": bool(1.0 - qw / base_qps[np_] <= share + 0.05),
                              "stages_ms_without": base[np_][1], "stages_ms_with": st_w,
                              "parity_vs_oracle": o_par, "parity_queries": Po})
                 log(f"[bench] overlay {nd}: nprobe {np_}: {base_qps[np_]:.0f} -> {qw:.0f} qps "

@@ -38,7 +38,7 @@
  *                       (delta_topk above 32 as "seg"), "mix" in one tile
  *                       stream with each list's main rows, "seg" in their
  *                       own tiles after each list's main rows; unset:
- *                       "direct" up to 48 delta rows per list on average,
+ *                       "direct" up to 100 delta rows per list on average,
  *                       else "mix"
  *
  * Citations are paths inside the reference project

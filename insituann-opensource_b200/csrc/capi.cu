@@ -876,7 +876,7 @@ void adopt_f32_lists(IndexCtx* x, int* d_counts, float* d_rows, int nlist, long 
 // Unset: "direct" for deltas of at most kDirectRowsPerList rows per list on
 // average (a LUT would cost more than it saves), else "mix".
 enum DeltaMode { kDeltaAuto = -1, kDeltaDirect = 0, kDeltaMix = 1, kDeltaSeg = 2 };
-constexpr long long kDirectRowsPerList = 48;
+constexpr long long kDirectRowsPerList = 100;
 DeltaMode delta_mode() {
     const char* e = std::getenv("INSITU_PQ_DELTA");
     if (e && std::strcmp(e, "direct") == 0) return kDeltaDirect;
