@@ -25,8 +25,9 @@
  *
  * Environment (read on every call; every choice gives the same results bit
  * for bit):
- *   INSITU_SCRATCH_MB   per-batch scratch budget (default 6144); larger
- *                       batches run in query sub-batches inside one call
+ *   INSITU_SCRATCH_MB   per-batch scratch budget in MB (default: an eighth
+ *                       of the device's memory, 1 to 24 GB); larger batches
+ *                       run in query sub-batches inside one call
  *   INSITU_ROUTE_TC     routing kernels: 1 (default) fused tensor-core
  *                       kernel where it applies, 2 fused or tensor-core
  *                       matrix, 3 tensor-core matrix, 0 CUDA cores only

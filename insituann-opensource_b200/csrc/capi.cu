@@ -203,11 +203,20 @@ thread_local std::string g_err;
 std::atomic<unsigned long long> g_launches{0};
 
 // device memory budget for per-batch candidate / routing scratch
+// INSITU_SCRATCH_MB, else an eighth of the current device's memory, at most
+// 24 GB and at least 1 GB (22.9 GB on a 183 GB B200: a 10k-query batch of
+// the 100M-row index runs as one sub-batch, whose groups share each list's
+// LUT and tile reads among more queries than two half batches would)
 size_t scratch_budget() {
     const char* e = getenv("INSITU_SCRATCH_MB");
     long mb = e ? atol(e) : 0;
-    if (mb <= 0) mb = 6144;
-    return (size_t)mb << 20;
+    if (mb > 0) return (size_t)mb << 20;
+    size_t free_b = 0, total_b = 0;
+    if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
+        cudaGetLastError();
+        total_b = (size_t)48 << 30;
+    }
+    return std::min<size_t>((size_t)24 << 30, std::max<size_t>((size_t)1 << 30, total_b / 8));
 }
 
 template <class T>
