@@ -787,13 +787,21 @@ def main():
             step(np_)
             ids, _ = results()
             rec = synth.recall_at_k(ids, gt, k) if rank == 0 else None
+            step(np_)                 # buffers for this nprobe are in place after the first step
             barrier()
-            t0 = time.perf_counter()
-            reps = 3
+            reps = 5
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(ext)
             for _ in range(reps):
                 step(np_)
+            s1.record(ext)
             barrier()
-            dt = (time.perf_counter() - t0) / reps
+            ms = s0.elapsed_time(s1)
+            if N > 1:
+                t = torch.tensor([ms], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                ms = float(t.item())
+            dt = ms / 1000.0 / reps
             sweep.append({"nprobe": np_, "recall@10": rec, "qps": nq / dt})
             if rank == 0:
                 log(f"[bench] nprobe {np_}: recall@10 {rec} qps {nq / dt:.0f}")
