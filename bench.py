@@ -1009,8 +1009,7 @@ def main():
                 pr = batch.get_probes(nq, np_)
                 dsum = float(dseg["counts"][pr].sum())
                 share = dsum / (dsum + float(counts[pr].sum()))
-                # how the library searches this delta (INSITU_PQ_DELTA, else its size rule)
-                mode = os.environ.get("INSITU_PQ_DELTA") or ("direct" if nd <= 100 * nlist else "mix")
+                mode = index.delta_mode()          # how the library searches this delta
                 runs.append({"delta_vectors": nd, "nprobe": np_, "delta_search": mode,
                              "qps_without": base_qps[np_], "qps_with": qw,
                              "overhead": 1.0 - qw / base_qps[np_], "delta_share_of_scanned": share,

@@ -327,6 +327,15 @@ int ivf_pq_publish_delta(void* idx_ctx, const uint8_t* codes, const int* ids, co
                          const float* raw_f32, long long n_delta);
 int ivf_pq_clear_delta(void* idx_ctx);
 /*
+ * How the published delta is searched, fixed when it was published
+ * (INSITU_PQ_DELTA, else by its size): 0 none published, 1 a delta kernel of
+ * its own after the main scan (a delta_topk above 32 is searched as 3), 2 in
+ * one tile stream with each list's main rows, 3 in its own tiles after each
+ * list's main rows; IVF_EINVAL for a bad context.  Every mode returns the same
+ * results.
+ */
+int ivf_pq_delta_mode(void* idx_ctx);
+/*
  * Online insert (the pipeline the reference's README describes as not
  * released, README.md:16-24): n new vectors d_x [n, d] -- device rows, uint8
  * (x_is_u8 = 1) or fp32 as the index's rerank rows -- with reported ids

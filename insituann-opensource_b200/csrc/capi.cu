@@ -127,6 +127,7 @@ struct IndexCtx {
     float* codebook_t = nullptr;   // [256, M, dsub]
     Segment main, delta;
     bool has_delta = false;
+    int delta_search = 0;        // ivf_pq_delta_mode: 0 none, 1 direct, 2 combined stream, 3 own tiles
     // host copy of the published delta segment in delta-position order (list
     // major), kept so ivf_pq_insert can grow it
     std::vector<uint8_t> h_dcodes, h_draw_u8;
@@ -934,6 +935,7 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
     std::vector<uint8_t> hc((size_t)n_delta * x->M), hu;
     std::vector<float> hf;
     std::vector<int32_t> hi((size_t)n_delta), hcnt(counts, counts + x->nlist);
+    DeltaMode mode = kDeltaSeg;
     try {
         load_lists(x, s, codes, (size_t)x->M, offsets, counts, ids, key_offsets, x->nlist, n_delta);
         if (f32) s.rr_f32 = dcopy(raw_f32, (size_t)n_delta * x->d, s.owned);
@@ -949,7 +951,7 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
                 ck(cudaMemcpy(hu.data(), s.rr_u8, hu.size(), cudaMemcpyDeviceToHost), "delta copy");
             }
         }
-        DeltaMode mode = delta_mode();
+        mode = delta_mode();
         if (mode == kDeltaAuto) mode = n_delta <= kDirectRowsPerList * x->nlist ? kDeltaDirect : kDeltaMix;
         build_gring(s, counts, x->nlist, x->M, x->d, mode == kDeltaDirect);
         if (n_delta > 0 && s.gring && x->main.gring && mode == kDeltaMix) build_mix(x, s, counts);
@@ -966,6 +968,12 @@ void publish_delta_locked(IndexCtx* x, const uint8_t* codes, const int* ids, con
     x->delta.release();
     x->delta = std::move(s);
     x->has_delta = n_delta > 0;
+    // how run_pq will search it (the direct kernel needs its shapes and the
+    // row-major codes; the combined stream needs its tiles)
+    x->delta_search = n_delta <= 0                                                       ? 0
+                      : mode == kDeltaDirect && x->delta.data && pq_group_usable(x->M, x->d) ? 1
+                      : x->delta.mix                                                      ? 2
+                                                                                          : 3;
     x->h_dcodes.swap(hc);
     x->h_dids.swap(hi);
     x->h_dcounts.swap(hcnt);
@@ -1484,12 +1492,24 @@ int ivf_pq_clear_delta(void* idx_ctx) {
         ck(cudaDeviceSynchronize(), "cudaDeviceSynchronize");
         x->delta.release();
         x->has_delta = false;
+        x->delta_search = 0;
         x->h_dcodes.clear();
         x->h_dids.clear();
         x->h_dcounts.clear();
         x->h_draw_u8.clear();
         x->h_draw_f32.clear();
     });
+}
+
+int ivf_pq_delta_mode(void* idx_ctx) {
+    IndexCtx* x = nullptr;
+    try {
+        x = as_index(idx_ctx);
+    } catch (...) {
+        return IVF_EINVAL;
+    }
+    std::shared_lock<std::shared_mutex> rd(x->rw);
+    return x->delta_search;
 }
 
 int ivf_pq_insert(void* idx_ctx, const void* d_x, int x_is_u8, const int* ids, long long n) {

@@ -36,6 +36,7 @@ EXPORTS = [
     "ivf_register_index_instance", "ivf_get_index_instance", "ivf_unregister_index_instance",
     "coarse_handle_init", "coarse_handle_release", "coarse_search", "coarse_get_last_timing",
     "ivf_u8_load", "ivf_pq_load", "ivf_set_shard", "ivf_pq_publish_delta", "ivf_pq_clear_delta",
+    "ivf_pq_delta_mode",
     "ivf_route", "ivf_set_probes", "ivf_get_probes", "ivf_u8_search", "ivf_pq_search", "ivf_get_results_i32",
     "ivf_pipeline_stage1_prepare_device", "ivf_get_results_device", "ivf_batch_stream",
     "ivf_route_keys", "ivf_route_merge", "ivf_route_merge_shards", "ivf_set_deleted", "ivf_pq_search_shard", "ivf_pq_merge_shards",
@@ -80,6 +81,7 @@ _SIGS = {
     "ivf_set_shard": ([vp, i32, vp, vp], i32),
     "ivf_pq_publish_delta": ([vp, vp, vp, vp, vp, vp, vp, vp, i64], i32),
     "ivf_pq_clear_delta": ([vp], i32),
+    "ivf_pq_delta_mode": ([vp], i32),
     "ivf_route": ([vp, vp, i32, i32], i32),
     "ivf_set_probes": ([vp, vp, i32, i32], i32),
     "ivf_get_probes": ([vp, vp, i32, i32], i32),
@@ -259,6 +261,13 @@ class Index:
 
     def clear_delta(self):
         self._check(self.L.ivf_pq_clear_delta(self.h))
+
+    def delta_mode(self):
+        """how the published delta is searched: None, "direct", "mix" or "seg" (ivf_pq_delta_mode)"""
+        r = self.L.ivf_pq_delta_mode(self.h)
+        if r < 0:
+            self._check(r)
+        return [None, "direct", "mix", "seg"][r]
 
     def insert(self, rows, ids):
         """online insert of device rows (torch uint8 / float32 [n, d]) with ids (int32 [n]) into the delta"""

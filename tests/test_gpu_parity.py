@@ -38,13 +38,16 @@ def gpu_exact(e, q_u8, probes, k, route=False, nprobe=None):
     return out
 
 
-def gpu_pq(p, q, probes, k, R, delta=None, delta_topk=16, f32=False):
+def gpu_pq(p, q, probes, k, R, delta=None, delta_topk=16, f32=False, delta_mode=None):
+    """delta_mode: when given, the mode the library must report for the published delta"""
     nq, nprobe = probes.shape
     index = ib.Index().load_pq(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"],
                                base_u8=None if f32 else p["base_u8"], base_f32=p["base_f32"] if f32 else None)
     if delta is not None:
         index.publish_delta(delta["codes"], delta["ids"], delta["counts"], delta["offsets"],
                             raw_u8=delta.get("raw_u8"), raw_f32=delta.get("raw_f32"))
+        if delta_mode is not None:
+            assert index.delta_mode() == delta_mode
     b = ib.Batch(nq, q.shape[1], nprobe, k, len(p["counts"]))
     b.stage1_prepare(q)
     b.set_probes(probes)
@@ -337,7 +340,7 @@ def test_pq_overlay(cuda_ok, pq_medium, mode, monkeypatch):
     probes, _ = oracle.route_l2(q, p["centroids"], nprobe)
     probes[::7, 0] = 3
     for dtk in (16, 5, 48):
-        gi, gd = gpu_pq(p, q, probes, k, R, delta=delta, delta_topk=dtk)
+        gi, gd = gpu_pq(p, q, probes, k, R, delta=delta, delta_topk=dtk, delta_mode=mode)
         oi, od = oracle.pq_search(p["centroids"], p["codebook"], p["codes"], p["offsets"], p["counts"], p["r2o"], q,
                                   probes, k, rerank_n=R, base_u8=p["base_u8"], delta=delta, delta_topk=dtk)
         assert np.array_equal(gi, oi) and np.array_equal(gd, od)
