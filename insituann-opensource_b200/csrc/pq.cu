@@ -1626,6 +1626,29 @@ bool pq_delta_direct_usable(int M, int d, int Rd) {
     return Rd >= 1 && Rd <= 32 && pq_group_usable(M, d) && d <= kPMaxD;
 }
 
+namespace {
+
+// the shared-memory codebook where it fits in one CTA, else the codebook
+// gathered through L1
+template <int MM, int DS>
+cudaError_t launch_delta_direct(const PQParams& p, const int32_t* probes, int nq, int nprobe, int nlist_global,
+                                const int32_t* list_map, int Rd, uint64_t* out, int sms, cudaStream_t st) {
+    constexpr size_t smem = delta_smem_bytes<MM, DS>();
+    if constexpr (smem <= 220 * 1024) {
+        cudaError_t e = cudaFuncSetAttribute(delta_direct_smem_kernel<MM, DS>,
+                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e) return e;
+        const int grid = nq < sms ? nq : sms;
+        delta_direct_smem_kernel<MM, DS><<<grid, kDW2 * 32, smem, st>>>(p, probes, nq, nprobe, nlist_global,
+                                                                        list_map, Rd, out);
+    } else {
+        delta_direct_kernel<MM, DS><<<nq, kDW * 32, 0, st>>>(p, probes, nprobe, nlist_global, list_map, Rd, out);
+    }
+    return cudaGetLastError();
+}
+
+}  // namespace
+
 cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, int nprobe, int nlist_global,
                             const int32_t* list_map, int Rd, uint64_t* out, cudaStream_t st) {
     if (!pq_delta_direct_usable(p.M, p.d, Rd) || !p.delta.data || !p.codebook_t) return cudaErrorInvalidValue;
@@ -1635,24 +1658,8 @@ cudaError_t pq_delta_direct(const PQParams& p, const int32_t* probes, int nq, in
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     note_launch();
-    // the shared-memory codebook where it fits in one CTA, else the codebook
-    // gathered through L1
-#define ISB_DIRECT(MM, DS)                                                                                    \
-    if (p.M == MM && ds == DS) {                                                                              \
-        constexpr size_t smem = delta_smem_bytes<MM, DS>();                                                   \
-        if constexpr (smem <= 220 * 1024) {                                                                   \
-            cudaError_t e = cudaFuncSetAttribute(delta_direct_smem_kernel<MM, DS>,                            \
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);     \
-            if (e) return e;                                                                                  \
-            const int grid = nq < sms ? nq : sms;                                                             \
-            delta_direct_smem_kernel<MM, DS><<<grid, kDW2 * 32, smem, st>>>(p, probes, nq, nprobe, nlist_global, \
-                                                                            list_map, Rd, out);               \
-        } else {                                                                                              \
-            delta_direct_kernel<MM, DS><<<nq, kDW * 32, 0, st>>>(p, probes, nprobe, nlist_global, list_map, Rd, \
-                                                                 out);                                        \
-        }                                                                                                     \
-        return cudaGetLastError();                                                                            \
-    }
+#define ISB_DIRECT(MM, DS) \
+    if (p.M == MM && ds == DS) return launch_delta_direct<MM, DS>(p, probes, nq, nprobe, nlist_global, list_map, Rd, out, sms, st);
     ISB_DIRECT(16, 2) ISB_DIRECT(16, 4) ISB_DIRECT(16, 8)
     ISB_DIRECT(32, 2) ISB_DIRECT(32, 4) ISB_DIRECT(32, 8)
     ISB_DIRECT(48, 2) ISB_DIRECT(48, 4)
