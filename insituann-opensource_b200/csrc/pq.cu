@@ -153,7 +153,11 @@ constexpr int kGQ = 4;      // queries per group
 // g = 16T + i - j, v = 8*floor(g/8) + j, blk = g mod 8 (0 outside the list);
 // its 16-byte piece u = b/16 sits at tile offset (8u + j)*16, so each of a
 // group's MPL 16-byte loads reads one whole 128-byte line, and the lane
-// indexes the bytes statically.
+// indexes the bytes statically.  A stripe starts on a multiple of 8 rows, on
+// a tile or half way into one (load_tile takes half-tile indices).  With a
+// published delta the scan may read a combined stream instead (mix_stripes):
+// the same layout over positions that interleave each stripe's main and
+// delta rows.
 //
 // The sums of queries (0,1) and (2,3) are float2 pairs added with the packed
 // fp32x2 instructions (__fadd2_rn: two independent round-to-nearest adds).  A
