@@ -41,3 +41,4 @@ def test_no_device_calls_fail_cleanly():
     # a null / foreign context is rejected, not dereferenced blindly
     assert lib.ivf_route(None, None, 1, 1) == -1
     assert lib.ivf_check_index_initialized_wrapper(None) == 0
+    assert lib.ivf_pq_delta_mode(None) == -1
